@@ -1,0 +1,442 @@
+// Python bindings of the glm53 CUDA kernels (torch tensors -> raw pointers; launches on the current stream).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "launchers.h"
+
+namespace {
+
+using at::Tensor;
+using OptT = c10::optional<Tensor>;
+
+void check(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, "glm53 kernel ", what, " failed: ", cudaGetErrorString(e));
+}
+
+template <class T>
+T* P(const Tensor& t) { return reinterpret_cast<T*>(t.data_ptr()); }
+template <class T>
+T* P(const OptT& t) { return (t.has_value() && t->defined()) ? reinterpret_cast<T*>(t->data_ptr()) : nullptr; }
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void cuda_check(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+
+// ------------------------------------------------------------------------------------------------- GEMV
+void gemv(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, int64_t mode, double limit) {
+  cuda_check(x, "x"); cuda_check(w, "w"); cuda_check(y, "y");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16, "x must be bf16");
+  TORCH_CHECK(x.stride(-1) == 1 && w.stride(-1) == 1 && y.stride(-1) == 1, "inner dims must be contiguous");
+  const bool batched = w.dim() == 3;
+  TORCH_CHECK(x.dim() == (batched ? 3 : 2) && y.dim() == x.dim(), "rank mismatch");
+  GemvArgs p{};
+  p.x = P<const __nv_bfloat16>(x);
+  p.w = w.data_ptr();
+  p.scale = P<const float>(scale);
+  p.y = y.data_ptr();
+  p.batch = batched ? (int)w.size(0) : 1;
+  p.M = (int)x.size(-2);
+  p.K = (int)x.size(-1);
+  p.N = (int)w.size(-2);
+  TORCH_CHECK(w.size(-1) == p.K, "K mismatch: x ", p.K, " w ", w.size(-1));
+  p.ldx = x.stride(-2);
+  p.bsx = batched ? x.stride(0) : 0;
+  p.bsw = batched ? w.stride(0) : 0;
+  p.bss = (batched && scale.has_value()) ? scale->stride(0) : 0;
+  p.ldy = y.stride(-2);
+  p.bsy = batched ? y.stride(0) : 0;
+  p.mode = (int)mode;
+  p.limit = (float)limit;
+  if (mode == GEMV_BF16 || mode == GEMV_SWIGLU) {
+    TORCH_CHECK(y.scalar_type() == at::kBFloat16, "y must be bf16");
+  } else {
+    TORCH_CHECK(y.scalar_type() == at::kFloat, "y must be fp32");
+  }
+  TORCH_CHECK(y.size(-2) >= p.M, "y rows");
+  if (w.scalar_type() == at::kByte || w.scalar_type() == at::kFloat8_e4m3fn) {
+    TORCH_CHECK(scale.has_value(), "fp8 weights need a scale");
+    check(g53_gemv_fp8(p, stream()), "gemv_fp8");
+  } else {
+    TORCH_CHECK(w.scalar_type() == at::kBFloat16, "weights must be fp8 (uint8) or bf16");
+    check(g53_gemv_bf16(p, stream()), "gemv_bf16");
+  }
+}
+
+// ------------------------------------------------------------------------------------------------- MoE
+void moe_route(const Tensor& logits, const Tensor& bias, int64_t top_k, double scale, bool norm,
+               const Tensor& topk_ids, const Tensor& topk_w, const Tensor& group_count, const Tensor& group_expert,
+               const Tensor& group_offset, const Tensor& pair_token, const Tensor& pair_expert, const Tensor& pair_w,
+               const Tensor& pair_of) {
+  RouteArgs a{};
+  a.logits = P<const float>(logits);
+  a.bias = P<const float>(bias);
+  a.R = (int)logits.size(0);
+  a.E = (int)logits.size(1);
+  a.top_k = (int)top_k;
+  a.scale = (float)scale;
+  a.norm = norm ? 1 : 0;
+  a.topk_ids = P<int>(topk_ids);
+  a.topk_w = P<float>(topk_w);
+  a.group_count = P<int>(group_count);
+  a.group_expert = P<int>(group_expert);
+  a.group_offset = P<int>(group_offset);
+  a.pair_token = P<int>(pair_token);
+  a.pair_expert = P<int>(pair_expert);
+  a.pair_w = P<float>(pair_w);
+  a.pair_of = P<int>(pair_of);
+  a.max_groups = (int)group_expert.size(0);
+  TORCH_CHECK(group_offset.size(0) >= a.max_groups + 1, "group_offset too small");
+  check(g53_moe_route(a, stream()), "moe_route");
+}
+
+Exl3Args exl3_args(const Tensor& x, const Tensor& tr_g, const Tensor& suh_g, const Tensor& svh_g, const Tensor& tr_u,
+                   const Tensor& suh_u, const Tensor& svh_u, const Tensor& tr_d, const Tensor& suh_d,
+                   const Tensor& svh_d, const Tensor& group_count, const Tensor& group_expert,
+                   const Tensor& group_offset, const Tensor& pair_token, const Tensor& pair_expert,
+                   const Tensor& pair_w, const Tensor& xh_g, const Tensor& xh_u, const Tensor& xd, const Tensor& yd,
+                   double limit) {
+  Exl3Args a{};
+  a.x = P<const __nv_bfloat16>(x);
+  a.ldx = x.stride(0);
+  a.tr_g = P<const int16_t>(tr_g); a.suh_g = P<const __half>(suh_g); a.svh_g = P<const __half>(svh_g);
+  a.tr_u = P<const int16_t>(tr_u); a.suh_u = P<const __half>(suh_u); a.svh_u = P<const __half>(svh_u);
+  a.tr_d = P<const int16_t>(tr_d); a.suh_d = P<const __half>(suh_d); a.svh_d = P<const __half>(svh_d);
+  a.K = (int)suh_g.size(-1);
+  a.N = (int)svh_g.size(-1);
+  a.Dout = (int)svh_d.size(-1);
+  a.group_count = P<const int>(group_count);
+  a.group_expert = P<const int>(group_expert);
+  a.group_offset = P<const int>(group_offset);
+  a.pair_token = P<const int>(pair_token);
+  a.pair_expert = P<const int>(pair_expert);
+  a.pair_w = P<const float>(pair_w);
+  a.max_groups = (int)group_expert.size(0);
+  a.pairs = (int)pair_token.size(0);
+  a.limit = (float)limit;
+  a.xh_g = P<__half>(xh_g); a.xh_u = P<__half>(xh_u); a.xd = P<__half>(xd); a.yd = P<float>(yd);
+  TORCH_CHECK(tr_g.scalar_type() == at::kShort && tr_d.scalar_type() == at::kShort, "trellis must be int16");
+  TORCH_CHECK(xh_g.size(0) >= a.pairs && xd.size(0) >= a.pairs && yd.size(0) >= a.pairs, "scratch rows");
+  return a;
+}
+
+void exl3_moe(const Tensor& x, const Tensor& tr_g, const Tensor& suh_g, const Tensor& svh_g, const Tensor& tr_u,
+              const Tensor& suh_u, const Tensor& svh_u, const Tensor& tr_d, const Tensor& suh_d, const Tensor& svh_d,
+              const Tensor& group_count, const Tensor& group_expert, const Tensor& group_offset,
+              const Tensor& pair_token, const Tensor& pair_expert, const Tensor& pair_w, const Tensor& xh_g,
+              const Tensor& xh_u, const Tensor& xd, const Tensor& yd, double limit) {
+  Exl3Args a = exl3_args(x, tr_g, suh_g, svh_g, tr_u, suh_u, svh_u, tr_d, suh_d, svh_d, group_count, group_expert,
+                         group_offset, pair_token, pair_expert, pair_w, xh_g, xh_u, xd, yd, limit);
+  check(g53_exl3_rot_in(a, stream()), "exl3_rot_in");
+  check(g53_exl3_gate_up(a, stream()), "exl3_gate_up");
+  check(g53_exl3_down(a, stream()), "exl3_down");
+}
+
+void moe_combine(const Tensor& yd, const Tensor& pair_of, int64_t top_k, const Tensor& out, bool accumulate) {
+  check(g53_moe_combine(P<const float>(yd), P<const int>(pair_of), (int)out.size(0), (int)top_k, (int)out.size(1),
+                        P<float>(out), accumulate ? 1 : 0, stream()),
+        "moe_combine");
+}
+
+Tensor exl3_unpack(const Tensor& tr, int64_t K, int64_t N) {
+  auto out = torch::empty({K, N}, tr.options().dtype(at::kHalf));
+  check(g53_exl3_unpack(P<const int16_t>(tr), (int)K, (int)N, P<__half>(out), stream()), "exl3_unpack");
+  return out;
+}
+
+// ------------------------------------------------------------------------------------------------- mHC / norms
+void hc_post_pre(const Tensor& X, const OptT& branch, const OptT& post, const OptT& comb, const OptT& fn,
+                 const OptT& base, const OptT& hscale, const OptT& norm_w, const OptT& normed,
+                 const OptT& post_out, const OptT& comb_out, const Tensor& part, double eps, double hc_eps,
+                 int64_t iters) {
+  HcArgs a{};
+  a.X = P<__nv_bfloat16>(X);
+  a.branch = P<const float>(branch);
+  a.post = P<const float>(post);
+  a.comb = P<const float>(comb);
+  a.fn = P<const __nv_bfloat16>(fn);
+  a.base = P<const float>(base);
+  a.hscale = P<const float>(hscale);
+  a.norm_w = P<const __nv_bfloat16>(norm_w);
+  a.normed = P<__nv_bfloat16>(normed);
+  a.post_out = P<float>(post_out);
+  a.comb_out = P<float>(comb_out);
+  a.part = P<float>(part);
+  a.R = (int)X.size(0);
+  a.S = (int)X.size(1);
+  a.D = (int)X.size(2);
+  a.eps = (float)eps;
+  a.hc_eps = (float)hc_eps;
+  a.iters = (int)iters;
+  TORCH_CHECK(X.is_contiguous(), "X must be contiguous [R, S, D]");
+  TORCH_CHECK(part.numel() >= (int64_t)a.R * (a.D / 256) * 32, "part scratch too small");
+  check(g53_hc_post_pre(a, stream()), "hc_post_pre");
+}
+
+void embed(const Tensor& ids, const Tensor& table, const Tensor& X) {
+  check(g53_embed(P<const int>(ids), P<const __nv_bfloat16>(table), (int)X.size(0), (int)X.size(2), (int)X.size(1),
+                  P<__nv_bfloat16>(X), stream()),
+        "embed");
+}
+
+void stream_mean_norm(const Tensor& X, const Tensor& w, double eps, const OptT& hidden, const Tensor& normed) {
+  check(g53_stream_mean_norm(P<const __nv_bfloat16>(X), (int)X.size(0), (int)X.size(1), (int)X.size(2),
+                             P<const __nv_bfloat16>(w), (float)eps, P<__nv_bfloat16>(hidden),
+                             P<__nv_bfloat16>(normed), stream()),
+        "stream_mean_norm");
+}
+
+void rmsnorm(const Tensor& x, const Tensor& w, double eps, const Tensor& y) {
+  TORCH_CHECK(x.stride(-1) == 1 && y.stride(-1) == 1);
+  check(g53_rmsnorm(P<const __nv_bfloat16>(x), x.stride(0), P<const __nv_bfloat16>(w), (int)x.size(0),
+                    (int)x.size(1), (float)eps, P<__nv_bfloat16>(y), y.stride(0), stream()),
+        "rmsnorm");
+}
+
+// ------------------------------------------------------------------------------------------------- KDA
+// seq: int32 [5, B] device tensor: rows row0, nrows, state-in index, state-out index, conv slot
+KdaArgs kda_args(const Tensor& proj, const Tensor& seq, int64_t max_rows, int64_t H, int64_t Dh, int64_t taps) {
+  KdaArgs a{};
+  a.proj = P<const __nv_bfloat16>(proj);
+  a.ldp = proj.stride(0);
+  TORCH_CHECK(seq.scalar_type() == at::kInt && seq.dim() == 2 && seq.size(0) == 5 && seq.stride(1) == 1,
+              "seq must be int32 [5, B] (rows contiguous)");
+  const int B = (int)seq.size(1);
+  const int64_t ld = seq.stride(0);
+  const int* s = P<const int>(seq);
+  a.row0 = s; a.nrows = s + ld; a.s_in = s + 2 * ld; a.s_out = s + 3 * ld; a.conv_slot = s + 4 * ld;
+  a.B = B;
+  a.max_rows = (int)max_rows;
+  a.R = (int)proj.size(0);
+  a.H = (int)H; a.Dh = (int)Dh; a.taps = (int)taps;
+  return a;
+}
+
+void kda_conv(const Tensor& proj, const Tensor& seq, int64_t max_rows, const Tensor& conv_w, const Tensor& conv_pool,
+              const Tensor& qkv, int64_t H, int64_t Dh) {
+  KdaArgs a = kda_args(proj, seq, max_rows, H, Dh, conv_w.size(1));
+  a.conv_w = P<const float>(conv_w);
+  a.conv_pool = P<__nv_bfloat16>(conv_pool);
+  a.qkv = P<__nv_bfloat16>(qkv);
+  check(g53_kda_conv(a, stream()), "kda_conv");
+}
+
+void kda_conv_commit(const Tensor& proj, const Tensor& seq, const Tensor& conv_pool, int64_t H, int64_t Dh,
+                     int64_t taps) {
+  KdaArgs a = kda_args(proj, seq, 0, H, Dh, taps);
+  a.conv_pool = P<__nv_bfloat16>(conv_pool);
+  check(g53_kda_conv_commit(a, stream()), "kda_conv_commit");
+}
+
+void kda_recurrent(const Tensor& proj, const Tensor& seq, const Tensor& f, const Tensor& qkv, const Tensor& a_log,
+                   const Tensor& dt_bias, const Tensor& S_pool, const OptT& o_raw, int64_t H, int64_t Dh,
+                   int64_t b_off, double lower) {
+  KdaArgs a = kda_args(proj, seq, 0, H, Dh, 0);
+  a.f = P<const __nv_bfloat16>(f);
+  a.qkv = P<__nv_bfloat16>(qkv);
+  a.a_log = P<const float>(a_log);
+  a.dt_bias = P<const float>(dt_bias);
+  a.S_pool = P<float>(S_pool);
+  a.o_raw = P<float>(o_raw);
+  a.b_off = (int)b_off;
+  a.lower = (float)lower;
+  check(g53_kda_recurrent(a, stream()), "kda_recurrent");
+}
+
+void kda_gated_norm(const Tensor& o_raw, const Tensor& gate, const Tensor& o_norm, const Tensor& out, int64_t H,
+                    int64_t Dh, double eps) {
+  KdaArgs a{};
+  a.o_raw = P<float>(o_raw);
+  a.gate = P<const __nv_bfloat16>(gate);
+  a.o_norm = P<const __nv_bfloat16>(o_norm);
+  a.out = P<__nv_bfloat16>(out);
+  a.R = (int)out.size(0);
+  a.H = (int)H; a.Dh = (int)Dh; a.eps = (float)eps;
+  check(g53_kda_gated_norm(a, stream()), "kda_gated_norm");
+}
+
+// ------------------------------------------------------------------------------------------------- MLA / DSA
+void mla_prep(const Tensor& qkv_a, const Tensor& q_norm, const Tensor& kv_norm, const Tensor& qr,
+              const Tensor& kv_cache, const Tensor& kv_scale, const OptT& kpe_cache, const Tensor& slots,
+              const Tensor& positions, int64_t q_lora, int64_t kv_lora, int64_t rope, double eps, double theta) {
+  MlaPrepArgs a{};
+  a.qkv_a = P<const __nv_bfloat16>(qkv_a);
+  a.ld = qkv_a.stride(0);
+  a.q_norm = P<const __nv_bfloat16>(q_norm);
+  a.kv_norm = P<const __nv_bfloat16>(kv_norm);
+  a.qr = P<__nv_bfloat16>(qr);
+  a.kv_cache = P<uint8_t>(kv_cache);
+  a.kv_scale = P<float>(kv_scale);
+  a.kpe_cache = P<__nv_bfloat16>(kpe_cache);
+  a.slots = P<const int>(slots);
+  a.positions = P<const int>(positions);
+  a.R = (int)qkv_a.size(0);
+  a.q_lora = (int)q_lora; a.kv_lora = (int)kv_lora; a.rope = (int)rope;
+  a.eps = (float)eps; a.theta = (float)theta;
+  check(g53_mla_prep(a, stream()), "mla_prep");
+}
+
+void rope_q(const Tensor& q, const Tensor& positions, int64_t nope, int64_t rope, double theta) {
+  TORCH_CHECK(q.is_contiguous() && q.dim() == 3);
+  check(g53_rope_q(P<__nv_bfloat16>(q), (int)q.size(0), (int)q.size(1), (int)q.size(2), (int)nope, (int)rope,
+                   P<const int>(positions), (float)theta, stream()),
+        "rope_q");
+}
+
+void mla_decode(const Tensor& q_lat, const OptT& q_pe, int64_t q_pe_ld, int64_t q_pe_hs, const Tensor& kv_cache,
+                const Tensor& kv_scale, const OptT& kpe_cache, const Tensor& sel, const Tensor& sel_count,
+                int64_t rope, double sm_scale, int64_t splits, const Tensor& part_o, const Tensor& part_ml,
+                const Tensor& o_lat) {
+  MlaAttnArgs a{};
+  a.q_lat = P<const __nv_bfloat16>(q_lat);
+  a.q_pe = P<const __nv_bfloat16>(q_pe);
+  a.q_pe_ld = q_pe_ld;
+  a.q_pe_hs = (int)q_pe_hs;
+  a.kv_cache = P<const uint8_t>(kv_cache);
+  a.kv_scale = P<const float>(kv_scale);
+  a.kpe_cache = P<const __nv_bfloat16>(kpe_cache);
+  a.sel = P<const int>(sel);
+  a.sel_count = P<const int>(sel_count);
+  a.max_sel = (int)sel.size(1);
+  a.R = (int)q_lat.size(0);
+  a.H = (int)q_lat.size(1);
+  a.L = (int)q_lat.size(2);
+  a.rope = (int)rope;
+  a.sm_scale = (float)sm_scale;
+  a.splits = (int)splits;
+  a.part_o = P<float>(part_o);
+  a.part_ml = P<float>(part_ml);
+  a.o_lat = P<__nv_bfloat16>(o_lat);
+  TORCH_CHECK(part_o.numel() >= (int64_t)a.R * a.splits * a.H * a.L, "part_o too small");
+  check(g53_mla_decode(a, stream()), "mla_decode");
+}
+
+DsaArgs dsa_args(const Tensor& iproj, const Tensor& ln_w, const Tensor& ln_b, const Tensor& ape, const OptT& qi,
+                 const Tensor& ik_cache, const Tensor& ig_cache, const Tensor& pool_cache, const Tensor& pool_scale,
+                 const Tensor& slots, const Tensor& positions, const Tensor& block_table, const Tensor& row_seq,
+                 int64_t block_size, int64_t IH, int64_t kpool, int64_t topk_pools, double eps, const OptT& logits,
+                 const OptT& sel, const OptT& sel_count) {
+  DsaArgs a{};
+  a.iproj = P<const float>(iproj);
+  a.ldi = iproj.stride(0);
+  a.ln_w = P<const float>(ln_w);
+  a.ln_b = P<const float>(ln_b);
+  a.ape = P<const float>(ape);
+  a.qi = P<const __nv_bfloat16>(qi);
+  a.ik_cache = P<__nv_bfloat16>(ik_cache);
+  a.ig_cache = P<float>(ig_cache);
+  a.pool_cache = P<uint8_t>(pool_cache);
+  a.pool_scale = P<float>(pool_scale);
+  a.slots = P<const int>(slots);
+  a.positions = P<const int>(positions);
+  a.block_table = P<const int>(block_table);
+  a.row_seq = P<const int>(row_seq);
+  a.bt_ld = block_table.dim() == 2 ? (int)block_table.stride(0) : 0;
+  a.block_size = (int)block_size;
+  a.R = (int)iproj.size(0);
+  a.IH = (int)IH;
+  a.ID = (int)ln_w.size(0);
+  a.kpool = (int)kpool;
+  a.topk_pools = (int)topk_pools;
+  a.eps = (float)eps;
+  a.logits = P<float>(logits);
+  a.max_pools = (logits.has_value() && logits->defined()) ? (int)logits->size(1) : 0;
+  a.sel = P<int>(sel);
+  a.sel_count = P<int>(sel_count);
+  a.max_sel = (sel.has_value() && sel->defined()) ? (int)sel->size(1) : 0;
+  return a;
+}
+
+void dsa_update(const Tensor& iproj, const Tensor& ln_w, const Tensor& ln_b, const Tensor& ape,
+                const Tensor& ik_cache, const Tensor& ig_cache, const Tensor& pool_cache, const Tensor& pool_scale,
+                const Tensor& slots, const Tensor& positions, const Tensor& block_table, const Tensor& row_seq,
+                int64_t block_size, int64_t IH, int64_t kpool, double eps) {
+  DsaArgs a = dsa_args(iproj, ln_w, ln_b, ape, {}, ik_cache, ig_cache, pool_cache, pool_scale, slots, positions,
+                       block_table, row_seq, block_size, IH, kpool, 0, eps, {}, {}, {});
+  check(g53_dsa_update(a, stream()), "dsa_update");
+}
+
+void dsa_select(const Tensor& iproj, const Tensor& qi, const Tensor& ln_w, const Tensor& pool_cache,
+                const Tensor& pool_scale, const Tensor& positions, const Tensor& block_table, const Tensor& row_seq,
+                int64_t block_size, int64_t IH, int64_t kpool, int64_t topk_pools, const Tensor& logits,
+                const Tensor& sel, const Tensor& sel_count) {
+  DsaArgs a = dsa_args(iproj, ln_w, ln_w, ln_w, qi, pool_cache, pool_scale, pool_cache, pool_scale, positions,
+                       positions, block_table, row_seq, block_size, IH, kpool, topk_pools, 0, logits, sel, sel_count);
+  a.ik_cache = nullptr;
+  a.ig_cache = nullptr;
+  check(g53_dsa_logits(a, stream()), "dsa_logits");
+  check(g53_dsa_select(a, stream()), "dsa_select");
+}
+
+// ------------------------------------------------------------------------------------------------- sampling
+void argmax_rows(const Tensor& logits, int64_t vocab_offset, const Tensor& best_val, const Tensor& best_id) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(-1) == 1);
+  check(g53_argmax_rows(P<const float>(logits), (int)logits.size(0), (int)logits.size(1), logits.stride(0),
+                        (int)vocab_offset, P<float>(best_val), P<int>(best_id), stream()),
+        "argmax_rows");
+}
+
+void greedy_verify(const Tensor& draft, const Tensor& target, bool forced, const Tensor& accepted,
+                   const Tensor& next_tokens) {
+  VerifyArgs a{};
+  a.draft = P<const int>(draft);
+  a.target_argmax = P<const int>(target);
+  a.B = (int)draft.size(0);
+  a.K = (int)draft.size(1);
+  a.forced = forced ? 1 : 0;
+  a.accepted = P<int>(accepted);
+  a.next_tokens = P<int>(next_tokens);
+  check(g53_greedy_verify(a, stream()), "greedy_verify");
+}
+
+void rejection_sample(const Tensor& target_probs, const Tensor& draft_probs, const Tensor& draft, int64_t seed,
+                      const Tensor& positions, bool block, const Tensor& accepted, const Tensor& next_tokens,
+                      const OptT& scratch) {
+  RejectArgs a{};
+  a.target_probs = P<const float>(target_probs);
+  a.draft_probs = P<const float>(draft_probs);
+  a.draft = P<const int>(draft);
+  a.B = (int)draft.size(0);
+  a.K = (int)draft.size(1);
+  a.V = (int)target_probs.size(2);
+  a.seed = (uint64_t)seed;
+  a.positions = P<const int64_t>(positions);
+  a.block = block ? 1 : 0;
+  a.accepted = P<int>(accepted);
+  a.next_tokens = P<int>(next_tokens);
+  a.scratch = P<float>(scratch);
+  check(g53_rejection_sample(a, stream()), "rejection_sample");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "glm53 sm_100a kernels";
+  m.def("gemv", &gemv);
+  m.def("moe_route", &moe_route);
+  m.def("exl3_moe", &exl3_moe);
+  m.def("moe_combine", &moe_combine);
+  m.def("exl3_unpack", &exl3_unpack);
+  m.def("hc_post_pre", &hc_post_pre);
+  m.def("embed", &embed);
+  m.def("stream_mean_norm", &stream_mean_norm);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("kda_conv", &kda_conv);
+  m.def("kda_conv_commit", &kda_conv_commit);
+  m.def("kda_recurrent", &kda_recurrent);
+  m.def("kda_gated_norm", &kda_gated_norm);
+  m.def("mla_prep", &mla_prep);
+  m.def("rope_q", &rope_q);
+  m.def("mla_decode", &mla_decode);
+  m.def("dsa_update", &dsa_update);
+  m.def("dsa_select", &dsa_select);
+  m.def("argmax_rows", &argmax_rows);
+  m.def("greedy_verify", &greedy_verify);
+  m.def("rejection_sample", &rejection_sample);
+  m.attr("GEMV_BF16") = (int)GEMV_BF16;
+  m.attr("GEMV_F32") = (int)GEMV_F32;
+  m.attr("GEMV_F32_ACC") = (int)GEMV_F32_ACC;
+  m.attr("GEMV_SWIGLU") = (int)GEMV_SWIGLU;
+}

@@ -1,0 +1,257 @@
+// DSA lightning indexer over pooled index keys.
+//
+//   update   per row: index key = LayerNorm(wk x) (bf16) and pool gate scores into the token-slot caches; rows
+//            that complete a pool of `kpool` tokens then compress it: per channel softmax over the pool's tokens
+//            of (gate + ape), weighted key sum -> bf16 -> Hadamard-128 -> bf16 -> e4m3 with a power-of-two scale
+//            (the pool lives at pool slot = token slot of its first token / kpool)
+//            (reference: code/fork/tests/kpoolring/ref/kpool_compress_vllm58454.py:139-257)
+//   logits   per (row, pool): sum_h relu((Hq_h . k_pool) * scale) * w_h / sqrt(IH * ID), the queries rotated by
+//            the same Hadamard transform (so q.k is preserved) and held in shared memory
+//   select   per row: a query sees its own (partial) pool and the top (topk_pools - 1) earlier complete pools,
+//            chosen by a 4-pass 8-bit radix select on the logits (ties: lower pool index), expanded to token
+//            slots in ascending position order; while the row has at most topk_pools - 1 complete pools it sees
+//            every earlier key (dense).
+#include "common.cuh"
+#include "launchers.h"
+
+namespace g53 {
+
+__device__ __forceinline__ int slot_of(const int* bt, int bs, int p) { return bt[p / bs] * bs + p % bs; }
+
+__global__ void __launch_bounds__(128) dsa_keys_kernel(DsaArgs a) {
+  const int r = blockIdx.x;
+  const float* x = a.iproj + (int64_t)r * a.ldi;
+  __shared__ float red[32];
+  const int c = threadIdx.x;   // ID == 128 channels, one per thread
+  const float v = x[c];
+  const float mean = block_sum(v, red) / (float)a.ID;
+  const float d = v - mean;
+  const float var = block_sum(d * d, red) / (float)a.ID;
+  const float y = d * rsqrtf(var + a.eps) * a.ln_w[c] + a.ln_b[c];
+  const int slot = a.slots[r];
+  a.ik_cache[(int64_t)slot * a.ID + c] = f2bf(y);
+  a.ig_cache[(int64_t)slot * a.ID + c] = x[a.ID + a.IH + c];
+}
+
+// one warp per row; rows whose position completes a pool compress it
+__global__ void dsa_pool_kernel(DsaArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= a.R) return;
+  const int pos = a.positions[r];
+  const int kp = a.kpool;
+  if ((pos + 1) % kp != 0) return;
+  const int p0 = pos + 1 - kp;
+  const int* bt = a.block_table + (int64_t)a.row_seq[r] * a.bt_ld;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f}, mx[4], den[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) mx[i] = -INFINITY;
+  for (int s = 0; s < kp; ++s) {
+    const int slot = slot_of(bt, a.block_size, p0 + s);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = lane * 4 + i;
+      mx[i] = fmaxf(mx[i], a.ig_cache[(int64_t)slot * a.ID + c] + a.ape[s * a.ID + c]);
+    }
+  }
+  for (int s = 0; s < kp; ++s) {
+    const int slot = slot_of(bt, a.block_size, p0 + s);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = lane * 4 + i;
+      const float e = __expf(a.ig_cache[(int64_t)slot * a.ID + c] + a.ape[s * a.ID + c] - mx[i]);
+      den[i] += e;
+      acc[i] += e * bf2f(a.ik_cache[(int64_t)slot * a.ID + c]);
+    }
+  }
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = round_bf16(acc[i] / den[i]);
+  fwht128_warp(v);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) { v[i] = round_bf16(v[i]); amax = fmaxf(amax, fabsf(v[i])); }
+  amax = fmaxf(warp_max(amax), 1e-4f);
+  const float scale = exp2f(ceilf(log2f(amax / 448.f)));
+  const int pslot = slot_of(bt, a.block_size, p0) / kp;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_fp8_e4m3 q8(v[i] / scale);
+    a.pool_cache[(int64_t)pslot * a.ID + lane * 4 + i] = q8.__x;
+  }
+  if (lane == 0) a.pool_scale[pslot] = scale;
+}
+
+constexpr int kMaxIH = 64;
+
+__global__ void __launch_bounds__(256) dsa_logits_kernel(DsaArgs a) {
+  const int r = blockIdx.x;
+  const int pos = a.positions[r];
+  const int c = pos / a.kpool;
+  const int j = blockIdx.y * blockDim.x + threadIdx.x;
+  if ((int)(blockIdx.y * blockDim.x) >= c) return;
+  __shared__ float qs[kMaxIH][128];
+  __shared__ float hw[kMaxIH];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int h = wid; h < a.IH; h += blockDim.x >> 5) {
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = bf2f(a.qi[(int64_t)r * a.IH * 128 + h * 128 + lane * 4 + i]);
+    fwht128_warp(v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qs[h][lane * 4 + i] = round_bf16(v[i]);
+  }
+  if (threadIdx.x < a.IH) hw[threadIdx.x] = a.iproj[(int64_t)r * a.ldi + a.ID + threadIdx.x];
+  __syncthreads();
+  if (j >= c) return;
+  const int* bt = a.block_table + (int64_t)a.row_seq[r] * a.bt_ld;
+  const int pslot = slot_of(bt, a.block_size, j * a.kpool) / a.kpool;
+  const uint8_t* pk = a.pool_cache + (int64_t)pslot * 128;
+  float kv[128];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint4 w = *reinterpret_cast<const uint4*>(pk + i * 16);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t h01 = e4m3x2_to_f16x2((uint16_t)(ws[k] & 0xffffu));
+      const uint32_t h23 = e4m3x2_to_f16x2((uint16_t)(ws[k] >> 16));
+      const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+      const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+      kv[i * 16 + k * 4 + 0] = f01.x; kv[i * 16 + k * 4 + 1] = f01.y;
+      kv[i * 16 + k * 4 + 2] = f23.x; kv[i * 16 + k * 4 + 3] = f23.y;
+    }
+  }
+  const float s = a.pool_scale[pslot];
+  float logit = 0.f;
+  for (int h = 0; h < a.IH; ++h) {
+    float d = 0.f;
+#pragma unroll
+    for (int i = 0; i < 128; ++i) d += qs[h][i] * kv[i];
+    logit += fmaxf(d * s, 0.f) * hw[h];
+  }
+  a.logits[(int64_t)r * a.max_pools + j] = logit * rsqrtf((float)(a.IH * a.ID));
+}
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// exclusive scan of an int over the block (blockDim multiple of 32, <= 1024); returns (prefix, total)
+__device__ __forceinline__ int2 block_scan(int v, int* wsum) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) wsum[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    int t = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    if (lane < nw) wsum[lane] = t;   // inclusive warp-total prefix
+  }
+  __syncthreads();
+  const int before = wid > 0 ? wsum[wid - 1] : 0;
+  const int total = wsum[nw - 1];
+  return make_int2(before + x - v, total);
+}
+
+__global__ void __launch_bounds__(1024) dsa_select_kernel(DsaArgs a) {
+  const int r = blockIdx.x;
+  const int tid = threadIdx.x, bd = blockDim.x;
+  const int pos = a.positions[r];
+  const int kp = a.kpool, P = a.topk_pools;
+  const int c = pos / kp;
+  const int* bt = a.block_table + (int64_t)a.row_seq[r] * a.bt_ld;
+  int* out = a.sel + (int64_t)r * a.max_sel;
+  if (c <= P - 1) {
+    for (int p = tid; p <= pos; p += bd) out[p] = slot_of(bt, a.block_size, p);
+    if (tid == 0) a.sel_count[r] = pos + 1;
+    return;
+  }
+  const int K = P - 1;
+  const float* lg = a.logits + (int64_t)r * a.max_pools;
+  __shared__ int hist[256];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_rem;
+  __shared__ int wsum[32];
+  uint32_t prefix = 0u, mask = 0u;
+  int rem = K;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = tid; i < 256; i += bd) hist[i] = 0;
+    __syncthreads();
+    for (int j = tid; j < c; j += bd) {
+      const uint32_t u = order_key(lg[j]);
+      if ((u & mask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int acc = 0, b = 255;
+      for (; b > 0; --b) {
+        if (acc + hist[b] >= rem) break;
+        acc += hist[b];
+      }
+      s_prefix = prefix | ((uint32_t)b << shift);
+      s_rem = rem - acc;
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    rem = s_rem;
+    mask |= 255u << shift;
+  }
+  int base_eq = 0, base_sel = 0;
+  for (int j0 = 0; j0 < c; j0 += bd) {
+    const int j = j0 + tid;
+    const uint32_t u = j < c ? order_key(lg[j]) : 0u;
+    const int eq = (j < c) && (u == prefix);
+    const int gt = (j < c) && (u > prefix);
+    const int2 se = block_scan(eq, wsum);
+    const int selected = gt || (eq && (base_eq + se.x) < rem);
+    const int2 ss = block_scan(selected, wsum);
+    if (selected) {
+      const int o = (base_sel + ss.x) * kp;
+      for (int i = 0; i < kp; ++i) out[o + i] = slot_of(bt, a.block_size, j * kp + i);
+    }
+    base_eq += se.y;
+    base_sel += ss.y;
+  }
+  for (int p = c * kp + tid; p <= pos; p += bd) out[K * kp + (p - c * kp)] = slot_of(bt, a.block_size, p);
+  if (tid == 0) a.sel_count[r] = K * kp + (pos - c * kp + 1);
+}
+
+}  // namespace g53
+
+using namespace g53;
+
+cudaError_t g53_dsa_update(const DsaArgs& a, cudaStream_t st) {
+  if (a.ID != 128) return cudaErrorInvalidValue;
+  dsa_keys_kernel<<<a.R, 128, 0, st>>>(a);
+  G53_CHECK_LAUNCH();
+  dsa_pool_kernel<<<(a.R + 7) / 8, 256, 0, st>>>(a);
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}
+
+cudaError_t g53_dsa_logits(const DsaArgs& a, cudaStream_t st) {
+  if (a.ID != 128 || a.IH > kMaxIH) return cudaErrorInvalidValue;
+  dim3 grid(a.R, (a.max_pools + 255) / 256);
+  dsa_logits_kernel<<<grid, 256, 0, st>>>(a);
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}
+
+cudaError_t g53_dsa_select(const DsaArgs& a, cudaStream_t st) {
+  dsa_select_kernel<<<a.R, 1024, 0, st>>>(a);
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}

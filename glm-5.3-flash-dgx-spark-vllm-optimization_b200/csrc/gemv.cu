@@ -1,0 +1,171 @@
+// Small-M GEMM ("GEMV") for decode: Y[M, N] = X[M, K] @ W[N, K]^T with M <= 16 activation rows.
+//
+// Weight-stationary, swap-AB on tensor cores: the weight tile is the 16-row A operand of mma.m16n8k16 and the
+// (at most 16) activation rows are the 8-wide B operand, so every weight byte is loaded once, by one lane, with
+// 16-byte loads, and the tensor core does the multiply (CUDA-core FMA would be compute-bound at M = 8).  The
+// reduction dimension is permuted inside every 64-element chunk identically for A and B (a dot product does not
+// depend on the order), which lets lane (g, q) read 16 contiguous bytes of weight rows g and g+8 and 16
+// contiguous activations of token g for four consecutive mma steps.
+//
+// Weights: fp8 e4m3 with an fp32 scale per output row (converted exactly to f16 in registers; activations bf16
+// converted to f16 -- exact in f16's normal range), or bf16 (router / indexer projections, bf16 mma).
+// K is split across the warps of a CTA; the partial tiles are summed in a fixed order (deterministic).
+//
+// Reference counterparts: code/fork/kernels/fp8_gemv.cu:96 (Marlin-layout fp8 GEMV, M <= 64) and
+// code/fork/kernels/gemv_bf16.cu:83 (router / small bf16 GEMM).
+#include "common.cuh"
+#include "launchers.h"
+
+namespace g53 {
+
+template <bool FP8, int KS, int NT>
+__global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
+  constexpr int CH = FP8 ? 64 : 32;            // k elements per lane-load chunk (16 bytes of weight)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int ks = warp % KS, tile = warp / KS;
+  const int b = blockIdx.y;
+  const int n0 = (blockIdx.x * NT + tile) * 16;
+  const int nchunk = p.K / CH;
+  const bool two = p.M > 8;
+
+  const uint8_t* wbase = reinterpret_cast<const uint8_t*>(p.w) + (int64_t)b * p.bsw * (FP8 ? 1 : 2);
+  const __nv_bfloat16* xb = p.x + (int64_t)b * p.bsx;
+  const int esz = FP8 ? 1 : 2;
+  const bool rA = (n0 + g) < p.N, rB = (n0 + g + 8) < p.N;
+  const uint8_t* wr0 = wbase + ((int64_t)(n0 + g) * p.K) * esz;
+  const uint8_t* wr1 = wbase + ((int64_t)(n0 + g + 8) * p.K) * esz;
+  const bool t0 = g < p.M, t1 = (g + 8) < p.M;
+  const __nv_bfloat16* x0 = xb + (int64_t)g * p.ldx;
+  const __nv_bfloat16* x1 = xb + (int64_t)(g + 8) * p.ldx;
+
+  float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint4 z4 = make_uint4(0, 0, 0, 0);
+
+#pragma unroll 4
+  for (int c = ks; c < nchunk; c += KS) {
+    const int kb = c * CH + q * (CH / 4);
+    uint4 wa = rA ? ldg_nc_v4(wr0 + (int64_t)kb * esz) : z4;
+    uint4 wb = rB ? ldg_nc_v4(wr1 + (int64_t)kb * esz) : z4;
+    if constexpr (FP8) {
+      // 16 activations per lane (two 16-byte loads), for tokens g and g+8
+      uint4 xa0 = t0 ? *reinterpret_cast<const uint4*>(x0 + kb) : z4;
+      uint4 xa1 = t0 ? *reinterpret_cast<const uint4*>(x0 + kb + 8) : z4;
+      uint4 xc0 = z4, xc1 = z4;
+      if (two && t1) {
+        xc0 = *reinterpret_cast<const uint4*>(x1 + kb);
+        xc1 = *reinterpret_cast<const uint4*>(x1 + kb + 8);
+      }
+      const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
+      const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+      const uint32_t xav[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
+      const uint32_t xcv[8] = {xc0.x, xc0.y, xc0.z, xc0.w, xc1.x, xc1.y, xc1.z, xc1.w};
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        uint32_t a[4];
+        a[0] = e4m3x2_to_f16x2((uint16_t)(wav[s] & 0xffffu));
+        a[1] = e4m3x2_to_f16x2((uint16_t)(wbv[s] & 0xffffu));
+        a[2] = e4m3x2_to_f16x2((uint16_t)(wav[s] >> 16));
+        a[3] = e4m3x2_to_f16x2((uint16_t)(wbv[s] >> 16));
+        mma_f16_16816(acc0, a, bf16x2_to_f16x2(xav[2 * s]), bf16x2_to_f16x2(xav[2 * s + 1]));
+        if (two) mma_f16_16816(acc1, a, bf16x2_to_f16x2(xcv[2 * s]), bf16x2_to_f16x2(xcv[2 * s + 1]));
+      }
+    } else {
+      uint4 xa = t0 ? *reinterpret_cast<const uint4*>(x0 + kb) : z4;
+      uint4 xc = (two && t1) ? *reinterpret_cast<const uint4*>(x1 + kb) : z4;
+      const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
+      const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+      const uint32_t xav[4] = {xa.x, xa.y, xa.z, xa.w};
+      const uint32_t xcv[4] = {xc.x, xc.y, xc.z, xc.w};
+#pragma unroll
+      for (int s = 0; s < 2; ++s) {
+        uint32_t a[4] = {wav[2 * s], wbv[2 * s], wav[2 * s + 1], wbv[2 * s + 1]};
+        mma_bf16_16816(acc0, a, xav[2 * s], xav[2 * s + 1]);
+        if (two) mma_bf16_16816(acc1, a, xcv[2 * s], xcv[2 * s + 1]);
+      }
+    }
+  }
+
+  // cross-warp (split-K) reduction in fixed order
+  __shared__ float red[KS][NT][16][17];
+  __shared__ float red2[KS][NT][16][17];
+  red[ks][tile][g][2 * q] = acc0[0];
+  red[ks][tile][g][2 * q + 1] = acc0[1];
+  red[ks][tile][g + 8][2 * q] = acc0[2];
+  red[ks][tile][g + 8][2 * q + 1] = acc0[3];
+  if (two) {
+    red2[ks][tile][g][2 * q] = acc1[0];
+    red2[ks][tile][g][2 * q + 1] = acc1[1];
+    red2[ks][tile][g + 8][2 * q] = acc1[2];
+    red2[ks][tile][g + 8][2 * q + 1] = acc1[3];
+  }
+  __syncthreads();
+  const float* scale = p.scale ? p.scale + (int64_t)b * p.bss : nullptr;
+  if (p.mode == GEMV_SWIGLU) {
+    // rows 0..7 of every 16-row tile are gate rows j0..j0+7, rows 8..15 the matching up rows
+    for (int e = threadIdx.x; e < NT * 8 * 16; e += blockDim.x) {
+      const int t = e / (8 * 16), r = (e / 16) % 8, tok = e % 16;
+      if (tok >= p.M) continue;
+      const int nt0 = (blockIdx.x * NT + t) * 16;
+      if (nt0 + r + 8 >= p.N) continue;
+      float gv = 0.f, uv = 0.f;
+#pragma unroll
+      for (int s = 0; s < KS; ++s) {
+        gv += tok < 8 ? red[s][t][r][tok] : red2[s][t][r][tok - 8];
+        uv += tok < 8 ? red[s][t][r + 8][tok] : red2[s][t][r + 8][tok - 8];
+      }
+      if (scale) { gv *= scale[nt0 + r]; uv *= scale[nt0 + r + 8]; }
+      // y stored as bf16 values of g and u first (the MLP output rounding points), then the activation
+      gv = round_bf16(gv);
+      uv = round_bf16(uv);
+      gv = fminf(gv, p.limit);
+      uv = fminf(fmaxf(uv, -p.limit), p.limit);
+      const float act = siluf_(gv) * uv;
+      __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.y) + (int64_t)b * p.bsy;
+      y[(int64_t)tok * p.ldy + (nt0 >> 1) + r] = f2bf(act);
+    }
+    return;
+  }
+  for (int e = threadIdx.x; e < NT * 16 * 16; e += blockDim.x) {
+    const int t = e / 256, r = (e / 16) % 16, tok = e % 16;
+    const int n = (blockIdx.x * NT + t) * 16 + r;
+    if (tok >= p.M || n >= p.N) continue;
+    float v = 0.f;
+#pragma unroll
+    for (int s = 0; s < KS; ++s) v += tok < 8 ? red[s][t][r][tok] : red2[s][t][r][tok - 8];
+    if (scale) v *= scale[n];
+    const int64_t off = (int64_t)b * p.bsy + (int64_t)tok * p.ldy + n;
+    if (p.mode == GEMV_BF16) {
+      reinterpret_cast<__nv_bfloat16*>(p.y)[off] = f2bf(v);
+    } else if (p.mode == GEMV_F32) {
+      reinterpret_cast<float*>(p.y)[off] = v;
+    } else {  // GEMV_F32_ACC
+      reinterpret_cast<float*>(p.y)[off] += v;
+    }
+  }
+}
+
+template <bool FP8>
+static cudaError_t launch_gemv_t(const GemvArgs& p, cudaStream_t st) {
+  const int CH = FP8 ? 64 : 32;
+  if (p.K % CH != 0 || p.M < 1 || p.M > 16) return cudaErrorInvalidValue;
+  const int nchunk = p.K / CH;
+  int ks = 8;
+  while (ks > 1 && nchunk < ks * 2) ks >>= 1;
+  const int tiles = (p.N + 15) / 16;
+  const int nt = 8 / ks;
+  dim3 grid((tiles + nt - 1) / nt, p.batch);
+  switch (ks) {
+    case 8: gemv_kernel<FP8, 8, 1><<<grid, 256, 0, st>>>(p); break;
+    case 4: gemv_kernel<FP8, 4, 2><<<grid, 256, 0, st>>>(p); break;
+    case 2: gemv_kernel<FP8, 2, 4><<<grid, 256, 0, st>>>(p); break;
+    default: gemv_kernel<FP8, 1, 8><<<grid, 256, 0, st>>>(p); break;
+  }
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}
+
+}  // namespace g53
+
+cudaError_t g53_gemv_fp8(const GemvArgs& p, cudaStream_t st) { return g53::launch_gemv_t<true>(p, st); }
+cudaError_t g53_gemv_bf16(const GemvArgs& p, cudaStream_t st) { return g53::launch_gemv_t<false>(p, st); }

@@ -1,0 +1,184 @@
+// Kimi delta attention (KDA): causal depthwise conv, the recurrent delta-rule step, the gated output norm.
+//
+// Recurrence per head (state S[v][k], fp32), for each row t in order (code/fork/glm53_kda_lazy.py:160-178):
+//   q, k <- l2-normalised (q * Dh^-1/2); g = lower * sigmoid(exp(A_log) * (f + dt_bias)); S <- S * exp(g)[k]
+//   v' = sigmoid(b) * (v - S k); S <- S + v' k^T; o = S q
+// Window design for speculative verification: the kernel reads the committed state S_in and writes the state
+// after its last row to S_out (the other buffer of a double buffer) and never writes S_in, so a verify window of
+// R rows needs no per-row state stores; committing fewer rows (keep < R) re-runs the kernel on the first `keep`
+// rows (their conv outputs stay in the layer's qkv scratch) into S_out.  This is the reference's "lazy commit"
+// (code/fork/glm53_kda_lazy.py:1-30) built into the kernel contract.
+//
+// Mapping: CTA = (head, 32 value rows); thread (vr, kq) owns S[vr][kq*Dh/4 .. +Dh/4); dot products over k are
+// reduced over the 4 threads of a row group.
+#include "common.cuh"
+#include "launchers.h"
+
+namespace g53 {
+
+constexpr int kConvRB = 64;   // rows per conv thread
+
+// grid (channel blocks, row blocks, sequences)
+__global__ void kda_conv_kernel(KdaArgs a) {
+  const int C = 3 * a.H * a.Dh;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.z;
+  if (c >= C) return;
+  const int base = a.row0[b], n = a.nrows[b];
+  const int t0 = blockIdx.y * kConvRB;
+  if (t0 >= n) return;
+  const int t1 = min(t0 + kConvRB, n);
+  const int T = a.taps;   // <= 8
+  const __nv_bfloat16* win = a.conv_pool + (int64_t)a.conv_slot[b] * (T - 1) * C;
+  float w[8], hist[8];
+  for (int i = 0; i < T; ++i) w[i] = a.conv_w[(int64_t)c * T + i];
+  for (int i = 0; i < T - 1; ++i) {
+    const int t = t0 - (T - 1) + i;
+    hist[i] = t < 0 ? bf2f(win[(int64_t)(T - 1 + t) * C + c]) : bf2f(a.proj[(int64_t)(base + t) * a.ldp + c]);
+  }
+  for (int t = t0; t < t1; ++t) {
+    hist[T - 1] = bf2f(a.proj[(int64_t)(base + t) * a.ldp + c]);
+    float s = 0.f;
+    for (int i = 0; i < T; ++i) s += w[i] * hist[i];
+    a.qkv[(int64_t)(base + t) * C + c] = f2bf(siluf_(s));
+    for (int i = 0; i < T - 1; ++i) hist[i] = hist[i + 1];
+  }
+}
+
+// grid (channel blocks, sequences): window <- last taps-1 rows of [window ; proj rows 0..nrows-1]
+__global__ void kda_conv_commit_kernel(KdaArgs a) {
+  const int C = 3 * a.H * a.Dh;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.y;
+  if (c >= C) return;
+  const int T = a.taps;
+  const int base = a.row0[b], keep = a.nrows[b];
+  __nv_bfloat16* win = a.conv_pool + (int64_t)a.conv_slot[b] * (T - 1) * C;
+  float rows[8];
+  for (int i = 0; i < T - 1; ++i) {
+    const int idx = keep + i;
+    rows[i] = idx < T - 1 ? bf2f(win[(int64_t)idx * C + c]) : bf2f(a.proj[(int64_t)(base + idx - (T - 1)) * a.ldp + c]);
+  }
+  for (int i = 0; i < T - 1; ++i) win[(int64_t)i * C + c] = f2bf(rows[i]);
+}
+
+// grid (H, Dh/32, sequences)
+template <int DH>
+__global__ void __launch_bounds__(128) kda_recurrent_kernel(KdaArgs a) {
+  constexpr int KP = DH / 4;
+  const int h = blockIdx.x, b = blockIdx.z;
+  const int vr = threadIdx.x >> 2, kq = threadIdx.x & 3;
+  const int v = blockIdx.y * 32 + vr;
+  const int k0 = kq * KP;
+  const int HD = a.H * DH;
+  const int base = a.row0[b], n = a.nrows[b];
+  const int64_t sstride = (int64_t)a.H * DH * DH;
+  float S[KP];
+  const float* sin = a.S_pool + a.s_in[b] * sstride + ((int64_t)h * DH + v) * DH + k0;
+#pragma unroll
+  for (int j = 0; j < KP; j += 4) {
+    const float4 t = *reinterpret_cast<const float4*>(sin + j);
+    S[j] = t.x; S[j + 1] = t.y; S[j + 2] = t.z; S[j + 3] = t.w;
+  }
+  const float ea = __expf(a.a_log[h]);
+  float dtb[KP];
+#pragma unroll
+  for (int j = 0; j < KP; ++j) dtb[j] = a.dt_bias[h * DH + k0 + j];
+  for (int tt = 0; tt < n; ++tt) {
+    const int t = base + tt;
+    const __nv_bfloat16* row = a.qkv + (int64_t)t * 3 * HD;
+    float q[KP], k[KP];
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int j = 0; j < KP; ++j) {
+      q[j] = bf2f(row[h * DH + k0 + j]);
+      k[j] = bf2f(row[HD + h * DH + k0 + j]);
+      sq += q[j] * q[j];
+      sk += k[j] * k[j];
+    }
+    sq = group_sum<4>(sq);
+    sk = group_sum<4>(sk);
+    const float qn = rsqrtf(sq + 1e-6f) * rsqrtf((float)DH);
+    const float kn = rsqrtf(sk + 1e-6f);
+    const float vv = bf2f(row[2 * HD + h * DH + v]);
+    const float beta = sigmoidf_(bf2f(a.proj[(int64_t)t * a.ldp + a.b_off + h]));
+    const __nv_bfloat16* fr = a.f + (int64_t)t * HD + h * DH + k0;
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < KP; ++j) {
+      const float g = a.lower * sigmoidf_(ea * (bf2f(fr[j]) + dtb[j]));
+      S[j] *= __expf(g);
+      k[j] *= kn;
+      q[j] *= qn;
+      dot += S[j] * k[j];
+    }
+    dot = group_sum<4>(dot);
+    const float vn = beta * (vv - dot);
+    float o = 0.f;
+#pragma unroll
+    for (int j = 0; j < KP; ++j) {
+      S[j] += vn * k[j];
+      o += S[j] * q[j];
+    }
+    o = group_sum<4>(o);
+    if (a.o_raw && kq == 0) a.o_raw[(int64_t)t * HD + h * DH + v] = o;
+  }
+  float* sout = a.S_pool + a.s_out[b] * sstride + ((int64_t)h * DH + v) * DH + k0;
+#pragma unroll
+  for (int j = 0; j < KP; j += 4) *reinterpret_cast<float4*>(sout + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+}
+
+// one warp per (row, head)
+__global__ void kda_gated_norm_kernel(KdaArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int idx = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (idx >= a.R * a.H) return;
+  const int t = idx / a.H, h = idx % a.H;
+  const int HD = a.H * a.Dh;
+  const float* o = a.o_raw + (int64_t)t * HD + h * a.Dh;
+  float ss = 0.f;
+  for (int i = lane; i < a.Dh; i += 32) ss += o[i] * o[i];
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)a.Dh + a.eps);
+  const __nv_bfloat16* gt = a.gate + (int64_t)t * HD + h * a.Dh;
+  for (int i = lane; i < a.Dh; i += 32)
+    a.out[(int64_t)t * HD + h * a.Dh + i] = f2bf(o[i] * r * bf2f(a.o_norm[i]) * sigmoidf_(bf2f(gt[i])));
+}
+
+}  // namespace g53
+
+using namespace g53;
+
+cudaError_t g53_kda_conv(const KdaArgs& a, cudaStream_t st) {
+  if (a.taps > 8 || a.taps < 2) return cudaErrorInvalidValue;
+  const int C = 3 * a.H * a.Dh;
+  dim3 grid((C + 255) / 256, (a.max_rows + kConvRB - 1) / kConvRB, a.B);
+  kda_conv_kernel<<<grid, 256, 0, st>>>(a);
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}
+
+cudaError_t g53_kda_conv_commit(const KdaArgs& a, cudaStream_t st) {
+  if (a.taps > 8 || a.taps < 2) return cudaErrorInvalidValue;
+  const int C = 3 * a.H * a.Dh;
+  dim3 grid((C + 255) / 256, a.B);
+  kda_conv_commit_kernel<<<grid, 256, 0, st>>>(a);
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}
+
+cudaError_t g53_kda_recurrent(const KdaArgs& a, cudaStream_t st) {
+  dim3 grid(a.H, a.Dh / 32, a.B);
+  if (a.Dh == 128) kda_recurrent_kernel<128><<<grid, 128, 0, st>>>(a);
+  else if (a.Dh == 64) kda_recurrent_kernel<64><<<grid, 128, 0, st>>>(a);
+  else return cudaErrorInvalidValue;
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}
+
+cudaError_t g53_kda_gated_norm(const KdaArgs& a, cudaStream_t st) {
+  const int warps = a.R * a.H;
+  kda_gated_norm_kernel<<<(warps + 7) / 8, 256, 0, st>>>(a);
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}

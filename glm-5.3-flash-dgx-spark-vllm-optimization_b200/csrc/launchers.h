@@ -1,0 +1,207 @@
+// Host-side launch interface of the glm53 CUDA kernels (raw pointers + stream; no torch headers, so the .cu
+// files compile fast). bindings.cpp wraps these for Python.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+// ---------------------------------------------------------------- small-M GEMM (gemv.cu)
+enum GemvMode { GEMV_BF16 = 0, GEMV_F32 = 1, GEMV_F32_ACC = 2, GEMV_SWIGLU = 3 };
+
+struct GemvArgs {
+  const __nv_bfloat16* x; int64_t ldx; int64_t bsx;   // activations [batch][M][K] (row stride ldx)
+  const void* w; int64_t bsw;                          // weights [batch][N][K] (fp8 bytes or bf16)
+  const float* scale; int64_t bss;                     // per-row scale [batch][N] (may be null for bf16)
+  void* y; int64_t ldy; int64_t bsy;                   // output [batch][M][ldy]
+  int M, N, K, batch;
+  int mode;
+  float limit;                                         // SwiGLU clamp
+};
+cudaError_t g53_gemv_fp8(const GemvArgs& p, cudaStream_t st);
+cudaError_t g53_gemv_bf16(const GemvArgs& p, cudaStream_t st);
+
+// ---------------------------------------------------------------- MoE (moe.cu)
+struct RouteArgs {
+  const float* logits;        // [R, E] fp32 router logits
+  const float* bias;          // [E]
+  int R, E, top_k;
+  float scale; int norm;
+  int* topk_ids;              // [R, top_k]
+  float* topk_w;              // [R, top_k]
+  // grouping (sorted by expert, then row-major pair index)
+  int* group_count;           // [1]   number of distinct experts U
+  int* group_expert;          // [max_groups]
+  int* group_offset;          // [max_groups + 1]
+  int* pair_token;            // [R*top_k] token row of each sorted pair
+  int* pair_expert;           // [R*top_k] expert of each sorted pair
+  float* pair_w;              // [R*top_k] routing weight of each sorted pair
+  int* pair_of;               // [R*top_k] sorted position of pair (r, k)
+  int max_groups;
+};
+cudaError_t g53_moe_route(const RouteArgs& a, cudaStream_t st);
+
+struct Exl3Args {
+  // x rows [T, K] (bf16) for rot_in; the experts' stacked tensors
+  const __nv_bfloat16* x; int64_t ldx;
+  const int16_t* tr_g; const __half* suh_g; const __half* svh_g;    // gate: trellis [E, K/16, N/16, 64]
+  const int16_t* tr_u; const __half* suh_u; const __half* svh_u;    // up
+  const int16_t* tr_d; const __half* suh_d; const __half* svh_d;    // down [E, N/16, D/16, 64]
+  int K;        // hidden (gate/up input, down output)
+  int N;        // local expert width (gate/up output, down input)
+  int Dout;     // down output width (== K)
+  // routing
+  const int* group_count; const int* group_expert; const int* group_offset;
+  const int* pair_token; const int* pair_expert; const float* pair_w;
+  int max_groups, pairs, top_k;
+  float limit;
+  // scratch
+  __half* xh_g; __half* xh_u;   // [pairs, K] rotated inputs
+  __half* xd;                   // [pairs, N] rotated down input
+  float* yd;                    // [pairs, Dout] weighted expert outputs
+};
+cudaError_t g53_exl3_rot_in(const Exl3Args& a, cudaStream_t st);
+cudaError_t g53_exl3_gate_up(const Exl3Args& a, cudaStream_t st);
+cudaError_t g53_exl3_down(const Exl3Args& a, cudaStream_t st);
+// out[r, :] (+)= sum_k yd[pair_of[r, k], :]  (slot order), fp32
+cudaError_t g53_moe_combine(const float* yd, const int* pair_of, int R, int top_k, int D, float* out,
+                            int accumulate, cudaStream_t st);
+// one-tile decode for tests: W_q [K, N] fp16 from trellis [K/16, N/16, 64]
+cudaError_t g53_exl3_unpack(const int16_t* tr, int K, int N, __half* out, cudaStream_t st);
+
+// ---------------------------------------------------------------- mHC / norms (mhc.cu)
+struct HcArgs {
+  __nv_bfloat16* X;           // [R, S, D] residual streams (bf16), updated in place by post
+  const float* branch;        // [R, D] fp32 branch output (post) or null (pre only)
+  const float* post; const float* comb;   // [R, S], [R, S, S] from the previous pre
+  const __nv_bfloat16* fn;    // [n_mix, S*D]
+  const float* base; const float* hscale; // [n_mix], [3]
+  const __nv_bfloat16* norm_w;  // [D]
+  __nv_bfloat16* normed;      // [R, D] out
+  float* post_out; float* comb_out;       // [R, S], [R, S, S] out
+  float* part;                // [R, NB, 32] scratch partial dots (+ sum of squares in slot n_mix)
+  int R, S, D;
+  float eps, hc_eps; int iters;
+};
+cudaError_t g53_hc_post_pre(const HcArgs& a, cudaStream_t st);   // (optional post) then pre
+cudaError_t g53_embed(const int* ids, const __nv_bfloat16* table, int R, int D, int S, __nv_bfloat16* X,
+                      cudaStream_t st);
+cudaError_t g53_stream_mean_norm(const __nv_bfloat16* X, int R, int S, int D, const __nv_bfloat16* w, float eps,
+                                 __nv_bfloat16* hidden, __nv_bfloat16* normed, cudaStream_t st);
+cudaError_t g53_rmsnorm(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* w, int R, int D, float eps,
+                        __nv_bfloat16* y, int64_t ldy, cudaStream_t st);
+
+// ---------------------------------------------------------------- KDA (kda.cu)
+struct KdaArgs {
+  const __nv_bfloat16* proj; int64_t ldp;   // [R, ldp]: q|k|v (3*H*Dh) then f_a, g_a, b (H) at b_off
+  const __nv_bfloat16* f;                    // [R, H*Dh] f_b output (decay logits)
+  const __nv_bfloat16* gate;                 // [R, H*Dh] g_b output (output gate logits)
+  const float* conv_w;                       // [3*H*Dh, taps]
+  __nv_bfloat16* conv_pool;                  // [slots][taps-1][3*H*Dh] conv windows (rows oldest first)
+  const float* a_log; const float* dt_bias;  // [H], [H*Dh]
+  const __nv_bfloat16* o_norm;               // [Dh]
+  float* S_pool;                             // [states][H][Dh][Dh] recurrent states (v-major)
+  __nv_bfloat16* qkv;                        // [R, 3*H*Dh] conv outputs (kept for replay)
+  float* o_raw;                              // [R, H*Dh] recurrent outputs before the gated norm (may be null)
+  __nv_bfloat16* out;                        // [R, H*Dh] gated-normed output
+  // sequences of the launch: rows [row0[b], row0[b] + nrows[b])
+  const int* row0; const int* nrows;         // [B]
+  const int* s_in; const int* s_out;         // [B] state pool index read / written
+  const int* conv_slot;                      // [B] conv pool slot
+  int B, max_rows;                           // sequences, max rows of one sequence
+  int R, H, Dh, taps, b_off;
+  float lower, eps;
+};
+cudaError_t g53_kda_conv(const KdaArgs& a, cudaStream_t st);          // qkv = silu(conv(window ++ proj rows))
+cudaError_t g53_kda_recurrent(const KdaArgs& a, cudaStream_t st);     // per sequence: S_in -> S_out, o_raw
+cudaError_t g53_kda_gated_norm(const KdaArgs& a, cudaStream_t st);    // out = rmsnorm(o_raw) * w * sigmoid(gate)
+cudaError_t g53_kda_conv_commit(const KdaArgs& a, cudaStream_t st);   // window <- last taps-1 of window ++ nrows rows
+struct KdaChunkArgs {
+  const __nv_bfloat16* qkv;    // [T, 3*H*Dh] post-conv q|k|v (bf16)
+  const __nv_bfloat16* f; const __nv_bfloat16* proj; int64_t ldp;
+  const float* a_log; const float* dt_bias;
+  float* S;                    // [H, Dh, Dh] in/out state
+  float* o_raw;                // [T, H*Dh]
+  int T, H, Dh, b_off, chunk;
+  float lower;
+};
+cudaError_t g53_kda_chunk(const KdaChunkArgs& a, cudaStream_t st);
+
+// ---------------------------------------------------------------- MLA / DSA (mla.cu, dsa.cu)
+struct MlaPrepArgs {
+  const __nv_bfloat16* qkv_a; int64_t ld;    // [R, q_lora + kv_lora + rope]
+  const __nv_bfloat16* q_norm; const __nv_bfloat16* kv_norm;
+  __nv_bfloat16* qr;                          // [R, q_lora]
+  uint8_t* kv_cache; float* kv_scale; __nv_bfloat16* kpe_cache;   // latent cache (per slot)
+  const int* slots;                           // [R] cache slot of each row
+  const int* positions;                       // [R] absolute positions (rope)
+  int R, q_lora, kv_lora, rope;
+  float eps, theta;
+};
+cudaError_t g53_mla_prep(const MlaPrepArgs& a, cudaStream_t st);
+cudaError_t g53_rope_q(__nv_bfloat16* q, int R, int H, int qk, int nope, int rope, const int* positions, float theta,
+                       cudaStream_t st);
+
+struct MlaAttnArgs {
+  const __nv_bfloat16* q_lat;   // [R, H, L] absorbed queries (bf16)
+  const __nv_bfloat16* q_pe;    // rope part of the queries: row r head h at q_pe + r*q_pe_ld + h*q_pe_hs (or null)
+  int64_t q_pe_ld; int q_pe_hs;
+  const uint8_t* kv_cache; const float* kv_scale; const __nv_bfloat16* kpe_cache;
+  const int* sel;               // [R, max_sel] selected cache slots
+  const int* sel_count;         // [R]
+  int max_sel;
+  int R, H, L, rope;
+  float sm_scale;
+  int splits;                   // key splits (flash-decoding); chunk = ceil(max_sel / splits)
+  float* part_o;                // [R, splits, H, L] scratch
+  float* part_ml;               // [R, splits, H, 2]
+  __nv_bfloat16* o_lat;         // [R, H, L] out (bf16)
+};
+cudaError_t g53_mla_decode(const MlaAttnArgs& a, cudaStream_t st);
+
+struct DsaArgs {
+  const float* iproj; int64_t ldi;  // [R, ID + IH + ID] fp32: index key | head weights | pool gate scores
+  const float* ln_w; const float* ln_b; const float* ape;   // [ID], [ID], [kpool, ID]
+  const __nv_bfloat16* qi;       // [R, IH*ID] index queries (bf16, before the Hadamard transform)
+  __nv_bfloat16* ik_cache;       // [token slots, ID] normalised index keys (bf16)
+  float* ig_cache;               // [token slots, ID] pool gate scores
+  uint8_t* pool_cache; float* pool_scale;   // [pool slots, ID] e4m3, [pool slots] power-of-two scales
+  const int* slots;              // [R] token slot of each row
+  const int* positions;          // [R] absolute position of each row
+  const int* block_table;        // token page tables [sequences, max_blocks]
+  const int* row_seq;            // [R] sequence (page-table row) of each row
+  int bt_ld;
+  int block_size;                // tokens per page (a multiple of kpool)
+  int R, IH, ID, kpool, topk_pools;
+  float eps;
+  float* logits;                 // [R, max_pools] scratch
+  int max_pools;
+  int* sel; int* sel_count; int max_sel;   // out: selected token slots per row
+};
+cudaError_t g53_dsa_update(const DsaArgs& a, cudaStream_t st);   // index keys, gate scores, completed pools
+cudaError_t g53_dsa_logits(const DsaArgs& a, cudaStream_t st);  // pool logits of every row
+cudaError_t g53_dsa_select(const DsaArgs& a, cudaStream_t st);
+
+// ---------------------------------------------------------------- sampling / verify (sample.cu)
+cudaError_t g53_argmax_rows(const float* logits, int R, int V, int64_t ld, int vocab_offset, float* best_val,
+                            int* best_id, cudaStream_t st);
+struct VerifyArgs {
+  const int* draft;          // [B, K] draft tokens
+  const int* target_argmax;  // [B, K+1] target greedy tokens per verify row
+  int B, K;
+  int forced;                // accept all K drafts (benchmark mode)
+  int* accepted;             // [B] accepted draft count
+  int* next_tokens;          // [B, K+1] emitted tokens (accepted drafts + correction/bonus)
+};
+cudaError_t g53_greedy_verify(const VerifyArgs& a, cudaStream_t st);
+struct RejectArgs {
+  const float* target_probs;   // [B, K+1, V]
+  const float* draft_probs;    // [B, K, V]
+  const int* draft;            // [B, K]
+  int B, K, V;
+  uint64_t seed; const int64_t* positions;   // [B] position of row 0
+  int block;                   // 0: standard rejection, 1: block verification
+  int* accepted; int* next_tokens;
+  float* scratch;              // [B, K+1] block acceptance stats
+};
+cudaError_t g53_rejection_sample(const RejectArgs& a, cudaStream_t st);

@@ -1,0 +1,243 @@
+// Manifold-constrained hyper-connections (mHC) with S residual streams, embedding and norms.
+//
+// hc_post_pre = (optional) mHC post of the previous block fused with mHC pre of the next one:
+//   partial  grid (D/256 column blocks, row groups): each thread owns one column d of every stream; with a branch
+//            it first writes X_s[d] = bf16(post_s * bf16(branch[d]) + sum_j comb[j, s] X_j[d]); then it adds its
+//            column's share of the n_mix mixing dots (fn rows held in registers, loaded once per CTA) and of the
+//            sum of squares; per-CTA partials are reduced in a fixed warp order
+//   finish   one CTA per row: partials summed in column-block order -> r = rsqrt(mean(X^2) + eps);
+//            pre = sigmoid + eps, post = 2 sigmoid, comb = Sinkhorn(softmax + eps); collapsed = bf16(sum pre_s X_s);
+//            normed = bf16(rmsnorm(collapsed) * w)
+// Reference counterparts: code/fork/kernels/mhc_post_prenorm.cu:34 (prefill post+prenorm) and
+// code/fork/kernels/smallops.cu:134 (decode mHC); math as code/fork/docs/ref/tf_glue.py:123-175.
+#include "common.cuh"
+#include "launchers.h"
+
+namespace g53 {
+
+constexpr int kDB = 256;     // columns per partial CTA
+constexpr int kRB = 16;      // rows per partial CTA
+constexpr int kMaxMix = 24;
+
+template <int S>
+__global__ void __launch_bounds__(kDB) hc_partial_kernel(HcArgs a) {
+  constexpr int NM = 2 * S + S * S;
+  const int d = blockIdx.x * kDB + threadIdx.x;
+  const int NB = a.D / kDB;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __shared__ float red[kDB / 32][NM + 1];
+  const bool pre = a.fn != nullptr;     // post only when no mixing weights are given
+  float fnv[NM][S];
+#pragma unroll
+  for (int i = 0; i < NM; ++i)
+#pragma unroll
+    for (int s = 0; s < S; ++s) fnv[i][s] = pre ? bf2f(a.fn[(int64_t)i * S * a.D + s * a.D + d]) : 0.f;
+  const int r0 = blockIdx.y * kRB;
+  for (int r = r0; r < min(r0 + kRB, a.R); ++r) {
+    __nv_bfloat16* xr = a.X + (int64_t)r * S * a.D;
+    float x[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) x[s] = bf2f(xr[s * a.D + d]);
+    if (a.branch) {
+      const float b = round_bf16(a.branch[(int64_t)r * a.D + d]);
+      float nx[S];
+#pragma unroll
+      for (int s = 0; s < S; ++s) {
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < S; ++j) m += a.comb[(r * S + j) * S + s] * x[j];
+        nx[s] = round_bf16(a.post[r * S + s] * b + m);
+      }
+#pragma unroll
+      for (int s = 0; s < S; ++s) { x[s] = nx[s]; xr[s * a.D + d] = f2bf(nx[s]); }
+    }
+    if (!pre) continue;
+    float v[NM + 1];
+#pragma unroll
+    for (int i = 0; i < NM; ++i) {
+      float t = 0.f;
+#pragma unroll
+      for (int s = 0; s < S; ++s) t += fnv[i][s] * x[s];
+      v[i] = warp_sum(t);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int s = 0; s < S; ++s) ss += x[s] * x[s];
+    v[NM] = warp_sum(ss);
+    if (lane == 0) {
+#pragma unroll
+      for (int i = 0; i <= NM; ++i) red[wid][i] = v[i];
+    }
+    __syncthreads();
+    if (threadIdx.x <= NM) {
+      float t = 0.f;
+      for (int w = 0; w < kDB / 32; ++w) t += red[w][threadIdx.x];
+      a.part[((int64_t)r * NB + blockIdx.x) * 32 + threadIdx.x] = t;
+    }
+    __syncthreads();
+  }
+}
+
+template <int S>
+__global__ void __launch_bounds__(512) hc_finish_kernel(HcArgs a) {
+  constexpr int NM = 2 * S + S * S;
+  const int r = blockIdx.x;
+  const int NB = a.D / kDB;
+  __shared__ float mix[32];
+  __shared__ float pre_s[S], post_s[S], comb_s[S * S];
+  __shared__ float red[32];
+  if (threadIdx.x <= NM) {
+    float t = 0.f;
+    for (int b = 0; b < NB; ++b) t += a.part[((int64_t)r * NB + b) * 32 + threadIdx.x];
+    mix[threadIdx.x] = t;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const float rinv = rsqrtf(mix[NM] / (float)(S * a.D) + a.eps);
+    float c[S][S];
+    for (int s = 0; s < S; ++s) {
+      pre_s[s] = sigmoidf_(mix[s] * rinv * a.hscale[0] + a.base[s]) + a.hc_eps;
+      post_s[s] = 2.f * sigmoidf_(mix[S + s] * rinv * a.hscale[1] + a.base[S + s]);
+    }
+    for (int i = 0; i < S; ++i) {
+      float mx = -INFINITY;
+      for (int j = 0; j < S; ++j) {
+        c[i][j] = mix[2 * S + i * S + j] * rinv * a.hscale[2] + a.base[2 * S + i * S + j];
+        mx = fmaxf(mx, c[i][j]);
+      }
+      float sum = 0.f;
+      for (int j = 0; j < S; ++j) { c[i][j] = __expf(c[i][j] - mx); sum += c[i][j]; }
+      for (int j = 0; j < S; ++j) c[i][j] = c[i][j] / sum + a.hc_eps;
+    }
+    for (int it = 0; it < a.iters; ++it) {
+      if (it > 0) {
+        for (int i = 0; i < S; ++i) {
+          float sum = 0.f;
+          for (int j = 0; j < S; ++j) sum += c[i][j];
+          for (int j = 0; j < S; ++j) c[i][j] /= (sum + a.hc_eps);
+        }
+      }
+      for (int j = 0; j < S; ++j) {
+        float sum = 0.f;
+        for (int i = 0; i < S; ++i) sum += c[i][j];
+        for (int i = 0; i < S; ++i) c[i][j] /= (sum + a.hc_eps);
+      }
+    }
+    for (int i = 0; i < S; ++i)
+      for (int j = 0; j < S; ++j) comb_s[i * S + j] = c[i][j];
+  }
+  __syncthreads();
+  if (threadIdx.x < S) a.post_out[r * S + threadIdx.x] = post_s[threadIdx.x];
+  if (threadIdx.x < S * S) a.comb_out[r * S * S + threadIdx.x] = comb_s[threadIdx.x];
+  const __nv_bfloat16* xr = a.X + (int64_t)r * S * a.D;
+  float ss = 0.f;
+  constexpr int kPer = 16;   // columns per thread (D <= 8192)
+  float col[kPer];
+  int n = 0;
+  for (int d = threadIdx.x; d < a.D; d += blockDim.x, ++n) {
+    float t = 0.f;
+#pragma unroll
+    for (int s = 0; s < S; ++s) t += pre_s[s] * bf2f(xr[s * a.D + d]);
+    t = round_bf16(t);
+    col[n] = t;
+    ss += t * t;
+  }
+  ss = block_sum(ss, red);
+  const float rinv = rsqrtf(ss / (float)a.D + a.eps);
+  n = 0;
+  for (int d = threadIdx.x; d < a.D; d += blockDim.x, ++n)
+    a.normed[(int64_t)r * a.D + d] = f2bf(col[n] * rinv * bf2f(a.norm_w[d]));
+}
+
+__global__ void embed_kernel(const int* ids, const __nv_bfloat16* table, int D, int S, __nv_bfloat16* X) {
+  const int r = blockIdx.y;
+  const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (d >= D) return;
+  const uint4 v = *reinterpret_cast<const uint4*>(table + (int64_t)ids[r] * D + d);
+  for (int s = 0; s < S; ++s) *reinterpret_cast<uint4*>(X + ((int64_t)r * S + s) * D + d) = v;
+}
+
+__global__ void __launch_bounds__(512) stream_mean_norm_kernel(const __nv_bfloat16* X, int S, int D,
+                                                               const __nv_bfloat16* w, float eps,
+                                                               __nv_bfloat16* hidden, __nv_bfloat16* normed) {
+  const int r = blockIdx.x;
+  __shared__ float red[32];
+  float col[16];
+  float ss = 0.f;
+  int n = 0;
+  for (int d = threadIdx.x; d < D; d += blockDim.x, ++n) {
+    float t = 0.f;
+    for (int s = 0; s < S; ++s) t += bf2f(X[((int64_t)r * S + s) * D + d]);
+    t = round_bf16(t / (float)S);
+    if (hidden) hidden[(int64_t)r * D + d] = f2bf(t);
+    col[n] = t;
+    ss += t * t;
+  }
+  ss = block_sum(ss, red);
+  const float rinv = rsqrtf(ss / (float)D + eps);
+  n = 0;
+  for (int d = threadIdx.x; d < D; d += blockDim.x, ++n) normed[(int64_t)r * D + d] = f2bf(col[n] * rinv * bf2f(w[d]));
+}
+
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* w,
+                                                      int D, float eps, __nv_bfloat16* y, int64_t ldy) {
+  const int r = blockIdx.x;
+  __shared__ float red[32];
+  float col[32];
+  float ss = 0.f;
+  int n = 0;
+  for (int d = threadIdx.x; d < D; d += blockDim.x, ++n) {
+    const float t = bf2f(x[(int64_t)r * ldx + d]);
+    col[n] = t;
+    ss += t * t;
+  }
+  ss = block_sum(ss, red);
+  const float rinv = rsqrtf(ss / (float)D + eps);
+  n = 0;
+  for (int d = threadIdx.x; d < D; d += blockDim.x, ++n) y[(int64_t)r * ldy + d] = f2bf(col[n] * rinv * bf2f(w[d]));
+}
+
+}  // namespace g53
+
+using namespace g53;
+
+cudaError_t g53_hc_post_pre(const HcArgs& a, cudaStream_t st) {
+  if (a.D % kDB || a.D > 8192 || (a.S != 2 && a.S != 4)) return cudaErrorInvalidValue;
+  dim3 g1(a.D / kDB, (a.R + kRB - 1) / kRB);
+  if (a.S == 4) {
+    hc_partial_kernel<4><<<g1, kDB, 0, st>>>(a);
+    G53_CHECK_LAUNCH();
+    if (a.fn) hc_finish_kernel<4><<<a.R, 512, 0, st>>>(a);
+  } else {
+    hc_partial_kernel<2><<<g1, kDB, 0, st>>>(a);
+    G53_CHECK_LAUNCH();
+    if (a.fn) hc_finish_kernel<2><<<a.R, 512, 0, st>>>(a);
+  }
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}
+
+cudaError_t g53_embed(const int* ids, const __nv_bfloat16* table, int R, int D, int S, __nv_bfloat16* X,
+                      cudaStream_t st) {
+  if (D % 8) return cudaErrorInvalidValue;
+  dim3 grid((D / 8 + 127) / 128, R);
+  embed_kernel<<<grid, 128, 0, st>>>(ids, table, D, S, X);
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}
+
+cudaError_t g53_stream_mean_norm(const __nv_bfloat16* X, int R, int S, int D, const __nv_bfloat16* w, float eps,
+                                 __nv_bfloat16* hidden, __nv_bfloat16* normed, cudaStream_t st) {
+  if (D > 8192) return cudaErrorInvalidValue;
+  stream_mean_norm_kernel<<<R, 512, 0, st>>>(X, S, D, w, eps, hidden, normed);
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}
+
+cudaError_t g53_rmsnorm(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* w, int R, int D, float eps,
+                        __nv_bfloat16* y, int64_t ldy, cudaStream_t st) {
+  if (D > 8192) return cudaErrorInvalidValue;
+  rmsnorm_kernel<<<R, 256, 0, st>>>(x, ldx, w, D, eps, y, ldy);
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}

@@ -1,0 +1,406 @@
+"""GPU model runtime: the GLM-5.3-Flash forward pass on this engine's sm_100a kernels.
+
+One ``Runtime`` per rank.  Every forward reads its inputs from static device buffers (``Batch``) and writes into
+preallocated scratch, so a decode step can be captured once in a CUDA graph and replayed.  A forward covers R rows
+that belong to B sequences (a decode window of K+1 rows per request, or one prefill chunk); per row it needs the
+token id, position, KV token slot and sequence index, per sequence the page table, the KDA state-pool indices (read
+/ write) and the conv-window slot.
+
+Layer structure (code/fork/docs/ref/tf_forward.py:278-301): mHC pre -> KDA or MLA/DSA -> [all-reduce] -> mHC post
+fused with the next mHC pre -> dense MLP or MoE -> [all-reduce] -> ...; the final mHC post is followed by the
+stream mean, the final RMSNorm and the vocabulary-parallel lm_head.
+
+KDA verify windows: the recurrent kernel reads state ``s_in`` and writes the state after the window's last row to
+``s_out``; ``commit`` keeps the first ``keep`` rows of each sequence (re-running the recurrence over them when
+keep < rows, from the layer's saved window inputs) and shifts the conv windows.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ..config import ModelConfig
+from ..ops import kernels as K
+from .weights import Linear8, Weights
+
+bf16, f32, i32 = torch.bfloat16, torch.float32, torch.int32
+
+
+@dataclass
+class RuntimeConfig:
+    max_rows: int = 16            # rows of one forward
+    max_seqs: int = 1             # sequences with KDA state / conv windows
+    kv_slots: int = 8192          # token slots of the paged caches (a multiple of block_size)
+    block_size: int = 64
+    max_blocks: int = 128         # page-table width per sequence
+    decode_rows: int = 16         # forwards of at most this many rows keep per-layer KDA window inputs (replay)
+    mla_splits: int = 4           # key splits of the decode attention
+    moe_chunk: int = 256          # rows per routed-MoE launch group (routing kernel capacity)
+    attn_chunk: int = 1024        # rows per attention launch group (scratch bound)
+    logit_rows: int = 16
+
+
+def interleave_gate_up(gu: Linear8) -> Linear8:
+    """[gate; up] rows -> 16-row tiles of (8 gate rows, the matching 8 up rows): the layout the GEMV SwiGLU
+    epilogue expects."""
+    n = gu.w.shape[0] // 2
+    assert n % 8 == 0
+    g, u = gu.w[:n].view(n // 8, 8, -1), gu.w[n:].view(n // 8, 8, -1)
+    gs, us = gu.s[:n].view(n // 8, 8), gu.s[n:].view(n // 8, 8)
+    w = torch.stack([g, u], 1).reshape(2 * n, -1).contiguous()
+    s = torch.stack([gs, us], 1).reshape(2 * n).contiguous()
+    return Linear8(w, s)
+
+
+class Batch:
+    """Static device buffers describing the rows and sequences of a forward."""
+
+    def __init__(self, rc: RuntimeConfig, device):
+        R, B = rc.max_rows, rc.max_seqs
+        self.ids = torch.zeros(R, dtype=i32, device=device)
+        self.positions = torch.zeros(R, dtype=i32, device=device)
+        self.slots = torch.zeros(R, dtype=i32, device=device)
+        self.row_seq = torch.zeros(R, dtype=i32, device=device)
+        self.kda_seq = torch.zeros(5, B, dtype=i32, device=device)        # row0, nrows, s_in, s_out, conv_slot
+        self.commit_seq = torch.zeros(5, B, dtype=i32, device=device)     # same with nrows = kept rows
+        self.block_table = torch.zeros(B, rc.max_blocks, dtype=i32, device=device)
+        self.logit_rows = torch.zeros(rc.logit_rows, dtype=torch.int64, device=device)
+        self.host = torch.zeros(4 * R + 10 * B + rc.logit_rows, dtype=i32, pin_memory=torch.cuda.is_available())
+        self.R = 0
+        self.B = 0
+        self.max_rows_per_seq = 0
+        self.n_logits = 0
+
+
+class Runtime:
+    def __init__(self, w: Weights, rc: RuntimeConfig, comm=None):
+        self.w, self.rc, self.comm = w, rc, comm
+        c = self.cfg = w.cfg
+        dev = self.device = w.device
+        self.tp = w.world
+        R = rc.max_rows
+        D, S = c.hidden, c.streams
+        self.batch = Batch(rc, dev)
+        # --- GPU-layout weights (SwiGLU-interleaved gate/up) ---
+        self.gu_il = {}
+        for lw in w.layers:
+            m = lw.mlp if lw.mlp is not None else lw.moe.shared
+            self.gu_il[lw.index] = interleave_gate_up(m.gu)
+        # --- activations ---
+        self.X = torch.zeros(R, S, D, dtype=bf16, device=dev)
+        self.normed = torch.zeros(R, D, dtype=bf16, device=dev)
+        self.post = [torch.zeros(R, S, dtype=f32, device=dev) for _ in range(2)]
+        self.comb = [torch.zeros(R, S, S, dtype=f32, device=dev) for _ in range(2)]
+        self.part = torch.zeros(R, D // 256, 32, dtype=f32, device=dev)
+        self.branch = torch.zeros(R, D, dtype=f32, device=dev)
+        self.hidden = torch.zeros(R, D, dtype=bf16, device=dev)
+        self.fnormed = torch.zeros(R, D, dtype=bf16, device=dev)
+        self.lrows = torch.zeros(rc.logit_rows, D, dtype=bf16, device=dev)
+        self.logits = torch.zeros(rc.logit_rows, w.head.n, dtype=f32, device=dev)
+        # --- KDA ---
+        kda = [lw for lw in w.layers if lw.kind == "kda"]
+        self.kda_index = {lw.index: i for i, lw in enumerate(kda)}
+        if kda:
+            k0 = kda[0].kda
+            H, Dh = k0.heads, c.lin_dim
+            self.kH, self.kDh = H, Dh
+            width = k0.in_proj.n
+            self.kda_width = width
+            C3 = 3 * H * Dh
+            self.S_pool = [torch.zeros(2 * rc.max_seqs, H, Dh, Dh, dtype=f32, device=dev) for _ in kda]
+            self.conv_pool = [torch.zeros(rc.max_seqs, c.conv - 1, C3, dtype=bf16, device=dev) for _ in kda]
+            dr = min(rc.decode_rows, R)
+            self.kproj_l = [torch.zeros(dr, width, dtype=bf16, device=dev) for _ in kda]
+            self.kf_l = [torch.zeros(dr, H * Dh, dtype=bf16, device=dev) for _ in kda]
+            self.kqkv_l = [torch.zeros(dr, C3, dtype=bf16, device=dev) for _ in kda]
+            self.kproj = torch.zeros(R, width, dtype=bf16, device=dev)
+            self.kf = torch.zeros(R, H * Dh, dtype=bf16, device=dev)
+            self.kqkv = torch.zeros(R, C3, dtype=bf16, device=dev)
+            self.kg = torch.zeros(R, H * Dh, dtype=bf16, device=dev)
+            self.ko = torch.zeros(R, H * Dh, dtype=f32, device=dev)
+            self.kout = torch.zeros(R, H * Dh, dtype=bf16, device=dev)
+        # --- MLA / DSA ---
+        mla = [lw for lw in w.layers if lw.kind == "mla"]
+        self.mla_index = {lw.index: i for i, lw in enumerate(mla)}
+        if mla:
+            a0 = mla[0].mla
+            H = self.mH = a0.heads
+            L, rope = c.kv_lora, c.qk_rope
+            ns = rc.kv_slots
+            assert ns % rc.block_size == 0 and rc.block_size % c.kpool == 0
+            self.kv = [torch.zeros(ns, L, dtype=torch.uint8, device=dev) for _ in mla]
+            self.kv_scale = [torch.zeros(ns, dtype=f32, device=dev) for _ in mla]
+            self.kpe = [torch.zeros(ns, max(rope, 1), dtype=bf16, device=dev) for _ in mla]
+            self.ik = [torch.zeros(ns, c.index_dim, dtype=bf16, device=dev) for _ in mla]
+            self.ig = [torch.zeros(ns, c.index_dim, dtype=f32, device=dev) for _ in mla]
+            self.pool = [torch.zeros(ns // c.kpool, c.index_dim, dtype=torch.uint8, device=dev) for _ in mla]
+            self.pool_scale = [torch.zeros(ns // c.kpool, dtype=f32, device=dev) for _ in mla]
+            AR = min(R, rc.attn_chunk)
+            self.qkv_a = torch.zeros(R, a0.qkv_a.n, dtype=bf16, device=dev)
+            self.qr = torch.zeros(R, c.q_lora, dtype=bf16, device=dev)
+            self.q = torch.zeros(R, H, c.qk_dim, dtype=bf16, device=dev)
+            self.q_lat = torch.zeros(R, H, L, dtype=bf16, device=dev)
+            self.o_lat = torch.zeros(R, H, L, dtype=bf16, device=dev)
+            self.obuf = torch.zeros(R, H * c.v_dim, dtype=bf16, device=dev)
+            self.iproj = torch.zeros(R, 2 * c.index_dim + c.index_heads, dtype=f32, device=dev)
+            self.qi = torch.zeros(R, c.index_heads * c.index_dim, dtype=bf16, device=dev)
+            self.max_pools = rc.max_blocks * rc.block_size // c.kpool
+            self.dsa_logits = torch.zeros(AR, self.max_pools, dtype=f32, device=dev)
+            self.max_sel = max(c.index_topk, 1)
+            self.sel = torch.zeros(AR, max(self.max_sel, c.index_topk), dtype=i32, device=dev)
+            self.sel_count = torch.zeros(AR, dtype=i32, device=dev)
+            self.splits = rc.mla_splits
+            self.part_o = torch.zeros(AR * rc.mla_splits * H * L, dtype=f32, device=dev)
+            self.part_ml = torch.zeros(AR * rc.mla_splits * H * 2, dtype=f32, device=dev)
+        # --- MLP / MoE ---
+        MR = min(R, rc.moe_chunk)
+        tk = c.top_k
+        P = MR * tk
+        widths = [self.gu_il[i].w.shape[0] // 2 for i in self.gu_il]
+        self.act = torch.zeros(R, max(widths), dtype=bf16, device=dev)
+        self.rlogits = torch.zeros(MR, c.experts, dtype=f32, device=dev)
+        self.topk_ids = torch.zeros(MR, tk, dtype=i32, device=dev)
+        self.topk_w = torch.zeros(MR, tk, dtype=f32, device=dev)
+        self.max_groups = min(P, c.experts)
+        self.group_count = torch.zeros(1, dtype=i32, device=dev)
+        self.group_expert = torch.zeros(self.max_groups, dtype=i32, device=dev)
+        self.group_offset = torch.zeros(self.max_groups + 1, dtype=i32, device=dev)
+        self.pair_token = torch.zeros(P, dtype=i32, device=dev)
+        self.pair_expert = torch.zeros(P, dtype=i32, device=dev)
+        self.pair_w = torch.zeros(P, dtype=f32, device=dev)
+        self.pair_of = torch.zeros(P, dtype=i32, device=dev)
+        moe0 = next((lw.moe for lw in w.layers if lw.moe is not None), None)
+        if moe0 is not None:
+            self.xh_g = torch.zeros(P, D, dtype=torch.float16, device=dev)
+            self.xh_u = torch.zeros(P, D, dtype=torch.float16, device=dev)
+            self.xd = torch.zeros(P, moe0.gate.n, dtype=torch.float16, device=dev)
+            self.yd = torch.zeros(P, D, dtype=f32, device=dev)
+
+    # ------------------------------------------------------------------------------------------------------------
+    # host-side batch staging (pinned buffer -> one H2D copy per array)
+    # ------------------------------------------------------------------------------------------------------------
+    def stage(self, ids, positions, slots, row_seq, seqs, block_tables, logit_rows) -> int:
+        """ids/positions/slots/row_seq: per-row ints; seqs: per sequence (row0, nrows, s_in, s_out, conv_slot);
+        block_tables: per sequence list of page ids; logit_rows: rows whose logits are computed."""
+        b = self.batch
+        R, B = len(ids), len(seqs)
+        if R > self.rc.max_rows or B > self.rc.max_seqs or len(logit_rows) > self.rc.logit_rows:
+            raise ValueError("batch exceeds the runtime's static buffers")
+        dev = self.device
+        b.ids[:R].copy_(torch.as_tensor(ids, dtype=i32), non_blocking=True)
+        b.positions[:R].copy_(torch.as_tensor(positions, dtype=i32), non_blocking=True)
+        b.slots[:R].copy_(torch.as_tensor(slots, dtype=i32), non_blocking=True)
+        b.row_seq[:R].copy_(torch.as_tensor(row_seq, dtype=i32), non_blocking=True)
+        sq = torch.as_tensor(seqs, dtype=i32).t().contiguous()
+        b.kda_seq[:, :B].copy_(sq, non_blocking=True)
+        for i, bt in enumerate(block_tables):
+            if len(bt) > self.rc.max_blocks:
+                raise ValueError("page table wider than max_blocks")
+            b.block_table[i, :len(bt)].copy_(torch.as_tensor(bt, dtype=i32), non_blocking=True)
+        b.logit_rows[:len(logit_rows)].copy_(torch.as_tensor(logit_rows, dtype=torch.int64), non_blocking=True)
+        b.R, b.B = R, B
+        b.max_rows_per_seq = max(s[1] for s in seqs)
+        b.n_logits = len(logit_rows)
+        return R
+
+    # ------------------------------------------------------------------------------------------------------------
+    # forward
+    # ------------------------------------------------------------------------------------------------------------
+    def allreduce(self, t: torch.Tensor):
+        if self.comm is not None and self.tp > 1:
+            self.comm.all_reduce(t)
+
+    def forward(self, R: int | None = None, keep_window: bool | None = None, logits: bool = True):
+        b = self.batch
+        R = b.R if R is None else R
+        c = self.cfg
+        if keep_window is None:
+            keep_window = R <= self.rc.decode_rows
+        self._keep_window = keep_window
+        Kc = K.C()
+        X = self.X[:R]
+        Kc.embed(b.ids[:R], self.w.embed, X)
+        cur = 0
+        first = True
+        for lw in self.w.layers:
+            # post of the previous FFN (none before layer 0) fused with this layer's attention pre
+            nxt = 1 - cur
+            Kc.hc_post_pre(X, None if first else self.branch[:R], None if first else self.post[cur][:R],
+                           None if first else self.comb[cur][:R], lw.attn_hc.fn, lw.attn_hc.base, lw.attn_hc.scale,
+                           lw.in_norm, self.normed[:R], self.post[nxt][:R], self.comb[nxt][:R], self.part[:R],
+                           c.eps, c.hc_eps, c.hc_iters)
+            cur = nxt
+            first = False
+            if lw.kind == "kda":
+                self._kda(lw, R)
+            else:
+                self._mla(lw, R)
+            self.allreduce(self.branch[:R])
+            nxt = 1 - cur
+            Kc.hc_post_pre(X, self.branch[:R], self.post[cur][:R], self.comb[cur][:R], lw.ffn_hc.fn,
+                           lw.ffn_hc.base, lw.ffn_hc.scale, lw.post_norm, self.normed[:R], self.post[nxt][:R],
+                           self.comb[nxt][:R], self.part[:R], c.eps, c.hc_eps, c.hc_iters)
+            cur = nxt
+            if lw.mlp is not None:
+                self._mlp(lw, R)
+            else:
+                self._moe(lw, R)
+            self.allreduce(self.branch[:R])
+        Kc.hc_post_pre(X, self.branch[:R], self.post[cur][:R], self.comb[cur][:R], None, None, None, None, None,
+                       None, None, self.part[:R], c.eps, c.hc_eps, c.hc_iters)
+        Kc.stream_mean_norm(X, self.w.norm, c.eps, self.hidden[:R], self.fnormed[:R])
+        if not logits:
+            return None
+        n = b.n_logits
+        torch.index_select(self.fnormed[:R], 0, b.logit_rows[:n], out=self.lrows[:n])
+        K.linear8(self.lrows[:n], self.w.head.w, self.w.head.s, self.logits[:n], K.GEMV_F32)
+        return self.logits[:n]
+
+    # ---- blocks ------------------------------------------------------------------------------------------------
+    def _kda(self, lw, R):
+        c, k, b = self.cfg, lw.kda, self.batch
+        Kc = K.C()
+        li = self.kda_index[lw.index]
+        H, Dh = self.kH, self.kDh
+        if self._keep_window:
+            proj, fb, qkv = self.kproj_l[li][:R], self.kf_l[li][:R], self.kqkv_l[li][:R]
+        else:
+            proj, fb, qkv = self.kproj[:R], self.kf[:R], self.kqkv[:R]
+        C3 = 3 * H * Dh
+        K.linear8(self.normed[:R], k.in_proj.w, k.in_proj.s, proj)
+        K.linear8(proj[:, C3:C3 + Dh], k.f_b.w, k.f_b.s, fb)
+        K.linear8(proj[:, C3 + Dh:C3 + 2 * Dh], k.g_b.w, k.g_b.s, self.kg[:R])
+        seq = b.kda_seq[:, :b.B]
+        Kc.kda_conv(proj, seq, b.max_rows_per_seq, k.conv, self.conv_pool[li], qkv, H, Dh)
+        if not self._keep_window:       # prefill chunk: every row is kept, shift the conv window now
+            Kc.kda_conv_commit(proj, seq, self.conv_pool[li], H, Dh, c.conv)
+        Kc.kda_recurrent(proj, seq, fb, qkv, k.a_log, k.dt_bias, self.S_pool[li], self.ko[:R], H, Dh,
+                         C3 + 2 * Dh, c.lower)
+        Kc.kda_gated_norm(self.ko[:R], self.kg[:R], k.o_norm, self.kout[:R], H, Dh, c.eps)
+        K.linear8(self.kout[:R], k.o_proj.w, k.o_proj.s, self.branch[:R], K.GEMV_F32)
+
+    def _mla(self, lw, R):
+        c, a, b = self.cfg, lw.mla, self.batch
+        Kc = K.C()
+        li = self.mla_index[lw.index]
+        H, L, rope, nope = self.mH, c.kv_lora, c.qk_rope, c.qk_nope
+        K.linear8(self.normed[:R], a.qkv_a.w, a.qkv_a.s, self.qkv_a[:R])
+        Kc.mla_prep(self.qkv_a[:R], a.q_norm, a.kv_norm, self.qr[:R], self.kv[li], self.kv_scale[li],
+                    self.kpe[li] if rope else None, b.slots[:R], b.positions[:R], c.q_lora, L, rope, c.eps,
+                    c.rope_theta)
+        K.linear8(self.qr[:R], a.q_b.w, a.q_b.s, self.q[:R].view(R, H * c.qk_dim))
+        if rope:
+            Kc.rope_q(self.q[:R], b.positions[:R], nope, rope, c.rope_theta)
+        # absorbed query: q_lat[r, h] = q_nope[r, h] @ W_uk[h]   (batched over heads)
+        for r0 in range(0, R, K.GEMV_MAX_M):
+            r1 = min(R, r0 + K.GEMV_MAX_M)
+            Kc.gemv(self.q[r0:r1, :, :nope].transpose(0, 1), a.w_uk_t.w, a.w_uk_t.s,
+                    self.q_lat[r0:r1].transpose(0, 1), K.GEMV_BF16, 0.0)
+        # indexer
+        K.linear_bf16(self.normed[:R], a.index.proj, self.iproj[:R])
+        Kc.dsa_update(self.iproj[:R], a.index.ln_w, a.index.ln_b, a.index.ape, self.ik[li], self.ig[li],
+                      self.pool[li], self.pool_scale[li], b.slots[:R], b.positions[:R], b.block_table,
+                      b.row_seq[:R], self.rc.block_size, c.index_heads, c.kpool, c.eps)
+        K.linear8(self.qr[:R], a.index.wq_b.w, a.index.wq_b.s, self.qi[:R])
+        AR = self.sel.shape[0]
+        sm_scale = c.qk_dim ** -0.5
+        splits = self.splits if R <= self.rc.decode_rows else 1
+        for r0 in range(0, R, AR):
+            r1 = min(R, r0 + AR)
+            n = r1 - r0
+            Kc.dsa_select(self.iproj[r0:r1], self.qi[r0:r1], a.index.ln_w, self.pool[li], self.pool_scale[li],
+                          b.positions[r0:r1], b.block_table, b.row_seq[r0:r1], self.rc.block_size, c.index_heads,
+                          c.kpool, c.pools_selected, self.dsa_logits[:n], self.sel[:n], self.sel_count[:n])
+            qpe = self.q[r0:r1, :, nope:] if rope else None
+            Kc.mla_decode(self.q_lat[r0:r1], qpe, H * c.qk_dim, c.qk_dim, self.kv[li], self.kv_scale[li],
+                          self.kpe[li] if rope else None, self.sel[:n], self.sel_count[:n], rope, sm_scale, splits,
+                          self.part_o, self.part_ml, self.o_lat[r0:r1])
+        ob = self.obuf[:R].view(R, H, c.v_dim)
+        for r0 in range(0, R, K.GEMV_MAX_M):
+            r1 = min(R, r0 + K.GEMV_MAX_M)
+            Kc.gemv(self.o_lat[r0:r1].transpose(0, 1), a.w_uv.w, a.w_uv.s, ob[r0:r1].transpose(0, 1),
+                    K.GEMV_BF16, 0.0)
+        K.linear8(self.obuf[:R], a.o_proj.w, a.o_proj.s, self.branch[:R], K.GEMV_F32)
+
+    def _mlp(self, lw, R):
+        m = lw.mlp
+        gu = self.gu_il[lw.index]
+        act = self.act[:R, :m.width]
+        K.linear8(self.normed[:R], gu.w, gu.s, act, K.GEMV_SWIGLU, self.cfg.limit)
+        K.linear8(act, m.down.w, m.down.s, self.branch[:R], K.GEMV_F32)
+
+    def _moe(self, lw, R):
+        c, m = self.cfg, lw.moe
+        Kc = K.C()
+        MR = self.rlogits.shape[0]
+        for r0 in range(0, R, MR):
+            r1 = min(R, r0 + MR)
+            n = r1 - r0
+            P = n * c.top_k
+            x = self.normed[r0:r1]
+            K.linear_bf16(x, m.router, self.rlogits[:n])
+            groups = min(P, c.experts)
+            Kc.moe_route(self.rlogits[:n], m.bias, c.top_k, c.routed_scale, c.norm_topk, self.topk_ids[:n],
+                         self.topk_w[:n], self.group_count, self.group_expert[:groups],
+                         self.group_offset[:groups + 1], self.pair_token[:P], self.pair_expert[:P], self.pair_w[:P],
+                         self.pair_of[:P])
+            Kc.exl3_moe(x, m.gate.trellis, m.gate.suh, m.gate.svh, m.up.trellis, m.up.suh, m.up.svh,
+                        m.down.trellis, m.down.suh, m.down.svh, self.group_count, self.group_expert[:groups],
+                        self.group_offset[:groups + 1], self.pair_token[:P], self.pair_expert[:P], self.pair_w[:P],
+                        self.xh_g, self.xh_u, self.xd, self.yd, c.limit)
+            Kc.moe_combine(self.yd, self.pair_of[:P], c.top_k, self.branch[r0:r1], False)
+        # shared expert, accumulated into the branch
+        s = m.shared
+        gu = self.gu_il[lw.index]
+        act = self.act[:R, :s.width]
+        K.linear8(self.normed[:R], gu.w, gu.s, act, K.GEMV_SWIGLU, c.limit)
+        K.linear8(act, s.down.w, s.down.s, self.branch[:R], K.GEMV_F32_ACC)
+
+    # ------------------------------------------------------------------------------------------------------------
+    # commit of a verify window
+    # ------------------------------------------------------------------------------------------------------------
+    def commit(self, seqs_keep, replay: bool = True):
+        """seqs_keep: per sequence (row0, keep, s_in, s_out, conv_slot): the rows kept of the last forward, which
+        must have run with keep_window.  ``replay`` re-runs the KDA recurrence over the kept rows (needed when a
+        sequence keeps fewer rows than its window) so s_out holds the state after the last kept row."""
+        b = self.batch
+        Kc = K.C()
+        B = len(seqs_keep)
+        sq = torch.as_tensor(seqs_keep, dtype=i32).t().contiguous()
+        b.commit_seq[:, :B].copy_(sq, non_blocking=True)
+        seq = b.commit_seq[:, :B]
+        for lw in self.w.layers:
+            if lw.kind != "kda":
+                continue
+            li = self.kda_index[lw.index]
+            k = lw.kda
+            H, Dh = self.kH, self.kDh
+            C3 = 3 * H * Dh
+            proj = self.kproj_l[li]
+            if replay:
+                Kc.kda_recurrent(proj, seq, self.kf_l[li], self.kqkv_l[li], k.a_log, k.dt_bias, self.S_pool[li],
+                                 None, H, Dh, C3 + 2 * Dh, self.cfg.lower)
+            Kc.kda_conv_commit(proj, seq, self.conv_pool[li], H, Dh, self.cfg.conv)
+
+
+class Graphed:
+    """A CUDA graph of one runtime call with fixed shapes (the batch buffers it reads are static).  Capture needs
+    the batch staged with a valid window; warm-up runs on a side stream first, as CUDA graph capture requires."""
+
+    def __init__(self, fn, warmup: int = 2):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                fn()
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = fn()
+
+    def __call__(self):
+        self.graph.replay()
+        return self.out

@@ -1,0 +1,84 @@
+"""Build and load the in-tree CUDA extension (``glm53_C``) for sm_100a.
+
+The extension is compiled with nvcc for ``-gencode arch=compute_100a,code=sm_100a`` only (no other architecture)
+into ``<package>/_build/``, next to the sources, so the built ``.so`` travels with the source tree.  ``load()``
+imports a built library directly (no rebuild check) and builds it when it is missing; ``build()`` always runs the
+(incremental, ninja) build.  On a machine with a CUDA device the extension is mandatory: ``require()`` raises if it
+cannot be loaded, so no op silently falls back to PyTorch.
+"""
+
+from __future__ import annotations
+
+import glob
+import importlib.util
+import os
+import sys
+import threading
+
+_PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CSRC = os.path.join(_PKG, "csrc")
+BUILD_DIR = os.path.join(_PKG, "_build")
+NAME = "glm53_C"
+ARCH_FLAGS = ["-gencode=arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH_FLAGS + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xptxas=-v"]
+
+_lock = threading.Lock()
+_mod = None
+
+
+def sources() -> list[str]:
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + [os.path.join(CSRC, "bindings.cpp")]
+
+
+def so_path() -> str:
+    return os.path.join(BUILD_DIR, NAME + ".so")
+
+
+def build(verbose: bool = False):
+    """Compile every CUDA source for sm_100a (incremental) and return the loaded module."""
+    global _mod
+    import torch.utils.cpp_extension as ce
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    os.environ.setdefault("MAX_JOBS", str(os.cpu_count() or 8))
+    # the -gencode flags in extra_cuda_cflags replace torch's own arch list
+    os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
+    with _lock:
+        _mod = ce.load(name=NAME, sources=sources(), extra_cuda_cflags=NVCC_FLAGS,
+                       extra_cflags=["-O3", "-std=c++17"], build_directory=BUILD_DIR, verbose=verbose,
+                       with_cuda=True)
+    return _mod
+
+
+def _import_so(path: str):
+    import torch  # noqa: F401  (the extension links against torch's libraries)
+    spec = importlib.util.spec_from_file_location(NAME, path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    sys.modules[NAME] = mod
+    return mod
+
+
+def load(build_if_missing: bool = True):
+    global _mod
+    if _mod is not None:
+        return _mod
+    with _lock:
+        if _mod is not None:
+            return _mod
+        if os.path.exists(so_path()):
+            _mod = _import_so(so_path())
+            return _mod
+    if build_if_missing:
+        return build()
+    return None
+
+
+def require():
+    """The extension, or an exception: kernels never fall back to eager PyTorch on a GPU machine."""
+    try:
+        mod = load()
+    except Exception as e:  # pragma: no cover - exercised only when the build is broken
+        raise RuntimeError(f"glm53 CUDA extension could not be loaded: {e}") from e
+    if mod is None:
+        raise RuntimeError("glm53 CUDA extension is not built (run __graft_entry__.build())")
+    return mod

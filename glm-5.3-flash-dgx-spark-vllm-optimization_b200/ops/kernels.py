@@ -1,0 +1,43 @@
+"""Thin Python wrappers over the CUDA extension (glm53_C).  Every wrapper launches on the current CUDA stream and
+works on preallocated outputs, so a sequence of calls can be captured in a CUDA graph."""
+
+from __future__ import annotations
+
+import torch
+
+from . import _ext
+
+GEMV_BF16, GEMV_F32, GEMV_F32_ACC, GEMV_SWIGLU = 0, 1, 2, 3
+GEMV_MAX_M = 16
+
+
+def C():
+    return _ext.require()
+
+
+def linear8(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor, y: torch.Tensor, mode: int = GEMV_BF16,
+            limit: float = 0.0) -> torch.Tensor:
+    """y[M, N] (mode) = x[M, K] @ (w8[N, K] * s)^T for any M (chunks of 16 rows through the small-M kernel, or
+    the large-M GEMM when it is available)."""
+    M = x.shape[-2]
+    g = C().gemv
+    if M <= GEMV_MAX_M:
+        g(x, w, s, y, mode, limit)
+        return y
+    gemm = getattr(C(), "gemm_w8", None)
+    if gemm is not None and M >= 64:
+        gemm(x, w, s, y, mode, limit)
+        return y
+    for m0 in range(0, M, GEMV_MAX_M):
+        m1 = min(M, m0 + GEMV_MAX_M)
+        g(x[..., m0:m1, :], w, s, y[..., m0:m1, :], mode, limit)
+    return y
+
+
+def linear_bf16(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    """y fp32 [M, N] = x bf16 [M, K] @ w bf16 [N, K]^T."""
+    M = x.shape[0]
+    for m0 in range(0, M, GEMV_MAX_M):
+        m1 = min(M, m0 + GEMV_MAX_M)
+        C().gemv(x[m0:m1], w, None, y[m0:m1], GEMV_F32, 0.0)
+    return y

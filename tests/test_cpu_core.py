@@ -1,0 +1,121 @@
+"""CPU tests: EXL3 codec, configuration, random init, and the fp32 reference model."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+
+def _slow_unpack_tile(words16: np.ndarray, bits: int = 4) -> np.ndarray:
+    """Independent decoder of one tile: read the circular bitstream bit by bit (MSB first within each
+    little-endian 32-bit word), evaluate the mcg codebook in Python integers, place by the fragment map."""
+    w32 = [int(words16[2 * i]) & 0xFFFF | ((int(words16[2 * i + 1]) & 0xFFFF) << 16) for i in range(8 * bits)]
+    total = 32 * len(w32)
+
+    def bit(b):
+        b %= total
+        return (w32[b // 32] >> (31 - b % 32)) & 1
+
+    out = np.zeros((16, 16), dtype=np.float16)
+    for p in range(256):
+        end = (p + 1) * bits
+        s = 0
+        for b in range(end - 16, end):
+            s = (s << 1) | bit(b)
+        x = (s * 0xCBAC1FED) & 0xFFFFFFFF
+        x = (x & 0x8FFF8FFF) ^ 0x3B603B60
+        lo = np.array([x & 0xFFFF], dtype=np.uint16).view(np.float16)[0]
+        hi = np.array([x >> 16], dtype=np.uint16).view(np.float16)[0]
+        v = np.float16(np.float64(lo) + np.float64(hi))
+        lane, j = p // 8, p % 8
+        out[2 * (lane % 4) + (j & 1) + 8 * ((j >> 1) & 1), lane // 4 + 8 * (j >> 2)] = v
+    return out
+
+
+def test_exl3_unpack_matches_bitwise_decoder():
+    from glm53.ops import exl3
+    g = torch.Generator().manual_seed(0)
+    tr, _, _ = exl3.random_linear(128, 128, generator=g)
+    full = exl3.unpack(tr).numpy()
+    for kt, nt in [(0, 0), (3, 5), (7, 7)]:
+        ref = _slow_unpack_tile(tr[kt, nt].numpy())
+        assert np.array_equal(full[kt * 16:(kt + 1) * 16, nt * 16:(nt + 1) * 16].view(np.uint16), ref.view(np.uint16))
+
+
+def test_hadamard_orthonormal_and_rotate():
+    from glm53.ops import exl3
+    h = exl3.hadamard(128)
+    assert torch.allclose(h @ h.t(), torch.eye(128, dtype=torch.float64), atol=1e-12)
+    x = torch.randn(3, 256, dtype=torch.float64)
+    y = exl3.rotate(exl3.rotate(x))
+    assert torch.allclose(x, y, atol=1e-12)
+
+
+def test_exl3_linear_consistent_with_dequantize():
+    from glm53.ops import exl3
+    g = torch.Generator().manual_seed(2)
+    tr, su, sv = exl3.random_linear(256, 128, generator=g)
+    x = torch.randn(4, 256)
+    ref = (x.double() @ exl3.dequantize(tr, su, sv)).float()
+    got = exl3.linear(x, tr, su, sv, f16_input=False)
+    assert torch.allclose(got, ref, atol=1e-4, rtol=1e-4)
+    w = exl3.dequantize(tr, su, sv)
+    assert abs(w.std().item() - 1 / math.sqrt(256)) < 0.01
+
+
+def test_full_config_layer_plan():
+    import glm53
+    c = glm53.full_config()
+    assert c.layers == 45
+    assert c.mla_layers() == list(range(3, 45, 4))
+    assert len(c.kda_layers()) == 34 and len(c.moe_layers()) == 42
+    assert c.mlp_kinds[:3] == ["dense"] * 3
+    assert c.vocab == 154880 and c.n_mix == 24 and c.kda_proj_width == 3 * 64 * 128 + 256 + 64
+    for tp in (1, 2, 4, 8):
+        c.validate(tp)
+
+
+def test_random_source_deterministic(tiny_cfg):
+    from glm53.models import weights as W
+    a = W.RandomSource(tiny_cfg, seed=3)
+    b = W.RandomSource(tiny_cfg, seed=3)
+    name = "model.layers.1.self_attn.q_proj.weight"
+    assert torch.equal(a.get(name), b.get(name))
+    assert not torch.equal(a.get(name), W.RandomSource(tiny_cfg, seed=4).get(name))
+
+
+def test_fp8_row_quantisation():
+    from glm53.models.weights import quantize_fp8_rows
+    w = torch.randn(64, 128)
+    q = quantize_fp8_rows(w)
+    err = (q.dequant() - w).abs() / w.abs().amax(1, keepdim=True)
+    assert err.max() < 0.07
+
+
+def test_oracle_tiny_deterministic(tiny_weights):
+    from glm53.models.reference import ReferenceModel
+    m1, m2 = ReferenceModel(tiny_weights), ReferenceModel(tiny_weights)
+    toks = [5, 17, 99, 1024, 7, 7, 3000, 12]
+    a = m1.prefill(toks)
+    b = m2.prefill(toks)
+    assert torch.isfinite(a).all() and torch.equal(a, b)
+    assert a.shape == (tiny_weights.cfg.vocab,)
+
+
+def test_oracle_dsa_sparse_rows(tiny_cfg, tiny_weights):
+    """Past index_topk tokens a query sees (P-1) pools + its own partial pool."""
+    from glm53.models.reference import ReferenceModel
+    m = ReferenceModel(tiny_weights)
+    c = tiny_cfg
+    toks = torch.randint(0, c.vocab, (c.index_topk + 9,), generator=torch.Generator().manual_seed(0)).tolist()
+    m.prefill(toks)
+    st = m.state.mla[c.mla_layers()[0]]
+    assert len(st.pool) == len(toks) // c.kpool
+    from glm53.models.reference import index_select
+    t = len(toks) - 1
+    qi = torch.randn(c.index_heads, c.index_dim)
+    hw = torch.rand(c.index_heads)
+    sel = index_select(c, st, qi, hw, t)
+    assert len(sel) == (c.pools_selected - 1) * c.kpool + (t % c.kpool) + 1
+    assert sel == sorted(sel) and sel[-1] == t

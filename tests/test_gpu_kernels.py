@@ -1,0 +1,198 @@
+"""Numerics of each CUDA kernel against a plain fp32 PyTorch reference of the same op (GPU only)."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def C():
+    from glm53.ops import _ext
+    return _ext.require()
+
+
+def test_exl3_unpack_bitexact(C):
+    from glm53.ops import exl3
+    g = torch.Generator().manual_seed(1)
+    tr, _, _ = exl3.random_linear(256, 384, generator=g)
+    ref = exl3.unpack(tr)
+    out = C.exl3_unpack(tr.to(DEV), 256, 384).cpu()
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("M", [1, 3, 8, 11, 16])
+@pytest.mark.parametrize("N,K", [(64, 128), (900, 512), (2048, 4096)])
+def test_gemv_fp8(C, M, N, K):
+    from glm53.models.weights import quantize_fp8_rows
+    from glm53.ops import kernels as Kk
+    torch.manual_seed(M * 7 + N)
+    w = quantize_fp8_rows(torch.randn(N, K) / math.sqrt(K))
+    x = torch.randn(M, K).to(torch.bfloat16)
+    ref = x.float() @ w.dequant().t()
+    wd, sd, xd = w.w.to(DEV), w.s.to(DEV), x.to(DEV)
+    y = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    Kk.C().gemv(xd, wd, sd, y, Kk.GEMV_F32, 0.0)
+    torch.testing.assert_close(y.cpu(), ref, atol=2e-3, rtol=2e-3)
+    yb = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    Kk.C().gemv(xd, wd, sd, yb, Kk.GEMV_BF16, 0.0)
+    torch.testing.assert_close(yb.float().cpu(), ref, atol=2e-2, rtol=2e-2)
+    acc = torch.ones(M, N, dtype=torch.float32, device=DEV)
+    Kk.C().gemv(xd, wd, sd, acc, Kk.GEMV_F32_ACC, 0.0)
+    torch.testing.assert_close(acc.cpu(), ref + 1, atol=2e-3, rtol=2e-3)
+
+
+def test_gemv_swiglu_and_batched(C):
+    from glm53.models.runtime import interleave_gate_up
+    from glm53.models.weights import quantize_fp8_rows
+    from glm53.models.reference import swiglu
+    from glm53.ops import kernels as Kk
+    torch.manual_seed(0)
+    W, Kd, M = 256, 512, 8
+    gu = quantize_fp8_rows(torch.randn(2 * W, Kd) / math.sqrt(Kd))
+    x = torch.randn(M, Kd).to(torch.bfloat16)
+    full = x.float() @ gu.dequant().t()
+    g, u = full[:, :W].to(torch.bfloat16).float(), full[:, W:].to(torch.bfloat16).float()
+    ref = swiglu(g, u, 10.0)
+    il = interleave_gate_up(gu)
+    y = torch.empty(M, W, dtype=torch.bfloat16, device=DEV)
+    Kk.C().gemv(x.to(DEV), il.w.to(DEV), il.s.to(DEV), y, Kk.GEMV_SWIGLU, 10.0)
+    torch.testing.assert_close(y.float().cpu(), ref, atol=3e-2, rtol=3e-2)
+    # batched: [B, N, K] weights, per-batch strided inputs / outputs
+    Bn, N2, K2 = 4, 128, 64
+    wb = quantize_fp8_rows(torch.randn(Bn, N2, K2) / 8)
+    xb = torch.randn(M, Bn, 96).to(torch.bfloat16)            # use [:, :, :64] as a strided view
+    ref = torch.einsum("mbk,bnk->mbn", xb[:, :, :K2].float(), wb.dequant())
+    yb = torch.empty(M, Bn, N2, dtype=torch.float32, device=DEV)
+    xd = xb.to(DEV)
+    Kk.C().gemv(xd[:, :, :K2].transpose(0, 1), wb.w.to(DEV), wb.s.to(DEV), yb.transpose(0, 1), Kk.GEMV_F32, 0.0)
+    torch.testing.assert_close(yb.cpu(), ref, atol=2e-3, rtol=2e-3)
+
+
+def test_gemv_bf16(C):
+    from glm53.ops import kernels as Kk
+    torch.manual_seed(3)
+    x = torch.randn(5, 512).to(torch.bfloat16)
+    w = (torch.randn(288, 512) / 20).to(torch.bfloat16)
+    ref = x.float() @ w.float().t()
+    y = torch.empty(5, 288, device=DEV)
+    Kk.linear_bf16(x.to(DEV), w.to(DEV), y)
+    torch.testing.assert_close(y.cpu(), ref, atol=1e-3, rtol=1e-3)
+
+
+def _moe_ref(moe, cfg, x):
+    from glm53.models import reference as R
+    out = torch.zeros(x.shape[0], cfg.hidden)
+    ids, w = R.route(x, moe, cfg)
+    for r in range(x.shape[0]):
+        for k in range(cfg.top_k):
+            out[r] += w[r, k] * R.expert_forward(moe, int(ids[r, k]), x[r:r + 1], cfg)[0]
+    return out, ids
+
+
+@pytest.mark.parametrize("rows", [1, 8, 37])
+def test_moe_routed_exl3(C, tiny_cfg, tiny_weights, rows):
+    from glm53.models.runtime import Runtime, RuntimeConfig
+    cfg = tiny_cfg
+    lw = next(l for l in tiny_weights.layers if l.moe is not None)
+    w = tiny_weights
+    torch.manual_seed(rows)
+    x = torch.randn(rows, cfg.hidden).to(torch.bfloat16)
+    ref, ids = _moe_ref(lw.moe, cfg, x.float())
+    wd = _to_dev(w)
+    rt = Runtime(wd, RuntimeConfig(max_rows=64, kv_slots=256, max_blocks=4))
+    m = wd.layers[lw.index].moe
+    from glm53.ops import kernels as Kk
+    Kc = Kk.C()
+    xd = x.to(DEV)
+    P = rows * cfg.top_k
+    G = min(P, cfg.experts)
+    Kk.linear_bf16(xd, m.router, rt.rlogits[:rows])
+    Kc.moe_route(rt.rlogits[:rows], m.bias, cfg.top_k, cfg.routed_scale, cfg.norm_topk, rt.topk_ids[:rows],
+                 rt.topk_w[:rows], rt.group_count, rt.group_expert[:G], rt.group_offset[:G + 1], rt.pair_token[:P],
+                 rt.pair_expert[:P], rt.pair_w[:P], rt.pair_of[:P])
+    assert torch.equal(rt.topk_ids[:rows].cpu().long(), ids)
+    Kc.exl3_moe(xd, m.gate.trellis, m.gate.suh, m.gate.svh, m.up.trellis, m.up.suh, m.up.svh, m.down.trellis,
+                m.down.suh, m.down.svh, rt.group_count, rt.group_expert[:G], rt.group_offset[:G + 1],
+                rt.pair_token[:P], rt.pair_expert[:P], rt.pair_w[:P], rt.xh_g, rt.xh_u, rt.xd, rt.yd, cfg.limit)
+    out = torch.empty(rows, cfg.hidden, device=DEV)
+    Kc.moe_combine(rt.yd, rt.pair_of[:P], cfg.top_k, out, False)
+    torch.testing.assert_close(out.cpu(), ref, atol=2e-2, rtol=2e-2)
+
+
+def _to_dev(w):
+    import copy
+    from glm53.models import weights as W
+
+    def conv(o):
+        if isinstance(o, torch.Tensor):
+            return o.to(DEV)
+        if isinstance(o, list):
+            return [conv(v) for v in o]
+        if hasattr(o, "__dataclass_fields__"):
+            o2 = copy.copy(o)
+            for k in o.__dataclass_fields__:
+                setattr(o2, k, conv(getattr(o, k)))
+            return o2
+        return o
+    return conv(w)
+
+
+def test_hc_post_pre(C, tiny_cfg, tiny_weights):
+    from glm53.models import reference as R
+    cfg = tiny_cfg
+    lw = tiny_weights.layers[1]
+    torch.manual_seed(5)
+    Rr, S, D = 6, cfg.streams, cfg.hidden
+    X = torch.randn(Rr, S, D).to(torch.bfloat16)
+    branch = torch.randn(Rr, D)
+    pre0, post0, comb0 = R.hc_mix(X.float(), lw.attn_hc.fn, lw.attn_hc.base, lw.attn_hc.scale, S, cfg.eps,
+                                  cfg.hc_eps, cfg.hc_iters)
+    Xn = R.hc_post(X.float(), branch, post0, comb0)
+    normed_ref, post_ref, comb_ref = R.hc_pre(Xn, lw.ffn_hc, lw.post_norm, cfg)
+    Xd = X.to(DEV).contiguous()
+    normed = torch.empty(Rr, D, dtype=torch.bfloat16, device=DEV)
+    post = torch.empty(Rr, S, device=DEV)
+    comb = torch.empty(Rr, S, S, device=DEV)
+    part = torch.empty(Rr, D // 256, 32, device=DEV)
+    C.hc_post_pre(Xd, branch.to(DEV), post0.to(DEV), comb0.to(DEV), lw.ffn_hc.fn.to(DEV), lw.ffn_hc.base.to(DEV),
+                  lw.ffn_hc.scale.to(DEV), lw.post_norm.to(DEV), normed, post, comb, part, cfg.eps, cfg.hc_eps,
+                  cfg.hc_iters)
+    torch.testing.assert_close(Xd.float().cpu(), Xn, atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(post.cpu(), post_ref, atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(comb.cpu(), comb_ref, atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(normed.float().cpu(), normed_ref, atol=3e-2, rtol=2e-2)
+
+
+def test_dsa_select_radix(C):
+    """Radix top-k over pool logits equals a stable sort (ties -> lower index), expanded to token slots."""
+    torch.manual_seed(0)
+    kp, P, bs = 4, 16, 64
+    pos = 700
+    c = pos // kp
+    logits = torch.randn(1, 256)
+    logits[0, 10] = logits[0, 11] = logits[0, 12] = 5.0      # ties
+    from glm53.ops import kernels as Kk
+    Kc = Kk.C()
+    iproj = torch.zeros(1, 2 * 128 + 4, device=DEV)
+    qi = torch.zeros(1, 4 * 128, dtype=torch.bfloat16, device=DEV)
+    # run the select kernel alone by passing precomputed logits: zero pools give zero logits, so write the logits
+    # after the logits kernel through a custom path: use pool cache = 0 and compare with the expected dense rule
+    pool = torch.zeros(1024, 128, dtype=torch.uint8, device=DEV)
+    ps = torch.ones(1024, device=DEV)
+    bt = torch.arange(16, dtype=torch.int32, device=DEV).view(1, 16)
+    out_l = torch.zeros(1, 256, device=DEV)
+    sel = torch.zeros(1, P * kp, dtype=torch.int32, device=DEV)
+    cnt = torch.zeros(1, dtype=torch.int32, device=DEV)
+    positions = torch.tensor([pos], dtype=torch.int32, device=DEV)
+    rs = torch.zeros(1, dtype=torch.int32, device=DEV)
+    Kc.dsa_select(iproj, qi, torch.ones(128, device=DEV), pool, ps, positions, bt, rs, bs, 4, kp, P, out_l, sel, cnt)
+    # all-zero logits: ties everywhere -> the lowest P-1 pools are chosen
+    n = int(cnt.item())
+    assert n == (P - 1) * kp + (pos % kp) + 1
+    exp = list(range((P - 1) * kp)) + list(range(c * kp, pos + 1))
+    assert sel[0, :n].cpu().tolist() == exp

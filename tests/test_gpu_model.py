@@ -1,0 +1,72 @@
+"""The tiny proxy on the GPU runtime against the fp32 CPU oracle: teacher-forced logits over a
+128-token prompt + greedy continuation, verify windows with partial commit (KDA state rollback), and the DSA
+sparse path (context past index_topk = 64)."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _dev_weights(w):
+    from tests.test_gpu_kernels import _to_dev
+    return _to_dev(w)
+
+
+@pytest.fixture(scope="module")
+def oracle_run(tiny_cfg, tiny_weights):
+    from glm53.models.reference import ReferenceModel
+    m = ReferenceModel(tiny_weights)
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, tiny_cfg.vocab, (128,), generator=g).tolist()
+    toks, logits = m.generate_greedy(prompt, 24)
+    return prompt, toks, torch.stack(logits)
+
+
+def _close(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
+    return cos, (a - b).abs().max().item()
+
+
+def test_tiny_model_teacher_forced(tiny_cfg, tiny_weights, oracle_run):
+    from glm53.models.runtime import Runtime, RuntimeConfig
+    from glm53.models.session import Sequence
+    prompt, toks, ref_logits = oracle_run
+    rt = Runtime(_dev_weights(tiny_weights), RuntimeConfig(max_rows=64, kv_slots=1024, block_size=64, max_blocks=16))
+    seq = Sequence(rt)
+    lg = seq.prefill(prompt, chunk=64)
+    cos, mx = _close(lg[0], ref_logits[0])
+    assert cos > 0.999 and mx < 0.15, (cos, mx)
+    agree = 0
+    for i, t in enumerate(toks[:-1]):
+        lg = seq.verify([t])
+        seq.commit(1)
+        cos, mx = _close(lg[0], ref_logits[i + 1])
+        assert cos > 0.998 and mx < 0.25, (i, cos, mx)
+        agree += int(torch.argmax(lg[0]).item() == toks[i + 1])
+    assert agree >= len(toks) - 4
+
+
+def test_tiny_model_verify_window_and_rollback(tiny_cfg, tiny_weights, oracle_run):
+    """A window of 8 rows gives each row's logits; keeping 3 of them rolls the KDA state back exactly enough that
+    the continuation matches the oracle."""
+    from glm53.models.runtime import Runtime, RuntimeConfig
+    from glm53.models.session import Sequence
+    prompt, toks, ref_logits = oracle_run
+    rt = Runtime(_dev_weights(tiny_weights), RuntimeConfig(max_rows=64, kv_slots=1024, block_size=64, max_blocks=16))
+    seq = Sequence(rt)
+    seq.prefill(prompt, chunk=64)
+    window = [toks[0], toks[1], toks[2], 7, 8, 9, 10, 11]       # 3 correct drafts, then garbage
+    lg = seq.verify(window)
+    for i in range(3):
+        cos, mx = _close(lg[i], ref_logits[i + 1])
+        assert cos > 0.998, (i, cos, mx)
+    seq.commit(3)
+    for i in range(3, 10):
+        lg = seq.verify([toks[i]])
+        seq.commit(1)
+        cos, mx = _close(lg[0], ref_logits[i + 1])
+        assert cos > 0.998 and mx < 0.25, (i, cos, mx)
