@@ -181,7 +181,8 @@ def main():
     fwd = (lambda: rt.forward(rows, keep_window=True))
     if not args.no_graph:
         g_fwd = Graphed(fwd)
-        g_commit = Graphed(lambda: rt.commit([seq._seq_desc(rows)], replay=False))
+        rt.stage_commit([seq._seq_desc(rows)])
+        g_commit = Graphed(lambda: rt.commit(None, replay=False))
     drafts = torch.randint(0, cfg.vocab, (args.steps + args.warmup + 2, K), generator=gen)
 
     def step(i, tok):
@@ -194,8 +195,7 @@ def main():
         if args.no_graph:
             rt.commit([seq._seq_desc(rows)], replay=False)
         else:
-            # the commit graph reads commit_seq, staged with the same descriptor
-            rt.batch.commit_seq[:, :1].copy_(torch.tensor([list(seq._seq_desc(rows))], dtype=torch.int32).t())
+            rt.stage_commit([seq._seq_desc(rows)])      # the commit graph reads the staged descriptor
             g_commit()
         seq.cur = 1 - seq.cur
         seq.pos += rows

@@ -44,6 +44,10 @@ void gemv(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, 
   TORCH_CHECK(w.size(-1) == p.K, "K mismatch: x ", p.K, " w ", w.size(-1));
   p.ldx = x.stride(-2);
   p.bsx = batched ? x.stride(0) : 0;
+  // 16-byte vector loads of activations and weights: refuse operands that would fault
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && p.ldx % 8 == 0 && p.bsx % 8 == 0,
+              "gemv: activation rows must start on 16-byte boundaries (row stride ", p.ldx, ")");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0, "gemv: weights must be 16-byte aligned");
   p.bsw = batched ? w.stride(0) : 0;
   p.bss = (batched && scale.has_value()) ? scale->stride(0) : 0;
   p.ldy = y.stride(-2);
@@ -63,6 +67,58 @@ void gemv(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, 
     TORCH_CHECK(w.scalar_type() == at::kBFloat16, "weights must be fp8 (uint8) or bf16");
     check(g53_gemv_bf16(p, stream()), "gemv_bf16");
   }
+}
+
+// ------------------------------------------------------------------------------------------------- GEMM
+Tensor& err_word(const Tensor& like) {
+  static std::vector<Tensor> words(64);
+  const int dev = like.get_device();
+  if (!words[dev].defined()) words[dev] = torch::zeros({4}, like.options().dtype(at::kInt));
+  return words[dev];
+}
+
+void gemm_common(const Tensor& a, bool fp8, const OptT& a_scale, const Tensor& w, const OptT& w_scale, const Tensor& y,
+                 int64_t mode, double limit) {
+  GemmArgs p{};
+  p.a = a.data_ptr(); p.lda = a.stride(0);
+  p.b = w.data_ptr(); p.ldb = w.stride(0);
+  p.a_scale = P<const float>(a_scale);
+  p.b_scale = P<const float>(w_scale);
+  p.y = y.data_ptr(); p.ldy = y.stride(0);
+  p.M = (int)a.size(0); p.N = (int)w.size(0); p.K = (int)a.size(1);
+  p.mode = (int)mode; p.fp8 = fp8 ? 1 : 0; p.limit = (float)limit;
+  p.err = P<int>(err_word(a));
+  TORCH_CHECK(w.size(1) == p.K, "K mismatch");
+  if (mode == GEMV_BF16 || mode == GEMV_SWIGLU) {
+    TORCH_CHECK(y.scalar_type() == at::kBFloat16, "y must be bf16");
+  } else {
+    TORCH_CHECK(y.scalar_type() == at::kFloat, "y must be fp32");
+  }
+  check(g53_gemm_sm100(p, stream()), "gemm_sm100");
+}
+
+// W8A8: bf16 activations quantised per row to e4m3, fp8 weights with per-row scales
+void gemm_w8(const Tensor& x, const Tensor& w, const Tensor& scale, const Tensor& y, int64_t mode, double limit) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1);
+  const int64_t M = x.size(0), K = x.size(1);
+  auto q = torch::empty({M, K}, x.options().dtype(at::kByte));
+  auto qs = torch::empty({M}, x.options().dtype(at::kFloat));
+  check(g53_quant_rows_e4m3(P<const __nv_bfloat16>(x), x.stride(0), (int)M, (int)K, P<uint8_t>(q), P<float>(qs),
+                            stream()),
+        "quant_rows_e4m3");
+  gemm_common(q, true, qs, w, scale, y, mode, limit);
+}
+
+void gemm_bf16(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, int64_t mode, double limit) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16);
+  gemm_common(x, false, {}, w, scale, y, mode, limit);
+}
+
+int64_t gemm_error(const Tensor& like) {
+  auto& e = err_word(like);
+  const int64_t v = e[0].item<int>();
+  e.zero_();
+  return v;
 }
 
 // ------------------------------------------------------------------------------------------------- MoE
@@ -415,6 +471,9 @@ void rejection_sample(const Tensor& target_probs, const Tensor& draft_probs, con
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "glm53 sm_100a kernels";
   m.def("gemv", &gemv);
+  m.def("gemm_w8", &gemm_w8);
+  m.def("gemm_bf16", &gemm_bf16);
+  m.def("gemm_error", &gemm_error);
   m.def("moe_route", &moe_route);
   m.def("exl3_moe", &exl3_moe);
   m.def("moe_combine", &moe_combine);

@@ -1,0 +1,344 @@
+// Large-M GEMM for prefill on the 5th-generation tensor cores: Y[M, N] = (A[M, K] @ B[N, K]^T) * scales.
+//
+//   A  activations, K-major (bf16, or e4m3 with one fp32 scale per row)
+//   B  weights [N, K], K-major (bf16, or e4m3 with one fp32 scale per output row: the engine's fp8 weights)
+//
+// One CTA computes a 128 x BN tile.  Warp roles (192 threads):
+//   warp 0    TMA producer: one elected thread loads 128-byte-swizzled K-slices of A and B into a STAGES-deep
+//             shared-memory ring (cp.async.bulk.tensor, mbarrier complete_tx)
+//   warp 1    allocates BN TMEM columns; one thread issues tcgen05.mma (M=128, N=BN, kind::f16 or kind::f8f6f4)
+//             from shared-memory descriptors, accumulating in TMEM; tcgen05.commit frees each ring slot and
+//             finally signals the epilogue
+//   warps 2-5 epilogue: tcgen05.ld of the accumulator (one TMEM lane = one output row per thread), scales,
+//             optional SwiGLU over (8 gate, 8 up) row groups of the weight, bf16 / fp32 / fp32-accumulate stores
+// Every mbarrier wait is bounded; a wait that runs out sets an error word and the CTA stops issuing work (and
+// frees its TMEM), so a broken pipeline returns an error to the host instead of hanging the GPU.
+// No TMA multicast is used.
+// Reference counterparts: code/fork/kernels/fp8_w8a8.cu:134-219 (CUTLASS SM120 W8A8 GEMM) and
+// code/fork/kernels/fp8_large_m.cu (dequant + GEMM for large M).
+#include <cuda.h>
+#include "common.cuh"
+#include "launchers.h"
+
+namespace g53 {
+
+constexpr int kBM = 128;
+constexpr uint32_t kSpinLimit = 1u << 26;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// bounded wait: returns false (and records `code`) when the limit is reached or another thread already failed
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* fail, int* err, int code) {
+  uint32_t n = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if (*fail) return false;
+    if (++n > kSpinLimit) {
+      *fail = 1;
+      atomicExch(err, code);
+      return false;
+    }
+    if (n > 64) __nanosleep(64);
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major operand, 128-byte swizzle, 8-row groups 1024 bytes apart
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;                     // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;           // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                     // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                     // layout: 128-byte swizzle
+  return d;
+}
+
+// instruction descriptor: D f32, A/B format, both K-major, N and M
+__device__ __forceinline__ uint32_t umma_idesc(int fmt_ab, int n, int m) {
+  uint32_t d = 0;
+  d |= 1u << 4;                                // D = f32
+  d |= (uint32_t)fmt_ab << 7;                  // A format
+  d |= (uint32_t)fmt_ab << 10;                 // B format
+  d |= (uint32_t)(n >> 3) << 17;
+  d |= (uint32_t)(m >> 4) << 24;
+  return d;
+}
+
+template <bool FP8>
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  if constexpr (FP8) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+  } else {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+  }
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BN, bool FP8, int STAGES>
+__global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
+                                                            const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
+  constexpr int BK = FP8 ? 128 : 64;               // one 128-byte swizzle row per operand row
+  constexpr int A_BYTES = kBM * 128;
+  constexpr int B_BYTES = BN * 128;
+  constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr int UK = FP8 ? 32 : 16;                // K per tcgen05.mma
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t acc_bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ volatile int fail;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    fail = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&acc_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"((uint32_t)BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (kb >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1, &fail, p.err, 1)) break;
+        uint8_t* a_dst = smem + s * STAGE_BYTES;
+        uint8_t* b_dst = a_dst + A_BYTES;
+        mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+        tma_load_2d(&tmA, &full_bar[s], a_dst, kb * BK, m0);
+        tma_load_2d(&tmB, &full_bar[s], b_dst, kb * BK, n0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc(FP8 ? 0 : 1, BN, kBM);
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (!mbar_wait(&full_bar[s], ph, &fail, p.err, 2)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
+        const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+        for (int k = 0; k < BK / UK; ++k) {
+          const uint32_t koff = k * UK * (FP8 ? 1 : 2);    // bytes along the swizzled row
+          umma<FP8>(tmem, umma_desc_sw128(a_addr + koff), umma_desc_sw128(b_addr + koff), idesc,
+                    (kb > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty_bar[s]);
+      }
+      umma_commit(&acc_bar);
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
+    const int quad = warp & 3;
+    const int row = m0 + quad * 32 + lane;
+    int okw = 0;
+    if (lane == 0) okw = mbar_wait(&acc_bar, 0, &fail, p.err, 3) ? 1 : 0;
+    const bool ok = __shfl_sync(0xffffffffu, okw, 0) != 0;     // warp-uniform: tcgen05.ld is .sync.aligned
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok) {
+      const float rs = (p.a_scale && row < p.M) ? p.a_scale[row] : 1.f;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c0, v);
+        if (row >= p.M) continue;
+        const int nb = n0 + c0;
+        if (p.mode == GEMV_SWIGLU) {
+          // columns: two groups of (8 gate rows, 8 matching up rows) of the interleaved weight
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int ng = nb + g * 16 + i, nu = ng + 8;
+              if (nu >= p.N) continue;
+              float gv = round_bf16(v[g * 16 + i] * rs * (p.b_scale ? p.b_scale[ng] : 1.f));
+              float uv = round_bf16(v[g * 16 + 8 + i] * rs * (p.b_scale ? p.b_scale[nu] : 1.f));
+              gv = fminf(gv, p.limit);
+              uv = fminf(fmaxf(uv, -p.limit), p.limit);
+              reinterpret_cast<__nv_bfloat16*>(p.y)[(int64_t)row * p.ldy + ((nb + g * 16) >> 1) + i] =
+                  f2bf(siluf_(gv) * uv);
+            }
+          }
+          continue;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int n = nb + i;
+          if (n >= p.N) break;
+          const float val = v[i] * rs * (p.b_scale ? p.b_scale[n] : 1.f);
+          const int64_t off = (int64_t)row * p.ldy + n;
+          if (p.mode == GEMV_BF16) reinterpret_cast<__nv_bfloat16*>(p.y)[off] = f2bf(val);
+          else if (p.mode == GEMV_F32) reinterpret_cast<float*>(p.y)[off] = val;
+          else reinterpret_cast<float*>(p.y)[off] += val;
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN));
+  }
+}
+
+// per-row e4m3 quantisation of bf16 activations: scale = amax / 448
+__global__ void __launch_bounds__(256) quant_rows_e4m3_kernel(const __nv_bfloat16* x, int64_t ldx, int K,
+                                                              uint8_t* q, float* scale) {
+  const int r = blockIdx.x;
+  __shared__ float red[32];
+  float amax = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) amax = fmaxf(amax, fabsf(bf2f(x[(int64_t)r * ldx + k])));
+  amax = warp_max(amax);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  float m = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+  const float s = fmaxf(m, 1e-8f) / 448.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const __nv_fp8_e4m3 v(bf2f(x[(int64_t)r * ldx + k]) / s);
+    q[(int64_t)r * K + k] = v.__x;
+  }
+  if (threadIdx.x == 0) scale[r] = s;
+}
+
+}  // namespace g53
+
+using namespace g53;
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D K-major tile map: rows x K, box = box_rows x 128 bytes, 128-byte swizzle
+bool make_map(CUtensorMap* m, const void* base, bool fp8, int64_t rows, int64_t K, int64_t ld_elems, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const int esz = fp8 ? 1 : 2;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld_elems * esz)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / esz), (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, bool FP8, int STAGES>
+cudaError_t launch(const GemmArgs& p, cudaStream_t st) {
+  CUtensorMap ta, tb;
+  if (!make_map(&ta, p.a, FP8, p.M, p.K, p.lda, kBM)) return cudaErrorInvalidValue;
+  if (!make_map(&tb, p.b, FP8, p.N, p.K, p.ldb, BN)) return cudaErrorInvalidValue;
+  const int smem = STAGES * (kBM * 128 + BN * 128) + 1024;
+  auto kern = gemm_sm100_kernel<BN, FP8, STAGES>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((p.N + BN - 1) / BN, (p.M + kBM - 1) / kBM);
+  kern<<<grid, 192, smem, st>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t g53_gemm_sm100(const GemmArgs& p, cudaStream_t st) {
+  // alignment rules of the tensor maps: 16-byte aligned bases and row strides
+  const int esz = p.fp8 ? 1 : 2;
+  if ((reinterpret_cast<uintptr_t>(p.a) & 15) || (reinterpret_cast<uintptr_t>(p.b) & 15) ||
+      ((p.lda * esz) & 15) || ((p.ldb * esz) & 15) || (p.K * esz) % 16)
+    return cudaErrorInvalidValue;
+  if (p.fp8) return p.N >= 256 ? launch<256, true, 4>(p, st) : launch<128, true, 6>(p, st);
+  return p.N >= 256 ? launch<256, false, 4>(p, st) : launch<128, false, 6>(p, st);
+}
+
+cudaError_t g53_quant_rows_e4m3(const __nv_bfloat16* x, int64_t ldx, int R, int K, uint8_t* q, float* scale,
+                                cudaStream_t st) {
+  quant_rows_e4m3_kernel<<<R, 256, 0, st>>>(x, ldx, K, q, scale);
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}

@@ -21,6 +21,21 @@ struct GemvArgs {
 cudaError_t g53_gemv_fp8(const GemvArgs& p, cudaStream_t st);
 cudaError_t g53_gemv_bf16(const GemvArgs& p, cudaStream_t st);
 
+// ---------------------------------------------------------------- large-M GEMM (gemm_sm100.cu)
+struct GemmArgs {
+  const void* a; int64_t lda;          // [M, K] activations (bf16 or e4m3), K-major
+  const void* b; int64_t ldb;          // [N, K] weights (bf16 or e4m3), K-major
+  const float* a_scale;                // [M] (e4m3 activations) or null
+  const float* b_scale;                // [N] or null
+  void* y; int64_t ldy;
+  int M, N, K, mode, fp8;
+  float limit;
+  int* err;                            // device error word (bounded waits that ran out)
+};
+cudaError_t g53_gemm_sm100(const GemmArgs& p, cudaStream_t st);
+cudaError_t g53_quant_rows_e4m3(const __nv_bfloat16* x, int64_t ldx, int R, int K, uint8_t* q, float* scale,
+                                cudaStream_t st);
+
 // ---------------------------------------------------------------- MoE (moe.cu)
 struct RouteArgs {
   const float* logits;        // [R, E] fp32 router logits

@@ -71,6 +71,7 @@ class Batch:
         self.host = torch.zeros(4 * R + 10 * B + rc.logit_rows, dtype=i32, pin_memory=torch.cuda.is_available())
         self.R = 0
         self.B = 0
+        self.commit_B = 0
         self.max_rows_per_seq = 0
         self.n_logits = 0
 
@@ -109,6 +110,7 @@ class Runtime:
             self.kH, self.kDh = H, Dh
             width = k0.in_proj.n
             self.kda_width = width
+            width = (width + 63) // 64 * 64          # padded row stride: 16-byte aligned rows for vector loads
             C3 = 3 * H * Dh
             self.S_pool = [torch.zeros(2 * rc.max_seqs, H, Dh, Dh, dtype=f32, device=dev) for _ in kda]
             self.conv_pool = [torch.zeros(rc.max_seqs, c.conv - 1, C3, dtype=bf16, device=dev) for _ in kda]
@@ -362,16 +364,24 @@ class Runtime:
     # ------------------------------------------------------------------------------------------------------------
     # commit of a verify window
     # ------------------------------------------------------------------------------------------------------------
-    def commit(self, seqs_keep, replay: bool = True):
-        """seqs_keep: per sequence (row0, keep, s_in, s_out, conv_slot): the rows kept of the last forward, which
-        must have run with keep_window.  ``replay`` re-runs the KDA recurrence over the kept rows (needed when a
-        sequence keeps fewer rows than its window) so s_out holds the state after the last kept row."""
+    def stage_commit(self, seqs_keep):
+        """Stage the per-sequence (row0, keep, s_in, s_out, conv_slot) of a commit (outside any graph)."""
         b = self.batch
-        Kc = K.C()
         B = len(seqs_keep)
         sq = torch.as_tensor(seqs_keep, dtype=i32).t().contiguous()
-        b.commit_seq[:, :B].copy_(sq, non_blocking=True)
-        seq = b.commit_seq[:, :B]
+        b.commit_seq[:, :B].copy_(sq)
+        b.commit_B = B
+
+    def commit(self, seqs_keep=None, replay: bool = True):
+        """Keep rows of the last forward (run with keep_window): ``seqs_keep`` per sequence (row0, keep, s_in,
+        s_out, conv_slot), or None to use the staged descriptor (graph replays).  ``replay`` re-runs the KDA
+        recurrence over the kept rows (needed when a sequence keeps fewer rows than its window) so s_out holds
+        the state after the last kept row; the conv windows shift by the kept rows."""
+        b = self.batch
+        Kc = K.C()
+        if seqs_keep is not None:
+            self.stage_commit(seqs_keep)
+        seq = b.commit_seq[:, :b.commit_B]
         for lw in self.w.layers:
             if lw.kind != "kda":
                 continue

@@ -34,6 +34,16 @@ def so_path() -> str:
     return os.path.join(BUILD_DIR, NAME + ".so")
 
 
+def stale() -> bool:
+    """True when a source or header is newer than the built library."""
+    so = so_path()
+    if not os.path.exists(so):
+        return True
+    t = os.path.getmtime(so)
+    deps = sources() + glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh"))
+    return any(os.path.getmtime(f) > t for f in deps)
+
+
 def build(verbose: bool = False):
     """Compile every CUDA source for sm_100a (incremental) and return the loaded module."""
     global _mod
@@ -65,7 +75,7 @@ def load(build_if_missing: bool = True):
     with _lock:
         if _mod is not None:
             return _mod
-        if os.path.exists(so_path()):
+        if os.path.exists(so_path()) and not stale():
             _mod = _import_so(so_path())
             return _mod
     if build_if_missing:

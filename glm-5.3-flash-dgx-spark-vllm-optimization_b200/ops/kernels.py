@@ -3,12 +3,18 @@ works on preallocated outputs, so a sequence of calls can be captured in a CUDA 
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import _ext
 
+# the tcgen05 GEMM serves M >= GEMM_MIN_M rows (set GLM53_TCGEN05_GEMM=0 to route large M through the small-M kernel)
+GEMM_ENABLED = os.environ.get("GLM53_TCGEN05_GEMM", "0") == "1"
+
 GEMV_BF16, GEMV_F32, GEMV_F32_ACC, GEMV_SWIGLU = 0, 1, 2, 3
 GEMV_MAX_M = 16
+GEMM_MIN_M = 64          # rows from which the tcgen05 GEMM replaces the small-M kernel
 
 
 def C():
@@ -24,9 +30,8 @@ def linear8(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor, y: torch.Tensor, 
     if M <= GEMV_MAX_M:
         g(x, w, s, y, mode, limit)
         return y
-    gemm = getattr(C(), "gemm_w8", None)
-    if gemm is not None and M >= 64:
-        gemm(x, w, s, y, mode, limit)
+    if GEMM_ENABLED and M >= GEMM_MIN_M and x.dim() == 2:
+        C().gemm_w8(x, w, s, y, mode, limit)
         return y
     for m0 in range(0, M, GEMV_MAX_M):
         m1 = min(M, m0 + GEMV_MAX_M)
@@ -37,6 +42,9 @@ def linear8(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor, y: torch.Tensor, 
 def linear_bf16(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     """y fp32 [M, N] = x bf16 [M, K] @ w bf16 [N, K]^T."""
     M = x.shape[0]
+    if GEMM_ENABLED and M >= GEMM_MIN_M and x.stride(-1) == 1:
+        C().gemm_bf16(x, w, None, y, GEMV_F32, 0.0)
+        return y
     for m0 in range(0, M, GEMV_MAX_M):
         m1 = min(M, m0 + GEMV_MAX_M)
         C().gemv(x[m0:m1], w, None, y[m0:m1], GEMV_F32, 0.0)

@@ -1,0 +1,66 @@
+"""The tcgen05 GEMM (TMA + TMEM, kind::f16 and kind::f8f6f4) against an fp32 PyTorch reference (GPU only)."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def C():
+    from glm53.ops import _ext
+    return _ext.require()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 512), (200, 300, 1024), (1000, 4096, 4096), (64, 128, 128)])
+def test_gemm_bf16(C, M, N, K):
+    torch.manual_seed(M + N)
+    a = torch.randn(M, K, device=DEV).to(torch.bfloat16)
+    b = (torch.randn(N, K, device=DEV) / math.sqrt(K)).to(torch.bfloat16)
+    ref = a.float() @ b.float().t()
+    y = torch.zeros(M, N, device=DEV)
+    C.gemm_bf16(a, b, None, y, 1, 0.0)
+    torch.cuda.synchronize()
+    assert C.gemm_error(y) == 0
+    torch.testing.assert_close(y, ref, atol=2e-3, rtol=2e-3)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 512), (300, 1000, 2048), (2048, 4096, 4096)])
+def test_gemm_w8a8(C, M, N, K):
+    from glm53.models.weights import quantize_fp8_rows
+    torch.manual_seed(K)
+    w = quantize_fp8_rows(torch.randn(N, K) / math.sqrt(K))
+    x = torch.randn(M, K).to(torch.bfloat16)
+    amax = x.float().abs().amax(1, keepdim=True).clamp_min(1e-8)
+    xs = amax / 448.0
+    xq = (x.float() / xs).to(torch.float8_e4m3fn).float() * xs
+    ref = xq @ w.dequant().t()
+    y = torch.zeros(M, N, device=DEV)
+    C.gemm_w8(x.to(DEV), w.w.to(DEV), w.s.to(DEV), y, 1, 0.0)
+    torch.cuda.synchronize()
+    assert C.gemm_error(y) == 0
+    torch.testing.assert_close(y.cpu(), ref, atol=3e-3, rtol=3e-3)
+    yb = torch.zeros(M, N, device=DEV, dtype=torch.bfloat16)
+    C.gemm_w8(x.to(DEV), w.w.to(DEV), w.s.to(DEV), yb, 0, 0.0)
+    torch.testing.assert_close(yb.float().cpu(), ref, atol=3e-2, rtol=3e-2)
+
+
+def test_gemm_swiglu(C):
+    from glm53.models.runtime import interleave_gate_up
+    from glm53.models.weights import quantize_fp8_rows
+    from glm53.models.reference import swiglu
+    torch.manual_seed(0)
+    M, W, K = 256, 512, 1024
+    gu = quantize_fp8_rows(torch.randn(2 * W, K) / math.sqrt(K))
+    x = torch.randn(M, K).to(torch.bfloat16)
+    amax = x.float().abs().amax(1, keepdim=True).clamp_min(1e-8)
+    xq = (x.float() / (amax / 448)).to(torch.float8_e4m3fn).float() * (amax / 448)
+    full = xq @ gu.dequant().t()
+    ref = swiglu(full[:, :W].to(torch.bfloat16).float(), full[:, W:].to(torch.bfloat16).float(), 10.0)
+    il = interleave_gate_up(gu)
+    y = torch.zeros(M, W, device=DEV, dtype=torch.bfloat16)
+    C.gemm_w8(x.to(DEV), il.w.to(DEV), il.s.to(DEV), y, 3, 10.0)
+    torch.testing.assert_close(y.float().cpu(), ref, atol=5e-2, rtol=5e-2)
