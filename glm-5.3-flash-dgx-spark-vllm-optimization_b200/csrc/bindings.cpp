@@ -227,7 +227,7 @@ void hc_post_pre(const Tensor& X, const OptT& branch, const OptT& post, const Op
   a.hc_eps = (float)hc_eps;
   a.iters = (int)iters;
   TORCH_CHECK(X.is_contiguous(), "X must be contiguous [R, S, D]");
-  TORCH_CHECK(part.numel() >= (int64_t)a.R * (a.D / 256) * 32, "part scratch too small");
+  TORCH_CHECK(part.numel() >= (int64_t)a.R * (a.D / 64) * 32, "part scratch too small");
   check(g53_hc_post_pre(a, stream()), "hc_post_pre");
 }
 
@@ -299,6 +299,21 @@ void kda_recurrent(const Tensor& proj, const Tensor& seq, const Tensor& f, const
   a.b_off = (int)b_off;
   a.lower = (float)lower;
   check(g53_kda_recurrent(a, stream()), "kda_recurrent");
+}
+
+void kda_chunk(const Tensor& proj, const Tensor& seq, const Tensor& f, const Tensor& qkv, const Tensor& a_log,
+               const Tensor& dt_bias, const Tensor& S_pool, const Tensor& o_raw, int64_t H, int64_t Dh, int64_t b_off,
+               double lower) {
+  KdaArgs a = kda_args(proj, seq, 0, H, Dh, 0);
+  a.f = P<const __nv_bfloat16>(f);
+  a.qkv = P<__nv_bfloat16>(qkv);
+  a.a_log = P<const float>(a_log);
+  a.dt_bias = P<const float>(dt_bias);
+  a.S_pool = P<float>(S_pool);
+  a.o_raw = P<float>(o_raw);
+  a.b_off = (int)b_off;
+  a.lower = (float)lower;
+  check(g53_kda_chunk(a, stream()), "kda_chunk");
 }
 
 void kda_gated_norm(const Tensor& o_raw, const Tensor& gate, const Tensor& o_norm, const Tensor& out, int64_t H,
@@ -486,6 +501,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kda_conv_commit", &kda_conv_commit);
   m.def("kda_recurrent", &kda_recurrent);
   m.def("kda_gated_norm", &kda_gated_norm);
+  m.def("kda_chunk", &kda_chunk);
   m.def("mla_prep", &mla_prep);
   m.def("rope_q", &rope_q);
   m.def("mla_decode", &mla_decode);

@@ -13,12 +13,15 @@
 //
 // Reference counterparts: code/fork/kernels/fp8_gemv.cu:96 (Marlin-layout fp8 GEMV, M <= 64) and
 // code/fork/kernels/gemv_bf16.cu:83 (router / small bf16 GEMM).
+#include <cooperative_groups.h>
 #include "common.cuh"
 #include "launchers.h"
 
+namespace cg = cooperative_groups;
+
 namespace g53 {
 
-template <bool FP8, int KS, int NT>
+template <bool FP8, int KS, int NT, int CL>
 __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
   constexpr int CH = FP8 ? 64 : 32;            // k elements per lane-load chunk (16 bytes of weight)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -26,7 +29,11 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
   const int ks = warp % KS, tile = warp / KS;
   const int b = blockIdx.y;
   const int n0 = (blockIdx.x * NT + tile) * 16;
-  const int nchunk = p.K / CH;
+  const int nchunk_all = p.K / CH;
+  // cluster split of K: CTA z of the cluster covers chunks [c_lo, c_hi)
+  const int per = (nchunk_all + CL - 1) / CL;
+  const int c_lo = (CL > 1 ? (int)blockIdx.z : 0) * per;
+  const int nchunk = min(nchunk_all, c_lo + per);
   const bool two = p.M > 8;
 
   const uint8_t* wbase = reinterpret_cast<const uint8_t*>(p.w) + (int64_t)b * p.bsw * (FP8 ? 1 : 2);
@@ -43,7 +50,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
   const uint4 z4 = make_uint4(0, 0, 0, 0);
 
 #pragma unroll 4
-  for (int c = ks; c < nchunk; c += KS) {
+  for (int c = c_lo + ks; c < nchunk; c += KS) {
     const int kb = c * CH + q * (CH / 4);
     uint4 wa = rA ? ldg_nc_v4(wr0 + (int64_t)kb * esz) : z4;
     uint4 wb = rB ? ldg_nc_v4(wr1 + (int64_t)kb * esz) : z4;
@@ -100,6 +107,34 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
     red2[ks][tile][g + 8][2 * q + 1] = acc1[3];
   }
   __syncthreads();
+  // tile sums (fixed warp order) -> tot[t][row][tok]
+  __shared__ float tot[NT][16][17];
+  for (int e = threadIdx.x; e < NT * 16 * 16; e += blockDim.x) {
+    const int t = e / 256, r = (e / 16) % 16, tok = e % 16;
+    float v = 0.f;
+    if (tok < p.M) {
+#pragma unroll
+      for (int s2 = 0; s2 < KS; ++s2) v += tok < 8 ? red[s2][t][r][tok] : red2[s2][t][r][tok - 8];
+    }
+    tot[t][r][tok] = v;
+  }
+  if constexpr (CL > 1) {
+    // cluster reduction over distributed shared memory, in rank order, by rank 0
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (cluster.block_rank() == 0) {
+      for (int e = threadIdx.x; e < NT * 16 * 16; e += blockDim.x) {
+        const int t = e / 256, r = (e / 16) % 16, tok = e % 16;
+        float v = tot[t][r][tok];
+        for (int q2 = 1; q2 < CL; ++q2) v += cluster.map_shared_rank(&tot[0][0][0], q2)[(t * 16 + r) * 17 + tok];
+        tot[t][r][tok] = v;
+      }
+    }
+    cluster.sync();
+    if (cluster.block_rank() != 0) return;
+  } else {
+    __syncthreads();
+  }
   const float* scale = p.scale ? p.scale + (int64_t)b * p.bss : nullptr;
   if (p.mode == GEMV_SWIGLU) {
     // rows 0..7 of every 16-row tile are gate rows j0..j0+7, rows 8..15 the matching up rows
@@ -108,12 +143,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
       if (tok >= p.M) continue;
       const int nt0 = (blockIdx.x * NT + t) * 16;
       if (nt0 + r + 8 >= p.N) continue;
-      float gv = 0.f, uv = 0.f;
-#pragma unroll
-      for (int s = 0; s < KS; ++s) {
-        gv += tok < 8 ? red[s][t][r][tok] : red2[s][t][r][tok - 8];
-        uv += tok < 8 ? red[s][t][r + 8][tok] : red2[s][t][r + 8][tok - 8];
-      }
+      float gv = tot[t][r][tok], uv = tot[t][r + 8][tok];
       if (scale) { gv *= scale[nt0 + r]; uv *= scale[nt0 + r + 8]; }
       // y stored as bf16 values of g and u first (the MLP output rounding points), then the activation
       gv = round_bf16(gv);
@@ -130,9 +160,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
     const int t = e / 256, r = (e / 16) % 16, tok = e % 16;
     const int n = (blockIdx.x * NT + t) * 16 + r;
     if (tok >= p.M || n >= p.N) continue;
-    float v = 0.f;
-#pragma unroll
-    for (int s = 0; s < KS; ++s) v += tok < 8 ? red[s][t][r][tok] : red2[s][t][r][tok - 8];
+    float v = tot[t][r][tok];
     if (scale) v *= scale[n];
     const int64_t off = (int64_t)b * p.bsy + (int64_t)tok * p.ldy + n;
     if (p.mode == GEMV_BF16) {
@@ -142,6 +170,32 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
     } else {  // GEMV_F32_ACC
       reinterpret_cast<float*>(p.y)[off] += v;
     }
+  }
+}
+
+template <bool FP8, int KS, int NT>
+static cudaError_t launch_cfg(const GemvArgs& p, dim3 grid, int cl, cudaStream_t st) {
+  if (cl <= 1) {
+    gemv_kernel<FP8, KS, NT, 1><<<grid, 256, 0, st>>>(p);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  grid.z = cl;
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = cl;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  switch (cl) {
+    case 2: return cudaLaunchKernelEx(&cfg, gemv_kernel<FP8, KS, NT, 2>, p);
+    case 4: return cudaLaunchKernelEx(&cfg, gemv_kernel<FP8, KS, NT, 4>, p);
+    default: return cudaLaunchKernelEx(&cfg, gemv_kernel<FP8, KS, NT, 8>, p);
   }
 }
 
@@ -155,14 +209,16 @@ static cudaError_t launch_gemv_t(const GemvArgs& p, cudaStream_t st) {
   const int tiles = (p.N + 15) / 16;
   const int nt = 8 / ks;
   dim3 grid((tiles + nt - 1) / nt, p.batch);
+  // too few CTAs to cover the SMs: split K across a cluster (DSMEM reduction)
+  int cl = 1;
+  const int ctas = grid.x * grid.y;
+  while (cl < 8 && ctas * cl < 296 && nchunk >= ks * cl * 4) cl <<= 1;
   switch (ks) {
-    case 8: gemv_kernel<FP8, 8, 1><<<grid, 256, 0, st>>>(p); break;
-    case 4: gemv_kernel<FP8, 4, 2><<<grid, 256, 0, st>>>(p); break;
-    case 2: gemv_kernel<FP8, 2, 4><<<grid, 256, 0, st>>>(p); break;
-    default: gemv_kernel<FP8, 1, 8><<<grid, 256, 0, st>>>(p); break;
+    case 8: return launch_cfg<FP8, 8, 1>(p, grid, cl, st);
+    case 4: return launch_cfg<FP8, 4, 2>(p, grid, cl, st);
+    case 2: return launch_cfg<FP8, 2, 4>(p, grid, cl, st);
+    default: return launch_cfg<FP8, 1, 8>(p, grid, cl, st);
   }
-  G53_CHECK_LAUNCH();
-  return cudaSuccess;
 }
 
 }  // namespace g53

@@ -131,16 +131,8 @@ cudaError_t g53_kda_conv(const KdaArgs& a, cudaStream_t st);          // qkv = s
 cudaError_t g53_kda_recurrent(const KdaArgs& a, cudaStream_t st);     // per sequence: S_in -> S_out, o_raw
 cudaError_t g53_kda_gated_norm(const KdaArgs& a, cudaStream_t st);    // out = rmsnorm(o_raw) * w * sigmoid(gate)
 cudaError_t g53_kda_conv_commit(const KdaArgs& a, cudaStream_t st);   // window <- last taps-1 of window ++ nrows rows
-struct KdaChunkArgs {
-  const __nv_bfloat16* qkv;    // [T, 3*H*Dh] post-conv q|k|v (bf16)
-  const __nv_bfloat16* f; const __nv_bfloat16* proj; int64_t ldp;
-  const float* a_log; const float* dt_bias;
-  float* S;                    // [H, Dh, Dh] in/out state
-  float* o_raw;                // [T, H*Dh]
-  int T, H, Dh, b_off, chunk;
-  float lower;
-};
-cudaError_t g53_kda_chunk(const KdaChunkArgs& a, cudaStream_t st);
+// chunked (64-token) form of g53_kda_recurrent for prefill: same inputs/outputs, per-sequence rows in chunks
+cudaError_t g53_kda_chunk(const KdaArgs& a, cudaStream_t st);
 
 // ---------------------------------------------------------------- MLA / DSA (mla.cu, dsa.cu)
 struct MlaPrepArgs {

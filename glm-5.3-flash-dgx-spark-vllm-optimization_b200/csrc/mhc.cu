@@ -15,7 +15,7 @@
 
 namespace g53 {
 
-constexpr int kDB = 256;     // columns per partial CTA
+constexpr int kDB = 64;      // columns per partial CTA (one per thread)
 constexpr int kRB = 16;      // rows per partial CTA
 constexpr int kMaxMix = 24;
 
@@ -24,8 +24,7 @@ __global__ void __launch_bounds__(kDB) hc_partial_kernel(HcArgs a) {
   constexpr int NM = 2 * S + S * S;
   const int d = blockIdx.x * kDB + threadIdx.x;
   const int NB = a.D / kDB;
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  __shared__ float red[kDB / 32][NM + 1];
+  __shared__ float red[kDB][NM + 2];
   const bool pre = a.fn != nullptr;     // post only when no mixing weights are given
   float fnv[NM][S];
 #pragma unroll
@@ -52,30 +51,46 @@ __global__ void __launch_bounds__(kDB) hc_partial_kernel(HcArgs a) {
       for (int s = 0; s < S; ++s) { x[s] = nx[s]; xr[s * a.D + d] = f2bf(nx[s]); }
     }
     if (!pre) continue;
-    float v[NM + 1];
 #pragma unroll
     for (int i = 0; i < NM; ++i) {
       float t = 0.f;
 #pragma unroll
       for (int s = 0; s < S; ++s) t += fnv[i][s] * x[s];
-      v[i] = warp_sum(t);
+      red[threadIdx.x][i] = t;
     }
     float ss = 0.f;
 #pragma unroll
     for (int s = 0; s < S; ++s) ss += x[s] * x[s];
-    v[NM] = warp_sum(ss);
-    if (lane == 0) {
-#pragma unroll
-      for (int i = 0; i <= NM; ++i) red[wid][i] = v[i];
-    }
+    red[threadIdx.x][NM] = ss;
     __syncthreads();
     if (threadIdx.x <= NM) {
       float t = 0.f;
-      for (int w = 0; w < kDB / 32; ++w) t += red[w][threadIdx.x];
+      for (int c = 0; c < kDB; ++c) t += red[c][threadIdx.x];      // fixed order
       a.part[((int64_t)r * NB + blockIdx.x) * 32 + threadIdx.x] = t;
     }
     __syncthreads();
   }
+}
+
+// Sinkhorn on one warp: lane l < S*S holds comb[l / S][l % S]; rows reduce over the low log2(S) lane bits,
+// columns over the next log2(S) bits
+template <int S>
+__device__ __forceinline__ float warp_row_sum(float v) {
+#pragma unroll
+  for (int o = 1; o < S; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+template <int S>
+__device__ __forceinline__ float warp_row_max(float v) {
+#pragma unroll
+  for (int o = 1; o < S; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+template <int S>
+__device__ __forceinline__ float warp_col_sum(float v) {
+#pragma unroll
+  for (int o = S; o < S * S; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
 }
 
 template <int S>
@@ -86,45 +101,30 @@ __global__ void __launch_bounds__(512) hc_finish_kernel(HcArgs a) {
   __shared__ float mix[32];
   __shared__ float pre_s[S], post_s[S], comb_s[S * S];
   __shared__ float red[32];
-  if (threadIdx.x <= NM) {
+  // partial sums: warp w sums mixes in fixed block order
+  if (threadIdx.x < 32 && threadIdx.x <= NM) {
     float t = 0.f;
     for (int b = 0; b < NB; ++b) t += a.part[((int64_t)r * NB + b) * 32 + threadIdx.x];
     mix[threadIdx.x] = t;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
     const float rinv = rsqrtf(mix[NM] / (float)(S * a.D) + a.eps);
-    float c[S][S];
-    for (int s = 0; s < S; ++s) {
-      pre_s[s] = sigmoidf_(mix[s] * rinv * a.hscale[0] + a.base[s]) + a.hc_eps;
-      post_s[s] = 2.f * sigmoidf_(mix[S + s] * rinv * a.hscale[1] + a.base[S + s]);
+    if (lane < S) {
+      pre_s[lane] = sigmoidf_(mix[lane] * rinv * a.hscale[0] + a.base[lane]) + a.hc_eps;
+      post_s[lane] = 2.f * sigmoidf_(mix[S + lane] * rinv * a.hscale[1] + a.base[S + lane]);
     }
-    for (int i = 0; i < S; ++i) {
-      float mx = -INFINITY;
-      for (int j = 0; j < S; ++j) {
-        c[i][j] = mix[2 * S + i * S + j] * rinv * a.hscale[2] + a.base[2 * S + i * S + j];
-        mx = fmaxf(mx, c[i][j]);
-      }
-      float sum = 0.f;
-      for (int j = 0; j < S; ++j) { c[i][j] = __expf(c[i][j] - mx); sum += c[i][j]; }
-      for (int j = 0; j < S; ++j) c[i][j] = c[i][j] / sum + a.hc_eps;
-    }
+    const int li = lane < S * S ? lane : 0;
+    float c = mix[2 * S + li] * rinv * a.hscale[2] + a.base[2 * S + li];
+    const float mx = warp_row_max<S>(c);
+    c = __expf(c - mx);
+    c = c / warp_row_sum<S>(c) + a.hc_eps;
     for (int it = 0; it < a.iters; ++it) {
-      if (it > 0) {
-        for (int i = 0; i < S; ++i) {
-          float sum = 0.f;
-          for (int j = 0; j < S; ++j) sum += c[i][j];
-          for (int j = 0; j < S; ++j) c[i][j] /= (sum + a.hc_eps);
-        }
-      }
-      for (int j = 0; j < S; ++j) {
-        float sum = 0.f;
-        for (int i = 0; i < S; ++i) sum += c[i][j];
-        for (int i = 0; i < S; ++i) c[i][j] /= (sum + a.hc_eps);
-      }
+      if (it > 0) c = c / (warp_row_sum<S>(c) + a.hc_eps);
+      c = c / (warp_col_sum<S>(c) + a.hc_eps);
     }
-    for (int i = 0; i < S; ++i)
-      for (int j = 0; j < S; ++j) comb_s[i * S + j] = c[i][j];
+    if (lane < S * S) comb_s[lane] = c;
   }
   __syncthreads();
   if (threadIdx.x < S) a.post_out[r * S + threadIdx.x] = post_s[threadIdx.x];

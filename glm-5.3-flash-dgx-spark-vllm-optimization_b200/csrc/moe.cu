@@ -52,7 +52,7 @@ __device__ __forceinline__ void trellis_frags(uint32_t cur, uint32_t prev, uint3
 // routing: sigmoid scores, top-k of score + bias (ties -> lower id), normalised weights; then grouping of the
 // R*top_k (row, slot) pairs by expert (ascending id; within an expert, ascending pair index).  One CTA.
 // ---------------------------------------------------------------------------------------------------------------
-constexpr int kMaxE = 1024;
+constexpr int kMaxE = 512;
 constexpr int kMaxPairs = 2048;
 
 __global__ void __launch_bounds__(1024) moe_route_kernel(RouteArgs a) {
@@ -64,23 +64,26 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(RouteArgs a) {
   const int P = a.R * a.top_k;
   for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
-  // top-k per row: one warp per row
+  // top-k per row: one warp per row; lane l holds candidates e = l + 32 i in registers
+  constexpr int kPerLane = kMaxE / 32;
   for (int r = wid; r < a.R; r += nw) {
     const float* lg = a.logits + (int64_t)r * a.E;
+    float cv[kPerLane];
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) {
+      const int e = lane + 32 * i;
+      cv[i] = e < a.E ? sigmoidf_(lg[e]) + a.bias[e] : -INFINITY;
+    }
     float sel_sum = 0.f;
-    unsigned long long taken[kMaxE / 64] = {};
-    (void)taken;
-    int picks[16];
-    float wts[16];
+    int pick_l = 0;
+    float wt_l = 0.f;
     for (int k = 0; k < a.top_k; ++k) {
       float best = -INFINITY;
       int bid = 0x7fffffff;
-      for (int e = lane; e < a.E; e += 32) {
-        bool used = false;
-        for (int j = 0; j < k; ++j) used |= (picks[j] == e);
-        if (used) continue;
-        const float c = sigmoidf_(lg[e]) + a.bias[e];
-        if (c > best || (c == best && e < bid)) { best = c; bid = e; }
+#pragma unroll
+      for (int i = 0; i < kPerLane; ++i) {
+        const int e = lane + 32 * i;
+        if (cv[i] > best) { best = cv[i]; bid = e; }      // ascending e within a lane: first max = lowest id
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
@@ -88,18 +91,21 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(RouteArgs a) {
         const int oi = __shfl_xor_sync(0xffffffffu, bid, o);
         if (ob > best || (ob == best && oi < bid)) { best = ob; bid = oi; }
       }
-      picks[k] = bid;
-      wts[k] = sigmoidf_(lg[bid]);
-      sel_sum += wts[k];
-    }
-    if (lane == 0) {
-      const float inv = a.norm ? 1.f / (sel_sum + 1e-20f) : 1.f;
-      for (int k = 0; k < a.top_k; ++k) {
-        a.topk_ids[r * a.top_k + k] = picks[k];
-        a.topk_w[r * a.top_k + k] = wts[k] * inv * a.scale;
-        pe[r * a.top_k + k] = picks[k];
-        atomicAdd(&cnt[picks[k]], 1);
+      if ((bid & 31) == lane) {
+#pragma unroll
+        for (int i = 0; i < kPerLane; ++i)
+          if (lane + 32 * i == bid) cv[i] = -INFINITY;
       }
+      const float w = sigmoidf_(lg[bid]);
+      sel_sum += w;
+      if (lane == k) { pick_l = bid; wt_l = w; }
+    }
+    const float inv = a.norm ? 1.f / (sel_sum + 1e-20f) : 1.f;
+    if (lane < a.top_k) {
+      a.topk_ids[r * a.top_k + lane] = pick_l;
+      a.topk_w[r * a.top_k + lane] = wt_l * inv * a.scale;
+      pe[r * a.top_k + lane] = pick_l;
+      atomicAdd(&cnt[pick_l], 1);
     }
   }
   __syncthreads();
@@ -367,7 +373,7 @@ __global__ void exl3_unpack_kernel(const int16_t* tr, int K, int N, __half* out)
 using namespace g53;
 
 cudaError_t g53_moe_route(const RouteArgs& a, cudaStream_t st) {
-  if (a.E > kMaxE || a.R * a.top_k > kMaxPairs || a.top_k > 16) return cudaErrorInvalidValue;
+  if (a.E > kMaxE || a.R * a.top_k > kMaxPairs || a.top_k > 32) return cudaErrorInvalidValue;
   moe_route_kernel<<<1, 1024, 0, st>>>(a);
   G53_CHECK_LAUNCH();
   return cudaSuccess;

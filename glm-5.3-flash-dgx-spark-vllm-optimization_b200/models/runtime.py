@@ -27,6 +27,7 @@ from ..ops import kernels as K
 from .weights import Linear8, Weights
 
 bf16, f32, i32 = torch.bfloat16, torch.float32, torch.int32
+KDA_CHUNK_MIN_ROWS = 32     # prefill windows longer than this use the chunked KDA kernel
 
 
 @dataclass
@@ -95,7 +96,7 @@ class Runtime:
         self.normed = torch.zeros(R, D, dtype=bf16, device=dev)
         self.post = [torch.zeros(R, S, dtype=f32, device=dev) for _ in range(2)]
         self.comb = [torch.zeros(R, S, S, dtype=f32, device=dev) for _ in range(2)]
-        self.part = torch.zeros(R, D // 256, 32, dtype=f32, device=dev)
+        self.part = torch.zeros(R, D // 64, 32, dtype=f32, device=dev)
         self.branch = torch.zeros(R, D, dtype=f32, device=dev)
         self.hidden = torch.zeros(R, D, dtype=bf16, device=dev)
         self.fnormed = torch.zeros(R, D, dtype=bf16, device=dev)
@@ -279,7 +280,11 @@ class Runtime:
         Kc.kda_conv(proj, seq, b.max_rows_per_seq, k.conv, self.conv_pool[li], qkv, H, Dh)
         if not self._keep_window:       # prefill chunk: every row is kept, shift the conv window now
             Kc.kda_conv_commit(proj, seq, self.conv_pool[li], H, Dh, c.conv)
-        Kc.kda_recurrent(proj, seq, fb, qkv, k.a_log, k.dt_bias, self.S_pool[li], self.ko[:R], H, Dh,
+        if self._keep_window or b.max_rows_per_seq <= KDA_CHUNK_MIN_ROWS:
+            Kc.kda_recurrent(proj, seq, fb, qkv, k.a_log, k.dt_bias, self.S_pool[li], self.ko[:R], H, Dh,
+                             C3 + 2 * Dh, c.lower)
+        else:       # prefill: 64-token chunked form of the same recurrence
+            Kc.kda_chunk(proj, seq, fb, qkv, k.a_log, k.dt_bias, self.S_pool[li], self.ko[:R], H, Dh,
                          C3 + 2 * Dh, c.lower)
         Kc.kda_gated_norm(self.ko[:R], self.kg[:R], k.o_norm, self.kout[:R], H, Dh, c.eps)
         K.linear8(self.kout[:R], k.o_proj.w, k.o_proj.s, self.branch[:R], K.GEMV_F32)

