@@ -109,6 +109,18 @@ void gemm_w8(const Tensor& x, const Tensor& w, const Tensor& scale, const Tensor
   gemm_common(q, true, qs, w, scale, y, mode, limit);
 }
 
+// W8A16: the fp8 weight widened exactly to bf16 in a scratch, then the bf16 tcgen05 GEMM with the per-row
+// weight scales applied in the epilogue (same numerics as the small-M kernel: bf16 activations, exact weights)
+void gemm_w8a16(const Tensor& x, const Tensor& w, const Tensor& scale, const Tensor& y, int64_t mode, double limit,
+                const Tensor& scratch) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1);
+  TORCH_CHECK(scratch.scalar_type() == at::kBFloat16 && scratch.numel() >= w.numel(), "scratch too small");
+  TORCH_CHECK(w.is_contiguous());
+  check(g53_e4m3_to_bf16(P<const uint8_t>(w), w.numel(), P<__nv_bfloat16>(scratch), stream()), "e4m3_to_bf16");
+  auto wb = scratch.flatten().narrow(0, 0, w.numel()).view({w.size(0), w.size(1)});
+  gemm_common(x, false, {}, wb, scale, y, mode, limit);
+}
+
 void gemm_bf16(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, int64_t mode, double limit) {
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16);
   gemm_common(x, false, {}, w, scale, y, mode, limit);
@@ -188,6 +200,77 @@ void exl3_moe(const Tensor& x, const Tensor& tr_g, const Tensor& suh_g, const Te
   check(g53_exl3_rot_in(a, stream()), "exl3_rot_in");
   check(g53_exl3_gate_up(a, stream()), "exl3_gate_up");
   check(g53_exl3_down(a, stream()), "exl3_down");
+}
+
+void exl3_rot_in(const Tensor& x, const Tensor& suh_g, const Tensor& suh_u, const Tensor& pair_token,
+                 const Tensor& pair_expert, const Tensor& xh_g, const Tensor& xh_u) {
+  Exl3Args a{};
+  a.x = P<const __nv_bfloat16>(x);
+  a.ldx = x.stride(0);
+  a.suh_g = P<const __half>(suh_g);
+  a.suh_u = P<const __half>(suh_u);
+  a.K = (int)suh_g.size(-1);
+  a.pair_token = P<const int>(pair_token);
+  a.pair_expert = P<const int>(pair_expert);
+  a.pairs = (int)pair_token.size(0);
+  a.xh_g = P<__half>(xh_g);
+  a.xh_u = P<__half>(xh_u);
+  TORCH_CHECK(xh_g.size(0) >= a.pairs && xh_u.size(0) >= a.pairs);
+  check(g53_exl3_rot_in(a, stream()), "exl3_rot_in");
+}
+
+void moe_route_large(const Tensor& logits, const Tensor& bias, int64_t top_k, double scale, bool norm,
+                     const Tensor& topk_ids, const Tensor& topk_w, const Tensor& group_count,
+                     const Tensor& group_expert, const Tensor& group_offset, const Tensor& pair_token,
+                     const Tensor& pair_expert, const Tensor& pair_w, const Tensor& pair_of, const Tensor& counts,
+                     const Tensor& fill) {
+  RouteArgs a{};
+  a.logits = P<const float>(logits);
+  a.bias = P<const float>(bias);
+  a.R = (int)logits.size(0);
+  a.E = (int)logits.size(1);
+  a.top_k = (int)top_k;
+  a.scale = (float)scale;
+  a.norm = norm ? 1 : 0;
+  a.topk_ids = P<int>(topk_ids);
+  a.topk_w = P<float>(topk_w);
+  a.group_count = P<int>(group_count);
+  a.group_expert = P<int>(group_expert);
+  a.group_offset = P<int>(group_offset);
+  a.pair_token = P<int>(pair_token);
+  a.pair_expert = P<int>(pair_expert);
+  a.pair_w = P<float>(pair_w);
+  a.pair_of = P<int>(pair_of);
+  a.max_groups = (int)group_expert.size(0);
+  TORCH_CHECK(counts.numel() >= a.E && fill.numel() >= a.E);
+  check(g53_moe_route_large(a, P<int>(counts), P<int>(fill), stream()), "moe_route_large");
+}
+
+void moe_prefill(const Tensor& tr0, const OptT& tr1, const Tensor& svh0, const OptT& svh1, const OptT& suh_next,
+                 const OptT& pair_w, const Tensor& group_count, const Tensor& group_expert, const Tensor& group_offset,
+                 const Tensor& x0, const OptT& x1, const Tensor& out, double limit, bool gate_up) {
+  MoePrefillArgs p{};
+  p.tr0 = P<const int16_t>(tr0);
+  p.tr1 = tr1.has_value() ? P<const int16_t>(tr1) : p.tr0;
+  p.svh0 = P<const __half>(svh0);
+  p.svh1 = P<const __half>(svh1);
+  p.suh_next = P<const __half>(suh_next);
+  p.pair_w = P<const float>(pair_w);
+  p.group_count = P<const int>(group_count);
+  p.group_expert = P<const int>(group_expert);
+  p.group_offset = P<const int>(group_offset);
+  p.x0 = P<const __half>(x0);
+  p.x1 = P<const __half>(x1);
+  p.rows = x0.size(0);
+  p.K = (int)x0.size(1);
+  p.N = (int)svh0.size(-1);
+  p.max_groups = (int)group_expert.size(0);
+  p.out = out.data_ptr();
+  p.limit = (float)limit;
+  p.err = P<int>(err_word(x0));
+  TORCH_CHECK(x0.scalar_type() == at::kHalf && x0.is_contiguous(), "activations must be contiguous f16");
+  TORCH_CHECK(out.size(0) >= p.rows && out.size(1) == p.N, "out shape");
+  check(g53_moe_prefill(p, gate_up, stream()), "moe_prefill");
 }
 
 void moe_combine(const Tensor& yd, const Tensor& pair_of, int64_t top_k, const Tensor& out, bool accumulate) {
@@ -488,10 +571,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv", &gemv);
   m.def("gemm_w8", &gemm_w8);
   m.def("gemm_bf16", &gemm_bf16);
+  m.def("gemm_w8a16", &gemm_w8a16);
   m.def("gemm_error", &gemm_error);
   m.def("moe_route", &moe_route);
   m.def("exl3_moe", &exl3_moe);
   m.def("moe_combine", &moe_combine);
+  m.def("moe_route_large", &moe_route_large);
+  m.def("moe_prefill", &moe_prefill);
+  m.def("exl3_rot_in", &exl3_rot_in);
   m.def("exl3_unpack", &exl3_unpack);
   m.def("hc_post_pre", &hc_post_pre);
   m.def("embed", &embed);

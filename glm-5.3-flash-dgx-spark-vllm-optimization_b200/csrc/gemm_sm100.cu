@@ -17,6 +17,7 @@
 // Reference counterparts: code/fork/kernels/fp8_w8a8.cu:134-219 (CUTLASS SM120 W8A8 GEMM) and
 // code/fork/kernels/fp8_large_m.cu (dequant + GEMM for large M).
 #include <cuda.h>
+#include <algorithm>
 #include "common.cuh"
 #include "launchers.h"
 
@@ -273,9 +274,40 @@ __global__ void __launch_bounds__(256) quant_rows_e4m3_kernel(const __nv_bfloat1
   if (threadIdx.x == 0) scale[r] = s;
 }
 
+// exact e4m3 -> bf16 widening of a weight matrix (16 bytes in, 32 bytes out per thread-iteration)
+__global__ void e4m3_to_bf16_kernel(const uint8_t* w, int64_t n16, __nv_bfloat16* out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 v = reinterpret_cast<const uint4*>(w)[i];
+    const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t h01 = e4m3x2_to_f16x2((uint16_t)(ws[k] & 0xffffu));
+      const uint32_t h23 = e4m3x2_to_f16x2((uint16_t)(ws[k] >> 16));
+      const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+      const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+      __nv_bfloat162 b01 = __floats2bfloat162_rn(f01.x, f01.y), b23 = __floats2bfloat162_rn(f23.x, f23.y);
+      o[2 * k] = *reinterpret_cast<uint32_t*>(&b01);
+      o[2 * k + 1] = *reinterpret_cast<uint32_t*>(&b23);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out) + 2 * i;
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
 }  // namespace g53
 
 using namespace g53;
+
+cudaError_t g53_e4m3_to_bf16(const uint8_t* w, int64_t n, __nv_bfloat16* out, cudaStream_t st) {
+  if (n % 16 || (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return cudaErrorInvalidValue;
+  const int64_t n16 = n / 16;
+  const int blocks = (int)std::min<int64_t>((n16 + 255) / 256, 148 * 16);
+  e4m3_to_bf16_kernel<<<blocks, 256, 0, st>>>(w, n16, out);
+  return cudaGetLastError();
+}
 
 namespace {
 

@@ -194,8 +194,14 @@ cudaError_t g53_kda_gated_norm(const KdaArgs& a, cudaStream_t st) {
 // M and P use a reference row r (start of t's 16-row sub-chunk): e^{G_t - G_s} = e^{G_t - G_r} e^{G_r - G_s}, so
 // both factors are bounded (|g| <= |lower| per step keeps e^{G_r - G_s} <= e^{15 |lower|}) and each inner product
 // is a plain dot product of pre-scaled rows.  v' comes from forward substitution over the chunk.
-// CTA = (head, 32 value rows, sequence); thread (vr, kc) keeps S[vr][kc*DH/8 .. +DH/8) in registers.
+// CTA = (head, 32 value rows, sequence); thread (vr, kc) keeps S[vr][kc*DH/8 .. +DH/8) in registers.  The CTAs of
+// one head form a thread-block cluster: M and P do not depend on the value rows, so CTA rank j computes the rows
+// of sub-chunk j (j, j+4, ... for fewer CTAs) and every CTA gathers the others' rows over distributed shared
+// memory.
 // ---------------------------------------------------------------------------------------------------------------
+#include <cooperative_groups.h>
+namespace cg = cooperative_groups;
+
 namespace g53 {
 
 constexpr int kCh = 64;      // chunk rows
@@ -280,8 +286,11 @@ __global__ void __launch_bounds__(256, 1) kda_chunk_kernel(KdaArgs a) {
       }
     }
     __syncthreads();
-    // 3. M (strictly lower) and P (lower incl. diagonal), one 16-row sub-chunk of t at a time
-    for (int j = 0; j < kCh / kSub; ++j) {
+    // 3. M (strictly lower) and P (lower incl. diagonal) for this CTA's 16-row sub-chunks of t; every thread a
+    //    strip of 4 s columns of one row t
+    cg::cluster_group cluster = cg::this_cluster();
+    const int crank = (int)cluster.block_rank(), csize = (int)cluster.num_blocks();
+    for (int j = crank; j < kCh / kSub; j += csize) {
       const int r = j * kSub;
       const int ns = r + kSub;                          // s ranges over [0, ns)
       for (int e = tid; e < kSub * DH; e += blockDim.x) {
@@ -295,23 +304,46 @@ __global__ void __launch_bounds__(256, 1) kda_chunk_kernel(KdaArgs a) {
         sX[s * P1 + c] = sK[s * P1 + c] * __expf(sG[r * P1 + c] - sG[s * P1 + c]);
       }
       __syncthreads();
-      for (int e = tid; e < kSub * ns; e += blockDim.x) {
-        const int t = e / ns, s = e % ns;
+      const int strips = ns / 4;
+      for (int e = tid; e < kSub * strips; e += blockDim.x) {
+        const int t = e / strips, s0 = (e % strips) * 4;
         const int tt = r + t;
-        float m = 0.f, pp = 0.f;
-        if (s <= tt) {
-#pragma unroll 8
+        float m[4] = {0.f, 0.f, 0.f, 0.f}, pp[4] = {0.f, 0.f, 0.f, 0.f};
+        if (s0 <= tt) {
+#pragma unroll 4
           for (int c = 0; c < DH; ++c) {
-            const float bs = sX[s * P1 + c];
-            m += sA[t * P1 + c] * bs;
-            pp += sQt[t * P1 + c] * bs;
+            const float av = sA[t * P1 + c], qv = sQt[t * P1 + c];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float bs = sX[(s0 + i) * P1 + c];
+              m[i] += av * bs;
+              pp[i] += qv * bs;
+            }
           }
         }
-        sM[tt * (kCh + 1) + s] = s < tt ? m : 0.f;
-        sP[tt * (kCh + 1) + s] = pp;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int s = s0 + i;
+          sM[tt * (kCh + 1) + s] = s < tt ? m[i] : 0.f;
+          sP[tt * (kCh + 1) + s] = s <= tt ? pp[i] : 0.f;
+        }
       }
       __syncthreads();
     }
+    // gather the other CTAs' sub-chunk rows of M and P
+    cluster.sync();
+    for (int j = 0; j < kCh / kSub; ++j) {
+      const int owner = j % csize;
+      if (owner == crank) continue;
+      const float* rM = cluster.map_shared_rank(sM, owner);
+      const float* rP = cluster.map_shared_rank(sP, owner);
+      for (int e = tid; e < kSub * (kCh + 1); e += blockDim.x) {
+        const int idx = j * kSub * (kCh + 1) + e;
+        sM[idx] = rM[idx];
+        sP[idx] = rP[idx];
+      }
+    }
+    cluster.sync();
     // 4. scaled rows for the chunk-start state: K e^{G}, Q e^{G}; and k_s e^{G_C - G_s} for the state update
     const int last = n - 1;
     for (int e = tid; e < kCh * DH; e += blockDim.x) {
@@ -378,17 +410,30 @@ cudaError_t g53_kda_chunk(const KdaArgs& a, cudaStream_t st) {
   const size_t smem = sizeof(float) * ((size_t)4 * kCh * P1 + 2 * kSub * P1 + 2 * kCh * (kCh + 1) + kCh * 33 +
                                        kCh + kCh * 33);
   dim3 grid(a.H, DH / 32, a.B);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = DH / 32;               // the value blocks of one head
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   cudaError_t e;
   if (DH == 128) {
     e = cudaFuncSetAttribute(kda_chunk_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    kda_chunk_kernel<128><<<grid, 256, smem, st>>>(a);
+    e = cudaLaunchKernelEx(&cfg, kda_chunk_kernel<128>, a);
   } else if (DH == 64) {
     e = cudaFuncSetAttribute(kda_chunk_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    kda_chunk_kernel<64><<<grid, 256, smem, st>>>(a);
+    e = cudaLaunchKernelEx(&cfg, kda_chunk_kernel<64>, a);
   } else {
     return cudaErrorInvalidValue;
   }
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

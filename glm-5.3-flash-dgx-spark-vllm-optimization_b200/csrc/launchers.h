@@ -33,6 +33,7 @@ struct GemmArgs {
   int* err;                            // device error word (bounded waits that ran out)
 };
 cudaError_t g53_gemm_sm100(const GemmArgs& p, cudaStream_t st);
+cudaError_t g53_e4m3_to_bf16(const uint8_t* w, int64_t n, __nv_bfloat16* out, cudaStream_t st);
 cudaError_t g53_quant_rows_e4m3(const __nv_bfloat16* x, int64_t ldx, int R, int K, uint8_t* q, float* scale,
                                 cudaStream_t st);
 
@@ -81,6 +82,25 @@ cudaError_t g53_exl3_down(const Exl3Args& a, cudaStream_t st);
 // out[r, :] (+)= sum_k yd[pair_of[r, k], :]  (slot order), fp32
 cudaError_t g53_moe_combine(const float* yd, const int* pair_of, int R, int top_k, int D, float* out,
                             int accumulate, cudaStream_t st);
+// prefill: tcgen05 grouped expert GEMM with in-shared-memory trellis decode (moe_prefill_sm100.cu)
+struct MoePrefillArgs {
+  const int16_t* tr0; const int16_t* tr1;         // gate/up trellis (gate_up) or down trellis (tr1 unused)
+  const __half* svh0; const __half* svh1;         // output scales of tr0 / tr1
+  const __half* suh_next;                         // gate_up: suh of the down projection
+  const float* pair_w;                            // down: routing weight per sorted pair
+  const int* group_count; const int* group_expert; const int* group_offset;
+  const __half* x0; const __half* x1;             // rotated inputs [rows, K] (gate, up) or xd (down)
+  int64_t rows;                                   // rows of x0 / x1 (sorted pairs)
+  int K, N, max_groups;
+  void* out;                                      // gate_up: f16 [rows, N] down input; down: f32 [rows, N]
+  float limit;
+  int* err;
+};
+cudaError_t g53_moe_prefill(const MoePrefillArgs& p, bool gate_up, cudaStream_t st);
+// scalable routing for prefill: per-row top-k, expert histogram, scan, scatter (positions within an expert in
+// arrival order: outputs per pair do not depend on it)
+cudaError_t g53_moe_route_large(const RouteArgs& a, int* counts, int* fill, cudaStream_t st);
+
 // one-tile decode for tests: W_q [K, N] fp16 from trellis [K/16, N/16, 64]
 cudaError_t g53_exl3_unpack(const int16_t* tr, int K, int N, __half* out, cudaStream_t st);
 

@@ -417,3 +417,120 @@ cudaError_t g53_exl3_unpack(const int16_t* tr, int K, int N, __half* out, cudaSt
   G53_CHECK_LAUNCH();
   return cudaSuccess;
 }
+
+// ---------------------------------------------------------------------------------------------------------------
+// routing for large row counts (prefill chunks): many CTAs
+// ---------------------------------------------------------------------------------------------------------------
+namespace g53 {
+
+__global__ void __launch_bounds__(256) moe_topk_kernel(RouteArgs a, int* counts) {
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= a.R) return;
+  constexpr int kPerLane = kMaxE / 32;
+  const float* lg = a.logits + (int64_t)r * a.E;
+  float cv[kPerLane];
+#pragma unroll
+  for (int i = 0; i < kPerLane; ++i) {
+    const int e = lane + 32 * i;
+    cv[i] = e < a.E ? sigmoidf_(lg[e]) + a.bias[e] : -INFINITY;
+  }
+  float sel_sum = 0.f, wt_l = 0.f;
+  int pick_l = 0;
+  for (int k = 0; k < a.top_k; ++k) {
+    float best = -INFINITY;
+    int bid = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i)
+      if (cv[i] > best) { best = cv[i]; bid = lane + 32 * i; }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bid, o);
+      if (ob > best || (ob == best && oi < bid)) { best = ob; bid = oi; }
+    }
+    if ((bid & 31) == lane) {
+#pragma unroll
+      for (int i = 0; i < kPerLane; ++i)
+        if (lane + 32 * i == bid) cv[i] = -INFINITY;
+    }
+    const float w = sigmoidf_(lg[bid]);
+    sel_sum += w;
+    if (lane == k) { pick_l = bid; wt_l = w; }
+  }
+  const float inv = a.norm ? 1.f / (sel_sum + 1e-20f) : 1.f;
+  if (lane < a.top_k) {
+    a.topk_ids[r * a.top_k + lane] = pick_l;
+    a.topk_w[r * a.top_k + lane] = wt_l * inv * a.scale;
+    atomicAdd(&counts[pick_l], 1);
+  }
+}
+
+__global__ void __launch_bounds__(1024) moe_scan_kernel(RouteArgs a, int* counts, int* fill) {
+  __shared__ int wsum[32];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  // E <= 1024: one element per thread, block-wide exclusive scan of counts and of the used flags
+  const int c = tid < a.E ? counts[tid] : 0;
+  const int used = c > 0;
+  int xs = c, xu = used;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int ys = __shfl_up_sync(0xffffffffu, xs, o), yu = __shfl_up_sync(0xffffffffu, xu, o);
+    if (lane >= o) { xs += ys; xu += yu; }
+  }
+  __shared__ int wu[32];
+  if (lane == 31) { wsum[wid] = xs; wu[wid] = xu; }
+  __syncthreads();
+  if (wid == 0) {
+    int ts = wsum[lane], tu = wu[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int ys = __shfl_up_sync(0xffffffffu, ts, o), yu = __shfl_up_sync(0xffffffffu, tu, o);
+      if (lane >= o) { ts += ys; tu += yu; }
+    }
+    wsum[lane] = ts;
+    wu[lane] = tu;
+  }
+  __syncthreads();
+  const int start = (wid > 0 ? wsum[wid - 1] : 0) + xs - c;
+  const int uidx = (wid > 0 ? wu[wid - 1] : 0) + xu - used;
+  if (tid < a.E) {
+    fill[tid] = start;
+    if (used && uidx < a.max_groups) {
+      a.group_expert[uidx] = tid;
+      a.group_offset[uidx] = start;
+    }
+  }
+  const int total_used = wu[31];
+  const int total = wsum[31];
+  if (tid == 0) a.group_count[0] = total_used;
+  for (int v = total_used + tid; v <= a.max_groups; v += blockDim.x) a.group_offset[v] = total;
+}
+
+__global__ void moe_scatter_kernel(RouteArgs a, int* fill) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.R * a.top_k) return;
+  const int e = a.topk_ids[i];
+  const int pos = atomicAdd(&fill[e], 1);
+  a.pair_of[i] = pos;
+  a.pair_token[pos] = i / a.top_k;
+  a.pair_expert[pos] = e;
+  a.pair_w[pos] = a.topk_w[i];
+}
+
+}  // namespace g53
+
+cudaError_t g53_moe_route_large(const RouteArgs& a, int* counts, int* fill, cudaStream_t st) {
+  using namespace g53;
+  if (a.E > 1024 || a.E > kMaxE || a.top_k > 32) return cudaErrorInvalidValue;
+  cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int) * a.E, st);
+  if (e != cudaSuccess) return e;
+  moe_topk_kernel<<<(a.R + 7) / 8, 256, 0, st>>>(a, counts);
+  G53_CHECK_LAUNCH();
+  moe_scan_kernel<<<1, 1024, 0, st>>>(a, counts, fill);
+  G53_CHECK_LAUNCH();
+  const int P = a.R * a.top_k;
+  moe_scatter_kernel<<<(P + 255) / 256, 256, 0, st>>>(a, fill);
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}

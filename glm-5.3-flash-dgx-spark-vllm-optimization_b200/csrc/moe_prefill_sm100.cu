@@ -1,0 +1,410 @@
+// Routed EXL3 MoE for prefill chunks on the 5th-generation tensor cores.
+//
+// One CTA = (128 output channels of one expert, that expert's token rows).  Swap-AB: the 128 output channels are
+// the MMA's M dimension (TMEM lanes) and the expert's tokens (up to 256 per pass) are N (TMEM columns), so the
+// weights of an expert are decoded once per pass however many tokens it received.
+//
+//   warps 0-7   trellis decoders: each 16x16 tile is decoded in registers (ExLlamaV3's mcg codebook, the same
+//               arithmetic as moe.cu) and stored to shared memory in the K-major 128-byte-swizzled layout that a
+//               UMMA descriptor reads (the lane's fragment registers are (k, k+1) pairs, one 32-bit store each);
+//               after the main loop they are the epilogue warps
+//   warp 8      TMA producer: rotated activations of the expert's token rows (rows of one expert are contiguous in
+//               the sorted pair order) as 64x64 boxes, 128-byte swizzle, no multicast
+//   warp 9      TMEM allocation; one thread issues tcgen05.mma kind::f16 (f16 x f16 -> f32) per 16-wide k step
+// Stages are handed over with mbarriers (decoders arrive after fence.proxy.async, TMA by complete_tx, the MMA
+// frees a stage with tcgen05.commit).  Epilogue per 32 token columns: tcgen05.ld -> shared-memory transpose ->
+// per token row: Hadamard-128, * svh, then
+//   gate/up  SwiGLU with clamp, * suh of the down projection, Hadamard-128 -> f16 rotated down input
+//   down     * routing weight -> fp32 per-pair output
+// All waits are bounded (error word + early exit); TMEM is freed on every path.
+// Reference counterpart: code/fork/kernels/moe_e4m3.cu:1500 (persistent prefill MoE) and
+// code/fork/docs/ref/mia_exl3-fat-kernel (ExLlamaV3 fat grouped kernels).
+#include <cuda.h>
+#include "common.cuh"
+#include "launchers.h"
+
+namespace g53 {
+namespace mp {
+
+constexpr uint32_t kSpin = 1u << 26;
+constexpr int kDecWarps = 8;
+constexpr int kThreads = (kDecWarps + 2) * 32;
+constexpr int kNmax = 256;            // tokens per pass
+constexpr int kBK = 64;               // k per stage (one 128-byte swizzle row of f16)
+
+__device__ __forceinline__ uint32_t su32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n));
+}
+__device__ __forceinline__ void bar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool bar_try(uint64_t* b, uint32_t ph) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0,1,0,p;\n}\n"
+               : "=r"(ok) : "r"(su32(b)), "r"(ph) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t ph, volatile int* fail, int* err, int code) {
+  uint32_t n = 0;
+  while (!bar_try(b, ph)) {
+    if (*fail) return false;
+    if (++n > kSpin) { *fail = 1; atomicExch(err, code); return false; }
+    if (n > 64) __nanosleep(32);
+  }
+  return true;
+}
+__device__ __forceinline__ void named_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n)); }
+
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+  // D f32, A f16, B f16 (format 0), K-major both, N, M = 128
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile("{\n .reg .pred p;\n setp.ne.u32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+               ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint64_t* b) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tma_2d(const CUtensorMap* m, uint64_t* bar, void* dst, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+               ::"r"(su32(dst)), "l"(m), "r"(x), "r"(y), "r"(su32(bar)) : "memory");
+}
+
+// mcg trellis decode (same rules as moe.cu): 4 f16x2 fragment registers of lane l from words cur (l) / prev (l-1)
+__device__ __forceinline__ uint32_t mcg_x(uint32_t s) { return ((s * 0xCBAC1FEDu) & 0x8FFF8FFFu) ^ 0x3B603B60u; }
+__device__ __forceinline__ uint32_t mcg_pair(uint32_t s0, uint32_t s1) {
+  const uint32_t x0 = mcg_x(s0), x1 = mcg_x(s1);
+  const uint32_t lo = __byte_perm(x0, x1, 0x5410), hi = __byte_perm(x0, x1, 0x7632);
+  __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&lo), *reinterpret_cast<const __half2*>(&hi));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+__device__ __forceinline__ void frags(uint32_t cur, uint32_t prev, uint32_t (&b)[4]) {
+  b[0] = mcg_pair(__funnelshift_r(cur, prev, 28) & 0xffffu, __funnelshift_r(cur, prev, 24) & 0xffffu);
+  b[1] = mcg_pair(__funnelshift_r(cur, prev, 20) & 0xffffu, cur >> 16);
+  b[2] = mcg_pair((cur >> 12) & 0xffffu, (cur >> 8) & 0xffffu);
+  b[3] = mcg_pair((cur >> 4) & 0xffffu, cur & 0xffffu);
+}
+
+// byte offset of element (row, k) (k even) in a 128-row x 64-k f16 tile, K-major, 128-byte swizzle
+__device__ __forceinline__ uint32_t sw_off(int row, int k) {
+  return (uint32_t)(row * 128 + ((((k * 2) >> 4) ^ (row & 7)) << 4) + ((k * 2) & 15));
+}
+
+template <bool GU>
+__global__ void __launch_bounds__(kThreads, 1) moe_prefill_kernel(const __grid_constant__ CUtensorMap tb0,
+                                                                  const __grid_constant__ CUtensorMap tb1,
+                                                                  MoePrefillArgs p) {
+  constexpr int NM = GU ? 2 : 1;                       // weight matrices
+  constexpr int STAGES = GU ? 2 : 4;
+  constexpr int A_BYTES = 128 * 128;                   // 128 rows x 64 f16
+  constexpr int B_BYTES = kNmax * 128;                 // 256 token rows x 64 f16
+  constexpr int STAGE = NM * (A_BYTES + B_BYTES);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t a_full[STAGES], b_full[STAGES], empty[STAGES], acc_full, tmem_free;
+  __shared__ uint32_t tmem_base;
+  __shared__ volatile int fail;
+
+  const int u = blockIdx.y;
+  if (u >= p.group_count[0] || u >= p.max_groups) return;
+  const int e = p.group_expert[u];
+  const int p0 = p.group_offset[u];
+  const int np = p.group_offset[u + 1] - p0;
+  const int nb = blockIdx.x;                            // 128-channel output block
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int KT = p.K / 16, NT = p.N / 16;
+  const int nkb = p.K / kBK;
+  const int passes = (np + kNmax - 1) / kNmax;
+
+  if (threadIdx.x == 0) {
+    fail = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      bar_init(&a_full[s], kDecWarps);
+      bar_init(&b_full[s], 1);
+      bar_init(&empty[s], 1);
+    }
+    bar_init(&acc_full, 1);
+    bar_init(&tmem_free, kDecWarps);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kDecWarps + 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base)),
+                 "r"((uint32_t)(NM * kNmax)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+
+  if (warp < kDecWarps) {
+    // ------------------------------------------------------------------ decoders, then epilogue
+    const uint32_t* trw[2] = {reinterpret_cast<const uint32_t*>(p.tr0), reinterpret_cast<const uint32_t*>(p.tr1)};
+    constexpr int TILES = NM * 4 * 8;                   // (matrix, k-tile, n-tile) of one stage
+    constexpr int PER = TILES / kDecWarps;
+    const int src = (lane + 31) & 31;
+    const int g = lane >> 2, q = lane & 3;
+    int it = 0;                                         // global stage counter (continues across passes)
+    for (int pass = 0; pass < passes; ++pass) {
+      const int rows = min(kNmax, np - pass * kNmax);
+      uint32_t wcur[PER];
+      auto load = [&](int kb, uint32_t (&w)[PER]) {
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+          const int idx = warp + i * kDecWarps;
+          const int m = idx / 32, kt = (idx / 8) & 3, nt = idx & 7;
+          const int64_t tile = ((int64_t)e * KT + kb * 4 + kt) * NT + nb * 8 + nt;
+          w[i] = ldg_nc_u32(trw[m] + tile * 32 + lane);
+        }
+      };
+      load(0, wcur);
+      for (int kb = 0; kb < nkb; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        uint32_t wnext[PER];
+        if (kb + 1 < nkb) load(kb + 1, wnext);
+        if (it >= STAGES) {
+          int okw = 0;
+          if (lane == 0) okw = bar_wait(&empty[s], ph ^ 1, &fail, p.err, 11) ? 1 : 0;
+          if (!__shfl_sync(0xffffffffu, okw, 0)) break;
+        }
+        uint8_t* abase = sm + s * STAGE;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+          const int idx = warp + i * kDecWarps;
+          const int m = idx / 32, kt = (idx / 8) & 3, nt = idx & 7;
+          uint32_t b[4];
+          frags(wcur[i], __shfl_sync(0xffffffffu, wcur[i], src), b);
+          uint8_t* at = abase + m * A_BYTES;
+          const int n0 = nt * 16 + g, k0 = kt * 16 + 2 * q;
+          *reinterpret_cast<uint32_t*>(at + sw_off(n0, k0)) = b[0];
+          *reinterpret_cast<uint32_t*>(at + sw_off(n0, k0 + 8)) = b[1];
+          *reinterpret_cast<uint32_t*>(at + sw_off(n0 + 8, k0)) = b[2];
+          *reinterpret_cast<uint32_t*>(at + sw_off(n0 + 8, k0 + 8)) = b[3];
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) bar_arrive(&a_full[s]);
+        if (kb + 1 < nkb) {
+#pragma unroll
+          for (int i = 0; i < PER; ++i) wcur[i] = wnext[i];
+        }
+      }
+      // ---- epilogue of this pass
+      int okw = 0;
+      if (lane == 0) okw = bar_wait(&acc_full, pass & 1, &fail, p.err, 12) ? 1 : 0;
+      const bool ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
+      __syncwarp();
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      float* zb = reinterpret_cast<float*>(sm);          // [2][32][129] transposition buffer (stages are idle)
+      const int quad = warp & 3, half = warp >> 2;
+      for (int c0 = 0; c0 < rows; c0 += 32) {
+        if (ok) {
+          float v[32];
+          if (GU) {
+            // warps 0-3: gate columns, warps 4-7: up columns
+            tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + half * kNmax + c0, v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) zb[(half * 32 + j) * 129 + quad * 32 + lane] = v[j];
+          } else {
+            // warps 0-3: columns c0.., warps 4-7: columns c0+32..
+            tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c0 + half * 32, v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) zb[(half * 32 + j) * 129 + quad * 32 + lane] = v[j];
+          }
+        }
+        named_sync(1, kDecWarps * 32);
+        const int ncols = GU ? min(32, rows - c0) : min(64, rows - c0);
+        for (int j = warp; j < ncols; j += kDecWarps) {
+          const int pr = p0 + pass * kNmax + c0 + j;        // sorted pair row
+          const int col = nb * 128 + lane * 4;
+          if (GU) {
+            float vg[4], vu[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) { vg[i] = zb[j * 129 + lane * 4 + i]; vu[i] = zb[(32 + j) * 129 + lane * 4 + i]; }
+            fwht128_warp(vg);
+            fwht128_warp(vu);
+            float act[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              float gv = vg[i] * __half2float(p.svh0[(int64_t)e * p.N + col + i]);
+              float uv = vu[i] * __half2float(p.svh1[(int64_t)e * p.N + col + i]);
+              gv = fminf(gv, p.limit);
+              uv = fminf(fmaxf(uv, -p.limit), p.limit);
+              act[i] = siluf_(gv) * uv * __half2float(p.suh_next[(int64_t)e * p.N + col + i]);
+            }
+            fwht128_warp(act);
+            __half2* o = reinterpret_cast<__half2*>(reinterpret_cast<__half*>(p.out) + (int64_t)pr * p.N + col);
+            o[0] = __floats2half2_rn(act[0], act[1]);
+            o[1] = __floats2half2_rn(act[2], act[3]);
+          } else {
+            float v[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = zb[j * 129 + lane * 4 + i];
+            fwht128_warp(v);
+            const float w = p.pair_w[pr];
+            float4 o;
+            o.x = v[0] * __half2float(p.svh0[(int64_t)e * p.N + col + 0]) * w;
+            o.y = v[1] * __half2float(p.svh0[(int64_t)e * p.N + col + 1]) * w;
+            o.z = v[2] * __half2float(p.svh0[(int64_t)e * p.N + col + 2]) * w;
+            o.w = v[3] * __half2float(p.svh0[(int64_t)e * p.N + col + 3]) * w;
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (int64_t)pr * p.N + col) = o;
+          }
+        }
+        named_sync(1, kDecWarps * 32);
+        if (!GU) c0 += 32;                               // down consumed 64 columns in this step
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) bar_arrive(&tmem_free);
+      if (!ok) break;
+    }
+  } else if (warp == kDecWarps) {
+    // ------------------------------------------------------------------ TMA producer (B: token rows)
+    if (lane == 0) {
+      int it = 0;
+      for (int pass = 0; pass < passes; ++pass) {
+        const int rows = min(kNmax, np - pass * kNmax);
+        const int boxes = (rows + 63) / 64;
+        // the epilogue of the previous pass uses the stage buffers as its transposition buffer
+        if (pass > 0 && !bar_wait(&tmem_free, (pass - 1) & 1, &fail, p.err, 17)) break;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (it >= STAGES && !bar_wait(&empty[s], ph ^ 1, &fail, p.err, 13)) break;
+          uint8_t* bbase = sm + s * STAGE + NM * A_BYTES;
+          bar_expect_tx(&b_full[s], (uint32_t)(NM * boxes * 64 * 128));
+          for (int bx = 0; bx < boxes; ++bx) {
+            const int row = p0 + pass * kNmax + bx * 64;
+            tma_2d(&tb0, &b_full[s], bbase + bx * 64 * 128, kb * kBK, row);
+            if (GU) tma_2d(&tb1, &b_full[s], bbase + B_BYTES + bx * 64 * 128, kb * kBK, row);
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int it = 0;
+      for (int pass = 0; pass < passes && !fail; ++pass) {
+        const int rows = min(kNmax, np - pass * kNmax);
+        const int n = (rows + 15) / 16 * 16;
+        const uint32_t idesc = idesc_f16(n);
+        if (pass > 0 && !bar_wait(&tmem_free, (pass - 1) & 1, &fail, p.err, 14)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        bool broke = false;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!bar_wait(&a_full[s], ph, &fail, p.err, 15) || !bar_wait(&b_full[s], ph, &fail, p.err, 16)) {
+            broke = true;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a0 = su32(sm + s * STAGE);
+          const uint32_t b0 = a0 + NM * A_BYTES;
+#pragma unroll
+          for (int m = 0; m < NM; ++m) {
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              mma_f16(tmem + m * kNmax, desc_sw128(a0 + m * A_BYTES + k * 32), desc_sw128(b0 + m * B_BYTES + k * 32),
+                      idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit(&empty[s]);
+        }
+        mma_commit(&acc_full);
+        if (broke) break;
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == kDecWarps + 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(NM * kNmax)));
+  }
+}
+
+}  // namespace mp
+}  // namespace g53
+
+using namespace g53;
+
+namespace {
+typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                             const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                             CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeFn enc() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(ptr);
+  }
+  return fn;
+}
+bool act_map(CUtensorMap* m, const void* base, int64_t rows, int64_t K) {
+  EncodeFn fn = enc();
+  if (!fn || (reinterpret_cast<uintptr_t>(base) & 15) || (K * 2) % 16) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(K * 2)};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
+cudaError_t g53_moe_prefill(const MoePrefillArgs& p, bool gate_up, cudaStream_t st) {
+  using namespace g53::mp;
+  if (p.K % kBK || p.N % 128) return cudaErrorInvalidValue;
+  CUtensorMap t0, t1;
+  if (!act_map(&t0, p.x0, p.rows, p.K)) return cudaErrorInvalidValue;
+  if (gate_up && !act_map(&t1, p.x1, p.rows, p.K)) return cudaErrorInvalidValue;
+  if (!gate_up) t1 = t0;
+  const int NM = gate_up ? 2 : 1, STAGES = gate_up ? 2 : 4;
+  const int smem = STAGES * NM * (128 * 128 + kNmax * 128) + 1024;
+  dim3 grid(p.N / 128, p.max_groups);
+  cudaError_t e;
+  if (gate_up) {
+    e = cudaFuncSetAttribute(moe_prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    moe_prefill_kernel<true><<<grid, kThreads, smem, st>>>(t0, t1, p);
+  } else {
+    e = cudaFuncSetAttribute(moe_prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    moe_prefill_kernel<false><<<grid, kThreads, smem, st>>>(t0, t1, p);
+  }
+  return cudaGetLastError();
+}

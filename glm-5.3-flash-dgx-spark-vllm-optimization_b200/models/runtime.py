@@ -28,6 +28,7 @@ from .weights import Linear8, Weights
 
 bf16, f32, i32 = torch.bfloat16, torch.float32, torch.int32
 KDA_CHUNK_MIN_ROWS = 32     # prefill windows longer than this use the chunked KDA kernel
+MOE_PREFILL_MIN_ROWS = 64   # forwards with more rows route the experts through the tcgen05 prefill kernels
 
 
 @dataclass
@@ -39,7 +40,8 @@ class RuntimeConfig:
     max_blocks: int = 128         # page-table width per sequence
     decode_rows: int = 16         # forwards of at most this many rows keep per-layer KDA window inputs (replay)
     mla_splits: int = 4           # key splits of the decode attention
-    moe_chunk: int = 256          # rows per routed-MoE launch group (routing kernel capacity)
+    moe_chunk: int = 256          # rows per routed-MoE launch group of the decode path (routing kernel capacity)
+    moe_prefill_rows: int = 8192  # rows per routed-MoE launch group of the prefill (tcgen05) path
     attn_chunk: int = 1024        # rows per attention launch group (scratch bound)
     logit_rows: int = 16
 
@@ -176,6 +178,25 @@ class Runtime:
         self.pair_w = torch.zeros(P, dtype=f32, device=dev)
         self.pair_of = torch.zeros(P, dtype=i32, device=dev)
         moe0 = next((lw.moe for lw in w.layers if lw.moe is not None), None)
+        self.prefill_moe = R > MOE_PREFILL_MIN_ROWS and moe0 is not None
+        if self.prefill_moe:
+            # prefill path: one routing group of up to moe_prefill_rows rows
+            PR = min(R, rc.moe_prefill_rows)
+            self.p_rows = PR
+            PP = PR * tk
+            self.p_logits = torch.zeros(PR, c.experts, dtype=f32, device=dev)
+            self.p_topk_ids = torch.zeros(PR, tk, dtype=i32, device=dev)
+            self.p_topk_w = torch.zeros(PR, tk, dtype=f32, device=dev)
+            self.p_groups = c.experts
+            self.p_group_expert = torch.zeros(c.experts, dtype=i32, device=dev)
+            self.p_group_offset = torch.zeros(c.experts + 1, dtype=i32, device=dev)
+            self.p_pair_token = torch.zeros(PP, dtype=i32, device=dev)
+            self.p_pair_expert = torch.zeros(PP, dtype=i32, device=dev)
+            self.p_pair_w = torch.zeros(PP, dtype=f32, device=dev)
+            self.p_pair_of = torch.zeros(PP, dtype=i32, device=dev)
+            self.p_counts = torch.zeros(c.experts, dtype=i32, device=dev)
+            self.p_fill = torch.zeros(c.experts, dtype=i32, device=dev)
+            P = max(P, PP)
         if moe0 is not None:
             self.xh_g = torch.zeros(P, D, dtype=torch.float16, device=dev)
             self.xh_u = torch.zeros(P, D, dtype=torch.float16, device=dev)
@@ -339,9 +360,37 @@ class Runtime:
         K.linear8(self.normed[:R], gu.w, gu.s, act, K.GEMV_SWIGLU, self.cfg.limit)
         K.linear8(act, m.down.w, m.down.s, self.branch[:R], K.GEMV_F32)
 
+    def _moe_prefill(self, lw, R):
+        """Routed experts of a prefill chunk: scalable routing, rotated inputs, tcgen05 gate/up and down with the
+        trellis decoded into shared memory once per (expert, 128-channel block), then the slot-ordered combine."""
+        c, m = self.cfg, lw.moe
+        Kc = K.C()
+        for r0 in range(0, R, self.p_rows):
+            r1 = min(R, r0 + self.p_rows)
+            n = r1 - r0
+            P = n * c.top_k
+            x = self.normed[r0:r1]
+            K.linear_bf16(x, m.router, self.p_logits[:n])
+            Kc.moe_route_large(self.p_logits[:n], m.bias, c.top_k, c.routed_scale, c.norm_topk, self.p_topk_ids[:n],
+                               self.p_topk_w[:n], self.group_count, self.p_group_expert, self.p_group_offset,
+                               self.p_pair_token[:P], self.p_pair_expert[:P], self.p_pair_w[:P],
+                               self.p_pair_of[:P], self.p_counts, self.p_fill)
+            Kc.exl3_rot_in(x, m.gate.suh, m.up.suh, self.p_pair_token[:P], self.p_pair_expert[:P], self.xh_g,
+                           self.xh_u)
+            Kc.moe_prefill(m.gate.trellis, m.up.trellis, m.gate.svh, m.up.svh, m.down.suh, None, self.group_count,
+                           self.p_group_expert, self.p_group_offset, self.xh_g[:P], self.xh_u[:P], self.xd[:P],
+                           c.limit, True)
+            Kc.moe_prefill(m.down.trellis, None, m.down.svh, None, None, self.p_pair_w[:P], self.group_count,
+                           self.p_group_expert, self.p_group_offset, self.xd[:P], None, self.yd[:P], c.limit, False)
+            Kc.moe_combine(self.yd, self.p_pair_of[:P], c.top_k, self.branch[r0:r1], False)
+
     def _moe(self, lw, R):
         c, m = self.cfg, lw.moe
         Kc = K.C()
+        if self.prefill_moe and R > MOE_PREFILL_MIN_ROWS:
+            self._moe_prefill(lw, R)
+            self._shared_expert(lw, R)
+            return
         MR = self.rlogits.shape[0]
         for r0 in range(0, R, MR):
             r1 = min(R, r0 + MR)
@@ -359,7 +408,11 @@ class Runtime:
                         self.group_offset[:groups + 1], self.pair_token[:P], self.pair_expert[:P], self.pair_w[:P],
                         self.xh_g, self.xh_u, self.xd, self.yd, c.limit)
             Kc.moe_combine(self.yd, self.pair_of[:P], c.top_k, self.branch[r0:r1], False)
-        # shared expert, accumulated into the branch
+        self._shared_expert(lw, R)
+
+    def _shared_expert(self, lw, R):
+        """The shared expert (fp8 SwiGLU MLP), accumulated into the branch."""
+        c, m = self.cfg, lw.moe
         s = m.shared
         gu = self.gu_il[lw.index]
         act = self.act[:R, :s.width]

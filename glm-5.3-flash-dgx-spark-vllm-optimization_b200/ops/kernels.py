@@ -10,7 +10,25 @@ import torch
 from . import _ext
 
 # the tcgen05 GEMM serves M >= GEMM_MIN_M rows (set GLM53_TCGEN05_GEMM=0 to route large M through the small-M kernel)
-GEMM_ENABLED = os.environ.get("GLM53_TCGEN05_GEMM", "0") == "1"
+GEMM_ENABLED = os.environ.get("GLM53_TCGEN05_GEMM", "1") == "1"
+# large-M fp8 projections: exact W8A16 (weights widened to bf16, bf16 activations: the numerics of the decode
+# kernel) by default; GLM53_PREFILL_W8A8=1 quantises activations per row to e4m3 instead (2x tensor throughput,
+# different numerics -- the trade the reference's production prefill made)
+PREFILL_W8A8 = os.environ.get("GLM53_PREFILL_W8A8", "0") == "1"
+_scratch: dict = {}
+
+
+def _w_scratch(numel: int, device) -> torch.Tensor:
+    t = _scratch.get(device)
+    if t is None or t.numel() < numel:
+        t = torch.empty(numel, dtype=torch.bfloat16, device=device)
+        _scratch[device] = t
+    return t
+
+
+def reserve_gemm_scratch(numel: int, device) -> None:
+    """Allocate the W8A16 widening scratch up front (before CUDA-graph capture or large allocations)."""
+    _w_scratch(numel, torch.device(device))
 
 GEMV_BF16, GEMV_F32, GEMV_F32_ACC, GEMV_SWIGLU = 0, 1, 2, 3
 GEMV_MAX_M = 16
@@ -31,7 +49,10 @@ def linear8(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor, y: torch.Tensor, 
         g(x, w, s, y, mode, limit)
         return y
     if GEMM_ENABLED and M >= GEMM_MIN_M and x.dim() == 2:
-        C().gemm_w8(x, w, s, y, mode, limit)
+        if PREFILL_W8A8:
+            C().gemm_w8(x, w, s, y, mode, limit)
+        else:
+            C().gemm_w8a16(x, w, s, y, mode, limit, _w_scratch(w.numel(), x.device))
         return y
     for m0 in range(0, M, GEMV_MAX_M):
         m1 = min(M, m0 + GEMV_MAX_M)

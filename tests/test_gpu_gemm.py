@@ -64,3 +64,19 @@ def test_gemm_swiglu(C):
     y = torch.zeros(M, W, device=DEV, dtype=torch.bfloat16)
     C.gemm_w8(x.to(DEV), il.w.to(DEV), il.s.to(DEV), y, 3, 10.0)
     torch.testing.assert_close(y.float().cpu(), ref, atol=5e-2, rtol=5e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 128, 256), (300, 1000, 2048)])
+def test_gemm_w8a16(C, M, N, K):
+    """Exact-weight path: fp8 widened to bf16, bf16 activations, per-row scale epilogue."""
+    from glm53.models.weights import quantize_fp8_rows
+    torch.manual_seed(K + 1)
+    w = quantize_fp8_rows(torch.randn(N, K) / math.sqrt(K))
+    x = torch.randn(M, K).to(torch.bfloat16)
+    ref = x.float() @ w.dequant().t()
+    y = torch.zeros(M, N, device=DEV)
+    scratch = torch.empty(N * K, dtype=torch.bfloat16, device=DEV)
+    C.gemm_w8a16(x.to(DEV), w.w.to(DEV), w.s.to(DEV), y, 1, 0.0, scratch)
+    torch.cuda.synchronize()
+    assert C.gemm_error(y) == 0
+    torch.testing.assert_close(y.cpu(), ref, atol=2e-3, rtol=2e-3)
