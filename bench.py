@@ -107,36 +107,28 @@ def main():
         print(json.dumps({"impl": "reference", "metric": METRIC, "unavailable": REFERENCE_UNAVAILABLE}))
         return
     import torch
-    import glm53
-    from glm53.models import weights as W
-    from glm53.models.runtime import Graphed, Runtime, RuntimeConfig
-    from glm53.models.session import Sequence
-    from glm53.ops.sampling import GreedySampler
+    from glm53.api.offline import LLM, LLMOptions
+    from glm53.engine.llm import SamplingParams, State
     from glm53.parallel import dist as D
 
     rank, local, world = D.init()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
     comm = D.NcclComm() if world > 1 else None
-    dev = torch.device("cuda", local)
-    cfg = glm53.full_config(args.layers) if args.model == "full" else glm53.tiny_config()
-    t0 = time.time()
-    w = W.prepare(W.RandomSource(cfg, seed=0, device=dev), cfg, rank=rank, world=world, device=dev)
-    torch.cuda.synchronize()
-    t_load = time.time() - t0
     K = args.k
     rows = K + 1
-    chunk = min(args.prefill_chunk, max(args.context, 16))
-    bs = 64
-    ctx_cap = args.context + rows * (args.steps + args.warmup + 4) + 64
-    if not args.no_prefill:
-        ctx_cap = max(ctx_cap, args.prefill_tokens + 64)
-    max_blocks = (ctx_cap + bs - 1) // bs
-    rc = RuntimeConfig(max_rows=max(chunk, 16), max_seqs=1, kv_slots=max_blocks * bs, block_size=bs,
-                       max_blocks=max_blocks, decode_rows=16, mla_splits=4, logit_rows=16)
-    rt = Runtime(w, rc, comm=comm)
-    seq = Sequence(rt)
-    sampler = GreedySampler(16, world, w.rank * w.head.n, comm, dev)
+    chunk = args.prefill_chunk
+    max_len = max(args.context, args.prefill_tokens if not args.no_prefill else 0) + rows * (args.steps +
+                                                                                              args.warmup + 8) + 64
+    t0 = time.time()
+    llm = LLM(LLMOptions(model=args.model, layers=args.layers if args.layers != 45 else None, max_seqs=1,
+                         max_model_len=max_len, prefill_chunk=chunk, speculative=True, k_fixed=K,
+                         force_accept=True, checkpoints=0, cuda_graphs=not args.no_graph), comm=comm, rank=rank,
+              world=world)
+    torch.cuda.synchronize()
+    t_load = time.time() - t0
+    eng = llm.engine
+    cfg = llm.cfg
     gen = torch.Generator().manual_seed(1234)
     stream = torch.cuda.current_stream()
 
@@ -145,76 +137,49 @@ def main():
             comm.barrier()
         torch.cuda.synchronize()
 
-    # ---------------- cold prefill (separate sequence state: reset afterwards) ----------------
+    def run_until(pred):
+        while not pred():
+            eng.step()
+
+    # ---------------- cold prefill through the engine: TTFT of a max_tokens=1 request ----------------
     prefill = None
     if not args.no_prefill:
+        warm = torch.randint(0, cfg.vocab, (min(chunk, args.prefill_tokens),), generator=gen).tolist()
+        rid = eng.add_request(warm, SamplingParams(max_tokens=1, ignore_eos=True))     # warm-up: kernels, allocator
+        run_until(lambda: rid in eng.done)
         ptoks = torch.randint(0, cfg.vocab, (args.prefill_tokens,), generator=gen).tolist()
-        seq.prefill(ptoks[:min(2048, len(ptoks))], chunk=min(chunk, 2048))      # warm-up (kernels, allocator)
-        seq.reset()
         barrier_sync()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.perf_counter()
         e0.record(stream)
-        seq.prefill(ptoks, chunk=chunk)
+        rid = eng.add_request(ptoks, SamplingParams(max_tokens=1, ignore_eos=True))
+        run_until(lambda: rid in eng.done)
         e1.record(stream)
         barrier_sync()
+        wall = time.perf_counter() - w0
         ms = e0.elapsed_time(e1)
         ms = comm.max_scalar(ms) if comm else ms
+        wall = comm.max_scalar(wall) if comm else wall
         prefill = {"tokens": args.prefill_tokens, "chunk": chunk, "ttft_s": ms / 1e3,
-                   "tok_s": args.prefill_tokens / (ms / 1e3), "vs_published": args.prefill_tokens / (ms / 1e3) /
-                   PUBLISHED_PREFILL_TOK_S}
-        seq.reset()
+                   "tok_s": args.prefill_tokens / (ms / 1e3), "e2e_tok_s": args.prefill_tokens / wall,
+                   "vs_published": args.prefill_tokens / (ms / 1e3) / PUBLISHED_PREFILL_TOK_S}
 
-    # ---------------- context for decode ----------------
+    # ---------------- decode: a request with a random context, K drafts per step, acceptance forced ----------------
     ctx = torch.randint(0, cfg.vocab, (args.context,), generator=gen).tolist()
-    logits = seq.prefill(ctx, chunk=chunk)
-    last = int(sampler(logits)[0].item())
-
-    # pinned staging of each step's inputs and outputs (the end-to-end path's H2D / D2H)
-    h_in = torch.zeros(rows, dtype=torch.int32, pin_memory=True)
-    h_out = torch.zeros(rows, dtype=torch.int32, pin_memory=True)
-
-    def stage_window(tokens):
-        seq.stage(tokens, list(range(rows)))
-        seq._window = rows
-
-    stage_window([last] + [0] * K)
-    fwd = (lambda: rt.forward(rows, keep_window=True))
-    if not args.no_graph:
-        g_fwd = Graphed(fwd)
-        rt.stage_commit([seq._seq_desc(rows)])
-        g_commit = Graphed(lambda: rt.commit(None, replay=False))
-    drafts = torch.randint(0, cfg.vocab, (args.steps + args.warmup + 2, K), generator=gen)
-
-    def step(i, tok):
-        h_in[0] = tok
-        h_in[1:] = drafts[i]
-        stage_window(h_in.tolist())
-        lg = g_fwd() if not args.no_graph else fwd()
-        tgt = sampler(lg)                                  # greedy target tokens of every row
-        h_out.copy_(tgt, non_blocking=True)                # D2H of the step result
-        if args.no_graph:
-            rt.commit([seq._seq_desc(rows)], replay=False)
-        else:
-            rt.stage_commit([seq._seq_desc(rows)])      # the commit graph reads the staged descriptor
-            g_commit()
-        seq.cur = 1 - seq.cur
-        seq.pos += rows
-        return tgt
-
-    for i in range(args.warmup):
-        step(i, last)
-        torch.cuda.synchronize()
-        last = int(h_out[-1])
+    rid = eng.add_request(ctx, SamplingParams(max_tokens=max_len - args.context - 8, ignore_eos=True))
+    run_until(lambda: eng.running and eng.running[0].state == State.RUNNING)
+    req = eng.running[0]
+    for _ in range(args.warmup):
+        eng.step()
     barrier_sync()
+    n_tok0 = len(req.output)
     clocks = ClockSampler(local)
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
     wall0 = time.perf_counter()
-    for i in range(args.steps):
-        step(args.warmup + i, last)
-        torch.cuda.synchronize()                            # the host reads the emitted tokens every step
-        last = int(h_out[-1])
+    e0.record(stream)
+    for _ in range(args.steps):
+        eng.step()                       # stage (pinned H2D) -> verify graph -> sample -> D2H tokens -> commit -> draft
     e1.record(stream)
     barrier_sync()
     wall = time.perf_counter() - wall0
@@ -222,15 +187,16 @@ def main():
     ms = e0.elapsed_time(e1)
     ms = comm.max_scalar(ms) if comm else ms
     wall = comm.max_scalar(wall) if comm else wall
+    emitted = len(req.output) - n_tok0
     ms_step = ms / args.steps
-    tok_s = rows / (ms_step / 1e3)
+    tok_s = emitted / (ms / 1e3)
+    h2d = int(getattr(llm.backend.rt.batch, "h2d_bytes", 0))
 
-    # kernel launches of one step (counted with the profiler on an untimed step)
     launches = None
     try:
         from torch.profiler import ProfilerActivity, profile
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            step(args.warmup + args.steps, last)
+            eng.step()
             torch.cuda.synchronize()
         names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
         ours = [n for n in names if "g53" in n]
@@ -242,25 +208,26 @@ def main():
         out = {
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": tok_s / PUBLISHED_DECODE_TOK_S, "dtype": "bf16 activations / fp8 e4m3 dense / EXL3 4bpw",
+            "vs_baseline": tok_s / PUBLISHED_DECODE_TOK_S,
+            "dtype": "bf16 activations; fp8 e4m3 dense weights; EXL3 4-bpw experts; fp8 latent KV",
             "data": "synthetic: random-init weights (seed 0), uniform random token ids",
-            "config": {"model": f"glm-5.3-flash {cfg.layers} layers, 288 experts top-8, EXL3 4bpw, vocab {cfg.vocab}"
-                       if args.model == "full" else "glm53-tiny", "global_batch": 1, "seq_len": args.context,
-                       "parallelism": f"tp{world}", "K": K, "tokens_per_step": rows,
-                       "acceptance": "forced (all K drafts accepted)", "cuda_graph": not args.no_graph,
-                       "l2": "inputs larger than L2: each step streams tens of GB of weights"},
+            "config": {"model": f"glm-5.3-flash {cfg.layers} layers (34 KDA + 11 MLA/DSA), 288 experts top-8 + shared,"
+                                f" EXL3 4bpw, vocab {cfg.vocab}" if args.model == "full" else "glm53-tiny",
+                       "global_batch": 1, "seq_len": args.context, "parallelism": f"tp{world}", "K": K,
+                       "tokens_per_step": rows, "acceptance": "forced (all K drafts accepted)",
+                       "drafter": "1-layer block drafter in every step", "cuda_graph": not args.no_graph,
+                       "l2": "inputs larger than L2: every step streams ~35 GB of weights (no flush needed)"},
             "prefill": prefill,
-            "e2e": {"value": rows * args.steps / wall, "unit": "tok/s",
-                    "h2d_bytes_per_step": int(h_in.numel() * 4), "d2h_bytes_per_step": int(h_out.numel() * 4),
-                    "note": "host loop: pinned H2D of the window tokens, graph replay, D2H of the verified tokens"},
+            "e2e": {"value": emitted / wall, "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": 4 * rows,
+                    "note": "public engine API (LLMEngine.step): pinned H2D of the window, D2H of verified tokens"},
             "gpu_launches": (launches.get("per_step_ours", 0) * args.steps) if isinstance(launches, dict) else None,
             "launch_detail": launches,
             "clocks": ck,
             "load_s": t_load,
         }
         print(json.dumps(out))
-    if not args.no_graph:
-        del g_fwd, g_commit
+    llm.backend._graphs.clear()
     if comm:
         import torch.distributed as dist
         dist.barrier()

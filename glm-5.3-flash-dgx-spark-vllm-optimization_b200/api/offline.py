@@ -1,0 +1,79 @@
+"""Offline entry point: ``LLM(...).generate(prompts, params)`` builds the model (a checkpoint directory in the EXL3
+layout, or random-init weights of a named architecture), the GPU backend and the engine, and runs requests to
+completion."""
+
+from __future__ import annotations
+
+import os
+import time
+from dataclasses import dataclass
+
+import torch
+
+from ..config import ModelConfig, config_by_name
+from ..engine.backend import GPUBackend
+from ..engine.llm import EngineConfig, LLMEngine, SamplingParams
+from ..engine.tokenizer import ByteTokenizer
+from ..models import weights as W
+from ..models.runtime import RuntimeConfig
+
+
+@dataclass
+class LLMOptions:
+    model: str = "tiny"                 # "tiny", "full", or a checkpoint directory
+    seed: int = 0
+    max_seqs: int = 4
+    max_model_len: int = 8192
+    page_size: int = 64
+    kv_pages: int | None = None         # default: enough for max_seqs * max_model_len
+    prefill_chunk: int = 2048
+    speculative: bool = True
+    k_set: tuple[int, ...] = (4, 5, 7)
+    k_fixed: int | None = None
+    force_accept: bool = False
+    checkpoints: int = 4
+    cuda_graphs: bool = True
+    layers: int | None = None           # truncate the full architecture (smoke use)
+
+
+class LLM:
+    def __init__(self, opts: LLMOptions | None = None, comm=None, rank: int = 0, world: int = 1, **kw):
+        opts = opts or LLMOptions(**kw)
+        self.opts = opts
+        dev = torch.device("cuda", torch.cuda.current_device())
+        if os.path.isdir(opts.model):
+            cfg = W.load_config(opts.model)
+            src = W.SafetensorsSource(opts.model)
+        else:
+            cfg = config_by_name(opts.model)
+            if opts.layers:
+                from ..config import full_config
+                cfg = full_config(opts.layers) if opts.model in ("full", "glm53", "glm-5.3-flash") else cfg
+            src = W.RandomSource(cfg, seed=opts.seed, device=dev)
+        self.cfg: ModelConfig = cfg
+        t0 = time.time()
+        self.weights = W.prepare(src, cfg, rank=rank, world=world, device=dev)
+        self.load_s = time.time() - t0
+        pages = opts.kv_pages or max(64, opts.max_seqs * ((opts.max_model_len + opts.page_size - 1)
+                                                           // opts.page_size + 2))
+        kmax = max(opts.k_set) if opts.k_fixed is None else opts.k_fixed
+        rc = RuntimeConfig(max_rows=max(opts.prefill_chunk, 16), max_seqs=opts.max_seqs,
+                           kv_slots=pages * opts.page_size, block_size=opts.page_size,
+                           max_blocks=(opts.max_model_len + opts.page_size - 1) // opts.page_size + 2,
+                           decode_rows=max(16, opts.max_seqs * (kmax + 1)),
+                           logit_rows=max(16, opts.max_seqs * (kmax + 1)))
+        self.backend = GPUBackend(self.weights, rc, comm=comm, drafter=opts.speculative,
+                                  cuda_graphs=opts.cuda_graphs, checkpoints=opts.checkpoints)
+        ec = EngineConfig(max_seqs=opts.max_seqs, page_size=opts.page_size, num_pages=pages,
+                          max_model_len=opts.max_model_len, prefill_chunk=opts.prefill_chunk,
+                          speculative=opts.speculative, k_set=opts.k_set, k_fixed=opts.k_fixed,
+                          force_accept=opts.force_accept, checkpoints=opts.checkpoints,
+                          cuda_graphs=opts.cuda_graphs)
+        self.engine = LLMEngine(self.backend, ec, eos=tuple(cfg.eos))
+        self.tokenizer = ByteTokenizer(cfg.vocab)
+
+    def generate(self, prompts, params: SamplingParams | None = None) -> list[dict]:
+        """prompts: strings (byte-tokenized) or token-id lists.  Returns per prompt the token ids and text."""
+        ids = [self.tokenizer.encode(p) if isinstance(p, str) else list(p) for p in prompts]
+        outs = self.engine.generate(ids, params or SamplingParams())
+        return [{"token_ids": o, "text": self.tokenizer.decode(o)} for o in outs]

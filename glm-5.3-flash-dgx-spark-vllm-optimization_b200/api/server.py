@@ -1,0 +1,252 @@
+"""OpenAI-compatible HTTP server.
+
+  GET  /health                 200 when the engine loop is alive
+  GET  /v1/models              the served model
+  POST /v1/completions         prompt (string or token ids), max_tokens, temperature, top_p, top_k, seed, stop,
+                               stream (server-sent events)
+  POST /v1/chat/completions    messages (chat template of the byte tokenizer), same sampling fields, stream
+  GET  /metrics                Prometheus text: requests running / waiting, prompt / generation tokens, speculative
+                               drafts / accepted tokens, prefix-cache hits / queries, finished requests
+
+One engine thread owns the GPU and steps the engine whenever requests are pending; HTTP handlers hand requests to
+it through a queue and receive tokens through per-request queues.  The reference serves the same API through vLLM
+(code/kit/launcher/start.sh:2666-2684; Responses-input robustness: code/vllm-patches/responses_utils.patch).
+
+  python -m glm53.api.server --model tiny --port 8000
+"""
+
+from __future__ import annotations
+
+import argparse
+import asyncio
+import json
+import queue
+import threading
+import time
+import uuid
+
+from ..engine.llm import SamplingParams
+
+try:  # the HTTP stack is optional for offline use
+    from fastapi import FastAPI, HTTPException, Request
+    from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+except ImportError:  # pragma: no cover
+    FastAPI = None
+
+
+class EngineLoop:
+    """Runs ``engine.step()`` on its own thread; thread-safe submission and per-request token streams."""
+
+    def __init__(self, llm):
+        self.llm = llm
+        self.engine = llm.engine
+        self.inbox: queue.Queue = queue.Queue()
+        self.streams: dict[str, tuple[asyncio.AbstractEventLoop, asyncio.Queue]] = {}
+        self.alive = True
+        self.error: str | None = None
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+
+    def submit(self, prompt_ids, params: SamplingParams, loop, q) -> str:
+        rid = f"cmpl-{uuid.uuid4().hex[:16]}"
+        self.streams[rid] = (loop, q)
+        self.inbox.put((rid, prompt_ids, params))
+        return rid
+
+    def _run(self):
+        while self.alive:
+            try:
+                while True:
+                    rid, ids, params = self.inbox.get(block=not self.engine.has_work(), timeout=0.05)
+                    try:
+                        self.engine.add_request(ids, params, rid=rid)
+                    except ValueError as e:
+                        self._push(rid, {"error": str(e), "finished": True})
+            except queue.Empty:
+                pass
+            if not self.engine.has_work():
+                continue
+            try:
+                outs = self.engine.step()
+            except Exception as e:  # pragma: no cover - surfaced to clients and /health
+                self.error = repr(e)
+                self.alive = False
+                for rid in list(self.streams):
+                    self._push(rid, {"error": self.error, "finished": True})
+                raise
+            for o in outs:
+                self._push(o.rid, {"tokens": o.new_tokens, "finished": o.finished, "reason": o.finish_reason})
+
+    def _push(self, rid, item):
+        s = self.streams.get(rid)
+        if s is None:
+            return
+        loop, q = s
+        loop.call_soon_threadsafe(q.put_nowait, item)
+        if item.get("finished"):
+            self.streams.pop(rid, None)
+
+
+def _params(body: dict, tok) -> SamplingParams:
+    stop_ids = tuple(body.get("stop_token_ids") or ())
+    return SamplingParams(max_tokens=int(body.get("max_tokens") or 64), temperature=float(body.get("temperature", 0.0)),
+                          top_p=float(body.get("top_p", 1.0)), top_k=int(body.get("top_k", 0) or 0),
+                          seed=body.get("seed"), stop_token_ids=stop_ids,
+                          ignore_eos=bool(body.get("ignore_eos", False)))
+
+
+def _stop_strings(body) -> list[str]:
+    s = body.get("stop")
+    if s is None:
+        return []
+    return [s] if isinstance(s, str) else list(s)
+
+
+def build_app(llm, model_name: str = "glm-5.3-flash"):
+    if FastAPI is None:
+        raise RuntimeError("fastapi is not installed")
+    app = FastAPI()
+    loop_holder = {"engine": EngineLoop(llm)}
+    tok = llm.tokenizer
+
+    @app.get("/health")
+    async def health():
+        el = loop_holder["engine"]
+        if not el.alive:
+            raise HTTPException(status_code=503, detail=el.error or "engine stopped")
+        return {"status": "ok"}
+
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "glm53",
+                                            "max_model_len": llm.engine.cfg.max_model_len}]}
+
+    @app.get("/metrics")
+    async def metrics():
+        e = llm.engine
+        m = e.metrics
+        pc = e.kv.alloc.stats
+        lines = [
+            "# TYPE glm53_num_requests_running gauge", f"glm53_num_requests_running {len(e.running)}",
+            "# TYPE glm53_num_requests_waiting gauge", f"glm53_num_requests_waiting {len(e.waiting)}",
+            "# TYPE glm53_prompt_tokens_total counter", f"glm53_prompt_tokens_total {m['prompt_tokens']}",
+            "# TYPE glm53_generation_tokens_total counter", f"glm53_generation_tokens_total {m['generation_tokens']}",
+            "# TYPE glm53_spec_decode_num_drafts_total counter", f"glm53_spec_decode_num_drafts_total {m['spec_drafts']}",
+            "# TYPE glm53_spec_decode_num_accepted_tokens_total counter",
+            f"glm53_spec_decode_num_accepted_tokens_total {m['spec_accepted']}",
+            "# TYPE glm53_prefix_cache_hits_total counter", f"glm53_prefix_cache_hits_total {pc['hits']}",
+            "# TYPE glm53_prefix_cache_queries_total counter", f"glm53_prefix_cache_queries_total {pc['queries']}",
+            "# TYPE glm53_prefix_cached_tokens_total counter",
+            f"glm53_prefix_cached_tokens_total {m['prefix_cached_tokens']}",
+            "# TYPE glm53_request_success_total counter", f"glm53_request_success_total {m['requests_finished']}",
+        ]
+        return PlainTextResponse("\n".join(lines) + "\n")
+
+    async def _run(prompt_ids, params, stops, chat: bool, stream: bool, body: dict):
+        loop = asyncio.get_running_loop()
+        q: asyncio.Queue = asyncio.Queue()
+        rid = loop_holder["engine"].submit(prompt_ids, params, loop, q)
+        created = int(time.time())
+        obj = "chat.completion" if chat else "text_completion"
+
+        async def events():
+            text_so_far = ""
+            toks = []
+            while True:
+                item = await q.get()
+                if "error" in item:
+                    yield {"error": item["error"]}
+                    return
+                toks += item["tokens"]
+                text = tok.decode(toks)
+                delta = text[len(text_so_far):]
+                reason = item.get("reason")
+                for s in stops:
+                    k = text.find(s)
+                    if k >= 0:
+                        delta = text[len(text_so_far):k]
+                        text = text[:k]
+                        reason = "stop"
+                        item["finished"] = True
+                        break
+                text_so_far = text
+                yield {"delta": delta, "tokens": item["tokens"], "finished": item["finished"], "reason": reason,
+                       "all": toks, "text": text}
+                if item["finished"]:
+                    return
+
+        def choice(delta=None, text=None, reason=None, toks=None):
+            if chat:
+                if delta is not None:
+                    return {"index": 0, "delta": {"role": "assistant", "content": delta}, "finish_reason": reason}
+                return {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
+            return {"index": 0, "text": delta if delta is not None else text, "finish_reason": reason,
+                    "token_ids": toks}
+
+        if stream:
+            async def sse():
+                async for ev in events():
+                    if "error" in ev:
+                        yield f"data: {json.dumps({'error': ev['error']})}\n\n"
+                        break
+                    chunk = {"id": rid, "object": obj + (".chunk" if chat else ""), "created": created,
+                             "model": model_name,
+                             "choices": [choice(delta=ev["delta"], reason=ev["reason"] if ev["finished"] else None,
+                                                toks=ev["tokens"])]}
+                    yield f"data: {json.dumps(chunk)}\n\n"
+                yield "data: [DONE]\n\n"
+            return StreamingResponse(sse(), media_type="text/event-stream")
+        last = None
+        async for ev in events():
+            if "error" in ev:
+                raise HTTPException(status_code=400, detail=ev["error"])
+            last = ev
+        usage = {"prompt_tokens": len(prompt_ids), "completion_tokens": len(last["all"]) if last else 0}
+        usage["total_tokens"] = usage["prompt_tokens"] + usage["completion_tokens"]
+        return JSONResponse({"id": rid, "object": obj, "created": created, "model": model_name,
+                             "choices": [choice(text=last["text"] if last else "", reason=last["reason"] if last
+                                                else "stop", toks=last["all"] if last else [])],
+                             "usage": usage})
+
+    @app.post("/v1/completions")
+    async def completions(req: Request):
+        body = await req.json()
+        prompt = body.get("prompt", "")
+        if isinstance(prompt, list) and prompt and isinstance(prompt[0], int):
+            ids = list(prompt)
+        elif isinstance(prompt, list):
+            ids = tok.encode("".join(str(p) for p in prompt))
+        else:
+            ids = tok.encode(str(prompt))
+        return await _run(ids, _params(body, tok), _stop_strings(body), False, bool(body.get("stream")), body)
+
+    @app.post("/v1/chat/completions")
+    async def chat(req: Request):
+        body = await req.json()
+        msgs = [m for m in body.get("messages", []) if isinstance(m, dict)]     # skip unknown input items
+        ids = tok.encode(tok.apply_chat_template(msgs))
+        return await _run(ids, _params(body, tok), _stop_strings(body), True, bool(body.get("stream")), body)
+
+    return app
+
+
+def serve(argv=None):
+    ap = argparse.ArgumentParser(description="OpenAI-compatible GLM-5.3-Flash server on B200")
+    ap.add_argument("--model", default="tiny")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--max-seqs", type=int, default=4)
+    ap.add_argument("--max-model-len", type=int, default=8192)
+    ap.add_argument("--prefill-chunk", type=int, default=2048)
+    ap.add_argument("--no-spec", action="store_true")
+    ap.add_argument("--served-model-name", default="glm-5.3-flash")
+    args = ap.parse_args(argv)
+    import uvicorn
+    from .offline import LLM, LLMOptions
+    llm = LLM(LLMOptions(model=args.model, max_seqs=args.max_seqs, max_model_len=args.max_model_len,
+                         prefill_chunk=args.prefill_chunk, speculative=not args.no_spec))
+    uvicorn.run(build_app(llm, args.served_model_name), host=args.host, port=args.port, log_level="info")
+
+
+if __name__ == "__main__":
+    serve()

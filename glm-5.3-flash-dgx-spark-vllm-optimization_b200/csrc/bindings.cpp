@@ -334,6 +334,20 @@ void rmsnorm(const Tensor& x, const Tensor& w, double eps, const Tensor& y) {
         "rmsnorm");
 }
 
+void rmsnorm_f32(const Tensor& x, const Tensor& w, double eps, const Tensor& y) {
+  TORCH_CHECK(x.is_contiguous() && y.is_contiguous() && x.scalar_type() == at::kFloat);
+  check(g53_rmsnorm_f32(P<const float>(x), P<const __nv_bfloat16>(w), (int)x.size(0), (int)x.size(1), (float)eps,
+                        P<__nv_bfloat16>(y), stream()),
+        "rmsnorm_f32");
+}
+
+void block_attn(const Tensor& qkv, int64_t H, int64_t Dh, int64_t block, double scale, const Tensor& o) {
+  TORCH_CHECK(qkv.is_contiguous() && o.is_contiguous());
+  check(g53_block_attn(P<const __nv_bfloat16>(qkv), (int)qkv.size(0), (int)H, (int)Dh, (int)block, (float)scale,
+                       P<__nv_bfloat16>(o), stream()),
+        "block_attn");
+}
+
 // ------------------------------------------------------------------------------------------------- KDA
 // seq: int32 [5, B] device tensor: rows row0, nrows, state-in index, state-out index, conv slot
 KdaArgs kda_args(const Tensor& proj, const Tensor& seq, int64_t max_rows, int64_t H, int64_t Dh, int64_t taps) {
@@ -584,6 +598,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed", &embed);
   m.def("stream_mean_norm", &stream_mean_norm);
   m.def("rmsnorm", &rmsnorm);
+  m.def("rmsnorm_f32", &rmsnorm_f32);
+  m.def("block_attn", &block_attn);
   m.def("kda_conv", &kda_conv);
   m.def("kda_conv_commit", &kda_conv_commit);
   m.def("kda_recurrent", &kda_recurrent);

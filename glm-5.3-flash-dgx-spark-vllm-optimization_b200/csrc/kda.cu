@@ -194,7 +194,8 @@ cudaError_t g53_kda_gated_norm(const KdaArgs& a, cudaStream_t st) {
 // M and P use a reference row r (start of t's 16-row sub-chunk): e^{G_t - G_s} = e^{G_t - G_r} e^{G_r - G_s}, so
 // both factors are bounded (|g| <= |lower| per step keeps e^{G_r - G_s} <= e^{15 |lower|}) and each inner product
 // is a plain dot product of pre-scaled rows.  v' comes from forward substitution over the chunk.
-// CTA = (head, 32 value rows, sequence); thread (vr, kc) keeps S[vr][kc*DH/8 .. +DH/8) in registers.  The CTAs of
+// CTA = (head, 32 value rows, sequence); thread (vr, kc) keeps S[vr][kc + 8j] (j < DH/8) in registers (strided
+// channels: the 8 kc threads of a row read 8 consecutive shared-memory words, no bank conflicts).  The CTAs of
 // one head form a thread-block cluster: M and P do not depend on the value rows, so CTA rank j computes the rows
 // of sub-chunk j (j, j+4, ... for fewer CTAs) and every CTA gathers the others' rows over distributed shared
 // memory.
@@ -235,9 +236,9 @@ __global__ void __launch_bounds__(256, 1) kda_chunk_kernel(KdaArgs a) {
 
   float S[KPT];
   {
-    const float* sin = a.S_pool + a.s_in[b] * sstride + ((int64_t)h * DH + v0 + vr) * DH + kc * KPT;
+    const float* sin = a.S_pool + a.s_in[b] * sstride + ((int64_t)h * DH + v0 + vr) * DH + kc;
 #pragma unroll
-    for (int j = 0; j < KPT; ++j) S[j] = sin[j];
+    for (int j = 0; j < KPT; ++j) S[j] = sin[8 * j];
   }
 
   for (int c0 = 0; c0 < n_all; c0 += kCh) {
@@ -360,8 +361,8 @@ __global__ void __launch_bounds__(256, 1) kda_chunk_kernel(KdaArgs a) {
       float du = 0.f, dq = 0.f;
 #pragma unroll
       for (int j = 0; j < KPT; ++j) {
-        du += S[j] * sK[t * P1 + kc * KPT + j];
-        dq += S[j] * sQ[t * P1 + kc * KPT + j];
+        du += S[j] * sK[t * P1 + kc + 8 * j];
+        dq += S[j] * sQ[t * P1 + kc + 8 * j];
       }
       du = group_sum<8>(du);
       dq = group_sum<8>(dq);
@@ -389,16 +390,16 @@ __global__ void __launch_bounds__(256, 1) kda_chunk_kernel(KdaArgs a) {
     // 8. state: S <- S diag(e^{G_C}) + sum_s v'_s (k_s e^{G_C - G_s})^T
 #pragma unroll
     for (int j = 0; j < KPT; ++j) {
-      const int c = kc * KPT + j;
+      const int c = kc + 8 * j;
       float acc = S[j] * __expf(sG[last * P1 + c]);
       for (int s = 0; s < n; ++s) acc += sU[s * 33 + vr] * sX[s * P1 + c];
       S[j] = acc;
     }
     __syncthreads();
   }
-  float* sout = a.S_pool + a.s_out[b] * sstride + ((int64_t)h * DH + v0 + vr) * DH + kc * KPT;
+  float* sout = a.S_pool + a.s_out[b] * sstride + ((int64_t)h * DH + v0 + vr) * DH + kc;
 #pragma unroll
-  for (int j = 0; j < KPT; ++j) sout[j] = S[j];
+  for (int j = 0; j < KPT; ++j) sout[8 * j] = S[j];
 }
 
 }  // namespace g53

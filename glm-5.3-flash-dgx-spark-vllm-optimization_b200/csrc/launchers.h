@@ -126,6 +126,11 @@ cudaError_t g53_stream_mean_norm(const __nv_bfloat16* X, int R, int S, int D, co
 cudaError_t g53_rmsnorm(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16* w, int R, int D, float eps,
                         __nv_bfloat16* y, int64_t ldy, cudaStream_t st);
 
+cudaError_t g53_rmsnorm_f32(const float* x, const __nv_bfloat16* w, int R, int D, float eps, __nv_bfloat16* y,
+                            cudaStream_t st);
+cudaError_t g53_block_attn(const __nv_bfloat16* qkv, int R, int H, int Dh, int block, float scale, __nv_bfloat16* o,
+                           cudaStream_t st);
+
 // ---------------------------------------------------------------- KDA (kda.cu)
 struct KdaArgs {
   const __nv_bfloat16* proj; int64_t ldp;   // [R, ldp]: q|k|v (3*H*Dh) then f_a, g_a, b (H) at b_off

@@ -241,3 +241,62 @@ cudaError_t g53_rmsnorm(const __nv_bfloat16* x, int64_t ldx, const __nv_bfloat16
   G53_CHECK_LAUNCH();
   return cudaSuccess;
 }
+
+// ---------------------------------------------------------------------------------------------------------------
+// drafter helpers: RMSNorm of an fp32 residual row (bf16 out), and causal attention inside a block of <= 16 rows
+// ---------------------------------------------------------------------------------------------------------------
+namespace g53 {
+
+__global__ void __launch_bounds__(256) rmsnorm_f32_kernel(const float* x, const __nv_bfloat16* w, int D, float eps,
+                                                          __nv_bfloat16* y) {
+  const int r = blockIdx.x;
+  __shared__ float red[32];
+  float ss = 0.f;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) { const float t = x[(int64_t)r * D + d]; ss += t * t; }
+  ss = block_sum(ss, red);
+  const float rinv = rsqrtf(ss / (float)D + eps);
+  for (int d = threadIdx.x; d < D; d += blockDim.x)
+    y[(int64_t)r * D + d] = f2bf(x[(int64_t)r * D + d] * rinv * bf2f(w[d]));
+}
+
+// qkv [R, 3, H, Dh] bf16 -> o [R, H, Dh] bf16; row i attends to rows 0..i of its block (blocks of `block` rows)
+__global__ void block_attn_kernel(const __nv_bfloat16* qkv, int R, int H, int Dh, int block, float scale,
+                                  __nv_bfloat16* o) {
+  const int h = blockIdx.x, r = blockIdx.y;
+  const int lane = threadIdx.x;      // one warp
+  const int b0 = (r / block) * block;
+  const int64_t rs = (int64_t)3 * H * Dh;
+  float s[16];
+  float mx = -INFINITY;
+  for (int j = b0; j <= r; ++j) {
+    float d = 0.f;
+    for (int c = lane; c < Dh; c += 32)
+      d += bf2f(qkv[r * rs + h * Dh + c]) * bf2f(qkv[j * rs + H * Dh + h * Dh + c]);
+    d = warp_sum(d) * scale;
+    s[j - b0] = d;
+    mx = fmaxf(mx, d);
+  }
+  float den = 0.f;
+  for (int j = b0; j <= r; ++j) { s[j - b0] = __expf(s[j - b0] - mx); den += s[j - b0]; }
+  for (int c = lane; c < Dh; c += 32) {
+    float acc = 0.f;
+    for (int j = b0; j <= r; ++j) acc += s[j - b0] * bf2f(qkv[j * rs + 2 * H * Dh + h * Dh + c]);
+    o[((int64_t)r * H + h) * Dh + c] = f2bf(acc / den);
+  }
+}
+
+}  // namespace g53
+
+cudaError_t g53_rmsnorm_f32(const float* x, const __nv_bfloat16* w, int R, int D, float eps, __nv_bfloat16* y,
+                            cudaStream_t st) {
+  g53::rmsnorm_f32_kernel<<<R, 256, 0, st>>>(x, w, D, eps, y);
+  return cudaGetLastError();
+}
+
+cudaError_t g53_block_attn(const __nv_bfloat16* qkv, int R, int H, int Dh, int block, float scale, __nv_bfloat16* o,
+                           cudaStream_t st) {
+  if (block > 16 || block < 1) return cudaErrorInvalidValue;
+  dim3 grid(H, R);
+  g53::block_attn_kernel<<<grid, 32, 0, st>>>(qkv, R, H, Dh, block, scale, o);
+  return cudaGetLastError();
+}

@@ -144,8 +144,8 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(RouteArgs a) {
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) exl3_rot_in_kernel(Exl3Args a) {
   const int lane = threadIdx.x & 31;
-  const int blk = blockIdx.x * 4 + (threadIdx.x >> 5);
-  const int p = blockIdx.y;
+  const int blk = blockIdx.y * 4 + (threadIdx.x >> 5);
+  const int p = blockIdx.x;                      // pairs on grid.x (prefill chunks exceed 65535 pairs)
   if (blk * 128 >= a.K) return;
   const int r = a.pair_token[p], e = a.pair_expert[p];
   const int c0 = blk * 128 + lane * 4;
@@ -380,7 +380,7 @@ cudaError_t g53_moe_route(const RouteArgs& a, cudaStream_t st) {
 }
 
 cudaError_t g53_exl3_rot_in(const Exl3Args& a, cudaStream_t st) {
-  dim3 grid((a.K / 128 + 3) / 4, a.pairs);
+  dim3 grid(a.pairs, (a.K / 128 + 3) / 4);
   exl3_rot_in_kernel<<<grid, 128, 0, st>>>(a);
   G53_CHECK_LAUNCH();
   return cudaSuccess;

@@ -1,0 +1,404 @@
+"""The serving engine: continuous batching with chunked prefill, paged caches with prefix reuse, and speculative
+decoding with a block drafter and adaptive K.
+
+Per ``step()``:
+  1. admit waiting requests (a request slot + pages; prefix-cache reuse where a KDA state checkpoint exists)
+  2. prefill: the next chunk of each prefilling request (chunk ends aligned to the checkpoint interval, so the KDA
+     state can be saved at page-aligned prefixes), several requests in one forward up to ``prefill_chunk`` rows;
+     the request whose prompt completes samples its first token
+  3. decode: every running request contributes a window [last token, K drafts]; one forward verifies all windows;
+     greedy / forced / sampled acceptance; commit keeps the accepted rows (KDA replay when a window is cut); the
+     drafter proposes the next K tokens; adaptive K updates per request
+Reference behaviour: vLLM's V1 engine as configured by the reference (code/kit/launcher/start.sh:2666-2741), chunked
+prefill aligned to KDA blocks (code/kit/launcher/overlay/patch_mamba_align_chunking.py), DFlash2 speculative decoding
+with adaptive K (README.md:40, REPRODUCE.md:333).
+"""
+
+from __future__ import annotations
+
+import itertools
+import time
+from dataclasses import dataclass, field
+from enum import Enum
+
+import torch
+
+from .kv_manager import KVManager, OutOfPages, SeqCache, StateSlots, page_hash
+from .spec import AdaptiveK, greedy_accept
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 64
+    temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+    seed: int | None = None
+    stop_token_ids: tuple[int, ...] = ()
+    ignore_eos: bool = False
+
+
+@dataclass
+class EngineConfig:
+    max_seqs: int = 4
+    page_size: int = 64
+    num_pages: int = 256
+    max_model_len: int = 8192
+    prefill_chunk: int = 8192
+    speculative: bool = True
+    k_set: tuple[int, ...] = (4, 5, 7)
+    k_fixed: int | None = None
+    ema_alpha: float = 0.25
+    k_margin: float = 1.0
+    force_accept: bool = False             # benchmark mode: every draft accepted
+    block_verify: bool = False             # sampled requests: block verification instead of standard
+    checkpoints: int = 0                   # KDA state checkpoint slots (prefix cache for hybrid state)
+    checkpoint_pages: int = 8              # checkpoint interval in pages
+    prefill_first: bool = True             # a step with waiting prefill runs it before decode
+    cuda_graphs: bool = True
+
+
+class State(Enum):
+    WAITING = 0
+    PREFILL = 1
+    RUNNING = 2
+    FINISHED = 3
+
+
+@dataclass
+class Request:
+    rid: str
+    prompt: list[int]
+    params: SamplingParams
+    arrival: float = field(default_factory=time.time)
+    state: State = State.WAITING
+    output: list[int] = field(default_factory=list)
+    cache: SeqCache = field(default_factory=SeqCache)
+    slot: int = -1
+    cur: int = 0
+    pos: int = 0                            # tokens committed to the caches
+    drafts: list[int] = field(default_factory=list)
+    draft_logits: torch.Tensor | None = None
+    hidden: torch.Tensor | None = None
+    adaptive: AdaptiveK | None = None
+    first_token_time: float | None = None
+    finish_reason: str | None = None
+    cached_tokens: int = 0
+    accepted: list = field(default_factory=list)
+
+    @property
+    def tokens(self) -> list[int]:
+        return self.prompt + self.output
+
+
+@dataclass
+class RequestOutput:
+    rid: str
+    new_tokens: list[int]
+    finished: bool
+    finish_reason: str | None
+    output: list[int]
+
+
+class LLMEngine:
+    def __init__(self, backend, cfg: EngineConfig, eos: tuple[int, ...] = ()):
+        self.b = backend
+        self.cfg = cfg
+        self.eos = set(eos)
+        self.kv = KVManager(cfg.num_pages, cfg.page_size, (cfg.max_model_len + cfg.page_size - 1) // cfg.page_size)
+        self.slots = StateSlots(cfg.max_seqs, cfg.checkpoints)
+        self.waiting: list[Request] = []
+        self.running: list[Request] = []
+        self.done: dict[str, Request] = {}
+        self._ids = itertools.count()
+        self.metrics = {"prompt_tokens": 0, "generation_tokens": 0, "steps": 0, "spec_drafts": 0,
+                        "spec_accepted": 0, "prefix_cached_tokens": 0, "requests_finished": 0}
+
+    # ------------------------------------------------------------------------------------------------ requests
+    def add_request(self, prompt: list[int], params: SamplingParams | None = None, rid: str | None = None) -> str:
+        params = params or SamplingParams()
+        if len(prompt) == 0:
+            raise ValueError("empty prompt")
+        if len(prompt) + params.max_tokens > self.cfg.max_model_len:
+            raise ValueError(f"prompt + max_tokens exceeds max_model_len {self.cfg.max_model_len}")
+        rid = rid or f"req-{next(self._ids)}"
+        r = Request(rid, list(prompt), params)
+        r.adaptive = AdaptiveK(self.cfg.k_set, self.cfg.ema_alpha, self.cfg.k_margin, fixed=self.cfg.k_fixed)
+        self.waiting.append(r)
+        self.metrics["prompt_tokens"] += len(prompt)
+        return rid
+
+    def abort(self, rid: str) -> None:
+        for q in (self.waiting, self.running):
+            for r in q:
+                if r.rid == rid:
+                    r.finish_reason = "abort"
+                    self._finish(r)
+                    return
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    # ------------------------------------------------------------------------------------------------ admission
+    def _admit(self) -> None:
+        while self.waiting and self.slots.free:
+            r = self.waiting[0]
+            pids, hashes = self.kv.match_prefix(r.prompt[:-1])     # always recompute at least the last token
+            start = 0
+            ck = None
+            if pids and self.cfg.checkpoints:
+                # the longest cached prefix that also has a KDA state checkpoint
+                for n in range(len(hashes), 0, -1):
+                    ck = self.slots.find(hashes[n - 1])
+                    if ck is not None and ck.tokens == n * self.cfg.page_size:
+                        pids, hashes = pids[:n], hashes[:n]
+                        start = n * self.cfg.page_size
+                        break
+                    ck = None
+            if not self.kv.can_grow(SeqCache(pages=list(pids if start else [])), len(r.prompt) + 8):
+                break
+            self.waiting.pop(0)
+            r.slot = self.slots.alloc()
+            r.cur = 0
+            self.b.reset_state(r.slot)
+            if start:
+                self.kv.adopt_prefix(r.cache, pids, hashes)
+                self.b.load_state(ck.slot, r.slot, r.cur)
+                r.pos = start
+                r.cached_tokens = start
+                self.metrics["prefix_cached_tokens"] += start
+            r.state = State.PREFILL
+            self.running.append(r)
+
+    # ------------------------------------------------------------------------------------------------ step
+    def step(self) -> list[RequestOutput]:
+        self.metrics["steps"] += 1
+        self._admit()
+        outs: list[RequestOutput] = []
+        prefill = [r for r in self.running if r.state == State.PREFILL]
+        decode = [r for r in self.running if r.state == State.RUNNING]
+        if prefill and (self.cfg.prefill_first or not decode):
+            outs += self._prefill_step(prefill)
+        decode = [r for r in self.running if r.state == State.RUNNING]
+        if decode:
+            outs += self._decode_step(decode)
+        return outs
+
+    def _rows(self, r: Request, tokens: list[int], pos0: int):
+        from .backend import SeqRows
+        n = len(tokens)
+        self.kv.grow(r.cache, pos0 + n)
+        positions = list(range(pos0, pos0 + n))
+        return SeqRows(tokens, positions, [self.kv.slot(r.cache, p) for p in positions], list(r.cache.pages),
+                       r.slot, r.cur)
+
+    def _prefill_step(self, reqs: list[Request]) -> list[RequestOutput]:
+        budget = self.cfg.prefill_chunk
+        batch, ends = [], []
+        interval = self.cfg.checkpoint_pages * self.cfg.page_size if self.cfg.checkpoints else 0
+        for r in reqs:
+            if budget <= 0:
+                break
+            remaining = len(r.prompt) - r.pos
+            n = min(remaining, budget)
+            if interval:
+                # end the chunk on a checkpoint boundary when one lies inside it
+                nxt = (r.pos // interval + 1) * interval
+                if r.pos + n > nxt and nxt < len(r.prompt):
+                    n = nxt - r.pos
+            try:
+                rows = self._rows(r, r.prompt[r.pos:r.pos + n], r.pos)
+            except OutOfPages:
+                break
+            batch.append((r, rows))
+            budget -= n
+        if not batch:
+            return []
+        logit_rows, row = [], 0
+        finishing = []
+        for r, rows in batch:
+            row += len(rows.tokens)
+            if r.pos + len(rows.tokens) == len(r.prompt):
+                logit_rows.append(row - 1)
+                finishing.append((r, row - 1))
+        logits = self.b.prefill([rows for _, rows in batch], logit_rows)
+        outs = []
+        for r, rows in batch:
+            r.pos += len(rows.tokens)
+            r.cur = 1 - r.cur
+            self.kv.commit_tokens(r.cache, r.tokens, r.pos)
+            if interval and r.pos % interval == 0 and r.cache.hashes:
+                h = r.cache.hashes[r.pos // self.cfg.page_size - 1]
+                ck = self.slots.checkpoint_slot(h, r.pos)
+                if ck is not None:
+                    self.b.save_state(r.slot, r.cur, ck.slot)
+        if finishing:
+            toks = self._sample_rows(logits, [r for r, _ in finishing])
+            for i, (r, row_idx) in enumerate(finishing):
+                r.state = State.RUNNING
+                r.first_token_time = time.time()
+                r.hidden = self.b.hidden(row_idx).clone()
+                outs.append(self._emit(r, [toks[i]]))
+                if r.state == State.RUNNING and self.cfg.speculative and self.b.drafter is not None:
+                    self._draft(r)
+        return outs
+
+    def _sample_rows(self, logits: torch.Tensor, reqs: list[Request]) -> list[int]:
+        """One token per row: greedy rows by argmax, sampled rows with temperature / top-k / top-p."""
+        greedy = self.b.argmax(logits)
+        out = []
+        full = None
+        for i, r in enumerate(reqs):
+            p = r.params
+            if p.temperature <= 0:
+                out.append(greedy[i])
+                continue
+            if full is None:
+                full = self.b.full_logits(logits).float()
+            out.append(sample_token(full[i], p, seed_key(r, len(r.output))))
+        return out
+
+    def _draft(self, r: Request) -> None:
+        k = r.adaptive.current()
+        drafts, lg = self.b.draft(r.output[-1], r.hidden, k)
+        r.drafts = drafts[:k]
+        r.draft_logits = lg[:k].clone() if r.params.temperature > 0 else None
+
+    def _decode_step(self, reqs: list[Request]) -> list[RequestOutput]:
+        spec = self.cfg.speculative and self.b.drafter is not None
+        batch = []
+        for r in list(reqs):
+            window = [r.output[-1]] + (r.drafts if spec else [])
+            try:
+                batch.append((r, self._rows(r, window, r.pos)))
+            except OutOfPages:
+                r.finish_reason = "length"
+                self._finish(r)
+        if not batch:
+            return []
+        logits = self.b.verify([rows for _, rows in batch])
+        greedy = self.b.argmax(logits)
+        outs, keeps, row = [], [], 0
+        for r, rows in batch:
+            n_rows = len(rows.tokens)
+            tgt = greedy[row:row + n_rows]
+            drafts = rows.tokens[1:]
+            if self.cfg.force_accept:
+                n_acc = len(drafts)
+                new = drafts + [tgt[-1]]
+            elif r.params.temperature <= 0:
+                n_acc = greedy_accept(drafts, tgt)
+                new = drafts[:n_acc] + [tgt[n_acc]]
+            else:
+                n_acc, new = self._sampled_accept(r, logits[row:row + n_rows], drafts)
+            keeps.append(n_acc + 1)
+            r._new = new
+            r._last_row = row + n_acc
+            row += n_rows
+            if drafts:
+                self.metrics["spec_drafts"] += len(drafts)
+                self.metrics["spec_accepted"] += n_acc
+                r.accepted.append(n_acc)
+                r.adaptive.update(n_acc)
+        self.b.commit(keeps)
+        for (r, rows), keep in zip(batch, keeps):
+            r.pos += keep
+            r.cur = 1 - r.cur
+            self.kv.commit_tokens(r.cache, r.tokens, r.pos)
+            r.hidden = self.b.hidden(r._last_row).clone()
+            outs.append(self._emit(r, r._new))
+            if r.state == State.RUNNING and spec:
+                self._draft(r)
+        return outs
+
+    def _sampled_accept(self, r: Request, logits: torch.Tensor, drafts: list[int]):
+        """Rejection sampling of one request's window (CUDA kernel; standard or block verification)."""
+        from ..ops import kernels as K
+        p = r.params
+        full = self.b.full_logits(logits).float()
+        tp = torch.softmax(apply_filters(full / p.temperature, p), -1)
+        k = len(drafts)
+        if k == 0:
+            return 0, [sample_token(full[0], p, seed_key(r, len(r.output)))]
+        dl = self.b.full_logits(r.draft_logits).float()[:k]
+        dp = torch.softmax(apply_filters(dl / p.temperature, p), -1)
+        dev = tp.device
+        acc = torch.zeros(1, dtype=torch.int32, device=dev)
+        nxt = torch.zeros(1, k + 1, dtype=torch.int32, device=dev)
+        K.C().rejection_sample(tp.view(1, k + 1, -1).contiguous(), dp.view(1, k, -1).contiguous(),
+                               torch.tensor([drafts], dtype=torch.int32, device=dev),
+                               int(p.seed if p.seed is not None else hash(r.rid)) & ((1 << 62) - 1),
+                               torch.tensor([r.pos], dtype=torch.int64, device=dev), self.cfg.block_verify, acc, nxt,
+                               None)
+        n = int(acc.item())
+        row = nxt[0].tolist()
+        return n, row[:n + 1]
+
+    # ------------------------------------------------------------------------------------------------ outputs
+    def _emit(self, r: Request, new: list[int]) -> RequestOutput:
+        emitted = []
+        for t in new:
+            emitted.append(t)
+            r.output.append(t)
+            self.metrics["generation_tokens"] += 1
+            if (t in self.eos and not r.params.ignore_eos) or t in r.params.stop_token_ids:
+                r.finish_reason = "stop"
+                break
+            if len(r.output) >= r.params.max_tokens:
+                r.finish_reason = "length"
+                break
+        if r.finish_reason is not None:
+            self._finish(r)
+        return RequestOutput(r.rid, emitted, r.state == State.FINISHED, r.finish_reason, list(r.output))
+
+    def _finish(self, r: Request) -> None:
+        if r in self.running:
+            self.running.remove(r)
+        if r in self.waiting:
+            self.waiting.remove(r)
+        if r.slot >= 0:
+            self.slots.release(r.slot)
+            r.slot = -1
+        self.kv.free(r.cache)
+        r.state = State.FINISHED
+        self.done[r.rid] = r
+        self.metrics["requests_finished"] += 1
+
+    # ------------------------------------------------------------------------------------------------ offline
+    def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None,
+                 on_step=None) -> list[list[int]]:
+        if not isinstance(params, list):
+            params = [params or SamplingParams()] * len(prompts)
+        rids = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
+        while any(rid not in self.done for rid in rids):
+            outs = self.step()
+            if on_step:
+                on_step(outs)
+        return [self.done[rid].output for rid in rids]
+
+
+def seed_key(r: Request, index: int) -> int:
+    base = r.params.seed if r.params.seed is not None else (hash(r.rid) & 0xFFFFFFFF)
+    return (base * 1000003 + index) & ((1 << 63) - 1)
+
+
+def apply_filters(logits: torch.Tensor, p: SamplingParams) -> torch.Tensor:
+    x = logits
+    if p.top_k and p.top_k > 0:
+        kth = torch.topk(x, min(p.top_k, x.shape[-1]), dim=-1).values[..., -1:]
+        x = torch.where(x < kth, torch.full_like(x, float("-inf")), x)
+    if p.top_p < 1.0:
+        srt, idx = torch.sort(x, dim=-1, descending=True)
+        cum = torch.softmax(srt, -1).cumsum(-1)
+        drop = cum - torch.softmax(srt, -1) > p.top_p
+        srt = torch.where(drop, torch.full_like(srt, float("-inf")), srt)
+        x = torch.full_like(x, float("-inf")).scatter(-1, idx, srt)
+    return x
+
+
+def sample_token(logits: torch.Tensor, p: SamplingParams, key: int) -> int:
+    x = apply_filters(logits / max(p.temperature, 1e-6), p)
+    g = torch.Generator(device=x.device)
+    g.manual_seed(key)
+    probs = torch.softmax(x, -1)
+    return int(torch.multinomial(probs, 1, generator=g).item())

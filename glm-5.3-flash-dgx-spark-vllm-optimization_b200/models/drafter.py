@@ -1,0 +1,106 @@
+"""Block drafter for speculative decoding: one transformer layer that proposes K tokens in a single forward.
+
+Role of the reference's DFlash2 drafter (code/fork/docs/DRAFTER_IMPL.md:46-52; README.md:40): it reads the
+target's hidden state and drafts a block (block size 8, so K <= 7) that the target verifies in one window.  This
+drafter is a 1-layer block model ("a random-init 1-layer block drafter with block size 8"):
+
+  x_i   = fc([h ; emb(t_i)]) + slot_i          i = 0..K-1,  t_0 = last committed token, t_i = MASK (i > 0),
+                                               h = the target's final hidden state (stream mean) of that token
+  x    += o_proj(block_causal_attn(qkv(rmsnorm(x))))
+  x    += down(SwiGLU(gate_up(rmsnorm(x))))
+  logits_i = lm_head(rmsnorm(x_i))             the target's fp8 vocabulary-parallel head, shared
+  draft_i  = argmax logits_i                   (row i proposes the token at position p + 1 + i)
+
+Weights are fp8 e4m3 with per-row scales like the target's dense projections, random-initialised (seed-keyed), and
+replicated on every tensor-parallel rank; only the shared head is vocabulary-sharded.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from ..config import ModelConfig
+from ..ops import kernels as K
+from .runtime import interleave_gate_up
+from .weights import Linear8, quantize_fp8_rows, _seed_of
+
+MASK_TOKEN = 0
+
+
+@dataclass
+class DrafterConfig:
+    block: int = 8              # K <= block - 1 drafts, plus the anchor row
+    heads: int = 32
+    head_dim: int = 128
+    mlp_width: int = 8192
+
+
+class BlockDrafter:
+    def __init__(self, cfg: ModelConfig, target_w, dc: DrafterConfig | None = None, seed: int = 1,
+                 device="cuda"):
+        self.cfg, self.tw = cfg, target_w
+        dc = dc or DrafterConfig(heads=max(1, cfg.hidden // 128), head_dim=min(128, cfg.hidden),
+                                 mlp_width=2 * cfg.hidden)
+        self.dc = dc
+        D = cfg.hidden
+        H, Dh = dc.heads, dc.head_dim
+        dev = torch.device(device)
+
+        def lin(name, n, k):
+            g = torch.Generator(device=dev)
+            g.manual_seed(_seed_of(seed, name))
+            return quantize_fp8_rows(torch.randn(n, k, generator=g, device=dev) / math.sqrt(k))
+
+        def norm(name, n):
+            g = torch.Generator(device=dev)
+            g.manual_seed(_seed_of(seed, name))
+            return (1 + 0.05 * torch.randn(n, generator=g, device=dev)).to(torch.bfloat16)
+
+        self.fc = lin("drafter.fc", D, 2 * D)
+        self.qkv = lin("drafter.qkv", 3 * H * Dh, D)
+        self.o = lin("drafter.o", D, H * Dh)
+        self.gu = interleave_gate_up(lin("drafter.gate_up", 2 * dc.mlp_width, D))
+        self.down = lin("drafter.down", D, dc.mlp_width)
+        self.n1, self.n2, self.nf = norm("drafter.n1", D), norm("drafter.n2", D), norm("drafter.nf", D)
+        g = torch.Generator(device=dev)
+        g.manual_seed(_seed_of(seed, "drafter.slot"))
+        self.slot_emb = (torch.randn(dc.block, D, generator=g, device=dev) * 0.1).float()
+        R = dc.block
+        bf = torch.bfloat16
+        self.inp = torch.zeros(R, 2 * D, dtype=bf, device=dev)
+        self.emb = torch.zeros(R, 1, D, dtype=bf, device=dev)
+        self.x = torch.zeros(R, D, dtype=torch.float32, device=dev)
+        self.xn = torch.zeros(R, D, dtype=bf, device=dev)
+        self.qkv_buf = torch.zeros(R, 3 * H * Dh, dtype=bf, device=dev)
+        self.att = torch.zeros(R, H * Dh, dtype=bf, device=dev)
+        self.act = torch.zeros(R, dc.mlp_width, dtype=bf, device=dev)
+        self.logits = torch.zeros(R, target_w.head.n, dtype=torch.float32, device=dev)
+        self.ids = torch.full((R,), MASK_TOKEN, dtype=torch.int32, device=dev)
+
+    @torch.no_grad()
+    def forward(self, last_token: torch.Tensor, hidden: torch.Tensor, k: int) -> torch.Tensor:
+        """last_token: int32 [1] (device); hidden: bf16 [D] target hidden of that token. Returns logits [k, V_local]
+        (the caller samples / argmaxes them through the tensor-parallel sampler)."""
+        Kc = K.C()
+        D = self.cfg.hidden
+        R = max(k, 1)
+        self.ids[:1].copy_(last_token)
+        # [h ; emb(t_i)]
+        Kc.embed(self.ids[:R], self.tw.embed, self.emb[:R])
+        self.inp[:R, D:].copy_(self.emb[:R, 0])
+        self.inp[:R, :D].copy_(hidden.view(1, D).expand(R, D))
+        self.x[:R].copy_(self.slot_emb[:R])
+        K.linear8(self.inp[:R], self.fc.w, self.fc.s, self.x[:R], K.GEMV_F32_ACC)
+        Kc.rmsnorm_f32(self.x[:R], self.n1, self.cfg.eps, self.xn[:R])
+        K.linear8(self.xn[:R], self.qkv.w, self.qkv.s, self.qkv_buf[:R])
+        Kc.block_attn(self.qkv_buf[:R], self.dc.heads, self.dc.head_dim, R, self.dc.head_dim ** -0.5, self.att[:R])
+        K.linear8(self.att[:R], self.o.w, self.o.s, self.x[:R], K.GEMV_F32_ACC)
+        Kc.rmsnorm_f32(self.x[:R], self.n2, self.cfg.eps, self.xn[:R])
+        K.linear8(self.xn[:R], self.gu.w, self.gu.s, self.act[:R], K.GEMV_SWIGLU, self.cfg.limit)
+        K.linear8(self.act[:R], self.down.w, self.down.s, self.x[:R], K.GEMV_F32_ACC)
+        Kc.rmsnorm_f32(self.x[:R], self.nf, self.cfg.eps, self.xn[:R])
+        K.linear8(self.xn[:R], self.tw.head.w, self.tw.head.s, self.logits[:R], K.GEMV_F32)
+        return self.logits[:R]

@@ -208,26 +208,57 @@ class Runtime:
     # ------------------------------------------------------------------------------------------------------------
     def stage(self, ids, positions, slots, row_seq, seqs, block_tables, logit_rows) -> int:
         """ids/positions/slots/row_seq: per-row ints; seqs: per sequence (row0, nrows, s_in, s_out, conv_slot);
-        block_tables: per sequence list of page ids; logit_rows: rows whose logits are computed."""
+        block_tables: per sequence list of page ids; logit_rows: rows whose logits are computed.  Everything is
+        packed into one pinned host buffer and copied to the static device buffers asynchronously."""
         b = self.batch
         R, B = len(ids), len(seqs)
         if R > self.rc.max_rows or B > self.rc.max_seqs or len(logit_rows) > self.rc.logit_rows:
             raise ValueError("batch exceeds the runtime's static buffers")
-        dev = self.device
-        b.ids[:R].copy_(torch.as_tensor(ids, dtype=i32), non_blocking=True)
-        b.positions[:R].copy_(torch.as_tensor(positions, dtype=i32), non_blocking=True)
-        b.slots[:R].copy_(torch.as_tensor(slots, dtype=i32), non_blocking=True)
-        b.row_seq[:R].copy_(torch.as_tensor(row_seq, dtype=i32), non_blocking=True)
-        sq = torch.as_tensor(seqs, dtype=i32).t().contiguous()
-        b.kda_seq[:, :B].copy_(sq, non_blocking=True)
-        for i, bt in enumerate(block_tables):
-            if len(bt) > self.rc.max_blocks:
-                raise ValueError("page table wider than max_blocks")
-            b.block_table[i, :len(bt)].copy_(torch.as_tensor(bt, dtype=i32), non_blocking=True)
-        b.logit_rows[:len(logit_rows)].copy_(torch.as_tensor(logit_rows, dtype=torch.int64), non_blocking=True)
+        nbt = max((len(t) for t in block_tables), default=0)
+        if nbt > self.rc.max_blocks:
+            raise ValueError("page table wider than max_blocks")
+        n_needed = 4 * R + 5 * B + B * nbt + 2 * len(logit_rows) + 1
+        if b.host.numel() < n_needed:
+            b.host = torch.zeros(2 * n_needed, dtype=i32, pin_memory=torch.cuda.is_available())
+        # the previous staging copies must have left the pinned buffer before it is rewritten
+        if getattr(b, "staged", None) is not None:
+            b.staged.synchronize()
+        h = b.host.numpy()
+        o = 0
+        segs = []
+        for arr in (ids, positions, slots, row_seq):
+            h[o:o + R] = arr
+            segs.append((o, R))
+            o += R
+        sq = [list(col) for col in zip(*seqs)]          # 5 rows of B
+        for row in sq:
+            h[o:o + B] = row
+            o += B
+        sq_off = o - 5 * B
+        bt_off = o
+        for t in block_tables:
+            h[o:o + len(t)] = t
+            o += nbt
+        o += o & 1                                        # 8-byte alignment of the int64 logit-row indices
+        lr = h[o:o + 2 * len(logit_rows)].view("int64")
+        lr[:] = logit_rows
+        lr_off = o
+        hb = b.host
+        for dst, (off, n) in zip((b.ids, b.positions, b.slots, b.row_seq), segs):
+            dst[:n].copy_(hb[off:off + n], non_blocking=True)
+        b.kda_seq[:, :B].copy_(hb[sq_off:sq_off + 5 * B].view(5, B), non_blocking=True)
+        if nbt:
+            b.block_table[:B, :nbt].copy_(hb[bt_off:bt_off + B * nbt].view(B, nbt), non_blocking=True)
+        if logit_rows:
+            b.logit_rows[:len(logit_rows)].copy_(hb[lr_off:lr_off + 2 * len(logit_rows)].view(torch.int64),
+                                                 non_blocking=True)
+        if torch.cuda.is_available():
+            b.staged = torch.cuda.Event()
+            b.staged.record()
         b.R, b.B = R, B
         b.max_rows_per_seq = max(s[1] for s in seqs)
         b.n_logits = len(logit_rows)
+        b.h2d_bytes = 4 * n_needed
         return R
 
     # ------------------------------------------------------------------------------------------------------------

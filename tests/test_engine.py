@@ -1,0 +1,108 @@
+"""Engine logic on CPU with a deterministic fake backend: exact greedy speculative decoding, forced acceptance,
+adaptive K, chunked prefill, paging and prefix reuse with KDA checkpoints, concurrency, limits."""
+
+import pytest
+
+from glm53.engine.kv_manager import KVManager, OutOfPages, PageAllocator, SeqCache, page_hash
+from glm53.engine.llm import EngineConfig, LLMEngine, SamplingParams
+from glm53.engine.spec import AdaptiveK, greedy_accept
+from tests.fake_backend import FakeBackend, reference_greedy
+
+
+def _engine(**kw):
+    cfg = EngineConfig(**{"max_seqs": 4, "page_size": 16, "num_pages": 128, "max_model_len": 1024,
+                          "prefill_chunk": 48, "cuda_graphs": False, **kw})
+    return LLMEngine(FakeBackend(max_seqs=cfg.max_seqs, checkpoints=cfg.checkpoints), cfg)
+
+
+@pytest.mark.parametrize("spec", [False, True])
+def test_greedy_output_equals_target_greedy(spec):
+    e = _engine(speculative=spec)
+    prompt = list(range(20, 120))
+    out = e.generate([prompt], SamplingParams(max_tokens=40))[0]
+    assert out == reference_greedy(prompt, 40)
+    if spec:
+        m = e.metrics
+        assert 0 < m["spec_accepted"] < m["spec_drafts"]     # the drafter is wrong every third position
+
+
+def test_forced_acceptance_emits_k_plus_one():
+    e = _engine(force_accept=True, k_fixed=7)
+    e.add_request(list(range(20, 60)), SamplingParams(max_tokens=64))
+    e.step()                                                # prefill + first token (+ first decode window)
+    n0 = len(e.running[0].output) if e.running else 64
+    e.step()
+    n1 = len(e.running[0].output) if e.running else 64
+    assert n1 - n0 == 8
+
+
+def test_adaptive_k():
+    ak = AdaptiveK((4, 5, 7), alpha=0.25, margin=1.0)
+    assert ak.current() == 7
+    for _ in range(20):
+        ak.update(1)
+    assert ak.current() == 4
+    for _ in range(40):
+        ak.update(7)
+    assert ak.current() == 7
+    assert greedy_accept([1, 2, 3], [1, 2, 9, 4]) == 2
+
+
+def test_concurrent_requests_and_chunked_prefill():
+    e = _engine(max_seqs=3, prefill_chunk=32)
+    prompts = [list(range(30 + i, 130 + 3 * i)) for i in range(5)]
+    outs = e.generate(prompts, [SamplingParams(max_tokens=10 + 5 * i) for i in range(5)])
+    for p, o, i in zip(prompts, outs, range(5)):
+        assert o == reference_greedy(p, 10 + 5 * i)
+    assert e.metrics["requests_finished"] == 5
+    assert not e.running and not e.waiting
+    assert e.kv.alloc.num_free == 128                      # every page back (free or evictable)
+
+
+def test_prefix_reuse_with_state_checkpoint():
+    e = _engine(checkpoints=4, checkpoint_pages=2, page_size=16)
+    shared = list(range(40, 40 + 96))                       # 3 checkpoint intervals of 32 tokens
+    a = e.generate([shared + [7, 8, 9]], SamplingParams(max_tokens=8))[0]
+    b_prompt = shared + [5, 6]
+    b = e.generate([b_prompt], SamplingParams(max_tokens=8))[0]
+    assert b == reference_greedy(b_prompt, 8)
+    assert e.metrics["prefix_cached_tokens"] == 96
+    assert e.b.calls["load"] == 1
+    assert a == reference_greedy(shared + [7, 8, 9], 8)
+
+
+def test_stop_tokens_and_max_len():
+    e = _engine()
+    prompt = list(range(20, 50))
+    ref = reference_greedy(prompt, 30)
+    out = e.generate([prompt], SamplingParams(max_tokens=30, stop_token_ids=(ref[5],)))[0]
+    assert out == ref[:6]
+    with pytest.raises(ValueError):
+        e.add_request(list(range(1000)), SamplingParams(max_tokens=100))
+
+
+def test_page_allocator_prefix_cache_and_eviction():
+    pa = PageAllocator(4, 8)
+    p0, p1 = pa.alloc(), pa.alloc()
+    h0 = page_hash(None, list(range(8)))
+    pa.register(p0, h0)
+    pa.release(p0)
+    pa.release(p1)
+    assert pa.num_free == 4
+    assert pa.lookup(h0) == p0
+    got = [pa.alloc() for _ in range(4)]                   # the cached page is evicted last
+    assert p0 in got and pa.stats["evictions"] == 1
+    with pytest.raises(OutOfPages):
+        pa.alloc()
+
+
+def test_kv_manager_slots():
+    kv = KVManager(16, 8, 4)
+    sc = SeqCache()
+    kv.grow(sc, 20)
+    assert len(sc.pages) == 3
+    assert kv.slot(sc, 9) == sc.pages[1] * 8 + 1
+    with pytest.raises(OutOfPages):
+        kv.grow(sc, 40)
+    kv.free(sc)
+    assert kv.alloc.num_free == 16

@@ -1,0 +1,54 @@
+"""The engine on the GPU with the tiny proxy: greedy speculative decoding emits exactly the tokens of greedy
+decoding without speculation (per-row kernels are independent of window composition), concurrent requests, and a
+prefix-cache hit (KDA checkpoint + shared pages) reproduces the cold-start output."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _llm(**kw):
+    from glm53.api.offline import LLM, LLMOptions
+    opts = dict(model="tiny", max_seqs=4, max_model_len=1024, prefill_chunk=128, page_size=64, checkpoints=4)
+    opts.update(kw)
+    return LLM(LLMOptions(**opts))
+
+
+def _prompts(n, length, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randint(16, 4096, (length + 7 * i,), generator=g).tolist() for i in range(n)]
+
+
+def test_spec_greedy_equals_plain_greedy():
+    from glm53.engine.llm import SamplingParams
+    prompts = _prompts(3, 150)
+    sp = SamplingParams(max_tokens=40, ignore_eos=True)
+    plain = _llm(speculative=False).engine.generate(prompts, sp)
+    spec_llm = _llm(speculative=True)
+    spec = spec_llm.engine.generate(prompts, sp)
+    assert spec == plain
+    m = spec_llm.engine.metrics
+    assert m["spec_drafts"] > 0
+
+
+def test_forced_acceptance_and_text_api():
+    from glm53.engine.llm import SamplingParams
+    llm = _llm(speculative=True, k_fixed=7, force_accept=True)
+    out = llm.generate(["hello B200"], SamplingParams(max_tokens=33, ignore_eos=True))
+    assert len(out[0]["token_ids"]) == 33
+    assert isinstance(out[0]["text"], str)
+
+
+def test_prefix_cache_hit_reproduces_output():
+    from glm53.engine.llm import SamplingParams
+    llm = _llm(speculative=False, checkpoints=4)
+    base = _prompts(1, 300, seed=3)[0]
+    a = llm.engine.generate([base], SamplingParams(max_tokens=16, ignore_eos=True))[0]
+    # the engine saved KDA checkpoints every 8 pages (512 tokens) -> use a 64-token page interval here
+    llm2 = _llm(speculative=False, checkpoints=4)
+    llm2.engine.cfg.checkpoint_pages = 1
+    a2 = llm2.engine.generate([base], SamplingParams(max_tokens=16, ignore_eos=True))[0]
+    b = llm2.engine.generate([base], SamplingParams(max_tokens=16, ignore_eos=True))[0]
+    assert llm2.engine.metrics["prefix_cached_tokens"] >= 256
+    assert a == a2 == b
