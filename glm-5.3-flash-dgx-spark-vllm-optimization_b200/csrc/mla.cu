@@ -344,3 +344,79 @@ cudaError_t g53_mla_decode(const MlaAttnArgs& a, cudaStream_t st) {
   G53_CHECK_LAUNCH();
   return cudaSuccess;
 }
+
+// ---------------------------------------------------------------------------------------------------------------
+// Allocation-free entry point (declared in mla_noalloc.h): the split partials of the flash-decoding kernel live in
+// a file-scope device array instead of caller-provided scratch.
+// ---------------------------------------------------------------------------------------------------------------
+#include <mutex>
+#include "mla_noalloc.h"
+
+static __device__ __align__(256) float g53_mla_noalloc_scratch[G53_MLA_NOALLOC_MAX_PARTIAL + G53_MLA_NOALLOC_MAX_STATS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+float* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of the scratch array on the current device (looked up once per device).  A host-side use of the
+// symbol name itself would give a host stand-in address, not device memory, so the address is always taken from
+// cudaGetSymbolAddress with the device current.
+cudaError_t noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g53_mla_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return e != cudaSuccess ? e : cudaErrorInvalidSymbol;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+}  // namespace
+
+extern "C" int g53_mla_decode_noalloc(const void* q_lat, const void* q_pe, int64_t q_pe_ld, int q_pe_hs,
+                                      const void* kv_cache, const float* kv_scale, const void* kpe_cache,
+                                      const int* sel, const int* sel_count, int max_sel, int R, int H, int L, int rope,
+                                      float sm_scale, int splits, void* o_lat, void* stream) {
+  if (R < 1 || H < 1 || L < 1 || splits < 1) return (int)cudaErrorInvalidValue;
+  const int64_t partial = (int64_t)R * splits * H * L;
+  const int64_t stats = (int64_t)R * splits * H * 2;
+  if (partial > G53_MLA_NOALLOC_MAX_PARTIAL || stats > G53_MLA_NOALLOC_MAX_STATS) return G53_NOALLOC_ERR_TOO_LARGE;
+  float* scratch = nullptr;
+  const cudaError_t e = noalloc_scratch(&scratch);
+  if (e != cudaSuccess) return G53_NOALLOC_ERR_SYMBOL;
+  MlaAttnArgs a{};
+  a.q_lat = static_cast<const __nv_bfloat16*>(q_lat);
+  a.q_pe = static_cast<const __nv_bfloat16*>(q_pe);
+  a.q_pe_ld = q_pe_ld;
+  a.q_pe_hs = q_pe_hs;
+  a.kv_cache = static_cast<const uint8_t*>(kv_cache);
+  a.kv_scale = kv_scale;
+  a.kpe_cache = static_cast<const __nv_bfloat16*>(kpe_cache);
+  a.sel = sel;
+  a.sel_count = sel_count;
+  a.max_sel = max_sel;
+  a.R = R;
+  a.H = H;
+  a.L = L;
+  a.rope = rope;
+  a.sm_scale = sm_scale;
+  a.splits = splits;
+  a.part_o = scratch;
+  a.part_ml = scratch + G53_MLA_NOALLOC_MAX_PARTIAL;
+  a.o_lat = static_cast<__nv_bfloat16*>(o_lat);
+  return (int)g53_mla_decode(a, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" const char* g53_mla_decode_noalloc_error(int code) {
+  if (code == 0) return "ok";
+  if (code == G53_NOALLOC_ERR_TOO_LARGE)
+    return "problem too large for the fixed scratch: R*splits*H*L must be <= 2^20 and R*splits*H*2 <= 2^15";
+  if (code == G53_NOALLOC_ERR_SYMBOL) return "could not obtain the device address of the scratch array";
+  return cudaGetErrorString(static_cast<cudaError_t>(code));
+}
