@@ -48,6 +48,7 @@ void gemv(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, 
   TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && p.ldx % 8 == 0 && p.bsx % 8 == 0,
               "gemv: activation rows must start on 16-byte boundaries (row stride ", p.ldx, ")");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0, "gemv: weights must be 16-byte aligned");
+  p.push_ptrs = nullptr;
   p.bsw = batched ? w.stride(0) : 0;
   p.bss = (batched && scale.has_value()) ? scale->stride(0) : 0;
   p.ldy = y.stride(-2);
@@ -131,6 +132,35 @@ int64_t gemm_error(const Tensor& like) {
   const int64_t v = e[0].item<int>();
   e.zero_();
   return v;
+}
+
+// fused tensor-parallel variant: the fp32 partial is also pushed into every rank's receive slot (peer memory)
+void gemv_push(const Tensor& x, const Tensor& w, const Tensor& scale, const Tensor& y, int64_t mode,
+               const Tensor& push_ptrs, const Tensor& push_flags, const Tensor& push_done, int64_t slot, int64_t rank,
+               int64_t world, const Tensor& err) {
+  TORCH_CHECK(mode == GEMV_F32 || mode == GEMV_F32_ACC, "push needs an fp32 output mode");
+  TORCH_CHECK(w.dim() == 2 && x.dim() == 2 && y.is_contiguous() && y.stride(0) * y.size(0) <= slot);
+  GemvArgs p{};
+  p.x = P<const __nv_bfloat16>(x);
+  p.w = w.data_ptr();
+  p.scale = P<const float>(scale);
+  p.y = y.data_ptr();
+  p.batch = 1;
+  p.M = (int)x.size(0);
+  p.K = (int)x.size(1);
+  p.N = (int)w.size(0);
+  p.ldx = x.stride(0);
+  p.ldy = y.stride(0);
+  p.mode = (int)mode;
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && p.ldx % 8 == 0, "gemv: misaligned activations");
+  p.push_ptrs = reinterpret_cast<float* const*>(push_ptrs.data_ptr());
+  p.push_flags = reinterpret_cast<unsigned* const*>(push_flags.data_ptr());
+  p.push_done = reinterpret_cast<unsigned*>(push_done.data_ptr());
+  p.push_slot = slot;
+  p.push_rank = (int)rank;
+  p.push_world = (int)world;
+  p.err = P<int>(err);
+  check(g53_gemv_fp8(p, stream()), "gemv_push");
 }
 
 // ------------------------------------------------------------------------------------------------- MoE
@@ -310,6 +340,7 @@ void hc_post_pre(const Tensor& X, const OptT& branch, const OptT& post, const Op
   a.hc_eps = (float)hc_eps;
   a.iters = (int)iters;
   TORCH_CHECK(X.is_contiguous(), "X must be contiguous [R, S, D]");
+  a.gath = nullptr;
   TORCH_CHECK(part.numel() >= (int64_t)a.R * (a.D / 64) * 32, "part scratch too small");
   check(g53_hc_post_pre(a, stream()), "hc_post_pre");
 }
@@ -346,6 +377,41 @@ void block_attn(const Tensor& qkv, int64_t H, int64_t Dh, int64_t block, double 
   check(g53_block_attn(P<const __nv_bfloat16>(qkv), (int)qkv.size(0), (int)H, (int)Dh, (int)block, (float)scale,
                        P<__nv_bfloat16>(o), stream()),
         "block_attn");
+}
+
+// post (reducing the ranks' pushed partials in rank order) fused with pre
+void hc_post_pre_tp(const Tensor& X, const Tensor& gath, int64_t slot, int64_t world, const Tensor& flags,
+                    const Tensor& epoch, const Tensor& done, const Tensor& err, const Tensor& post,
+                    const Tensor& comb, const OptT& fn, const OptT& base, const OptT& hscale, const OptT& norm_w,
+                    const OptT& normed, const OptT& post_out, const OptT& comb_out, const Tensor& part, double eps,
+                    double hc_eps, int64_t iters) {
+  HcArgs a{};
+  a.X = P<__nv_bfloat16>(X);
+  a.post = P<const float>(post);
+  a.comb = P<const float>(comb);
+  a.fn = P<const __nv_bfloat16>(fn);
+  a.base = P<const float>(base);
+  a.hscale = P<const float>(hscale);
+  a.norm_w = P<const __nv_bfloat16>(norm_w);
+  a.normed = P<__nv_bfloat16>(normed);
+  a.post_out = P<float>(post_out);
+  a.comb_out = P<float>(comb_out);
+  a.part = P<float>(part);
+  a.R = (int)X.size(0);
+  a.S = (int)X.size(1);
+  a.D = (int)X.size(2);
+  a.eps = (float)eps;
+  a.hc_eps = (float)hc_eps;
+  a.iters = (int)iters;
+  a.gath = P<const float>(gath);
+  a.gath_slot = slot;
+  a.world = (int)world;
+  a.flags = reinterpret_cast<const unsigned*>(flags.data_ptr());
+  a.epoch = reinterpret_cast<unsigned*>(epoch.data_ptr());
+  a.done = reinterpret_cast<unsigned*>(done.data_ptr());
+  a.err = P<int>(err);
+  TORCH_CHECK(X.is_contiguous());
+  check(g53_hc_post_pre(a, stream()), "hc_post_pre_tp");
 }
 
 // ------------------------------------------------------------------------------------------------- KDA
@@ -595,6 +661,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("exl3_rot_in", &exl3_rot_in);
   m.def("exl3_unpack", &exl3_unpack);
   m.def("hc_post_pre", &hc_post_pre);
+  m.def("hc_post_pre_tp", &hc_post_pre_tp);
+  m.def("gemv_push", &gemv_push);
   m.def("embed", &embed);
   m.def("stream_mean_norm", &stream_mean_norm);
   m.def("rmsnorm", &rmsnorm);

@@ -101,6 +101,28 @@ __device__ __forceinline__ uint32_t ldg_nc_u32(const void* p) {
   return r;
 }
 
+// ---- cross-GPU signalling over peer memory (system scope) ----
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Wait until *p - target >= 0 (wrap-around order).  Bounded: after ~2^22 polls (about a second with the back-off)
+// the wait records `code` in *err and returns false, so a peer that never arrives cannot hang the GPU.
+__device__ __forceinline__ bool wait_flag_geq(const unsigned* p, unsigned target, int* err, int code) {
+  for (uint32_t n = 0;; ++n) {
+    if ((int)(ld_acquire_sys(p) - target) >= 0) return true;
+    if (n > (1u << 22)) {
+      if (err) atomicExch(err, code);
+      return false;
+    }
+    if (n > 32) __nanosleep(128);
+  }
+}
+
 // In-warp orthonormal 128-point Walsh-Hadamard transform (Sylvester order). Lane l holds elements 4l..4l+3.
 __device__ __forceinline__ void fwht128_warp(float (&v)[4]) {
   const int lane = threadIdx.x & 31;

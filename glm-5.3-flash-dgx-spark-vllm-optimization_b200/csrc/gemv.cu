@@ -165,10 +165,29 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
     const int64_t off = (int64_t)b * p.bsy + (int64_t)tok * p.ldy + n;
     if (p.mode == GEMV_BF16) {
       reinterpret_cast<__nv_bfloat16*>(p.y)[off] = f2bf(v);
-    } else if (p.mode == GEMV_F32) {
-      reinterpret_cast<float*>(p.y)[off] = v;
-    } else {  // GEMV_F32_ACC
-      reinterpret_cast<float*>(p.y)[off] += v;
+    } else {
+      float* yf = reinterpret_cast<float*>(p.y);
+      if (p.mode == GEMV_F32_ACC) v += yf[off];
+      yf[off] = v;
+      if (p.push_ptrs) {
+        // this rank's partial into its slot of every rank's receive buffer (peer stores over NVLink)
+        const int64_t so = (int64_t)p.push_rank * p.push_slot + off;
+        for (int j = 0; j < p.push_world; ++j) p.push_ptrs[j][so] = v;
+      }
+    }
+  }
+  if (p.push_ptrs) {
+    // the last CTA to finish raises this rank's arrival flag on every rank (release after all CTAs' stores)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      const unsigned total = gridDim.x * gridDim.y;
+      const unsigned prev = atomicAdd(p.push_done, 1u);
+      if (prev == total - 1) {
+        *p.push_done = 0u;
+        __threadfence_system();
+        for (int j = 0; j < p.push_world; ++j) red_release_sys_add(p.push_flags[j] + p.push_rank, 1u);
+      }
     }
   }
 }

@@ -17,6 +17,15 @@ struct GemvArgs {
   int M, N, K, batch;
   int mode;
   float limit;                                         // SwiGLU clamp
+  // fused all-gather of the fp32 partial (tensor-parallel row-parallel projections, modes F32 / F32_ACC): every
+  // output element is also stored into each rank's receive slot `push_rank` over peer memory, and the last CTA
+  // raises this rank's arrival flag on every peer (release); null push_ptrs = no push
+  float* const* push_ptrs;                             // [world] receive-buffer base on each rank (this parity)
+  unsigned* const* push_flags;                         // [world] arrival flags base on each rank (this parity)
+  unsigned* push_done;                                 // local CTA completion counter
+  int64_t push_slot;                                   // elements per rank slot
+  int push_rank, push_world;
+  int* err;                                            // device error word (bounded waits)
 };
 cudaError_t g53_gemv_fp8(const GemvArgs& p, cudaStream_t st);
 cudaError_t g53_gemv_bf16(const GemvArgs& p, cudaStream_t st);
@@ -117,6 +126,15 @@ struct HcArgs {
   float* part;                // [R, NB, 32] scratch partial dots (+ sum of squares in slot n_mix)
   int R, S, D;
   float eps, hc_eps; int iters;
+  // fused reduce of the tensor-parallel partials: branch = sum over ranks (rank order) of gath[j] once every rank's
+  // arrival flag reached epoch + 1 (bounded wait); null gath = branch is already reduced
+  const float* gath;          // [world][slot] receive buffer of this parity (local)
+  int64_t gath_slot;
+  int world;
+  const unsigned* flags;      // [world] arrival flags of this parity (local)
+  unsigned* epoch;            // consumptions of this parity so far (local)
+  unsigned* done;             // CTA completion counter (local)
+  int* err;
 };
 cudaError_t g53_hc_post_pre(const HcArgs& a, cudaStream_t st);   // (optional post) then pre
 cudaError_t g53_embed(const int* ids, const __nv_bfloat16* table, int R, int D, int S, __nv_bfloat16* X,

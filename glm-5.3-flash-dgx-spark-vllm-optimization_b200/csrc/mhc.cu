@@ -32,13 +32,28 @@ __global__ void __launch_bounds__(kDB) hc_partial_kernel(HcArgs a) {
 #pragma unroll
     for (int s = 0; s < S; ++s) fnv[i][s] = pre ? bf2f(a.fn[(int64_t)i * S * a.D + s * a.D + d]) : 0.f;
   const int r0 = blockIdx.y * kRB;
+  if (a.gath) {
+    // tensor-parallel partials pushed by every rank's producer: wait for all arrival flags of this parity
+    if (threadIdx.x == 0) {
+      const unsigned target = *reinterpret_cast<volatile unsigned*>(a.epoch) + 1u;
+      for (int j = 0; j < a.world; ++j) wait_flag_geq(a.flags + j, target, a.err, 21);
+    }
+    __syncthreads();
+  }
   for (int r = r0; r < min(r0 + kRB, a.R); ++r) {
     __nv_bfloat16* xr = a.X + (int64_t)r * S * a.D;
     float x[S];
 #pragma unroll
     for (int s = 0; s < S; ++s) x[s] = bf2f(xr[s * a.D + d]);
-    if (a.branch) {
-      const float b = round_bf16(a.branch[(int64_t)r * a.D + d]);
+    if (a.branch || a.gath) {
+      float bsum;
+      if (a.gath) {
+        bsum = 0.f;
+        for (int j = 0; j < a.world; ++j) bsum += a.gath[(int64_t)j * a.gath_slot + (int64_t)r * a.D + d];
+      } else {
+        bsum = a.branch[(int64_t)r * a.D + d];
+      }
+      const float b = round_bf16(bsum);
       float nx[S];
 #pragma unroll
       for (int s = 0; s < S; ++s) {
@@ -69,6 +84,19 @@ __global__ void __launch_bounds__(kDB) hc_partial_kernel(HcArgs a) {
       a.part[((int64_t)r * NB + blockIdx.x) * 32 + threadIdx.x] = t;
     }
     __syncthreads();
+  }
+  if (a.gath) {
+    // the last CTA marks this parity's receive buffer consumed (every CTA read the epoch before counting in)
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      const unsigned prev = atomicAdd(a.done, 1u);
+      if (prev == gridDim.x * gridDim.y - 1) {
+        *a.done = 0u;
+        __threadfence();
+        atomicAdd(a.epoch, 1u);
+      }
+    }
   }
 }
 

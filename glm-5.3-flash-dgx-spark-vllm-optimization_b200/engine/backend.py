@@ -98,7 +98,10 @@ class GPUBackend:
 
     @torch.no_grad()
     def argmax(self, logits: torch.Tensor) -> list[int]:
-        return self.sampler(logits).tolist()
+        out = self.sampler(logits).tolist()          # synchronises: kernel error words can be read now
+        if self.rt.px is not None:
+            self.rt.px.check()
+        return out
 
     @torch.no_grad()
     def full_logits(self, logits: torch.Tensor) -> torch.Tensor:

@@ -88,6 +88,11 @@ class Runtime:
         R = rc.max_rows
         D, S = c.hidden, c.streams
         self.batch = Batch(rc, dev)
+        self.px = None
+        self._fused = False
+        if comm is not None and self.tp > 1 and getattr(comm, "fused", False):
+            from ..parallel.fused import PeerExchange
+            self.px = PeerExchange(min(R, rc.decode_rows, K.GEMV_MAX_M), D, dev)
         # --- GPU-layout weights (SwiGLU-interleaved gate/up) ---
         self.gu_il = {}
         for lw in w.layers:
@@ -280,32 +285,33 @@ class Runtime:
         Kc.embed(b.ids[:R], self.w.embed, X)
         cur = 0
         first = True
+        # decode windows under tensor parallelism: block partials are pushed to the peers by the block's last GEMV
+        # and reduced inside the next mHC kernel (parallel/fused.py); otherwise an all-reduce between the two
+        self._fused = self.px is not None and R <= min(self.px.rows, K.GEMV_MAX_M)
+        self._point = 0
         for lw in self.w.layers:
             # post of the previous FFN (none before layer 0) fused with this layer's attention pre
             nxt = 1 - cur
-            Kc.hc_post_pre(X, None if first else self.branch[:R], None if first else self.post[cur][:R],
-                           None if first else self.comb[cur][:R], lw.attn_hc.fn, lw.attn_hc.base, lw.attn_hc.scale,
-                           lw.in_norm, self.normed[:R], self.post[nxt][:R], self.comb[nxt][:R], self.part[:R],
-                           c.eps, c.hc_eps, c.hc_iters)
+            if first:
+                Kc.hc_post_pre(X, None, None, None, lw.attn_hc.fn, lw.attn_hc.base, lw.attn_hc.scale, lw.in_norm,
+                               self.normed[:R], self.post[nxt][:R], self.comb[nxt][:R], self.part[:R], c.eps,
+                               c.hc_eps, c.hc_iters)
+            else:
+                self._post_pre(X, R, cur, nxt, lw.attn_hc, lw.in_norm)
             cur = nxt
             first = False
             if lw.kind == "kda":
                 self._kda(lw, R)
             else:
                 self._mla(lw, R)
-            self.allreduce(self.branch[:R])
             nxt = 1 - cur
-            Kc.hc_post_pre(X, self.branch[:R], self.post[cur][:R], self.comb[cur][:R], lw.ffn_hc.fn,
-                           lw.ffn_hc.base, lw.ffn_hc.scale, lw.post_norm, self.normed[:R], self.post[nxt][:R],
-                           self.comb[nxt][:R], self.part[:R], c.eps, c.hc_eps, c.hc_iters)
+            self._post_pre(X, R, cur, nxt, lw.ffn_hc, lw.post_norm)
             cur = nxt
             if lw.mlp is not None:
                 self._mlp(lw, R)
             else:
                 self._moe(lw, R)
-            self.allreduce(self.branch[:R])
-        Kc.hc_post_pre(X, self.branch[:R], self.post[cur][:R], self.comb[cur][:R], None, None, None, None, None,
-                       None, None, self.part[:R], c.eps, c.hc_eps, c.hc_iters)
+        self._post_pre(X, R, cur, None, None, None)
         Kc.stream_mean_norm(X, self.w.norm, c.eps, self.hidden[:R], self.fnormed[:R])
         if not logits:
             return None
@@ -313,6 +319,34 @@ class Runtime:
         torch.index_select(self.fnormed[:R], 0, b.logit_rows[:n], out=self.lrows[:n])
         K.linear8(self.lrows[:n], self.w.head.w, self.w.head.s, self.logits[:n], K.GEMV_F32)
         return self.logits[:n]
+
+    def _post_pre(self, X, R, cur, nxt, hc, norm_w):
+        """mHC post of the block just computed (reducing the tensor-parallel partials) fused with the next pre
+        (hc None: post only)."""
+        c = self.cfg
+        Kc = K.C()
+        pre = (hc.fn, hc.base, hc.scale, norm_w, self.normed[:R], self.post[nxt][:R], self.comb[nxt][:R]) \
+            if hc is not None else (None,) * 7
+        if self._fused:
+            px, p = self.px, self._point % 2
+            Kc.hc_post_pre_tp(X, px.gath[p], px.slot, px.world, px.flags[p], px.epoch[p:p + 1],
+                              px.done_cons[p:p + 1], px.err, self.post[cur][:R], self.comb[cur][:R], *pre,
+                              self.part[:R], c.eps, c.hc_eps, c.hc_iters)
+        else:
+            self.allreduce(self.branch[:R])
+            Kc.hc_post_pre(X, self.branch[:R], self.post[cur][:R], self.comb[cur][:R], *pre, self.part[:R], c.eps,
+                           c.hc_eps, c.hc_iters)
+        self._point += 1
+
+    def _final_linear(self, x, lin, R, mode=K.GEMV_F32):
+        """The row-parallel projection that ends a block: writes the block's fp32 partial into ``branch``; in the
+        fused tensor-parallel mode it also pushes it into every rank's receive slot."""
+        if self._fused:
+            px, p = self.px, self._point % 2
+            K.C().gemv_push(x, lin.w, lin.s, self.branch[:R], mode, px.push_ptrs[p], px.push_flags[p],
+                            px.done_prod[p:p + 1], px.slot, px.rank, px.world, px.err)
+        else:
+            K.linear8(x, lin.w, lin.s, self.branch[:R], mode)
 
     # ---- blocks ------------------------------------------------------------------------------------------------
     def _kda(self, lw, R):
@@ -339,7 +373,7 @@ class Runtime:
             Kc.kda_chunk(proj, seq, fb, qkv, k.a_log, k.dt_bias, self.S_pool[li], self.ko[:R], H, Dh,
                          C3 + 2 * Dh, c.lower)
         Kc.kda_gated_norm(self.ko[:R], self.kg[:R], k.o_norm, self.kout[:R], H, Dh, c.eps)
-        K.linear8(self.kout[:R], k.o_proj.w, k.o_proj.s, self.branch[:R], K.GEMV_F32)
+        self._final_linear(self.kout[:R], k.o_proj, R)
 
     def _mla(self, lw, R):
         c, a, b = self.cfg, lw.mla, self.batch
@@ -382,14 +416,14 @@ class Runtime:
             r1 = min(R, r0 + K.GEMV_MAX_M)
             Kc.gemv(self.o_lat[r0:r1].transpose(0, 1), a.w_uv.w, a.w_uv.s, ob[r0:r1].transpose(0, 1),
                     K.GEMV_BF16, 0.0)
-        K.linear8(self.obuf[:R], a.o_proj.w, a.o_proj.s, self.branch[:R], K.GEMV_F32)
+        self._final_linear(self.obuf[:R], a.o_proj, R)
 
     def _mlp(self, lw, R):
         m = lw.mlp
         gu = self.gu_il[lw.index]
         act = self.act[:R, :m.width]
         K.linear8(self.normed[:R], gu.w, gu.s, act, K.GEMV_SWIGLU, self.cfg.limit)
-        K.linear8(act, m.down.w, m.down.s, self.branch[:R], K.GEMV_F32)
+        self._final_linear(act, m.down, R)
 
     def _moe_prefill(self, lw, R):
         """Routed experts of a prefill chunk: scalable routing, rotated inputs, tcgen05 gate/up and down with the
@@ -448,7 +482,7 @@ class Runtime:
         gu = self.gu_il[lw.index]
         act = self.act[:R, :s.width]
         K.linear8(self.normed[:R], gu.w, gu.s, act, K.GEMV_SWIGLU, c.limit)
-        K.linear8(act, s.down.w, s.down.s, self.branch[:R], K.GEMV_F32_ACC)
+        self._final_linear(act, s.down, R, K.GEMV_F32_ACC)
 
     # ------------------------------------------------------------------------------------------------------------
     # commit of a verify window

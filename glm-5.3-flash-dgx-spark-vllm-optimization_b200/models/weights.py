@@ -465,6 +465,15 @@ def prepare(src: TensorSource, cfg: ModelConfig, *, rank: int = 0, world: int = 
     def lin(t):
         return quantize_fp8_rows(t.to(dev))
 
+    def lin_rowpar(t):
+        """Row-parallel projection: quantise the whole weight (per-row scales over all inputs), then take this
+        rank's input columns, so every tensor-parallel degree holds slices of the same fp8 weights and the rank
+        partials add up to the unsharded result."""
+        q = quantize_fp8_rows(t.to(dev))
+        if world == 1:
+            return q
+        return Linear8(_rows(q.w, rank, world, 1).contiguous(), q.s)
+
     def f32(t):
         return t.float().to(dev).contiguous()
 
@@ -485,7 +494,7 @@ def prepare(src: TensorSource, cfg: ModelConfig, *, rank: int = 0, world: int = 
         return KDAW(in_proj, lin(_rows(g(a + "f_b_proj.weight"), rank, world)),
                     lin(_rows(g(a + "g_b_proj.weight"), rank, world)), f32(conv),
                     f32(_rows(g(a + "A_log"), rank, world)), f32(_rows(g(a + "dt_bias"), rank, world)),
-                    bf(g(a + "o_norm.weight")), lin(_rows(g(a + "o_proj.weight"), rank, world, 1)), Hl)
+                    bf(g(a + "o_norm.weight")), lin_rowpar(g(a + "o_proj.weight")), Hl)
 
     def mla(i):
         a = f"{P}layers.{i}.self_attn."
@@ -502,13 +511,12 @@ def prepare(src: TensorSource, cfg: ModelConfig, *, rank: int = 0, world: int = 
                        f32(g(ix + "k_norm.bias")), f32(g(ix + "index_kpool_compress_ape")))
         return MLAW(qkv_a, bf(g(a + "q_a_layernorm.weight")), bf(g(a + "kv_a_layernorm.weight")),
                     lin(_rows(g(a + "q_b_proj.weight"), rank, world)), w_uk_t, w_uv,
-                    lin(_rows(g(a + "o_proj.weight"), rank, world, 1)), index, Hl)
+                    lin_rowpar(g(a + "o_proj.weight")), index, Hl)
 
     def mlp(prefix, width):
         gate = _rows(g(prefix + "gate_proj.weight"), rank, world).to(dev)
         up = _rows(g(prefix + "up_proj.weight"), rank, world).to(dev)
-        down = _rows(g(prefix + "down_proj.weight"), rank, world, 1).to(dev)
-        return MLPW(lin(torch.cat([gate, up], 0)), lin(down), width // world)
+        return MLPW(lin(torch.cat([gate, up], 0)), lin_rowpar(g(prefix + "down_proj.weight")), width // world)
 
     def experts(i, proj):
         st = src.experts(i, proj, c.experts)

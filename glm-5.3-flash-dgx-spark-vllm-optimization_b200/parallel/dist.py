@@ -44,8 +44,10 @@ def init(backend: str | None = None, timeout_s: float = 120.0):
 class NcclComm:
     """Baseline collectives over the default process group."""
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, fused: bool | None = None):
         self.group = group
+        # decode windows reduce the tensor-parallel partials inside the kernels (parallel/fused.py) unless disabled
+        self.fused = (os.environ.get("GLM53_FUSED_TP", "1") == "1") if fused is None else fused
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
 
