@@ -1,0 +1,243 @@
+"""Kernel microbenchmarks (one GPU): each case builds random inputs of the full model's shapes, times the kernel with
+CUDA events after warm-up (an L2 flush -- a 256 MB write -- between timed iterations) and prints one JSON line with
+the time and the achieved rate against the measured peaks (MEASURED_PEAKS.json when present).
+
+  python -m glm53.utils.kernel_bench moe --tokens 1 8 64 512 8192 [--tp 1]      (BASELINE configs[1])
+  python -m glm53.utils.kernel_bench gemv|gemm|kda|mla|all
+  --iters 1 --warmup 1 makes a case small enough to capture under ncu
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0)
+    return 6650.0, 1590.0
+
+
+class Timer:
+    def __init__(self, warmup: int, iters: int, flush: bool = True):
+        self.warmup, self.iters = warmup, iters
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda") if flush else None
+
+    def __call__(self, fn) -> float:
+        for _ in range(self.warmup):
+            fn()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(self.iters):
+            if self.flush is not None:
+                self.flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            tot += e0.elapsed_time(e1)
+        return tot / self.iters
+
+
+def emit(d):
+    print(json.dumps(d), flush=True)
+
+
+def bench_moe(args, T: Timer):
+    """One MoE layer: routing + routed EXL3 experts (+ combine), hidden 4096, 288 experts of width 2048/tp."""
+    import glm53
+    from glm53.models.runtime import Runtime, RuntimeConfig
+    from glm53.models.weights import MoEW, MLPW, LayerW, HCW, Weights, quantize_fp8_rows
+    from glm53.ops import exl3
+    cfg = glm53.full_config(4)
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    D, W, E = cfg.hidden, cfg.moe_width // args.tp, cfg.experts
+    from glm53.models.weights import Exl3Stack
+    gate = Exl3Stack(*exl3.random_linear(D, W, generator=g, device=dev, lead=(E,)))
+    up = Exl3Stack(*exl3.random_linear(D, W, generator=g, device=dev, lead=(E,)))
+    down = Exl3Stack(*exl3.random_linear(W, D, generator=g, device=dev, lead=(E,)))
+    router = (torch.randn(E, D, generator=g, device=dev) / math.sqrt(D)).to(torch.bfloat16)
+    shared = MLPW(quantize_fp8_rows(torch.randn(2 * W, D, device=dev) / 64), quantize_fp8_rows(
+        torch.randn(D, W, device=dev) / 45), W)
+    moe = MoEW(router, torch.zeros(E, device=dev), gate, up, down, shared)
+    hbm, _ = peaks()
+    for n in args.tokens:
+        rc = RuntimeConfig(max_rows=max(n, 16), kv_slots=64, block_size=64, max_blocks=1, moe_chunk=256,
+                           moe_prefill_rows=8192)
+        lw = LayerW(3, "mla", "moe", None, None, None, None, moe=moe)
+        w = Weights(cfg, torch.zeros(16, D, dtype=torch.bfloat16, device=dev), [lw],
+                    torch.ones(D, dtype=torch.bfloat16, device=dev), quantize_fp8_rows(torch.randn(16, D, device=dev)))
+        rt = Runtime.__new__(Runtime)
+        _moe_only_runtime(rt, w, rc, dev)
+        rt.normed[:n].copy_(torch.randn(n, D, generator=g, device=dev).to(torch.bfloat16))
+        ms = T(lambda: rt._moe(lw, n))
+        # bytes: trellis of the distinct experts touched (4 bits/weight) + the shared expert
+        distinct = int(min(E, E * (1 - (1 - 1 / E) ** (n * cfg.top_k))))
+        wbytes = distinct * 3 * D * W // 2 + 3 * D * W
+        emit({"case": "moe_layer", "tokens": n, "tp": args.tp, "ms": ms, "distinct_experts_est": distinct,
+              "weight_GBps": wbytes / ms / 1e6, "frac_of_hbm": wbytes / ms / 1e6 / hbm,
+              "path": "decode (in-register trellis, mma.sync)" if n <= 64 else "prefill (tcgen05, smem trellis)"})
+        del rt
+
+
+def _moe_only_runtime(rt, w, rc, dev):
+    """A Runtime holding only the MoE scratch (no attention / KDA caches)."""
+    import types
+    from glm53.models import runtime as RT
+    c = w.cfg
+    rt.w, rt.rc, rt.comm, rt.cfg, rt.device, rt.tp = w, rc, None, c, dev, 1
+    rt.px, rt._fused = None, False
+    R = rc.max_rows
+    D = c.hidden
+    rt.gu_il = {lw.index: RT.interleave_gate_up(lw.moe.shared.gu) for lw in w.layers}
+    rt.normed = torch.zeros(R, D, dtype=torch.bfloat16, device=dev)
+    rt.branch = torch.zeros(R, D, dtype=torch.float32, device=dev)
+    rt.act = torch.zeros(R, max(g.w.shape[0] // 2 for g in rt.gu_il.values()), dtype=torch.bfloat16, device=dev)
+    MR = min(R, rc.moe_chunk)
+    tk = c.top_k
+    P = MR * tk
+    rt.rlogits = torch.zeros(MR, c.experts, device=dev)
+    rt.topk_ids = torch.zeros(MR, tk, dtype=torch.int32, device=dev)
+    rt.topk_w = torch.zeros(MR, tk, device=dev)
+    rt.max_groups = min(P, c.experts)
+    rt.group_count = torch.zeros(1, dtype=torch.int32, device=dev)
+    rt.group_expert = torch.zeros(rt.max_groups, dtype=torch.int32, device=dev)
+    rt.group_offset = torch.zeros(rt.max_groups + 1, dtype=torch.int32, device=dev)
+    for n in ("pair_token", "pair_expert", "pair_of"):
+        setattr(rt, n, torch.zeros(P, dtype=torch.int32, device=dev))
+    rt.pair_w = torch.zeros(P, device=dev)
+    moe0 = w.layers[0].moe
+    rt.prefill_moe = R > RT.MOE_PREFILL_MIN_ROWS
+    if rt.prefill_moe:
+        PR = min(R, rc.moe_prefill_rows)
+        rt.p_rows = PR
+        PP = PR * tk
+        rt.p_logits = torch.zeros(PR, c.experts, device=dev)
+        rt.p_topk_ids = torch.zeros(PR, tk, dtype=torch.int32, device=dev)
+        rt.p_topk_w = torch.zeros(PR, tk, device=dev)
+        rt.p_group_expert = torch.zeros(c.experts, dtype=torch.int32, device=dev)
+        rt.p_group_offset = torch.zeros(c.experts + 1, dtype=torch.int32, device=dev)
+        for n in ("p_pair_token", "p_pair_expert", "p_pair_of"):
+            setattr(rt, n, torch.zeros(PP, dtype=torch.int32, device=dev))
+        rt.p_pair_w = torch.zeros(PP, device=dev)
+        rt.p_counts = torch.zeros(c.experts, dtype=torch.int32, device=dev)
+        rt.p_fill = torch.zeros(c.experts, dtype=torch.int32, device=dev)
+        P = max(P, PP)
+    rt.xh_g = torch.zeros(P, D, dtype=torch.float16, device=dev)
+    rt.xh_u = torch.zeros(P, D, dtype=torch.float16, device=dev)
+    rt.xd = torch.zeros(P, moe0.gate.n, dtype=torch.float16, device=dev)
+    rt.yd = torch.zeros(P, D, device=dev)
+
+
+def bench_gemv(args, T: Timer):
+    from glm53.models.weights import quantize_fp8_rows
+    from glm53.ops import kernels as K
+    hbm, _ = peaks()
+    for (N, Kd, name) in [(24896, 4096, "kda_in_proj"), (4096, 8192, "kda_o_proj"), (4096, 16384, "mla_o_proj"),
+                          (2048, 4096, "mla_qkv_a"), (154880, 4096, "lm_head"), (288, 4096, "router_bf16")]:
+        for M in args.rows:
+            x = torch.randn(M, Kd, device="cuda").to(torch.bfloat16)
+            y = torch.empty(M, N, device="cuda")
+            if name == "router_bf16":
+                w = (torch.randn(N, Kd, device="cuda") / 64).to(torch.bfloat16)
+                ms = T(lambda: K.C().gemv(x, w, None, y, K.GEMV_F32, 0.0))
+                nbytes = N * Kd * 2
+            else:
+                q = quantize_fp8_rows(torch.randn(N, Kd, device="cuda") / 64)
+                ms = T(lambda: K.C().gemv(x, q.w, q.s, y, K.GEMV_F32, 0.0))
+                nbytes = N * Kd
+            emit({"case": "gemv", "proj": name, "M": M, "N": N, "K": Kd, "ms": ms, "GBps": nbytes / ms / 1e6,
+                  "frac_of_hbm": nbytes / ms / 1e6 / hbm})
+
+
+def bench_gemm(args, T: Timer):
+    from glm53.models.weights import quantize_fp8_rows
+    from glm53.ops import kernels as K
+    _, tflops = peaks()
+    for (M, N, Kd) in [(8192, 24896, 4096), (8192, 4096, 8192), (8192, 24576, 4096), (4096, 4096, 4096)]:
+        x = torch.randn(M, Kd, device="cuda").to(torch.bfloat16)
+        q = quantize_fp8_rows(torch.randn(N, Kd, device="cuda") / 64)
+        y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        scratch = torch.empty(N * Kd, dtype=torch.bfloat16, device="cuda")
+        ms = T(lambda: K.C().gemm_w8a16(x, q.w, q.s, y, K.GEMV_BF16, 0.0, scratch))
+        wb = scratch[:N * Kd].view(N, Kd)
+        ms_bf = T(lambda: K.C().gemm_bf16(x, wb, q.s, y, K.GEMV_BF16, 0.0))
+        fl = 2.0 * M * N * Kd
+        emit({"case": "gemm_tcgen05", "M": M, "N": N, "K": Kd, "ms_w8a16": ms, "ms_bf16_only": ms_bf,
+              "tflops": fl / ms_bf / 1e9, "frac_of_bf16_peak": fl / ms_bf / 1e9 / tflops})
+
+
+def bench_kda(args, T: Timer):
+    from glm53.ops import kernels as K
+    H, Dh = 64 // args.tp, 128
+    for Tn in args.kda_rows:
+        HD = H * Dh
+        ldp = (3 * HD + 2 * Dh + H + 63) // 64 * 64
+        proj = (torch.randn(Tn, ldp, device="cuda") * 0.5).to(torch.bfloat16)
+        qkv = torch.randn(Tn, 3 * HD, device="cuda").to(torch.bfloat16)
+        f = torch.randn(Tn, HD, device="cuda").to(torch.bfloat16)
+        a_log = torch.zeros(H, device="cuda")
+        dt = torch.zeros(HD, device="cuda")
+        S = torch.zeros(2, H, Dh, Dh, device="cuda")
+        o = torch.empty(Tn, HD, device="cuda")
+        seq = torch.tensor([[0], [Tn], [0], [1], [0]], dtype=torch.int32, device="cuda")
+        fn = K.C().kda_chunk if Tn > 32 else K.C().kda_recurrent
+        ms = T(lambda: fn(proj, seq, f, qkv, a_log, dt, S, o, H, Dh, 3 * HD + 2 * Dh, -5.0))
+        emit({"case": "kda_chunk" if Tn > 32 else "kda_recurrent", "rows": Tn, "heads": H, "ms": ms,
+              "tokens_per_s": Tn / ms * 1e3})
+
+
+def bench_mla(args, T: Timer):
+    from glm53.ops import kernels as K
+    H, L = 64 // args.tp, 512
+    for R in args.mla_rows:
+        slots = 8192
+        q = torch.randn(R, H, L, device="cuda").to(torch.bfloat16)
+        kv = torch.randint(0, 120, (slots, L), dtype=torch.uint8, device="cuda")
+        sc = torch.rand(slots, device="cuda") * 0.01
+        sel = torch.randint(0, slots, (R, 2048), dtype=torch.int32, device="cuda")
+        cnt = torch.full((R,), 2048, dtype=torch.int32, device="cuda")
+        splits = 4 if R <= 16 else 1
+        po = torch.empty(R * splits * H * L, device="cuda")
+        pm = torch.empty(R * splits * H * 2, device="cuda")
+        o = torch.empty_like(q)
+        ms = T(lambda: K.C().mla_decode(q, None, 0, 0, kv, sc, None, sel, cnt, 0, 0.0625, splits, po, pm, o))
+        fl = 4.0 * R * H * 2048 * L
+        emit({"case": "mla_sparse_attn", "rows": R, "heads": H, "keys": 2048, "ms": ms, "tflops": fl / ms / 1e9})
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["moe", "gemv", "gemm", "kda", "mla", "all"])
+    ap.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 64, 512, 8192])
+    ap.add_argument("--rows", type=int, nargs="+", default=[8])
+    ap.add_argument("--kda-rows", type=int, nargs="+", default=[8, 8192])
+    ap.add_argument("--mla-rows", type=int, nargs="+", default=[8, 1024])
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--no-flush", action="store_true")
+    args = ap.parse_args(argv)
+    import sys
+    sys.path.insert(0, ROOT)
+    import glm53  # noqa: F401
+    T = Timer(args.warmup, args.iters, flush=not args.no_flush)
+    cases = ["moe", "gemv", "gemm", "kda", "mla"] if args.case == "all" else [args.case]
+    for c in cases:
+        globals()["bench_" + c](args, T)
+
+
+if __name__ == "__main__":
+    main()
