@@ -1,0 +1,175 @@
+"""Step-level profiles of the serving path on one GPU.
+
+  python -m glm53.utils.step_profile forward --rows 8        kernel breakdown of one decode window forward
+  python -m glm53.utils.step_profile prefill --chunk 4096    kernel breakdown of one prefill chunk (context = chunk)
+  python -m glm53.utils.step_profile engine --k 7            wall time of each phase of LLMEngine.step()
+
+``forward`` / ``prefill`` aggregate device time per kernel name with torch.profiler (CUDA activity only).
+``engine`` runs a speculative decode through the public engine API and times each backend call (with a
+synchronize before and after, so device and host time of a phase are attributed to it) next to the plain step time
+measured with no instrumentation.  Random-init weights; synthetic token ids.
+"""
+
+from __future__ import annotations
+
+import argparse
+import collections
+import json
+import time
+
+import torch
+
+
+def _kernel_table(fn, reps: int = 1, top: int = 30):
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for e in prof.events():
+        if e.device_type.name == "CUDA":
+            a = agg[e.name[:100]]
+            a[0] += 1
+            a[1] += e.device_time_total
+    rows = sorted(agg.items(), key=lambda kv: -kv[1][1])
+    total = sum(v[1] for v in agg.values()) / reps
+    return total, [(n, c // reps, t / reps) for n, (c, t) in rows[:top]]
+
+
+def _runtime(cfg, rows: int, ctx: int):
+    from ..models import weights as W
+    from ..models.runtime import Runtime, RuntimeConfig
+    from ..models.session import Sequence
+    dev = torch.device("cuda", 0)
+    w = W.prepare(W.RandomSource(cfg, seed=0, device=dev), cfg, device=dev)
+    bs = 64
+    blocks = (ctx + rows * 8 + bs - 1) // bs + 2
+    rc = RuntimeConfig(max_rows=max(rows, 16), max_seqs=1, kv_slots=blocks * bs, block_size=bs, max_blocks=blocks)
+    rt = Runtime(w, rc)
+    return rt, Sequence(rt)
+
+
+def cmd_forward(a):
+    from .. import full_config
+    from ..models.runtime import Graphed
+    cfg = full_config()
+    rt, seq = _runtime(cfg, max(a.chunk, a.rows), a.context + a.rows * 16)
+    g = torch.Generator().manual_seed(0)
+    seq.prefill(torch.randint(0, cfg.vocab, (a.context,), generator=g).tolist(), chunk=a.chunk)
+    R = a.rows
+
+    def step():
+        seq.stage([1] * R, list(range(R)))
+        seq._window = R
+        rt.forward(R, keep_window=True)
+        seq.commit(R)
+
+    for _ in range(3):
+        step()
+    total, rows = _kernel_table(step, reps=2)
+    graph = Graphed(lambda: rt.forward(R, keep_window=True))
+    seq.stage([1] * R, list(range(R)))
+    for _ in range(3):
+        graph()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        graph()
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"mode": "forward", "rows": R, "context": a.context, "kernel_sum_us": total,
+                      "graph_replay_us": e0.elapsed_time(e1) * 100.0}))
+    for n, c, t in rows:
+        print(f"{t:10.1f} us {c:6d}x  {n}")
+
+
+def cmd_prefill(a):
+    from .. import full_config
+    cfg = full_config()
+    CH = a.chunk
+    rt, seq = _runtime(cfg, CH, 3 * CH)
+    g = torch.Generator().manual_seed(0)
+    toks = torch.randint(0, cfg.vocab, (3 * CH,), generator=g).tolist()
+    seq.prefill(toks[:CH], chunk=CH)
+    total, rows = _kernel_table(lambda: seq.prefill(toks[CH:2 * CH], chunk=CH))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    seq.prefill(toks[2 * CH:], chunk=CH)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    print(json.dumps({"mode": "prefill", "chunk": CH, "kernel_sum_ms": total / 1e3, "timed_chunk_ms": ms,
+                      "tok_s": CH / (ms / 1e3)}))
+    for n, c, t in rows:
+        print(f"{t / 1e3:10.2f} ms {c:6d}x  {n}")
+
+
+def cmd_engine(a):
+    from ..api.offline import LLM, LLMOptions
+    from ..engine.llm import SamplingParams, State
+    K = a.k
+    llm = LLM(LLMOptions(model="full", max_seqs=1, max_model_len=a.context + (K + 1) * (2 * a.steps + 16) + 64,
+                         prefill_chunk=4096, speculative=True, k_fixed=K, force_accept=True, checkpoints=0))
+    eng = llm.engine
+    g = torch.Generator().manual_seed(0)
+    ctx = torch.randint(0, llm.cfg.vocab, (a.context,), generator=g).tolist()
+    eng.add_request(ctx, SamplingParams(max_tokens=(K + 1) * (2 * a.steps + 8), ignore_eos=True))
+    while not (eng.running and eng.running[0].state == State.RUNNING):
+        eng.step()
+    for _ in range(3):
+        eng.step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        eng.step()
+    torch.cuda.synchronize()
+    plain = (time.perf_counter() - t0) * 1e3 / a.steps
+
+    acc = collections.defaultdict(float)
+
+    def wrap(obj, name, label):
+        f = getattr(obj, name)
+
+        def timed(*args, **kw):
+            torch.cuda.synchronize()
+            s = time.perf_counter()
+            out = f(*args, **kw)
+            torch.cuda.synchronize()
+            acc[label] += time.perf_counter() - s
+            return out
+        setattr(obj, name, timed)
+
+    b = eng.b
+    for name in ("verify", "argmax", "commit", "draft", "hidden"):
+        wrap(b, name, "backend." + name)
+    wrap(eng.kv, "commit_tokens", "kv.commit_tokens")
+    wrap(eng, "_emit", "engine._emit")
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        eng.step()
+    torch.cuda.synchronize()
+    inst = (time.perf_counter() - t0) * 1e3 / a.steps
+    phases = {k: v * 1e3 / a.steps for k, v in sorted(acc.items(), key=lambda kv: -kv[1])}
+    print(json.dumps({"mode": "engine", "k": K, "context": a.context, "plain_step_ms": plain,
+                      "instrumented_step_ms": inst, "phases_ms": phases,
+                      "unattributed_ms": inst - sum(phases.values())}))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("mode", choices=["forward", "prefill", "engine"])
+    ap.add_argument("--rows", type=int, default=8)
+    ap.add_argument("--chunk", type=int, default=4096)
+    ap.add_argument("--context", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=7)
+    ap.add_argument("--steps", type=int, default=20)
+    a = ap.parse_args()
+    {"forward": cmd_forward, "prefill": cmd_prefill, "engine": cmd_engine}[a.mode](a)
+
+
+if __name__ == "__main__":
+    main()
