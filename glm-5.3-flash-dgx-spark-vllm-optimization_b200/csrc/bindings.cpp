@@ -215,8 +215,12 @@ Exl3Args exl3_args(const Tensor& x, const Tensor& tr_g, const Tensor& suh_g, con
   a.pairs = (int)pair_token.size(0);
   a.limit = (float)limit;
   a.xh_g = P<__half>(xh_g); a.xh_u = P<__half>(xh_u); a.xd = P<__half>(xd); a.yd = P<float>(yd);
+  a.decode_layout = 1;
   TORCH_CHECK(tr_g.scalar_type() == at::kShort && tr_d.scalar_type() == at::kShort, "trellis must be int16");
-  TORCH_CHECK(xh_g.size(0) >= a.pairs && xd.size(0) >= a.pairs && yd.size(0) >= a.pairs, "scratch rows");
+  // decode layout: rotated inputs are duplicated f16 pairs, 2K (2N) halves per pair
+  TORCH_CHECK(xh_g.numel() >= (int64_t)a.pairs * 2 * a.K && xh_u.numel() >= (int64_t)a.pairs * 2 * a.K &&
+                  xd.numel() >= (int64_t)a.pairs * 2 * a.N && yd.size(0) >= a.pairs,
+              "exl3_moe scratch too small (xh: pairs x 2K halves, xd: pairs x 2N halves)");
   return a;
 }
 

@@ -72,8 +72,9 @@ __device__ __forceinline__ uint32_t f32x2_to_f16x2(float lo, float hi) {
 }
 
 // mma.sync m16n8k16, f16 inputs, fp32 accumulate: D = A*B + D
+// (no `volatile` on the pure tensor-core / read-only load asm below: the scheduler may reorder and overlap them)
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -81,7 +82,7 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)
 }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -90,14 +91,14 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
 
 __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
   return r;
 }
 
 __device__ __forceinline__ uint32_t ldg_nc_u32(const void* p) {
   uint32_t r;
-  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
   return r;
 }
 
@@ -142,6 +143,33 @@ __device__ __forceinline__ void fwht128_warp(float (&v)[4]) {
   const float s = 0.08838834764831845f;   // 1/sqrt(128)
 #pragma unroll
   for (int i = 0; i < 4; ++i) v[i] *= s;
+}
+
+// exclusive scan of an int over the block (blockDim multiple of 32, <= 1024); returns (prefix, total)
+__device__ __forceinline__ int2 block_scan(int v, int* wsum) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  __syncthreads();
+  if (lane == 31) wsum[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    int t = lane < nw ? wsum[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, t, o);
+      if (lane >= o) t += y;
+    }
+    if (lane < nw) wsum[lane] = t;   // inclusive warp-total prefix
+  }
+  __syncthreads();
+  const int before = wid > 0 ? wsum[wid - 1] : 0;
+  const int total = wsum[nw - 1];
+  return make_int2(before + x - v, total);
 }
 
 }  // namespace g53

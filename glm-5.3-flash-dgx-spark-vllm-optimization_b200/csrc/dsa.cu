@@ -138,33 +138,6 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-// exclusive scan of an int over the block (blockDim multiple of 32, <= 1024); returns (prefix, total)
-__device__ __forceinline__ int2 block_scan(int v, int* wsum) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  int x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  __syncthreads();
-  if (lane == 31) wsum[wid] = x;
-  __syncthreads();
-  if (wid == 0) {
-    int t = lane < nw ? wsum[lane] : 0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, t, o);
-      if (lane >= o) t += y;
-    }
-    if (lane < nw) wsum[lane] = t;   // inclusive warp-total prefix
-  }
-  __syncthreads();
-  const int before = wid > 0 ? wsum[wid - 1] : 0;
-  const int total = wsum[nw - 1];
-  return make_int2(before + x - v, total);
-}
-
 __global__ void __launch_bounds__(1024) dsa_select_kernel(DsaArgs a) {
   const int r = blockIdx.x;
   const int tid = threadIdx.x, bd = blockDim.x;

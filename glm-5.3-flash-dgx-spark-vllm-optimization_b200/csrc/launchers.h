@@ -84,6 +84,7 @@ struct Exl3Args {
   __half* xh_g; __half* xh_u;   // [pairs, K] rotated inputs
   __half* xd;                   // [pairs, N] rotated down input
   float* yd;                    // [pairs, Dout] weighted expert outputs
+  int decode_layout;            // 1: xh/xd rows in the decode fragment layout (moe.cu perm_k); 0: natural order
 };
 cudaError_t g53_exl3_rot_in(const Exl3Args& a, cudaStream_t st);
 cudaError_t g53_exl3_gate_up(const Exl3Args& a, cudaStream_t st);

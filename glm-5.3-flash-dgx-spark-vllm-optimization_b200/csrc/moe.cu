@@ -3,16 +3,20 @@
 // EXL3 path (the trellis format is described in ops/exl3.py):
 //   rot_in    xh[p] = f16(H128(x[token(p)] * suh[expert(p)]))                 (gate and up, per sorted pair)
 //   gate_up   per (expert group, 128-column block): Z = xh @ W_q on tensor cores, the trellis decoded in
-//             registers straight into mma.m16n8k16 B fragments (each lane decodes the 8 values of its fragment
-//             from its own 32-bit word and its left neighbour's); epilogue in shared memory: H128 of the gate and
+//             registers straight into mma.m16n8k16 fragments (each lane decodes the 8 values of its fragment
+//             from its own 32-bit word and its left neighbour's); the weight tile is the A operand (16 features)
+//             and up to 8 tokens are the B operand; epilogue in shared memory: H128 of the gate and
 //             up rows, * svh, SwiGLU with clamp, * suh of the down projection, H128 -> f16 down input
 //   down      same GEMM over the local expert width; epilogue H128, * svh, * routing weight -> fp32 per pair
 //   combine   out[r] = sum over slots (fixed order) of the pair outputs
 // One CTA owns one full 128-column Hadamard block of one expert, so both output rotations stay on chip.
 // Reference counterparts: code/fork/kernels/exl3.cu:110 (grouped_kernel), :322 (rot_in), :371/:455 (epilogues),
 // :529/:582 (route_prep / route_ids).
+#include <cooperative_groups.h>
 #include "common.cuh"
 #include "launchers.h"
+
+namespace cg = cooperative_groups;
 
 namespace g53 {
 
@@ -59,7 +63,6 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(RouteArgs a) {
   __shared__ int cnt[kMaxE];
   __shared__ int start[kMaxE + 1];
   __shared__ int pe[kMaxPairs];
-  __shared__ float red[32];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
   const int P = a.R * a.top_k;
   for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
@@ -109,23 +112,20 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(RouteArgs a) {
     }
   }
   __syncthreads();
-  // exclusive scan of counts (serial per warp chunk; E <= 1024)
-  if (tid == 0) {
-    int s = 0, u = 0;
-    for (int e = 0; e < a.E; ++e) {
-      start[e] = s;
-      if (cnt[e] > 0) {
-        if (u < a.max_groups) { a.group_expert[u] = e; a.group_offset[u] = s; }
-        ++u;
-      }
-      s += cnt[e];
+  // exclusive scans of the counts and of the non-empty flags (packed: count in bits 0-15, flag in bits 16-31)
+  {
+    __shared__ int wsum[32];
+    const int c = tid < a.E ? cnt[tid] : 0;
+    const int2 sc = block_scan(c | ((c > 0) << 16), wsum);
+    const int s = sc.x & 0xffff, u = sc.x >> 16, total = sc.y & 0xffff, groups = sc.y >> 16;
+    if (tid < a.E) {
+      start[tid] = s;
+      if (c > 0 && u < a.max_groups) { a.group_expert[u] = tid; a.group_offset[u] = s; }
     }
-    start[a.E] = s;
-    a.group_count[0] = u;
-    for (int v = u; v <= a.max_groups; ++v) a.group_offset[v] = s;
+    if (tid == 0) { start[a.E] = total; a.group_count[0] = groups; }
+    for (int v = groups + tid; v <= a.max_groups; v += blockDim.x) a.group_offset[v] = total;
   }
   __syncthreads();
-  (void)red;
   // stable placement: rank of pair i among earlier pairs of the same expert
   for (int i = tid; i < P; i += blockDim.x) {
     const int e = pe[i];
@@ -137,6 +137,67 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(RouteArgs a) {
     a.pair_expert[pos] = e;
     a.pair_w[pos] = a.topk_w[i];
   }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Decode-path trellis evaluation with split codebook halves.
+//
+// A codebook value is fp16(lo) + fp16(hi) of the masked product x = (s * 0xCBAC1FED & 0x8FFF8FFF) ^ 0x3B603B60.
+// The decode kernels never add the halves on the CUDA cores: the 32-bit x is itself an f16x2 register holding
+// (lo, hi), and it enters the tensor core as two consecutive k entries of the A operand, against the same input
+// value duplicated in the B operand, so the MMA forms lo*x_k + hi*x_k in fp32.  Against the format's single fp16
+// rounding of lo + hi this differs by at most half an fp16 ulp of the weight (the same order as the fp16 rounding
+// of the rotated inputs) and it saves the packing and the fp16 add of every value: per state the CUDA cores do
+// the window extraction, one IMAD and one LOP3.
+//
+// Per 16x16 tile, lane (g, q) holds states j = 0..7 at (k, n) = (2q + (j&1) + 8((j>>1)&1), g + 8(j>>2)).  The
+// tile becomes two m16n8k16 steps with the weight as A (16 features x 16 virtual k) and 8 tokens as B; virtual k
+// slots (q, q+4) of step t carry original k (2q + 8t, 2q + 1 + 8t):
+//   step 0: A = {x0, x4, x1, x5}, B = {dup(in[2q]),     dup(in[2q+1])}
+//   step 1: A = {x2, x6, x3, x7}, B = {dup(in[2q+8]),   dup(in[2q+9])}
+// The rotated inputs (xh_g, xh_u, xd) of the decode path are stored as duplicated f16 pairs, one 32-bit word per
+// element, ordered so that lane quad q finds the 4 words of each k-tile together and the 4 k-tiles of a 64-wide
+// chunk next to each other: word(k) below.  A row of K elements takes 2K halves.
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ int dup_word(int k) {
+  const int w = k & 63, t = w >> 4, kk = w & 15;
+  const int q = (kk & 7) >> 1, i = (kk & 1) | ((kk >> 3) << 1);
+  return (k & ~63) | (q << 4) | (t << 2) | i;
+}
+
+__device__ __forceinline__ uint32_t dup_half(float v) {
+  const __half h = __float2half_rn(v);
+  const uint32_t b = __half_as_ushort(h);
+  return b | (b << 16);
+}
+
+// the 8 masked products of lane's fragment.  The window extraction is spread over the ALU and FMA pipes (the
+// decode is bound by the ALU pipe): right shifts of whole words use the high half of an integer multiply, and the
+// lowest window uses s7 * C = cur * C - s3 * (C << 16) (mod 2^32) instead of masking cur.
+__device__ __forceinline__ void trellis_x8(uint32_t cur, uint32_t prev, uint32_t (&x)[8]) {
+  constexpr uint32_t C = 0xCBAC1FEDu, Cn = 0u - (C << 16);
+  const uint32_t v = __funnelshift_r(cur, prev, 20);     // bits [20, 52) of (prev:cur)
+  const uint32_t y = __umulhi(cur, 1u << 28);            // cur >> 4
+  const uint32_t s3 = __umulhi(cur, 1u << 16);           // cur >> 16
+  uint32_t s[7];
+  s[0] = __byte_perm(v, 0u, 0x4421);                     // bits [28, 44)
+  s[1] = __funnelshift_r(cur, prev, 24) & 0xffffu;       // bits [24, 40)
+  s[2] = v & 0xffffu;                                    // bits [20, 36)
+  s[3] = s3;
+  s[4] = __byte_perm(y, 0u, 0x4421);                     // bits [12, 28)
+  s[5] = __byte_perm(cur, 0u, 0x4421);                   // bits [8, 24)
+  s[6] = y & 0xffffu;                                    // bits [4, 20)
+#pragma unroll
+  for (int j = 0; j < 7; ++j) x[j] = ((s[j] * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;
+  x[7] = ((cur * C + s3 * Cn) & 0x8FFF8FFFu) ^ 0x3B603B60u;   // bits [0, 16)
+}
+
+// one 16x16 trellis tile (two k16 steps) against 8 tokens' duplicated inputs b = {w0, w1, w2, w3}
+__device__ __forceinline__ void tile_mma(float (&c)[4], const uint32_t (&x)[8], const uint4& b) {
+  const uint32_t a0[4] = {x[0], x[4], x[1], x[5]};
+  const uint32_t a1[4] = {x[2], x[6], x[3], x[7]};
+  mma_f16_16816(c, a0, b.x, b.y);
+  mma_f16_16816(c, a1, b.z, b.w);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -160,43 +221,68 @@ __global__ void __launch_bounds__(128) exl3_rot_in_kernel(Exl3Args a) {
   for (int i = 0; i < 4; ++i) { g[i] = xv[i] * __half2float(sg[i]); u[i] = xv[i] * __half2float(su[i]); }
   fwht128_warp(g);
   fwht128_warp(u);
+  if (a.decode_layout) {                         // duplicated words (see dup_word); (k, k+1) are adjacent words
+    uint32_t* og = reinterpret_cast<uint32_t*>(a.xh_g) + (int64_t)p * a.K;
+    uint32_t* ou = reinterpret_cast<uint32_t*>(a.xh_u) + (int64_t)p * a.K;
+    const int w0 = dup_word(c0), w2 = dup_word(c0 + 2);
+    *reinterpret_cast<uint2*>(og + w0) = make_uint2(dup_half(g[0]), dup_half(g[1]));
+    *reinterpret_cast<uint2*>(og + w2) = make_uint2(dup_half(g[2]), dup_half(g[3]));
+    *reinterpret_cast<uint2*>(ou + w0) = make_uint2(dup_half(u[0]), dup_half(u[1]));
+    *reinterpret_cast<uint2*>(ou + w2) = make_uint2(dup_half(u[2]), dup_half(u[3]));
+    return;
+  }
   __half2* og = reinterpret_cast<__half2*>(a.xh_g + (int64_t)p * a.K + c0);
   __half2* ou = reinterpret_cast<__half2*>(a.xh_u + (int64_t)p * a.K + c0);
   og[0] = __floats2half2_rn(g[0], g[1]); og[1] = __floats2half2_rn(g[2], g[3]);
   ou[0] = __floats2half2_rn(u[0], u[1]); ou[1] = __floats2half2_rn(u[2], u[3]);
 }
 
-// A fragment (16 rows x 16 k, f16) of rotated inputs rows [row0, row0+16) at k-tile kt; rows >= nrows are zero
-__device__ __forceinline__ void load_a_frag(const __half* xh, int64_t ld, int row0, int nrows, int kt,
-                                            uint32_t (&a)[4]) {
+// accumulator (16 features x 8 tokens) of one warp's n-tile -> z[token][feature]
+__device__ __forceinline__ void acc_to_smem(const float (&c)[4], int warp, float (*z)[132]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-  const int k = kt * 16 + 2 * q;
-  if (g < nrows) {
-    const __half* r = xh + (int64_t)(row0 + g) * ld + k;
-    a[0] = *reinterpret_cast<const uint32_t*>(r);
-    a[2] = *reinterpret_cast<const uint32_t*>(r + 8);
-  } else {
-    a[0] = a[2] = 0u;
-  }
-  if (g + 8 < nrows) {
-    const __half* r = xh + (int64_t)(row0 + g + 8) * ld + k;
-    a[1] = *reinterpret_cast<const uint32_t*>(r);
-    a[3] = *reinterpret_cast<const uint32_t*>(r + 8);
-  } else {
-    a[1] = a[3] = 0u;
+  const int t = 2 * q, f = warp * 16 + g;
+  z[t][f] = c[0];
+  z[t + 1][f] = c[1];
+  z[t][f + 8] = c[2];
+  z[t + 1][f + 8] = c[3];
+}
+
+// split-K over a cluster along z: rank 0 adds the other ranks' partial tiles (fixed rank order) to its own
+template <int KSPL>
+__device__ __forceinline__ void cluster_reduce_tile(float (*z)[132], int nrows) {
+  if constexpr (KSPL > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (cluster.block_rank() == 0) {
+      for (int i = threadIdx.x; i < 8 * 128; i += blockDim.x) {
+        const int t = i >> 7, f = i & 127;
+        if (t >= nrows) continue;
+        float v = z[t][f];
+#pragma unroll
+        for (int r = 1; r < KSPL; ++r) v += cluster.map_shared_rank(&z[0][0], r)[t * 132 + f];
+        z[t][f] = v;
+      }
+    }
   }
 }
 
-// ---------------------------------------------------------------------------------------------------------------
-// gate + up: grid (N/128 column blocks, max_groups), 8 warps; warp w owns n-tile (block*8 + w)
-// ---------------------------------------------------------------------------------------------------------------
-constexpr int kPf = 4;   // k-tiles of trellis words prefetched per warp
+template <int KSPL>
+__device__ __forceinline__ void cluster_release() {
+  if constexpr (KSPL > 1) cg::this_cluster().sync();   // rank 0 has read every rank's tile
+}
 
-__global__ void __launch_bounds__(256) exl3_gate_up_kernel(Exl3Args a) {
+// ---------------------------------------------------------------------------------------------------------------
+// gate + up: grid (N/128 column blocks, max_groups, KSPL), 8 warps; warp w owns n-tile (block*8 + w) of gate and
+// up; the KSPL CTAs of a cluster split K and rank 0 reduces and runs the epilogue.
+// Up to 8 tokens of the group per pass (one n8 block; a decode window of R <= 8 rows never has more per expert);
+// larger groups decode the trellis again for every further 8 tokens.
+// ---------------------------------------------------------------------------------------------------------------
+template <int KSPL>
+__global__ void __launch_bounds__(256, 4) exl3_gate_up_kernel(Exl3Args a) {
   const int u = blockIdx.y;
   if (u >= a.group_count[0] || u >= a.max_groups) return;
-  __shared__ float zg[16][132];
-  __shared__ float zu[16][132];
+  __shared__ float zg[8][132];
+  __shared__ float zu[8][132];
   const int e = a.group_expert[u];
   const int p0 = a.group_offset[u];
   const int np = a.group_offset[u + 1] - p0;
@@ -204,49 +290,52 @@ __global__ void __launch_bounds__(256) exl3_gate_up_kernel(Exl3Args a) {
   const int nb = blockIdx.x;
   const int nt = nb * 8 + warp;
   const int KT = a.K / 16, NT = a.N / 16;
+  const int ks = KSPL > 1 ? (int)blockIdx.z : 0, cper = a.K / 64 / KSPL, c_lo = ks * cper, c_hi = c_lo + cper;
   const uint32_t* wg = reinterpret_cast<const uint32_t*>(a.tr_g) + ((int64_t)e * KT * NT + nt) * 32 + lane;
   const uint32_t* wu = reinterpret_cast<const uint32_t*>(a.tr_u) + ((int64_t)e * KT * NT + nt) * 32 + lane;
   const int64_t kstride = (int64_t)NT * 32;
   const int src = (lane + 31) & 31;
 
-  for (int m0 = 0; m0 < np; m0 += 16) {
-    const int nrows = min(16, np - m0);
-    float ag[2][4] = {}, au[2][4] = {};
-    uint32_t pg[kPf], pu[kPf];
+  for (int m0 = 0; m0 < np; m0 += 8) {
+    const int nrows = min(8, np - m0);
+    // token columns past the group read the group's first row: their MMA columns are never stored
+    const int64_t r0 = (int64_t)(p0 + m0 + (g < nrows ? g : 0)) * 2 * a.K + q * 32;
+    float cg[4] = {}, cu[4] = {};
+    uint32_t pg[4], pu[4];
 #pragma unroll
-    for (int i = 0; i < kPf; ++i) {
-      pg[i] = i < KT ? ldg_nc_u32(wg + i * kstride) : 0u;
-      pu[i] = i < KT ? ldg_nc_u32(wu + i * kstride) : 0u;
+    for (int i = 0; i < 4; ++i) {
+      pg[i] = ldg_nc_u32(wg + (4 * c_lo + i) * kstride);
+      pu[i] = ldg_nc_u32(wu + (4 * c_lo + i) * kstride);
     }
-    for (int kt0 = 0; kt0 < KT; kt0 += kPf) {
+    for (int c = c_lo; c < c_hi; ++c) {
+      uint32_t ng[4], nu[4];
+      const int64_t noff = (c + 1 < c_hi ? 4 * c + 4 : 4 * c) * kstride;   // the last chunk reloads itself
 #pragma unroll
-      for (int i = 0; i < kPf; ++i) {
-        const int kt = kt0 + i;
-        if (kt >= KT) break;
-        const uint32_t cg = pg[i], cu = pu[i];
-        const int nk = kt + kPf;
-        pg[i] = nk < KT ? ldg_nc_u32(wg + nk * kstride) : 0u;
-        pu[i] = nk < KT ? ldg_nc_u32(wu + nk * kstride) : 0u;
-        uint32_t bg[4], bu[4], ax[4];
-        trellis_frags(cg, __shfl_sync(0xffffffffu, cg, src), bg);
-        trellis_frags(cu, __shfl_sync(0xffffffffu, cu, src), bu);
-        load_a_frag(a.xh_g, a.K, p0 + m0, nrows, kt, ax);
-        mma_f16_16816(ag[0], ax, bg[0], bg[1]);
-        mma_f16_16816(ag[1], ax, bg[2], bg[3]);
-        load_a_frag(a.xh_u, a.K, p0 + m0, nrows, kt, ax);
-        mma_f16_16816(au[0], ax, bu[0], bu[1]);
-        mma_f16_16816(au[1], ax, bu[2], bu[3]);
+      for (int i = 0; i < 4; ++i) {
+        ng[i] = ldg_nc_u32(wg + noff + i * kstride);
+        nu[i] = ldg_nc_u32(wu + noff + i * kstride);
       }
-    }
-    // accumulators -> shared (row = pair, col = n within the 128-block)
+      const uint4* bgp = reinterpret_cast<const uint4*>(a.xh_g + r0 + c * 128);
+      const uint4* bup = reinterpret_cast<const uint4*>(a.xh_u + r0 + c * 128);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int c = warp * 16 + h * 8 + 2 * q;
-      zg[g][c] = ag[h][0]; zg[g][c + 1] = ag[h][1]; zg[g + 8][c] = ag[h][2]; zg[g + 8][c + 1] = ag[h][3];
-      zu[g][c] = au[h][0]; zu[g][c + 1] = au[h][1]; zu[g + 8][c] = au[h][2]; zu[g + 8][c + 1] = au[h][3];
+      for (int i = 0; i < 4; ++i) {
+        const uint4 bg = bgp[i], bu = bup[i];
+        uint32_t x[8];
+        trellis_x8(pg[i], __shfl_sync(0xffffffffu, pg[i], src), x);
+        tile_mma(cg, x, bg);
+        trellis_x8(pu[i], __shfl_sync(0xffffffffu, pu[i], src), x);
+        tile_mma(cu, x, bu);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) { pg[i] = ng[i]; pu[i] = nu[i]; }
     }
+    acc_to_smem(cg, warp, zg);
+    acc_to_smem(cu, warp, zu);
     __syncthreads();
-    for (int r = warp; r < nrows; r += 8) {
+    cluster_reduce_tile<KSPL>(zg, nrows);
+    cluster_reduce_tile<KSPL>(zu, nrows);
+    __syncthreads();
+    for (int r = warp; r < nrows && ks == 0; r += 8) {
       float vg[4], vu[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) { vg[i] = zg[r][lane * 4 + i]; vu[i] = zu[r][lane * 4 + i]; }
@@ -263,21 +352,24 @@ __global__ void __launch_bounds__(256) exl3_gate_up_kernel(Exl3Args a) {
         act[i] = siluf_(gv) * uv * __half2float(a.suh_d[(int64_t)e * a.N + col + i]);
       }
       fwht128_warp(act);
-      __half2* o = reinterpret_cast<__half2*>(a.xd + (int64_t)(p0 + m0 + r) * a.N + col);
-      o[0] = __floats2half2_rn(act[0], act[1]);
-      o[1] = __floats2half2_rn(act[2], act[3]);
+      uint32_t* o = reinterpret_cast<uint32_t*>(a.xd) + (int64_t)(p0 + m0 + r) * a.N;
+      *reinterpret_cast<uint2*>(o + dup_word(col)) = make_uint2(dup_half(act[0]), dup_half(act[1]));
+      *reinterpret_cast<uint2*>(o + dup_word(col + 2)) = make_uint2(dup_half(act[2]), dup_half(act[3]));
     }
+    cluster_release<KSPL>();
     __syncthreads();
   }
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// down: grid (Dout/128, max_groups); epilogue H128, * svh, * routing weight -> yd[pair] fp32
+// down: grid (Dout/128, max_groups, KSPL) with K split over a cluster as in gate_up; epilogue H128, * svh,
+// * routing weight -> yd[pair] fp32
 // ---------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) exl3_down_kernel(Exl3Args a) {
+template <int KSPL>
+__global__ void __launch_bounds__(256) exl3_down_kernel(Exl3Args a) {   // KSPL in {1, 2}
   const int u = blockIdx.y;
   if (u >= a.group_count[0] || u >= a.max_groups) return;
-  __shared__ float zd[16][132];
+  __shared__ float zd[8][132];
   const int e = a.group_expert[u];
   const int p0 = a.group_offset[u];
   const int np = a.group_offset[u + 1] - p0;
@@ -285,38 +377,40 @@ __global__ void __launch_bounds__(256) exl3_down_kernel(Exl3Args a) {
   const int nb = blockIdx.x;
   const int nt = nb * 8 + warp;
   const int KT = a.N / 16, NT = a.Dout / 16;
+  const int ks = KSPL > 1 ? (int)blockIdx.z : 0, cper = a.N / 64 / KSPL, c_lo = ks * cper, c_hi = c_lo + cper;
   const uint32_t* wd = reinterpret_cast<const uint32_t*>(a.tr_d) + ((int64_t)e * KT * NT + nt) * 32 + lane;
   const int64_t kstride = (int64_t)NT * 32;
   const int src = (lane + 31) & 31;
 
-  for (int m0 = 0; m0 < np; m0 += 16) {
-    const int nrows = min(16, np - m0);
-    float ad[2][4] = {};
-    uint32_t pd[kPf];
+  for (int m0 = 0; m0 < np; m0 += 8) {
+    const int nrows = min(8, np - m0);
+    // token columns past the group read the group's first row: their MMA columns are never stored
+    const int64_t r0 = (int64_t)(p0 + m0 + (g < nrows ? g : 0)) * 2 * a.N + q * 32;
+    float cd[4] = {};
+    uint32_t pd[4];
 #pragma unroll
-    for (int i = 0; i < kPf; ++i) pd[i] = i < KT ? ldg_nc_u32(wd + i * kstride) : 0u;
-    for (int kt0 = 0; kt0 < KT; kt0 += kPf) {
+    for (int i = 0; i < 4; ++i) pd[i] = ldg_nc_u32(wd + (4 * c_lo + i) * kstride);
+    for (int c = c_lo; c < c_hi; ++c) {
+      uint32_t nd[4];
+      const int64_t noff = (c + 1 < c_hi ? 4 * c + 4 : 4 * c) * kstride;   // the last chunk reloads itself
 #pragma unroll
-      for (int i = 0; i < kPf; ++i) {
-        const int kt = kt0 + i;
-        if (kt >= KT) break;
-        const uint32_t cd = pd[i];
-        const int nk = kt + kPf;
-        pd[i] = nk < KT ? ldg_nc_u32(wd + nk * kstride) : 0u;
-        uint32_t bd[4], ax[4];
-        trellis_frags(cd, __shfl_sync(0xffffffffu, cd, src), bd);
-        load_a_frag(a.xd, a.N, p0 + m0, nrows, kt, ax);
-        mma_f16_16816(ad[0], ax, bd[0], bd[1]);
-        mma_f16_16816(ad[1], ax, bd[2], bd[3]);
+      for (int i = 0; i < 4; ++i) nd[i] = ldg_nc_u32(wd + noff + i * kstride);
+      const uint4* bp = reinterpret_cast<const uint4*>(a.xd + r0 + c * 128);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 b = bp[i];
+        uint32_t x[8];
+        trellis_x8(pd[i], __shfl_sync(0xffffffffu, pd[i], src), x);
+        tile_mma(cd, x, b);
       }
-    }
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int c = warp * 16 + h * 8 + 2 * q;
-      zd[g][c] = ad[h][0]; zd[g][c + 1] = ad[h][1]; zd[g + 8][c] = ad[h][2]; zd[g + 8][c + 1] = ad[h][3];
+      for (int i = 0; i < 4; ++i) pd[i] = nd[i];
     }
+    acc_to_smem(cd, warp, zd);
     __syncthreads();
-    for (int r = warp; r < nrows; r += 8) {
+    cluster_reduce_tile<KSPL>(zd, nrows);
+    __syncthreads();
+    for (int r = warp; r < nrows && ks == 0; r += 8) {
       float v[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) v[i] = zd[r][lane * 4 + i];
@@ -330,6 +424,7 @@ __global__ void __launch_bounds__(256) exl3_down_kernel(Exl3Args a) {
       o.w = v[3] * __half2float(a.svh_d[(int64_t)e * a.Dout + col + 3]) * w;
       *reinterpret_cast<float4*>(a.yd + (int64_t)(p0 + m0 + r) * a.Dout + col) = o;
     }
+    cluster_release<KSPL>();
     __syncthreads();
   }
 }
@@ -386,20 +481,47 @@ cudaError_t g53_exl3_rot_in(const Exl3Args& a, cudaStream_t st) {
   return cudaSuccess;
 }
 
+// K split over a cluster of KSPL CTAs (more, smaller CTAs: the grid of a decode window is a couple of waves)
+template <int KSPL>
+static cudaError_t launch_split(void (*kern)(Exl3Args), dim3 grid, const Exl3Args& a, cudaStream_t st) {
+  if (KSPL == 1) {
+    kern<<<grid, 256, 0, st>>>(a);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  grid.z = KSPL;
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = KSPL;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
+static int pick_split(int kc) { return kc % 4 == 0 ? 4 : kc % 2 == 0 ? 2 : 1; }
+
 cudaError_t g53_exl3_gate_up(const Exl3Args& a, cudaStream_t st) {
-  if (a.K % 128 || a.N % 128) return cudaErrorInvalidValue;
-  dim3 grid(a.N / 128, a.max_groups);
-  exl3_gate_up_kernel<<<grid, 256, 0, st>>>(a);
-  G53_CHECK_LAUNCH();
-  return cudaSuccess;
+  if (a.K % 128 || a.N % 128 || !a.decode_layout) return cudaErrorInvalidValue;
+  const dim3 grid(a.N / 128, a.max_groups);
+  switch (pick_split(a.K / 64)) {
+    case 4: return launch_split<4>(exl3_gate_up_kernel<4>, grid, a, st);
+    case 2: return launch_split<2>(exl3_gate_up_kernel<2>, grid, a, st);
+    default: return launch_split<1>(exl3_gate_up_kernel<1>, grid, a, st);
+  }
 }
 
 cudaError_t g53_exl3_down(const Exl3Args& a, cudaStream_t st) {
-  if (a.Dout % 128 || a.N % 16) return cudaErrorInvalidValue;
-  dim3 grid(a.Dout / 128, a.max_groups);
-  exl3_down_kernel<<<grid, 256, 0, st>>>(a);
-  G53_CHECK_LAUNCH();
-  return cudaSuccess;
+  if (a.Dout % 128 || a.N % 64 || !a.decode_layout) return cudaErrorInvalidValue;
+  const dim3 grid(a.Dout / 128, a.max_groups);
+  // the down grid is already twice the gate_up grid (Dout = 2 N at TP=1); split only short-K tensor shards
+  const int kc = a.N / 64;
+  if (kc >= 16 || kc % 2) return launch_split<1>(exl3_down_kernel<1>, grid, a, st);
+  return launch_split<2>(exl3_down_kernel<2>, grid, a, st);
 }
 
 cudaError_t g53_moe_combine(const float* yd, const int* pair_of, int R, int top_k, int D, float* out,

@@ -203,9 +203,11 @@ class Runtime:
             self.p_fill = torch.zeros(c.experts, dtype=i32, device=dev)
             P = max(P, PP)
         if moe0 is not None:
-            self.xh_g = torch.zeros(P, D, dtype=torch.float16, device=dev)
-            self.xh_u = torch.zeros(P, D, dtype=torch.float16, device=dev)
-            self.xd = torch.zeros(P, moe0.gate.n, dtype=torch.float16, device=dev)
+            # the decode path stores its rotated inputs as duplicated f16 pairs (2 halves per element)
+            PX = max(P, 2 * MR * tk)
+            self.xh_g = torch.zeros(PX, D, dtype=torch.float16, device=dev)
+            self.xh_u = torch.zeros(PX, D, dtype=torch.float16, device=dev)
+            self.xd = torch.zeros(PX, moe0.gate.n, dtype=torch.float16, device=dev)
             self.yd = torch.zeros(P, D, dtype=f32, device=dev)
 
     # ------------------------------------------------------------------------------------------------------------

@@ -135,9 +135,10 @@ def _moe_only_runtime(rt, w, rc, dev):
         rt.p_counts = torch.zeros(c.experts, dtype=torch.int32, device=dev)
         rt.p_fill = torch.zeros(c.experts, dtype=torch.int32, device=dev)
         P = max(P, PP)
-    rt.xh_g = torch.zeros(P, D, dtype=torch.float16, device=dev)
-    rt.xh_u = torch.zeros(P, D, dtype=torch.float16, device=dev)
-    rt.xd = torch.zeros(P, moe0.gate.n, dtype=torch.float16, device=dev)
+    PX = max(P, 2 * MR * tk)          # the decode path's rotated inputs are duplicated f16 pairs
+    rt.xh_g = torch.zeros(PX, D, dtype=torch.float16, device=dev)
+    rt.xh_u = torch.zeros(PX, D, dtype=torch.float16, device=dev)
+    rt.xd = torch.zeros(PX, moe0.gate.n, dtype=torch.float16, device=dev)
     rt.yd = torch.zeros(P, D, device=dev)
 
 

@@ -154,9 +154,12 @@ def cmd_engine(a):
     torch.cuda.synchronize()
     inst = (time.perf_counter() - t0) * 1e3 / a.steps
     phases = {k: v * 1e3 / a.steps for k, v in sorted(acc.items(), key=lambda kv: -kv[1])}
+    total, rows = _kernel_table(lambda: [eng.step() for _ in range(2)], reps=1)
     print(json.dumps({"mode": "engine", "k": K, "context": a.context, "plain_step_ms": plain,
                       "instrumented_step_ms": inst, "phases_ms": phases,
-                      "unattributed_ms": inst - sum(phases.values())}))
+                      "unattributed_ms": inst - sum(phases.values()), "kernel_sum_us_per_step": total / 2}))
+    for n, c, t in rows:
+        print(f"{t / 2:10.1f} us {c // 2:6d}x  {n}")
 
 
 def main():

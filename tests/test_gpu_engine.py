@@ -1,6 +1,8 @@
 """The engine on the GPU with the tiny proxy: greedy speculative decoding emits exactly the tokens of greedy
 decoding without speculation (per-row kernels are independent of window composition), concurrent requests, and a
-prefix-cache hit (KDA checkpoint + shared pages) reproduces the cold-start output."""
+prefix-cache hit (KDA checkpoint + shared pages) reproduces the cold-start output of the same chunking.  (Runs with
+different prefill chunk boundaries are not compared token for token: chunk size selects between the chunked and the
+recurrent KDA kernels and between the prefill and decode MoE kernels, whose fp32 summation orders differ.)"""
 
 import pytest
 import torch
@@ -42,13 +44,11 @@ def test_forced_acceptance_and_text_api():
 
 def test_prefix_cache_hit_reproduces_output():
     from glm53.engine.llm import SamplingParams
-    llm = _llm(speculative=False, checkpoints=4)
     base = _prompts(1, 300, seed=3)[0]
-    a = llm.engine.generate([base], SamplingParams(max_tokens=16, ignore_eos=True))[0]
-    # the engine saved KDA checkpoints every 8 pages (512 tokens) -> use a 64-token page interval here
+    # the engine saves KDA checkpoints every 8 pages (512 tokens) by default -> use a 64-token interval here
     llm2 = _llm(speculative=False, checkpoints=4)
     llm2.engine.cfg.checkpoint_pages = 1
     a2 = llm2.engine.generate([base], SamplingParams(max_tokens=16, ignore_eos=True))[0]
     b = llm2.engine.generate([base], SamplingParams(max_tokens=16, ignore_eos=True))[0]
     assert llm2.engine.metrics["prefix_cached_tokens"] >= 256
-    assert a == a2 == b
+    assert a2 == b
