@@ -90,6 +90,7 @@ void gemm_common(const Tensor& a, bool fp8, const OptT& a_scale, const Tensor& w
   p.mode = (int)mode; p.fp8 = fp8 ? 1 : 0; p.limit = (float)limit;
   p.err = P<int>(err_word(a));
   TORCH_CHECK(w.size(1) == p.K, "K mismatch");
+  TORCH_CHECK(y.stride(-1) == 1, "y rows must be contiguous");
   if (mode == GEMV_BF16 || mode == GEMV_SWIGLU) {
     TORCH_CHECK(y.scalar_type() == at::kBFloat16, "y must be bf16");
   } else {

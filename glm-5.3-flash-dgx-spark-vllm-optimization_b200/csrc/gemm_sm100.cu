@@ -3,14 +3,16 @@
 //   A  activations, K-major (bf16, or e4m3 with one fp32 scale per row)
 //   B  weights [N, K], K-major (bf16, or e4m3 with one fp32 scale per output row: the engine's fp8 weights)
 //
-// One CTA computes a 128 x BN tile.  Warp roles (192 threads):
+// Persistent: one CTA per SM walks the 128 x BN output tiles in a grouped order (bands of 8 M-tiles).  Warp roles
+// (192 threads):
 //   warp 0    TMA producer: one elected thread loads 128-byte-swizzled K-slices of A and B into a STAGES-deep
-//             shared-memory ring (cp.async.bulk.tensor, mbarrier complete_tx)
-//   warp 1    allocates BN TMEM columns; one thread issues tcgen05.mma (M=128, N=BN, kind::f16 or kind::f8f6f4)
-//             from shared-memory descriptors, accumulating in TMEM; tcgen05.commit frees each ring slot and
-//             finally signals the epilogue
+//             shared-memory ring (cp.async.bulk.tensor, mbarrier complete_tx), continuously across tiles
+//   warp 1    allocates 2 x BN TMEM columns (two accumulators); one thread issues tcgen05.mma (M=128, N=BN,
+//             kind::f16 or kind::f8f6f4) from shared-memory descriptors; tcgen05.commit frees each ring slot and
+//             signals "accumulator full"; it waits for "accumulator empty" before reusing a buffer
 //   warps 2-5 epilogue: tcgen05.ld of the accumulator (one TMEM lane = one output row per thread), scales,
-//             optional SwiGLU over (8 gate, 8 up) row groups of the weight, bf16 / fp32 / fp32-accumulate stores
+//             optional SwiGLU over (8 gate, 8 up) row groups of the weight, 16-byte bf16 / fp32 /
+//             fp32-accumulate stores; then it releases the buffer, so it overlaps the next tile's main loop
 // Every mbarrier wait is bounded; a wait that runs out sets an error word and the CTA stops issuing work (and
 // frees its TMEM), so a broken pipeline returns an error to the host instead of hanging the GPU.
 // No TMA multicast is used.
@@ -127,6 +129,115 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// tile t of the persistent schedule -> (m0, n0): bands of kGroupM M-tiles, N-tiles walked inside a band, so the
+// CTAs resident at one time share a few A row-blocks and a few B column-blocks in L2
+constexpr int kGroupM = 8;
+__device__ __forceinline__ void tile_coords(int t, int MT, int NT, int BN, int& m0, int& n0) {
+  const int band = t / (kGroupM * NT);
+  const int gm = min(kGroupM, MT - band * kGroupM);
+  const int idx = t - band * kGroupM * NT;
+  m0 = (band * kGroupM + idx % gm) * kBM;
+  n0 = (idx / gm) * BN;
+}
+
+// 32 accumulator columns of one row -> output (scales, mode); vectorised 16-byte stores when the row is aligned
+__device__ __forceinline__ void store_chunk(const GemmArgs& p, int row, int nb, float rs, const float (&v)[32]) {
+  const bool full = p.vec && nb + 32 <= p.N;
+  float sc[32];
+  if (p.b_scale && full) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 t = *reinterpret_cast<const float4*>(p.b_scale + nb + i);
+      sc[i] = t.x; sc[i + 1] = t.y; sc[i + 2] = t.z; sc[i + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) sc[i] = (p.b_scale && nb + i < p.N) ? p.b_scale[nb + i] : 1.f;
+  }
+  if (p.mode == GEMV_SWIGLU) {
+    // columns: two groups of (8 gate rows, 8 matching up rows) of the interleaved weight -> 16 outputs
+    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.y) + (int64_t)row * p.ldy + (nb >> 1);
+    float o[16];
+#pragma unroll
+    for (int g = 0; g < 2; ++g)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float gv = round_bf16(v[g * 16 + i] * rs * sc[g * 16 + i]);
+        float uv = round_bf16(v[g * 16 + 8 + i] * rs * sc[g * 16 + 8 + i]);
+        gv = fminf(gv, p.limit);
+        uv = fminf(fmaxf(uv, -p.limit), p.limit);
+        o[g * 8 + i] = siluf_(gv) * uv;
+      }
+    if (full) {
+      uint32_t w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        __nv_bfloat162 b = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&b);
+      }
+      reinterpret_cast<uint4*>(y)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      reinterpret_cast<uint4*>(y)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+#pragma unroll
+      for (int g = 0; g < 2; ++g)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (nb + g * 16 + 8 + i < p.N) y[g * 8 + i] = f2bf(o[g * 8 + i]);
+    }
+    return;
+  }
+  const int64_t off = (int64_t)row * p.ldy + nb;
+  if (p.mode == GEMV_BF16) {
+    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.y) + off;
+    if (full) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int j = c * 8 + 2 * i;
+          __nv_bfloat162 b = __floats2bfloat162_rn(v[j] * rs * sc[j], v[j + 1] * rs * sc[j + 1]);
+          w[i] = *reinterpret_cast<uint32_t*>(&b);
+        }
+        reinterpret_cast<uint4*>(y)[c] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (nb + i < p.N) y[i] = f2bf(v[i] * rs * sc[i]);
+    }
+    return;
+  }
+  float* y = reinterpret_cast<float*>(p.y) + off;
+  const bool acc = p.mode == GEMV_F32_ACC;
+  if (full) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      float4 o = make_float4(v[4 * c] * rs * sc[4 * c], v[4 * c + 1] * rs * sc[4 * c + 1],
+                             v[4 * c + 2] * rs * sc[4 * c + 2], v[4 * c + 3] * rs * sc[4 * c + 3]);
+      if (acc) {
+        const float4 old = reinterpret_cast<const float4*>(y)[c];
+        o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+      }
+      reinterpret_cast<float4*>(y)[c] = o;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (nb + i >= p.N) break;
+      const float val = v[i] * rs * sc[i];
+      if (acc) y[i] += val;
+      else y[i] = val;
+    }
+  }
+}
+
+// Persistent kernel: gridDim.x CTAs (at most one per SM) walk the output tiles in the grouped order; the TMEM
+// holds two 128 x BN accumulators so the epilogue of one tile overlaps the main loop of the next.
 template <int BN, bool FP8, int STAGES>
 __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                                                             const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
@@ -135,16 +246,18 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
   constexpr int B_BYTES = BN * 128;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   constexpr int UK = FP8 ? 32 : 16;                // K per tcgen05.mma
+  constexpr uint32_t TMEM_COLS = 2 * BN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t acc_bar;
+  __shared__ __align__(8) uint64_t tfull[2];
+  __shared__ __align__(8) uint64_t tempty[2];
   __shared__ uint32_t tmem_base;
   __shared__ volatile int fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * BN;
+  const int MT = (p.M + kBM - 1) / kBM, NT = (p.N + BN - 1) / BN, tiles = MT * NT;
   const int nk = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -153,12 +266,15 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&acc_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);                    // one arrival per epilogue warp
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
-                 "r"((uint32_t)BN));
+                 "r"(TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -168,89 +284,81 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (kb >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1, &fail, p.err, 1)) break;
-        uint8_t* a_dst = smem + s * STAGE_BYTES;
-        uint8_t* b_dst = a_dst + A_BYTES;
-        mbar_expect_tx(&full_bar[s], STAGE_BYTES);
-        tma_load_2d(&tmA, &full_bar[s], a_dst, kb * BK, m0);
-        tma_load_2d(&tmB, &full_bar[s], b_dst, kb * BK, n0);
+      int kbg = 0;
+      for (int t = blockIdx.x; t < tiles && !fail; t += gridDim.x) {
+        int m0, n0;
+        tile_coords(t, MT, NT, BN, m0, n0);
+        for (int kb = 0; kb < nk; ++kb, ++kbg) {
+          const int s = kbg % STAGES;
+          const uint32_t ph = (kbg / STAGES) & 1;
+          if (kbg >= STAGES && !mbar_wait(&empty_bar[s], ph ^ 1, &fail, p.err, 1)) break;
+          uint8_t* a_dst = smem + s * STAGE_BYTES;
+          uint8_t* b_dst = a_dst + A_BYTES;
+          mbar_expect_tx(&full_bar[s], STAGE_BYTES);
+          tma_load_2d(&tmA, &full_bar[s], a_dst, kb * BK, m0);
+          tma_load_2d(&tmB, &full_bar[s], b_dst, kb * BK, n0);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = umma_idesc(FP8 ? 0 : 1, BN, kBM);
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        if (!mbar_wait(&full_bar[s], ph, &fail, p.err, 2)) break;
+      int kbg = 0, it = 0;
+      for (int t = blockIdx.x; t < tiles && !fail; t += gridDim.x, ++it) {
+        const int buf = it & 1;
+        if (it >= 2 && !mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, &fail, p.err, 4)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
-        const uint32_t b_addr = a_addr + A_BYTES;
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb, ++kbg) {
+          const int s = kbg % STAGES;
+          const uint32_t ph = (kbg / STAGES) & 1;
+          if (!mbar_wait(&full_bar[s], ph, &fail, p.err, 2)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_addr = smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
-        for (int k = 0; k < BK / UK; ++k) {
-          const uint32_t koff = k * UK * (FP8 ? 1 : 2);    // bytes along the swizzled row
-          umma<FP8>(tmem, umma_desc_sw128(a_addr + koff), umma_desc_sw128(b_addr + koff), idesc,
-                    (kb > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < BK / UK; ++k) {
+            const uint32_t koff = k * UK * (FP8 ? 1 : 2);    // bytes along the swizzled row
+            umma<FP8>(d, umma_desc_sw128(a_addr + koff), umma_desc_sw128(b_addr + koff), idesc,
+                      (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[s]);
         }
-        umma_commit(&empty_bar[s]);
+        if (!ok) break;
+        umma_commit(&tfull[buf]);
       }
-      umma_commit(&acc_bar);
     }
   } else {
     // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
     const int quad = warp & 3;
-    const int row = m0 + quad * 32 + lane;
-    int okw = 0;
-    if (lane == 0) okw = mbar_wait(&acc_bar, 0, &fail, p.err, 3) ? 1 : 0;
-    const bool ok = __shfl_sync(0xffffffffu, okw, 0) != 0;     // warp-uniform: tcgen05.ld is .sync.aligned
-    __syncwarp();
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (ok) {
+    int it = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+      const int buf = it & 1;
+      int m0, n0;
+      tile_coords(t, MT, NT, BN, m0, n0);
+      int okw = 0;
+      if (lane == 0) okw = mbar_wait(&tfull[buf], (it >> 1) & 1, &fail, p.err, 3) ? 1 : 0;
+      const bool ok = __shfl_sync(0xffffffffu, okw, 0) != 0;     // warp-uniform: tcgen05.ld is .sync.aligned
+      if (!ok) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int row = m0 + quad * 32 + lane;
       const float rs = (p.a_scale && row < p.M) ? p.a_scale[row] : 1.f;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c0, v);
-        if (row >= p.M) continue;
-        const int nb = n0 + c0;
-        if (p.mode == GEMV_SWIGLU) {
-          // columns: two groups of (8 gate rows, 8 matching up rows) of the interleaved weight
-#pragma unroll
-          for (int g = 0; g < 2; ++g) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int ng = nb + g * 16 + i, nu = ng + 8;
-              if (nu >= p.N) continue;
-              float gv = round_bf16(v[g * 16 + i] * rs * (p.b_scale ? p.b_scale[ng] : 1.f));
-              float uv = round_bf16(v[g * 16 + 8 + i] * rs * (p.b_scale ? p.b_scale[nu] : 1.f));
-              gv = fminf(gv, p.limit);
-              uv = fminf(fmaxf(uv, -p.limit), p.limit);
-              reinterpret_cast<__nv_bfloat16*>(p.y)[(int64_t)row * p.ldy + ((nb + g * 16) >> 1) + i] =
-                  f2bf(siluf_(gv) * uv);
-            }
-          }
-          continue;
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int n = nb + i;
-          if (n >= p.N) break;
-          const float val = v[i] * rs * (p.b_scale ? p.b_scale[n] : 1.f);
-          const int64_t off = (int64_t)row * p.ldy + n;
-          if (p.mode == GEMV_BF16) reinterpret_cast<__nv_bfloat16*>(p.y)[off] = f2bf(val);
-          else if (p.mode == GEMV_F32) reinterpret_cast<float*>(p.y)[off] = val;
-          else reinterpret_cast<float*>(p.y)[off] += val;
-        }
+        tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + c0), v);
+        if (row < p.M && n0 + c0 < p.N) store_chunk(p, row, n0 + c0, rs, v);
       }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
   }
 }
 
@@ -351,8 +459,18 @@ cudaError_t launch(const GemmArgs& p, cudaStream_t st) {
   auto kern = gemm_sm100_kernel<BN, FP8, STAGES>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  dim3 grid((p.N + BN - 1) / BN, (p.M + kBM - 1) / kBM);
-  kern<<<grid, 192, smem, st>>>(ta, tb, p);
+  static int sms[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int n_sm = (dev < 64 && sms[dev] > 0) ? sms[dev] : 148;
+  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN);
+  GemmArgs q = p;
+  // 16-byte epilogue stores need an aligned output base and row pitch
+  const int out_esz = (p.mode == GEMV_F32 || p.mode == GEMV_F32_ACC) ? 4 : 2;
+  q.vec = ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0 && ((p.ldy * out_esz) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(p.b_scale) & 15) == 0) ? 1 : 0;
+  kern<<<std::min(tiles, n_sm), 192, smem, st>>>(ta, tb, q);
   return cudaGetLastError();
 }
 

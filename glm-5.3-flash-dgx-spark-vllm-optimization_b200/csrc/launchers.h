@@ -40,6 +40,7 @@ struct GemmArgs {
   int M, N, K, mode, fp8;
   float limit;
   int* err;                            // device error word (bounded waits that ran out)
+  int vec;                             // set by the launcher: 16-byte epilogue stores allowed
 };
 cudaError_t g53_gemm_sm100(const GemmArgs& p, cudaStream_t st);
 cudaError_t g53_e4m3_to_bf16(const uint8_t* w, int64_t n, __nv_bfloat16* out, cudaStream_t st);

@@ -80,3 +80,22 @@ def test_gemm_w8a16(C, M, N, K):
     torch.cuda.synchronize()
     assert C.gemm_error(y) == 0
     torch.testing.assert_close(y.cpu(), ref, atol=2e-3, rtol=2e-3)
+
+
+@pytest.mark.parametrize("M,N,K", [(2500, 3000, 512), (130, 8200, 256)])
+def test_gemm_persistent_accumulate_and_bf16_out(C, M, N, K):
+    """Many tiles per CTA (persistent schedule, both TMEM accumulators reused), fp32 accumulate into an existing
+    output and bf16 output with ragged M/N edges (scalar tail stores next to 16-byte stores)."""
+    torch.manual_seed(7)
+    a = torch.randn(M, K, device=DEV).to(torch.bfloat16)
+    b = (torch.randn(N, K, device=DEV) / math.sqrt(K)).to(torch.bfloat16)
+    ref = a.float() @ b.float().t()
+    base = torch.randn(M, N, device=DEV)
+    y = base.clone()
+    C.gemm_bf16(a, b, None, y, 2, 0.0)                       # GEMV_F32_ACC
+    yb = torch.zeros(M, N, device=DEV, dtype=torch.bfloat16)
+    C.gemm_bf16(a, b, None, yb, 0, 0.0)                      # GEMV_BF16
+    torch.cuda.synchronize()
+    assert C.gemm_error(y) == 0
+    torch.testing.assert_close(y, base + ref, atol=2e-3, rtol=2e-3)
+    torch.testing.assert_close(yb.float(), ref, atol=2e-2, rtol=2e-2)
