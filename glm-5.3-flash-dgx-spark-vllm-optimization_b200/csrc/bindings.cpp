@@ -78,19 +78,33 @@ Tensor& err_word(const Tensor& like) {
   return words[dev];
 }
 
+// a [M, K] or [B, M, K], w [N, K] or [B, N, K], y [M, N] or [B, M, N]; rows K-major (inner stride 1), batch and
+// row strides free (e.g. per-head views of [rows, heads, dim] activations)
 void gemm_common(const Tensor& a, bool fp8, const OptT& a_scale, const Tensor& w, const OptT& w_scale, const Tensor& y,
                  int64_t mode, double limit) {
+  const bool bat = a.dim() == 3;
+  TORCH_CHECK(w.dim() == a.dim() && y.dim() == a.dim(), "a, w and y must all be 2-D or all 3-D");
+  TORCH_CHECK(a.stride(-1) == 1 && w.stride(-1) == 1 && y.stride(-1) == 1, "rows must be contiguous");
   GemmArgs p{};
-  p.a = a.data_ptr(); p.lda = a.stride(0);
-  p.b = w.data_ptr(); p.ldb = w.stride(0);
+  p.a = a.data_ptr(); p.lda = a.stride(-2);
+  p.b = w.data_ptr(); p.ldb = w.stride(-2);
   p.a_scale = P<const float>(a_scale);
   p.b_scale = P<const float>(w_scale);
-  p.y = y.data_ptr(); p.ldy = y.stride(0);
-  p.M = (int)a.size(0); p.N = (int)w.size(0); p.K = (int)a.size(1);
+  p.y = y.data_ptr(); p.ldy = y.stride(-2);
+  p.M = (int)a.size(-2); p.N = (int)w.size(-2); p.K = (int)a.size(-1);
   p.mode = (int)mode; p.fp8 = fp8 ? 1 : 0; p.limit = (float)limit;
   p.err = P<int>(err_word(a));
-  TORCH_CHECK(w.size(1) == p.K, "K mismatch");
-  TORCH_CHECK(y.stride(-1) == 1, "y rows must be contiguous");
+  if (bat) {
+    TORCH_CHECK(w.size(0) == a.size(0) && y.size(0) == a.size(0), "batch mismatch");
+    p.batch = (int)a.size(0);
+    p.bsa = a.stride(0); p.bsb = w.stride(0); p.bsy = y.stride(0);
+    if (w_scale.has_value()) {
+      TORCH_CHECK(w_scale->dim() == 2 && w_scale->stride(1) == 1, "batched scales must be [B, N]");
+      p.bss = w_scale->stride(0);
+    }
+  }
+  TORCH_CHECK(w.size(-1) == p.K, "K mismatch");
+  TORCH_CHECK(y.size(-2) == p.M, "y rows mismatch");
   if (mode == GEMV_BF16 || mode == GEMV_SWIGLU) {
     TORCH_CHECK(y.scalar_type() == at::kBFloat16, "y must be bf16");
   } else {
@@ -115,11 +129,11 @@ void gemm_w8(const Tensor& x, const Tensor& w, const Tensor& scale, const Tensor
 // weight scales applied in the epilogue (same numerics as the small-M kernel: bf16 activations, exact weights)
 void gemm_w8a16(const Tensor& x, const Tensor& w, const Tensor& scale, const Tensor& y, int64_t mode, double limit,
                 const Tensor& scratch) {
-  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1);
   TORCH_CHECK(scratch.scalar_type() == at::kBFloat16 && scratch.numel() >= w.numel(), "scratch too small");
   TORCH_CHECK(w.is_contiguous());
   check(g53_e4m3_to_bf16(P<const uint8_t>(w), w.numel(), P<__nv_bfloat16>(scratch), stream()), "e4m3_to_bf16");
-  auto wb = scratch.flatten().narrow(0, 0, w.numel()).view({w.size(0), w.size(1)});
+  auto wb = scratch.flatten().narrow(0, 0, w.numel()).view(w.sizes());
   gemm_common(x, false, {}, wb, scale, y, mode, limit);
 }
 

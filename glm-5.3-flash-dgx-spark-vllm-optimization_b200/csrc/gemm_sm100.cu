@@ -65,10 +65,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return true;
 }
 
-__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y) {
+// 3-D tiled load (k, row, batch); x = k is a multiple of the 128-byte box row, so it is 16-byte aligned
+__device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y, int z) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
 
@@ -145,22 +146,23 @@ __device__ __forceinline__ void tile_coords(int t, int MT, int NT, int BN, int& 
 }
 
 // 32 accumulator columns of one row -> output (scales, mode); vectorised 16-byte stores when the row is aligned
-__device__ __forceinline__ void store_chunk(const GemmArgs& p, int row, int nb, float rs, const float (&v)[32]) {
+__device__ __forceinline__ void store_chunk(const GemmArgs& p, void* ybase, const float* bscale, int row, int nb,
+                                            float rs, const float (&v)[32]) {
   const bool full = p.vec && nb + 32 <= p.N;
   float sc[32];
-  if (p.b_scale && full) {
+  if (bscale && full) {
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
-      const float4 t = *reinterpret_cast<const float4*>(p.b_scale + nb + i);
+      const float4 t = *reinterpret_cast<const float4*>(bscale + nb + i);
       sc[i] = t.x; sc[i + 1] = t.y; sc[i + 2] = t.z; sc[i + 3] = t.w;
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) sc[i] = (p.b_scale && nb + i < p.N) ? p.b_scale[nb + i] : 1.f;
+    for (int i = 0; i < 32; ++i) sc[i] = (bscale && nb + i < p.N) ? bscale[nb + i] : 1.f;
   }
   if (p.mode == GEMV_SWIGLU) {
     // columns: two groups of (8 gate rows, 8 matching up rows) of the interleaved weight -> 16 outputs
-    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.y) + (int64_t)row * p.ldy + (nb >> 1);
+    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(ybase) + (int64_t)row * p.ldy + (nb >> 1);
     float o[16];
 #pragma unroll
     for (int g = 0; g < 2; ++g)
@@ -192,7 +194,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& p, int row, int nb, 
   }
   const int64_t off = (int64_t)row * p.ldy + nb;
   if (p.mode == GEMV_BF16) {
-    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.y) + off;
+    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(ybase) + off;
     if (full) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -212,7 +214,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& p, int row, int nb, 
     }
     return;
   }
-  float* y = reinterpret_cast<float*>(p.y) + off;
+  float* y = reinterpret_cast<float*>(ybase) + off;
   const bool acc = p.mode == GEMV_F32_ACC;
   if (full) {
 #pragma unroll
@@ -257,7 +259,8 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
   __shared__ volatile int fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int MT = (p.M + kBM - 1) / kBM, NT = (p.N + BN - 1) / BN, tiles = MT * NT;
+  const int MT = (p.M + kBM - 1) / kBM, NT = (p.N + BN - 1) / BN, per_batch = MT * NT;
+  const int tiles = per_batch * max(p.batch, 1);
   const int nk = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -287,7 +290,8 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
       int kbg = 0;
       for (int t = blockIdx.x; t < tiles && !fail; t += gridDim.x) {
         int m0, n0;
-        tile_coords(t, MT, NT, BN, m0, n0);
+        const int bz = t / per_batch;
+        tile_coords(t - bz * per_batch, MT, NT, BN, m0, n0);
         for (int kb = 0; kb < nk; ++kb, ++kbg) {
           const int s = kbg % STAGES;
           const uint32_t ph = (kbg / STAGES) & 1;
@@ -295,8 +299,8 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
           uint8_t* a_dst = smem + s * STAGE_BYTES;
           uint8_t* b_dst = a_dst + A_BYTES;
           mbar_expect_tx(&full_bar[s], STAGE_BYTES);
-          tma_load_2d(&tmA, &full_bar[s], a_dst, kb * BK, m0);
-          tma_load_2d(&tmB, &full_bar[s], b_dst, kb * BK, n0);
+          tma_load_3d(&tmA, &full_bar[s], a_dst, kb * BK, m0, bz);
+          tma_load_3d(&tmB, &full_bar[s], b_dst, kb * BK, n0, bz);
         }
       }
     }
@@ -336,7 +340,11 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
       const int buf = it & 1;
       int m0, n0;
-      tile_coords(t, MT, NT, BN, m0, n0);
+      const int bz = t / per_batch;
+      tile_coords(t - bz * per_batch, MT, NT, BN, m0, n0);
+      void* ybase = reinterpret_cast<uint8_t*>(p.y) +
+                    bz * p.bsy * ((p.mode == GEMV_F32 || p.mode == GEMV_F32_ACC) ? 4 : 2);
+      const float* bscale = p.b_scale ? p.b_scale + bz * p.bss : nullptr;
       int okw = 0;
       if (lane == 0) okw = mbar_wait(&tfull[buf], (it >> 1) & 1, &fail, p.err, 3) ? 1 : 0;
       const bool ok = __shfl_sync(0xffffffffu, okw, 0) != 0;     // warp-uniform: tcgen05.ld is .sync.aligned
@@ -348,7 +356,7 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
         tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * BN + c0), v);
-        if (row < p.M && n0 + c0 < p.N) store_chunk(p, row, n0 + c0, rs, v);
+        if (row < p.M && n0 + c0 < p.N) store_chunk(p, ybase, bscale, row, n0 + c0, rs, v);
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
@@ -435,16 +443,18 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D K-major tile map: rows x K, box = box_rows x 128 bytes, 128-byte swizzle
-bool make_map(CUtensorMap* m, const void* base, bool fp8, int64_t rows, int64_t K, int64_t ld_elems, int box_rows) {
+// 3-D K-major tile map: batch x rows x K, box = 1 x box_rows x 128 bytes, 128-byte swizzle
+bool make_map(CUtensorMap* m, const void* base, bool fp8, int64_t rows, int64_t K, int64_t ld_elems, int64_t batch,
+              int64_t bs_elems, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const int esz = fp8 ? 1 : 2;
-  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)(ld_elems * esz)};
-  cuuint32_t box[2] = {(cuuint32_t)(128 / esz), (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+  if (batch <= 1) { batch = 1; bs_elems = rows * ld_elems; }
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld_elems * esz), (cuuint64_t)(bs_elems * esz)};
+  cuuint32_t box[3] = {(cuuint32_t)(128 / esz), (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base),
                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -453,8 +463,8 @@ bool make_map(CUtensorMap* m, const void* base, bool fp8, int64_t rows, int64_t 
 template <int BN, bool FP8, int STAGES>
 cudaError_t launch(const GemmArgs& p, cudaStream_t st) {
   CUtensorMap ta, tb;
-  if (!make_map(&ta, p.a, FP8, p.M, p.K, p.lda, kBM)) return cudaErrorInvalidValue;
-  if (!make_map(&tb, p.b, FP8, p.N, p.K, p.ldb, BN)) return cudaErrorInvalidValue;
+  if (!make_map(&ta, p.a, FP8, p.M, p.K, p.lda, p.batch, p.bsa, kBM)) return cudaErrorInvalidValue;
+  if (!make_map(&tb, p.b, FP8, p.N, p.K, p.ldb, p.batch, p.bsb, BN)) return cudaErrorInvalidValue;
   const int smem = STAGES * (kBM * 128 + BN * 128) + 1024;
   auto kern = gemm_sm100_kernel<BN, FP8, STAGES>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -464,11 +474,12 @@ cudaError_t launch(const GemmArgs& p, cudaStream_t st) {
   cudaGetDevice(&dev);
   if (dev < 64 && sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
   const int n_sm = (dev < 64 && sms[dev] > 0) ? sms[dev] : 148;
-  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN);
+  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * std::max(p.batch, 1);
   GemmArgs q = p;
   // 16-byte epilogue stores need an aligned output base and row pitch
   const int out_esz = (p.mode == GEMV_F32 || p.mode == GEMV_F32_ACC) ? 4 : 2;
   q.vec = ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0 && ((p.ldy * out_esz) & 15) == 0 &&
+           ((p.bsy * out_esz) & 15) == 0 && ((p.bss * 4) & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(p.b_scale) & 15) == 0) ? 1 : 0;
   kern<<<std::min(tiles, n_sm), 192, smem, st>>>(ta, tb, q);
   return cudaGetLastError();
@@ -482,6 +493,7 @@ cudaError_t g53_gemm_sm100(const GemmArgs& p, cudaStream_t st) {
   if ((reinterpret_cast<uintptr_t>(p.a) & 15) || (reinterpret_cast<uintptr_t>(p.b) & 15) ||
       ((p.lda * esz) & 15) || ((p.ldb * esz) & 15) || (p.K * esz) % 16)
     return cudaErrorInvalidValue;
+  if (p.batch > 1 && (((p.bsa * esz) & 15) || ((p.bsb * esz) & 15) || p.a_scale)) return cudaErrorInvalidValue;
   if (p.fp8) return p.N >= 256 ? launch<256, true, 4>(p, st) : launch<128, true, 6>(p, st);
   return p.N >= 256 ? launch<256, false, 4>(p, st) : launch<128, false, 6>(p, st);
 }

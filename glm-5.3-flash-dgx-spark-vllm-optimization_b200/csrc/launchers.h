@@ -41,6 +41,9 @@ struct GemmArgs {
   float limit;
   int* err;                            // device error word (bounded waits that ran out)
   int vec;                             // set by the launcher: 16-byte epilogue stores allowed
+  // batched GEMM (e.g. per attention head): batch strides in elements of A, B, Y and of b_scale
+  int batch;                           // 0 or 1: a single GEMM
+  int64_t bsa, bsb, bsy, bss;
 };
 cudaError_t g53_gemm_sm100(const GemmArgs& p, cudaStream_t st);
 cudaError_t g53_e4m3_to_bf16(const uint8_t* w, int64_t n, __nv_bfloat16* out, cudaStream_t st);

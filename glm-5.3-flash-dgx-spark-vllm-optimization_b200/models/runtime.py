@@ -390,10 +390,7 @@ class Runtime:
         if rope:
             Kc.rope_q(self.q[:R], b.positions[:R], nope, rope, c.rope_theta)
         # absorbed query: q_lat[r, h] = q_nope[r, h] @ W_uk[h]   (batched over heads)
-        for r0 in range(0, R, K.GEMV_MAX_M):
-            r1 = min(R, r0 + K.GEMV_MAX_M)
-            Kc.gemv(self.q[r0:r1, :, :nope].transpose(0, 1), a.w_uk_t.w, a.w_uk_t.s,
-                    self.q_lat[r0:r1].transpose(0, 1), K.GEMV_BF16, 0.0)
+        K.linear8(self.q[:R, :, :nope].transpose(0, 1), a.w_uk_t.w, a.w_uk_t.s, self.q_lat[:R].transpose(0, 1))
         # indexer
         K.linear_bf16(self.normed[:R], a.index.proj, self.iproj[:R])
         Kc.dsa_update(self.iproj[:R], a.index.ln_w, a.index.ln_b, a.index.ape, self.ik[li], self.ig[li],
@@ -414,10 +411,7 @@ class Runtime:
                           self.kpe[li] if rope else None, self.sel[:n], self.sel_count[:n], rope, sm_scale, splits,
                           self.part_o, self.part_ml, self.o_lat[r0:r1])
         ob = self.obuf[:R].view(R, H, c.v_dim)
-        for r0 in range(0, R, K.GEMV_MAX_M):
-            r1 = min(R, r0 + K.GEMV_MAX_M)
-            Kc.gemv(self.o_lat[r0:r1].transpose(0, 1), a.w_uv.w, a.w_uv.s, ob[r0:r1].transpose(0, 1),
-                    K.GEMV_BF16, 0.0)
+        K.linear8(self.o_lat[:R].transpose(0, 1), a.w_uv.w, a.w_uv.s, ob.transpose(0, 1))
         self._final_linear(self.obuf[:R], a.o_proj, R)
 
     def _mlp(self, lw, R):

@@ -42,14 +42,15 @@ def C():
 def linear8(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor, y: torch.Tensor, mode: int = GEMV_BF16,
             limit: float = 0.0) -> torch.Tensor:
     """y[M, N] (mode) = x[M, K] @ (w8[N, K] * s)^T for any M (chunks of 16 rows through the small-M kernel, or
-    the large-M GEMM when it is available)."""
+    the large-M GEMM when it is available).  Batched form: x [B, M, K], w [B, N, K], s [B, N], y [B, M, N] (per
+    attention head; any batch and row strides with contiguous rows)."""
     M = x.shape[-2]
     g = C().gemv
     if M <= GEMV_MAX_M:
         g(x, w, s, y, mode, limit)
         return y
-    if GEMM_ENABLED and M >= GEMM_MIN_M and x.dim() == 2:
-        if PREFILL_W8A8:
+    if GEMM_ENABLED and M >= GEMM_MIN_M:
+        if PREFILL_W8A8 and x.dim() == 2:
             C().gemm_w8(x, w, s, y, mode, limit)
         else:
             C().gemm_w8a16(x, w, s, y, mode, limit, _w_scratch(w.numel(), x.device))

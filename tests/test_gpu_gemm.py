@@ -99,3 +99,20 @@ def test_gemm_persistent_accumulate_and_bf16_out(C, M, N, K):
     assert C.gemm_error(y) == 0
     torch.testing.assert_close(y, base + ref, atol=2e-3, rtol=2e-3)
     torch.testing.assert_close(yb.float(), ref, atol=2e-2, rtol=2e-2)
+
+
+def test_gemm_w8a16_batched_per_head_views(C):
+    """Batched (per-head) GEMM on strided views, the layout of the absorbed MLA projections at prefill:
+    x = q[:, :, :nope].transpose(0, 1) ([H, R, nope] with row stride H*qk), y = q_lat.transpose(0, 1)."""
+    from glm53.models.weights import quantize_fp8_rows
+    torch.manual_seed(11)
+    R, H, nope, rope, L = 300, 6, 64, 32, 128
+    q = torch.randn(R, H, nope + rope, device=DEV).to(torch.bfloat16)
+    w = quantize_fp8_rows(torch.randn(H, L, nope) / math.sqrt(nope))
+    ref = torch.einsum("rhk,hnk->rhn", q[:, :, :nope].float().cpu(), w.dequant())
+    y = torch.zeros(R, H, L, device=DEV, dtype=torch.bfloat16)
+    scratch = torch.empty(w.w.numel(), dtype=torch.bfloat16, device=DEV)
+    C.gemm_w8a16(q[:, :, :nope].transpose(0, 1), w.w.to(DEV), w.s.to(DEV), y.transpose(0, 1), 0, 0.0, scratch)
+    torch.cuda.synchronize()
+    assert C.gemm_error(y) == 0
+    torch.testing.assert_close(y.float().cpu(), ref, atol=2e-2, rtol=2e-2)
