@@ -485,8 +485,12 @@ void kda_recurrent(const Tensor& proj, const Tensor& seq, const Tensor& f, const
 
 void kda_chunk(const Tensor& proj, const Tensor& seq, const Tensor& f, const Tensor& qkv, const Tensor& a_log,
                const Tensor& dt_bias, const Tensor& S_pool, const Tensor& o_raw, int64_t H, int64_t Dh, int64_t b_off,
-               double lower) {
+               double lower, const Tensor& scratch) {
   KdaArgs a = kda_args(proj, seq, 0, H, Dh, 0);
+  TORCH_CHECK(scratch.scalar_type() == at::kFloat && scratch.is_contiguous(), "kda_chunk scratch must be fp32");
+  const int64_t per_slot = g53_kda_chunk_scratch_floats(64, 0, (int)H, (int)Dh) / 2;   // one slot, all heads
+  a.scr = P<float>(scratch);
+  a.scr_slots = (int)(scratch.numel() / per_slot);
   a.f = P<const __nv_bfloat16>(f);
   a.qkv = P<__nv_bfloat16>(qkv);
   a.a_log = P<const float>(a_log);
@@ -692,6 +696,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kda_recurrent", &kda_recurrent);
   m.def("kda_gated_norm", &kda_gated_norm);
   m.def("kda_chunk", &kda_chunk);
+  m.def("kda_chunk_scratch_floats", [](int64_t max_rows, int64_t max_seqs, int64_t H, int64_t Dh) {
+    return g53_kda_chunk_scratch_floats((int)max_rows, (int)max_seqs, (int)H, (int)Dh);
+  });
   m.def("mla_prep", &mla_prep);
   m.def("rope_q", &rope_q);
   m.def("mla_decode", &mla_decode);

@@ -174,13 +174,16 @@ struct KdaArgs {
   int B, max_rows;                           // sequences, max rows of one sequence
   int R, H, Dh, taps, b_off;
   float lower, eps;
+  float* scr; int scr_slots;                 // chunked prefill: per-(chunk slot, head) records (kda_chunk.cu)
 };
 cudaError_t g53_kda_conv(const KdaArgs& a, cudaStream_t st);          // qkv = silu(conv(window ++ proj rows))
 cudaError_t g53_kda_recurrent(const KdaArgs& a, cudaStream_t st);     // per sequence: S_in -> S_out, o_raw
 cudaError_t g53_kda_gated_norm(const KdaArgs& a, cudaStream_t st);    // out = rmsnorm(o_raw) * w * sigmoid(gate)
 cudaError_t g53_kda_conv_commit(const KdaArgs& a, cudaStream_t st);   // window <- last taps-1 of window ++ nrows rows
-// chunked (64-token) form of g53_kda_recurrent for prefill: same inputs/outputs, per-sequence rows in chunks
+// chunked (64-token) form of g53_kda_recurrent for prefill: same inputs/outputs, per-sequence rows in chunks;
+// needs a.scr with g53_kda_chunk_scratch_floats(max_rows, max_seqs, H, Dh) floats (scr_slots = rows/64 + seqs + 1)
 cudaError_t g53_kda_chunk(const KdaArgs& a, cudaStream_t st);
+int64_t g53_kda_chunk_scratch_floats(int max_rows, int max_seqs, int H, int Dh);
 
 // ---------------------------------------------------------------- MLA / DSA (mla.cu, dsa.cu)
 struct MlaPrepArgs {

@@ -130,6 +130,12 @@ class Runtime:
             self.kf = torch.zeros(R, H * Dh, dtype=bf16, device=dev)
             self.kqkv = torch.zeros(R, C3, dtype=bf16, device=dev)
             self.kg = torch.zeros(R, H * Dh, dtype=bf16, device=dev)
+            # chunked prefill records per (64-row chunk slot, head): Q~, K~, K^ [64, Dh], T, P [64, 64], e^{G_C} [Dh]
+            # (slots = chunks of the longest launch + sequences + 1; layout in csrc/kda_chunk.cu)
+            self.kda_scr = None
+            if R > KDA_CHUNK_MIN_ROWS:
+                slots = (R + 63) // 64 + rc.max_seqs + 1
+                self.kda_scr = torch.empty(slots * H * (3 * 64 * Dh + 2 * 64 * 64 + Dh), dtype=f32, device=dev)
             self.ko = torch.zeros(R, H * Dh, dtype=f32, device=dev)
             self.kout = torch.zeros(R, H * Dh, dtype=bf16, device=dev)
         # --- MLA / DSA ---
@@ -373,7 +379,7 @@ class Runtime:
                              C3 + 2 * Dh, c.lower)
         else:       # prefill: 64-token chunked form of the same recurrence
             Kc.kda_chunk(proj, seq, fb, qkv, k.a_log, k.dt_bias, self.S_pool[li], self.ko[:R], H, Dh,
-                         C3 + 2 * Dh, c.lower)
+                         C3 + 2 * Dh, c.lower, self.kda_scr)
         Kc.kda_gated_norm(self.ko[:R], self.kg[:R], k.o_norm, self.kout[:R], H, Dh, c.eps)
         self._final_linear(self.kout[:R], k.o_proj, R)
 

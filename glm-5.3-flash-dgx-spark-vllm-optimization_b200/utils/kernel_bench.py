@@ -194,8 +194,11 @@ def bench_kda(args, T: Timer):
         S = torch.zeros(2, H, Dh, Dh, device="cuda")
         o = torch.empty(Tn, HD, device="cuda")
         seq = torch.tensor([[0], [Tn], [0], [1], [0]], dtype=torch.int32, device="cuda")
-        fn = K.C().kda_chunk if Tn > 32 else K.C().kda_recurrent
-        ms = T(lambda: fn(proj, seq, f, qkv, a_log, dt, S, o, H, Dh, 3 * HD + 2 * Dh, -5.0))
+        if Tn > 32:
+            scr = torch.empty(K.C().kda_chunk_scratch_floats(Tn, 1, H, Dh), device="cuda")
+            ms = T(lambda: K.C().kda_chunk(proj, seq, f, qkv, a_log, dt, S, o, H, Dh, 3 * HD + 2 * Dh, -5.0, scr))
+        else:
+            ms = T(lambda: K.C().kda_recurrent(proj, seq, f, qkv, a_log, dt, S, o, H, Dh, 3 * HD + 2 * Dh, -5.0))
         emit({"case": "kda_chunk" if Tn > 32 else "kda_recurrent", "rows": Tn, "heads": H, "ms": ms,
               "tokens_per_s": Tn / ms * 1e3})
 

@@ -21,8 +21,15 @@ def _inputs(T, H, Dh, seed):
     return proj, qkv, f, a_log, dt_bias, 3 * HD + 2 * Dh
 
 
+def _close(a, b, rel=4e-3, abs_=3e-2):
+    """tf32 tensor-core products in the chunked scan against the fp32 recurrent kernel"""
+    err = (a - b).float()
+    assert err.norm() <= rel * b.float().norm() + 1e-6, (err.norm().item(), b.norm().item())
+    assert err.abs().max().item() <= abs_
+
+
 @pytest.mark.parametrize("Dh", [64, 128])
-@pytest.mark.parametrize("T", [64, 200])
+@pytest.mark.parametrize("T", [64, 200, 1000])
 def test_kda_chunk_matches_recurrent(Dh, T):
     from glm53.ops import kernels as Kk
     C = Kk.C()
@@ -36,9 +43,33 @@ def test_kda_chunk_matches_recurrent(Dh, T):
     C.kda_recurrent(proj, seq, f, qkv, a_log, dt_bias, S, o1, H, Dh, b_off, -5.0)
     seq2 = torch.tensor([[0], [T], [0], [3], [0]], dtype=torch.int32, device=DEV)
     o2 = torch.zeros(T, H * Dh, device=DEV)
-    C.kda_chunk(proj, seq2, f, qkv, a_log, dt_bias, S, o2, H, Dh, b_off, -5.0)
-    torch.testing.assert_close(o2, o1, atol=2e-3, rtol=2e-3)
-    torch.testing.assert_close(S[3], S[1], atol=2e-3, rtol=2e-3)
+    scr = torch.empty(C.kda_chunk_scratch_floats(T, 1, H, Dh), device=DEV)
+    C.kda_chunk(proj, seq2, f, qkv, a_log, dt_bias, S, o2, H, Dh, b_off, -5.0, scr)
+    _close(o2, o1)
+    _close(S[3], S[1])
+
+
+def test_kda_chunk_two_sequences_unaligned():
+    """Two sequences in one chunked launch, the second starting at a row that is not a multiple of 64."""
+    from glm53.ops import kernels as Kk
+    C = Kk.C()
+    H, Dh = 4, 128
+    n0, n1 = 150, 230
+    T = n0 + n1
+    proj, qkv, f, a_log, dt_bias, b_off = _inputs(T, H, Dh, 5)
+    S = torch.randn(8, H, Dh, Dh, device=DEV) * 0.1
+    o_ref = torch.zeros(T, H * Dh, device=DEV)
+    S_ref = S.clone()
+    for row0, n, si, so in [(0, n0, 0, 1), (n0, n1, 2, 3)]:
+        sq = torch.tensor([[row0], [n], [si], [so], [0]], dtype=torch.int32, device=DEV)
+        C.kda_recurrent(proj, sq, f, qkv, a_log, dt_bias, S_ref, o_ref, H, Dh, b_off, -5.0)
+    seq = torch.tensor([[0, n0], [n0, n1], [0, 2], [5, 7], [0, 1]], dtype=torch.int32, device=DEV)
+    o = torch.zeros(T, H * Dh, device=DEV)
+    scr = torch.empty(C.kda_chunk_scratch_floats(T, 2, H, Dh), device=DEV)
+    C.kda_chunk(proj, seq, f, qkv, a_log, dt_bias, S, o, H, Dh, b_off, -5.0, scr)
+    _close(o, o_ref)
+    _close(S[5], S_ref[1])
+    _close(S[7], S_ref[3])
 
 
 def test_kda_multi_sequence_and_replay():
