@@ -1,3 +1,4 @@
+#include <cstdlib>
 // Python bindings of the glm53 CUDA kernels (torch tensors -> raw pointers; launches on the current stream).
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -615,6 +616,29 @@ void dsa_update(const Tensor& iproj, const Tensor& ln_w, const Tensor& ln_b, con
   check(g53_dsa_update(a, stream()), "dsa_update");
 }
 
+// the tcgen05 indexer logits are used unless GLM53_TC_DSA=0
+static bool tc_dsa_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("GLM53_TC_DSA");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// logits only (tests and benchmarks): tensor-core or CUDA-core kernel
+void dsa_logits(const Tensor& iproj, const Tensor& qi, const Tensor& ln_w, const Tensor& pool_cache,
+                const Tensor& pool_scale, const Tensor& positions, const Tensor& block_table, const Tensor& row_seq,
+                int64_t block_size, int64_t IH, int64_t kpool, const Tensor& logits, bool tensor_cores) {
+  DsaArgs a = dsa_args(iproj, ln_w, ln_w, ln_w, qi, pool_cache, pool_scale, pool_cache, pool_scale, positions,
+                       positions, block_table, row_seq, block_size, IH, kpool, 0, 0, logits, {}, {});
+  a.ik_cache = nullptr;
+  a.ig_cache = nullptr;
+  a.err = P<int>(err_word(logits));
+  if (tensor_cores) check(g53_dsa_logits_tc(a, stream()), "dsa_logits_tc");
+  else check(g53_dsa_logits(a, stream()), "dsa_logits");
+}
+
 void dsa_select(const Tensor& iproj, const Tensor& qi, const Tensor& ln_w, const Tensor& pool_cache,
                 const Tensor& pool_scale, const Tensor& positions, const Tensor& block_table, const Tensor& row_seq,
                 int64_t block_size, int64_t IH, int64_t kpool, int64_t topk_pools, const Tensor& logits,
@@ -623,7 +647,12 @@ void dsa_select(const Tensor& iproj, const Tensor& qi, const Tensor& ln_w, const
                        positions, block_table, row_seq, block_size, IH, kpool, topk_pools, 0, logits, sel, sel_count);
   a.ik_cache = nullptr;
   a.ig_cache = nullptr;
-  check(g53_dsa_logits(a, stream()), "dsa_logits");
+  a.err = P<int>(err_word(logits));
+  // tcgen05 logits where the head count fits the kernel (IH | 32, ID = 128); the CUDA-core kernel otherwise
+  if (tc_dsa_enabled() && g53_dsa_logits_tc(a, stream()) == cudaSuccess) {
+  } else {
+    check(g53_dsa_logits(a, stream()), "dsa_logits");
+  }
   check(g53_dsa_select(a, stream()), "dsa_select");
 }
 
@@ -696,6 +725,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kda_recurrent", &kda_recurrent);
   m.def("kda_gated_norm", &kda_gated_norm);
   m.def("kda_chunk", &kda_chunk);
+  m.def("dsa_logits", &dsa_logits);
   m.def("kda_chunk_scratch_floats", [](int64_t max_rows, int64_t max_seqs, int64_t H, int64_t Dh) {
     return g53_kda_chunk_scratch_floats((int)max_rows, (int)max_seqs, (int)H, (int)Dh);
   });

@@ -235,9 +235,11 @@ struct DsaArgs {
   float* logits;                 // [R, max_pools] scratch
   int max_pools;
   int* sel; int* sel_count; int max_sel;   // out: selected token slots per row
+  int* err;                      // device error word (bounded waits of the tensor-core logits kernel)
 };
 cudaError_t g53_dsa_update(const DsaArgs& a, cudaStream_t st);   // index keys, gate scores, completed pools
-cudaError_t g53_dsa_logits(const DsaArgs& a, cudaStream_t st);  // pool logits of every row
+cudaError_t g53_dsa_logits(const DsaArgs& a, cudaStream_t st);  // pool logits of every row (CUDA cores)
+cudaError_t g53_dsa_logits_tc(const DsaArgs& a, cudaStream_t st);   // same on tcgen05 (dsa_tc.cu)
 cudaError_t g53_dsa_select(const DsaArgs& a, cudaStream_t st);
 
 // ---------------------------------------------------------------- sampling / verify (sample.cu)
