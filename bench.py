@@ -39,7 +39,8 @@ REFERENCE_UNAVAILABLE = ("the reference is a vLLM plugin/overlay kit for an arm6
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms; only the samples taken between mark() and stop()
+    (the timed region) are reported (at least the first sample after mark(), for very short regions)."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -49,26 +50,43 @@ class ClockSampler:
         self.idx = gpu_index
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         self.proc = None
+        self.n0 = 0
+
+    def _lines(self) -> list[str]:
+        self.file.flush()
+        with open(self.file.name) as f:
+            return [l.strip() for l in f.read().splitlines() if l.strip()]
 
     def start(self):
+        """Start sampling and wait (at most 3 s) until the first sample is written."""
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.idx), "-lms", "200"], stdout=self.file,
+                                          "-i", str(self.idx), "-lms", "50"], stdout=self.file,
                                          stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 3.0 and not self._lines():
+            time.sleep(0.02)
+
+    def mark(self):
+        """The timed region starts now."""
+        if self.proc is not None:
+            self.n0 = len(self._lines())
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        t0 = time.time()
+        while time.time() - t0 < 1.0 and len(self._lines()) <= self.n0:
+            time.sleep(0.01)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        self.file.flush()
-        self.file.seek(0)
-        rows = [l.strip().split(", ") for l in self.file.read().splitlines() if l.strip()]
+        rows = [l.split(", ") for l in self._lines()[self.n0:]]
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
@@ -175,6 +193,8 @@ def main():
     n_tok0 = len(req.output)
     clocks = ClockSampler(local)
     clocks.start()
+    barrier_sync()
+    clocks.mark()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     wall0 = time.perf_counter()
     e0.record(stream)
