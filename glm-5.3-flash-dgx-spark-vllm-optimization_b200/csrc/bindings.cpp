@@ -252,6 +252,97 @@ void exl3_moe(const Tensor& x, const Tensor& tr_g, const Tensor& suh_g, const Te
   check(g53_exl3_down(a, stream()), "exl3_down");
 }
 
+// Expert-parallel MoE step (ep_moe.cu): dispatch -> plan -> rot_in -> gate_up -> down (epilogue stores into the
+// sources' combine rows) -> combine.  `peer` int64 [6, world] (device): addresses on every rank of recv_x, recv_meta,
+// recv_cnt, disp_flag[p][rank], comb, comb_flag[p][rank]; `local` int64 [6] (host): this rank's disp_flag[p],
+// comb_flag[p], recv_cnt, recv_meta, comb, recv_x of parity p; `state` int32 [16] (device, parity p): counters
+// (0 dispatch, 1 down, 2 combine), 3 pair count, 4 received rows, 5 epoch, 8 error code.
+void ep_moe_step(const Tensor& x, const Tensor& out, const Tensor& pair_token, const Tensor& pair_expert,
+                 const Tensor& pair_w, const Tensor& pair_of, const Tensor& tr_g, const Tensor& suh_g,
+                 const Tensor& svh_g, const Tensor& tr_u, const Tensor& suh_u, const Tensor& svh_u, const Tensor& tr_d,
+                 const Tensor& suh_d, const Tensor& svh_d, const Tensor& peer, const Tensor& local, const Tensor& state,
+                 const Tensor& seg, const Tensor& groups, const Tensor& rp_i, const Tensor& rp_w, const Tensor& rp_out,
+                 const Tensor& xh_g, const Tensor& xh_u, const Tensor& xd, int64_t El, int64_t rank, int64_t world,
+                 int64_t cap, int64_t recv_cap, int64_t top_k, double limit, bool tensor_core_experts) {
+  const int T = (int)x.size(0), K = (int)x.size(1), W = (int)world;
+  TORCH_CHECK(peer.dim() == 2 && peer.size(0) == 6 && peer.size(1) == W && peer.scalar_type() == at::kLong);
+  TORCH_CHECK(local.device().is_cpu() && local.numel() == 6 && local.scalar_type() == at::kLong);
+  TORCH_CHECK(state.numel() >= 16 && state.scalar_type() == at::kInt);
+  TORCH_CHECK(T * top_k <= cap && W * El <= 1024 && out.scalar_type() == at::kFloat);
+  TORCH_CHECK(xh_g.numel() >= recv_cap * 2 * K && xd.numel() >= recv_cap * 2 * svh_g.size(-1), "EP scratch");
+  const int64_t* pp = P<const int64_t>(peer);
+  const int64_t* lp = local.data_ptr<int64_t>();
+  int* st = P<int>(state);
+  EpArgs e{};
+  e.n_pairs = st + 3;
+  e.pair_token = P<const int>(pair_token); e.pair_expert = P<const int>(pair_expert); e.pair_w = P<const float>(pair_w);
+  e.x = P<const __nv_bfloat16>(x); e.ldx = x.stride(0);
+  e.K = K; e.El = (int)El; e.rank = (int)rank; e.world = W; e.cap = (int)cap; e.recv_cap = (int)recv_cap;
+  e.recv_x = pp; e.recv_meta = pp + W; e.recv_cnt = pp + 2 * W; e.disp_flags = pp + 3 * W; e.comb = pp + 4 * W;
+  e.done = reinterpret_cast<unsigned*>(st + 0); e.done2 = reinterpret_cast<unsigned*>(st + 2);
+  e.epoch = reinterpret_cast<unsigned*>(st + 5);
+  e.err = st + 8;
+  e.my_disp_flags = reinterpret_cast<const unsigned*>(lp[0]);
+  e.my_comb_flags = reinterpret_cast<const unsigned*>(lp[1]);
+  e.my_cnt = reinterpret_cast<const int*>(lp[2]);
+  e.my_meta = reinterpret_cast<const void*>(lp[3]);
+  e.my_comb = reinterpret_cast<const float*>(lp[4]);
+  int* sg = P<int>(seg);
+  e.seg_base = sg; e.seg_cnt = sg + W * El; e.seg_src = sg + 2 * W * El;
+  e.n_recv = st + 4;
+  int* gr = P<int>(groups);
+  e.group_count = gr; e.group_expert = gr + 1; e.group_offset = gr + 1 + El;
+  e.rp_token = P<int>(rp_i); e.rp_expert = P<int>(rp_i) + recv_cap; e.rp_w = P<float>(rp_w);
+  e.rp_out = P<int64_t>(rp_out);
+  cudaStream_t s = stream();
+  // state[3] holds this step's pair count (T * top_k), set by the caller
+  check(g53_ep_dispatch(e, (int)(T * top_k), s), "ep_dispatch");
+  check(g53_ep_plan(e, s), "ep_plan");
+  Exl3Args a{};
+  a.x = reinterpret_cast<const __nv_bfloat16*>(lp[5]); a.ldx = K;
+  a.tr_g = P<const int16_t>(tr_g); a.suh_g = P<const __half>(suh_g); a.svh_g = P<const __half>(svh_g);
+  a.tr_u = P<const int16_t>(tr_u); a.suh_u = P<const __half>(suh_u); a.svh_u = P<const __half>(svh_u);
+  a.tr_d = P<const int16_t>(tr_d); a.suh_d = P<const __half>(suh_d); a.svh_d = P<const __half>(svh_d);
+  a.K = K; a.N = (int)svh_g.size(-1); a.Dout = (int)svh_d.size(-1);
+  a.group_count = e.group_count; a.group_expert = e.group_expert; a.group_offset = e.group_offset;
+  a.pair_token = e.rp_token; a.pair_expert = e.rp_expert; a.pair_w = e.rp_w;
+  a.max_groups = (int)El; a.pairs = (int)recv_cap; a.limit = (float)limit;
+  a.xh_g = P<__half>(xh_g); a.xh_u = P<__half>(xh_u); a.xd = P<__half>(xd); a.yd = nullptr;
+  a.decode_layout = tensor_core_experts ? 0 : 1;
+  a.pair_count = e.n_recv;
+  // the receiver's group count is only known on the device: bounded grid rows, CTAs stride over the groups
+  a.launch_groups = (int)std::min<int64_t>(El, std::max<int64_t>(8, (int64_t)W * T * top_k));
+  check(g53_exl3_rot_in(a, s), "ep rot_in");
+  if (!tensor_core_experts) {
+    // few rows per expert: trellis decoded in registers (mma.sync)
+    check(g53_exl3_gate_up(a, s), "ep gate_up");
+    a.out_ptrs = e.rp_out;
+    a.done = reinterpret_cast<unsigned*>(st + 1);
+    a.push_flags = pp + 5 * W;
+    a.push_world = W;
+    check(g53_exl3_down(a, s), "ep down");
+  } else {
+    // many rows per expert: tcgen05 grouped GEMMs with the trellis decoded into shared memory
+    MoePrefillArgs q{};
+    q.tr0 = a.tr_g; q.tr1 = a.tr_u; q.svh0 = a.svh_g; q.svh1 = a.svh_u; q.suh_next = a.suh_d;
+    q.group_count = e.group_count; q.group_expert = e.group_expert; q.group_offset = e.group_offset;
+    q.x0 = a.xh_g; q.x1 = a.xh_u; q.rows = recv_cap; q.K = K; q.N = a.N; q.max_groups = (int)El;
+    q.out = a.xd; q.limit = (float)limit; q.err = st + 8;
+    check(g53_moe_prefill(q, true, s), "ep moe_prefill gate_up");
+    MoePrefillArgs r{};
+    r.tr0 = a.tr_d; r.tr1 = a.tr_d; r.svh0 = a.svh_d; r.pair_w = e.rp_w;
+    r.group_count = e.group_count; r.group_expert = e.group_expert; r.group_offset = e.group_offset;
+    r.x0 = a.xd; r.rows = recv_cap; r.K = a.N; r.N = a.Dout; r.max_groups = (int)El;
+    r.out = nullptr; r.limit = (float)limit; r.err = st + 8;
+    r.out_ptrs = e.rp_out;
+    r.done = reinterpret_cast<unsigned*>(st + 1);
+    r.push_flags = pp + 5 * W;
+    r.push_world = W;
+    check(g53_moe_prefill(r, false, s), "ep moe_prefill down");
+  }
+  check(g53_ep_combine(e, P<const int>(pair_of), T, (int)top_k, P<float>(out), s), "ep_combine");
+}
+
 void exl3_rot_in(const Tensor& x, const Tensor& suh_g, const Tensor& suh_u, const Tensor& pair_token,
                  const Tensor& pair_expert, const Tensor& xh_g, const Tensor& xh_u) {
   Exl3Args a{};
@@ -711,6 +802,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route_large", &moe_route_large);
   m.def("moe_prefill", &moe_prefill);
   m.def("exl3_rot_in", &exl3_rot_in);
+  m.def("ep_moe_step", &ep_moe_step);
   m.def("exl3_unpack", &exl3_unpack);
   m.def("hc_post_pre", &hc_post_pre);
   m.def("hc_post_pre_tp", &hc_post_pre_tp);

@@ -88,9 +88,44 @@ struct Exl3Args {
   __half* xh_g; __half* xh_u;   // [pairs, K] rotated inputs
   __half* xd;                   // [pairs, N] rotated down input
   float* yd;                    // [pairs, Dout] weighted expert outputs
-  int decode_layout;            // 1: xh/xd rows in the decode fragment layout (moe.cu perm_k); 0: natural order
+  int decode_layout;            // 1: xh/xd rows in the decode fragment layout (moe.cu dup_word); 0: natural order
+  // expert parallelism (ep_moe.cu): device-side pair count for rot_in, and the down epilogue's per-pair output
+  // row addresses (peer memory) with the flags released by its last CTA
+  const int* pair_count;        // [1] or null
+  const int64_t* out_ptrs;      // [pairs] or null: output row of each pair (else yd)
+  unsigned* done;               // last-CTA counter (out_ptrs mode)
+  const int64_t* push_flags;    // [push_world] flag addresses released after the last CTA
+  int push_world;
+  int launch_groups;            // > 0: grid rows of the group loop (CTAs stride over the group table)
 };
 cudaError_t g53_exl3_rot_in(const Exl3Args& a, cudaStream_t st);
+// ---------------------------------------------------------------- expert parallelism (ep_moe.cu)
+struct EpArgs {
+  // source side (this step's sorted pairs and the peer buffers of parity p)
+  const int* n_pairs;                        // [1]
+  const int* pair_token; const int* pair_expert; const float* pair_w;
+  const __nv_bfloat16* x; int64_t ldx;
+  int K, El, rank, world, cap, recv_cap;
+  const int64_t* recv_x; const int64_t* recv_meta; const int64_t* recv_cnt;   // [world] peer addresses
+  const int64_t* disp_flags;                 // [world] address of disp_flag[p][rank] on each rank
+  const int64_t* comb;                       // [world] address of comb[p] on each rank
+  unsigned* done; unsigned* done2;           // local last-CTA counters
+  unsigned* epoch;                           // local epoch[p]
+  int* err;
+  // receiver side (this rank's buffers of parity p)
+  const unsigned* my_disp_flags;             // [world]
+  const unsigned* my_comb_flags;             // [world]
+  const int* my_cnt;                         // [world][El]
+  const void* my_meta;                       // int4 [world][cap]
+  const float* my_comb;                      // [cap][K]
+  int* seg_base; int* seg_cnt; int* seg_src;  // [world*El]
+  int* n_recv;
+  int* group_count; int* group_expert; int* group_offset;   // [1], [El], [El+1]
+  int* rp_token; int* rp_expert; float* rp_w; int64_t* rp_out;   // [recv_cap]
+};
+cudaError_t g53_ep_dispatch(const EpArgs& a, int max_pairs, cudaStream_t st);
+cudaError_t g53_ep_plan(const EpArgs& a, cudaStream_t st);
+cudaError_t g53_ep_combine(const EpArgs& a, const int* pair_of, int R, int top_k, float* out, cudaStream_t st);
 cudaError_t g53_exl3_gate_up(const Exl3Args& a, cudaStream_t st);
 cudaError_t g53_exl3_down(const Exl3Args& a, cudaStream_t st);
 // out[r, :] (+)= sum_k yd[pair_of[r, k], :]  (slot order), fp32
@@ -109,6 +144,8 @@ struct MoePrefillArgs {
   void* out;                                      // gate_up: f16 [rows, N] down input; down: f32 [rows, N]
   float limit;
   int* err;
+  // expert parallelism (down): per-row output addresses (peer memory) and the flags released by the last CTA
+  const int64_t* out_ptrs; unsigned* done; const int64_t* push_flags; int push_world;
 };
 cudaError_t g53_moe_prefill(const MoePrefillArgs& p, bool gate_up, cudaStream_t st);
 // scalable routing for prefill: per-row top-k, expert histogram, scan, scatter (positions within an expert in

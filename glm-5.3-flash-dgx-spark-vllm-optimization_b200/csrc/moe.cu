@@ -12,6 +12,7 @@
 // One CTA owns one full 128-column Hadamard block of one expert, so both output rotations stay on chip.
 // Reference counterparts: code/fork/kernels/exl3.cu:110 (grouped_kernel), :322 (rot_in), :371/:455 (epilogues),
 // :529/:582 (route_prep / route_ids).
+#include <algorithm>
 #include <cooperative_groups.h>
 #include "common.cuh"
 #include "launchers.h"
@@ -206,35 +207,37 @@ __device__ __forceinline__ void tile_mma(float (&c)[4], const uint32_t (&x)[8], 
 __global__ void __launch_bounds__(128) exl3_rot_in_kernel(Exl3Args a) {
   const int lane = threadIdx.x & 31;
   const int blk = blockIdx.y * 4 + (threadIdx.x >> 5);
-  const int p = blockIdx.x;                      // pairs on grid.x (prefill chunks exceed 65535 pairs)
   if (blk * 128 >= a.K) return;
-  const int r = a.pair_token[p], e = a.pair_expert[p];
-  const int c0 = blk * 128 + lane * 4;
-  const __nv_bfloat16* xr = a.x + (int64_t)r * a.ldx + c0;
-  float xv[4];
+  const int np = a.pair_count ? min(*a.pair_count, a.pairs) : a.pairs;
+  for (int p = blockIdx.x; p < np; p += gridDim.x) {   // pairs on grid.x (prefill chunks exceed 65535 pairs)
+    const int r = a.pair_token[p], e = a.pair_expert[p];
+    const int c0 = blk * 128 + lane * 4;
+    const __nv_bfloat16* xr = a.x + (int64_t)r * a.ldx + c0;
+    float xv[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) xv[i] = bf2f(xr[i]);
-  float g[4], u[4];
-  const __half* sg = a.suh_g + (int64_t)e * a.K + c0;
-  const __half* su = a.suh_u + (int64_t)e * a.K + c0;
+    for (int i = 0; i < 4; ++i) xv[i] = bf2f(xr[i]);
+    float g[4], u[4];
+    const __half* sg = a.suh_g + (int64_t)e * a.K + c0;
+    const __half* su = a.suh_u + (int64_t)e * a.K + c0;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) { g[i] = xv[i] * __half2float(sg[i]); u[i] = xv[i] * __half2float(su[i]); }
-  fwht128_warp(g);
-  fwht128_warp(u);
-  if (a.decode_layout) {                         // duplicated words (see dup_word); (k, k+1) are adjacent words
-    uint32_t* og = reinterpret_cast<uint32_t*>(a.xh_g) + (int64_t)p * a.K;
-    uint32_t* ou = reinterpret_cast<uint32_t*>(a.xh_u) + (int64_t)p * a.K;
-    const int w0 = dup_word(c0), w2 = dup_word(c0 + 2);
-    *reinterpret_cast<uint2*>(og + w0) = make_uint2(dup_half(g[0]), dup_half(g[1]));
-    *reinterpret_cast<uint2*>(og + w2) = make_uint2(dup_half(g[2]), dup_half(g[3]));
-    *reinterpret_cast<uint2*>(ou + w0) = make_uint2(dup_half(u[0]), dup_half(u[1]));
-    *reinterpret_cast<uint2*>(ou + w2) = make_uint2(dup_half(u[2]), dup_half(u[3]));
-    return;
+    for (int i = 0; i < 4; ++i) { g[i] = xv[i] * __half2float(sg[i]); u[i] = xv[i] * __half2float(su[i]); }
+    fwht128_warp(g);
+    fwht128_warp(u);
+    if (a.decode_layout) {                         // duplicated words (see dup_word); (k, k+1) are adjacent words
+      uint32_t* og = reinterpret_cast<uint32_t*>(a.xh_g) + (int64_t)p * a.K;
+      uint32_t* ou = reinterpret_cast<uint32_t*>(a.xh_u) + (int64_t)p * a.K;
+      const int w0 = dup_word(c0), w2 = dup_word(c0 + 2);
+      *reinterpret_cast<uint2*>(og + w0) = make_uint2(dup_half(g[0]), dup_half(g[1]));
+      *reinterpret_cast<uint2*>(og + w2) = make_uint2(dup_half(g[2]), dup_half(g[3]));
+      *reinterpret_cast<uint2*>(ou + w0) = make_uint2(dup_half(u[0]), dup_half(u[1]));
+      *reinterpret_cast<uint2*>(ou + w2) = make_uint2(dup_half(u[2]), dup_half(u[3]));
+      continue;
+    }
+    __half2* og = reinterpret_cast<__half2*>(a.xh_g + (int64_t)p * a.K + c0);
+    __half2* ou = reinterpret_cast<__half2*>(a.xh_u + (int64_t)p * a.K + c0);
+    og[0] = __floats2half2_rn(g[0], g[1]); og[1] = __floats2half2_rn(g[2], g[3]);
+    ou[0] = __floats2half2_rn(u[0], u[1]); ou[1] = __floats2half2_rn(u[2], u[3]);
   }
-  __half2* og = reinterpret_cast<__half2*>(a.xh_g + (int64_t)p * a.K + c0);
-  __half2* ou = reinterpret_cast<__half2*>(a.xh_u + (int64_t)p * a.K + c0);
-  og[0] = __floats2half2_rn(g[0], g[1]); og[1] = __floats2half2_rn(g[2], g[3]);
-  ou[0] = __floats2half2_rn(u[0], u[1]); ou[1] = __floats2half2_rn(u[2], u[3]);
 }
 
 // accumulator (16 features x 8 tokens) of one warp's n-tile -> z[token][feature]
@@ -278,11 +281,7 @@ __device__ __forceinline__ void cluster_release() {
 // larger groups decode the trellis again for every further 8 tokens.
 // ---------------------------------------------------------------------------------------------------------------
 template <int KSPL>
-__global__ void __launch_bounds__(256, 4) exl3_gate_up_kernel(Exl3Args a) {
-  const int u = blockIdx.y;
-  if (u >= a.group_count[0] || u >= a.max_groups) return;
-  __shared__ float zg[8][132];
-  __shared__ float zu[8][132];
+__device__ __forceinline__ void gate_up_group(const Exl3Args& a, int u, float (*zg)[132], float (*zu)[132]) {
   const int e = a.group_expert[u];
   const int p0 = a.group_offset[u];
   const int np = a.group_offset[u + 1] - p0;
@@ -361,15 +360,36 @@ __global__ void __launch_bounds__(256, 4) exl3_gate_up_kernel(Exl3Args a) {
   }
 }
 
+// CTAs loop over the groups (grid.y may be smaller than the group table: a decode window routes to few experts)
+template <int KSPL>
+__global__ void __launch_bounds__(256, 4) exl3_gate_up_kernel(Exl3Args a) {
+  __shared__ float zg[8][132];
+  __shared__ float zu[8][132];
+  const int ng = min(a.group_count[0], a.max_groups);
+  for (int u = blockIdx.y; u < ng; u += gridDim.y) gate_up_group<KSPL>(a, u, zg, zu);
+}
+
+// expert parallelism: the last CTA of the down kernel (all pair rows stored into the sources' combine buffers and
+// made visible system-wide) releases one flag on every source rank
+__device__ __forceinline__ void ep_count_in(const Exl3Args& a) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned prev = atomicAdd(a.done, 1u);
+    if (prev == gridDim.x * gridDim.y * gridDim.z - 1) {
+      *a.done = 0u;
+      __threadfence_system();
+      for (int s = 0; s < a.push_world; ++s) red_release_sys_add(reinterpret_cast<unsigned*>(a.push_flags[s]), 1u);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // down: grid (Dout/128, max_groups, KSPL) with K split over a cluster as in gate_up; epilogue H128, * svh,
 // * routing weight -> yd[pair] fp32
 // ---------------------------------------------------------------------------------------------------------------
 template <int KSPL>
-__global__ void __launch_bounds__(256) exl3_down_kernel(Exl3Args a) {   // KSPL in {1, 2}
-  const int u = blockIdx.y;
-  if (u >= a.group_count[0] || u >= a.max_groups) return;
-  __shared__ float zd[8][132];
+__device__ __forceinline__ void down_group(const Exl3Args& a, int u, float (*zd)[132]) {   // KSPL in {1, 2}
   const int e = a.group_expert[u];
   const int p0 = a.group_offset[u];
   const int np = a.group_offset[u + 1] - p0;
@@ -422,11 +442,21 @@ __global__ void __launch_bounds__(256) exl3_down_kernel(Exl3Args a) {   // KSPL 
       o.y = v[1] * __half2float(a.svh_d[(int64_t)e * a.Dout + col + 1]) * w;
       o.z = v[2] * __half2float(a.svh_d[(int64_t)e * a.Dout + col + 2]) * w;
       o.w = v[3] * __half2float(a.svh_d[(int64_t)e * a.Dout + col + 3]) * w;
-      *reinterpret_cast<float4*>(a.yd + (int64_t)(p0 + m0 + r) * a.Dout + col) = o;
+      float* dst = a.out_ptrs ? reinterpret_cast<float*>(a.out_ptrs[p0 + m0 + r])     // the source's combine row
+                              : a.yd + (int64_t)(p0 + m0 + r) * a.Dout;
+      *reinterpret_cast<float4*>(dst + col) = o;
     }
     cluster_release<KSPL>();
     __syncthreads();
   }
+}
+
+template <int KSPL>
+__global__ void __launch_bounds__(256) exl3_down_kernel(Exl3Args a) {
+  __shared__ float zd[8][132];
+  const int ng = min(a.group_count[0], a.max_groups);
+  for (int u = blockIdx.y; u < ng; u += gridDim.y) down_group<KSPL>(a, u, zd);
+  if (a.out_ptrs) ep_count_in(a);                   // expert parallelism: every CTA counts towards the release
 }
 
 __global__ void moe_combine_kernel(const float* yd, const int* pair_of, int R, int top_k, int D, float* out,
@@ -475,7 +505,8 @@ cudaError_t g53_moe_route(const RouteArgs& a, cudaStream_t st) {
 }
 
 cudaError_t g53_exl3_rot_in(const Exl3Args& a, cudaStream_t st) {
-  dim3 grid(a.pairs, (a.K / 128 + 3) / 4);
+  // device-side pair count (expert parallelism): a bounded grid strides over the rows that arrived
+  dim3 grid(a.pair_count ? std::min(a.pairs, 1184) : a.pairs, (a.K / 128 + 3) / 4);
   exl3_rot_in_kernel<<<grid, 128, 0, st>>>(a);
   G53_CHECK_LAUNCH();
   return cudaSuccess;
@@ -507,7 +538,7 @@ static int pick_split(int kc) { return kc % 4 == 0 ? 4 : kc % 2 == 0 ? 2 : 1; }
 
 cudaError_t g53_exl3_gate_up(const Exl3Args& a, cudaStream_t st) {
   if (a.K % 128 || a.N % 128 || !a.decode_layout) return cudaErrorInvalidValue;
-  const dim3 grid(a.N / 128, a.max_groups);
+  const dim3 grid(a.N / 128, a.launch_groups > 0 ? std::min(a.launch_groups, a.max_groups) : a.max_groups);
   switch (pick_split(a.K / 64)) {
     case 4: return launch_split<4>(exl3_gate_up_kernel<4>, grid, a, st);
     case 2: return launch_split<2>(exl3_gate_up_kernel<2>, grid, a, st);
@@ -517,7 +548,8 @@ cudaError_t g53_exl3_gate_up(const Exl3Args& a, cudaStream_t st) {
 
 cudaError_t g53_exl3_down(const Exl3Args& a, cudaStream_t st) {
   if (a.Dout % 128 || a.N % 64 || !a.decode_layout) return cudaErrorInvalidValue;
-  const dim3 grid(a.Dout / 128, a.max_groups);
+  const dim3 grid(a.Dout / 128, a.launch_groups > 0 ? std::min(a.launch_groups, a.max_groups) : a.max_groups);
+  if (a.out_ptrs) return launch_split<1>(exl3_down_kernel<1>, grid, a, st);
   // the down grid is already twice the gate_up grid (Dout = 2 N at TP=1); split only short-K tensor shards
   const int kc = a.N / 64;
   if (kc >= 16 || kc % 2) return launch_split<1>(exl3_down_kernel<1>, grid, a, st);

@@ -118,6 +118,21 @@ __device__ __forceinline__ uint32_t sw_off(int row, int k) {
   return (uint32_t)(row * 128 + ((((k * 2) >> 4) ^ (row & 7)) << 4) + ((k * 2) & 15));
 }
 
+// expert parallelism: the last CTA of the down launch (every output row stored into the source ranks' combine
+// buffers and made visible system-wide) releases one flag on every source rank
+__device__ __forceinline__ void ep_count_in(const MoePrefillArgs& p) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned prev = atomicAdd(p.done, 1u);
+    if (prev == gridDim.x * gridDim.y * gridDim.z - 1) {
+      *p.done = 0u;
+      __threadfence_system();
+      for (int s = 0; s < p.push_world; ++s) red_release_sys_add(reinterpret_cast<unsigned*>(p.push_flags[s]), 1u);
+    }
+  }
+}
+
 template <bool GU>
 __global__ void __launch_bounds__(kThreads, 1) moe_prefill_kernel(const __grid_constant__ CUtensorMap tb0,
                                                                   const __grid_constant__ CUtensorMap tb1,
@@ -134,7 +149,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_prefill_kernel(const __grid_c
   __shared__ volatile int fail;
 
   const int u = blockIdx.y;
-  if (u >= p.group_count[0] || u >= p.max_groups) return;
+  if (u >= p.group_count[0] || u >= p.max_groups) {
+    if (!GU && p.out_ptrs) ep_count_in(p);          // expert parallelism: every CTA counts towards the release
+    return;
+  }
   const int e = p.group_expert[u];
   const int p0 = p.group_offset[u];
   const int np = p.group_offset[u + 1] - p0;
@@ -276,7 +294,9 @@ __global__ void __launch_bounds__(kThreads, 1) moe_prefill_kernel(const __grid_c
             o.y = v[1] * __half2float(p.svh0[(int64_t)e * p.N + col + 1]) * w;
             o.z = v[2] * __half2float(p.svh0[(int64_t)e * p.N + col + 2]) * w;
             o.w = v[3] * __half2float(p.svh0[(int64_t)e * p.N + col + 3]) * w;
-            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (int64_t)pr * p.N + col) = o;
+            float* dst = p.out_ptrs ? reinterpret_cast<float*>(p.out_ptrs[pr])       // the source rank's row
+                                    : reinterpret_cast<float*>(p.out) + (int64_t)pr * p.N;
+            *reinterpret_cast<float4*>(dst + col) = o;
           }
         }
         named_sync(1, kDecWarps * 32);
@@ -351,6 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1) moe_prefill_kernel(const __grid_c
   if (warp == kDecWarps + 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(NM * kNmax)));
   }
+  if (!GU && p.out_ptrs) ep_count_in(p);
 }
 
 }  // namespace mp

@@ -4,6 +4,8 @@ the time and the achieved rate against the measured peaks (MEASURED_PEAKS.json w
 
   python -m glm53.utils.kernel_bench moe --tokens 1 8 64 512 8192 [--tp 1]      (BASELINE configs[1])
   python -m glm53.utils.kernel_bench gemv|gemm|kda|mla|all
+  torchrun --nproc-per-node N -m glm53.utils.kernel_bench ep --tokens 1 8 64 512   (experts
+      EP-sharded over N GPUs, tokens per rank; dispatch/combine fused into the kernels)
   --iters 1 --warmup 1 makes a case small enough to capture under ncu
 """
 
@@ -222,9 +224,70 @@ def bench_mla(args, T: Timer):
         emit({"case": "mla_sparse_attn", "rows": R, "heads": H, "keys": 2048, "ms": ms, "tflops": fl / ms / 1e9})
 
 
+def bench_ep(args, T: Timer):
+    """One routed-MoE layer, experts sharded over the ranks; per step: route -> dispatch (peer stores) -> expert
+    GEMMs -> combine (peer stores from the down epilogue) -> slot-ordered sum.  Time = max over ranks of the CUDA
+    event time per step; roofline = slower of the expert-weight bytes at measured HBM bandwidth and the bytes a
+    rank sends over NVLink (dispatch bf16 rows + combine fp32 rows to other ranks) at 770 GB/s per direction."""
+    import torch.distributed as dist
+    from glm53 import full_config
+    from glm53.models import weights as W
+    from glm53.parallel import dist as D
+    from glm53.parallel.ep import EPMoE, local_experts
+    rank, local, world = D.init(timeout_s=120)
+    cfg = full_config(layers=4)
+    dev = torch.device("cuda", local)
+    src = W.RandomSource(cfg, seed=0, device=dev)
+    li = next(i for i, m in enumerate(cfg.mlp_kinds) if m == "moe") if hasattr(cfg, "mlp_kinds") else 3
+    stacks = {p: src.experts(li, p, cfg.experts) for p in ("gate_proj", "up_proj", "down_proj")}
+    g = torch.Generator(device=dev).manual_seed(7)
+    router = (torch.randn(cfg.experts, cfg.hidden, generator=g, device=dev) / math.sqrt(cfg.hidden)).to(torch.bfloat16)
+    bias = torch.zeros(cfg.experts, device=dev)
+    ep = EPMoE(cfg, router, bias, local_experts(stacks["gate_proj"], rank, world),
+               local_experts(stacks["up_proj"], rank, world), local_experts(stacks["down_proj"], rank, world),
+               max_tokens=max(args.tokens), rank=rank, world=world)
+    del stacks
+    hbm, _ = peaks()
+    gx = torch.Generator(device=dev).manual_seed(100 + rank)
+    for Tn in args.tokens:
+        x = torch.randn(Tn, cfg.hidden, generator=gx, device=dev).to(torch.bfloat16)
+        for _ in range(args.warmup):
+            ep.forward(x)
+        torch.cuda.synchronize()
+        ep.x_ex.check()
+        dist.barrier() if world > 1 else None
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.iters):
+            ep.forward(x)
+        e1.record()
+        torch.cuda.synchronize()
+        ep.x_ex.check()
+        ms = e0.elapsed_time(e1) / args.iters
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+        P = Tn * cfg.top_k
+        # distinct local experts hit (expected, uniform routing over all ranks' tokens)
+        E, El = cfg.experts, cfg.experts // world
+        hits = El * (1 - (1 - 1 / E) ** (P * world))
+        w_bytes = hits * 3 * cfg.hidden * cfg.moe_width * cfg.bits / 8
+        nv_bytes = P * (world - 1) / world * cfg.hidden * (2 + 4)
+        roof_ms = max(w_bytes / (hbm * 1e6), nv_bytes / (770.0 * 1e6))
+        if rank == 0:
+            emit({"case": "ep_moe_layer", "world": world, "tokens_per_rank": Tn, "ms": ms,
+                  "tokens_per_s": Tn * world / ms * 1e3, "path": "tcgen05" if ep.tensor_core_experts(Tn) else
+                  "register-decode", "hbm_weight_bytes": w_bytes, "nvlink_bytes_per_rank": nv_bytes,
+                  "roofline_ms": roof_ms, "frac_of_roofline": roof_ms / ms})
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["moe", "gemv", "gemm", "kda", "mla", "all"])
+    ap.add_argument("case", choices=["moe", "gemv", "gemm", "kda", "mla", "ep", "all"])
     ap.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 64, 512, 8192])
     ap.add_argument("--rows", type=int, nargs="+", default=[8])
     ap.add_argument("--kda-rows", type=int, nargs="+", default=[8, 8192])

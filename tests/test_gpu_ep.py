@@ -1,0 +1,118 @@
+"""Expert-parallel MoE with the dispatch / combine inside the kernels: one GPU (world 1: every exchange goes
+through the rank's own buffers) against the single-GPU MoE path, and two GPUs (each rank's tokens against the
+full MoE computed locally with all experts) when the box has them (GPU only)."""
+
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _moe_ref(cfg, w, x):
+    """The single-GPU decode MoE (routing + EXL3 gate/up/down + slot-ordered combine) over all experts."""
+    from glm53.ops import kernels as Kk
+    C = Kk.C()
+    T, tk, E, D = x.shape[0], cfg.top_k, cfg.experts, cfg.hidden
+    P = T * tk
+    G = min(P, E)
+    i32 = dict(dtype=torch.int32, device=DEV)
+    logits = torch.zeros(T, E, device=DEV)
+    Kk.linear_bf16(x, w.router, logits)
+    ids, tw = torch.zeros(T, tk, **i32), torch.zeros(T, tk, device=DEV)
+    gc, ge, go = torch.zeros(1, **i32), torch.zeros(G, **i32), torch.zeros(G + 1, **i32)
+    pt, pe, pw, po = torch.zeros(P, **i32), torch.zeros(P, **i32), torch.zeros(P, device=DEV), torch.zeros(P, **i32)
+    C.moe_route(logits, w.bias, tk, cfg.routed_scale, cfg.norm_topk, ids, tw, gc, ge, go, pt, pe, pw, po)
+    N = w.gate.n
+    xh_g = torch.zeros(2 * P, D, dtype=torch.float16, device=DEV)
+    xh_u = torch.zeros(2 * P, D, dtype=torch.float16, device=DEV)
+    xd = torch.zeros(2 * P, N, dtype=torch.float16, device=DEV)
+    yd = torch.zeros(P, D, device=DEV)
+    C.exl3_moe(x, w.gate.trellis, w.gate.suh, w.gate.svh, w.up.trellis, w.up.suh, w.up.svh, w.down.trellis,
+               w.down.suh, w.down.svh, gc, ge, go, pt, pe, pw, xh_g, xh_u, xd, yd, cfg.limit)
+    out = torch.zeros(T, D, device=DEV)
+    C.moe_combine(yd, po, tk, out, False)
+    return out
+
+
+def _layer(cfg, seed=0):
+    from glm53.models import weights as W
+    src = W.RandomSource(cfg, seed=seed, device=torch.device(DEV))
+    w = W.prepare(src, cfg, device=torch.device(DEV))
+    return next(lw.moe for lw in w.layers if lw.moe is not None)
+
+
+def test_ep_world1_matches_moe(tiny_cfg):
+    from glm53.parallel.ep import EPMoE, local_experts
+    cfg = tiny_cfg
+    m = _layer(cfg)
+    ep = EPMoE(cfg, m.router, m.bias, local_experts(m.gate, 0, 1), local_experts(m.up, 0, 1),
+               local_experts(m.down, 0, 1), max_tokens=40, rank=0, world=1)
+    g = torch.Generator(device=DEV).manual_seed(1)
+    for T in (1, 8, 37, 8):                               # several steps: both parities, epochs advance
+        # (37 tokens x top-4 over 16 experts = 9 rows per expert: the register-decode path; see below for tcgen05)
+        x = torch.randn(T, cfg.hidden, generator=g, device=DEV).to(torch.bfloat16)
+        out = ep.forward(x).clone()
+        ref = _moe_ref(cfg, m, x)
+        torch.cuda.synchronize()
+        ep.x_ex.check()
+        torch.testing.assert_close(out, ref, atol=1e-4, rtol=1e-4)
+
+
+def test_ep_world1_tensor_core_path(tiny_cfg):
+    """Enough rows per expert for the tcgen05 grouped GEMM path of the receiver."""
+    from glm53.parallel.ep import EPMoE, local_experts
+    cfg = tiny_cfg
+    m = _layer(cfg)
+    ep = EPMoE(cfg, m.router, m.bias, local_experts(m.gate, 0, 1), local_experts(m.up, 0, 1),
+               local_experts(m.down, 0, 1), max_tokens=200, rank=0, world=1)
+    g = torch.Generator(device=DEV).manual_seed(2)
+    x = torch.randn(200, cfg.hidden, generator=g, device=DEV).to(torch.bfloat16)
+    assert ep.tensor_core_experts(200)
+    out = ep.forward(x).clone()
+    ref = _moe_ref(cfg, m, x)
+    torch.cuda.synchronize()
+    ep.x_ex.check()
+    # the tcgen05 path rounds the decoded weights to f16 and sums the codebook halves once (the register path keeps
+    # them apart in fp32): compare with a relative tolerance
+    err = (out - ref).norm() / ref.norm()
+    assert err < 2e-3, err.item()
+
+
+def _worker(rank, world, port, result):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from glm53.config import tiny_config
+    from glm53.parallel import dist as D
+    from glm53.parallel.ep import EPMoE, local_experts
+    D.init(timeout_s=60)
+    try:
+        cfg = tiny_config()
+        m = _layer(cfg)
+        ep = EPMoE(cfg, m.router, m.bias, local_experts(m.gate, rank, world), local_experts(m.up, rank, world),
+                   local_experts(m.down, rank, world), max_tokens=32, rank=rank, world=world)
+        g = torch.Generator(device=DEV).manual_seed(100 + rank)
+        worst = 0.0
+        for T in (3, 16, 32, 1, 32):
+            x = torch.randn(T, cfg.hidden, generator=g, device=DEV).to(torch.bfloat16)
+            out = ep.forward(x).clone()
+            ref = _moe_ref(cfg, m, x)
+            torch.cuda.synchronize()
+            ep.x_ex.check()
+            worst = max(worst, ((out - ref).norm() / ref.norm().clamp_min(1e-6)).item())
+        dist.barrier()
+        result[rank] = worst
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_gpus():
+    import torch.multiprocessing as mp
+    mgr = mp.Manager()
+    result = mgr.dict()
+    mp.spawn(_worker, args=(2, 29533, result), nprocs=2, join=True)
+    assert len(result) == 2 and max(result.values()) < 2e-3, dict(result)
