@@ -143,6 +143,31 @@ void gemm_bf16(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor
   gemm_common(x, false, {}, w, scale, y, mode, limit);
 }
 
+// W8A16 GEMM whose fp32 output rows are also stored into every rank's receive slot (fused tensor-parallel
+// reduction at prefill; the consumer is hc_post_pre_tp)
+void gemm_w8a16_push(const Tensor& x, const Tensor& w, const Tensor& scale, const Tensor& y, int64_t mode,
+                     const Tensor& scratch, const Tensor& push_ptrs, const Tensor& push_flags, const Tensor& push_done,
+                     int64_t slot, int64_t rank, int64_t world) {
+  TORCH_CHECK(mode == GEMV_F32 || mode == GEMV_F32_ACC, "push needs an fp32 output mode");
+  TORCH_CHECK(x.dim() == 2 && y.is_contiguous() && y.stride(0) * y.size(0) <= slot);
+  TORCH_CHECK(scratch.scalar_type() == at::kBFloat16 && scratch.numel() >= w.numel(), "scratch too small");
+  check(g53_e4m3_to_bf16(P<const uint8_t>(w), w.numel(), P<__nv_bfloat16>(scratch), stream()), "e4m3_to_bf16");
+  auto wb = scratch.flatten().narrow(0, 0, w.numel()).view(w.sizes());
+  GemmArgs p{};
+  p.a = x.data_ptr(); p.lda = x.stride(0);
+  p.b = wb.data_ptr(); p.ldb = wb.stride(0);
+  p.b_scale = P<const float>(scale);
+  p.y = y.data_ptr(); p.ldy = y.stride(0);
+  p.M = (int)x.size(0); p.N = (int)w.size(0); p.K = (int)x.size(1);
+  p.mode = (int)mode; p.fp8 = 0;
+  p.err = P<int>(err_word(x));
+  p.push_ptrs = reinterpret_cast<float* const*>(push_ptrs.data_ptr());
+  p.push_flags = reinterpret_cast<unsigned* const*>(push_flags.data_ptr());
+  p.push_done = reinterpret_cast<unsigned*>(push_done.data_ptr());
+  p.push_slot = slot; p.push_rank = (int)rank; p.push_world = (int)world;
+  check(g53_gemm_sm100(p, stream()), "gemm_w8a16_push");
+}
+
 int64_t gemm_error(const Tensor& like) {
   auto& e = err_word(like);
   const int64_t v = e[0].item<int>();
@@ -796,6 +821,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16", &gemm_bf16);
   m.def("gemm_w8a16", &gemm_w8a16);
   m.def("gemm_error", &gemm_error);
+  m.def("gemm_w8a16_push", &gemm_w8a16_push);
   m.def("moe_route", &moe_route);
   m.def("exl3_moe", &exl3_moe);
   m.def("moe_combine", &moe_combine);

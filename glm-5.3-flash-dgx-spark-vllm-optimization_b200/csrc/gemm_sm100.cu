@@ -216,6 +216,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& p, void* ybase, cons
   }
   float* y = reinterpret_cast<float*>(ybase) + off;
   const bool acc = p.mode == GEMV_F32_ACC;
+  const int64_t poff = p.push_rank * p.push_slot + off;       // this rank's slot in every receive buffer
   if (full) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -226,14 +227,16 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& p, void* ybase, cons
         o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
       }
       reinterpret_cast<float4*>(y)[c] = o;
+      for (int j = 0; j < p.push_world; ++j) reinterpret_cast<float4*>(p.push_ptrs[j] + poff)[c] = o;
     }
   } else {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       if (nb + i >= p.N) break;
       const float val = v[i] * rs * sc[i];
-      if (acc) y[i] += val;
-      else y[i] = val;
+      const float o = acc ? y[i] + val : val;
+      y[i] = o;
+      for (int j = 0; j < p.push_world; ++j) p.push_ptrs[j][poff + i] = o;
     }
   }
 }
@@ -367,6 +370,16 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+  if (p.push_world > 0 && threadIdx.x == 0) {
+    // every row of this CTA is stored in the peers' slots: count in; the last CTA releases the flags
+    __threadfence_system();
+    const unsigned prev = atomicAdd(p.push_done, 1u);
+    if (prev == gridDim.x - 1) {
+      *p.push_done = 0u;
+      __threadfence_system();
+      for (int j = 0; j < p.push_world; ++j) red_release_sys_add(p.push_flags[j] + p.push_rank, 1u);
+    }
   }
 }
 

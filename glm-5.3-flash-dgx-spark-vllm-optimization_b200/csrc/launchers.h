@@ -44,6 +44,10 @@ struct GemmArgs {
   // batched GEMM (e.g. per attention head): batch strides in elements of A, B, Y and of b_scale
   int batch;                           // 0 or 1: a single GEMM
   int64_t bsa, bsb, bsy, bss;
+  // fused tensor-parallel reduction (fp32 modes): every output row is also stored into slot push_rank of every
+  // rank's receive buffer (peer memory); the last CTA releases flag [push_rank] on every rank
+  float* const* push_ptrs; unsigned* const* push_flags; unsigned* push_done;
+  int64_t push_slot; int push_rank, push_world;
 };
 cudaError_t g53_gemm_sm100(const GemmArgs& p, cudaStream_t st);
 cudaError_t g53_e4m3_to_bf16(const uint8_t* w, int64_t n, __nv_bfloat16* out, cudaStream_t st);

@@ -17,6 +17,8 @@ keep < rows, from the layer's saved window inputs) and shifts the conv windows.
 
 from __future__ import annotations
 
+import os
+
 import math
 from dataclasses import dataclass
 
@@ -90,9 +92,15 @@ class Runtime:
         self.batch = Batch(rc, dev)
         self.px = None
         self._fused = False
+        # prefill chunks (rows >= GEMM_MIN_M) can push their partials from the tcgen05 GEMM epilogue as well
+        # (GLM53_FUSED_TP_PREFILL=1).  Off by default: measured on 8192-row chunks it is slower than NCCL's ring
+        # all-reduce (32k prefill 10.1k vs 11.3k tok/s at TP2, 10.5k vs 15.3k at TP4) -- every rank stores its whole
+        # partial into every peer, (W-1) x the ring's bytes per rank, from the GEMM epilogue's 4 warps
+        self._fused_prefill = os.environ.get("GLM53_FUSED_TP_PREFILL", "0") == "1"
         if comm is not None and self.tp > 1 and getattr(comm, "fused", False):
             from ..parallel.fused import PeerExchange
-            self.px = PeerExchange(min(R, rc.decode_rows, K.GEMV_MAX_M), D, dev)
+            rows = R if (self._fused_prefill and R >= K.GEMM_MIN_M) else min(R, rc.decode_rows, K.GEMV_MAX_M)
+            self.px = PeerExchange(rows, D, dev)
         # --- GPU-layout weights (SwiGLU-interleaved gate/up) ---
         self.gu_il = {}
         for lw in w.layers:
@@ -293,9 +301,11 @@ class Runtime:
         Kc.embed(b.ids[:R], self.w.embed, X)
         cur = 0
         first = True
-        # decode windows under tensor parallelism: block partials are pushed to the peers by the block's last GEMV
-        # and reduced inside the next mHC kernel (parallel/fused.py); otherwise an all-reduce between the two
-        self._fused = self.px is not None and R <= min(self.px.rows, K.GEMV_MAX_M)
+        # tensor parallelism: block partials are pushed to the peers by the block's last projection (GEMV epilogue
+        # for decode windows, tcgen05 GEMM epilogue for prefill chunks) and reduced inside the next mHC kernel
+        # (parallel/fused.py); rows between the two kernels' ranges, or with the switch off, all-reduce by NCCL
+        self._fused = self.px is not None and R <= self.px.rows and (
+            R <= K.GEMV_MAX_M or (self._fused_prefill and R >= K.GEMM_MIN_M and K.GEMM_ENABLED))
         self._point = 0
         for lw in self.w.layers:
             # post of the previous FFN (none before layer 0) fused with this layer's attention pre
@@ -349,10 +359,15 @@ class Runtime:
     def _final_linear(self, x, lin, R, mode=K.GEMV_F32):
         """The row-parallel projection that ends a block: writes the block's fp32 partial into ``branch``; in the
         fused tensor-parallel mode it also pushes it into every rank's receive slot."""
-        if self._fused:
+        if self._fused and R <= K.GEMV_MAX_M:
             px, p = self.px, self._point % 2
             K.C().gemv_push(x, lin.w, lin.s, self.branch[:R], mode, px.push_ptrs[p], px.push_flags[p],
                             px.done_prod[p:p + 1], px.slot, px.rank, px.world, px.err)
+        elif self._fused:
+            px, p = self.px, self._point % 2
+            K.C().gemm_w8a16_push(x, lin.w, lin.s, self.branch[:R], mode, K._w_scratch(lin.w.numel(), x.device),
+                                  px.push_ptrs[p], px.push_flags[p], px.done_prod[p:p + 1], px.slot, px.rank,
+                                  px.world)
         else:
             K.linear8(x, lin.w, lin.s, self.branch[:R], mode)
 

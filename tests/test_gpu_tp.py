@@ -1,0 +1,55 @@
+"""Tensor parallelism on two GPUs (skipped with fewer): the fused reduction (partials pushed to the peers from the
+projection's epilogue -- GEMV for decode windows, tcgen05 GEMM for prefill chunks -- and summed in rank order
+inside the next mHC kernel) gives the same logits as the NCCL all-reduce path, for a prefill chunk and for decode
+windows (GPU only)."""
+
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _worker(rank, world, port, result):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from glm53.config import tiny_config
+    from glm53.models import weights as W
+    from glm53.models.runtime import Runtime, RuntimeConfig
+    from glm53.models.session import Sequence
+    from glm53.parallel import dist as D
+    D.init(timeout_s=60)
+    try:
+        cfg = tiny_config()
+        dev = torch.device("cuda", rank)
+        w = W.prepare(W.RandomSource(cfg, seed=0, device=dev), cfg, rank=rank, world=world, device=dev)
+        rc = RuntimeConfig(max_rows=128, max_seqs=1, kv_slots=64 * 8, block_size=64, max_blocks=8)
+        g = torch.Generator().manual_seed(3)
+        prompt = torch.randint(16, cfg.vocab, (200,), generator=g).tolist()
+        outs = []
+        for fused in (False, True):
+            rt = Runtime(w, rc, comm=D.NcclComm(fused=fused))
+            seq = Sequence(rt)
+            lg = [seq.prefill(prompt, chunk=128).clone()]          # chunks of 128 and 72 rows (tcgen05 GEMMs)
+            toks = [1, 2, 3, 4, 5, 6, 7, 8]
+            seq.stage(toks, list(range(8)))
+            lg.append(rt.forward(8, keep_window=True).clone())    # a decode window (GEMV epilogue push)
+            if rt.px is not None:
+                rt.px.check()
+            outs.append(torch.cat([x.flatten() for x in lg]))
+        result[rank] = (outs[0] - outs[1]).abs().max().item()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_tp_matches_nccl_two_gpus():
+    import torch.multiprocessing as mp
+    result = mp.Manager().dict()
+    mp.spawn(_worker, args=(2, 29541, result), nprocs=2, join=True)
+    assert len(result) == 2
+    # two ranks: a + b is the same fp32 sum in either order, so the paths agree bit for bit
+    assert max(result.values()) == 0.0, dict(result)
