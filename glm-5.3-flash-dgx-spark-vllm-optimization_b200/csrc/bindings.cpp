@@ -764,8 +764,9 @@ void dsa_select(const Tensor& iproj, const Tensor& qi, const Tensor& ln_w, const
   a.ik_cache = nullptr;
   a.ig_cache = nullptr;
   a.err = P<int>(err_word(logits));
-  // tcgen05 logits where the head count fits the kernel (IH | 32, ID = 128); the CUDA-core kernel otherwise
-  if (tc_dsa_enabled() && g53_dsa_logits_tc(a, stream()) == cudaSuccess) {
+  // tcgen05 logits for prefill-sized launches where the head count fits the kernel (IH | 32, ID = 128); decode
+  // windows (a few rows: one query tile, pools split over CTAs) are faster on the CUDA-core kernel
+  if (tc_dsa_enabled() && a.R >= 64 && g53_dsa_logits_tc(a, stream()) == cudaSuccess) {
   } else {
     check(g53_dsa_logits(a, stream()), "dsa_logits");
   }

@@ -9,7 +9,7 @@
 // rows (their conv outputs stay in the layer's qkv scratch) into S_out.  This is the reference's "lazy commit"
 // (code/fork/glm53_kda_lazy.py:1-30) built into the kernel contract.
 //
-// Mapping: CTA = (head, 32 value rows); thread (vr, kq) owns S[vr][kq*Dh/4 .. +Dh/4); dot products over k are
+// Mapping: CTA = (head, 32 value rows); thread (vr, kq) owns S[vr][kq + 4j] (j < Dh/4); dot products over k are
 // reduced over the 4 threads of a row group.
 #include "common.cuh"
 #include "launchers.h"
@@ -62,70 +62,80 @@ __global__ void kda_conv_commit_kernel(KdaArgs a) {
   for (int i = 0; i < T - 1; ++i) win[(int64_t)i * C + c] = f2bf(rows[i]);
 }
 
-// grid (H, Dh/32, sequences)
+// grid (H, Dh/32, sequences).  Rows are staged 8 at a time in shared memory (normalised q, k, the decay g,
+// this CTA's 32 values of v, beta) by all 128 threads with coalesced loads, so the sequential recurrence only reads
+// shared memory; the state stays in registers.
+constexpr int kRecRows = 8;
 template <int DH>
 __global__ void __launch_bounds__(128) kda_recurrent_kernel(KdaArgs a) {
   constexpr int KP = DH / 4;
+  __shared__ float sq[kRecRows][DH], sk[kRecRows][DH], sg[kRecRows][DH], sv[kRecRows][32], sb[kRecRows];
   const int h = blockIdx.x, b = blockIdx.z;
-  const int vr = threadIdx.x >> 2, kq = threadIdx.x & 3;
-  const int v = blockIdx.y * 32 + vr;
-  const int k0 = kq * KP;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int vr = tid >> 2, kq = tid & 3;
+  const int v0 = blockIdx.y * 32, v = v0 + vr;
+  // thread (vr, kq) owns state channels kq + 4 j (interleaved: the 4 threads of a row read 4 banks)
   const int HD = a.H * DH;
   const int base = a.row0[b], n = a.nrows[b];
   const int64_t sstride = (int64_t)a.H * DH * DH;
   float S[KP];
-  const float* sin = a.S_pool + a.s_in[b] * sstride + ((int64_t)h * DH + v) * DH + k0;
+  const float* sin = a.S_pool + a.s_in[b] * sstride + ((int64_t)h * DH + v) * DH + kq;
 #pragma unroll
-  for (int j = 0; j < KP; j += 4) {
-    const float4 t = *reinterpret_cast<const float4*>(sin + j);
-    S[j] = t.x; S[j + 1] = t.y; S[j + 2] = t.z; S[j + 3] = t.w;
-  }
+  for (int j = 0; j < KP; ++j) S[j] = sin[4 * j];
   const float ea = __expf(a.a_log[h]);
-  float dtb[KP];
+  for (int r0 = 0; r0 < n; r0 += kRecRows) {
+    const int nr = min(kRecRows, n - r0);
+    // stage: warp w normalises rows w, w + 4 (q and k: one row per warp, DH/32 elements per lane)
+    for (int rr = warp; rr < nr; rr += 4) {
+      const int t = base + r0 + rr;
+      const __nv_bfloat16* row = a.qkv + (int64_t)t * 3 * HD;
+      constexpr int PL = DH / 32;
+      float q[PL], k[PL];
+      float qq = 0.f, kk = 0.f;
 #pragma unroll
-  for (int j = 0; j < KP; ++j) dtb[j] = a.dt_bias[h * DH + k0 + j];
-  for (int tt = 0; tt < n; ++tt) {
-    const int t = base + tt;
-    const __nv_bfloat16* row = a.qkv + (int64_t)t * 3 * HD;
-    float q[KP], k[KP];
-    float sq = 0.f, sk = 0.f;
+      for (int i = 0; i < PL; ++i) {
+        const int c = lane + 32 * i;
+        q[i] = bf2f(row[h * DH + c]);
+        k[i] = bf2f(row[HD + h * DH + c]);
+        qq += q[i] * q[i];
+        kk += k[i] * k[i];
+        sg[rr][c] = a.lower * sigmoidf_(ea * (bf2f(a.f[(int64_t)t * HD + h * DH + c]) + a.dt_bias[h * DH + c]));
+      }
+      qq = warp_sum(qq);
+      kk = warp_sum(kk);
+      const float qn = rsqrtf(qq + 1e-6f) * rsqrtf((float)DH), kn = rsqrtf(kk + 1e-6f);
 #pragma unroll
-    for (int j = 0; j < KP; ++j) {
-      q[j] = bf2f(row[h * DH + k0 + j]);
-      k[j] = bf2f(row[HD + h * DH + k0 + j]);
-      sq += q[j] * q[j];
-      sk += k[j] * k[j];
+      for (int i = 0; i < PL; ++i) {
+        sq[rr][lane + 32 * i] = q[i] * qn;
+        sk[rr][lane + 32 * i] = k[i] * kn;
+      }
+      sv[rr][lane] = bf2f(row[2 * HD + h * DH + v0 + lane]);
+      if (lane == 0) sb[rr] = sigmoidf_(bf2f(a.proj[(int64_t)t * a.ldp + a.b_off + h]));
     }
-    sq = group_sum<4>(sq);
-    sk = group_sum<4>(sk);
-    const float qn = rsqrtf(sq + 1e-6f) * rsqrtf((float)DH);
-    const float kn = rsqrtf(sk + 1e-6f);
-    const float vv = bf2f(row[2 * HD + h * DH + v]);
-    const float beta = sigmoidf_(bf2f(a.proj[(int64_t)t * a.ldp + a.b_off + h]));
-    const __nv_bfloat16* fr = a.f + (int64_t)t * HD + h * DH + k0;
-    float dot = 0.f;
+    __syncthreads();
+    for (int rr = 0; rr < nr; ++rr) {
+      float dot = 0.f;
 #pragma unroll
-    for (int j = 0; j < KP; ++j) {
-      const float g = a.lower * sigmoidf_(ea * (bf2f(fr[j]) + dtb[j]));
-      S[j] *= __expf(g);
-      k[j] *= kn;
-      q[j] *= qn;
-      dot += S[j] * k[j];
-    }
-    dot = group_sum<4>(dot);
-    const float vn = beta * (vv - dot);
-    float o = 0.f;
+      for (int j = 0; j < KP; ++j) {
+        S[j] *= __expf(sg[rr][kq + 4 * j]);
+        dot += S[j] * sk[rr][kq + 4 * j];
+      }
+      dot = group_sum<4>(dot);
+      const float vn = sb[rr] * (sv[rr][vr] - dot);
+      float o = 0.f;
 #pragma unroll
-    for (int j = 0; j < KP; ++j) {
-      S[j] += vn * k[j];
-      o += S[j] * q[j];
+      for (int j = 0; j < KP; ++j) {
+        S[j] += vn * sk[rr][kq + 4 * j];
+        o += S[j] * sq[rr][kq + 4 * j];
+      }
+      o = group_sum<4>(o);
+      if (a.o_raw && kq == 0) a.o_raw[(int64_t)(base + r0 + rr) * HD + h * DH + v] = o;
     }
-    o = group_sum<4>(o);
-    if (a.o_raw && kq == 0) a.o_raw[(int64_t)t * HD + h * DH + v] = o;
+    __syncthreads();
   }
-  float* sout = a.S_pool + a.s_out[b] * sstride + ((int64_t)h * DH + v) * DH + k0;
+  float* sout = a.S_pool + a.s_out[b] * sstride + ((int64_t)h * DH + v) * DH + kq;
 #pragma unroll
-  for (int j = 0; j < KP; j += 4) *reinterpret_cast<float4*>(sout + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+  for (int j = 0; j < KP; ++j) sout[4 * j] = S[j];
 }
 
 // one warp per (row, head)

@@ -17,7 +17,6 @@ namespace g53 {
 
 constexpr int kDB = 64;      // columns per partial CTA (one per thread)
 constexpr int kRB = 16;      // rows per partial CTA
-constexpr int kMaxMix = 24;
 
 template <int S>
 __global__ void __launch_bounds__(kDB) hc_partial_kernel(HcArgs a) {
@@ -31,7 +30,8 @@ __global__ void __launch_bounds__(kDB) hc_partial_kernel(HcArgs a) {
   for (int i = 0; i < NM; ++i)
 #pragma unroll
     for (int s = 0; s < S; ++s) fnv[i][s] = pre ? bf2f(a.fn[(int64_t)i * S * a.D + s * a.D + d]) : 0.f;
-  const int r0 = blockIdx.y * kRB;
+  const int rb = (a.R + gridDim.y - 1) / gridDim.y;   // rows per CTA (1 for decode-sized launches)
+  const int r0 = blockIdx.y * rb;
   if (a.gath) {
     // tensor-parallel partials pushed by every rank's producer: wait for all arrival flags of this parity
     if (threadIdx.x == 0) {
@@ -40,7 +40,7 @@ __global__ void __launch_bounds__(kDB) hc_partial_kernel(HcArgs a) {
     }
     __syncthreads();
   }
-  for (int r = r0; r < min(r0 + kRB, a.R); ++r) {
+  for (int r = r0; r < min(r0 + rb, a.R); ++r) {
     __nv_bfloat16* xr = a.X + (int64_t)r * S * a.D;
     float x[S];
 #pragma unroll
@@ -78,10 +78,22 @@ __global__ void __launch_bounds__(kDB) hc_partial_kernel(HcArgs a) {
     for (int s = 0; s < S; ++s) ss += x[s] * x[s];
     red[threadIdx.x][NM] = ss;
     __syncthreads();
-    if (threadIdx.x <= NM) {
-      float t = 0.f;
-      for (int c = 0; c < kDB; ++c) t += red[c][threadIdx.x];      // fixed order
-      a.part[((int64_t)r * NB + blockIdx.x) * 32 + threadIdx.x] = t;
+    {
+      // 2 threads per output (columns c = h, h + 2, ...), 4 interleaved accumulators: fixed order, short chains
+      const int i = threadIdx.x >> 1, h = threadIdx.x & 1;
+      float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+      if (i <= NM) {
+#pragma unroll
+        for (int c = h; c < kDB; c += 8) {
+          t0 += red[c][i];
+          t1 += red[c + 2][i];
+          t2 += red[c + 4][i];
+          t3 += red[c + 6][i];
+        }
+      }
+      float t = (t0 + t1) + (t2 + t3);
+      t += __shfl_xor_sync(0xffffffffu, t, 1);
+      if (i <= NM && h == 0) a.part[((int64_t)r * NB + blockIdx.x) * 32 + i] = t;
     }
     __syncthreads();
   }
@@ -129,11 +141,22 @@ __global__ void __launch_bounds__(512) hc_finish_kernel(HcArgs a) {
   __shared__ float mix[32];
   __shared__ float pre_s[S], post_s[S], comb_s[S * S];
   __shared__ float red[32];
-  // partial sums: warp w sums mixes in fixed block order
-  if (threadIdx.x < 32 && threadIdx.x <= NM) {
-    float t = 0.f;
-    for (int b = 0; b < NB; ++b) t += a.part[((int64_t)r * NB + b) * 32 + threadIdx.x];
-    mix[threadIdx.x] = t;
+  // partial sums over the column blocks: warp w reads blocks w, w + nw, ... (coalesced 32-wide rows), then the
+  // per-warp sums are added in warp order (fixed order throughout)
+  {
+    __shared__ float wpart[16][33];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = min((int)(blockDim.x >> 5), 16);
+    if (w < nw) {
+      float t = 0.f;
+      for (int b = w; b < NB; b += nw) t += a.part[((int64_t)r * NB + b) * 32 + lane];
+      wpart[w][lane] = t;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = 0.f;
+      for (int j = 0; j < nw; ++j) t += wpart[j][threadIdx.x];
+      mix[threadIdx.x] = t;
+    }
   }
   __syncthreads();
   if (threadIdx.x < 32) {
@@ -158,23 +181,44 @@ __global__ void __launch_bounds__(512) hc_finish_kernel(HcArgs a) {
   if (threadIdx.x < S) a.post_out[r * S + threadIdx.x] = post_s[threadIdx.x];
   if (threadIdx.x < S * S) a.comb_out[r * S * S + threadIdx.x] = comb_s[threadIdx.x];
   const __nv_bfloat16* xr = a.X + (int64_t)r * S * a.D;
+  // 8 consecutive columns per thread and pass (16-byte loads of every stream issued together); D <= 8192
+  constexpr int kPass = 2;
+  float col[kPass][8];
   float ss = 0.f;
-  constexpr int kPer = 16;   // columns per thread (D <= 8192)
-  float col[kPer];
-  int n = 0;
-  for (int d = threadIdx.x; d < a.D; d += blockDim.x, ++n) {
-    float t = 0.f;
 #pragma unroll
-    for (int s = 0; s < S; ++s) t += pre_s[s] * bf2f(xr[s * a.D + d]);
-    t = round_bf16(t);
-    col[n] = t;
-    ss += t * t;
+  for (int ps = 0; ps < kPass; ++ps) {
+    const int d0 = (ps * blockDim.x + threadIdx.x) * 8;
+    if (d0 >= a.D) continue;
+    uint4 xs[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) xs[s] = *reinterpret_cast<const uint4*>(xr + (int64_t)s * a.D + d0);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float t = 0.f;
+#pragma unroll
+      for (int s = 0; s < S; ++s) t += pre_s[s] * bf2f(reinterpret_cast<const __nv_bfloat16*>(&xs[s])[e]);
+      t = round_bf16(t);
+      col[ps][e] = t;
+      ss += t * t;
+    }
   }
   ss = block_sum(ss, red);
   const float rinv = rsqrtf(ss / (float)a.D + a.eps);
-  n = 0;
-  for (int d = threadIdx.x; d < a.D; d += blockDim.x, ++n)
-    a.normed[(int64_t)r * a.D + d] = f2bf(col[n] * rinv * bf2f(a.norm_w[d]));
+#pragma unroll
+  for (int ps = 0; ps < kPass; ++ps) {
+    const int d0 = (ps * blockDim.x + threadIdx.x) * 8;
+    if (d0 >= a.D) continue;
+    const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + d0);
+    const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(&wv);
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_bfloat162 b2 = __floats2bfloat162_rn(col[ps][2 * e] * rinv * bf2f(wb[2 * e]),
+                                                col[ps][2 * e + 1] * rinv * bf2f(wb[2 * e + 1]));
+      o[e] = *reinterpret_cast<uint32_t*>(&b2);
+    }
+    *reinterpret_cast<uint4*>(a.normed + (int64_t)r * a.D + d0) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
 }
 
 __global__ void embed_kernel(const int* ids, const __nv_bfloat16* table, int D, int S, __nv_bfloat16* X) {
@@ -230,8 +274,9 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, in
 using namespace g53;
 
 cudaError_t g53_hc_post_pre(const HcArgs& a, cudaStream_t st) {
-  if (a.D % kDB || a.D > 8192 || (a.S != 2 && a.S != 4)) return cudaErrorInvalidValue;
-  dim3 g1(a.D / kDB, (a.R + kRB - 1) / kRB);
+  if (a.D % kDB || a.D > 8192 || a.D % 8 || (a.S != 2 && a.S != 4)) return cudaErrorInvalidValue;
+  // decode-sized launches: one row per CTA (more CTAs in flight); prefill: kRB rows per CTA (fn reuse)
+  dim3 g1(a.D / kDB, a.R <= kRB ? a.R : (a.R + kRB - 1) / kRB);
   if (a.S == 4) {
     hc_partial_kernel<4><<<g1, kDB, 0, st>>>(a);
     G53_CHECK_LAUNCH();

@@ -285,9 +285,32 @@ def bench_ep(args, T: Timer):
         dist.destroy_process_group()
 
 
+def bench_hc(args, T: Timer):
+    """mHC post (4 streams) fused with the next pre (24 mixing logits, Sinkhorn, collapse, rmsnorm) for R rows."""
+    from glm53.ops import kernels as K
+    S, D, NM = 4, 4096, 24
+    dev = "cuda"
+    for R in args.rows:
+        X = torch.randn(R, S, D, device=dev).to(torch.bfloat16)
+        branch = torch.randn(R, D, device=dev)
+        post = torch.rand(R, S, device=dev)
+        comb = torch.rand(R, S, S, device=dev) / S
+        fn = (torch.randn(NM, S * D, device=dev) / math.sqrt(S * D)).to(torch.bfloat16)
+        base = torch.zeros(NM, device=dev)
+        hscale = torch.ones(3, device=dev)
+        norm_w = torch.ones(D, device=dev).to(torch.bfloat16)
+        normed = torch.empty(R, D, device=dev).to(torch.bfloat16)
+        post_o, comb_o = torch.empty(R, S, device=dev), torch.empty(R, S, S, device=dev)
+        part = torch.empty(R * (D // 64) * 32, device=dev)
+        ms = T(lambda: K.C().hc_post_pre(X, branch, post, comb, fn, base, hscale, norm_w, normed, post_o, comb_o,
+                                          part, 1e-5, 1e-6, 20))
+        emit({"case": "hc_post_pre", "rows": R, "ms": ms,
+              "GBps": (R * S * D * 2 * 2 + R * D * 4 + NM * S * D * 2) / ms / 1e6})
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["moe", "gemv", "gemm", "kda", "mla", "ep", "all"])
+    ap.add_argument("case", choices=["moe", "gemv", "gemm", "kda", "mla", "ep", "hc", "all"])
     ap.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 64, 512, 8192])
     ap.add_argument("--rows", type=int, nargs="+", default=[8])
     ap.add_argument("--kda-rows", type=int, nargs="+", default=[8, 8192])
