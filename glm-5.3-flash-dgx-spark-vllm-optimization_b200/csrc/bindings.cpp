@@ -168,6 +168,42 @@ void gemm_w8a16_push(const Tensor& x, const Tensor& w, const Tensor& scale, cons
   check(g53_gemm_sm100(p, stream()), "gemm_w8a16_push");
 }
 
+// all-gather + GEMM (column-parallel input): y [W * rows, N] = A_all @ (w8 * s)^T with A row-sharded over the ranks;
+// shard j at ptrs[j] (host int64 list of device addresses, peer memory), row pitch lda; waits (bounded) for
+// flags[j] >= target (raised by rank j's signal_peers after it wrote its shard)
+void gemm_ag_w8a16(const Tensor& ptrs, const Tensor& ptrs_dev, int64_t rank, int64_t rows, int64_t K, int64_t lda,
+                   const Tensor& w, const Tensor& scale, const Tensor& y, int64_t mode, const Tensor& scratch,
+                   const Tensor& flags, int64_t target, const Tensor& stage, const Tensor& ready) {
+  TORCH_CHECK(ptrs.device().is_cpu() && ptrs.scalar_type() == at::kLong, "ptrs: host int64 addresses");
+  TORCH_CHECK(scratch.scalar_type() == at::kBFloat16 && scratch.numel() >= w.numel(), "scratch too small");
+  TORCH_CHECK(flags.scalar_type() == at::kInt && flags.numel() >= ptrs.numel());
+  const int W = (int)ptrs.numel();
+  check(g53_e4m3_to_bf16(P<const uint8_t>(w), w.numel(), P<__nv_bfloat16>(scratch), stream()), "e4m3_to_bf16");
+  auto wb = scratch.flatten().narrow(0, 0, w.numel()).view(w.sizes());
+  GemmArgs p{};
+  p.a = nullptr; p.lda = lda;
+  p.b = wb.data_ptr(); p.ldb = wb.stride(0);
+  p.b_scale = P<const float>(scale);
+  p.y = y.data_ptr(); p.ldy = y.stride(0);
+  p.M = (int)(W * rows); p.N = (int)w.size(0); p.K = (int)K;
+  p.mode = (int)mode; p.fp8 = 0;
+  p.err = P<int>(err_word(y));
+  p.ag_world = W; p.ag_rows = (int)rows; p.ag_rank = (int)rank; p.ag_ptrs = ptrs.data_ptr<int64_t>();
+  p.ag_ptrs_dev = P<const int64_t>(ptrs_dev);
+  p.ag_flags = reinterpret_cast<const unsigned*>(flags.data_ptr()); p.ag_target = (unsigned)target;
+  TORCH_CHECK(stage.scalar_type() == at::kBFloat16 && stage.numel() >= (int64_t)W * rows * K, "stage too small");
+  TORCH_CHECK(ready.scalar_type() == at::kInt && ready.numel() >= (int64_t)W * rows / 128, "ready too small");
+  p.ag_stage = P<__nv_bfloat16>(stage);
+  p.ag_ready = P<int>(ready);
+  TORCH_CHECK(y.size(0) == p.M && y.size(1) == p.N && y.stride(1) == 1, "y must be [W * rows, N]");
+  check(g53_gemm_sm100(p, stream()), "gemm_ag_w8a16");
+}
+
+void signal_peers(const Tensor& flag_addrs, int64_t rank) {
+  TORCH_CHECK(flag_addrs.scalar_type() == at::kLong && flag_addrs.is_cuda());
+  check(g53_signal_peers(P<const int64_t>(flag_addrs), (int)rank, (int)flag_addrs.numel(), stream()), "signal_peers");
+}
+
 int64_t gemm_error(const Tensor& like) {
   auto& e = err_word(like);
   const int64_t v = e[0].item<int>();
@@ -823,6 +859,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_w8a16", &gemm_w8a16);
   m.def("gemm_error", &gemm_error);
   m.def("gemm_w8a16_push", &gemm_w8a16_push);
+  m.def("gemm_ag_w8a16", &gemm_ag_w8a16);
+  m.def("signal_peers", &signal_peers);
   m.def("moe_route", &moe_route);
   m.def("exl3_moe", &exl3_moe);
   m.def("moe_combine", &moe_combine);

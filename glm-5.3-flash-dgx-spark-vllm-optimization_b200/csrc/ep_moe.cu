@@ -190,6 +190,19 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpArgs a, const int* pa
 
 using namespace g53;
 
+// one thread: everything this rank wrote before (stream order) becomes visible system-wide, then flag [rank] is
+// raised on every rank (publication of a shard for all-gather + GEMM)
+__global__ void signal_peers_kernel(const int64_t* flags, int rank, int world) {
+  __threadfence_system();
+  for (int j = 0; j < world; ++j) red_release_sys_add(reinterpret_cast<unsigned*>(flags[j]) + rank, 1u);
+}
+
+cudaError_t g53_signal_peers(const int64_t* flags, int rank, int world, cudaStream_t st) {
+  signal_peers_kernel<<<1, 1, 0, st>>>(flags, rank, world);
+  G53_CHECK_LAUNCH();
+  return cudaSuccess;
+}
+
 cudaError_t g53_ep_dispatch(const EpArgs& a, int max_pairs, cudaStream_t st) {
   if (a.K % 8 || a.world * a.El > 1024 || max_pairs < 0) return cudaErrorInvalidValue;
   // at least one block: it writes the (possibly zero) counts and releases the flags

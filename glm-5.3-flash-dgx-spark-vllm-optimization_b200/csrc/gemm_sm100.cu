@@ -130,6 +130,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -137,11 +139,11 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 // tile t of the persistent schedule -> (m0, n0): bands of kGroupM M-tiles, N-tiles walked inside a band, so the
 // CTAs resident at one time share a few A row-blocks and a few B column-blocks in L2
 constexpr int kGroupM = 8;
-__device__ __forceinline__ void tile_coords(int t, int MT, int NT, int BN, int& m0, int& n0) {
+__device__ __forceinline__ void tile_coords(int t, int MT, int NT, int BN, int& m0, int& n0, int mrot = 0) {
   const int band = t / (kGroupM * NT);
   const int gm = min(kGroupM, MT - band * kGroupM);
   const int idx = t - band * kGroupM * NT;
-  m0 = (band * kGroupM + idx % gm) * kBM;
+  m0 = ((band * kGroupM + idx % gm + mrot) % MT) * kBM;    // all-gather: start at this rank's own rows
   n0 = (idx / gm) * BN;
 }
 
@@ -243,9 +245,17 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& p, void* ybase, cons
 
 // Persistent kernel: gridDim.x CTAs (at most one per SM) walk the output tiles in the grouped order; the TMEM
 // holds two 128 x BN accumulators so the epilogue of one tile overlaps the main loop of the next.
+// Tensor maps of one launch.  All-gather + GEMM (ag_world > 0): A is row-sharded over the ranks of a group and
+// a[j] maps rank j's shard (its memory, reached over NVLink: plain TMA loads, no multicast); output rows
+// [j * ag_rows, (j + 1) * ag_rows) come from shard j.
+constexpr int kMaxAg = 8;
+struct GemmMaps {
+  CUtensorMap a[kMaxAg];
+  CUtensorMap b;
+};
+
 template <int BN, bool FP8, int STAGES>
-__global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
-                                                            const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
+__global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constant__ GemmMaps maps, GemmArgs p) {
   constexpr int BK = FP8 ? 128 : 64;               // one 128-byte swizzle row per operand row
   constexpr int A_BYTES = kBM * 128;
   constexpr int B_BYTES = BN * 128;
@@ -265,6 +275,7 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
   const int MT = (p.M + kBM - 1) / kBM, NT = (p.N + BN - 1) / BN, per_batch = MT * NT;
   const int tiles = per_batch * max(p.batch, 1);
   const int nk = (p.K + BK - 1) / BK;
+  const int mrot = p.ag_world > 0 ? p.ag_rank * (p.ag_rows / kBM) : 0;
 
   if (threadIdx.x == 0) {
     fail = 0;
@@ -294,7 +305,25 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
       for (int t = blockIdx.x; t < tiles && !fail; t += gridDim.x) {
         int m0, n0;
         const int bz = t / per_batch;
-        tile_coords(t - bz * per_batch, MT, NT, BN, m0, n0);
+        tile_coords(t - bz * per_batch, MT, NT, BN, m0, n0, mrot);
+        const CUtensorMap* ma = &maps.a[0];
+        int am0 = m0;
+        if (p.ag_world > 0) {
+          const int owner = m0 / p.ag_rows;
+          if (owner == p.ag_rank) {
+            ma = &maps.a[0];                          // this rank's own shard
+            am0 = m0 - owner * p.ag_rows;
+          } else {
+            // a peer's row block, copied once into the local staging buffer by the epilogue warps of some CTA
+            ma = &maps.a[1];
+            if (!wait_flag_geq(reinterpret_cast<const unsigned*>(p.ag_ready) + m0 / kBM, (unsigned)kBM * p.ag_target,
+                               p.err, 5)) {
+              fail = 1;
+              break;
+            }
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+          }
+        }
         for (int kb = 0; kb < nk; ++kb, ++kbg) {
           const int s = kbg % STAGES;
           const uint32_t ph = (kbg / STAGES) & 1;
@@ -302,8 +331,8 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
           uint8_t* a_dst = smem + s * STAGE_BYTES;
           uint8_t* b_dst = a_dst + A_BYTES;
           mbar_expect_tx(&full_bar[s], STAGE_BYTES);
-          tma_load_3d(&tmA, &full_bar[s], a_dst, kb * BK, m0, bz);
-          tma_load_3d(&tmB, &full_bar[s], b_dst, kb * BK, n0, bz);
+          tma_load_3d(ma, &full_bar[s], a_dst, kb * BK, am0, bz);
+          tma_load_3d(&maps.b, &full_bar[s], b_dst, kb * BK, n0, bz);
         }
       }
     }
@@ -339,12 +368,56 @@ __global__ void __launch_bounds__(192, 1) gemm_sm100_kernel(const __grid_constan
   } else {
     // epilogue warps 2..5 -> TMEM lane quadrant (warp % 4)
     const int quad = warp & 3;
+    if (p.ag_world > 0) {
+      // all-gather: before their first tile, the 4 epilogue warps of every CTA copy a share of the peers' rows over
+      // NVLink into the local staging buffer (each remote row crosses once), 4 rows (16 x 16-byte loads in flight
+      // per thread) at a time, and count the copied rows of each 128-row block (ready[block] reaches 128 x target)
+      const int et = threadIdx.x - 64;              // 0..127
+      const int per_shard = p.ag_rows / kBM;
+      const int vec = p.K / 8;                       // 16-byte vectors per row
+      const int units = (p.ag_world - 1) * p.ag_rows / 4;
+      int seen = -1;                                 // owner whose publish flag was observed
+      for (int u = blockIdx.x; u < units && !fail; u += gridDim.x) {
+        const int rr = u * 4;                        // row among the remote rows (peer order, skipping this rank)
+        int owner = rr / p.ag_rows;
+        owner += owner >= p.ag_rank ? 1 : 0;
+        const int orow = rr % p.ag_rows;             // row within the owner's shard
+        if (owner != seen) {
+          if (et == 0 && !wait_flag_geq(p.ag_flags + owner, p.ag_target, p.err, 6)) fail = 1;
+          named_bar(1, 128);
+          seen = owner;
+          if (fail) break;
+        }
+        const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(p.ag_ptrs_dev[owner]) + (int64_t)orow * p.lda;
+        const int grow = owner * p.ag_rows + orow;  // row of the gathered matrix
+        __nv_bfloat16* dst = p.ag_stage + (int64_t)grow * p.K;
+        for (int i0 = et; i0 < 4 * vec; i0 += 128 * 16) {
+          uint4 v[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const int j = i0 + k * 128;
+            if (j < 4 * vec) v[k] = *reinterpret_cast<const uint4*>(src + (int64_t)(j / vec) * p.lda + (j % vec) * 8);
+          }
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const int j = i0 + k * 128;
+            if (j < 4 * vec) *reinterpret_cast<uint4*>(dst + (int64_t)(j / vec) * p.K + (j % vec) * 8) = v[k];
+          }
+        }
+        // generic-proxy stores -> visible to the TMA (async proxy) loads of other CTAs, then counted
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __threadfence();
+        named_bar(1, 128);
+        if (et == 0) atomicAdd(reinterpret_cast<unsigned*>(p.ag_ready) + grow / kBM, 4u);
+      }
+      (void)per_shard;
+    }
     int it = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
       const int buf = it & 1;
       int m0, n0;
       const int bz = t / per_batch;
-      tile_coords(t - bz * per_batch, MT, NT, BN, m0, n0);
+      tile_coords(t - bz * per_batch, MT, NT, BN, m0, n0, mrot);
       void* ybase = reinterpret_cast<uint8_t*>(p.y) +
                     bz * p.bsy * ((p.mode == GEMV_F32 || p.mode == GEMV_F32_ACC) ? 4 : 2);
       const float* bscale = p.b_scale ? p.b_scale + bz * p.bss : nullptr;
@@ -475,9 +548,19 @@ bool make_map(CUtensorMap* m, const void* base, bool fp8, int64_t rows, int64_t 
 
 template <int BN, bool FP8, int STAGES>
 cudaError_t launch(const GemmArgs& p, cudaStream_t st) {
-  CUtensorMap ta, tb;
-  if (!make_map(&ta, p.a, FP8, p.M, p.K, p.lda, p.batch, p.bsa, kBM)) return cudaErrorInvalidValue;
-  if (!make_map(&tb, p.b, FP8, p.N, p.K, p.ldb, p.batch, p.bsb, BN)) return cudaErrorInvalidValue;
+  GemmMaps maps;
+  if (p.ag_world > 0) {
+    if (p.ag_world > kMaxAg || p.ag_rows % kBM || p.M != p.ag_world * p.ag_rows || p.batch > 1 || FP8 ||
+        !p.ag_stage || !p.ag_ready || !p.ag_ptrs_dev || p.K % 8)
+      return cudaErrorInvalidValue;
+    if (!make_map(&maps.a[0], reinterpret_cast<const void*>(p.ag_ptrs[p.ag_rank]), FP8, p.ag_rows, p.K, p.lda, 1, 0,
+                  kBM) ||
+        !make_map(&maps.a[1], p.ag_stage, FP8, p.M, p.K, p.K, 1, 0, kBM))
+      return cudaErrorInvalidValue;
+  } else if (!make_map(&maps.a[0], p.a, FP8, p.M, p.K, p.lda, p.batch, p.bsa, kBM)) {
+    return cudaErrorInvalidValue;
+  }
+  if (!make_map(&maps.b, p.b, FP8, p.N, p.K, p.ldb, p.batch, p.bsb, BN)) return cudaErrorInvalidValue;
   const int smem = STAGES * (kBM * 128 + BN * 128) + 1024;
   auto kern = gemm_sm100_kernel<BN, FP8, STAGES>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -494,7 +577,7 @@ cudaError_t launch(const GemmArgs& p, cudaStream_t st) {
   q.vec = ((reinterpret_cast<uintptr_t>(p.y) & 15) == 0 && ((p.ldy * out_esz) & 15) == 0 &&
            ((p.bsy * out_esz) & 15) == 0 && ((p.bss * 4) & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(p.b_scale) & 15) == 0) ? 1 : 0;
-  kern<<<std::min(tiles, n_sm), 192, smem, st>>>(ta, tb, q);
+  kern<<<std::min(tiles, n_sm), 192, smem, st>>>(maps, q);
   return cudaGetLastError();
 }
 
@@ -503,7 +586,7 @@ cudaError_t launch(const GemmArgs& p, cudaStream_t st) {
 cudaError_t g53_gemm_sm100(const GemmArgs& p, cudaStream_t st) {
   // alignment rules of the tensor maps: 16-byte aligned bases and row strides
   const int esz = p.fp8 ? 1 : 2;
-  if ((reinterpret_cast<uintptr_t>(p.a) & 15) || (reinterpret_cast<uintptr_t>(p.b) & 15) ||
+  if ((p.ag_world == 0 && (reinterpret_cast<uintptr_t>(p.a) & 15)) || (reinterpret_cast<uintptr_t>(p.b) & 15) ||
       ((p.lda * esz) & 15) || ((p.ldb * esz) & 15) || (p.K * esz) % 16)
     return cudaErrorInvalidValue;
   if (p.batch > 1 && (((p.bsa * esz) & 15) || ((p.bsb * esz) & 15) || p.a_scale)) return cudaErrorInvalidValue;

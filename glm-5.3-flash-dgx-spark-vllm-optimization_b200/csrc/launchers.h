@@ -48,6 +48,14 @@ struct GemmArgs {
   // rank's receive buffer (peer memory); the last CTA releases flag [push_rank] on every rank
   float* const* push_ptrs; unsigned* const* push_flags; unsigned* push_done;
   int64_t push_slot; int push_rank, push_world;
+  // all-gather + GEMM: A is [ag_world x ag_rows, K] row-sharded over ranks; shard j at ag_ptrs[j] (host array of
+  // device addresses, peer memory for j != rank) with row pitch lda; the producer waits for ag_flags[j] >= ag_target
+  int ag_world, ag_rows, ag_rank;
+  const int64_t* ag_ptrs;                // host array (tensor maps)
+  const int64_t* ag_ptrs_dev;            // the same addresses on the device (staging copies)
+  const unsigned* ag_flags; unsigned ag_target;
+  __nv_bfloat16* ag_stage;               // local [ag_world * ag_rows, K]: peers' rows, copied once per epoch
+  int* ag_ready;                         // local [ag_world * ag_rows / 128]: epoch of each staged row block
 };
 cudaError_t g53_gemm_sm100(const GemmArgs& p, cudaStream_t st);
 cudaError_t g53_e4m3_to_bf16(const uint8_t* w, int64_t n, __nv_bfloat16* out, cudaStream_t st);
@@ -128,6 +136,8 @@ struct EpArgs {
   int* rp_token; int* rp_expert; float* rp_w; int64_t* rp_out;   // [recv_cap]
 };
 cudaError_t g53_ep_dispatch(const EpArgs& a, int max_pairs, cudaStream_t st);
+// flags[j] = address of rank j's flag array: raise element [rank] on every rank after this rank's prior writes
+cudaError_t g53_signal_peers(const int64_t* flags, int rank, int world, cudaStream_t st);
 cudaError_t g53_ep_plan(const EpArgs& a, cudaStream_t st);
 cudaError_t g53_ep_combine(const EpArgs& a, const int* pair_of, int R, int top_k, float* out, cudaStream_t st);
 cudaError_t g53_exl3_gate_up(const Exl3Args& a, cudaStream_t st);

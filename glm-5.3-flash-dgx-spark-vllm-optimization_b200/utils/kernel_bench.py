@@ -4,6 +4,7 @@ the time and the achieved rate against the measured peaks (MEASURED_PEAKS.json w
 
   python -m glm53.utils.kernel_bench moe --tokens 1 8 64 512 8192 [--tp 1]      (BASELINE configs[1])
   python -m glm53.utils.kernel_bench gemv|gemm|kda|mla|all
+  torchrun --nproc-per-node N -m glm53.utils.kernel_bench ag --rows 1024 4096    (fused all-gather + GEMM vs NCCL)
   torchrun --nproc-per-node N -m glm53.utils.kernel_bench ep --tokens 1 8 64 512   (experts
       EP-sharded over N GPUs, tokens per rank; dispatch/combine fused into the kernels)
   --iters 1 --warmup 1 makes a case small enough to capture under ncu
@@ -285,6 +286,72 @@ def bench_ep(args, T: Timer):
         dist.destroy_process_group()
 
 
+def bench_ag(args, T: Timer):
+    """All-gather + GEMM of a column-parallel projection (KDA in_proj: K 4096 -> N 24896 / W) over the ranks'
+    row shards: fused (the GEMM's TMA producer loads peer shards) vs NCCL all_gather_into_tensor + the same GEMM.
+    Roofline: slower of the GEMM at measured bf16 peak and the (W-1) shards over NVLink at 770 GB/s."""
+    import torch.distributed as dist
+    from glm53.models.weights import quantize_fp8_rows
+    from glm53.ops import kernels as K
+    from glm53.parallel import dist as D
+    from glm53.parallel.ag_gemm import AGGemm
+    rank, local, world = D.init(timeout_s=120)
+    dev = torch.device("cuda", local)
+    _, peak = peaks()
+    Kd, N = 4096, (24896 // world + 15) // 16 * 16
+    w = quantize_fp8_rows(torch.randn(N, Kd, device=dev) / math.sqrt(Kd))
+    for rows in args.rows:
+        bufs = [AGGemm(rows, Kd, dev), AGGemm(rows, Kd, dev)]
+        y = torch.empty(world * rows, N, device=dev, dtype=torch.bfloat16)
+        mine = torch.randn(rows, Kd, device=dev).to(torch.bfloat16)
+        gathered = torch.empty(world * rows, Kd, device=dev, dtype=torch.bfloat16)
+        step = [0]
+
+        def fused():
+            ag = bufs[step[0] % 2]
+            step[0] += 1
+            ag.shard.copy_(mine)
+            ag.publish()
+            ag.gemm(w.w, w.s, y, K.GEMV_BF16)
+
+        def nccl():
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, mine)
+            else:
+                gathered.copy_(mine)
+            K.linear8(gathered, w.w, w.s, y, K.GEMV_BF16)
+
+        res = {}
+        for name, fn in (("fused", fused), ("nccl", nccl)):
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.iters):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.iters
+            if world > 1:
+                t = torch.tensor([ms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = t.item()
+            res[name] = ms
+        flops = 2.0 * world * rows * N * Kd
+        nv = (world - 1) * rows * Kd * 2
+        roof = max(flops / (peak * 1e9), nv / (770.0 * 1e6))
+        if rank == 0:
+            emit({"case": "ag_gemm", "world": world, "rows_per_rank": rows, "N": N, "K": Kd, "ms_fused": res["fused"],
+                  "ms_nccl_allgather_plus_gemm": res["nccl"], "roofline_ms": roof,
+                  "frac_of_roofline_fused": roof / res["fused"]})
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def bench_hc(args, T: Timer):
     """mHC post (4 streams) fused with the next pre (24 mixing logits, Sinkhorn, collapse, rmsnorm) for R rows."""
     from glm53.ops import kernels as K
@@ -310,7 +377,7 @@ def bench_hc(args, T: Timer):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["moe", "gemv", "gemm", "kda", "mla", "ep", "hc", "all"])
+    ap.add_argument("case", choices=["moe", "gemv", "gemm", "kda", "mla", "ep", "hc", "ag", "all"])
     ap.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 64, 512, 8192])
     ap.add_argument("--rows", type=int, nargs="+", default=[8])
     ap.add_argument("--kda-rows", type=int, nargs="+", default=[8, 8192])
