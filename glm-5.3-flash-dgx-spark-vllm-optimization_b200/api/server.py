@@ -4,7 +4,12 @@
   GET  /v1/models              the served model
   POST /v1/completions         prompt (string or token ids), max_tokens, temperature, top_p, top_k, seed, stop,
                                stream (server-sent events)
-  POST /v1/chat/completions    messages (chat template of the byte tokenizer), same sampling fields, stream
+  POST /v1/chat/completions    messages (chat template of the byte tokenizer), same sampling fields, stream;
+                               reasoning_effort (placed before the first user turn); the answer is split into
+                               reasoning_content (<think> ... </think>) and content, and tool calls are parsed
+                               into message.tool_calls (api/parsers.py)
+  POST /v1/responses           Responses API: input (string or items; unknown item types skipped), instructions,
+                               max_output_tokens; output items reasoning / message / function_call
   GET  /metrics                Prometheus text: requests running / waiting, prompt / generation tokens, speculative
                                drafts / accepted tokens, prefix-cache hits / queries, finished requests
 
@@ -26,9 +31,10 @@ import time
 import uuid
 
 from ..engine.llm import SamplingParams
+from . import parsers
 
 try:  # the HTTP stack is optional for offline use
-    from fastapi import FastAPI, HTTPException, Request
+    from fastapi import Depends, FastAPI, HTTPException, Request
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 except ImportError:  # pragma: no cover
     FastAPI = None
@@ -102,10 +108,17 @@ def _stop_strings(body) -> list[str]:
     return [s] if isinstance(s, str) else list(s)
 
 
-def build_app(llm, model_name: str = "glm-5.3-flash"):
+def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None, reasoning: bool = True):
+    """``api_key``: when set, /v1 routes need ``Authorization: Bearer <api_key>``.  ``reasoning``: split
+    ``<think>`` reasoning from the answer and apply stop strings to the answer only."""
     if FastAPI is None:
         raise RuntimeError("fastapi is not installed")
-    app = FastAPI()
+
+    async def auth(req: Request):
+        if api_key and req.headers.get("authorization", "") != f"Bearer {api_key}":
+            raise HTTPException(status_code=401, detail="invalid API key")
+
+    app = FastAPI(dependencies=[Depends(auth)] if api_key else [])
     loop_holder = {"engine": EngineLoop(llm)}
     tok = llm.tokenizer
 
@@ -161,14 +174,12 @@ def build_app(llm, model_name: str = "glm-5.3-flash"):
                 text = tok.decode(toks)
                 delta = text[len(text_so_far):]
                 reason = item.get("reason")
-                for s in stops:
-                    k = text.find(s)
-                    if k >= 0:
-                        delta = text[len(text_so_far):k]
-                        text = text[:k]
-                        reason = "stop"
-                        item["finished"] = True
-                        break
+                k = parsers.stop_index(text, stops, reasoning)
+                if k >= 0:
+                    delta = text[len(text_so_far):k]
+                    text = text[:k]
+                    reason = "stop"
+                    item["finished"] = True
                 text_so_far = text
                 yield {"delta": delta, "tokens": item["tokens"], "finished": item["finished"], "reason": reason,
                        "all": toks, "text": text}
@@ -179,7 +190,19 @@ def build_app(llm, model_name: str = "glm-5.3-flash"):
             if chat:
                 if delta is not None:
                     return {"index": 0, "delta": {"role": "assistant", "content": delta}, "finish_reason": reason}
-                return {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
+                msg = {"role": "assistant", "content": text}
+                if reasoning:
+                    r_text, text = parsers.split_reasoning(text)
+                    msg["content"] = text
+                    if r_text:
+                        msg["reasoning_content"] = r_text
+                if body.get("tools"):
+                    content, calls = parsers.parse_tool_calls(msg["content"])
+                    if calls:
+                        msg["content"] = content or None
+                        msg["tool_calls"] = calls
+                        reason = "tool_calls"
+                return {"index": 0, "message": msg, "finish_reason": reason}
             return {"index": 0, "text": delta if delta is not None else text, "finish_reason": reason,
                     "token_ids": toks}
 
@@ -224,8 +247,37 @@ def build_app(llm, model_name: str = "glm-5.3-flash"):
     async def chat(req: Request):
         body = await req.json()
         msgs = [m for m in body.get("messages", []) if isinstance(m, dict)]     # skip unknown input items
-        ids = tok.encode(tok.apply_chat_template(msgs))
+        ids = tok.encode(tok.apply_chat_template(msgs, reasoning_effort=body.get("reasoning_effort"),
+                                                 tools=body.get("tools")))
         return await _run(ids, _params(body, tok), _stop_strings(body), True, bool(body.get("stream")), body)
+
+    @app.post("/v1/responses")
+    async def responses(req: Request):
+        body = await req.json()
+        msgs = parsers.responses_input_to_messages(body.get("input"), body.get("instructions"))
+        ids = tok.encode(tok.apply_chat_template(msgs, reasoning_effort=(body.get("reasoning") or {}).get("effort"),
+                                                 tools=body.get("tools")))
+        cbody = dict(body, max_tokens=body.get("max_output_tokens") or body.get("max_tokens") or 64)
+        res = await _run(ids, _params(cbody, tok), _stop_strings(body), True, False, cbody)
+        data = json.loads(res.body)
+        msg = data["choices"][0]["message"]
+        output = []
+        if msg.get("reasoning_content"):
+            output.append({"type": "reasoning", "id": f"rs_{uuid.uuid4().hex[:16]}",
+                           "summary": [{"type": "summary_text", "text": msg["reasoning_content"]}]})
+        for call in msg.get("tool_calls") or []:
+            output.append({"type": "function_call", "id": f"fc_{uuid.uuid4().hex[:16]}", "call_id": call["id"],
+                           "name": call["function"]["name"], "arguments": call["function"]["arguments"]})
+        if msg.get("content"):
+            output.append({"type": "message", "id": f"msg_{uuid.uuid4().hex[:16]}", "role": "assistant",
+                           "status": "completed",
+                           "content": [{"type": "output_text", "text": msg["content"], "annotations": []}]})
+        u = data["usage"]
+        return JSONResponse({"id": "resp_" + data["id"], "object": "response", "created_at": data["created"],
+                             "model": model_name, "status": "completed", "output": output,
+                             "output_text": msg.get("content") or "",
+                             "usage": {"input_tokens": u["prompt_tokens"], "output_tokens": u["completion_tokens"],
+                                       "total_tokens": u["total_tokens"]}})
 
     return app
 
@@ -240,12 +292,15 @@ def serve(argv=None):
     ap.add_argument("--prefill-chunk", type=int, default=2048)
     ap.add_argument("--no-spec", action="store_true")
     ap.add_argument("--served-model-name", default="glm-5.3-flash")
+    ap.add_argument("--api-key", default=None, help="require Authorization: Bearer <key> on /v1 routes")
+    ap.add_argument("--no-reasoning-parser", action="store_true")
     args = ap.parse_args(argv)
     import uvicorn
     from .offline import LLM, LLMOptions
     llm = LLM(LLMOptions(model=args.model, max_seqs=args.max_seqs, max_model_len=args.max_model_len,
                          prefill_chunk=args.prefill_chunk, speculative=not args.no_spec))
-    uvicorn.run(build_app(llm, args.served_model_name), host=args.host, port=args.port, log_level="info")
+    uvicorn.run(build_app(llm, args.served_model_name, api_key=args.api_key, reasoning=not args.no_reasoning_parser),
+                host=args.host, port=args.port, log_level="info")
 
 
 if __name__ == "__main__":

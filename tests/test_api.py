@@ -63,3 +63,50 @@ def test_metrics(client):
 def test_too_long_is_400(client):
     r = client.post("/v1/completions", json={"prompt": list(range(3000)), "max_tokens": 10})
     assert r.status_code == 400
+
+
+def test_parsers_reasoning_tools_stops():
+    from glm53.api import parsers
+    r, a = parsers.split_reasoning("<think>plan it</think>\nThe answer")
+    assert (r, a) == ("plan it", "The answer")
+    assert parsers.split_reasoning("plain")[1] == "plain"
+    text = "pre <tool_call>get_weather\n<arg_key>city</arg_key>\n<arg_value>Paris</arg_value>\n" \
+           "<arg_key>days</arg_key>\n<arg_value>3</arg_value>\n</tool_call>"
+    content, calls = parsers.parse_tool_calls(text)
+    assert content == "pre" and calls[0]["function"]["name"] == "get_weather"
+    assert json.loads(calls[0]["function"]["arguments"]) == {"city": "Paris", "days": 3}
+    _, calls = parsers.parse_tool_calls('<tool_call>{"name": "f", "arguments": {"x": 1}}</tool_call>')
+    assert calls[0]["function"]["name"] == "f"
+    # stops inside the reasoning are ignored
+    t = "<think>STOP here</think>answer STOP"
+    assert parsers.stop_index(t, ["STOP"], True) == t.rfind("STOP")
+    assert parsers.stop_index(t, ["STOP"], False) == t.find("STOP")
+    msgs = parsers.responses_input_to_messages(
+        [{"type": "message", "role": "user", "content": [{"type": "input_text", "text": "hi"}]},
+         {"type": "reasoning", "summary": []}, {"type": "unknown_thing"}], "be brief")
+    assert msgs == [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hi"}]
+
+
+def test_chat_template_effort_placement():
+    tok = ByteTokenizer(512)
+    sys_msg = {"role": "system", "content": "S"}
+    a = tok.apply_chat_template([sys_msg, {"role": "user", "content": "u"}], reasoning_effort="high")
+    b = tok.apply_chat_template([sys_msg, {"role": "user", "content": "u"}], reasoning_effort="low")
+    head = tok.apply_chat_template([sys_msg], add_generation_prompt=False)
+    assert a.startswith(head) and b.startswith(head) and "Reasoning effort: high" in a
+
+
+def test_responses_endpoint(client):
+    r = client.post("/v1/responses", json={"input": [{"role": "user", "content": "hi"}, {"type": "bogus"}],
+                                           "max_output_tokens": 6})
+    body = r.json()
+    assert r.status_code == 200 and body["object"] == "response" and body["usage"]["output_tokens"] == 6
+
+
+def test_api_key():
+    from fastapi.testclient import TestClient
+    from glm53.api.server import build_app
+    app = build_app(FakeLLM(), "glm-test", api_key="sekret")
+    with TestClient(app) as c:
+        assert c.get("/v1/models").status_code == 401
+        assert c.get("/v1/models", headers={"Authorization": "Bearer sekret"}).status_code == 200
