@@ -34,6 +34,8 @@ class LLMOptions:
     checkpoints: int = 4
     cuda_graphs: bool = True
     layers: int | None = None           # truncate the full architecture (smoke use)
+    overrides: dict | None = None       # checkpoint name -> tensor or file replacing it at load
+    override_sha256: dict | None = None  # checkpoint name -> expected sha256 of the override file
 
 
 class LLM:
@@ -50,6 +52,8 @@ class LLM:
                 from ..config import full_config
                 cfg = full_config(opts.layers) if opts.model in ("full", "glm53", "glm-5.3-flash") else cfg
             src = W.RandomSource(cfg, seed=opts.seed, device=dev)
+        if opts.overrides:
+            src = W.OverrideSource(src, opts.overrides, opts.override_sha256)
         self.cfg: ModelConfig = cfg
         t0 = time.time()
         self.weights = W.prepare(src, cfg, rank=rank, world=world, device=dev)
@@ -71,6 +75,8 @@ class LLM:
                           cuda_graphs=opts.cuda_graphs)
         self.engine = LLMEngine(self.backend, ec, eos=tuple(cfg.eos))
         self.tokenizer = ByteTokenizer(cfg.vocab)
+        from ..utils.trace import maybe_attach
+        self.tracer = maybe_attach(self.engine, comm, rank)          # GLM53_TRACE=<path>: per-step records
 
     def generate(self, prompts, params: SamplingParams | None = None) -> list[dict]:
         """prompts: strings (byte-tokenized) or token-id lists.  Returns per prompt the token ids and text."""

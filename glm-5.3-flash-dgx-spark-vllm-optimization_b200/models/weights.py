@@ -228,6 +228,51 @@ class DictSource(TensorSource):
         return self.d[name]
 
 
+class OverrideSource(TensorSource):
+    """A source with some tensors replaced at load (the reference's o_proj transplant of layers 15-45,
+    README.md:43, data/ablit_transplant_sha256.csv): ``overrides`` maps a checkpoint name to a tensor or to a
+    ``.pt`` / ``.safetensors`` file holding it; ``sha256`` (optional) maps the same names to the expected digest of the
+    file bytes, and a mismatch refuses to load.  Shapes must match the base tensor."""
+
+    def __init__(self, base: TensorSource, overrides: dict, sha256: dict | None = None):
+        self.base, self.overrides, self.sha256 = base, dict(overrides), dict(sha256 or {})
+        for k in ("cfg", "device", "shapes"):
+            if hasattr(base, k):
+                setattr(self, k, getattr(base, k))
+
+    @staticmethod
+    def _digest(path: str) -> str:
+        import hashlib
+        h = hashlib.sha256()
+        with open(path, "rb") as f:
+            for blk in iter(lambda: f.read(1 << 20), b""):
+                h.update(blk)
+        return h.hexdigest()
+
+    def get(self, name):
+        if name not in self.overrides:
+            return self.base.get(name)
+        v = self.overrides[name]
+        if isinstance(v, str):
+            if name in self.sha256 and self._digest(v) != self.sha256[name].lower():
+                raise ValueError(f"override for {name}: sha256 mismatch ({v})")
+            if v.endswith(".safetensors"):
+                from safetensors.torch import load_file
+                d = load_file(v)
+                v = d[name] if name in d else next(iter(d.values()))
+            else:
+                v = torch.load(v, map_location="cpu", weights_only=True)
+        ref = self.base.get(name)
+        if tuple(v.shape) != tuple(ref.shape):
+            raise ValueError(f"override for {name}: shape {tuple(v.shape)} != {tuple(ref.shape)}")
+        return v.to(ref.dtype)
+
+    def experts(self, layer, proj, n_experts):
+        if not any(k.startswith(f"{P}layers.{layer}.mlp.experts.") for k in self.overrides):
+            return self.base.experts(layer, proj, n_experts)
+        return TensorSource.experts(self, layer, proj, n_experts)
+
+
 class SafetensorsSource(TensorSource):
     """Reads a (sharded) safetensors checkpoint directory lazily, tensor by tensor."""
 

@@ -119,3 +119,25 @@ def test_oracle_dsa_sparse_rows(tiny_cfg, tiny_weights):
     sel = index_select(c, st, qi, hw, t)
     assert len(sel) == (c.pools_selected - 1) * c.kpool + (t % c.kpool) + 1
     assert sel == sorted(sel) and sel[-1] == t
+
+
+def test_override_source_sha_and_shape(tmp_path, tiny_cfg):
+    import hashlib
+    import pytest
+    import torch
+    from glm53.models import weights as W
+    base = W.RandomSource(tiny_cfg, seed=0, device="cpu")
+    name = next(n for n in base.shapes if n.endswith("self_attn.o_proj.weight"))
+    ref = base.get(name)
+    new = torch.ones_like(ref)
+    path = str(tmp_path / "o.pt")
+    torch.save(new, path)
+    digest = hashlib.sha256(open(path, "rb").read()).hexdigest()
+    src = W.OverrideSource(base, {name: path}, {name: digest})
+    assert torch.equal(src.get(name), new)
+    other = next(n for n in base.shapes if n != name and not n.endswith(".trellis"))
+    assert torch.equal(src.get(other), base.get(other))
+    with pytest.raises(ValueError):
+        W.OverrideSource(base, {name: path}, {name: "0" * 64}).get(name)
+    with pytest.raises(ValueError):
+        W.OverrideSource(base, {name: torch.ones(3)}).get(name)

@@ -2,6 +2,7 @@
 adaptive K, chunked prefill, paging and prefix reuse with KDA checkpoints, concurrency, limits."""
 
 import pytest
+import torch
 
 from glm53.engine.kv_manager import KVManager, OutOfPages, PageAllocator, SeqCache, page_hash
 from glm53.engine.llm import EngineConfig, LLMEngine, SamplingParams
@@ -106,3 +107,42 @@ def test_kv_manager_slots():
         kv.grow(sc, 40)
     kv.free(sc)
     assert kv.alloc.num_free == 16
+
+
+def test_step_tracer_records(tmp_path):
+    """Per-step trace records (host phases, collectives) from the tracer on the fake backend."""
+    import json
+    from glm53.utils.trace import StepTracer, rank_skew
+    from glm53.engine.llm import EngineConfig, LLMEngine, SamplingParams
+
+    class Comm:
+        def all_reduce(self, t):
+            return t
+    eng = LLMEngine(FakeBackend(), EngineConfig(max_seqs=2, page_size=16, num_pages=64, max_model_len=512,
+                                                prefill_chunk=32, cuda_graphs=False))
+    comm = Comm()
+    tr = StepTracer(str(tmp_path / "trace"), 0).attach(eng, comm)
+    eng.add_request(list(range(20, 60)), SamplingParams(max_tokens=5))
+    while eng.has_work():
+        eng.step()
+        comm.all_reduce(torch.zeros(4))
+    tr.close()
+    recs = [json.loads(l) for l in open(tr.path)]
+    assert len(recs) >= 2 and all(r["rank"] == 0 for r in recs)
+    assert any("backend.prefill" in r["phases_ms"] for r in recs)
+    assert rank_skew([tr.path])[0]["start_skew_ms"] == 0.0
+
+
+def test_profiler_signal_and_memory_report(tmp_path):
+    import os
+    import signal
+    from glm53.utils.runtime_helpers import install_profiler_signal, memory_report
+    eng = LLMEngine(FakeBackend(), EngineConfig(max_seqs=2, page_size=16, num_pages=64, max_model_len=512,
+                                                prefill_chunk=32, cuda_graphs=False))
+    ctl = install_profiler_signal(eng, steps=2, out_dir=str(tmp_path))
+    os.kill(os.getpid(), signal.SIGUSR2)
+    eng.add_request(list(range(20, 40)), SamplingParams(max_tokens=6))
+    while eng.has_work():
+        eng.step()
+    assert os.path.exists(ctl.last_path)
+    assert isinstance(memory_report(), dict)
