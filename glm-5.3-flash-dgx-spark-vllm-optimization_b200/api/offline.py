@@ -36,6 +36,7 @@ class LLMOptions:
     layers: int | None = None           # truncate the full architecture (smoke use)
     overrides: dict | None = None       # checkpoint name -> tensor or file replacing it at load
     override_sha256: dict | None = None  # checkpoint name -> expected sha256 of the override file
+    vtrim_tau: float = 0.0              # verify trimming by drafter confidence (0: off)
 
 
 class LLM:
@@ -72,7 +73,7 @@ class LLM:
                           max_model_len=opts.max_model_len, prefill_chunk=opts.prefill_chunk,
                           speculative=opts.speculative, k_set=opts.k_set, k_fixed=opts.k_fixed,
                           force_accept=opts.force_accept, checkpoints=opts.checkpoints,
-                          cuda_graphs=opts.cuda_graphs)
+                          cuda_graphs=opts.cuda_graphs, vtrim_tau=opts.vtrim_tau)
         self.engine = LLMEngine(self.backend, ec, eos=tuple(cfg.eos))
         self.tokenizer = ByteTokenizer(cfg.vocab)
         from ..utils.trace import maybe_attach

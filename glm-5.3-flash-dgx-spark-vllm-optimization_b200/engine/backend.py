@@ -120,6 +120,24 @@ class GPUBackend:
         lg = self.drafter.forward(t, hidden, k)
         return self.draft_sampler(lg).tolist(), lg
 
+    @torch.no_grad()
+    def draft_confidence(self, logits: torch.Tensor) -> list[float]:
+        """Max softmax probability of each draft row over the whole (vocabulary-parallel) logits: each rank's
+        (max, sum exp(l - max)) pairs are gathered and combined, p_max = 1 / sum_j s_j exp(m_j - M)."""
+        lg = logits.float()
+        m = lg.max(-1).values
+        st = (lg - m[:, None]).exp().sum(-1)
+        if self.world > 1:
+            both = torch.stack([m, st]).flatten()
+            out = torch.empty(self.world * both.numel(), device=both.device)
+            self.comm.all_gather(out, both)
+            g = out.view(self.world, 2, -1)
+            M = g[:, 0].max(0).values
+            S = (g[:, 1] * (g[:, 0] - M).exp()).sum(0)
+        else:
+            S = st
+        return (1.0 / S).tolist()
+
     # ---------------------------------------------------------------------------------------------------------
     def save_state(self, state_slot: int, cur: int, ck: int) -> None:
         for S, cS in zip(self.rt.S_pool, self.ck_S):

@@ -56,6 +56,8 @@ class EngineConfig:
     checkpoint_pages: int = 8              # checkpoint interval in pages
     prefill_first: bool = True             # a step with waiting prefill runs it before decode
     cuda_graphs: bool = True
+    vtrim_tau: float = 0.0                 # > 0: verify only the drafts before the first one whose drafter
+                                           # confidence (max softmax probability) is below tau
 
 
 class State(Enum):
@@ -112,7 +114,10 @@ class LLMEngine:
         self.done: dict[str, Request] = {}
         self._ids = itertools.count()
         self.metrics = {"prompt_tokens": 0, "generation_tokens": 0, "steps": 0, "spec_drafts": 0,
-                        "spec_accepted": 0, "prefix_cached_tokens": 0, "requests_finished": 0}
+                        "spec_accepted": 0, "prefix_cached_tokens": 0, "requests_finished": 0, "vtrim_cut": 0}
+        # verify-trim records (drafted K, verified after the trim), most recent last
+        import collections
+        self.vtrim_records = collections.deque(maxlen=4096)
 
     # ------------------------------------------------------------------------------------------------ requests
     def add_request(self, prompt: list[int], params: SamplingParams | None = None, rid: str | None = None) -> str:
@@ -261,8 +266,16 @@ class LLMEngine:
     def _draft(self, r: Request) -> None:
         k = r.adaptive.current()
         drafts, lg = self.b.draft(r.output[-1], r.hidden, k)
-        r.drafts = drafts[:k]
-        r.draft_logits = lg[:k].clone() if r.params.temperature > 0 else None
+        n = k
+        if self.cfg.vtrim_tau > 0 and not self.cfg.force_accept:
+            # verify trimming (the reference's n* rule, code/fork/glm53_spec_vtrim.py:11-23): rows past the first
+            # low-confidence draft are unlikely to be accepted, so they are not verified
+            conf = self.b.draft_confidence(lg[:k])
+            n = next((i for i, c in enumerate(conf) if c < self.cfg.vtrim_tau), k)
+            self.metrics["vtrim_cut"] += k - n
+            self.vtrim_records.append((k, n))
+        r.drafts = drafts[:n]
+        r.draft_logits = lg[:n].clone() if r.params.temperature > 0 else None
 
     def _decode_step(self, reqs: list[Request]) -> list[RequestOutput]:
         spec = self.cfg.speculative and self.b.drafter is not None

@@ -380,6 +380,29 @@ class RandomSource(TensorSource):
         return Exl3Stack(tr, su, sv)
 
 
+def to_device(obj, device):
+    """A copy of prepared weights (dataclasses, lists, tensors) on another device (e.g. CPU-generated weights
+    moved to the GPU so that both sides of a comparison hold identical values)."""
+    import copy
+    if isinstance(obj, torch.Tensor):
+        return obj.to(device)
+    if isinstance(obj, list):
+        return [to_device(v, device) for v in obj]
+    if isinstance(obj, dict):
+        return {k: to_device(v, device) for k, v in obj.items()}
+    if hasattr(obj, "__dataclass_fields__"):
+        o = copy.copy(obj)
+        for k in obj.__dataclass_fields__:
+            setattr(o, k, to_device(getattr(obj, k), device))
+        if hasattr(o, "device"):
+            try:
+                o.device = torch.device(device)
+            except (AttributeError, TypeError):
+                pass
+        return o
+    return obj
+
+
 def checkpoint_shapes(cfg: ModelConfig) -> dict[str, tuple[tuple[int, ...], str]]:
     """name -> (shape, init kind) for every tensor of the checkpoint (EXL3 experts listed per expert)."""
     c = cfg

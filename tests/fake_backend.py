@@ -87,6 +87,11 @@ class FakeBackend:
             h.append(t)
         return drafts, torch.stack([onehot(t) for t in drafts])
 
+    def draft_confidence(self, logits):
+        """softmax max-probability of the one-hot-like rows, lowered for rows the drafter got wrong"""
+        p = torch.softmax(logits.float(), -1).max(-1).values
+        return [float(x) * (0.1 if self.err and (i + 1) % self.err == 0 else 1.0) for i, x in enumerate(p)]
+
     def save_state(self, slot, cur, ck):
         self.calls["save"] += 1
         self.ck[ck] = list(self.hist[slot])

@@ -141,3 +141,14 @@ def test_override_source_sha_and_shape(tmp_path, tiny_cfg):
         W.OverrideSource(base, {name: path}, {name: "0" * 64}).get(name)
     with pytest.raises(ValueError):
         W.OverrideSource(base, {name: torch.ones(3)}).get(name)
+
+
+def test_kl_harness_reference_vs_itself(tiny_cfg, tiny_weights):
+    """The harness on the CPU oracle against itself: zero KL, full top-1 agreement, finite NLL and intervals."""
+    import torch
+    from glm53.utils.klh import compare, reference_provider
+    run = reference_provider(tiny_weights)
+    seqs = [torch.randint(16, tiny_cfg.vocab, (24,), generator=torch.Generator().manual_seed(1)).tolist()]
+    res = compare(run, run, seqs, block=4)
+    assert res["kl_mean"] < 1e-12 and res["top1_agree"] == 1.0 and res["aa_kl_mean"] < 1e-12
+    assert res["positions"] == 23 and res["nll_a"] > 0

@@ -146,3 +146,16 @@ def test_profiler_signal_and_memory_report(tmp_path):
         eng.step()
     assert os.path.exists(ctl.last_path)
     assert isinstance(memory_report(), dict)
+
+
+def test_vtrim_cuts_verify_rows_keeps_output():
+    """Verify trimming: drafts after the first low-confidence one are not verified; greedy output unchanged."""
+    prompt = list(range(30, 70))
+    outs = {}
+    for tau in (0.0, 0.5):
+        eng = LLMEngine(FakeBackend(), EngineConfig(max_seqs=2, page_size=16, num_pages=64, max_model_len=512,
+                                                    prefill_chunk=32, cuda_graphs=False, k_fixed=7, vtrim_tau=tau))
+        outs[tau] = eng.generate([prompt], SamplingParams(max_tokens=30))[0]
+        if tau > 0:
+            assert eng.metrics["vtrim_cut"] > 0 and len(eng.vtrim_records) > 0
+    assert outs[0.0] == outs[0.5] == reference_greedy(prompt, 30)
