@@ -851,7 +851,10 @@ void rejection_sample(const Tensor& target_probs, const Tensor& draft_probs, con
 
 }  // namespace
 
+void register_exl3_codec(pybind11::module& m);   // exl3_codec.cpp (host codec)
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  register_exl3_codec(m);
   m.doc() = "glm53 sm_100a kernels";
   m.def("gemv", &gemv);
   m.def("gemm_w8", &gemm_w8);

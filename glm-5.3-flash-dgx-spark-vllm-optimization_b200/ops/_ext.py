@@ -27,7 +27,7 @@ _mod = None
 
 
 def sources() -> list[str]:
-    return sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + [os.path.join(CSRC, "bindings.cpp")]
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(glob.glob(os.path.join(CSRC, "*.cpp")))
 
 
 def so_path() -> str:

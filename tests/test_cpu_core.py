@@ -152,3 +152,17 @@ def test_kl_harness_reference_vs_itself(tiny_cfg, tiny_weights):
     res = compare(run, run, seqs, block=4)
     assert res["kl_mean"] < 1e-12 and res["top1_agree"] == 1.0 and res["aa_kl_mean"] < 1e-12
     assert res["positions"] == 23 and res["nll_a"] > 0
+
+
+def test_host_codec_matches_format_oracle():
+    """The C++ host codec (csrc/exl3_codec.cpp): all 65536 codebook states and a whole-matrix tile decode equal
+    the Python format oracle bit for bit (runs on the CPU when the extension is built)."""
+    import pytest
+    import torch
+    from glm53.ops import _ext, exl3
+    C = _ext.load(build_if_missing=False)
+    if C is None:
+        pytest.skip("extension not built")
+    assert torch.equal(C.exl3_codebook_cpu().view(torch.int16), exl3.codebook().view(torch.int16))
+    tr, _, _ = exl3.random_linear(512, 256, generator=torch.Generator().manual_seed(3))
+    assert torch.equal(C.exl3_decode_cpu(tr, 4).view(torch.int16), exl3.unpack(tr).view(torch.int16))
