@@ -695,10 +695,22 @@ void rope_q(const Tensor& q, const Tensor& positions, int64_t nope, int64_t rope
         "rope_q");
 }
 
+// the tensor-core sparse MLA kernel is used (where its shape applies) unless GLM53_TC_MLA=0
+static bool tc_mla_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("GLM53_TC_MLA");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+static bool mla_tc_shape(const MlaAttnArgs& a) { return a.L == 512 && a.rope == 0 && a.H >= 1 && a.H <= 64; }
+
+// tensor_cores: -1 default (GLM53_TC_MLA), 0 CUDA-core kernel, 1 tensor-core kernel (error if the shape does not fit)
 void mla_decode(const Tensor& q_lat, const OptT& q_pe, int64_t q_pe_ld, int64_t q_pe_hs, const Tensor& kv_cache,
                 const Tensor& kv_scale, const OptT& kpe_cache, const Tensor& sel, const Tensor& sel_count,
                 int64_t rope, double sm_scale, int64_t splits, const Tensor& part_o, const Tensor& part_ml,
-                const Tensor& o_lat) {
+                const Tensor& o_lat, int64_t tensor_cores) {
   MlaAttnArgs a{};
   a.q_lat = P<const __nv_bfloat16>(q_lat);
   a.q_pe = P<const __nv_bfloat16>(q_pe);
@@ -720,6 +732,9 @@ void mla_decode(const Tensor& q_lat, const OptT& q_pe, int64_t q_pe_ld, int64_t 
   a.part_ml = P<float>(part_ml);
   a.o_lat = P<__nv_bfloat16>(o_lat);
   TORCH_CHECK(part_o.numel() >= (int64_t)a.R * a.splits * a.H * a.L, "part_o too small");
+  a.use_tc = (tensor_cores < 0 ? tc_mla_enabled() : tensor_cores > 0) && mla_tc_shape(a) ? 1 : 0;
+  TORCH_CHECK(tensor_cores <= 0 || a.use_tc, "tensor-core MLA needs L = 512, no rope and at most 64 heads");
+  a.err = P<int>(err_word(q_lat));
   check(g53_mla_decode(a, stream()), "mla_decode");
 }
 
@@ -891,7 +906,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
   m.def("mla_prep", &mla_prep);
   m.def("rope_q", &rope_q);
-  m.def("mla_decode", &mla_decode);
+  m.def("mla_decode", &mla_decode, py::arg("q_lat"), py::arg("q_pe"), py::arg("q_pe_ld"), py::arg("q_pe_hs"),
+        py::arg("kv_cache"), py::arg("kv_scale"), py::arg("kpe_cache"), py::arg("sel"), py::arg("sel_count"),
+        py::arg("rope"), py::arg("sm_scale"), py::arg("splits"), py::arg("part_o"), py::arg("part_ml"),
+        py::arg("o_lat"), py::arg("tensor_cores") = -1);
   m.def("dsa_update", &dsa_update);
   m.def("dsa_select", &dsa_select);
   m.def("argmax_rows", &argmax_rows);

@@ -265,8 +265,12 @@ struct MlaAttnArgs {
   float* part_o;                // [R, splits, H, L] scratch
   float* part_ml;               // [R, splits, H, 2]
   __nv_bfloat16* o_lat;         // [R, H, L] out (bf16)
+  int use_tc;                   // 1: tensor-core kernel (L = 512, no rope, H <= 64); 0: CUDA-core kernel
+  int* err;                     // error word of the bounded waits (tensor-core kernel)
 };
 cudaError_t g53_mla_decode(const MlaAttnArgs& a, cudaStream_t st);
+// tensor-core attention only (no merge); splits > 1 leaves partials in part_o / part_ml
+cudaError_t g53_mla_attn_tc(const MlaAttnArgs& a, cudaStream_t st);
 
 struct DsaArgs {
   const float* iproj; int64_t ldi;  // [R, ID + IH + ID] fp32: index key | head weights | pool gate scores

@@ -333,6 +333,15 @@ cudaError_t g53_rope_q(__nv_bfloat16* q, int R, int H, int qk, int nope, int rop
 
 cudaError_t g53_mla_decode(const MlaAttnArgs& a, cudaStream_t st) {
   if (a.splits < 1 || a.splits > 16) return cudaErrorInvalidValue;
+  if (a.use_tc) {
+    cudaError_t e = g53_mla_attn_tc(a, st);
+    if (e != cudaSuccess) return e;
+    if (a.splits > 1) {
+      mla_merge_kernel<<<dim3(a.R, a.H), 128, 0, st>>>(a);
+      G53_CHECK_LAUNCH();
+    }
+    return cudaSuccess;
+  }
   dim3 grid(a.R, (a.H + 15) / 16, a.splits);
   if (a.L == 512 && a.rope == 0) mla_decode_kernel<512, 0><<<grid, 128, 0, st>>>(a);
   else if (a.L == 128 && a.rope == 32) mla_decode_kernel<128, 32><<<grid, 128, 0, st>>>(a);

@@ -216,13 +216,17 @@ def bench_mla(args, T: Timer):
         sc = torch.rand(slots, device="cuda") * 0.01
         sel = torch.randint(0, slots, (R, 2048), dtype=torch.int32, device="cuda")
         cnt = torch.full((R,), 2048, dtype=torch.int32, device="cuda")
-        splits = 4 if R <= 16 else 1
-        po = torch.empty(R * splits * H * L, device="cuda")
-        pm = torch.empty(R * splits * H * 2, device="cuda")
-        o = torch.empty_like(q)
-        ms = T(lambda: K.C().mla_decode(q, None, 0, 0, kv, sc, None, sel, cnt, 0, 0.0625, splits, po, pm, o))
         fl = 4.0 * R * H * 2048 * L
-        emit({"case": "mla_sparse_attn", "rows": R, "heads": H, "keys": 2048, "ms": ms, "tflops": fl / ms / 1e9})
+        for tcores in (0, 1):
+            # decode rows: key splits so that rows x splits fills the SMs (merged by a second kernel)
+            splits = (4 if not tcores else max(1, min(16, 148 // R))) if R <= 16 else 1
+            po = torch.empty(R * splits * H * L, device="cuda")
+            pm = torch.empty(R * splits * H * 2, device="cuda")
+            o = torch.empty_like(q)
+            ms = T(lambda: K.C().mla_decode(q, None, 0, 0, kv, sc, None, sel, cnt, 0, 0.0625, splits, po, pm, o,
+                                            tcores))
+            emit({"case": "mla_sparse_attn", "kernel": "tcgen05" if tcores else "mma.sync", "rows": R, "heads": H,
+                  "keys": 2048, "splits": splits, "ms": ms, "tflops": fl / ms / 1e9})
 
 
 def bench_ep(args, T: Timer):
