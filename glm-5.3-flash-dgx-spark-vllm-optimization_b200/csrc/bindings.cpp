@@ -731,9 +731,13 @@ void mla_decode(const Tensor& q_lat, const OptT& q_pe, int64_t q_pe_ld, int64_t 
   a.part_o = P<float>(part_o);
   a.part_ml = P<float>(part_ml);
   a.o_lat = P<__nv_bfloat16>(o_lat);
-  TORCH_CHECK(part_o.numel() >= (int64_t)a.R * a.splits * a.H * a.L, "part_o too small");
   a.use_tc = (tensor_cores < 0 ? tc_mla_enabled() : tensor_cores > 0) && mla_tc_shape(a) ? 1 : 0;
   TORCH_CHECK(tensor_cores <= 0 || a.use_tc, "tensor-core MLA needs L = 512, no rope and at most 64 heads");
+  // split partials (the CUDA-core kernel stages every row's partials, the tensor-core kernel only split rows)
+  if (!a.use_tc || a.splits > 1) {
+    TORCH_CHECK(part_o.numel() >= (int64_t)a.R * a.splits * a.H * a.L, "part_o too small");
+    TORCH_CHECK(part_ml.numel() >= (int64_t)a.R * a.splits * a.H * 2, "part_ml too small");
+  }
   a.err = P<int>(err_word(q_lat));
   check(g53_mla_decode(a, stream()), "mla_decode");
 }

@@ -41,7 +41,7 @@ class RuntimeConfig:
     block_size: int = 64
     max_blocks: int = 128         # page-table width per sequence
     decode_rows: int = 16         # forwards of at most this many rows keep per-layer KDA window inputs (replay)
-    mla_splits: int = 4           # key splits of the decode attention
+    mla_splits: int = 16          # most key splits of the decode attention (rows x splits fill the SMs)
     moe_chunk: int = 256          # rows per routed-MoE launch group of the decode path (routing kernel capacity)
     moe_prefill_rows: int = 8192  # rows per routed-MoE launch group of the prefill (tcgen05) path
     attn_chunk: int = 1024        # rows per attention launch group (scratch bound)
@@ -177,8 +177,11 @@ class Runtime:
             self.sel = torch.zeros(AR, max(self.max_sel, c.index_topk), dtype=i32, device=dev)
             self.sel_count = torch.zeros(AR, dtype=i32, device=dev)
             self.splits = rc.mla_splits
-            self.part_o = torch.zeros(AR * rc.mla_splits * H * L, dtype=f32, device=dev)
-            self.part_ml = torch.zeros(AR * rc.mla_splits * H * 2, dtype=f32, device=dev)
+            self.sms = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
+            # partials: decode-sized forwards split the keys; the CUDA-core kernel also stages unsplit rows here
+            PR = max(min(AR, rc.decode_rows) * rc.mla_splits, AR)
+            self.part_o = torch.zeros(PR * H * L, dtype=f32, device=dev)
+            self.part_ml = torch.zeros(PR * H * 2, dtype=f32, device=dev)
         # --- MLP / MoE ---
         MR = min(R, rc.moe_chunk)
         tk = c.top_k
@@ -420,7 +423,8 @@ class Runtime:
         K.linear8(self.qr[:R], a.index.wq_b.w, a.index.wq_b.s, self.qi[:R])
         AR = self.sel.shape[0]
         sm_scale = c.qk_dim ** -0.5
-        splits = self.splits if R <= self.rc.decode_rows else 1
+        # decode: split each row's keys so that rows x splits covers the SMs about twice (partials merged after)
+        splits = max(1, min(self.splits, 2 * self.sms // max(R, 1))) if R <= self.rc.decode_rows else 1
         for r0 in range(0, R, AR):
             r1 = min(R, r0 + AR)
             n = r1 - r0
