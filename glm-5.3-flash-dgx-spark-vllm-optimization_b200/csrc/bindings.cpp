@@ -488,10 +488,20 @@ Tensor exl3_unpack(const Tensor& tr, int64_t K, int64_t N) {
 }
 
 // ------------------------------------------------------------------------------------------------- mHC / norms
+// prefill-sized mHC launches use the tensor-core partial pass unless GLM53_TC_HC=0
+static bool tc_hc_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("GLM53_TC_HC");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 void hc_post_pre(const Tensor& X, const OptT& branch, const OptT& post, const OptT& comb, const OptT& fn,
                  const OptT& base, const OptT& hscale, const OptT& norm_w, const OptT& normed,
                  const OptT& post_out, const OptT& comb_out, const Tensor& part, double eps, double hc_eps,
-                 int64_t iters) {
+                 int64_t iters, int64_t tensor_cores) {
   HcArgs a{};
   a.X = P<__nv_bfloat16>(X);
   a.branch = P<const float>(branch);
@@ -513,6 +523,8 @@ void hc_post_pre(const Tensor& X, const OptT& branch, const OptT& post, const Op
   a.iters = (int)iters;
   TORCH_CHECK(X.is_contiguous(), "X must be contiguous [R, S, D]");
   a.gath = nullptr;
+  a.use_tc = (tensor_cores < 0 ? tc_hc_enabled() : tensor_cores > 0) ? 1 : 0;
+  a.err = P<int>(err_word(X));
   TORCH_CHECK(part.numel() >= (int64_t)a.R * (a.D / 64) * 32, "part scratch too small");
   check(g53_hc_post_pre(a, stream()), "hc_post_pre");
 }
@@ -891,7 +903,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("exl3_rot_in", &exl3_rot_in);
   m.def("ep_moe_step", &ep_moe_step);
   m.def("exl3_unpack", &exl3_unpack);
-  m.def("hc_post_pre", &hc_post_pre);
+  m.def("hc_post_pre", &hc_post_pre, py::arg("X"), py::arg("branch"), py::arg("post"), py::arg("comb"), py::arg("fn"),
+        py::arg("base"), py::arg("hscale"), py::arg("norm_w"), py::arg("normed"), py::arg("post_out"),
+        py::arg("comb_out"), py::arg("part"), py::arg("eps"), py::arg("hc_eps"), py::arg("iters"),
+        py::arg("tensor_cores") = -1);
   m.def("hc_post_pre_tp", &hc_post_pre_tp);
   m.def("gemv_push", &gemv_push);
   m.def("embed", &embed);

@@ -191,8 +191,12 @@ struct HcArgs {
   unsigned* epoch;            // consumptions of this parity so far (local)
   unsigned* done;             // CTA completion counter (local)
   int* err;
+  int use_tc;                 // 1: prefill-sized launches (R >= 256, S = 4, no fused reduce) use the tensor cores
+  int nb;                     // column blocks of `part` (set by the launcher)
 };
 cudaError_t g53_hc_post_pre(const HcArgs& a, cudaStream_t st);   // (optional post) then pre
+// tensor-core partial pass only (post + mixing dots + sums of squares into part [R, D / 512, 32])
+cudaError_t g53_hc_partial_tc(const HcArgs& a, cudaStream_t st);
 cudaError_t g53_embed(const int* ids, const __nv_bfloat16* table, int R, int D, int S, __nv_bfloat16* X,
                       cudaStream_t st);
 cudaError_t g53_stream_mean_norm(const __nv_bfloat16* X, int R, int S, int D, const __nv_bfloat16* w, float eps,

@@ -137,7 +137,7 @@ template <int S>
 __global__ void __launch_bounds__(512) hc_finish_kernel(HcArgs a) {
   constexpr int NM = 2 * S + S * S;
   const int r = blockIdx.x;
-  const int NB = a.D / kDB;
+  const int NB = a.nb;
   __shared__ float mix[32];
   __shared__ float pre_s[S], post_s[S], comb_s[S * S];
   __shared__ float red[32];
@@ -273,8 +273,19 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, in
 
 using namespace g53;
 
-cudaError_t g53_hc_post_pre(const HcArgs& a, cudaStream_t st) {
+cudaError_t g53_hc_post_pre(const HcArgs& args, cudaStream_t st) {
+  HcArgs a = args;
   if (a.D % kDB || a.D > 8192 || a.D % 8 || (a.S != 2 && a.S != 4)) return cudaErrorInvalidValue;
+  // prefill-sized launches: post + mixing dots on the tensor cores (column blocks of 512), then the same finish
+  if (a.use_tc && a.R >= 256 && a.S == 4 && a.fn && !a.gath && a.D % 512 == 0) {
+    a.nb = a.D / 512;
+    cudaError_t e = g53_hc_partial_tc(a, st);
+    if (e != cudaSuccess) return e;
+    hc_finish_kernel<4><<<a.R, 512, 0, st>>>(a);
+    G53_CHECK_LAUNCH();
+    return cudaSuccess;
+  }
+  a.nb = a.D / kDB;
   // decode-sized launches: one row per CTA (more CTAs in flight); prefill: kRB rows per CTA (fn reuse)
   dim3 g1(a.D / kDB, a.R <= kRB ? a.R : (a.R + kRB - 1) / kRB);
   if (a.S == 4) {

@@ -373,10 +373,11 @@ def bench_hc(args, T: Timer):
         normed = torch.empty(R, D, device=dev).to(torch.bfloat16)
         post_o, comb_o = torch.empty(R, S, device=dev), torch.empty(R, S, S, device=dev)
         part = torch.empty(R * (D // 64) * 32, device=dev)
-        ms = T(lambda: K.C().hc_post_pre(X, branch, post, comb, fn, base, hscale, norm_w, normed, post_o, comb_o,
-                                          part, 1e-5, 1e-6, 20))
-        emit({"case": "hc_post_pre", "rows": R, "ms": ms,
-              "GBps": (R * S * D * 2 * 2 + R * D * 4 + NM * S * D * 2) / ms / 1e6})
+        for tcores in ((1, 0) if R >= 256 else (0,)):
+            ms = T(lambda: K.C().hc_post_pre(X, branch, post, comb, fn, base, hscale, norm_w, normed, post_o,
+                                              comb_o, part, 1e-5, 1e-6, 20, tcores))
+            emit({"case": "hc_post_pre", "path": "tcgen05" if tcores else "cuda-core", "rows": R, "ms": ms,
+                  "GBps": (R * S * D * 2 * 2 + R * D * 4 + NM * S * D * 2 + R * D * 2 * 2) / ms / 1e6})
 
 
 def main(argv=None):

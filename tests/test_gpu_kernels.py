@@ -241,3 +241,45 @@ def test_moe_prefill_many_tokens_per_expert(C, tiny_cfg, tiny_weights):
     torch.cuda.synchronize()
     assert C.gemm_error(rt.branch) == 0
     torch.testing.assert_close(rt.branch[:rows].cpu(), ref, atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("rows", [300, 1024])
+@pytest.mark.parametrize("with_post", [True, False])
+def test_hc_post_pre_tensor_cores(C, rows, with_post):
+    """Prefill-sized mHC (4 streams, D = 4096): the tcgen05 partial pass (post + 24 mixing dots on the tensor
+    cores, 512-column blocks) against the fp32 reference and against the CUDA-core kernel."""
+    from types import SimpleNamespace
+    from glm53.models import reference as R
+    S, D = 4, 4096
+    g = torch.Generator().manual_seed(7)
+    X = (torch.randn(rows, S, D, generator=g)).to(torch.bfloat16)
+    branch = torch.randn(rows, D, generator=g)
+    fn = (torch.randn(2 * S + S * S, S * D, generator=g) * 0.02).to(torch.bfloat16)
+    base = torch.randn(2 * S + S * S, generator=g) * 0.1
+    scale = torch.tensor([1.0, 0.8, 1.2])
+    norm_w = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16)
+    post0 = torch.rand(rows, S, generator=g) * 2
+    comb0 = torch.softmax(torch.randn(rows, S, S, generator=g), -1)
+    cfg = SimpleNamespace(streams=S, eps=1e-6, hc_eps=1e-6, hc_iters=20)
+    Xn = R.hc_post(X.float(), branch, post0, comb0) if with_post else X.float()
+    normed_ref, post_ref, comb_ref = R.hc_pre(Xn, SimpleNamespace(fn=fn, base=base, scale=scale), norm_w.float(),
+                                              cfg)
+    outs = {}
+    for tcores in (1, 0):
+        Xd = X.to(DEV).contiguous()
+        normed = torch.empty(rows, D, dtype=torch.bfloat16, device=DEV)
+        post = torch.empty(rows, S, device=DEV)
+        comb = torch.empty(rows, S, S, device=DEV)
+        part = torch.empty(rows, D // 64, 32, device=DEV)
+        C.hc_post_pre(Xd, branch.to(DEV) if with_post else None, post0.to(DEV) if with_post else None,
+                      comb0.to(DEV) if with_post else None, fn.to(DEV), base.to(DEV), scale.to(DEV), norm_w.to(DEV),
+                      normed, post, comb, part, cfg.eps, cfg.hc_eps, cfg.hc_iters, tcores)
+        torch.cuda.synchronize()
+        outs[tcores] = (Xd.float().cpu(), normed.float().cpu(), post.cpu(), comb.cpu())
+    Xt, nt, pt, ct = outs[1]
+    torch.testing.assert_close(Xt, Xn, atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(Xt, outs[0][0], atol=0, rtol=0)          # same post arithmetic, bit for bit
+    torch.testing.assert_close(pt, post_ref, atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(ct, comb_ref, atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(nt, normed_ref, atol=3e-2, rtol=2e-2)
+    torch.testing.assert_close(pt, outs[0][2], atol=1e-5, rtol=1e-5)
