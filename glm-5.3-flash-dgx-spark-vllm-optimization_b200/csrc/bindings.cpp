@@ -27,7 +27,37 @@ void cuda_check(const Tensor& t, const char* name) {
 }
 
 // ------------------------------------------------------------------------------------------------- GEMV
-void gemv(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, int64_t mode, double limit) {
+// stream-K fp8 GEMV for large projections only with GLM53_STREAM_GEMV=1 (slower than the split-K kernel at 8
+// warps per SM: kept for measurements)
+static bool stream_gemv_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("GLM53_STREAM_GEMV");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+// per-device stream-K scratch: partials of up to SMs * 16 warps (2 tiles each) and zeroed per-tile counters
+static void stream_scratch(const Tensor& like, GemvArgs& p) {
+  static std::vector<Tensor> parts(64), cnts(64);
+  static std::vector<int> sms(64, 0);
+  const int dev = like.get_device();
+  if (!parts[dev].defined()) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    sms[dev] = n;
+    parts[dev] = torch::empty({(int64_t)n * 16 * 2 * 256}, like.options().dtype(at::kFloat));
+    cnts[dev] = torch::zeros({16384}, like.options().dtype(at::kInt));
+  }
+  p.stream_part = parts[dev].data_ptr<float>();
+  p.stream_cnt = cnts[dev].data_ptr<int>();
+  p.stream_tiles = 16384;
+  p.stream_sms = sms[dev];
+}
+
+void gemv(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, int64_t mode, double limit,
+          int64_t ks, int64_t cl) {
   cuda_check(x, "x"); cuda_check(w, "w"); cuda_check(y, "y");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16, "x must be bf16");
   TORCH_CHECK(x.stride(-1) == 1 && w.stride(-1) == 1 && y.stride(-1) == 1, "inner dims must be contiguous");
@@ -64,6 +94,9 @@ void gemv(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, 
   TORCH_CHECK(y.size(-2) >= p.M, "y rows");
   if (w.scalar_type() == at::kByte || w.scalar_type() == at::kFloat8_e4m3fn) {
     TORCH_CHECK(scale.has_value(), "fp8 weights need a scale");
+    if (stream_gemv_enabled()) stream_scratch(x, p);
+    p.force_ks = (int)ks;
+    p.force_cl = (int)cl;
     check(g53_gemv_fp8(p, stream()), "gemv_fp8");
   } else {
     TORCH_CHECK(w.scalar_type() == at::kBFloat16, "weights must be fp8 (uint8) or bf16");
@@ -475,9 +508,10 @@ void moe_prefill(const Tensor& tr0, const OptT& tr1, const Tensor& svh0, const O
   check(g53_moe_prefill(p, gate_up, stream()), "moe_prefill");
 }
 
-void moe_combine(const Tensor& yd, const Tensor& pair_of, int64_t top_k, const Tensor& out, bool accumulate) {
+// accumulate: 0 out = sum of the pair rows; 1 out += them (out first); 2 out = (sum of them) + out
+void moe_combine(const Tensor& yd, const Tensor& pair_of, int64_t top_k, const Tensor& out, int64_t accumulate) {
   check(g53_moe_combine(P<const float>(yd), P<const int>(pair_of), (int)out.size(0), (int)top_k, (int)out.size(1),
-                        P<float>(out), accumulate ? 1 : 0, stream()),
+                        P<float>(out), (int)accumulate, stream()),
         "moe_combine");
 }
 
@@ -887,7 +921,8 @@ void register_exl3_codec(pybind11::module& m);   // exl3_codec.cpp (host codec)
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_exl3_codec(m);
   m.doc() = "glm53 sm_100a kernels";
-  m.def("gemv", &gemv);
+  m.def("gemv", &gemv, py::arg("x"), py::arg("w"), py::arg("scale"), py::arg("y"), py::arg("mode"), py::arg("limit"),
+        py::arg("ks") = 0, py::arg("cl") = 0);
   m.def("gemm_w8", &gemm_w8);
   m.def("gemm_bf16", &gemm_bf16);
   m.def("gemm_w8a16", &gemm_w8a16);

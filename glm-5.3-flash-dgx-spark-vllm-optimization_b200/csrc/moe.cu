@@ -78,9 +78,7 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(RouteArgs a) {
       const int e = lane + 32 * i;
       cv[i] = e < a.E ? sigmoidf_(lg[e]) + a.bias[e] : -INFINITY;
     }
-    float sel_sum = 0.f;
     int pick_l = 0;
-    float wt_l = 0.f;
     for (int k = 0; k < a.top_k; ++k) {
       float best = -INFINITY;
       int bid = 0x7fffffff;
@@ -100,10 +98,12 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(RouteArgs a) {
         for (int i = 0; i < kPerLane; ++i)
           if (lane + 32 * i == bid) cv[i] = -INFINITY;
       }
-      const float w = sigmoidf_(lg[bid]);
-      sel_sum += w;
-      if (lane == k) { pick_l = bid; wt_l = w; }
+      if (lane == k) pick_l = bid;
     }
+    // routing weights of the picks: one load per lane (in parallel), summed over the picks in pick order
+    const float wt_l = lane < a.top_k ? sigmoidf_(lg[pick_l]) : 0.f;
+    float sel_sum = 0.f;
+    for (int k = 0; k < a.top_k; ++k) sel_sum += __shfl_sync(0xffffffffu, wt_l, k);
     const float inv = a.norm ? 1.f / (sel_sum + 1e-20f) : 1.f;
     if (lane < a.top_k) {
       a.topk_ids[r * a.top_k + lane] = pick_l;
@@ -464,10 +464,15 @@ __global__ void moe_combine_kernel(const float* yd, const int* pair_of, int R, i
   const int r = blockIdx.y;
   const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (d >= D) return;
-  float4 acc = accumulate ? *reinterpret_cast<const float4*>(out + (int64_t)r * D + d) : make_float4(0, 0, 0, 0);
+  // accumulate 1: out + y_0 + y_1 + ...; 2: (y_0 + y_1 + ...) + out (the routed sum first, then the value in out)
+  float4 acc = accumulate == 1 ? *reinterpret_cast<const float4*>(out + (int64_t)r * D + d) : make_float4(0, 0, 0, 0);
   for (int k = 0; k < top_k; ++k) {
     const float4 v = *reinterpret_cast<const float4*>(yd + (int64_t)pair_of[r * top_k + k] * D + d);
     acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  if (accumulate == 2) {
+    const float4 o = *reinterpret_cast<const float4*>(out + (int64_t)r * D + d);
+    acc.x += o.x; acc.y += o.y; acc.z += o.z; acc.w += o.w;
   }
   *reinterpret_cast<float4*>(out + (int64_t)r * D + d) = acc;
 }

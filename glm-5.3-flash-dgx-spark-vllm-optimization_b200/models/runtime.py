@@ -92,6 +92,13 @@ class Runtime:
         self.batch = Batch(rc, dev)
         self.px = None
         self._fused = False
+        # side stream for work that does not feed the next kernel (decode windows): the shared expert runs beside the
+        # routed experts (ALU-bound trellis decode vs a bandwidth-bound GEMV), the KDA output-gate projection beside
+        # the convolution and recurrence; forked and joined with events, so CUDA-graph capture records both branches
+        self.overlap = dev.type == "cuda" and os.environ.get("GLM53_OVERLAP", "1") == "1"
+        if self.overlap:
+            self.side = torch.cuda.Stream(device=dev)
+            self.ev_fork, self.ev_join = torch.cuda.Event(), torch.cuda.Event()
         # prefill chunks (rows >= GEMM_MIN_M) can push their partials from the tcgen05 GEMM epilogue as well
         # (GLM53_FUSED_TP_PREFILL=1).  Off by default: measured on 8192-row chunks it is slower than NCCL's ring
         # all-reduce (32k prefill 10.1k vs 11.3k tok/s at TP2, 10.5k vs 15.3k at TP4) -- every rank stores its whole
@@ -387,7 +394,15 @@ class Runtime:
         C3 = 3 * H * Dh
         K.linear8(self.normed[:R], k.in_proj.w, k.in_proj.s, proj)
         K.linear8(proj[:, C3:C3 + Dh], k.f_b.w, k.f_b.s, fb)
-        K.linear8(proj[:, C3 + Dh:C3 + 2 * Dh], k.g_b.w, k.g_b.s, self.kg[:R])
+        side = self.overlap and R <= K.GEMV_MAX_M
+        if side:        # output gate (read only by the gated norm) beside the convolution and recurrence
+            self.ev_fork.record()
+            with torch.cuda.stream(self.side):
+                self.side.wait_event(self.ev_fork)
+                K.linear8(proj[:, C3 + Dh:C3 + 2 * Dh], k.g_b.w, k.g_b.s, self.kg[:R])
+                self.ev_join.record()
+        else:
+            K.linear8(proj[:, C3 + Dh:C3 + 2 * Dh], k.g_b.w, k.g_b.s, self.kg[:R])
         seq = b.kda_seq[:, :b.B]
         Kc.kda_conv(proj, seq, b.max_rows_per_seq, k.conv, self.conv_pool[li], qkv, H, Dh)
         if not self._keep_window:       # prefill chunk: every row is kept, shift the conv window now
@@ -398,6 +413,8 @@ class Runtime:
         else:       # prefill: 64-token chunked form of the same recurrence
             Kc.kda_chunk(proj, seq, fb, qkv, k.a_log, k.dt_bias, self.S_pool[li], self.ko[:R], H, Dh,
                          C3 + 2 * Dh, c.lower, self.kda_scr)
+        if side:
+            torch.cuda.current_stream().wait_event(self.ev_join)
         Kc.kda_gated_norm(self.ko[:R], self.kg[:R], k.o_norm, self.kout[:R], H, Dh, c.eps)
         self._final_linear(self.kout[:R], k.o_proj, R)
 
@@ -468,7 +485,7 @@ class Runtime:
                            c.limit, True)
             Kc.moe_prefill(m.down.trellis, None, m.down.svh, None, None, self.p_pair_w[:P], self.group_count,
                            self.p_group_expert, self.p_group_offset, self.xd[:P], None, self.yd[:P], c.limit, False)
-            Kc.moe_combine(self.yd, self.p_pair_of[:P], c.top_k, self.branch[r0:r1], False)
+            Kc.moe_combine(self.yd, self.p_pair_of[:P], c.top_k, self.branch[r0:r1], 0)
 
     def _moe(self, lw, R):
         c, m = self.cfg, lw.moe
@@ -478,6 +495,34 @@ class Runtime:
             self._shared_expert(lw, R)
             return
         MR = self.rlogits.shape[0]
+        if self.overlap and not self._fused and R <= MR:
+            # the shared expert writes the branch on the side stream while the routed experts run; the routed
+            # slot-ordered sum is formed first and the shared output added last (the same fp32 operations as the
+            # sequential routed-then-shared order)
+            s = m.shared
+            self.ev_fork.record()
+            with torch.cuda.stream(self.side):
+                self.side.wait_event(self.ev_fork)
+                act = self.act[:R, :s.width]
+                K.linear8(self.normed[:R], self.gu_il[lw.index].w, self.gu_il[lw.index].s, act, K.GEMV_SWIGLU,
+                          c.limit)
+                K.linear8(act, s.down.w, s.down.s, self.branch[:R], K.GEMV_F32)
+                self.ev_join.record()
+            P = R * c.top_k
+            x = self.normed[:R]
+            K.linear_bf16(x, m.router, self.rlogits[:R])
+            groups = min(P, c.experts)
+            Kc.moe_route(self.rlogits[:R], m.bias, c.top_k, c.routed_scale, c.norm_topk, self.topk_ids[:R],
+                         self.topk_w[:R], self.group_count, self.group_expert[:groups],
+                         self.group_offset[:groups + 1], self.pair_token[:P], self.pair_expert[:P], self.pair_w[:P],
+                         self.pair_of[:P])
+            Kc.exl3_moe(x, m.gate.trellis, m.gate.suh, m.gate.svh, m.up.trellis, m.up.suh, m.up.svh,
+                        m.down.trellis, m.down.suh, m.down.svh, self.group_count, self.group_expert[:groups],
+                        self.group_offset[:groups + 1], self.pair_token[:P], self.pair_expert[:P], self.pair_w[:P],
+                        self.xh_g, self.xh_u, self.xd, self.yd, c.limit)
+            torch.cuda.current_stream().wait_event(self.ev_join)
+            Kc.moe_combine(self.yd, self.pair_of[:P], c.top_k, self.branch[:R], 2)
+            return
         for r0 in range(0, R, MR):
             r1 = min(R, r0 + MR)
             n = r1 - r0
@@ -493,7 +538,7 @@ class Runtime:
                         m.down.trellis, m.down.suh, m.down.svh, self.group_count, self.group_expert[:groups],
                         self.group_offset[:groups + 1], self.pair_token[:P], self.pair_expert[:P], self.pair_w[:P],
                         self.xh_g, self.xh_u, self.xd, self.yd, c.limit)
-            Kc.moe_combine(self.yd, self.pair_of[:P], c.top_k, self.branch[r0:r1], False)
+            Kc.moe_combine(self.yd, self.pair_of[:P], c.top_k, self.branch[r0:r1], 0)
         self._shared_expert(lw, R)
 
     def _shared_expert(self, lw, R):

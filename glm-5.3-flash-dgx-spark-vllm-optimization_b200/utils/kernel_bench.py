@@ -150,7 +150,9 @@ def bench_gemv(args, T: Timer):
     from glm53.ops import kernels as K
     hbm, _ = peaks()
     for (N, Kd, name) in [(24896, 4096, "kda_in_proj"), (4096, 8192, "kda_o_proj"), (4096, 16384, "mla_o_proj"),
-                          (2048, 4096, "mla_qkv_a"), (154880, 4096, "lm_head"), (288, 4096, "router_bf16")]:
+                          (2048, 4096, "mla_qkv_a"), (154880, 4096, "lm_head"), (288, 4096, "router_bf16"),
+                          (16384, 1536, "mla_q_b"), (4096, 4096, "shared_gate_up"), (4096, 2048, "shared_down"),
+                          (24576, 4096, "dense_gate_up"), (4096, 12288, "dense_down")]:
         for M in args.rows:
             x = torch.randn(M, Kd, device="cuda").to(torch.bfloat16)
             y = torch.empty(M, N, device="cuda")
@@ -160,8 +162,17 @@ def bench_gemv(args, T: Timer):
                 nbytes = N * Kd * 2
             else:
                 q = quantize_fp8_rows(torch.randn(N, Kd, device="cuda") / 64)
-                ms = T(lambda: K.C().gemv(x, q.w, q.s, y, K.GEMV_F32, 0.0))
                 nbytes = N * Kd
+                if args.sweep:
+                    # split-K shapes: warps per tile (ks) x cluster split (cl)
+                    for ks in (1, 2, 4, 8):
+                        for cl in (1, 2, 4, 8):
+                            if Kd // 64 < ks * cl * 2:
+                                continue
+                            ms = T(lambda: K.C().gemv(x, q.w, q.s, y, K.GEMV_F32, 0.0, ks, cl))
+                            emit({"case": "gemv_sweep", "proj": name, "M": M, "ks": ks, "cl": cl, "ms": ms,
+                                  "frac_of_hbm": nbytes / ms / 1e6 / hbm})
+                ms = T(lambda: K.C().gemv(x, q.w, q.s, y, K.GEMV_F32, 0.0))
             emit({"case": "gemv", "proj": name, "M": M, "N": N, "K": Kd, "ms": ms, "GBps": nbytes / ms / 1e6,
                   "frac_of_hbm": nbytes / ms / 1e6 / hbm})
 
@@ -391,6 +402,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--no-flush", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="gemv: every split-K shape")
     args = ap.parse_args(argv)
     import sys
     sys.path.insert(0, ROOT)

@@ -1,4 +1,4 @@
-"""Teacher-forced KL / NLL harness (the role of the reference's klh, code/ops/klh/klh.py:1-45): two logit providers
+"""Teacher-forced KL / NLL harness (the role of the reference's klh, code/operator/klh/klh.py:1-45): two logit providers
 read the same token sequences; per position the KL divergence KL(P_a || P_b) of their next-token distributions and
 each provider's negative log-likelihood of the actual next token are collected, with block-bootstrap confidence
 intervals (blocks of consecutive positions, so correlated neighbours do not shrink the interval) and an A/A noise

@@ -33,7 +33,7 @@ def _moe_ref(cfg, w, x):
     C.exl3_moe(x, w.gate.trellis, w.gate.suh, w.gate.svh, w.up.trellis, w.up.suh, w.up.svh, w.down.trellis,
                w.down.suh, w.down.svh, gc, ge, go, pt, pe, pw, xh_g, xh_u, xd, yd, cfg.limit)
     out = torch.zeros(T, D, device=DEV)
-    C.moe_combine(yd, po, tk, out, False)
+    C.moe_combine(yd, po, tk, out, 0)
     return out
 
 

@@ -120,7 +120,7 @@ def test_moe_routed_exl3(C, tiny_cfg, tiny_weights, rows):
                 m.down.suh, m.down.svh, rt.group_count, rt.group_expert[:G], rt.group_offset[:G + 1],
                 rt.pair_token[:P], rt.pair_expert[:P], rt.pair_w[:P], rt.xh_g, rt.xh_u, rt.xd, rt.yd, cfg.limit)
     out = torch.empty(rows, cfg.hidden, device=DEV)
-    Kc.moe_combine(rt.yd, rt.pair_of[:P], cfg.top_k, out, False)
+    Kc.moe_combine(rt.yd, rt.pair_of[:P], cfg.top_k, out, 0)
     torch.testing.assert_close(out.cpu(), ref, atol=2e-2, rtol=2e-2)
 
 
@@ -283,3 +283,48 @@ def test_hc_post_pre_tensor_cores(C, rows, with_post):
     torch.testing.assert_close(ct, comb_ref, atol=1e-4, rtol=1e-4)
     torch.testing.assert_close(nt, normed_ref, atol=3e-2, rtol=2e-2)
     torch.testing.assert_close(pt, outs[0][2], atol=1e-5, rtol=1e-5)
+
+
+@pytest.mark.parametrize("M", [1, 8, 12])
+@pytest.mark.parametrize("N,K", [(24896, 4096), (4100, 8192), (4096, 16384)])
+def test_gemv_fp8_stream_k(C, M, N, K):
+    """Large projections go through the stream-K kernel (every warp an equal run of 64-wide chunks, tiles split
+    between warps finished by the last one in warp order): all output modes against the fp32 reference, and two
+    launches in a row give identical bits (the per-tile counters reset themselves)."""
+    from glm53.models.weights import quantize_fp8_rows
+    from glm53.ops import kernels as Kk
+    g = torch.Generator(device=DEV).manual_seed(M * 13 + N)
+    wf = torch.randn(N, K, device=DEV, generator=g) / math.sqrt(K)
+    w = quantize_fp8_rows(wf)
+    x = torch.randn(M, K, device=DEV, generator=g).to(torch.bfloat16)
+    ref = x.float() @ w.dequant().t()
+    y = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    Kk.C().gemv(x, w.w, w.s, y, Kk.GEMV_F32, 0.0)
+    torch.testing.assert_close(y, ref, atol=2e-3, rtol=2e-3)
+    y2 = torch.empty_like(y)
+    Kk.C().gemv(x, w.w, w.s, y2, Kk.GEMV_F32, 0.0)
+    assert torch.equal(y, y2)
+    yb = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    Kk.C().gemv(x, w.w, w.s, yb, Kk.GEMV_BF16, 0.0)
+    torch.testing.assert_close(yb.float(), ref, atol=2e-2, rtol=2e-2)
+    acc = torch.ones(M, N, dtype=torch.float32, device=DEV)
+    Kk.C().gemv(x, w.w, w.s, acc, Kk.GEMV_F32_ACC, 0.0)
+    torch.testing.assert_close(acc, ref + 1, atol=2e-3, rtol=2e-3)
+
+
+def test_gemv_swiglu_stream_k(C):
+    from glm53.models.runtime import interleave_gate_up
+    from glm53.models.weights import quantize_fp8_rows
+    from glm53.models.reference import swiglu
+    from glm53.ops import kernels as Kk
+    torch.manual_seed(1)
+    Wd, Kd, M = 12288, 4096, 8
+    gu = quantize_fp8_rows(torch.randn(2 * Wd, Kd) / math.sqrt(Kd))
+    x = torch.randn(M, Kd).to(torch.bfloat16)
+    full = x.float() @ gu.dequant().t()
+    gg, uu = full[:, :Wd].to(torch.bfloat16).float(), full[:, Wd:].to(torch.bfloat16).float()
+    ref = swiglu(gg, uu, 10.0)
+    il = interleave_gate_up(gu)
+    y = torch.empty(M, Wd, dtype=torch.bfloat16, device=DEV)
+    Kk.C().gemv(x.to(DEV), il.w.to(DEV), il.s.to(DEV), y, Kk.GEMV_SWIGLU, 10.0)
+    torch.testing.assert_close(y.float().cpu(), ref, atol=3e-2, rtol=3e-2)
