@@ -27,7 +27,7 @@ namespace g53 {
 namespace mp {
 
 constexpr uint32_t kSpin = 1u << 26;
-constexpr int kDecWarps = 8;
+constexpr int kDecWarps = 16;
 constexpr int kThreads = (kDecWarps + 2) * 32;
 constexpr int kNmax = 256;            // tokens per pass
 constexpr int kBK = 64;               // k per stage (one 128-byte swizzle row of f16)
@@ -203,12 +203,14 @@ __global__ void __launch_bounds__(kThreads, 1) moe_prefill_kernel(const __grid_c
           w[i] = ldg_nc_u32(trw[m] + tile * 32 + lane);
         }
       };
+      uint32_t wnext[PER];                              // trellis words two stages ahead of the decode
       load(0, wcur);
+      if (nkb > 1) load(1, wnext);
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        uint32_t wnext[PER];
-        if (kb + 1 < nkb) load(kb + 1, wnext);
+        uint32_t wnext2[PER];
+        if (kb + 2 < nkb) load(kb + 2, wnext2);
         if (it >= STAGES) {
           int okw = 0;
           if (lane == 0) okw = bar_wait(&empty[s], ph ^ 1, &fail, p.err, 11) ? 1 : 0;
@@ -231,10 +233,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_prefill_kernel(const __grid_c
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) bar_arrive(&a_full[s]);
-        if (kb + 1 < nkb) {
 #pragma unroll
-          for (int i = 0; i < PER; ++i) wcur[i] = wnext[i];
-        }
+        for (int i = 0; i < PER; ++i) { wcur[i] = wnext[i]; wnext[i] = wnext2[i]; }
       }
       // ---- epilogue of this pass
       int okw = 0;
@@ -242,21 +242,22 @@ __global__ void __launch_bounds__(kThreads, 1) moe_prefill_kernel(const __grid_c
       const bool ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
       __syncwarp();
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      float* zb = reinterpret_cast<float*>(sm);          // [2][32][129] transposition buffer (stages are idle)
-      const int quad = warp & 3, half = warp >> 2;
+      float* zb = reinterpret_cast<float*>(sm);          // [2][32][132] transposition buffer (stages are idle)
+      constexpr int ZS = 132;                            // row stride: 16-byte aligned rows, conflict-free stores
+      const int quad = warp & 3, half = (warp >> 2) & 1;
       for (int c0 = 0; c0 < rows; c0 += 32) {
-        if (ok) {
+        if (ok && warp < 8) {                            // warps 0-7 read TMEM (4 lane quadrants x 2 halves)
           float v[32];
           if (GU) {
             // warps 0-3: gate columns, warps 4-7: up columns
             tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + half * kNmax + c0, v);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) zb[(half * 32 + j) * 129 + quad * 32 + lane] = v[j];
+            for (int j = 0; j < 32; ++j) zb[(half * 32 + j) * ZS + quad * 32 + lane] = v[j];
           } else {
             // warps 0-3: columns c0.., warps 4-7: columns c0+32..
             tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + c0 + half * 32, v);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) zb[(half * 32 + j) * 129 + quad * 32 + lane] = v[j];
+            for (int j = 0; j < 32; ++j) zb[(half * 32 + j) * ZS + quad * 32 + lane] = v[j];
           }
         }
         named_sync(1, kDecWarps * 32);
@@ -266,8 +267,10 @@ __global__ void __launch_bounds__(kThreads, 1) moe_prefill_kernel(const __grid_c
           const int col = nb * 128 + lane * 4;
           if (GU) {
             float vg[4], vu[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) { vg[i] = zb[j * 129 + lane * 4 + i]; vu[i] = zb[(32 + j) * 129 + lane * 4 + i]; }
+            const float4 g4 = *reinterpret_cast<const float4*>(&zb[j * ZS + lane * 4]);
+            const float4 u4 = *reinterpret_cast<const float4*>(&zb[(32 + j) * ZS + lane * 4]);
+            vg[0] = g4.x; vg[1] = g4.y; vg[2] = g4.z; vg[3] = g4.w;
+            vu[0] = u4.x; vu[1] = u4.y; vu[2] = u4.z; vu[3] = u4.w;
             fwht128_warp(vg);
             fwht128_warp(vu);
             float act[4];
@@ -285,8 +288,8 @@ __global__ void __launch_bounds__(kThreads, 1) moe_prefill_kernel(const __grid_c
             o[1] = __floats2half2_rn(act[2], act[3]);
           } else {
             float v[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) v[i] = zb[j * 129 + lane * 4 + i];
+            const float4 v4 = *reinterpret_cast<const float4*>(&zb[j * ZS + lane * 4]);
+            v[0] = v4.x; v[1] = v4.y; v[2] = v4.z; v[3] = v4.w;
             fwht128_warp(v);
             const float w = p.pair_w[pr];
             float4 o;
