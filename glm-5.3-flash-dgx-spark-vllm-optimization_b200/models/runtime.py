@@ -366,7 +366,7 @@ class Runtime:
                            c.hc_eps, c.hc_iters)
         self._point += 1
 
-    def _final_linear(self, x, lin, R, mode=K.GEMV_F32):
+    def _final_linear(self, x, lin, R, mode=K.GEMV_F32, proj=None):
         """The row-parallel projection that ends a block: writes the block's fp32 partial into ``branch``; in the
         fused tensor-parallel mode it also pushes it into every rank's receive slot."""
         if self._fused and R <= K.GEMV_MAX_M:
@@ -379,7 +379,7 @@ class Runtime:
                                   px.push_ptrs[p], px.push_flags[p], px.done_prod[p:p + 1], px.slot, px.rank,
                                   px.world)
         else:
-            K.linear8(x, lin.w, lin.s, self.branch[:R], mode)
+            K.linear8(x, lin.w, lin.s, self.branch[:R], mode, proj=proj)
 
     # ---- blocks ------------------------------------------------------------------------------------------------
     def _kda(self, lw, R):
@@ -392,7 +392,7 @@ class Runtime:
         else:
             proj, fb, qkv = self.kproj[:R], self.kf[:R], self.kqkv[:R]
         C3 = 3 * H * Dh
-        K.linear8(self.normed[:R], k.in_proj.w, k.in_proj.s, proj)
+        K.linear8(self.normed[:R], k.in_proj.w, k.in_proj.s, proj, proj="kda_in_proj")
         K.linear8(proj[:, C3:C3 + Dh], k.f_b.w, k.f_b.s, fb)
         side = self.overlap and R <= K.GEMV_MAX_M
         if side:        # output gate (read only by the gated norm) beside the convolution and recurrence
@@ -454,7 +454,7 @@ class Runtime:
                           self.part_o, self.part_ml, self.o_lat[r0:r1])
         ob = self.obuf[:R].view(R, H, c.v_dim)
         K.linear8(self.o_lat[:R].transpose(0, 1), a.w_uv.w, a.w_uv.s, ob.transpose(0, 1))
-        self._final_linear(self.obuf[:R], a.o_proj, R)
+        self._final_linear(self.obuf[:R], a.o_proj, R, proj="mla_o_proj")
 
     def _mlp(self, lw, R):
         m = lw.mlp

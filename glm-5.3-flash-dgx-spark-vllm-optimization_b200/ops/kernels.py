@@ -12,9 +12,13 @@ from . import _ext
 # the tcgen05 GEMM serves M >= GEMM_MIN_M rows (set GLM53_TCGEN05_GEMM=0 to route large M through the small-M kernel)
 GEMM_ENABLED = os.environ.get("GLM53_TCGEN05_GEMM", "1") == "1"
 # large-M fp8 projections: exact W8A16 (weights widened to bf16, bf16 activations: the numerics of the decode
-# kernel) by default; GLM53_PREFILL_W8A8=1 quantises activations per row to e4m3 instead (2x tensor throughput,
-# different numerics -- the trade the reference's production prefill made)
-PREFILL_W8A8 = os.environ.get("GLM53_PREFILL_W8A8", "0") == "1"
+# kernel), except the projections listed in GLM53_PREFILL_W8A8, which quantise their activations per row to e4m3
+# (kind::f8f6f4, 2x tensor throughput, different numerics).  The default is the reference's production choice:
+# the KDA input projection and the MLA output projection (its GLM53_DENSE_W8A8_ONLY=kda.in_proj_qkvbfg_a,
+# mla.o_proj); "all" = every large-M fp8 projection, "none" = exact W8A16 everywhere.
+_W8A8 = os.environ.get("GLM53_PREFILL_W8A8", "kda_in_proj,mla_o_proj").strip().lower()
+PREFILL_W8A8 = _W8A8 in ("1", "all")
+W8A8_PROJ = set() if _W8A8 in ("0", "none", "") else {p.strip() for p in _W8A8.split(",")}
 _scratch: dict = {}
 
 
@@ -40,17 +44,18 @@ def C():
 
 
 def linear8(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor, y: torch.Tensor, mode: int = GEMV_BF16,
-            limit: float = 0.0) -> torch.Tensor:
+            limit: float = 0.0, proj: str | None = None) -> torch.Tensor:
     """y[M, N] (mode) = x[M, K] @ (w8[N, K] * s)^T for any M (chunks of 16 rows through the small-M kernel, or
     the large-M GEMM when it is available).  Batched form: x [B, M, K], w [B, N, K], s [B, N], y [B, M, N] (per
-    attention head; any batch and row strides with contiguous rows)."""
+    attention head; any batch and row strides with contiguous rows).  `proj` names the projection for the W8A8
+    policy of large-M calls (GLM53_PREFILL_W8A8)."""
     M = x.shape[-2]
     g = C().gemv
     if M <= GEMV_MAX_M:
         g(x, w, s, y, mode, limit)
         return y
     if GEMM_ENABLED and M >= GEMM_MIN_M:
-        if PREFILL_W8A8 and x.dim() == 2:
+        if (PREFILL_W8A8 or proj in W8A8_PROJ) and x.dim() == 2:
             C().gemm_w8(x, w, s, y, mode, limit)
         else:
             C().gemm_w8a16(x, w, s, y, mode, limit, _w_scratch(w.numel(), x.device))

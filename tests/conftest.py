@@ -10,6 +10,24 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA (B200) device")
+    config.addinivalue_line("markers", "w8a8: runs with the default prefill W8A8 policy (others: exact W8A16)")
+
+
+@pytest.fixture(autouse=True)
+def _exact_prefill_projections(request, monkeypatch):
+    """Numerics tests compare against the fp32 oracle and across prefill / decode paths, so large-M projections run
+    in exact W8A16 unless a test is marked `w8a8` (the default policy quantises two projections' activations)."""
+    if request.node.get_closest_marker("w8a8"):
+        yield
+        return
+    try:
+        from glm53.ops import kernels as K
+    except Exception:  # pragma: no cover - the package imports on every supported host
+        yield
+        return
+    monkeypatch.setattr(K, "W8A8_PROJ", set())
+    monkeypatch.setattr(K, "PREFILL_W8A8", False)
+    yield
 
 
 @pytest.fixture(scope="session")

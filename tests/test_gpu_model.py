@@ -76,6 +76,18 @@ def test_tiny_model_dense_context_tight(dense_setup):
     assert agree >= len(oracle[1]) - 4
 
 
+@pytest.mark.w8a8
+def test_tiny_model_dense_context_w8a8_prefill(dense_setup):
+    """The default prefill policy (per-row e4m3 activations for the KDA input and MLA output projections, the
+    reference's production choice) stays close to the fp32 oracle; decode rows are exact W8A16 either way."""
+    from glm53.ops import kernels as K
+    assert {"kda_in_proj", "mla_o_proj"} <= K.W8A8_PROJ or K.PREFILL_W8A8 or not K.W8A8_PROJ
+    cfg, w, oracle = dense_setup
+    coss, agree = _run_teacher_forced(w, oracle)
+    assert coss.min() > 0.95 and (coss > 0.99).float().mean() >= 0.9, coss
+    assert agree >= len(oracle[1]) - 4
+
+
 def test_tiny_model_sparse_dsa(tiny_weights, oracle_run):
     # past index_topk a bf16/fp8 rounding difference can flip a near-tied DSA pool choice (a discrete change of a
     # few attended keys), which moves single steps; the bulk of the steps must still agree tightly
