@@ -24,7 +24,9 @@ namespace g53 {
 constexpr int kC = 64;       // chunk rows
 constexpr int kSubR = 16;    // sub-chunk rows (reference points)
 
-__host__ __device__ constexpr int64_t kda_scr_per_head(int dh) { return 3LL * kC * dh + 2LL * kC * kC + dh; }
+// record per (chunk slot, head), in floats: Q~, K~, K^ as fp16 [kC][dh] each (exact for the tf32 products; every
+// value is a unit-normalised row times a decay factor <= 1), T and P fp32 [kC][kC], e^{G_C} fp32 [dh]
+__host__ __device__ constexpr int64_t kda_scr_per_head(int dh) { return 3LL * kC * dh / 2 + 2LL * kC * kC + dh; }
 
 __device__ __forceinline__ int chunk_slot(int row0, int b, int c) { return row0 / kC + b + c; }
 
@@ -57,45 +59,83 @@ __global__ void __launch_bounds__(256, 1) kda_prep_kernel(KdaArgs a) {
   const int HD = a.H * DH;
   const float ea = __expf(a.a_log[h]);
 
-  // 1. rows: normalised q, k; raw g; beta
-  for (int t = warp; t < kC; t += 8) {
-    const int row = base + c0 + t;
-    constexpr int PL = DH / 32;
-    float q[PL], k[PL], g[PL];
-    float sq = 0.f, sk = 0.f;
+  // 1. rows: normalised q, k; raw g; beta.  A warp owns rows warp, warp + 8, ...; the loads of 4 rows are issued
+  //    together (raw bf16 in registers) before any of them is reduced, so the global latency is paid twice, not 8x
+  constexpr int PL = DH / 32;
+  for (int t0 = warp; t0 < kC; t0 += 32) {
+    __nv_bfloat16 rq[4][PL], rk[4][PL], rf[4][PL], rb[4];
 #pragma unroll
-    for (int i = 0; i < PL; ++i) {
-      const int c = lane + 32 * i;
-      if (t < n) {
-        const __nv_bfloat16* rp = a.qkv + (int64_t)row * 3 * HD;
-        q[i] = bf2f(rp[h * DH + c]);
-        k[i] = bf2f(rp[HD + h * DH + c]);
-        g[i] = a.lower * sigmoidf_(ea * (bf2f(a.f[(int64_t)row * HD + h * DH + c]) + a.dt_bias[h * DH + c]));
-      } else {
-        q[i] = k[i] = g[i] = 0.f;
+    for (int u = 0; u < 4; ++u) {
+      const int t = t0 + 8 * u, row = base + c0 + t;
+      const bool on = t < n;
+      const __nv_bfloat16* rp = a.qkv + (int64_t)(on ? row : base) * 3 * HD;
+      const __nv_bfloat16* fp = a.f + (int64_t)(on ? row : base) * HD + h * DH;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) {
+        const int c = lane + 32 * i;
+        rq[u][i] = rp[h * DH + c];
+        rk[u][i] = rp[HD + h * DH + c];
+        rf[u][i] = fp[c];
       }
-      sq += q[i] * q[i];
-      sk += k[i] * k[i];
+      rb[u] = a.proj[(int64_t)(on ? row : base) * a.ldp + a.b_off + h];
     }
-    sq = warp_sum(sq);
-    sk = warp_sum(sk);
-    const float qn = rsqrtf(sq + 1e-6f) * rsqrtf((float)DH), kn = rsqrtf(sk + 1e-6f);
 #pragma unroll
-    for (int i = 0; i < PL; ++i) {
-      const int c = lane + 32 * i;
-      sQ[t * P1 + c] = q[i] * qn;
-      sK[t * P1 + c] = k[i] * kn;
-      sG[t * P1 + c] = g[i];
+    for (int u = 0; u < 4; ++u) {
+      const int t = t0 + 8 * u;
+      const bool on = t < n;
+      float q[PL], k[PL], g[PL];
+      float sq = 0.f, sk = 0.f;
+#pragma unroll
+      for (int i = 0; i < PL; ++i) {
+        const int c = lane + 32 * i;
+        q[i] = on ? bf2f(rq[u][i]) : 0.f;
+        k[i] = on ? bf2f(rk[u][i]) : 0.f;
+        g[i] = on ? a.lower * sigmoidf_(ea * (bf2f(rf[u][i]) + a.dt_bias[h * DH + c])) : 0.f;
+        sq += q[i] * q[i];
+        sk += k[i] * k[i];
+      }
+      sq = warp_sum(sq);
+      sk = warp_sum(sk);
+      const float qn = rsqrtf(sq + 1e-6f) * rsqrtf((float)DH), kn = rsqrtf(sk + 1e-6f);
+#pragma unroll
+      for (int i = 0; i < PL; ++i) {
+        const int c = lane + 32 * i;
+        sQ[t * P1 + c] = q[i] * qn;
+        sK[t * P1 + c] = k[i] * kn;
+        sG[t * P1 + c] = g[i];
+      }
+      if (lane == 0) sB[t] = on ? sigmoidf_(bf2f(rb[u])) : 0.f;
     }
-    if (lane == 0) sB[t] = t < n ? sigmoidf_(bf2f(a.proj[(int64_t)row * a.ldp + a.b_off + h])) : 0.f;
   }
   __syncthreads();
-  // 2. cumulative log-decay per channel (rows past n add 0 and keep the last value)
-  for (int c = tid; c < DH; c += blockDim.x) {
-    float acc = 0.f;
-    for (int t = 0; t < kC; ++t) {
-      acc += sG[t * P1 + c];
-      sG[t * P1 + c] = acc;
+  // 2. cumulative log-decay per channel (rows past n add 0 and keep the last value): 4 segments of 16 rows per
+  //    channel summed in parallel (two per thread), then each segment adds the totals of the segments before it
+  {
+    constexpr int TPC = 256 / DH;                    // threads per channel (2 or 4)
+    constexpr int SPT = 4 / TPC;                     // segments per thread
+    const int c = tid % DH, sb = tid / DH;           // this thread's segments: sb, sb + TPC, ...
+    float acc[SPT];
+#pragma unroll
+    for (int i = 0; i < SPT; ++i) acc[i] = 0.f;
+#pragma unroll 4
+    for (int t = 0; t < 16; ++t) {
+#pragma unroll
+      for (int i = 0; i < SPT; ++i) {
+        const int r = (sb + TPC * i) * 16 + t;
+        acc[i] += sG[r * P1 + c];
+        sG[r * P1 + c] = acc[i];
+      }
+    }
+    __syncthreads();
+    const float tot0 = sG[15 * P1 + c], tot1 = sG[31 * P1 + c], tot2 = sG[47 * P1 + c];
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < SPT; ++i) {
+      const int sg = sb + TPC * i;
+      if (sg == 0) continue;
+      const float add = sg == 1 ? tot0 : (sg == 2 ? tot0 + tot1 : (tot0 + tot1) + tot2);
+#pragma unroll 4
+      for (int t = 0; t < 16; ++t) sG[(sg * 16 + t) * P1 + c] += add;
     }
   }
   __syncthreads();
@@ -146,18 +186,49 @@ __global__ void __launch_bounds__(256, 1) kda_prep_kernel(KdaArgs a) {
     if (s >= (t / kSubR + 1) * kSubR) { sM[t * (kC + 1) + s] = 0.f; sP[t * (kC + 1) + s] = 0.f; }
   }
   __syncthreads();
-  // 4. X = (I + diag(beta) M)^{-1}, unit lower triangular, by rows: X_t = e_t - beta_t sum_{s<t} M_ts X_s.
-  //    4 threads per column j split the sum over s (fixed order, shuffle-reduced)
+  // 4. X = (I + diag(beta) M)^{-1} (unit lower triangular) in 16 x 16 blocks: the four diagonal blocks by forward
+  //    substitution, one warp each with a column per lane held in registers (no block-wide barriers), then the
+  //    blocks below the diagonal by distance d = i - j: X_ij = -X_ii sum_{k=j}^{i-1} (diag(beta) M)_ik X_kj
   {
-    const int j = tid >> 2, part = tid & 3;
-    for (int e = tid; e < kC * kC; e += blockDim.x) sI[(e / kC) * (kC + 1) + e % kC] = (e / kC == e % kC) ? 1.f : 0.f;
+    for (int e = tid; e < kC * kC; e += blockDim.x) sI[(e / kC) * (kC + 1) + e % kC] = 0.f;
     __syncthreads();
-    for (int t = 1; t < kC; ++t) {
-      float acc = 0.f;
-      if (j < t)
-        for (int s = j + part; s < t; s += 4) acc += sM[t * (kC + 1) + s] * sI[s * (kC + 1) + j];
-      acc = group_sum<4>(acc);
-      if (j < t && part == 0) sI[t * (kC + 1) + j] = -sB[t] * acc;
+    if (warp < 4 && lane < kSubR) {
+      const int o = warp * kSubR, j = lane;
+      float x[kSubR];
+#pragma unroll
+      for (int t = 0; t < kSubR; ++t) x[t] = t == j ? 1.f : 0.f;
+#pragma unroll
+      for (int t = 1; t < kSubR; ++t) {
+        float acc = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < t; ++s2) acc += sM[(o + t) * (kC + 1) + o + s2] * x[s2];
+        if (t > j) x[t] = -sB[o + t] * acc;
+      }
+#pragma unroll
+      for (int t = 0; t < kSubR; ++t) sI[(o + t) * (kC + 1) + o + j] = x[t];
+    }
+    __syncthreads();
+    float* sW = sX;                                   // free until step 5: W blocks of one distance
+    for (int d = 1; d < kC / kSubR; ++d) {
+      const int nblk = kC / kSubR - d;
+      for (int e = tid; e < nblk * kSubR * kSubR; e += blockDim.x) {
+        const int j = e / (kSubR * kSubR), r = (e / kSubR) % kSubR, col = e % kSubR, i = j + d;
+        float w = 0.f;
+        for (int kb = j; kb < i; ++kb)
+#pragma unroll 4
+          for (int m = 0; m < kSubR; ++m)
+            w += sM[(kSubR * i + r) * (kC + 1) + kSubR * kb + m] * sI[(kSubR * kb + m) * (kC + 1) + kSubR * j + col];
+        sW[e] = w * sB[kSubR * i + r];
+      }
+      __syncthreads();
+      for (int e = tid; e < nblk * kSubR * kSubR; e += blockDim.x) {
+        const int j = e / (kSubR * kSubR), r = (e / kSubR) % kSubR, col = e % kSubR, i = j + d;
+        float x = 0.f;
+#pragma unroll 4
+        for (int m = 0; m < kSubR; ++m)
+          x += sI[(kSubR * i + r) * (kC + 1) + kSubR * i + m] * sW[j * kSubR * kSubR + m * kSubR + col];
+        sI[(kSubR * i + r) * (kC + 1) + kSubR * j + col] = -x;
+      }
       __syncthreads();
     }
   }
@@ -174,17 +245,17 @@ __global__ void __launch_bounds__(256, 1) kda_prep_kernel(KdaArgs a) {
   __syncthreads();
   // 6. write the chunk record: Q~, K~, K^ [kC][DH], T = X diag(beta) [kC][kC], P [kC][kC], e^{G_C} [DH]
   float* out = a.scr + ((int64_t)slot * a.H + h) * kda_scr_per_head(DH);
-  float* oQ = out;
-  float* oK = oQ + kC * DH;
-  float* oKb = oK + kC * DH;
-  float* oT = oKb + kC * DH;
+  __half* oQ = reinterpret_cast<__half*>(out);
+  __half* oK = oQ + kC * DH;
+  __half* oKb = oK + kC * DH;
+  float* oT = out + 3 * kC * DH / 2;
   float* oP = oT + kC * kC;
   float* oE = oP + kC * kC;
-  for (int e = tid; e < kC * DH; e += blockDim.x) {
-    const int t = e / DH, c = e % DH;
-    oQ[e] = sQ[t * P1 + c];
-    oK[e] = sK[t * P1 + c];
-    oKb[e] = sX[t * P1 + c];
+  for (int e = tid; e < kC * DH / 2; e += blockDim.x) {
+    const int t = (2 * e) / DH, c = (2 * e) % DH;
+    reinterpret_cast<__half2*>(oQ)[e] = __floats2half2_rn(sQ[t * P1 + c], sQ[t * P1 + c + 1]);
+    reinterpret_cast<__half2*>(oK)[e] = __floats2half2_rn(sK[t * P1 + c], sK[t * P1 + c + 1]);
+    reinterpret_cast<__half2*>(oKb)[e] = __floats2half2_rn(sX[t * P1 + c], sX[t * P1 + c + 1]);
   }
   for (int e = tid; e < kC * kC; e += blockDim.x) {
     const int t = e / kC, s = e % kC;
@@ -238,21 +309,46 @@ __device__ __forceinline__ void frag_b_kn(const float* p, int ld, uint32_t& b0, 
   b1 = to_tf32(p[(q + 4) * ld + g]);
 }
 
+// fp16 tile element -> tf32 operand (exact: fp16 has the tf32 mantissa width)
+__device__ __forceinline__ uint32_t h2tf(const __half* p) { return __float_as_uint(__half2float(*p)); }
+__device__ __forceinline__ void frag_a_row_h(const __half* p, int ld, uint32_t (&f)[4]) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  f[0] = h2tf(p + g * ld + q);
+  f[1] = h2tf(p + (g + 8) * ld + q);
+  f[2] = h2tf(p + g * ld + q + 4);
+  f[3] = h2tf(p + (g + 8) * ld + q + 4);
+}
+__device__ __forceinline__ void frag_b_kn_h(const __half* p, int ld, uint32_t& b0, uint32_t& b1) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  b0 = h2tf(p + q * ld + g);
+  b1 = h2tf(p + (q + 4) * ld + g);
+}
+__device__ __forceinline__ void cp16(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src), "r"(bytes) : "memory");
+}
+
+// shared-memory layout of one record buffer (floats): fp16 Q~ / K~ / K^ tiles, T, P, e^{G_C}, raw bf16 V slice
+template <int DH>
+struct ScanBuf {
+  static constexpr int LH = DH + 8;                        // row pitch (halves) of the fp16 tiles
+  static constexpr int LT = kC + 4;                        // row pitch of T and P
+  static constexpr int H3 = 3 * kC * LH / 2;               // floats of the three fp16 tiles
+  static constexpr int T_OFF = H3, P_OFF = H3 + kC * LT, E_OFF = H3 + 2 * kC * LT, V_OFF = E_OFF + DH;
+  static constexpr int FLOATS = V_OFF + kC * 32 / 2;        // + [kC][32] bf16 value slice
+};
+
 template <int DH>
 __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
-  constexpr int LD = DH + 4;       // row pitch of the [kC][DH] and [32][DH] tiles (conflict-free fragments)
-  constexpr int LT = kC + 4;       // row pitch of T and P
+  using B = ScanBuf<DH>;
+  constexpr int LH = B::LH, LT = B::LT;
+  constexpr int LD = DH + 4;       // row pitch of the fp32 state tile
   constexpr int LV = 36;           // row pitch of the [kC][32] value tiles
   extern __shared__ float sm[];
-  float* sQ = sm;                  // [kC][LD]  Q~
-  float* sKt = sQ + kC * LD;       // [kC][LD]  K~
-  float* sKb = sKt + kC * LD;      // [kC][LD]  K^
-  float* sT = sKb + kC * LD;       // [kC][LT]
-  float* sP = sT + kC * LT;        // [kC][LT]
-  float* sS = sP + kC * LT;        // [32][LD]  state rows v0..v0+31 (v-major), fp32
+  float* buf0 = sm;                // 2 record buffers (chunk ci uses buffer ci % 2; ci + 1 loads meanwhile)
+  float* sS = sm + 2 * B::FLOATS;  // [32][LD]  state rows v0..v0+31 (v-major), fp32
   float* sZ = sS + 32 * LD;        // [kC][LV]  V, then V - K~ S0^T
   float* sV = sZ + kC * LV;        // [kC][LV]  v'
-  float* sE = sV + kC * LV;        // [DH]      e^{G_C}
 
   const int h = blockIdx.x, b = blockIdx.z;
   const int v0 = blockIdx.y * 32;
@@ -260,6 +356,35 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
   const int HD = a.H * DH;
   const int base = a.row0[b], n_all = a.nrows[b];
   const int64_t sstride = (int64_t)a.H * DH * DH;
+  const int nchunks = (n_all + kC - 1) / kC;
+
+  // asynchronous copy of chunk ci's record and value slice into buffer bi (every thread issues its share)
+  auto issue = [&](int ci, int bi) {
+    const int slot = chunk_slot(base, b, ci);
+    if (slot >= a.scr_slots) return;
+    const float* rec = a.scr + ((int64_t)slot * a.H + h) * kda_scr_per_head(DH);
+    float* bf = buf0 + bi * B::FLOATS;
+    __half* hq = reinterpret_cast<__half*>(bf);
+    const __half* rh = reinterpret_cast<const __half*>(rec);
+    for (int e = tid; e < 3 * kC * (DH / 8); e += blockDim.x) {      // 16-byte pieces of the fp16 tiles
+      const int m = e / (kC * (DH / 8)), t = (e / (DH / 8)) % kC, c = e % (DH / 8);
+      cp16(hq + m * kC * LH + t * LH + c * 8, rh + (int64_t)m * kC * DH + t * DH + c * 8, 16u);
+    }
+    const float* rt = rec + 3 * kC * DH / 2;
+    for (int e = tid; e < 2 * kC * (kC / 4); e += blockDim.x) {       // T then P
+      const int m = e / (kC * (kC / 4)), t = (e / (kC / 4)) % kC, c = e % (kC / 4);
+      cp16(bf + B::T_OFF + m * kC * LT + t * LT + c * 4, rt + m * kC * kC + t * kC + c * 4, 16u);
+    }
+    for (int e = tid; e < DH / 4; e += blockDim.x) cp16(bf + B::E_OFF + e * 4, rt + 2 * kC * kC + e * 4, 16u);
+    const int c0 = ci * kC, n = min(kC, n_all - c0);
+    __nv_bfloat16* vr = reinterpret_cast<__nv_bfloat16*>(bf + B::V_OFF);
+    for (int e = tid; e < kC * 4; e += blockDim.x) {                  // 4 x 16 bytes per value row
+      const int t = e >> 2, c = e & 3;
+      const __nv_bfloat16* src = a.qkv + (int64_t)(base + c0 + (t < n ? t : 0)) * 3 * HD + 2 * HD + h * DH + v0 + c * 8;
+      cp16(vr + t * 32 + c * 8, src, t < n ? 16u : 0u);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
 
   {
     const float* sin = a.S_pool + a.s_in[b] * sstride + ((int64_t)h * DH + v0) * DH;
@@ -268,33 +393,27 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
       *reinterpret_cast<float4*>(sS + v * LD + c) = *reinterpret_cast<const float4*>(sin + v * DH + c);
     }
   }
+  if (nchunks > 0) issue(0, 0);
   // warp tiles: [kC x 32] outputs -> m-tile mt (16 rows), n-tiles 2 nh, 2 nh + 1 (8 columns each)
   const int mt = warp >> 1, nh = warp & 1;
-  for (int ci = 0; ci * kC < n_all; ++ci) {
+  for (int ci = 0; ci < nchunks; ++ci) {
     const int c0 = ci * kC;
     const int n = min(kC, n_all - c0);
-    const int slot = chunk_slot(base, b, ci);
-    if (slot >= a.scr_slots) break;
-    const float* rec = a.scr + ((int64_t)slot * a.H + h) * kda_scr_per_head(DH);
-    __syncthreads();
-    // load the chunk record and the value slice
-    for (int e = tid; e < kC * DH / 4; e += blockDim.x) {
-      const int t = e / (DH / 4), c = (e % (DH / 4)) * 4;
-      *reinterpret_cast<float4*>(sQ + t * LD + c) = *reinterpret_cast<const float4*>(rec + t * DH + c);
-      *reinterpret_cast<float4*>(sKt + t * LD + c) = *reinterpret_cast<const float4*>(rec + kC * DH + t * DH + c);
-      *reinterpret_cast<float4*>(sKb + t * LD + c) =
-          *reinterpret_cast<const float4*>(rec + 2 * kC * DH + t * DH + c);
-    }
-    for (int e = tid; e < kC * kC / 4; e += blockDim.x) {
-      const int t = e / (kC / 4), s = (e % (kC / 4)) * 4;
-      *reinterpret_cast<float4*>(sT + t * LT + s) = *reinterpret_cast<const float4*>(rec + 3 * kC * DH + t * kC + s);
-      *reinterpret_cast<float4*>(sP + t * LT + s) =
-          *reinterpret_cast<const float4*>(rec + 3 * kC * DH + kC * kC + t * kC + s);
-    }
-    for (int c = tid; c < DH; c += blockDim.x) sE[c] = rec[3 * kC * DH + 2 * kC * kC + c];
+    if (chunk_slot(base, b, ci) >= a.scr_slots) break;
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();                         // chunk ci landed for every thread; buffer (ci + 1) % 2 is free
+    if (ci + 1 < nchunks) issue(ci + 1, (ci + 1) & 1);
+    const float* bf = buf0 + (ci & 1) * B::FLOATS;
+    const __half* sQ = reinterpret_cast<const __half*>(bf);
+    const __half* sKt = sQ + kC * LH;
+    const __half* sKb = sKt + kC * LH;
+    const float* sT = bf + B::T_OFF;
+    const float* sP = bf + B::P_OFF;
+    const float* sE = bf + B::E_OFF;
+    const __nv_bfloat16* vr = reinterpret_cast<const __nv_bfloat16*>(bf + B::V_OFF);
     for (int e = tid; e < kC * 32; e += blockDim.x) {
       const int t = e >> 5, v = e & 31;
-      sZ[t * LV + v] = t < n ? bf2f(a.qkv[(int64_t)(base + c0 + t) * 3 * HD + 2 * HD + h * DH + v0 + v]) : 0.f;
+      sZ[t * LV + v] = bf2f(vr[t * 32 + v]);
     }
     __syncthreads();
     // (1) Z = V - K~ S0^T
@@ -302,7 +421,7 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
       float acc[2][4] = {};
       for (int k0 = 0; k0 < DH; k0 += 8) {
         uint32_t fa[4];
-        frag_a_row(sKt + mt * 16 * LD + k0, LD, fa);
+        frag_a_row_h(sKt + mt * 16 * LH + k0, LH, fa);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           uint32_t b0, b1;
@@ -348,7 +467,7 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
       float acc[2][4] = {};
       for (int k0 = 0; k0 < DH; k0 += 8) {
         uint32_t fa[4];
-        frag_a_row(sQ + mt * 16 * LD + k0, LD, fa);
+        frag_a_row_h(sQ + mt * 16 * LH + k0, LH, fa);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           uint32_t b0, b1;
@@ -399,7 +518,7 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
 #pragma unroll
         for (int j = 0; j < NTW; ++j) {
           uint32_t b0, b1;
-          frag_b_kn(sKb + k0 * LD + (nb0 + j) * 8, LD, b0, b1);
+          frag_b_kn_h(sKb + k0 * LH + (nb0 + j) * 8, LH, b0, b1);
           mma_tf32(acc[j], fa, b0, b1);
         }
       }
@@ -413,6 +532,7 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
       }
     }
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
   __syncthreads();
   float* sout = a.S_pool + a.s_out[b] * sstride + ((int64_t)h * DH + v0) * DH;
   for (int e = tid; e < 32 * DH / 4; e += blockDim.x) {
@@ -426,8 +546,7 @@ cudaError_t launch_chunk(const KdaArgs& a, cudaStream_t st) {
   constexpr int P1 = DH + 1;
   const size_t smem_prep =
       sizeof(float) * ((size_t)4 * kC * P1 + 2 * kSubR * P1 + 3 * kC * (kC + 1) + kC);
-  const size_t smem_scan =
-      sizeof(float) * ((size_t)3 * kC * (DH + 4) + 2 * kC * (kC + 4) + 32 * (DH + 4) + 2 * kC * 36 + DH);
+  const size_t smem_scan = sizeof(float) * ((size_t)2 * ScanBuf<DH>::FLOATS + 32 * (DH + 4) + 2 * kC * 36);
   cudaError_t e = cudaFuncSetAttribute(kda_prep_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem_prep);
   if (e != cudaSuccess) return e;

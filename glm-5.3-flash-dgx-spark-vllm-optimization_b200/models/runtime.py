@@ -145,12 +145,12 @@ class Runtime:
             self.kf = torch.zeros(R, H * Dh, dtype=bf16, device=dev)
             self.kqkv = torch.zeros(R, C3, dtype=bf16, device=dev)
             self.kg = torch.zeros(R, H * Dh, dtype=bf16, device=dev)
-            # chunked prefill records per (64-row chunk slot, head): Q~, K~, K^ [64, Dh], T, P [64, 64], e^{G_C} [Dh]
-            # (slots = chunks of the longest launch + sequences + 1; layout in csrc/kda_chunk.cu)
+            # chunked prefill records per (64-row chunk slot, head): Q~, K~, K^ [64, Dh] (fp16), T, P [64, 64],
+            # e^{G_C} [Dh] (slots = chunks of the longest launch + sequences + 1; layout in csrc/kda_chunk.cu)
             self.kda_scr = None
             if R > KDA_CHUNK_MIN_ROWS:
-                slots = (R + 63) // 64 + rc.max_seqs + 1
-                self.kda_scr = torch.empty(slots * H * (3 * 64 * Dh + 2 * 64 * 64 + Dh), dtype=f32, device=dev)
+                n = K.C().kda_chunk_scratch_floats(R, rc.max_seqs, H, Dh)
+                self.kda_scr = torch.empty(n, dtype=f32, device=dev)
             self.ko = torch.zeros(R, H * Dh, dtype=f32, device=dev)
             self.kout = torch.zeros(R, H * Dh, dtype=bf16, device=dev)
         # --- MLA / DSA ---
