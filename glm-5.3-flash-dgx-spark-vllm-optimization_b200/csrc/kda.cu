@@ -45,6 +45,57 @@ __global__ void kda_conv_kernel(KdaArgs a) {
   }
 }
 
+// vectorised form for a compile-time tap count: a thread owns 8 consecutive channels (16-byte loads and stores)
+// of kConvRB consecutive rows; the taps and the history stay in registers
+template <int T>
+__global__ void __launch_bounds__(256) kda_conv_vec_kernel(KdaArgs a) {
+  const int C = 3 * a.H * a.Dh;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const int b = blockIdx.z;
+  if (c >= C) return;
+  const int base = a.row0[b], n = a.nrows[b];
+  const int t0 = blockIdx.y * kConvRB;
+  if (t0 >= n) return;
+  const int t1 = min(t0 + kConvRB, n);
+  const __nv_bfloat16* win = a.conv_pool + (int64_t)a.conv_slot[b] * (T - 1) * C;
+  float w[T][8], hist[T][8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+#pragma unroll
+    for (int i = 0; i < T; ++i) w[i][e] = a.conv_w[(int64_t)(c + e) * T + i];
+  auto load8 = [&](const __nv_bfloat16* p, float (&o)[8]) {
+    const uint4 v = *reinterpret_cast<const uint4*>(p);
+    const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      o[2 * e] = __uint_as_float(ws[e] << 16);
+      o[2 * e + 1] = __uint_as_float(ws[e] & 0xffff0000u);
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < T - 1; ++i) {
+    const int t = t0 - (T - 1) + i;
+    load8(t < 0 ? win + (int64_t)(T - 1 + t) * C + c : a.proj + (int64_t)(base + t) * a.ldp + c, hist[i]);
+  }
+  for (int t = t0; t < t1; ++t) {
+    load8(a.proj + (int64_t)(base + t) * a.ldp + c, hist[T - 1]);
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < T; ++i) { s0 += w[i][e] * hist[i][e]; s1 += w[i][e + 1] * hist[i][e + 1]; }
+      __nv_bfloat162 p2 = __floats2bfloat162_rn(siluf_(s0), siluf_(s1));
+      o[e >> 1] = *reinterpret_cast<uint32_t*>(&p2);
+    }
+    *reinterpret_cast<uint4*>(a.qkv + (int64_t)(base + t) * C + c) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+    for (int i = 0; i < T - 1; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hist[i][e] = hist[i + 1][e];
+  }
+}
+
 // grid (channel blocks, sequences): window <- last taps-1 rows of [window ; proj rows 0..nrows-1]
 __global__ void kda_conv_commit_kernel(KdaArgs a) {
   const int C = 3 * a.H * a.Dh;
@@ -162,6 +213,14 @@ using namespace g53;
 cudaError_t g53_kda_conv(const KdaArgs& a, cudaStream_t st) {
   if (a.taps > 8 || a.taps < 2) return cudaErrorInvalidValue;
   const int C = 3 * a.H * a.Dh;
+  // 16-byte rows: the vectorised kernel (4 taps: the model's short convolution)
+  if (a.taps == 4 && C % 8 == 0 && a.ldp % 8 == 0 && (reinterpret_cast<uintptr_t>(a.proj) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(a.qkv) & 15) == 0 && (reinterpret_cast<uintptr_t>(a.conv_pool) & 15) == 0) {
+    dim3 grid((C / 8 + 255) / 256, (a.max_rows + kConvRB - 1) / kConvRB, a.B);
+    kda_conv_vec_kernel<4><<<grid, 256, 0, st>>>(a);
+    G53_CHECK_LAUNCH();
+    return cudaSuccess;
+  }
   dim3 grid((C + 255) / 256, (a.max_rows + kConvRB - 1) / kConvRB, a.B);
   kda_conv_kernel<<<grid, 256, 0, st>>>(a);
   G53_CHECK_LAUNCH();
