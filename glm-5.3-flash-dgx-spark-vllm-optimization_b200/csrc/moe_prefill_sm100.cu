@@ -27,8 +27,14 @@ namespace g53 {
 namespace mp {
 
 constexpr uint32_t kSpin = 1u << 26;
-constexpr int kDecWarps = 16;
-constexpr int kThreads = (kDecWarps + 2) * 32;
+// decoder warps: gate/up (two TMEM accumulators = all 512 columns, one CTA per SM) uses 16; down (256 columns,
+// two stages) runs two CTAs of 8 decoder warps per SM so one CTA's epilogue overlaps the other's decode
+template <bool GU> struct Cfg {
+  static constexpr int kDecWarps = GU ? 16 : 8;
+  static constexpr int kThreads = (kDecWarps + 2) * 32;
+  static constexpr int kStages = 2;
+  static constexpr int kMinBlocks = GU ? 1 : 2;
+};
 constexpr int kNmax = 256;            // tokens per pass
 constexpr int kBK = 64;               // k per stage (one 128-byte swizzle row of f16)
 
@@ -134,11 +140,12 @@ __device__ __forceinline__ void ep_count_in(const MoePrefillArgs& p) {
 }
 
 template <bool GU>
-__global__ void __launch_bounds__(kThreads, 1) moe_prefill_kernel(const __grid_constant__ CUtensorMap tb0,
+__global__ void __launch_bounds__(Cfg<GU>::kThreads, Cfg<GU>::kMinBlocks) moe_prefill_kernel(const __grid_constant__ CUtensorMap tb0,
                                                                   const __grid_constant__ CUtensorMap tb1,
                                                                   MoePrefillArgs p) {
   constexpr int NM = GU ? 2 : 1;                       // weight matrices
-  constexpr int STAGES = GU ? 2 : 4;
+  constexpr int STAGES = Cfg<GU>::kStages;
+  constexpr int kDecWarps = Cfg<GU>::kDecWarps;
   constexpr int A_BYTES = 128 * 128;                   // 128 rows x 64 f16
   constexpr int B_BYTES = kNmax * 128;                 // 256 token rows x 64 f16
   constexpr int STAGE = NM * (A_BYTES + B_BYTES);
@@ -417,18 +424,18 @@ cudaError_t g53_moe_prefill(const MoePrefillArgs& p, bool gate_up, cudaStream_t 
   if (!act_map(&t0, p.x0, p.rows, p.K)) return cudaErrorInvalidValue;
   if (gate_up && !act_map(&t1, p.x1, p.rows, p.K)) return cudaErrorInvalidValue;
   if (!gate_up) t1 = t0;
-  const int NM = gate_up ? 2 : 1, STAGES = gate_up ? 2 : 4;
+  const int NM = gate_up ? 2 : 1, STAGES = gate_up ? Cfg<true>::kStages : Cfg<false>::kStages;
   const int smem = STAGES * NM * (128 * 128 + kNmax * 128) + 1024;
   dim3 grid(p.N / 128, p.max_groups);
   cudaError_t e;
   if (gate_up) {
     e = cudaFuncSetAttribute(moe_prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    moe_prefill_kernel<true><<<grid, kThreads, smem, st>>>(t0, t1, p);
+    moe_prefill_kernel<true><<<grid, Cfg<true>::kThreads, smem, st>>>(t0, t1, p);
   } else {
     e = cudaFuncSetAttribute(moe_prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    moe_prefill_kernel<false><<<grid, kThreads, smem, st>>>(t0, t1, p);
+    moe_prefill_kernel<false><<<grid, Cfg<false>::kThreads, smem, st>>>(t0, t1, p);
   }
   return cudaGetLastError();
 }
