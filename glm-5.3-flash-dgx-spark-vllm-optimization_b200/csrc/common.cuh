@@ -9,6 +9,14 @@
 
 #define G53_CHECK_LAUNCH() do { cudaError_t e_ = cudaGetLastError(); if (e_ != cudaSuccess) return e_; } while (0)
 
+// Programmatic dependent launch.  A kernel launched with the programmatic-stream-serialization attribute may start
+// while the previous kernel of the stream still runs: it must call pdl_wait() before it reads anything that kernel
+// writes (pdl_wait returns at once when the launch has no programmatic dependency).  pdl_trigger() lets the
+// dependents of the calling kernel begin launching (they still wait for its completion in their own pdl_wait).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 namespace g53 {
 
 constexpr int kWarp = 32;

@@ -14,6 +14,7 @@
 // Reference counterparts: code/fork/kernels/fp8_gemv.cu:96 (Marlin-layout fp8 GEMV, M <= 64) and
 // code/fork/kernels/gemv_bf16.cu:83 (router / small bf16 GEMM).
 #include <algorithm>
+#include <cstdlib>
 #include <cooperative_groups.h>
 #include "common.cuh"
 #include "launchers.h"
@@ -49,6 +50,15 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
 
   float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
   const uint4 z4 = make_uint4(0, 0, 0, 0);
+
+  // the weights do not depend on the previous kernel: pull this warp's chunks towards L2 before waiting for it
+  for (int c = c_lo + ks; c < nchunk; c += KS) {
+    const int kb = c * CH + q * (CH / 4);
+    if (rA) prefetch_l2(wr0 + (int64_t)kb * esz);
+    if (rB) prefetch_l2(wr1 + (int64_t)kb * esz);
+  }
+  pdl_trigger();
+  pdl_wait();
 
 #pragma unroll 4
   for (int c = c_lo + ks; c < nchunk; c += KS) {
@@ -364,25 +374,42 @@ __global__ void __launch_bounds__(256, 1) gemv_stream_kernel(GemvArgs p, float* 
   }
 }
 
+// launched as a programmatic dependent of the previous kernel (weights prefetched before pdl_wait) unless
+// GLM53_PDL=0
+static bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("GLM53_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 template <bool FP8, int KS, int NT>
 static cudaError_t launch_cfg(const GemvArgs& p, dim3 grid, int cl, cudaStream_t st) {
-  if (cl <= 1) {
-    gemv_kernel<FP8, KS, NT, 1><<<grid, 256, 0, st>>>(p);
-    return cudaGetLastError();
-  }
   cudaLaunchConfig_t cfg = {};
-  grid.z = cl;
+  if (cl > 1) grid.z = cl;
   cfg.gridDim = grid;
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = cl;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (cl > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = cl;
+    ++na;
+  }
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = na;
+  if (cl <= 1) return cudaLaunchKernelEx(&cfg, gemv_kernel<FP8, KS, NT, 1>, p);
   switch (cl) {
     case 2: return cudaLaunchKernelEx(&cfg, gemv_kernel<FP8, KS, NT, 2>, p);
     case 4: return cudaLaunchKernelEx(&cfg, gemv_kernel<FP8, KS, NT, 4>, p);

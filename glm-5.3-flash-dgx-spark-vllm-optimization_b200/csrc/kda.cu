@@ -49,6 +49,7 @@ __global__ void kda_conv_kernel(KdaArgs a) {
 // of kConvRB consecutive rows; the taps and the history stay in registers
 template <int T>
 __global__ void __launch_bounds__(256) kda_conv_vec_kernel(KdaArgs a) {
+  pdl_trigger();                       // dependents (the next projection) may start prefetching
   const int C = 3 * a.H * a.Dh;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   const int b = blockIdx.z;
@@ -119,6 +120,7 @@ __global__ void kda_conv_commit_kernel(KdaArgs a) {
 constexpr int kRecRows = 8;
 template <int DH>
 __global__ void __launch_bounds__(128) kda_recurrent_kernel(KdaArgs a) {
+  pdl_trigger();                       // dependents (the next projection) may start prefetching
   constexpr int KP = DH / 4;
   __shared__ float sq[kRecRows][DH], sk[kRecRows][DH], sg[kRecRows][DH], sv[kRecRows][32], sb[kRecRows];
   const int h = blockIdx.x, b = blockIdx.z;
@@ -191,6 +193,7 @@ __global__ void __launch_bounds__(128) kda_recurrent_kernel(KdaArgs a) {
 
 // one warp per (row, head)
 __global__ void kda_gated_norm_kernel(KdaArgs a) {
+  pdl_trigger();                       // dependents (the next projection) may start prefetching
   const int lane = threadIdx.x & 31;
   const int idx = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (idx >= a.R * a.H) return;

@@ -20,6 +20,7 @@ constexpr int kRB = 16;      // rows per partial CTA
 
 template <int S>
 __global__ void __launch_bounds__(kDB) hc_partial_kernel(HcArgs a) {
+  pdl_trigger();                       // dependents (the next projection) may start prefetching
   constexpr int NM = 2 * S + S * S;
   const int d = blockIdx.x * kDB + threadIdx.x;
   const int NB = a.D / kDB;
@@ -135,6 +136,7 @@ __device__ __forceinline__ float warp_col_sum(float v) {
 
 template <int S>
 __global__ void __launch_bounds__(512) hc_finish_kernel(HcArgs a) {
+  pdl_trigger();                       // dependents (the next projection) may start prefetching
   constexpr int NM = 2 * S + S * S;
   const int r = blockIdx.x;
   const int NB = a.nb;

@@ -23,6 +23,7 @@ __device__ __forceinline__ void rope_pair(float x1, float x2, float ang, float& 
 }
 
 __global__ void __launch_bounds__(256) mla_prep_kernel(MlaPrepArgs a) {
+  pdl_trigger();                       // dependents (the next projection) may start prefetching
   const int r = blockIdx.x;
   __shared__ float red[32];
   __shared__ float vals[1024];
@@ -292,6 +293,7 @@ __global__ void __launch_bounds__(128) mla_decode_kernel(MlaAttnArgs a) {
 }
 
 __global__ void mla_merge_kernel(MlaAttnArgs a) {
+  pdl_trigger();                       // dependents (the next projection) may start prefetching
   const int r = blockIdx.x, h = blockIdx.y;
   const int S = a.splits;
   float M = -INFINITY;

@@ -461,6 +461,7 @@ __global__ void __launch_bounds__(256) exl3_down_kernel(Exl3Args a) {
 
 __global__ void moe_combine_kernel(const float* yd, const int* pair_of, int R, int top_k, int D, float* out,
                                    int accumulate) {
+  pdl_trigger();                       // dependents (the next projection) may start prefetching
   const int r = blockIdx.y;
   const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (d >= D) return;

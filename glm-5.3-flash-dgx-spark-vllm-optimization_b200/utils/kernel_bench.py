@@ -153,6 +153,8 @@ def bench_gemv(args, T: Timer):
                           (2048, 4096, "mla_qkv_a"), (154880, 4096, "lm_head"), (288, 4096, "router_bf16"),
                           (16384, 1536, "mla_q_b"), (4096, 4096, "shared_gate_up"), (4096, 2048, "shared_down"),
                           (24576, 4096, "dense_gate_up"), (4096, 12288, "dense_down")]:
+        if args.proj and name not in args.proj:
+            continue
         for M in args.rows:
             x = torch.randn(M, Kd, device="cuda").to(torch.bfloat16)
             y = torch.empty(M, N, device="cuda")
@@ -403,6 +405,7 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--no-flush", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="gemv: every split-K shape")
+    ap.add_argument("--proj", nargs="+", default=None, help="gemv: only these projections")
     args = ap.parse_args(argv)
     import sys
     sys.path.insert(0, ROOT)
