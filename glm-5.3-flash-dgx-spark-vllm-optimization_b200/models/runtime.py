@@ -394,7 +394,7 @@ class Runtime:
         C3 = 3 * H * Dh
         K.linear8(self.normed[:R], k.in_proj.w, k.in_proj.s, proj, proj="kda_in_proj")
         K.linear8(proj[:, C3:C3 + Dh], k.f_b.w, k.f_b.s, fb)
-        side = self.overlap and R <= K.GEMV_MAX_M
+        side = getattr(self, "overlap", False) and R <= K.GEMV_MAX_M
         if side:        # output gate (read only by the gated norm) beside the convolution and recurrence
             self.ev_fork.record()
             with torch.cuda.stream(self.side):
@@ -495,7 +495,7 @@ class Runtime:
             self._shared_expert(lw, R)
             return
         MR = self.rlogits.shape[0]
-        if self.overlap and not self._fused and R <= MR:
+        if getattr(self, "overlap", False) and not self._fused and R <= MR:
             # the shared expert writes the branch on the side stream while the routed experts run; the routed
             # slot-ordered sum is formed first and the shared output added last (the same fp32 operations as the
             # sequential routed-then-shared order)
