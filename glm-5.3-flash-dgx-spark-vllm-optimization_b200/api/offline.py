@@ -43,6 +43,10 @@ class LLM:
     def __init__(self, opts: LLMOptions | None = None, comm=None, rank: int = 0, world: int = 1, **kw):
         opts = opts or LLMOptions(**kw)
         self.opts = opts
+        if os.environ.get("GLM53_BOOT_CHECKS", "0") == "1":      # per-rank boot assertions (collective)
+            from ..utils import boot_checks
+            self.boot_report = boot_checks.run()
+            boot_checks.enforce(self.boot_report)
         dev = torch.device("cuda", torch.cuda.current_device())
         if os.path.isdir(opts.model):
             cfg = W.load_config(opts.model)

@@ -57,10 +57,14 @@ def reference_provider(weights_cpu):
     return run
 
 
-def runtime_provider(weights_gpu, window: int = 16):
+def runtime_provider(weights_gpu, window: int = 16, max_len: int = 4096):
+    """Logits of every position, the sequence run through the GPU runtime in windows of `window` rows: up to 16
+    rows take the decode kernels (GEMV, per-row attention), from 64 rows on the prefill kernels (tcgen05 GEMM,
+    chunked KDA)."""
     from ..models.runtime import Runtime, RuntimeConfig
     from ..models.session import Sequence
-    rc = RuntimeConfig(max_rows=window, max_seqs=1, kv_slots=64 * 64, block_size=64, max_blocks=64,
+    blocks = (max_len + 63) // 64
+    rc = RuntimeConfig(max_rows=window, max_seqs=1, kv_slots=64 * blocks, block_size=64, max_blocks=blocks,
                        logit_rows=window)
     rt = Runtime(weights_gpu, rc)
 
