@@ -56,6 +56,8 @@ static void stream_scratch(const Tensor& like, GemvArgs& p) {
   p.stream_sms = sms[dev];
 }
 
+Tensor& err_word(const Tensor& like);
+
 void gemv(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, int64_t mode, double limit,
           int64_t ks, int64_t cl) {
   cuda_check(x, "x"); cuda_check(w, "w"); cuda_check(y, "y");
@@ -97,6 +99,7 @@ void gemv(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, 
     if (stream_gemv_enabled()) stream_scratch(x, p);
     p.force_ks = (int)ks;
     p.force_cl = (int)cl;
+    p.err = err_word(x).data_ptr<int>();
     check(g53_gemv_fp8(p, stream()), "gemv_fp8");
   } else {
     TORCH_CHECK(w.scalar_type() == at::kBFloat16, "weights must be fp8 (uint8) or bf16");

@@ -427,10 +427,35 @@ static cudaError_t launch_stream(const GemvArgs& p, float* part, int* cnt, int s
   return cudaGetLastError();
 }
 
+// large fp8 projections go through the bulk-copy kernel (GLM53_BULK_GEMV=0 disables it; GLM53_BULK_GEMV_MIN sets
+// the weight size in bytes from which it is used).  Measured on B200 (L2 flushed, M = 8): 1.5x on the KDA input
+// projection and the lm_head shard (0.89 of measured HBM), 1.1-1.3x on the 4096-row output projections, 1.2x on
+// 8 MB shapes; for 9..16 rows with K > 4096 its 2 KB stages lose to the split-K kernel, which keeps those.
+static bool bulk_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("GLM53_BULK_GEMV");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+static int64_t bulk_min_bytes() {
+  static int64_t v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("GLM53_BULK_GEMV_MIN");
+    v = e ? std::atoll(e) : (int64_t)4 << 20;
+  }
+  return v;
+}
+
 template <bool FP8>
 static cudaError_t launch_gemv_t(const GemvArgs& p, cudaStream_t st) {
   const int CH = FP8 ? 64 : 32;
   if (p.K % CH != 0 || p.M < 1 || p.M > 16) return cudaErrorInvalidValue;
+  if (FP8 && g53_gemv_bulk_ok(p) &&
+      (p.force_ks == -1 || (p.force_ks == 0 && p.force_cl == 0 && bulk_enabled() && (p.M <= 8 || p.K <= 4096) &&
+                            (int64_t)p.N * p.K >= bulk_min_bytes())))
+    return g53_gemv_bulk(p, pdl_enabled(), st);
   if (FP8 && p.stream_part && p.force_ks == 0 && p.batch == 1 && p.push_ptrs == nullptr &&
       (int64_t)((p.N + 15) / 16) * (p.K / 64) >= (int64_t)p.stream_sms * 8 * 16 &&
       (p.N + 15) / 16 <= p.stream_tiles)

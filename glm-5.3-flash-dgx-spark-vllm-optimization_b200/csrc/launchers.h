@@ -29,10 +29,15 @@ struct GemvArgs {
   // stream-K scratch (large fp8 projections): [SMs * 16 warps][2][256] fp32 partials, [stream_tiles] counters
   // (zero between launches); null = the split-K kernel only
   float* stream_part; int* stream_cnt; int stream_tiles; int stream_sms;
-  int force_ks, force_cl;                              // split-K kernel shape overrides (0 = chosen by size)
+  int force_ks, force_cl;                              // split-K kernel shape overrides (0 = chosen by size; force_ks
+                                                       // -1 = the bulk-copy kernel, -2 = the split-K kernel
+                                                       // with its own shape choice)
 };
 cudaError_t g53_gemv_fp8(const GemvArgs& p, cudaStream_t st);
 cudaError_t g53_gemv_bf16(const GemvArgs& p, cudaStream_t st);
+// persistent bulk-copy (TMA) streamed variant for large fp8 projections (gemv_bulk.cu)
+bool g53_gemv_bulk_ok(const GemvArgs& p);
+cudaError_t g53_gemv_bulk(const GemvArgs& p, bool pdl, cudaStream_t st);
 
 // ---------------------------------------------------------------- large-M GEMM (gemm_sm100.cu)
 struct GemmArgs {

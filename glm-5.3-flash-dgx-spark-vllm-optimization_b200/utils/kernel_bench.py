@@ -155,6 +155,12 @@ def bench_gemv(args, T: Timer):
                           (24576, 4096, "dense_gate_up"), (4096, 12288, "dense_down")]:
         if args.proj and name not in args.proj:
             continue
+        if args.tp > 1:
+            # per-rank shape: row-parallel projections split K, replicated ones keep both, the rest split N
+            if name in ("kda_o_proj", "mla_o_proj", "shared_down", "dense_down"):
+                Kd //= args.tp
+            elif name not in ("mla_qkv_a", "router_bf16"):
+                N //= args.tp
         for M in args.rows:
             x = torch.randn(M, Kd, device="cuda").to(torch.bfloat16)
             y = torch.empty(M, N, device="cuda")
@@ -174,8 +180,22 @@ def bench_gemv(args, T: Timer):
                             ms = T(lambda: K.C().gemv(x, q.w, q.s, y, K.GEMV_F32, 0.0, ks, cl))
                             emit({"case": "gemv_sweep", "proj": name, "M": M, "ks": ks, "cl": cl, "ms": ms,
                                   "frac_of_hbm": nbytes / ms / 1e6 / hbm})
+                # size calibration: a device copy of the weight bytes (read + write) at this size
+                dst = torch.empty_like(q.w)
+                msc = T(lambda: dst.copy_(q.w))
+                emit({"case": "gemv_copy_ref", "proj": name, "bytes": nbytes, "ms": msc,
+                      "copy_GBps": 2 * nbytes / msc / 1e6})
+                del dst
+                # the two fp8 kernels: load-per-lane split-K (ks=-2: its own shape choice) and the bulk-copy ring
+                # (ks=-1); "ms" is the default dispatch
+                for kind, ks in (("loads", -2), ("bulk", -1)):
+                    if kind == "bulk" and Kd % 512:
+                        continue
+                    msk = T(lambda: K.C().gemv(x, q.w, q.s, y, K.GEMV_F32, 0.0, ks, 0))
+                    emit({"case": "gemv_kernel", "kernel": kind, "proj": name, "M": M, "ms": msk,
+                          "frac_of_hbm": nbytes / msk / 1e6 / hbm})
                 ms = T(lambda: K.C().gemv(x, q.w, q.s, y, K.GEMV_F32, 0.0))
-            emit({"case": "gemv", "proj": name, "M": M, "N": N, "K": Kd, "ms": ms, "GBps": nbytes / ms / 1e6,
+            emit({"case": "gemv", "proj": name, "tp": args.tp, "M": M, "N": N, "K": Kd, "ms": ms, "GBps": nbytes / ms / 1e6,
                   "frac_of_hbm": nbytes / ms / 1e6 / hbm})
 
 

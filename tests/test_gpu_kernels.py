@@ -328,3 +328,56 @@ def test_gemv_swiglu_stream_k(C):
     y = torch.empty(M, Wd, dtype=torch.bfloat16, device=DEV)
     Kk.C().gemv(x.to(DEV), il.w.to(DEV), il.s.to(DEV), y, Kk.GEMV_SWIGLU, 10.0)
     torch.testing.assert_close(y.float().cpu(), ref, atol=3e-2, rtol=3e-2)
+
+
+@pytest.mark.parametrize("M", [1, 8, 13, 16])
+@pytest.mark.parametrize("N,K", [(1000, 3072), (520, 1024), (272, 2048), (4096, 8192), (1000, 12288),
+                                 (24896, 4096)])
+def test_gemv_fp8_bulk(C, M, N, K):
+    """The bulk-copy (TMA ring) decode projection, forced (ks=-1): every output mode against the fp32 reference
+    (partial last tiles for N=1000, 520 and 272; 1, 2 and 4 KB stages; activations register-resident or streamed
+    from L2 by K and row count), and two launches in a row give identical bits."""
+    from glm53.models.weights import quantize_fp8_rows
+    from glm53.ops import kernels as Kk
+    g = torch.Generator(device=DEV).manual_seed(M * 31 + N + K)
+    w = quantize_fp8_rows(torch.randn(N, K, device=DEV, generator=g) / math.sqrt(K))
+    x = torch.randn(M, K, device=DEV, generator=g).to(torch.bfloat16)
+    ref = x.float() @ w.dequant().t()
+    y = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    Kk.C().gemv(x, w.w, w.s, y, Kk.GEMV_F32, 0.0, -1, 0)
+    torch.testing.assert_close(y, ref, atol=2e-3, rtol=2e-3)
+    y2 = torch.full_like(y, float("nan"))
+    Kk.C().gemv(x, w.w, w.s, y2, Kk.GEMV_F32, 0.0, -1, 0)
+    assert torch.equal(y, y2)
+    yb = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    Kk.C().gemv(x, w.w, w.s, yb, Kk.GEMV_BF16, 0.0, -1, 0)
+    torch.testing.assert_close(yb.float(), ref, atol=2e-2, rtol=2e-2)
+    acc = torch.ones(M, N, dtype=torch.float32, device=DEV)
+    Kk.C().gemv(x, w.w, w.s, acc, Kk.GEMV_F32_ACC, 0.0, -1, 0)
+    torch.testing.assert_close(acc, ref + 1, atol=2e-3, rtol=2e-3)
+    # a strided activation view (rows of a wider buffer) and an output with a row pitch
+    xw = torch.zeros(M, K + 64, device=DEV, dtype=torch.bfloat16)
+    xw[:, :K] = x
+    yw = torch.zeros(M, N + 16, device=DEV)
+    Kk.C().gemv(xw[:, :K], w.w, w.s, yw[:, :N], Kk.GEMV_F32, 0.0, -1, 0)
+    assert torch.equal(yw[:, :N], y) and (yw[:, N:] == 0).all()
+    assert Kk.C().gemm_error(x) == 0                     # no bounded wait ran out
+
+
+@pytest.mark.parametrize("M", [1, 8, 16])
+def test_gemv_swiglu_bulk(C, M):
+    from glm53.models.runtime import interleave_gate_up
+    from glm53.models.weights import quantize_fp8_rows
+    from glm53.models.reference import swiglu
+    from glm53.ops import kernels as Kk
+    torch.manual_seed(2)
+    Wd, Kd = 2048, 4096
+    gu = quantize_fp8_rows(torch.randn(2 * Wd, Kd) / math.sqrt(Kd))
+    x = torch.randn(M, Kd).to(torch.bfloat16)
+    full = x.float() @ gu.dequant().t()
+    gg, uu = full[:, :Wd].to(torch.bfloat16).float(), full[:, Wd:].to(torch.bfloat16).float()
+    ref = swiglu(gg, uu, 10.0)
+    il = interleave_gate_up(gu)
+    y = torch.empty(M, Wd, dtype=torch.bfloat16, device=DEV)
+    Kk.C().gemv(x.to(DEV), il.w.to(DEV), il.s.to(DEV), y, Kk.GEMV_SWIGLU, 10.0, -1, 0)
+    torch.testing.assert_close(y.float().cpu(), ref, atol=3e-2, rtol=3e-2)
