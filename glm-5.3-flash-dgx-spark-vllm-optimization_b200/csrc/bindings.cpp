@@ -276,6 +276,28 @@ void gemv_push(const Tensor& x, const Tensor& w, const Tensor& scale, const Tens
   check(g53_gemv_fp8(p, stream()), "gemv_push");
 }
 
+// the byte ranges of the given tensors, in order, at most max_bytes in total (at most four tensors)
+L2Ranges l2_ranges(const std::vector<Tensor>& ts, int64_t max_bytes) {
+  L2Ranges r{};
+  int64_t left = max_bytes;
+  for (const auto& t : ts) {
+    if (r.count == 4 || left <= 0) break;
+    cuda_check(t, "prefetched tensor");
+    TORCH_CHECK(t.is_contiguous(), "l2_prefetch: tensors must be contiguous");
+    const int64_t n = std::min<int64_t>(left, t.numel() * t.element_size());
+    r.ptr[r.count] = reinterpret_cast<const char*>(t.data_ptr());
+    r.bytes[r.count] = n;
+    ++r.count;
+    left -= n;
+  }
+  return r;
+}
+
+// prefetch the given tensors into L2 from a separate small kernel
+void l2_prefetch(const std::vector<Tensor>& ts, int64_t max_bytes) {
+  check(g53_l2_prefetch(l2_ranges(ts, max_bytes), stream()), "l2_prefetch");
+}
+
 // ------------------------------------------------------------------------------------------------- MoE
 void moe_route(const Tensor& logits, const Tensor& bias, int64_t top_k, double scale, bool norm,
                const Tensor& topk_ids, const Tensor& topk_w, const Tensor& group_count, const Tensor& group_expert,
@@ -341,9 +363,11 @@ void exl3_moe(const Tensor& x, const Tensor& tr_g, const Tensor& suh_g, const Te
               const Tensor& suh_u, const Tensor& svh_u, const Tensor& tr_d, const Tensor& suh_d, const Tensor& svh_d,
               const Tensor& group_count, const Tensor& group_expert, const Tensor& group_offset,
               const Tensor& pair_token, const Tensor& pair_expert, const Tensor& pair_w, const Tensor& xh_g,
-              const Tensor& xh_u, const Tensor& xd, const Tensor& yd, double limit) {
+              const Tensor& xh_u, const Tensor& xd, const Tensor& yd, double limit,
+              const std::vector<Tensor>& prefetch, int64_t prefetch_bytes) {
   Exl3Args a = exl3_args(x, tr_g, suh_g, svh_g, tr_u, suh_u, svh_u, tr_d, suh_d, svh_d, group_count, group_expert,
                          group_offset, pair_token, pair_expert, pair_w, xh_g, xh_u, xd, yd, limit);
+  a.pf = l2_ranges(prefetch, prefetch_bytes);
   check(g53_exl3_rot_in(a, stream()), "exl3_rot_in");
   check(g53_exl3_gate_up(a, stream()), "exl3_gate_up");
   check(g53_exl3_down(a, stream()), "exl3_down");
@@ -930,11 +954,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16", &gemm_bf16);
   m.def("gemm_w8a16", &gemm_w8a16);
   m.def("gemm_error", &gemm_error);
+  m.def("l2_prefetch", &l2_prefetch, py::arg("tensors"), py::arg("max_bytes"));
   m.def("gemm_w8a16_push", &gemm_w8a16_push);
   m.def("gemm_ag_w8a16", &gemm_ag_w8a16);
   m.def("signal_peers", &signal_peers);
   m.def("moe_route", &moe_route);
-  m.def("exl3_moe", &exl3_moe);
+  m.def("exl3_moe", &exl3_moe, py::arg("x"), py::arg("tr_g"), py::arg("suh_g"), py::arg("svh_g"), py::arg("tr_u"),
+        py::arg("suh_u"), py::arg("svh_u"), py::arg("tr_d"), py::arg("suh_d"), py::arg("svh_d"),
+        py::arg("group_count"), py::arg("group_expert"), py::arg("group_offset"), py::arg("pair_token"),
+        py::arg("pair_expert"), py::arg("pair_w"), py::arg("xh_g"), py::arg("xh_u"), py::arg("xd"), py::arg("yd"),
+        py::arg("limit"), py::arg("prefetch") = std::vector<Tensor>{}, py::arg("prefetch_bytes") = 0);
   m.def("moe_combine", &moe_combine);
   m.def("moe_route_large", &moe_route_large);
   m.def("moe_prefill", &moe_prefill);

@@ -104,6 +104,18 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void* p) {
   return r;
 }
 
+// L2 eviction-priority policy for data read once (streamed weights): such lines are replaced first, so data
+// prefetched into L2 for a later kernel survives the stream
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint32_t ldg_nc_u32_ef(const void* p, uint64_t pol) {
+  uint32_t r;
+  asm("ld.global.nc.L1::no_allocate.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(r) : "l"(p), "l"(pol));
+  return r;
+}
 __device__ __forceinline__ uint32_t ldg_nc_u32(const void* p) {
   uint32_t r;
   asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));

@@ -35,6 +35,14 @@ struct GemvArgs {
 };
 cudaError_t g53_gemv_fp8(const GemvArgs& p, cudaStream_t st);
 cudaError_t g53_gemv_bf16(const GemvArgs& p, cudaStream_t st);
+// L2 prefetch of up to four weight ranges (l2_prefetch.cu)
+struct L2Ranges {
+  const char* ptr[4];
+  int64_t bytes[4];
+  int count;
+};
+cudaError_t g53_l2_prefetch(const L2Ranges& r, cudaStream_t st);
+
 // persistent bulk-copy (TMA) streamed variant for large fp8 projections (gemv_bulk.cu)
 bool g53_gemv_bulk_ok(const GemvArgs& p);
 cudaError_t g53_gemv_bulk(const GemvArgs& p, bool pdl, cudaStream_t st);
@@ -118,6 +126,9 @@ struct Exl3Args {
   const int64_t* push_flags;    // [push_world] flag addresses released after the last CTA
   int push_world;
   int launch_groups;            // > 0: grid rows of the group loop (CTAs stride over the group table)
+  // decode: weight ranges the gate/up CTAs prefetch into L2 (64 KB bulk prefetches spread over the grid) while the
+  // ALU-bound trellis decode leaves HBM idle; count 0 = none
+  L2Ranges pf;
 };
 cudaError_t g53_exl3_rot_in(const Exl3Args& a, cudaStream_t st);
 // ---------------------------------------------------------------- expert parallelism (ep_moe.cu)

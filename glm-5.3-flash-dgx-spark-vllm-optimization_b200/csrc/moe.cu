@@ -294,6 +294,7 @@ __device__ __forceinline__ void gate_up_group(const Exl3Args& a, int u, float (*
   const uint32_t* wu = reinterpret_cast<const uint32_t*>(a.tr_u) + ((int64_t)e * KT * NT + nt) * 32 + lane;
   const int64_t kstride = (int64_t)NT * 32;
   const int src = (lane + 31) & 31;
+  const uint64_t pol = l2_evict_first_policy();     // the codes are read once per step: replace them first in L2
 
   for (int m0 = 0; m0 < np; m0 += 8) {
     const int nrows = min(8, np - m0);
@@ -303,16 +304,16 @@ __device__ __forceinline__ void gate_up_group(const Exl3Args& a, int u, float (*
     uint32_t pg[4], pu[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      pg[i] = ldg_nc_u32(wg + (4 * c_lo + i) * kstride);
-      pu[i] = ldg_nc_u32(wu + (4 * c_lo + i) * kstride);
+      pg[i] = ldg_nc_u32_ef(wg + (4 * c_lo + i) * kstride, pol);
+      pu[i] = ldg_nc_u32_ef(wu + (4 * c_lo + i) * kstride, pol);
     }
     for (int c = c_lo; c < c_hi; ++c) {
       uint32_t ng[4], nu[4];
       const int64_t noff = (c + 1 < c_hi ? 4 * c + 4 : 4 * c) * kstride;   // the last chunk reloads itself
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        ng[i] = ldg_nc_u32(wg + noff + i * kstride);
-        nu[i] = ldg_nc_u32(wu + noff + i * kstride);
+        ng[i] = ldg_nc_u32_ef(wg + noff + i * kstride, pol);
+        nu[i] = ldg_nc_u32_ef(wu + noff + i * kstride, pol);
       }
       const uint4* bgp = reinterpret_cast<const uint4*>(a.xh_g + r0 + c * 128);
       const uint4* bup = reinterpret_cast<const uint4*>(a.xh_u + r0 + c * 128);
@@ -360,11 +361,29 @@ __device__ __forceinline__ void gate_up_group(const Exl3Args& a, int u, float (*
   }
 }
 
+// this CTA's share of the L2 prefetch: 64 KB chunks of the concatenated ranges, chunk i by CTA i mod grid size
+__device__ __forceinline__ void l2_prefetch_share(const L2Ranges& r) {
+  constexpr int64_t kChunk = 64 << 10;
+  const int64_t cta = blockIdx.x + (int64_t)gridDim.x * (blockIdx.y + (int64_t)gridDim.y * blockIdx.z);
+  const int64_t ncta = (int64_t)gridDim.x * gridDim.y * gridDim.z;
+  int64_t base = 0;                              // chunk index of the first chunk of range j
+  for (int j = 0; j < r.count; ++j) {
+    const int64_t n = r.bytes[j], chunks = (n + kChunk - 1) / kChunk;
+    for (int64_t c = ((cta - base) % ncta + ncta) % ncta; c < chunks; c += ncta) {
+      const int64_t off = c * kChunk, rem = n - off;
+      const uint32_t sz = (uint32_t)((rem < kChunk ? rem : kChunk) & ~(int64_t)15);
+      if (sz) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(r.ptr[j] + off), "r"(sz) : "memory");
+    }
+    base += chunks;
+  }
+}
+
 // CTAs loop over the groups (grid.y may be smaller than the group table: a decode window routes to few experts)
 template <int KSPL>
 __global__ void __launch_bounds__(256, 4) exl3_gate_up_kernel(Exl3Args a) {
   __shared__ float zg[8][132];
   __shared__ float zu[8][132];
+  if (a.pf.count && threadIdx.x == 0) l2_prefetch_share(a.pf);
   const int ng = min(a.group_count[0], a.max_groups);
   for (int u = blockIdx.y; u < ng; u += gridDim.y) gate_up_group<KSPL>(a, u, zg, zu);
 }
@@ -401,6 +420,7 @@ __device__ __forceinline__ void down_group(const Exl3Args& a, int u, float (*zd)
   const uint32_t* wd = reinterpret_cast<const uint32_t*>(a.tr_d) + ((int64_t)e * KT * NT + nt) * 32 + lane;
   const int64_t kstride = (int64_t)NT * 32;
   const int src = (lane + 31) & 31;
+  const uint64_t pol = l2_evict_first_policy();     // the codes are read once per step: replace them first in L2
 
   for (int m0 = 0; m0 < np; m0 += 8) {
     const int nrows = min(8, np - m0);
@@ -409,12 +429,12 @@ __device__ __forceinline__ void down_group(const Exl3Args& a, int u, float (*zd)
     float cd[4] = {};
     uint32_t pd[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) pd[i] = ldg_nc_u32(wd + (4 * c_lo + i) * kstride);
+    for (int i = 0; i < 4; ++i) pd[i] = ldg_nc_u32_ef(wd + (4 * c_lo + i) * kstride, pol);
     for (int c = c_lo; c < c_hi; ++c) {
       uint32_t nd[4];
       const int64_t noff = (c + 1 < c_hi ? 4 * c + 4 : 4 * c) * kstride;   // the last chunk reloads itself
 #pragma unroll
-      for (int i = 0; i < 4; ++i) nd[i] = ldg_nc_u32(wd + noff + i * kstride);
+      for (int i = 0; i < 4; ++i) nd[i] = ldg_nc_u32_ef(wd + noff + i * kstride, pol);
       const uint4* bp = reinterpret_cast<const uint4*>(a.xd + r0 + c * 128);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {

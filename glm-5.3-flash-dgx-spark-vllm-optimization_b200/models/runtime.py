@@ -99,6 +99,12 @@ class Runtime:
         if self.overlap:
             self.side = torch.cuda.Stream(device=dev)
             self.ev_fork, self.ev_join = torch.cuda.Event(), torch.cuda.Event()
+        # L2 prefetch (decode windows, GLM53_L2_PREFETCH=1): the routed experts' gate/up CTAs prefetch the next
+        # layer's first projections into L2 while their ALU-bound trellis decode leaves HBM idle (the trellis loads
+        # are marked evict-first); GLM53_L2_PREFETCH_MB caps the bytes.  Off by default: measured on the TP1 decode
+        # step it is neutral (+0.5 % at 32 MiB, -0.7 % at 96 MiB), the bulk-copy GEMV already streaming near HBM rate
+        self.l2pf = dev.type == "cuda" and os.environ.get("GLM53_L2_PREFETCH", "0") == "1"
+        self.l2pf_bytes = int(float(os.environ.get("GLM53_L2_PREFETCH_MB", "32")) * 2 ** 20)
         # prefill chunks (rows >= GEMM_MIN_M) can push their partials from the tcgen05 GEMM epilogue as well
         # (GLM53_FUSED_TP_PREFILL=1).  Off by default: measured on 8192-row chunks it is slower than NCCL's ring
         # all-reduce (32k prefill 10.1k vs 11.3k tok/s at TP2, 10.5k vs 15.3k at TP4) -- every rank stores its whole
@@ -381,6 +387,23 @@ class Runtime:
         else:
             K.linear8(x, lin.w, lin.s, self.branch[:R], mode, proj=proj)
 
+    def _moe_prefetch(self, lw, R):
+        """(tensors, bytes) the routed experts' gate/up CTAs prefetch into L2: the next layer's first projections."""
+        if getattr(self, "l2pf", False) and R <= K.GEMV_MAX_M:
+            return self._next_layer_weights(lw), self.l2pf_bytes
+        return [], 0
+
+    def _next_layer_weights(self, lw):
+        """The first bandwidth-bound projections of the layer after `lw` (none after the last layer)."""
+        i = lw.index + 1
+        if i >= len(self.w.layers):
+            return []
+        nl = self.w.layers[i]
+        if nl.kind == "kda":
+            return [nl.kda.in_proj.w, nl.kda.f_b.w]
+        a = nl.mla
+        return [a.qkv_a.w, a.q_b.w, a.index.wq_b.w]
+
     # ---- blocks ------------------------------------------------------------------------------------------------
     def _kda(self, lw, R):
         c, k, b = self.cfg, lw.kda, self.batch
@@ -519,7 +542,7 @@ class Runtime:
             Kc.exl3_moe(x, m.gate.trellis, m.gate.suh, m.gate.svh, m.up.trellis, m.up.suh, m.up.svh,
                         m.down.trellis, m.down.suh, m.down.svh, self.group_count, self.group_expert[:groups],
                         self.group_offset[:groups + 1], self.pair_token[:P], self.pair_expert[:P], self.pair_w[:P],
-                        self.xh_g, self.xh_u, self.xd, self.yd, c.limit)
+                        self.xh_g, self.xh_u, self.xd, self.yd, c.limit, *self._moe_prefetch(lw, R))
             torch.cuda.current_stream().wait_event(self.ev_join)
             Kc.moe_combine(self.yd, self.pair_of[:P], c.top_k, self.branch[:R], 2)
             return
@@ -534,10 +557,11 @@ class Runtime:
                          self.topk_w[:n], self.group_count, self.group_expert[:groups],
                          self.group_offset[:groups + 1], self.pair_token[:P], self.pair_expert[:P], self.pair_w[:P],
                          self.pair_of[:P])
+            pf = self._moe_prefetch(lw, R) if r0 == 0 else ([], 0)
             Kc.exl3_moe(x, m.gate.trellis, m.gate.suh, m.gate.svh, m.up.trellis, m.up.suh, m.up.svh,
                         m.down.trellis, m.down.suh, m.down.svh, self.group_count, self.group_expert[:groups],
                         self.group_offset[:groups + 1], self.pair_token[:P], self.pair_expert[:P], self.pair_w[:P],
-                        self.xh_g, self.xh_u, self.xd, self.yd, c.limit)
+                        self.xh_g, self.xh_u, self.xd, self.yd, c.limit, *pf)
             Kc.moe_combine(self.yd, self.pair_of[:P], c.top_k, self.branch[r0:r1], 0)
         self._shared_expert(lw, R)
 

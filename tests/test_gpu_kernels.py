@@ -122,6 +122,13 @@ def test_moe_routed_exl3(C, tiny_cfg, tiny_weights, rows):
     out = torch.empty(rows, cfg.hidden, device=DEV)
     Kc.moe_combine(rt.yd, rt.pair_of[:P], cfg.top_k, out, 0)
     torch.testing.assert_close(out.cpu(), ref, atol=2e-2, rtol=2e-2)
+    # with the gate/up CTAs prefetching other weights into L2 (a hint): the same bits
+    y1 = rt.yd[:P].clone()
+    Kc.exl3_moe(xd, m.gate.trellis, m.gate.suh, m.gate.svh, m.up.trellis, m.up.suh, m.up.svh, m.down.trellis,
+                m.down.suh, m.down.svh, rt.group_count, rt.group_expert[:G], rt.group_offset[:G + 1],
+                rt.pair_token[:P], rt.pair_expert[:P], rt.pair_w[:P], rt.xh_g, rt.xh_u, rt.xd, rt.yd, cfg.limit,
+                [m.down.trellis, m.router], 1 << 20)
+    assert torch.equal(rt.yd[:P], y1)
 
 
 def _to_dev(w):
@@ -381,3 +388,16 @@ def test_gemv_swiglu_bulk(C, M):
     y = torch.empty(M, Wd, dtype=torch.bfloat16, device=DEV)
     Kk.C().gemv(x.to(DEV), il.w.to(DEV), il.s.to(DEV), y, Kk.GEMV_SWIGLU, 10.0, -1, 0)
     torch.testing.assert_close(y.float().cpu(), ref, atol=3e-2, rtol=3e-2)
+
+
+def test_l2_prefetch_leaves_results_unchanged(C):
+    """The L2 prefetch paths are hints only: the standalone prefetch kernel and the MoE gate/up CTAs' prefetch of
+    other weights change no result bit of the routed experts."""
+    from glm53.ops import kernels as Kk
+    g = torch.Generator(device=DEV).manual_seed(5)
+    a = torch.randn(3000, 1024, device=DEV, generator=g).to(torch.bfloat16)
+    b = torch.randn(777 * 16, device=DEV, generator=g)
+    Kk.C().l2_prefetch([a, b], 1 << 30)
+    Kk.C().l2_prefetch([a], 4096)
+    torch.cuda.synchronize()
+    assert Kk.C().gemm_error(a) == 0
