@@ -53,3 +53,51 @@ def test_fused_tp_matches_nccl_two_gpus():
     assert len(result) == 2
     # two ranks: a + b is the same fp32 sum in either order, so the paths agree bit for bit
     assert max(result.values()) == 0.0, dict(result)
+
+
+def _push_worker(rank, world, port, result):
+    """Row-parallel decode projection with the fused push (bulk-copy GEMV for these sizes): every rank's fp32
+    partial must land in its slot of every rank's receive buffer and the arrival flags must count one launch."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from glm53.models.weights import quantize_fp8_rows
+    from glm53.ops import kernels as Kk
+    from glm53.parallel import dist as D
+    from glm53.parallel.fused import PeerExchange
+    D.init(timeout_s=60)
+    try:
+        dev = torch.device("cuda", rank)
+        errs = []
+        for N, K in ((4096, 2048), (4096, 4096)):
+            rows = 8
+            px = PeerExchange(rows, N, dev)
+            g = torch.Generator(device=dev).manual_seed(11)
+            x = torch.randn(rows, K, device=dev, generator=g).to(torch.bfloat16)
+            ws = [quantize_fp8_rows(torch.randn(N, K, device=dev, generator=torch.Generator(device=dev).manual_seed(
+                100 + j)) / K ** 0.5) for j in range(world)]
+            y = torch.empty(rows, N, device=dev)
+            Kk.C().gemv_push(x, ws[rank].w, ws[rank].s, y, Kk.GEMV_F32, px.push_ptrs[0], px.push_flags[0],
+                             px.done_prod[0:1], px.slot, rank, world, px.err)
+            torch.cuda.synchronize()
+            dist.barrier()
+            for j in range(world):
+                ref = torch.empty(rows, N, device=dev)
+                Kk.C().gemv(x, ws[j].w, ws[j].s, ref, Kk.GEMV_F32, 0.0)
+                got = px.gath[0][j * px.slot:(j + 1) * px.slot].view(rows, N)
+                errs.append((got - ref).abs().max().item())
+            errs.append(float((px.flags[0] != 1).sum().item()))
+            px.check()
+            dist.barrier()
+        result[rank] = max(errs)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_gemv_push_bulk_two_gpus():
+    import torch.multiprocessing as mp
+    result = mp.Manager().dict()
+    mp.spawn(_push_worker, args=(2, 29547, result), nprocs=2, join=True)
+    assert len(result) == 2
+    assert max(result.values()) == 0.0, dict(result)
