@@ -851,12 +851,22 @@ DsaArgs dsa_args(const Tensor& iproj, const Tensor& ln_w, const Tensor& ln_b, co
   return a;
 }
 
+// ik_rows / ig_rows: [>= R, ID] row buffers of this launch; ik_ring / ig_ring: [state slots * ring, ID] tail rings;
+// seq_desc: [5, sequences] int32 (row0, nrows, s_in, s_out, state slot) of the launch
 void dsa_update(const Tensor& iproj, const Tensor& ln_w, const Tensor& ln_b, const Tensor& ape,
-                const Tensor& ik_cache, const Tensor& ig_cache, const Tensor& pool_cache, const Tensor& pool_scale,
-                const Tensor& slots, const Tensor& positions, const Tensor& block_table, const Tensor& row_seq,
-                int64_t block_size, int64_t IH, int64_t kpool, double eps) {
-  DsaArgs a = dsa_args(iproj, ln_w, ln_b, ape, {}, ik_cache, ig_cache, pool_cache, pool_scale, slots, positions,
+                const Tensor& ik_rows, const Tensor& ig_rows, const Tensor& ik_ring, const Tensor& ig_ring,
+                const Tensor& pool_cache, const Tensor& pool_scale, const Tensor& slots, const Tensor& positions,
+                const Tensor& block_table, const Tensor& row_seq, const Tensor& seq_desc, int64_t block_size,
+                int64_t IH, int64_t kpool, double eps) {
+  DsaArgs a = dsa_args(iproj, ln_w, ln_b, ape, {}, ik_rows, ig_rows, pool_cache, pool_scale, slots, positions,
                        block_table, row_seq, block_size, IH, kpool, 0, eps, {}, {}, {});
+  TORCH_CHECK(ik_rows.size(0) >= a.R && ig_rows.size(0) >= a.R, "dsa_update: row buffers too small");
+  TORCH_CHECK(ik_ring.size(0) % kDsaRing == 0 && ig_ring.size(0) == ik_ring.size(0), "dsa_update: ring shape");
+  TORCH_CHECK(seq_desc.dim() == 2 && seq_desc.size(0) == 5 && seq_desc.scalar_type() == at::kInt, "seq_desc");
+  a.ik_ring = P<__nv_bfloat16>(ik_ring);
+  a.ig_ring = P<float>(ig_ring);
+  a.seq_desc = P<const int>(seq_desc);
+  a.seq_ld = (int)seq_desc.stride(0);
   check(g53_dsa_update(a, stream()), "dsa_update");
 }
 
@@ -997,6 +1007,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rope"), py::arg("sm_scale"), py::arg("splits"), py::arg("part_o"), py::arg("part_ml"),
         py::arg("o_lat"), py::arg("tensor_cores") = -1);
   m.def("dsa_update", &dsa_update);
+  m.def("dsa_ring_positions", []() { return (int64_t)kDsaRing; });
   m.def("dsa_select", &dsa_select);
   m.def("argmax_rows", &argmax_rows);
   m.def("greedy_verify", &greedy_verify);

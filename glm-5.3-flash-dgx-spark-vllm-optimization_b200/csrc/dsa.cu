@@ -1,10 +1,15 @@
 // DSA lightning indexer over pooled index keys.
 //
-//   update   per row: index key = LayerNorm(wk x) (bf16) and pool gate scores into the token-slot caches; rows
-//            that complete a pool of `kpool` tokens then compress it: per channel softmax over the pool's tokens
-//            of (gate + ape), weighted key sum -> bf16 -> Hadamard-128 -> bf16 -> e4m3 with a power-of-two scale
+//   update   per row: index key = LayerNorm(wk x) (bf16) and pool gate scores into row buffers; rows that
+//            complete a pool of `kpool` tokens then compress it: per channel softmax over the pool's tokens of
+//            (gate + ape), weighted key sum -> bf16 -> Hadamard-128 -> bf16 -> e4m3 with a power-of-two scale
 //            (the pool lives at pool slot = token slot of its first token / kpool)
-//            (reference: code/fork/tests/kpoolring/ref/kpool_compress_vllm58454.py:139-257)
+//            (reference: code/fork/tests/kpoolring/ref/kpool_compress_vllm58454.py:139-257).  A pool's tokens
+//            come from this launch's row buffers or, for tokens of earlier launches, from the sequence's tail ring
+//            (kDsaRing positions, indexed by the sequence's state slot and position mod kDsaRing); after the pools
+//            the last kDsaRing rows of every sequence are copied into its ring.  Only open pools ever need raw
+//            keys, so the cache keeps no per-token index keys (the reference's kpool tail ring,
+//            code/fork/tests/kpoolring/ref/kpool_compress_vllm58454.py:734-887)
 //   logits   per (row, pool): sum_h relu((Hq_h . k_pool) * scale) * w_h / sqrt(IH * ID), the queries rotated by
 //            the same Hadamard transform (so q.k is preserved) and held in shared memory
 //   select   per row: a query sees its own (partial) pool and the top (topk_pools - 1) earlier complete pools,
@@ -28,9 +33,34 @@ __global__ void __launch_bounds__(128) dsa_keys_kernel(DsaArgs a) {
   const float d = v - mean;
   const float var = block_sum(d * d, red) / (float)a.ID;
   const float y = d * rsqrtf(var + a.eps) * a.ln_w[c] + a.ln_b[c];
-  const int slot = a.slots[r];
-  a.ik_cache[(int64_t)slot * a.ID + c] = f2bf(y);
-  a.ig_cache[(int64_t)slot * a.ID + c] = x[a.ID + a.IH + c];
+  a.ik_cache[(int64_t)r * a.ID + c] = f2bf(y);
+  a.ig_cache[(int64_t)r * a.ID + c] = x[a.ID + a.IH + c];
+}
+
+// (index key, gate) row of token position p of row r's sequence: this launch's row buffer when p is one of its
+// rows, else the sequence's tail ring
+__device__ __forceinline__ int64_t dsa_src_row(const DsaArgs& a, int r, int pos, int p, bool& ring) {
+  const int rr = r - (pos - p);
+  if (rr >= 0 && a.row_seq[rr] == a.row_seq[r] && a.positions[rr] == p) {
+    ring = false;
+    return rr;
+  }
+  ring = true;
+  const int owner = a.seq_desc[4 * a.seq_ld + a.row_seq[r]];
+  return (int64_t)owner * kDsaRing + (p % kDsaRing);
+}
+
+// after the pools: the last kDsaRing rows of every sequence into its ring (positions mod kDsaRing are distinct)
+__global__ void __launch_bounds__(128) dsa_ring_kernel(DsaArgs a) {
+  const int r = blockIdx.x;
+  const int b = a.row_seq[r];
+  const int last = a.seq_desc[b] + a.seq_desc[a.seq_ld + b] - 1;
+  if (r <= last - kDsaRing) return;
+  const int owner = a.seq_desc[4 * a.seq_ld + b];
+  const int64_t dst = ((int64_t)owner * kDsaRing + a.positions[r] % kDsaRing) * a.ID;
+  const int c = threadIdx.x;
+  a.ik_ring[dst + c] = a.ik_cache[(int64_t)r * a.ID + c];
+  a.ig_ring[dst + c] = a.ig_cache[(int64_t)r * a.ID + c];
 }
 
 // one warp per row; rows whose position completes a pool compress it
@@ -47,21 +77,26 @@ __global__ void dsa_pool_kernel(DsaArgs a) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) mx[i] = -INFINITY;
   for (int s = 0; s < kp; ++s) {
-    const int slot = slot_of(bt, a.block_size, p0 + s);
+    bool ring;
+    const int64_t src = dsa_src_row(a, r, pos, p0 + s, ring) * a.ID;
+    const float* ig = ring ? a.ig_ring : a.ig_cache;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int c = lane * 4 + i;
-      mx[i] = fmaxf(mx[i], a.ig_cache[(int64_t)slot * a.ID + c] + a.ape[s * a.ID + c]);
+      mx[i] = fmaxf(mx[i], ig[src + c] + a.ape[s * a.ID + c]);
     }
   }
   for (int s = 0; s < kp; ++s) {
-    const int slot = slot_of(bt, a.block_size, p0 + s);
+    bool ring;
+    const int64_t src = dsa_src_row(a, r, pos, p0 + s, ring) * a.ID;
+    const float* ig = ring ? a.ig_ring : a.ig_cache;
+    const __nv_bfloat16* ik = ring ? a.ik_ring : a.ik_cache;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int c = lane * 4 + i;
-      const float e = __expf(a.ig_cache[(int64_t)slot * a.ID + c] + a.ape[s * a.ID + c] - mx[i]);
+      const float e = __expf(ig[src + c] + a.ape[s * a.ID + c] - mx[i]);
       den[i] += e;
-      acc[i] += e * bf2f(a.ik_cache[(int64_t)slot * a.ID + c]);
+      acc[i] += e * bf2f(ik[src + c]);
     }
   }
   float v[4];
@@ -211,6 +246,8 @@ cudaError_t g53_dsa_update(const DsaArgs& a, cudaStream_t st) {
   dsa_keys_kernel<<<a.R, 128, 0, st>>>(a);
   G53_CHECK_LAUNCH();
   dsa_pool_kernel<<<(a.R + 7) / 8, 256, 0, st>>>(a);
+  G53_CHECK_LAUNCH();
+  dsa_ring_kernel<<<a.R, 128, 0, st>>>(a);
   G53_CHECK_LAUNCH();
   return cudaSuccess;
 }

@@ -296,12 +296,18 @@ cudaError_t g53_mla_decode(const MlaAttnArgs& a, cudaStream_t st);
 // tensor-core attention only (no merge); splits > 1 leaves partials in part_o / part_ml
 cudaError_t g53_mla_attn_tc(const MlaAttnArgs& a, cudaStream_t st);
 
+constexpr int kDsaRing = 32;     // tail-ring positions per sequence (>= a window's rows + kpool - 1)
 struct DsaArgs {
   const float* iproj; int64_t ldi;  // [R, ID + IH + ID] fp32: index key | head weights | pool gate scores
   const float* ln_w; const float* ln_b; const float* ape;   // [ID], [ID], [kpool, ID]
   const __nv_bfloat16* qi;       // [R, IH*ID] index queries (bf16, before the Hadamard transform)
-  __nv_bfloat16* ik_cache;       // [token slots, ID] normalised index keys (bf16)
-  float* ig_cache;               // [token slots, ID] pool gate scores
+  // raw index keys and pool gate scores are kept only until their pool is complete: this launch's rows in row
+  // buffers, earlier tokens of a still-open pool in a per-sequence tail ring of kDsaRing positions
+  __nv_bfloat16* ik_cache;       // [rows, ID] normalised index keys of this launch's rows (bf16)
+  float* ig_cache;               // [rows, ID] pool gate scores of this launch's rows
+  __nv_bfloat16* ik_ring;        // [state slots * kDsaRing, ID] tail ring of index keys
+  float* ig_ring;                // [state slots * kDsaRing, ID] tail ring of gate scores
+  const int* seq_desc; int seq_ld;   // [5, sequences]: row0, nrows, s_in, s_out, state slot (the ring owner)
   uint8_t* pool_cache; float* pool_scale;   // [pool slots, ID] e4m3, [pool slots] power-of-two scales
   const int* slots;              // [R] token slot of each row
   const int* positions;          // [R] absolute position of each row

@@ -171,8 +171,14 @@ class Runtime:
             self.kv = [torch.zeros(ns, L, dtype=torch.uint8, device=dev) for _ in mla]
             self.kv_scale = [torch.zeros(ns, dtype=f32, device=dev) for _ in mla]
             self.kpe = [torch.zeros(ns, max(rope, 1), dtype=bf16, device=dev) for _ in mla]
-            self.ik = [torch.zeros(ns, c.index_dim, dtype=bf16, device=dev) for _ in mla]
-            self.ig = [torch.zeros(ns, c.index_dim, dtype=f32, device=dev) for _ in mla]
+            # raw index keys / pool gate scores live only until their pool of kpool tokens is complete: this
+            # forward's rows in shared row buffers, earlier tokens of open pools in a per-sequence tail ring per layer
+            # (indexed by the sequence's state slot); the paged cache holds pooled keys only
+            ring = K.DSA_RING
+            self.ik_rows = torch.zeros(R, c.index_dim, dtype=bf16, device=dev)
+            self.ig_rows = torch.zeros(R, c.index_dim, dtype=f32, device=dev)
+            self.ik_ring = [torch.zeros(rc.max_seqs * ring, c.index_dim, dtype=bf16, device=dev) for _ in mla]
+            self.ig_ring = [torch.zeros(rc.max_seqs * ring, c.index_dim, dtype=f32, device=dev) for _ in mla]
             self.pool = [torch.zeros(ns // c.kpool, c.index_dim, dtype=torch.uint8, device=dev) for _ in mla]
             self.pool_scale = [torch.zeros(ns // c.kpool, dtype=f32, device=dev) for _ in mla]
             AR = min(R, rc.attn_chunk)
@@ -457,9 +463,10 @@ class Runtime:
         K.linear8(self.q[:R, :, :nope].transpose(0, 1), a.w_uk_t.w, a.w_uk_t.s, self.q_lat[:R].transpose(0, 1))
         # indexer
         K.linear_bf16(self.normed[:R], a.index.proj, self.iproj[:R])
-        Kc.dsa_update(self.iproj[:R], a.index.ln_w, a.index.ln_b, a.index.ape, self.ik[li], self.ig[li],
-                      self.pool[li], self.pool_scale[li], b.slots[:R], b.positions[:R], b.block_table,
-                      b.row_seq[:R], self.rc.block_size, c.index_heads, c.kpool, c.eps)
+        Kc.dsa_update(self.iproj[:R], a.index.ln_w, a.index.ln_b, a.index.ape, self.ik_rows, self.ig_rows,
+                      self.ik_ring[li], self.ig_ring[li], self.pool[li], self.pool_scale[li], b.slots[:R],
+                      b.positions[:R], b.block_table, b.row_seq[:R], b.kda_seq[:, :b.B], self.rc.block_size,
+                      c.index_heads, c.kpool, c.eps)
         K.linear8(self.qr[:R], a.index.wq_b.w, a.index.wq_b.s, self.qi[:R])
         AR = self.sel.shape[0]
         sm_scale = c.qk_dim ** -0.5

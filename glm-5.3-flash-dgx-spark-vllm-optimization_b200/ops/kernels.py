@@ -35,6 +35,7 @@ def reserve_gemm_scratch(numel: int, device) -> None:
     _w_scratch(numel, torch.device(device))
 
 GEMV_BF16, GEMV_F32, GEMV_F32_ACC, GEMV_SWIGLU = 0, 1, 2, 3
+DSA_RING = 32            # tail-ring positions per sequence of the DSA index keys (kDsaRing in csrc/launchers.h)
 GEMV_MAX_M = 16
 GEMM_MIN_M = 64          # rows from which the tcgen05 GEMM replaces the small-M kernel
 

@@ -5,8 +5,9 @@ For every context length a request with uniform random token ids is prefilled th
 same path as any prompt), then `--steps` speculative decode steps (K drafts, acceptance forced) are timed with CUDA
 events, max over ranks.  With `--concurrency C`, C such requests decode together (one verify window of C x (K+1)
 rows per step).  The KV bytes per token are read from the runtime's own cache allocation (fp8 latent + scale + rope
-key per MLA layer, DSA index keys, pool gate scores and pooled keys), so the capacity figure is what this engine
-stores, per GPU (the latent and index caches are replicated over tensor-parallel ranks).
+key per MLA layer and the pooled fp8 index keys + scales; raw index keys are kept only in a per-sequence tail ring,
+not per token), so the capacity figure is what this engine stores, per GPU (the latent and index caches are
+replicated over tensor-parallel ranks).
 
     python -m glm53.utils.longctx --contexts 4096 32768 131072 --steps 8
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m glm53.utils.longctx --contexts 131072 524288
@@ -30,7 +31,7 @@ def kv_bytes_per_token(rt) -> int:
     if not slots:
         return 0
     total = 0
-    for name in ("kv", "kv_scale", "kpe", "ik", "ig", "pool", "pool_scale"):
+    for name in ("kv", "kv_scale", "kpe", "pool", "pool_scale"):
         for t in getattr(rt, name, []):
             total += t.numel() * t.element_size()
     return total // slots

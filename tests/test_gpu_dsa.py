@@ -52,3 +52,80 @@ def test_dsa_logits_tc_matches_cuda_cores(IH, shape):
     for r, p in enumerate(d["pos"]):
         c = p // d["kpool"]
         torch.testing.assert_close(out[1][r, :c], out[0][r, :c], atol=1e-3, rtol=1e-3)
+
+
+def _pools_by_launches(launches, streams, IH=4, seed=9):
+    """Run dsa_update over a list of launches; each launch is a list of (sequence, first position, rows) runs.
+    `streams[s]` gives every position's iproj row of sequence s (a launch may override rows with `garbage`).
+    Returns the pool cache and scales."""
+    from glm53.ops import kernels as Kk
+    C = Kk.C()
+    ID, kpool, bs, pages, nseq = 128, 4, 64, 16, 2
+    slots_per_seq = pages // nseq * bs
+    pool_cache = torch.zeros(pages * bs // kpool, ID, dtype=torch.uint8, device=DEV)
+    pool_scale = torch.zeros(pages * bs // kpool, device=DEV)
+    ik_rows = torch.zeros(512, ID, dtype=torch.bfloat16, device=DEV)
+    ig_rows = torch.zeros(512, ID, device=DEV)
+    ring = Kk.DSA_RING
+    assert C.dsa_ring_positions() == ring
+    owners = [3, 1]                                   # state slots of the two sequences (ring owners)
+    ik_ring = torch.zeros(4 * ring, ID, dtype=torch.bfloat16, device=DEV)
+    ig_ring = torch.zeros(4 * ring, ID, device=DEV)
+    bt = torch.arange(pages, dtype=torch.int32, device=DEV).view(nseq, pages // nseq)
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    ln_w = 1 + 0.1 * torch.randn(ID, generator=g, device=DEV)
+    ln_b = 0.1 * torch.randn(ID, generator=g, device=DEV)
+    ape = torch.randn(kpool, ID, generator=g, device=DEV)
+    for runs in launches:
+        rows, pos, seq, slots, desc = [], [], [], [], []
+        for b, (s, p0, n, garbage) in enumerate(runs):
+            desc.append((len(rows), n, 0, 0, owners[s]))
+            for i in range(n):
+                p = p0 + i
+                rows.append(garbage[i] if garbage is not None and garbage[i] is not None else streams[s][p])
+                pos.append(p)
+                seq.append(b)
+                slots.append(int(bt[s, p // bs]) * bs + p % bs)
+        iproj = torch.stack(rows)
+        btl = torch.stack([bt[s] for s, _, _, _ in runs])
+        sd = torch.tensor(desc, dtype=torch.int32, device=DEV).t().contiguous()
+        C.dsa_update(iproj, ln_w, ln_b, ape, ik_rows, ig_rows, ik_ring, ig_ring, pool_cache, pool_scale,
+                     torch.tensor(slots, dtype=torch.int32, device=DEV), torch.tensor(pos, dtype=torch.int32,
+                                                                                      device=DEV),
+                     btl, torch.tensor(seq, dtype=torch.int32, device=DEV), sd, bs, IH, kpool, 1e-6)
+    torch.cuda.synchronize()
+    return pool_cache, pool_scale, slots_per_seq
+
+
+def test_dsa_pools_tail_ring_any_launch_split():
+    """Pooled index keys keep no per-token raw keys: a pool's tokens come from the launch's own rows or from the
+    sequence's tail ring.  The pools must be bit-identical whether the tokens arrive in one launch, in odd-sized
+    chunks (pools straddling launches), or in verify windows whose rejected rows carried other keys and were
+    rewritten by the next window -- with two sequences (different ring owners) interleaved in one launch."""
+    IH, ID = 4, 128
+    g = torch.Generator(device=DEV).manual_seed(1)
+    N = 150
+    streams = [torch.randn(N, ID + IH + ID, generator=g, device=DEV) for _ in range(2)]
+    whole = [[(0, 0, N, None), (1, 0, N, None)]]
+    chunks = []
+    p = 0
+    for n in (37, 1, 5, 64, 43):
+        chunks.append([(0, p, n, None), (1, p, n, None)])
+        p += n
+    # verify windows of 8 rows after a 50-token prefill: window w keeps a rows; rejected rows carry junk keys
+    windows = [[(0, 0, 50, None), (1, 0, 50, None)]]
+    p = 50
+    for keep in (3, 8, 1, 5, 8, 2, 7, 4, 8, 6, 8, 8, 3):
+        junk = [None] * keep + [torch.randn(ID + IH + ID, generator=g, device=DEV) for _ in range(8 - keep)]
+        windows.append([(0, p, 8, junk), (1, p, 8, junk)])
+        p += keep
+    final = p
+    windows.append([(0, p, N - p, None), (1, p, N - p, None)])
+    ref, ref_s, sps = _pools_by_launches(whole, streams)
+    for launches in (chunks, windows):
+        got, got_s, _ = _pools_by_launches(launches, streams)
+        for s in range(2):
+            base = s * sps // 4
+            npools = N // 4
+            assert torch.equal(got[base:base + npools], ref[base:base + npools]), (s, final)
+            assert torch.equal(got_s[base:base + npools], ref_s[base:base + npools])
