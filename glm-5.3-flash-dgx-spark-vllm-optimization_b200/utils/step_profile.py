@@ -2,6 +2,8 @@
 
   python -m glm53.utils.step_profile forward --rows 8        kernel breakdown of one decode window forward
   python -m glm53.utils.step_profile prefill --chunk 4096    kernel breakdown of one prefill chunk (context = chunk)
+  torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m glm53.utils.step_profile prefill --chunk 8192
+                                                              the same on rank 0 of a tensor-parallel group
   python -m glm53.utils.step_profile engine --k 7            wall time of each phase of LLMEngine.step()
 
 ``forward`` / ``prefill`` aggregate device time per kernel name with torch.profiler (CUDA activity only).
@@ -39,16 +41,26 @@ def _kernel_table(fn, reps: int = 1, top: int = 30):
 
 
 def _runtime(cfg, rows: int, ctx: int):
+    """Runtime + sequence on this process's GPU; under torchrun (WORLD_SIZE > 1) the weights are this rank's
+    tensor-parallel shard and the runtime reduces over NCCL (and the fused peer exchange)."""
     from ..models import weights as W
     from ..models.runtime import Runtime, RuntimeConfig
     from ..models.session import Sequence
-    dev = torch.device("cuda", 0)
-    w = W.prepare(W.RandomSource(cfg, seed=0, device=dev), cfg, device=dev)
+    from ..parallel import dist as D
+    rank, local, world = D.init()
+    comm = D.NcclComm() if world > 1 else None
+    dev = torch.device("cuda", local)
+    w = W.prepare(W.RandomSource(cfg, seed=0, device=dev), cfg, rank=rank, world=world, device=dev)
     bs = 64
     blocks = (ctx + rows * 8 + bs - 1) // bs + 2
     rc = RuntimeConfig(max_rows=max(rows, 16), max_seqs=1, kv_slots=blocks * bs, block_size=bs, max_blocks=blocks)
-    rt = Runtime(w, rc)
+    rt = Runtime(w, rc, comm=comm)
     return rt, Sequence(rt)
+
+
+def _rank0() -> bool:
+    import torch.distributed as dist
+    return not dist.is_initialized() or dist.get_rank() == 0
 
 
 def cmd_forward(a):
@@ -101,10 +113,16 @@ def cmd_prefill(a):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
-    print(json.dumps({"mode": "prefill", "chunk": CH, "kernel_sum_ms": total / 1e3, "timed_chunk_ms": ms,
-                      "tok_s": CH / (ms / 1e3)}))
-    for n, c, t in rows:
-        print(f"{t / 1e3:10.2f} ms {c:6d}x  {n}")
+    import torch.distributed as dist
+    tp = dist.get_world_size() if dist.is_initialized() else 1
+    if _rank0():
+        print(json.dumps({"mode": "prefill", "tp": tp, "chunk": CH, "kernel_sum_ms": total / 1e3,
+                          "timed_chunk_ms": ms, "tok_s": CH / (ms / 1e3)}))
+        for n, c, t in rows:
+            print(f"{t / 1e3:10.2f} ms {c:6d}x  {n}")
+    if tp > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def cmd_engine(a):
