@@ -709,6 +709,37 @@ void kda_recurrent(const Tensor& proj, const Tensor& seq, const Tensor& f, const
   check(g53_kda_recurrent(a, stream()), "kda_recurrent");
 }
 
+// fused decode window (rows per sequence <= 16, Dh 128, 4 taps): f_b / g_b from the f_a / g_a columns of proj,
+// conv (qkv and f stored for the commit replay), recurrence S_in -> S_out, gated norm into out
+void kda_decode(const Tensor& proj, const Tensor& seq, int64_t max_rows, const Tensor& fb_w, const Tensor& fb_s,
+                const Tensor& gb_w, const Tensor& gb_s, const Tensor& conv_w, const Tensor& conv_pool,
+                const Tensor& qkv, const Tensor& f_store, const Tensor& a_log, const Tensor& dt_bias,
+                const Tensor& o_norm, const Tensor& S_pool, const Tensor& out, int64_t H, int64_t Dh, int64_t fa_off,
+                int64_t b_off, double lower, double eps) {
+  KdaArgs a = kda_args(proj, seq, max_rows, H, Dh, conv_w.size(1));
+  TORCH_CHECK(fb_w.is_contiguous() && gb_w.is_contiguous() && fb_w.size(0) == H * Dh && fb_w.size(1) == Dh &&
+              gb_w.sizes() == fb_w.sizes(), "kda_decode: f_b / g_b must be [H*Dh, Dh] contiguous");
+  TORCH_CHECK(qkv.stride(0) == 3 * H * Dh && f_store.stride(0) == H * Dh && out.stride(0) == H * Dh,
+              "kda_decode: qkv / f / out rows must be dense");
+  a.fb_w = P<const uint8_t>(fb_w); a.fb_s = P<const float>(fb_s);
+  a.gb_w = P<const uint8_t>(gb_w); a.gb_s = P<const float>(gb_s);
+  a.conv_w = P<const float>(conv_w);
+  a.conv_pool = P<__nv_bfloat16>(conv_pool);
+  a.qkv = P<__nv_bfloat16>(qkv);
+  a.f_store = P<__nv_bfloat16>(f_store);
+  a.a_log = P<const float>(a_log);
+  a.dt_bias = P<const float>(dt_bias);
+  a.o_norm = P<const __nv_bfloat16>(o_norm);
+  a.S_pool = P<float>(S_pool);
+  a.out = P<__nv_bfloat16>(out);
+  a.fa_off = (int)fa_off;
+  a.b_off = (int)b_off;
+  a.lower = (float)lower;
+  a.eps = (float)eps;
+  TORCH_CHECK(g53_kda_decode_ok(a), "kda_decode: unsupported shape or alignment");
+  check(g53_kda_decode(a, stream()), "kda_decode");
+}
+
 void kda_chunk(const Tensor& proj, const Tensor& seq, const Tensor& f, const Tensor& qkv, const Tensor& a_log,
                const Tensor& dt_bias, const Tensor& S_pool, const Tensor& o_raw, int64_t H, int64_t Dh, int64_t b_off,
                double lower, const Tensor& scratch) {
@@ -1006,6 +1037,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("kv_cache"), py::arg("kv_scale"), py::arg("kpe_cache"), py::arg("sel"), py::arg("sel_count"),
         py::arg("rope"), py::arg("sm_scale"), py::arg("splits"), py::arg("part_o"), py::arg("part_ml"),
         py::arg("o_lat"), py::arg("tensor_cores") = -1);
+  m.def("kda_decode", &kda_decode);
   m.def("dsa_update", &dsa_update);
   m.def("dsa_ring_positions", []() { return (int64_t)kDsaRing; });
   m.def("dsa_select", &dsa_select);

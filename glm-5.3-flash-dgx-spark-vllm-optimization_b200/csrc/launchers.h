@@ -250,11 +250,19 @@ struct KdaArgs {
   int R, H, Dh, taps, b_off;
   float lower, eps;
   float* scr; int scr_slots;                 // chunked prefill: per-(chunk slot, head) records (kda_chunk.cu)
+  // fused decode step (kda_decode.cu): the f_b / g_b projections of the f_a / g_a columns computed in the kernel
+  const uint8_t* fb_w; const float* fb_s;    // [H*Dh, Dh] e4m3, [H*Dh] row scales
+  const uint8_t* gb_w; const float* gb_s;
+  int fa_off;                                // column of f_a in proj (g_a follows at fa_off + Dh)
+  __nv_bfloat16* f_store;                    // [R, H*Dh] decay logits kept for the commit replay
 };
 cudaError_t g53_kda_conv(const KdaArgs& a, cudaStream_t st);          // qkv = silu(conv(window ++ proj rows))
 cudaError_t g53_kda_recurrent(const KdaArgs& a, cudaStream_t st);     // per sequence: S_in -> S_out, o_raw
 cudaError_t g53_kda_gated_norm(const KdaArgs& a, cudaStream_t st);    // out = rmsnorm(o_raw) * w * sigmoid(gate)
 cudaError_t g53_kda_conv_commit(const KdaArgs& a, cudaStream_t st);   // window <- last taps-1 of window ++ nrows rows
+// one kernel for a decode window: f_b, g_b, conv, recurrence and gated norm (kda_decode.cu)
+bool g53_kda_decode_ok(const KdaArgs& a);
+cudaError_t g53_kda_decode(const KdaArgs& a, cudaStream_t st);
 // chunked (64-token) form of g53_kda_recurrent for prefill: same inputs/outputs, per-sequence rows in chunks;
 // needs a.scr with g53_kda_chunk_scratch_floats(max_rows, max_seqs, H, Dh) floats (scr_slots = rows/64 + seqs + 1)
 cudaError_t g53_kda_chunk(const KdaArgs& a, cudaStream_t st);

@@ -96,6 +96,9 @@ class Runtime:
         # routed experts (ALU-bound trellis decode vs a bandwidth-bound GEMV), the KDA output-gate projection beside
         # the convolution and recurrence; forked and joined with events, so CUDA-graph capture records both branches
         self.overlap = dev.type == "cuda" and os.environ.get("GLM53_OVERLAP", "1") == "1"
+        # decode windows run the KDA block tail (f_b, g_b, conv, recurrence, gated norm) as one kernel
+        # (GLM53_KDA_FUSED=0: the five-kernel path)
+        self.kda_fused = os.environ.get("GLM53_KDA_FUSED", "1") == "1"
         if self.overlap:
             self.side = torch.cuda.Stream(device=dev)
             self.ev_fork, self.ev_join = torch.cuda.Event(), torch.cuda.Event()
@@ -422,6 +425,14 @@ class Runtime:
             proj, fb, qkv = self.kproj[:R], self.kf[:R], self.kqkv[:R]
         C3 = 3 * H * Dh
         K.linear8(self.normed[:R], k.in_proj.w, k.in_proj.s, proj, proj="kda_in_proj")
+        if self._keep_window and self.kda_fused and Dh == 128 and c.conv == 4 and 1 <= b.max_rows_per_seq <= 16:
+            # decode window: f_b, g_b, conv, recurrence and gated norm in one kernel (conv outputs and decay
+            # logits stored for the commit replay)
+            Kc.kda_decode(proj, b.kda_seq[:, :b.B], b.max_rows_per_seq, k.f_b.w, k.f_b.s, k.g_b.w, k.g_b.s, k.conv,
+                          self.conv_pool[li], qkv, fb, k.a_log, k.dt_bias, k.o_norm, self.S_pool[li], self.kout[:R],
+                          H, Dh, C3, C3 + 2 * Dh, c.lower, c.eps)
+            self._final_linear(self.kout[:R], k.o_proj, R)
+            return
         K.linear8(proj[:, C3:C3 + Dh], k.f_b.w, k.f_b.s, fb)
         side = getattr(self, "overlap", False) and R <= K.GEMV_MAX_M
         if side:        # output gate (read only by the gated norm) beside the convolution and recurrence

@@ -99,3 +99,35 @@ def test_kda_multi_sequence_and_replay():
     C.kda_recurrent(proj[:3], torch.tensor([[0], [3], [0], [4], [0]], dtype=torch.int32, device=DEV), f[:3],
                     qkv[:3], a_log, dt_bias, S_c, o3, H, Dh, b_off, -5.0)
     torch.testing.assert_close(S_a[4], S_c[4], atol=1e-6, rtol=1e-6)
+
+
+def test_kda_decode_fused_matches_five_kernels():
+    """The fused decode-window kernel (f_b, g_b, conv, recurrence, gated norm in one launch) against the five-kernel
+    path on a model whose KDA heads have Dh = 128: every window's logits agree closely, and windows that keep fewer
+    rows than they verified (commit replay from the stored conv outputs and decay logits) keep agreeing."""
+    import dataclasses
+    from glm53.config import tiny_config
+    from glm53.models import weights as W
+    from glm53.models.runtime import Runtime, RuntimeConfig
+    from glm53.models.session import Sequence
+    cfg = dataclasses.replace(tiny_config(), lin_heads=2, lin_dim=128)
+    dev = torch.device("cuda", 0)
+    w = W.prepare(W.RandomSource(cfg, seed=0, device=dev), cfg, device=dev)
+    g = torch.Generator().manual_seed(5)
+    prompt = torch.randint(16, cfg.vocab, (150,), generator=g).tolist()
+    windows = [(torch.randint(16, cfg.vocab, (n,), generator=g).tolist(), keep)
+               for n, keep in ((8, 3), (8, 8), (5, 1), (1, 1), (8, 6), (16, 9))]
+    outs = []
+    for fused in (False, True):
+        rt = Runtime(w, RuntimeConfig(max_rows=64, max_seqs=1, kv_slots=64 * 8, block_size=64, max_blocks=8))
+        rt.kda_fused = fused
+        seq = Sequence(rt)
+        lg = [seq.prefill(prompt, chunk=64).float().clone()]
+        for toks, keep in windows:
+            lg.append(seq.verify(toks).float().clone())
+            seq.commit(keep)
+        outs.append(lg)
+    for a, b in zip(*outs):
+        cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
+        assert cos > 0.9999, cos
+        assert (a - b).abs().max().item() < 5e-2 * max(1.0, a.abs().max().item())
