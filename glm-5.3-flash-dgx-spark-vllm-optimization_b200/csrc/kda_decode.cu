@@ -9,7 +9,8 @@
 //      rounded to bf16 as the GEMVs round them; f is also stored for the commit replay;
 //   3. causal depthwise conv (4 taps, SiLU) of the head's 384 q/k/v channels, threads 0..383 one channel each,
 //      outputs rounded to bf16 and stored (the commit replay re-reads them);
-//   4. per row: l2-normalised q, k, the decay exponent and beta (one warp per row);
+//   4. per row: l2-normalised q, k, the decay factor exp(g) (once per channel, not per state row) and beta
+//      (one warp per row);
 //   5. the delta-rule recurrence over the rows with thread (v, kq) holding S[v][kq + 4j], exactly the arithmetic
 //      of kda_recurrent_kernel (kda.cu), so a commit that replays fewer rows from the stored conv outputs and
 //      decay logits reproduces the state;
@@ -39,7 +40,7 @@ struct Smem {
   float q[kMaxRows][DH];          // conv outputs (bf16 values), then normalised
   float k[kMaxRows][DH];
   float v[kMaxRows][DH];
-  float g[kMaxRows][DH];          // decay exponents
+  float g[kMaxRows][DH];          // decay factors exp(g), computed once per channel
   float o[kMaxRows][DH];          // recurrence outputs
   float beta[kMaxRows];
 };
@@ -120,25 +121,27 @@ __global__ void __launch_bounds__(kThreads, 1) kda_decode_kernel(KdaArgs a) {
   // 3. causal conv of the head's q / k / v channels (window rows oldest first, then the window's rows)
   if (part < 3) {
     const __nv_bfloat16* win = a.conv_pool + (int64_t)a.conv_slot[b] * 3 * C3 + cch;
-    float hist[4];
+    // every input of the channel first (window, then the rows: all loads in flight together), then the taps
+    float xs[3 + kMaxRows];
 #pragma unroll
-    for (int i = 0; i < 3; ++i) hist[i] = bf2f(win[(int64_t)i * C3]);
+    for (int i = 0; i < 3; ++i) xs[i] = bf2f(win[(int64_t)i * C3]);
+#pragma unroll
+    for (int t = 0; t < kMaxRows; ++t) xs[3 + t] = t < n ? bf2f(a.proj[(int64_t)(base + t) * a.ldp + cch]) : 0.f;
     float (*dst)[DH] = part == 0 ? sm.q : (part == 1 ? sm.k : sm.v);
-    for (int t = 0; t < n; ++t) {
-      hist[3] = bf2f(a.proj[(int64_t)(base + t) * a.ldp + cch]);
+#pragma unroll
+    for (int t = 0; t < kMaxRows; ++t) {
+      if (t >= n) break;
       float s = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) s += w[i] * hist[i];
+      for (int i = 0; i < 4; ++i) s += w[i] * xs[t + i];
       const __nv_bfloat16 o = f2bf(siluf_(s));
       a.qkv[(int64_t)(base + t) * C3 + cch] = o;
       dst[t][cc] = __bfloat162float(o);
-#pragma unroll
-      for (int i = 0; i < 3; ++i) hist[i] = hist[i + 1];
     }
   }
   __syncthreads();
 
-  // 4. normalised q, k, decay exponent and beta of every row (one warp per row)
+  // 4. normalised q, k, decay factors and beta of every row (one warp per row)
   const float ea = __expf(a.a_log[h]);
   for (int rr = warp; rr < n; rr += kThreads / 32) {
     constexpr int PL = DH / 32;
@@ -151,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_decode_kernel(KdaArgs a) {
       kv[i] = sm.k[rr][c];
       qq += qv[i] * qv[i];
       kk += kv[i] * kv[i];
-      sm.g[rr][c] = a.lower * sigmoidf_(ea * (sm.f[rr][c] + a.dt_bias[h * DH + c]));
+      sm.g[rr][c] = __expf(a.lower * sigmoidf_(ea * (sm.f[rr][c] + a.dt_bias[h * DH + c])));
     }
     qq = warp_sum(qq);
     kk = warp_sum(kk);
@@ -178,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_decode_kernel(KdaArgs a) {
       float dot = 0.f;
 #pragma unroll
       for (int j = 0; j < KP; ++j) {
-        S[j] *= __expf(sm.g[rr][kq + 4 * j]);
+        S[j] *= sm.g[rr][kq + 4 * j];
         dot += S[j] * sm.k[rr][kq + 4 * j];
       }
       dot = group_sum<4>(dot);

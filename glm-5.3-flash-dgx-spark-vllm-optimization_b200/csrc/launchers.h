@@ -215,6 +215,9 @@ struct HcArgs {
   int nb;                     // column blocks of `part` (set by the launcher)
 };
 cudaError_t g53_hc_post_pre(const HcArgs& a, cudaStream_t st);   // (optional post) then pre
+// decode windows (R <= 16, with pre): the whole post + pre in one cluster kernel (mhc_decode.cu)
+bool g53_hc_decode_ok(const HcArgs& a);
+cudaError_t g53_hc_decode(const HcArgs& a, cudaStream_t st);
 // tensor-core partial pass only (post + mixing dots + sums of squares into part [R, D / 512, 32])
 cudaError_t g53_hc_partial_tc(const HcArgs& a, cudaStream_t st);
 cudaError_t g53_embed(const int* ids, const __nv_bfloat16* table, int R, int D, int S, __nv_bfloat16* X,

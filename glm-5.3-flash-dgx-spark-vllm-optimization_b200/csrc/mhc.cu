@@ -10,6 +10,7 @@
 //            normed = bf16(rmsnorm(collapsed) * w)
 // Reference counterparts: code/fork/kernels/mhc_post_prenorm.cu:34 (prefill post+prenorm) and
 // code/fork/kernels/smallops.cu:134 (decode mHC); math as code/fork/docs/ref/tf_glue.py:123-175.
+#include <cstdlib>
 #include "common.cuh"
 #include "launchers.h"
 
@@ -275,9 +276,20 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* x, in
 
 using namespace g53;
 
+// decode windows take the one-kernel cluster form (mhc_decode.cu) unless GLM53_HC_FUSED=0
+static bool hc_fused_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("GLM53_HC_FUSED");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 cudaError_t g53_hc_post_pre(const HcArgs& args, cudaStream_t st) {
   HcArgs a = args;
   if (a.D % kDB || a.D > 8192 || a.D % 8 || (a.S != 2 && a.S != 4)) return cudaErrorInvalidValue;
+  if (hc_fused_enabled() && g53_hc_decode_ok(a)) return g53_hc_decode(a, st);
   // prefill-sized launches: post + mixing dots on the tensor cores (column blocks of 512), then the same finish
   if (a.use_tc && a.R >= 256 && a.S == 4 && a.fn && !a.gath && a.D % 512 == 0) {
     a.nb = a.D / 512;

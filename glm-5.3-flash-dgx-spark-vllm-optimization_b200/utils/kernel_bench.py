@@ -237,6 +237,28 @@ def bench_kda(args, T: Timer):
             ms = T(lambda: K.C().kda_recurrent(proj, seq, f, qkv, a_log, dt, S, o, H, Dh, 3 * HD + 2 * Dh, -5.0))
         emit({"case": "kda_chunk" if Tn > 32 else "kda_recurrent", "rows": Tn, "heads": H, "ms": ms,
               "tokens_per_s": Tn / ms * 1e3})
+        if Tn <= 16:
+            # the decode window's whole KDA block tail: fused kernel against the five-kernel sequence
+            from glm53.models.weights import quantize_fp8_rows
+            fb = quantize_fp8_rows(torch.randn(HD, Dh, device="cuda") / Dh ** 0.5)
+            gb = quantize_fp8_rows(torch.randn(HD, Dh, device="cuda") / Dh ** 0.5)
+            conv_w = torch.randn(3 * HD, 4, device="cuda") * 0.3
+            conv_pool = (torch.randn(2, 3, 3 * HD, device="cuda") * 0.5).to(torch.bfloat16)
+            o_norm = torch.ones(Dh, device="cuda", dtype=torch.bfloat16)
+            out = torch.empty(Tn, HD, device="cuda", dtype=torch.bfloat16)
+            gate = torch.empty(Tn, HD, device="cuda", dtype=torch.bfloat16)
+            C3 = 3 * HD
+            ms_f = T(lambda: K.C().kda_decode(proj, seq, Tn, fb.w, fb.s, gb.w, gb.s, conv_w, conv_pool, qkv, f, a_log,
+                                              dt, o_norm, S, out, H, Dh, C3, C3 + 2 * Dh, -5.0, 1e-6))
+
+            def five():
+                K.linear8(proj[:, C3:C3 + Dh], fb.w, fb.s, f)
+                K.linear8(proj[:, C3 + Dh:C3 + 2 * Dh], gb.w, gb.s, gate)
+                K.C().kda_conv(proj, seq, Tn, conv_w, conv_pool, qkv, H, Dh)
+                K.C().kda_recurrent(proj, seq, f, qkv, a_log, dt, S, o, H, Dh, C3 + 2 * Dh, -5.0)
+                K.C().kda_gated_norm(o, gate, o_norm, out, H, Dh, 1e-6)
+            ms_5 = T(five)
+            emit({"case": "kda_decode_window", "rows": Tn, "heads": H, "ms_fused": ms_f, "ms_five_kernels": ms_5})
 
 
 def bench_mla(args, T: Timer):

@@ -292,6 +292,60 @@ def test_hc_post_pre_tensor_cores(C, rows, with_post):
     torch.testing.assert_close(pt, outs[0][2], atol=1e-5, rtol=1e-5)
 
 
+@pytest.mark.parametrize("rows", [1, 8, 16])
+@pytest.mark.parametrize("with_post", [True, False])
+def test_hc_post_pre_decode_cluster(C, rows, with_post):
+    """Decode-sized mHC (4 streams, D = 4096) in one cluster kernel (8 CTAs per row, the row reductions through
+    distributed shared memory) against the fp32 reference, and the post arithmetic bit for bit against the
+    two-kernel path (prefill-sized launch of the same rows padded to 300)."""
+    from types import SimpleNamespace
+    from glm53.models import reference as R
+    S, D = 4, 4096
+    g = torch.Generator().manual_seed(11 + rows)
+    X = (torch.randn(rows, S, D, generator=g)).to(torch.bfloat16)
+    branch = torch.randn(rows, D, generator=g)
+    fn = (torch.randn(2 * S + S * S, S * D, generator=g) * 0.02).to(torch.bfloat16)
+    base = torch.randn(2 * S + S * S, generator=g) * 0.1
+    scale = torch.tensor([1.0, 0.8, 1.2])
+    norm_w = (1 + 0.1 * torch.randn(D, generator=g)).to(torch.bfloat16)
+    post0 = torch.rand(rows, S, generator=g) * 2
+    comb0 = torch.softmax(torch.randn(rows, S, S, generator=g), -1)
+    cfg = SimpleNamespace(streams=S, eps=1e-6, hc_eps=1e-6, hc_iters=20)
+    Xn = R.hc_post(X.float(), branch, post0, comb0) if with_post else X.float()
+    normed_ref, post_ref, comb_ref = R.hc_pre(Xn, SimpleNamespace(fn=fn, base=base, scale=scale), norm_w.float(),
+                                              cfg)
+    Xd = X.to(DEV).contiguous()
+    normed = torch.empty(rows, D, dtype=torch.bfloat16, device=DEV)
+    post = torch.empty(rows, S, device=DEV)
+    comb = torch.empty(rows, S, S, device=DEV)
+    part = torch.empty(rows, D // 64, 32, device=DEV)
+    C.hc_post_pre(Xd, branch.to(DEV) if with_post else None, post0.to(DEV) if with_post else None,
+                  comb0.to(DEV) if with_post else None, fn.to(DEV), base.to(DEV), scale.to(DEV), norm_w.to(DEV),
+                  normed, post, comb, part, cfg.eps, cfg.hc_eps, cfg.hc_iters, 0)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(Xd.float().cpu(), Xn, atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(post.cpu(), post_ref, atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(comb.cpu(), comb_ref, atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(normed.float().cpu(), normed_ref, atol=3e-2, rtol=2e-2)
+    # the same rows through the two-kernel path (a 300-row launch): identical post, close pre outputs
+    pad = 300
+    Xp = torch.zeros(pad, S, D, dtype=torch.bfloat16)
+    Xp[:rows] = X
+    bp, p0, c0 = torch.zeros(pad, D), torch.zeros(pad, S), torch.zeros(pad, S, S)
+    bp[:rows], p0[:rows], c0[:rows] = branch, post0, comb0
+    Xpd = Xp.to(DEV)
+    n2 = torch.empty(pad, D, dtype=torch.bfloat16, device=DEV)
+    po2, co2 = torch.empty(pad, S, device=DEV), torch.empty(pad, S, S, device=DEV)
+    pa2 = torch.empty(pad, D // 64, 32, device=DEV)
+    C.hc_post_pre(Xpd, bp.to(DEV) if with_post else None, p0.to(DEV) if with_post else None,
+                  c0.to(DEV) if with_post else None, fn.to(DEV), base.to(DEV), scale.to(DEV), norm_w.to(DEV),
+                  n2, po2, co2, pa2, cfg.eps, cfg.hc_eps, cfg.hc_iters, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(Xpd[:rows].cpu(), Xd.cpu())
+    torch.testing.assert_close(po2[:rows], post, atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(co2[:rows], comb, atol=1e-5, rtol=1e-5)
+
+
 @pytest.mark.parametrize("M", [1, 8, 12])
 @pytest.mark.parametrize("N,K", [(24896, 4096), (4100, 8192), (4096, 16384)])
 def test_gemv_fp8_stream_k(C, M, N, K):
