@@ -201,6 +201,26 @@ __device__ __forceinline__ void tile_mma(float (&c)[4], const uint32_t (&x)[8], 
   mma_f16_16816(c, a1, b.z, b.w);
 }
 
+// the same tile with the masked products written straight into the two A fragments in operand order
+// (a0 = {x0, x4, x1, x5}, a1 = {x2, x6, x3, x7}), so no value has to be moved into an operand register
+__device__ __forceinline__ void trellis_tile_mma(float (&c)[4], uint32_t cur, uint32_t prev, const uint4& b) {
+  constexpr uint32_t C = 0xCBAC1FEDu, Cn = 0u - (C << 16);
+  const uint32_t v = __funnelshift_r(cur, prev, 20);
+  const uint32_t y = __umulhi(cur, 1u << 28);
+  const uint32_t s3 = __umulhi(cur, 1u << 16);
+  uint32_t a0[4], a1[4];
+  a0[0] = ((__byte_perm(v, 0u, 0x4421) * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;                 // x0
+  a0[1] = ((__byte_perm(y, 0u, 0x4421) * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;                 // x4
+  a0[2] = (((__funnelshift_r(cur, prev, 24) & 0xffffu) * C) & 0x8FFF8FFFu) ^ 0x3B603B60u; // x1
+  a0[3] = ((__byte_perm(cur, 0u, 0x4421) * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;               // x5
+  mma_f16_16816(c, a0, b.x, b.y);
+  a1[0] = (((v & 0xffffu) * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;                              // x2
+  a1[1] = (((y & 0xffffu) * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;                              // x6
+  a1[2] = ((s3 * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;                                          // x3
+  a1[3] = ((cur * C + s3 * Cn) & 0x8FFF8FFFu) ^ 0x3B603B60u;                               // x7
+  mma_f16_16816(c, a1, b.z, b.w);
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // rot_in: one warp per (sorted pair, 128-block); gate and up rotated inputs in f16
 // ---------------------------------------------------------------------------------------------------------------
@@ -320,11 +340,8 @@ __device__ __forceinline__ void gate_up_group(const Exl3Args& a, int u, float (*
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint4 bg = bgp[i], bu = bup[i];
-        uint32_t x[8];
-        trellis_x8(pg[i], __shfl_sync(0xffffffffu, pg[i], src), x);
-        tile_mma(cg, x, bg);
-        trellis_x8(pu[i], __shfl_sync(0xffffffffu, pu[i], src), x);
-        tile_mma(cu, x, bu);
+        trellis_tile_mma(cg, pg[i], __shfl_sync(0xffffffffu, pg[i], src), bg);
+        trellis_tile_mma(cu, pu[i], __shfl_sync(0xffffffffu, pu[i], src), bu);
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i) { pg[i] = ng[i]; pu[i] = nu[i]; }
@@ -439,9 +456,7 @@ __device__ __forceinline__ void down_group(const Exl3Args& a, int u, float (*zd)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint4 b = bp[i];
-        uint32_t x[8];
-        trellis_x8(pd[i], __shfl_sync(0xffffffffu, pd[i], src), x);
-        tile_mma(cd, x, b);
+        trellis_tile_mma(cd, pd[i], __shfl_sync(0xffffffffu, pd[i], src), b);
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i) pd[i] = nd[i];
