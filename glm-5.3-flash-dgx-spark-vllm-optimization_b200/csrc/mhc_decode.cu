@@ -216,7 +216,6 @@ bool g53_hc_decode_ok(const HcArgs& a) {
 cudaError_t g53_hc_decode(const HcArgs& a, cudaStream_t st) {
   if (!g53_hc_decode_ok(a)) return cudaErrorInvalidValue;
   dim3 grid(g53::hd::kCl, a.R);
-  if (a.S == 4) g53::hd::hc_decode_kernel<4><<<grid, g53::hd::kT, 0, st>>>(a);
-  else g53::hd::hc_decode_kernel<2><<<grid, g53::hd::kT, 0, st>>>(a);
-  return cudaGetLastError();
+  if (a.S == 4) return g53_launch_pdl(g53::hd::hc_decode_kernel<4>, grid, dim3(g53::hd::kT), 0, st, 1, a);
+  return g53_launch_pdl(g53::hd::hc_decode_kernel<2>, grid, dim3(g53::hd::kT), 0, st, 1, a);
 }

@@ -64,6 +64,8 @@ __global__ void __launch_bounds__(1024) moe_route_kernel(RouteArgs a) {
   __shared__ int cnt[kMaxE];
   __shared__ int start[kMaxE + 1];
   __shared__ int pe[kMaxPairs];
+  pdl_wait();                          // the router logits come from the previous kernel
+  pdl_trigger();
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
   const int P = a.R * a.top_k;
   for (int e = tid; e < a.E; e += blockDim.x) cnt[e] = 0;
@@ -225,6 +227,8 @@ __device__ __forceinline__ void trellis_tile_mma(float (&c)[4], uint32_t cur, ui
 // rot_in: one warp per (sorted pair, 128-block); gate and up rotated inputs in f16
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) exl3_rot_in_kernel(Exl3Args a) {
+  pdl_wait();                          // pairs from the routing kernel
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const int blk = blockIdx.y * 4 + (threadIdx.x >> 5);
   if (blk * 128 >= a.K) return;
@@ -401,6 +405,8 @@ __global__ void __launch_bounds__(256, 4) exl3_gate_up_kernel(Exl3Args a) {
   __shared__ float zg[8][132];
   __shared__ float zu[8][132];
   if (a.pf.count && threadIdx.x == 0) l2_prefetch_share(a.pf);
+  pdl_wait();                          // rotated inputs and the group table from the previous kernels
+  pdl_trigger();
   const int ng = min(a.group_count[0], a.max_groups);
   for (int u = blockIdx.y; u < ng; u += gridDim.y) gate_up_group<KSPL>(a, u, zg, zu);
 }
@@ -489,6 +495,8 @@ __device__ __forceinline__ void down_group(const Exl3Args& a, int u, float (*zd)
 template <int KSPL>
 __global__ void __launch_bounds__(256) exl3_down_kernel(Exl3Args a) {
   __shared__ float zd[8][132];
+  pdl_wait();                          // the gate/up kernel's activations
+  pdl_trigger();
   const int ng = min(a.group_count[0], a.max_groups);
   for (int u = blockIdx.y; u < ng; u += gridDim.y) down_group<KSPL>(a, u, zd);
   if (a.out_ptrs) ep_count_in(a);                   // expert parallelism: every CTA counts towards the release
@@ -496,6 +504,7 @@ __global__ void __launch_bounds__(256) exl3_down_kernel(Exl3Args a) {
 
 __global__ void moe_combine_kernel(const float* yd, const int* pair_of, int R, int top_k, int D, float* out,
                                    int accumulate) {
+  pdl_wait();                          // the down kernel's expert outputs
   pdl_trigger();                       // dependents (the next projection) may start prefetching
   const int r = blockIdx.y;
   const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
@@ -540,39 +549,20 @@ using namespace g53;
 
 cudaError_t g53_moe_route(const RouteArgs& a, cudaStream_t st) {
   if (a.E > kMaxE || a.R * a.top_k > kMaxPairs || a.top_k > 32) return cudaErrorInvalidValue;
-  moe_route_kernel<<<1, 1024, 0, st>>>(a);
-  G53_CHECK_LAUNCH();
-  return cudaSuccess;
+  return g53_launch_pdl(moe_route_kernel, dim3(1), dim3(1024), 0, st, 1, a);
 }
 
 cudaError_t g53_exl3_rot_in(const Exl3Args& a, cudaStream_t st) {
   // device-side pair count (expert parallelism): a bounded grid strides over the rows that arrived
   dim3 grid(a.pair_count ? std::min(a.pairs, 1184) : a.pairs, (a.K / 128 + 3) / 4);
-  exl3_rot_in_kernel<<<grid, 128, 0, st>>>(a);
-  G53_CHECK_LAUNCH();
-  return cudaSuccess;
+  return g53_launch_pdl(exl3_rot_in_kernel, grid, dim3(128), 0, st, 1, a);
 }
 
 // K split over a cluster of KSPL CTAs (more, smaller CTAs: the grid of a decode window is a couple of waves)
 template <int KSPL>
 static cudaError_t launch_split(void (*kern)(Exl3Args), dim3 grid, const Exl3Args& a, cudaStream_t st) {
-  if (KSPL == 1) {
-    kern<<<grid, 256, 0, st>>>(a);
-    return cudaGetLastError();
-  }
-  cudaLaunchConfig_t cfg = {};
   grid.z = KSPL;
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(256);
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = KSPL;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, a);
+  return g53_launch_pdl(kern, grid, dim3(256), 0, st, KSPL, a);
 }
 
 static int pick_split(int kc) { return kc % 4 == 0 ? 4 : kc % 2 == 0 ? 2 : 1; }
@@ -601,9 +591,7 @@ cudaError_t g53_moe_combine(const float* yd, const int* pair_of, int R, int top_
                             int accumulate, cudaStream_t st) {
   if (D % 4) return cudaErrorInvalidValue;
   dim3 grid((D / 4 + 255) / 256, R);
-  moe_combine_kernel<<<grid, 256, 0, st>>>(yd, pair_of, R, top_k, D, out, accumulate);
-  G53_CHECK_LAUNCH();
-  return cudaSuccess;
+  return g53_launch_pdl(moe_combine_kernel, grid, dim3(256), 0, st, 1, yd, pair_of, R, top_k, D, out, accumulate);
 }
 
 cudaError_t g53_exl3_unpack(const int16_t* tr, int K, int N, __half* out, cudaStream_t st) {
