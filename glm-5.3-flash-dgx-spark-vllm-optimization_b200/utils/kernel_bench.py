@@ -431,7 +431,9 @@ def bench_hc(args, T: Timer):
         for tcores in ((1, 0) if R >= 256 else (0,)):
             ms = T(lambda: K.C().hc_post_pre(X, branch, post, comb, fn, base, hscale, norm_w, normed, post_o,
                                               comb_o, part, 1e-5, 1e-6, 20, tcores))
-            emit({"case": "hc_post_pre", "path": "tcgen05" if tcores else "cuda-core", "rows": R, "ms": ms,
+            fused = R <= 16 and os.environ.get("GLM53_HC_FUSED", "1") == "1"
+            path = "tcgen05" if tcores else ("cluster, one kernel" if fused else "cuda-core, two kernels")
+            emit({"case": "hc_post_pre", "path": path, "rows": R, "ms": ms,
                   "GBps": (R * S * D * 2 * 2 + R * D * 4 + NM * S * D * 2 + R * D * 2 * 2) / ms / 1e6})
 
 
