@@ -298,6 +298,31 @@ void l2_prefetch(const std::vector<Tensor>& ts, int64_t max_bytes) {
   check(g53_l2_prefetch(l2_ranges(ts, max_bytes), stream()), "l2_prefetch");
 }
 
+// grouped dynamic conv of the block drafter: x [T, H] bf16, delta [T, taps, H/gs] bf16, base [taps, H] bf16
+void dconv(const Tensor& x, const Tensor& delta, const Tensor& base, const Tensor& out, int64_t gs,
+           int64_t block_size) {
+  cuda_check(x, "x"); cuda_check(delta, "delta"); cuda_check(base, "base"); cuda_check(out, "out");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && delta.scalar_type() == at::kBFloat16 &&
+              base.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16, "dconv: bf16 tensors");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && x.stride(0) % 2 == 0, "dconv: x [T, H], unit inner stride");
+  const int64_t T = x.size(0), H = x.size(1);
+  TORCH_CHECK(base.dim() == 2 && base.size(1) == H && base.is_contiguous(), "dconv: base [taps, H] contiguous");
+  const int64_t taps = base.size(0);
+  TORCH_CHECK(gs >= 1 && H % gs == 0 && H % 2 == 0, "dconv: H must be even and a multiple of gs");
+  TORCH_CHECK(delta.is_contiguous() && delta.numel() == T * taps * (H / gs), "dconv: delta [T, taps, H/gs]");
+  TORCH_CHECK(out.is_contiguous() && out.size(0) == T && out.size(1) == H, "dconv: out [T, H] contiguous");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 4 == 0 && reinterpret_cast<uintptr_t>(base.data_ptr()) % 4 == 0 &&
+              reinterpret_cast<uintptr_t>(out.data_ptr()) % 4 == 0, "dconv: 4-byte aligned rows");
+  DconvArgs a{};
+  a.x = P<const __nv_bfloat16>(x); a.ldx = x.stride(0);
+  a.delta = P<const __nv_bfloat16>(delta);
+  a.base = P<const __nv_bfloat16>(base);
+  a.out = P<__nv_bfloat16>(out);
+  a.T = (int)T; a.H = (int)H; a.taps = (int)taps; a.gs = (int)gs; a.G = (int)(H / gs);
+  a.block_size = (int)block_size;
+  check(g53_dconv(a, stream()), "dconv");
+}
+
 // ------------------------------------------------------------------------------------------------- MoE
 void moe_route(const Tensor& logits, const Tensor& bias, int64_t top_k, double scale, bool norm,
                const Tensor& topk_ids, const Tensor& topk_w, const Tensor& group_count, const Tensor& group_expert,
@@ -1038,6 +1063,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rope"), py::arg("sm_scale"), py::arg("splits"), py::arg("part_o"), py::arg("part_ml"),
         py::arg("o_lat"), py::arg("tensor_cores") = -1);
   m.def("kda_decode", &kda_decode);
+  m.def("dconv", &dconv);
   m.def("dsa_update", &dsa_update);
   m.def("dsa_ring_positions", []() { return (int64_t)kDsaRing; });
   m.def("dsa_select", &dsa_select);

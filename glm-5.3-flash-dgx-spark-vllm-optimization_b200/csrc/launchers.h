@@ -35,6 +35,17 @@ struct GemvArgs {
 };
 cudaError_t g53_gemv_fp8(const GemvArgs& p, cudaStream_t st);
 cudaError_t g53_gemv_bf16(const GemvArgs& p, cudaStream_t st);
+// grouped dynamic conv of the block drafter (dconv.cu): out[t] = sum_k bf16(base[k] + delta[t][k][c / gs]) x[t - k]
+// within a draft block of block_size rows, with the eager op chain's bf16 roundings
+struct DconvArgs {
+  const __nv_bfloat16* x; int64_t ldx;       // [T, H] rows (inner stride 1)
+  const __nv_bfloat16* delta;                // [T, taps, G] per-row kernel deltas, G = H / gs (contiguous)
+  const __nv_bfloat16* base;                 // [taps, H] static kernel
+  __nv_bfloat16* out;                        // [T, H] contiguous
+  int T, H, taps, gs, G, block_size;
+};
+cudaError_t g53_dconv(const DconvArgs& a, cudaStream_t st);
+
 // L2 prefetch of up to four weight ranges (l2_prefetch.cu)
 struct L2Ranges {
   const char* ptr[4];

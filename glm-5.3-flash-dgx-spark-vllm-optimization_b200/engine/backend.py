@@ -116,8 +116,16 @@ class GPUBackend:
     @torch.no_grad()
     def draft(self, last_token: int, hidden: torch.Tensor, k: int):
         """K draft tokens (greedy) and their logits [k, V_local]."""
-        t = torch.tensor([last_token], dtype=torch.int32, device=hidden.device)
-        lg = self.drafter.forward(t, hidden, k)
+        self.drafter.stage(int(last_token), hidden)
+        if not self.cuda_graphs:
+            lg = self.drafter.run(k)
+        else:
+            # one CUDA graph per draft length: the drafter's dozen small launches replay without host overhead
+            g = self._graphs.get(("draft", k))
+            if g is None:
+                g = Graphed(lambda: self.drafter.run(k))
+                self._graphs[("draft", k)] = g
+            lg = g()
         return self.draft_sampler(lg).tolist(), lg
 
     @torch.no_grad()

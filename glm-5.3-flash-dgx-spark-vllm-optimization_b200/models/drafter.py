@@ -6,10 +6,16 @@ drafter is a 1-layer block model ("a random-init 1-layer bl
 
   x_i   = fc([h ; emb(t_i)]) + slot_i          i = 0..K-1,  t_0 = last committed token, t_i = MASK (i > 0),
                                                h = the target's final hidden state (stream mean) of that token
-  x    += o_proj(block_causal_attn(qkv(rmsnorm(x))))
-  x    += down(SwiGLU(gate_up(rmsnorm(x))))
+  x    += o_proj(block_causal_attn(qkv(dconv_a(rmsnorm(x)))))
+  x    += down(SwiGLU(gate_up(dconv_m(rmsnorm(x)))))
   logits_i = lm_head(rmsnorm(x_i))             the target's fp8 vocabulary-parallel head, shared
   draft_i  = argmax logits_i                   (row i proposes the token at position p + 1 + i)
+
+  dconv(y)_i = sum_k (base_k + delta_k(y_i)) * y_{i-k}   grouped dynamic causal conv inside the draft block
+                                               (taps 3, one kernel delta per group of 64 channels and row,
+                                               delta = a small fp8 projection of y; csrc/dconv.cu), the role of the
+                                               DFlash2 drafter's grouped conv around its attention and MLP
+                                               (code/fork/docs/DEC_SMALLOPS.md:12)
 
 Weights are fp8 e4m3 with per-row scales like the target's dense projections, random-initialised (seed-keyed), and
 replicated on every tensor-parallel rank; only the shared head is vocabulary-sharded.
@@ -36,6 +42,8 @@ class DrafterConfig:
     heads: int = 32
     head_dim: int = 128
     mlp_width: int = 8192
+    conv_taps: int = 3          # grouped dynamic conv on the attention and MLP inputs
+    conv_group: int = 64        # channels sharing one per-row kernel delta
 
 
 class BlockDrafter:
@@ -65,6 +73,18 @@ class BlockDrafter:
         self.gu = interleave_gate_up(lin("drafter.gate_up", 2 * dc.mlp_width, D))
         self.down = lin("drafter.down", D, dc.mlp_width)
         self.n1, self.n2, self.nf = norm("drafter.n1", D), norm("drafter.n2", D), norm("drafter.nf", D)
+        taps, G = dc.conv_taps, D // dc.conv_group
+
+        def conv_base(name):
+            g = torch.Generator(device=dev)
+            g.manual_seed(_seed_of(seed, name))
+            b = 0.1 * torch.randn(taps, D, generator=g, device=dev)
+            b[0] += 1.0                                   # near the identity: the current row dominates
+            return b.to(torch.bfloat16)
+        self.conv_a = (lin("drafter.conv_attn.delta", taps * G, D), conv_base("drafter.conv_attn.base"))
+        self.conv_m = (lin("drafter.conv_mlp.delta", taps * G, D), conv_base("drafter.conv_mlp.base"))
+        self.delta = torch.zeros(dc.block, taps * G, dtype=torch.bfloat16, device=dev)
+        self.xc = torch.zeros(dc.block, D, dtype=torch.bfloat16, device=dev)
         g = torch.Generator(device=dev)
         g.manual_seed(_seed_of(seed, "drafter.slot"))
         self.slot_emb = (torch.randn(dc.block, D, generator=g, device=dev) * 0.1).float()
@@ -79,27 +99,50 @@ class BlockDrafter:
         self.act = torch.zeros(R, dc.mlp_width, dtype=bf, device=dev)
         self.logits = torch.zeros(R, target_w.head.n, dtype=torch.float32, device=dev)
         self.ids = torch.full((R,), MASK_TOKEN, dtype=torch.int32, device=dev)
+        self.hid = torch.zeros(D, dtype=bf, device=dev)
+
+    def _dconv(self, conv, R: int) -> None:
+        """xc[:R] = grouped dynamic conv of xn[:R] (the kernel deltas projected from xn itself)."""
+        proj, base = conv
+        K.linear8(self.xn[:R], proj.w, proj.s, self.delta[:R])
+        K.C().dconv(self.xn[:R], self.delta[:R], base, self.xc[:R], self.dc.conv_group, self.dc.block)
 
     @torch.no_grad()
     def forward(self, last_token: torch.Tensor, hidden: torch.Tensor, k: int) -> torch.Tensor:
         """last_token: int32 [1] (device); hidden: bf16 [D] target hidden of that token. Returns logits [k, V_local]
         (the caller samples / argmaxes them through the tensor-parallel sampler)."""
+        self.stage(last_token, hidden)
+        return self.run(k)
+
+    def stage(self, last_token, hidden: torch.Tensor) -> None:
+        """Inputs of the next draft into the drafter's static buffers (outside any CUDA graph): the last token (a
+        device int32 [1] tensor or a Python int) and the target hidden state of that token."""
+        if isinstance(last_token, int):
+            self.ids[:1].fill_(last_token)
+        else:
+            self.ids[:1].copy_(last_token)
+        self.hid.copy_(hidden.view(-1))
+
+    @torch.no_grad()
+    def run(self, k: int) -> torch.Tensor:
+        """The draft block from the staged inputs (static buffers only: capturable as a CUDA graph per k)."""
         Kc = K.C()
         D = self.cfg.hidden
         R = max(k, 1)
-        self.ids[:1].copy_(last_token)
         # [h ; emb(t_i)]
         Kc.embed(self.ids[:R], self.tw.embed, self.emb[:R])
         self.inp[:R, D:].copy_(self.emb[:R, 0])
-        self.inp[:R, :D].copy_(hidden.view(1, D).expand(R, D))
+        self.inp[:R, :D].copy_(self.hid.view(1, D).expand(R, D))
         self.x[:R].copy_(self.slot_emb[:R])
         K.linear8(self.inp[:R], self.fc.w, self.fc.s, self.x[:R], K.GEMV_F32_ACC)
         Kc.rmsnorm_f32(self.x[:R], self.n1, self.cfg.eps, self.xn[:R])
-        K.linear8(self.xn[:R], self.qkv.w, self.qkv.s, self.qkv_buf[:R])
+        self._dconv(self.conv_a, R)
+        K.linear8(self.xc[:R], self.qkv.w, self.qkv.s, self.qkv_buf[:R])
         Kc.block_attn(self.qkv_buf[:R], self.dc.heads, self.dc.head_dim, R, self.dc.head_dim ** -0.5, self.att[:R])
         K.linear8(self.att[:R], self.o.w, self.o.s, self.x[:R], K.GEMV_F32_ACC)
         Kc.rmsnorm_f32(self.x[:R], self.n2, self.cfg.eps, self.xn[:R])
-        K.linear8(self.xn[:R], self.gu.w, self.gu.s, self.act[:R], K.GEMV_SWIGLU, self.cfg.limit)
+        self._dconv(self.conv_m, R)
+        K.linear8(self.xc[:R], self.gu.w, self.gu.s, self.act[:R], K.GEMV_SWIGLU, self.cfg.limit)
         K.linear8(self.act[:R], self.down.w, self.down.s, self.x[:R], K.GEMV_F32_ACC)
         Kc.rmsnorm_f32(self.x[:R], self.nf, self.cfg.eps, self.xn[:R])
         K.linear8(self.xn[:R], self.tw.head.w, self.tw.head.s, self.logits[:R], K.GEMV_F32)

@@ -455,3 +455,28 @@ def test_l2_prefetch_leaves_results_unchanged(C):
     Kk.C().l2_prefetch([a], 4096)
     torch.cuda.synchronize()
     assert Kk.C().gemm_error(a) == 0
+
+
+@pytest.mark.parametrize("T,blk", [(8, 8), (12, 5), (1, 8)])
+def test_dconv_matches_eager_chain(C, T, blk):
+    """The drafter's grouped dynamic conv kernel equals the eager bf16 op chain bit for bit (per-row kernel deltas
+    shared by channel groups, causal taps masked at draft-block boundaries)."""
+    from glm53.ops import kernels as Kk
+    H, taps, gs = 512, 3, 64
+    g = torch.Generator(device=DEV).manual_seed(T * 7 + blk)
+    x = torch.randn(T, H, device=DEV, generator=g).to(torch.bfloat16)
+    delta = (0.1 * torch.randn(T, taps, H // gs, device=DEV, generator=g)).to(torch.bfloat16)
+    base = (0.5 * torch.randn(taps, H, device=DEV, generator=g)).to(torch.bfloat16)
+    out = torch.empty(T, H, device=DEV, dtype=torch.bfloat16)
+    Kk.C().dconv(x, delta, base, out, gs, blk)
+    pos = torch.arange(T, device=DEV) % blk
+    ck = base[None] + delta.repeat_interleave(gs, -1)              # [T, taps, H] bf16
+    ref = ck[:, 0] * x
+    for k in range(1, taps):
+        xs = torch.zeros_like(x)
+        if T > k:
+            xs[k:] = x[:-k]
+        p = ck[:, k] * xs
+        p = p * (pos >= k)[:, None].to(torch.bfloat16)
+        ref = ref + p
+    assert torch.equal(out, ref)
