@@ -27,35 +27,6 @@ void cuda_check(const Tensor& t, const char* name) {
 }
 
 // ------------------------------------------------------------------------------------------------- GEMV
-// stream-K fp8 GEMV for large projections only with GLM53_STREAM_GEMV=1 (slower than the split-K kernel at 8
-// warps per SM: kept for measurements)
-static bool stream_gemv_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = std::getenv("GLM53_STREAM_GEMV");
-    v = (e && e[0] == '1') ? 1 : 0;
-  }
-  return v == 1;
-}
-
-// per-device stream-K scratch: partials of up to SMs * 16 warps (2 tiles each) and zeroed per-tile counters
-static void stream_scratch(const Tensor& like, GemvArgs& p) {
-  static std::vector<Tensor> parts(64), cnts(64);
-  static std::vector<int> sms(64, 0);
-  const int dev = like.get_device();
-  if (!parts[dev].defined()) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    sms[dev] = n;
-    parts[dev] = torch::empty({(int64_t)n * 16 * 2 * 256}, like.options().dtype(at::kFloat));
-    cnts[dev] = torch::zeros({16384}, like.options().dtype(at::kInt));
-  }
-  p.stream_part = parts[dev].data_ptr<float>();
-  p.stream_cnt = cnts[dev].data_ptr<int>();
-  p.stream_tiles = 16384;
-  p.stream_sms = sms[dev];
-}
-
 Tensor& err_word(const Tensor& like);
 
 void gemv(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, int64_t mode, double limit,
@@ -96,7 +67,6 @@ void gemv(const Tensor& x, const Tensor& w, const OptT& scale, const Tensor& y, 
   TORCH_CHECK(y.size(-2) >= p.M, "y rows");
   if (w.scalar_type() == at::kByte || w.scalar_type() == at::kFloat8_e4m3fn) {
     TORCH_CHECK(scale.has_value(), "fp8 weights need a scale");
-    if (stream_gemv_enabled()) stream_scratch(x, p);
     p.force_ks = (int)ks;
     p.force_cl = (int)cl;
     p.err = err_word(x).data_ptr<int>();

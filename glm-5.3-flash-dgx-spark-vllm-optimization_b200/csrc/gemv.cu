@@ -203,177 +203,6 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
   }
 }
 
-// ---------------------------------------------------------------------------------------------------------------
-// Stream-K variant for large fp8 projections (decode).  The work is the list of units (16-row tile t, 64-wide k
-// chunk c) in tile-major order; warp w of the grid takes the contiguous units [U w / W, U (w+1) / W), so every
-// warp streams the same number of weight bytes (no tail wave) and keeps kSD units of weight loads in flight across
-// tile boundaries.  A tile covered by one warp is finished by it; a tile split between warps w_lo..w_hi gets one
-// fp32 partial per warp (slot: the warp's first or last tile), and the warp that arrives last (per-tile counter)
-// adds the partials in warp order -- the result does not depend on arrival order -- and resets the counter.
-// ---------------------------------------------------------------------------------------------------------------
-constexpr int kSD = 12;                // units of weight loads in flight per warp
-
-__device__ __forceinline__ int64_t stream_warp_of(int64_t x, int64_t U, int64_t W) { return ((x + 1) * W - 1) / U; }
-
-template <bool TWO>
-__device__ __forceinline__ void stream_store(const GemvArgs& p, int t, const float (&a0)[4], const float (&a1)[4]) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-  const int n0 = t * 16;
-  if (p.mode == GEMV_SWIGLU) {
-    // rows 0..7 of the tile are gate rows, 8..15 the matching up rows
-    if (n0 + g + 8 >= p.N) return;
-    const float sg = p.scale ? p.scale[n0 + g] : 1.f, su = p.scale ? p.scale[n0 + g + 8] : 1.f;
-    __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(p.y);
-#pragma unroll
-    for (int h = 0; h < (TWO ? 2 : 1); ++h)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int tok = h * 8 + 2 * q + e;
-        if (tok >= p.M) continue;
-        const float* a = h ? a1 : a0;
-        float gv = round_bf16(a[e] * sg), uv = round_bf16(a[2 + e] * su);
-        gv = fminf(gv, p.limit);
-        uv = fminf(fmaxf(uv, -p.limit), p.limit);
-        y[(int64_t)tok * p.ldy + (n0 >> 1) + g] = f2bf(siluf_(gv) * uv);
-      }
-    return;
-  }
-#pragma unroll
-  for (int h = 0; h < (TWO ? 2 : 1); ++h)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int n = n0 + g + (i >= 2 ? 8 : 0), tok = h * 8 + 2 * q + (i & 1);
-      if (n >= p.N || tok >= p.M) continue;
-      float v = (h ? a1 : a0)[i];
-      if (p.scale) v *= p.scale[n];
-      const int64_t off = (int64_t)tok * p.ldy + n;
-      if (p.mode == GEMV_BF16) {
-        reinterpret_cast<__nv_bfloat16*>(p.y)[off] = f2bf(v);
-      } else {
-        float* yf = reinterpret_cast<float*>(p.y);
-        if (p.mode == GEMV_F32_ACC) v += yf[off];
-        yf[off] = v;
-      }
-    }
-}
-
-// a tile this warp finished only partly: publish the partial; the last of the tile's warps adds them in warp order
-template <bool TWO>
-__device__ __noinline__ void stream_partial(const GemvArgs& p, float* part, int* cnt, int t, int64_t wg, int64_t W,
-                                            int64_t U, int C, float a0_0, float a0_1, float a0_2, float a0_3,
-                                            float a1_0, float a1_1, float a1_2, float a1_3) {
-  const int lane = threadIdx.x & 31;
-  const int64_t first_u = U * wg / W;
-  const int side = (first_u / C == t) ? 0 : 1;
-  float* mine = part + ((wg * 2 + side) * 32 + lane) * 8;
-  *reinterpret_cast<float4*>(mine) = make_float4(a0_0, a0_1, a0_2, a0_3);
-  *reinterpret_cast<float4*>(mine + 4) = make_float4(a1_0, a1_1, a1_2, a1_3);
-  __threadfence();
-  __syncwarp();
-  const int64_t w_lo = stream_warp_of((int64_t)t * C, U, W), w_hi = stream_warp_of((int64_t)t * C + C - 1, U, W);
-  int last = 0;
-  if (lane == 0) last = atomicAdd(&cnt[t], 1) == (int)(w_hi - w_lo);
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (!last) return;
-  __threadfence();
-  float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int64_t w = w_lo; w <= w_hi; ++w) {
-    const int sd = ((U * w / W) / C == t) ? 0 : 1;
-    const float* src = part + ((w * 2 + sd) * 32 + lane) * 8;
-    const float4 v0 = __ldcg(reinterpret_cast<const float4*>(src));
-    const float4 v1 = __ldcg(reinterpret_cast<const float4*>(src + 4));
-    s0[0] += v0.x; s0[1] += v0.y; s0[2] += v0.z; s0[3] += v0.w;
-    s1[0] += v1.x; s1[1] += v1.y; s1[2] += v1.z; s1[3] += v1.w;
-  }
-  if (lane == 0) cnt[t] = 0;
-  stream_store<TWO>(p, t, s0, s1);
-}
-
-template <bool TWO>
-__global__ void __launch_bounds__(256, 1) gemv_stream_kernel(GemvArgs p, float* part, int* cnt) {
-  const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
-  const int64_t W = (int64_t)gridDim.x * 8, wg = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int C = p.K / 64, T = (p.N + 15) / 16;
-  const int64_t U = (int64_t)T * C;
-  const int64_t u0 = U * wg / W, u1 = U * (wg + 1) / W;
-  if (u0 >= u1) return;
-  const uint8_t* wbase = reinterpret_cast<const uint8_t*>(p.w);
-  const __nv_bfloat16* x0 = p.x + (int64_t)g * p.ldx + q * 16;
-  const __nv_bfloat16* x1 = p.x + (int64_t)(g + 8) * p.ldx + q * 16;
-  const bool t0 = g < p.M, t1 = TWO && (g + 8) < p.M;
-  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
-  // prefetch cursor (tile, chunk) and the first kSD units
-  int pt = (int)(u0 / C), pc = (int)(u0 % C);
-  uint4 ra[kSD], rb[kSD];
-#pragma unroll
-  for (int j = 0; j < kSD; ++j) {
-    ra[j] = rb[j] = z4;
-    if (u0 + j < u1) {
-      const int r = pt * 16 + g;
-      const uint8_t* src = wbase + (int64_t)r * p.K + pc * 64 + q * 16;
-      if (r < p.N) ra[j] = ldg_nc_v4(src);
-      if (r + 8 < p.N) rb[j] = ldg_nc_v4(src + (int64_t)8 * p.K);
-      if (++pc == C) { pc = 0; ++pt; }
-    }
-  }
-  int t = (int)(u0 / C), c = (int)(u0 % C);
-  bool whole = c == 0;                       // this warp started the current tile at its first chunk
-  float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-  for (int64_t base = u0; base < u1; base += kSD) {
-#pragma unroll
-    for (int j = 0; j < kSD; ++j) {
-      const int64_t uu = base + j;
-      if (uu < u1) {
-        const int kb = c * 64;
-        const uint4 xa0 = t0 ? *reinterpret_cast<const uint4*>(x0 + kb) : z4;
-        const uint4 xa1 = t0 ? *reinterpret_cast<const uint4*>(x0 + kb + 8) : z4;
-        uint4 xc0 = z4, xc1 = z4;
-        if (t1) {
-          xc0 = *reinterpret_cast<const uint4*>(x1 + kb);
-          xc1 = *reinterpret_cast<const uint4*>(x1 + kb + 8);
-        }
-        const uint32_t wav[4] = {ra[j].x, ra[j].y, ra[j].z, ra[j].w};
-        const uint32_t wbv[4] = {rb[j].x, rb[j].y, rb[j].z, rb[j].w};
-        const uint32_t xav[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
-        const uint32_t xcv[8] = {xc0.x, xc0.y, xc0.z, xc0.w, xc1.x, xc1.y, xc1.z, xc1.w};
-        // refill this slot with unit uu + kSD
-        ra[j] = rb[j] = z4;
-        if (uu + kSD < u1) {
-          const int r = pt * 16 + g;
-          const uint8_t* src = wbase + (int64_t)r * p.K + pc * 64 + q * 16;
-          if (r < p.N) ra[j] = ldg_nc_v4(src);
-          if (r + 8 < p.N) rb[j] = ldg_nc_v4(src + (int64_t)8 * p.K);
-          if (++pc == C) { pc = 0; ++pt; }
-        }
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          uint32_t a[4];
-          a[0] = e4m3x2_to_f16x2((uint16_t)(wav[s] & 0xffffu));
-          a[1] = e4m3x2_to_f16x2((uint16_t)(wbv[s] & 0xffffu));
-          a[2] = e4m3x2_to_f16x2((uint16_t)(wav[s] >> 16));
-          a[3] = e4m3x2_to_f16x2((uint16_t)(wbv[s] >> 16));
-          mma_f16_16816(acc0, a, bf16x2_to_f16x2(xav[2 * s]), bf16x2_to_f16x2(xav[2 * s + 1]));
-          if (TWO) mma_f16_16816(acc1, a, bf16x2_to_f16x2(xcv[2 * s]), bf16x2_to_f16x2(xcv[2 * s + 1]));
-        }
-        const bool tile_end = c == C - 1;
-        if (tile_end || uu == u1 - 1) {
-          if (whole && tile_end) {
-            stream_store<TWO>(p, t, acc0, acc1);
-          } else {
-            stream_partial<TWO>(p, part, cnt, t, wg, W, U, C, acc0[0], acc0[1], acc0[2], acc0[3], acc1[0], acc1[1],
-                                acc1[2], acc1[3]);
-          }
-#pragma unroll
-          for (int i = 0; i < 4; ++i) acc0[i] = acc1[i] = 0.f;
-          whole = true;
-        }
-        if (++c == C) { c = 0; ++t; }
-      }
-    }
-  }
-}
-
 // launched as a programmatic dependent of the previous kernel (weights prefetched before pdl_wait) unless
 // GLM53_PDL=0
 static bool pdl_enabled() {
@@ -417,16 +246,6 @@ static cudaError_t launch_cfg(const GemvArgs& p, dim3 grid, int cl, cudaStream_t
   }
 }
 
-// stream-K launch: one CTA of 8 warps per SM, at least 8 units per warp (part holds 16 warps per SM)
-static cudaError_t launch_stream(const GemvArgs& p, float* part, int* cnt, int sms, cudaStream_t st) {
-  const int64_t U = (int64_t)((p.N + 15) / 16) * (p.K / 64);
-  const int64_t warps = std::min<int64_t>((int64_t)sms * 8, U / 8);
-  const int grid = (int)std::max<int64_t>(1, warps / 8);
-  if (p.M > 8) gemv_stream_kernel<true><<<grid, 256, 0, st>>>(p, part, cnt);
-  else gemv_stream_kernel<false><<<grid, 256, 0, st>>>(p, part, cnt);
-  return cudaGetLastError();
-}
-
 // large fp8 projections go through the bulk-copy kernel (GLM53_BULK_GEMV=0 disables it; GLM53_BULK_GEMV_MIN sets
 // the weight size in bytes from which it is used).  Measured on B200 (L2 flushed, M = 8): 1.5x on the KDA input
 // projection and the lm_head shard (0.89 of measured HBM), 1.1-1.3x on the 4096-row output projections, 1.2x on
@@ -456,10 +275,6 @@ static cudaError_t launch_gemv_t(const GemvArgs& p, cudaStream_t st) {
       (p.force_ks == -1 || (p.force_ks == 0 && p.force_cl == 0 && bulk_enabled() && (p.M <= 8 || p.K <= 4096) &&
                             (int64_t)p.N * p.K >= bulk_min_bytes())))
     return g53_gemv_bulk(p, pdl_enabled(), st);
-  if (FP8 && p.stream_part && p.force_ks == 0 && p.batch == 1 && p.push_ptrs == nullptr &&
-      (int64_t)((p.N + 15) / 16) * (p.K / 64) >= (int64_t)p.stream_sms * 8 * 16 &&
-      (p.N + 15) / 16 <= p.stream_tiles)
-    return launch_stream(p, p.stream_part, p.stream_cnt, p.stream_sms, st);
   const int nchunk = p.K / CH;
   int ks = 8;
   while (ks > 1 && nchunk < ks * 2) ks >>= 1;

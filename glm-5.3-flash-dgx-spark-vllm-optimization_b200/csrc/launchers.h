@@ -26,9 +26,6 @@ struct GemvArgs {
   int64_t push_slot;                                   // elements per rank slot
   int push_rank, push_world;
   int* err;                                            // device error word (bounded waits)
-  // stream-K scratch (large fp8 projections): [SMs * 16 warps][2][256] fp32 partials, [stream_tiles] counters
-  // (zero between launches); null = the split-K kernel only
-  float* stream_part; int* stream_cnt; int stream_tiles; int stream_sms;
   int force_ks, force_cl;                              // split-K kernel shape overrides (0 = chosen by size; force_ks
                                                        // -1 = the bulk-copy kernel, -2 = the split-K kernel
                                                        // with its own shape choice)

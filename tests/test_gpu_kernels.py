@@ -348,10 +348,10 @@ def test_hc_post_pre_decode_cluster(C, rows, with_post):
 
 @pytest.mark.parametrize("M", [1, 8, 12])
 @pytest.mark.parametrize("N,K", [(24896, 4096), (4100, 8192), (4096, 16384)])
-def test_gemv_fp8_stream_k(C, M, N, K):
-    """Large projections go through the stream-K kernel (every warp an equal run of 64-wide chunks, tiles split
-    between warps finished by the last one in warp order): all output modes against the fp32 reference, and two
-    launches in a row give identical bits (the per-tile counters reset themselves)."""
+def test_gemv_fp8_large_default_dispatch(C, M, N, K):
+    """Large projections through the default dispatch (the bulk-copy kernel for up to 8 rows or K <= 4096, the
+    split-K kernel otherwise; a partial last tile for N = 4100): all output modes against the fp32 reference, and
+    two launches in a row give identical bits."""
     from glm53.models.weights import quantize_fp8_rows
     from glm53.ops import kernels as Kk
     g = torch.Generator(device=DEV).manual_seed(M * 13 + N)
@@ -373,7 +373,9 @@ def test_gemv_fp8_stream_k(C, M, N, K):
     torch.testing.assert_close(acc, ref + 1, atol=2e-3, rtol=2e-3)
 
 
-def test_gemv_swiglu_stream_k(C):
+def test_gemv_swiglu_large_default_dispatch(C):
+    """The interleaved SwiGLU output mode at the dense MLP's size (100 MB of fp8 weights) through the default
+    dispatch."""
     from glm53.models.runtime import interleave_gate_up
     from glm53.models.weights import quantize_fp8_rows
     from glm53.models.reference import swiglu
