@@ -93,6 +93,16 @@ class GPUBackend:
         replay = any(k < d[1] for d, k in zip(self._last_descs, keeps))
         self.rt.commit(descs, replay=replay)
 
+    @torch.no_grad()
+    def commit_rest(self, parts: list[tuple[int, int, int]]):
+        """After commit(): commit n further rows (from row `offset` of the window) of sequence i of the last window,
+        for each (i, offset, n), continuing from the state the first commit left in the other buffer."""
+        descs = []
+        for i, off, n in parts:
+            d = self._last_descs[i]
+            descs.append((d[0] + off, n, d[3], d[2], d[4]))
+        self.rt.commit(descs, replay=True)
+
     def hidden(self, row: int) -> torch.Tensor:
         return self.rt.hidden[row]
 

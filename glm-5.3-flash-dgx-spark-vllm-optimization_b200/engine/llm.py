@@ -232,11 +232,7 @@ class LLMEngine:
             r.pos += len(rows.tokens)
             r.cur = 1 - r.cur
             self.kv.commit_tokens(r.cache, r.tokens, r.pos)
-            if interval and r.pos % interval == 0 and r.cache.hashes:
-                h = r.cache.hashes[r.pos // self.cfg.page_size - 1]
-                ck = self.slots.checkpoint_slot(h, r.pos)
-                if ck is not None:
-                    self.b.save_state(r.slot, r.cur, ck.slot)
+            self._checkpoint(r)
         if finishing:
             toks = self._sample_rows(logits, [r for r, _ in finishing])
             for i, (r, row_idx) in enumerate(finishing):
@@ -313,16 +309,47 @@ class LLMEngine:
                 self.metrics["spec_accepted"] += n_acc
                 r.accepted.append(n_acc)
                 r.adaptive.update(n_acc)
-        self.b.commit(keeps)
-        for (r, rows), keep in zip(batch, keeps):
-            r.pos += keep
+        # a state checkpoint interval boundary strictly inside a sequence's kept rows splits its commit there, so
+        # the recurrent state at the boundary can be saved for later prefix hits (multi-turn follow-ups)
+        interval = self.cfg.checkpoint_pages * self.cfg.page_size if self.cfg.checkpoints else 0
+        first, rest = list(keeps), []
+        if interval:
+            for i, ((r, _), keep) in enumerate(zip(batch, keeps)):
+                bnd = (r.pos // interval + 1) * interval
+                if bnd < r.pos + keep:
+                    first[i] = bnd - r.pos
+                    rest.append((i, first[i], keep - first[i]))
+        self.b.commit(first)
+        for (r, rows), keep, k1 in zip(batch, keeps, first):
+            r.pos += k1
             r.cur = 1 - r.cur
-            self.kv.commit_tokens(r.cache, r.tokens, r.pos)
+            # the accepted drafts are not in r.output yet: hash the committed positions' own tokens
+            self.kv.commit_tokens(r.cache, r.tokens + r._new[:keep - 1], r.pos)
+            self._checkpoint(r)
+        if rest:
+            self.b.commit_rest(rest)
+            for i, _, n in rest:
+                r = batch[i][0]
+                r.pos += n
+                r.cur = 1 - r.cur
+                self.kv.commit_tokens(r.cache, r.tokens + r._new[:keeps[i] - 1], r.pos)
+                self._checkpoint(r)
+        for (r, rows), keep in zip(batch, keeps):
             r.hidden = self.b.hidden(r._last_row).clone()
             outs.append(self._emit(r, r._new))
             if r.state == State.RUNNING and spec:
                 self._draft(r)
         return outs
+
+    def _checkpoint(self, r: Request) -> None:
+        """Save the request's committed recurrent state when its committed length sits on a checkpoint boundary
+        (a page-aligned prefix whose pages are in the prefix cache)."""
+        interval = self.cfg.checkpoint_pages * self.cfg.page_size if self.cfg.checkpoints else 0
+        if not interval or r.pos % interval or len(r.cache.hashes) < r.pos // self.cfg.page_size:
+            return
+        ck = self.slots.checkpoint_slot(r.cache.hashes[r.pos // self.cfg.page_size - 1], r.pos)
+        if ck is not None:
+            self.b.save_state(r.slot, r.cur, ck.slot)
 
     def _sampled_accept(self, r: Request, logits: torch.Tensor, drafts: list[int]):
         """Rejection sampling of one request's window (CUDA kernel; standard or block verification)."""

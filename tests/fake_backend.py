@@ -29,7 +29,7 @@ class FakeBackend:
         self.ck = {}
         self.drafter = self
         self.err = drafter_error_every
-        self.calls = {"prefill": 0, "verify": 0, "commit": 0, "draft": 0, "save": 0, "load": 0}
+        self.calls = {"prefill": 0, "verify": 0, "commit": 0, "commit_rest": 0, "draft": 0, "save": 0, "load": 0}
         self._pending = []
         self._hidden = []
 
@@ -63,6 +63,13 @@ class FakeBackend:
         self.calls["commit"] += 1
         for (slot, toks), k in zip(self._pending, keeps):
             self.hist[slot] += toks[:k]
+
+    def commit_rest(self, parts):
+        self.calls["commit_rest"] += 1
+        for i, off, n in parts:
+            slot, toks = self._pending[i]
+            assert len(self.hist[slot]) >= off
+            self.hist[slot] += toks[off:off + n]
 
     def hidden(self, row):
         return self._hidden[row]

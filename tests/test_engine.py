@@ -159,3 +159,36 @@ def test_vtrim_cuts_verify_rows_keeps_output():
         if tau > 0:
             assert eng.metrics["vtrim_cut"] > 0 and len(eng.vtrim_records) > 0
     assert outs[0.0] == outs[0.5] == reference_greedy(prompt, 30)
+
+
+@pytest.mark.parametrize("force", [False, True])
+def test_decoded_pages_are_hashed_from_their_tokens(force):
+    """Pages filled during speculative decoding enter the prefix cache under the hash of the tokens they hold (the
+    accepted drafts are committed before they are emitted): the whole committed sequence matches afterwards."""
+    e = _engine(speculative=True, force_accept=force, k_fixed=7 if force else None)
+    prompt = list(range(30, 70))
+    out = e.generate([prompt], SamplingParams(max_tokens=90, ignore_eos=True))[0]
+    committed = prompt + out[:-1]                         # the last emitted token has no cache entry yet
+    pids, _ = e.kv.match_prefix(committed)
+    assert len(pids) == len(committed) // 16
+
+
+@pytest.mark.parametrize("force", [False, True])
+def test_decode_checkpoints_serve_follow_up_turns(force):
+    """State checkpoints are also taken where decoding crosses a checkpoint boundary (the window's commit is split
+    there), so a follow-up request that repeats prompt + answer resumes inside the answer and still produces the
+    target's greedy continuation."""
+    e = _engine(speculative=True, force_accept=force, k_fixed=7 if force else None, checkpoints=8,
+                checkpoint_pages=1)
+    prompt = list(range(30, 70))
+    out = e.generate([prompt], SamplingParams(max_tokens=70, ignore_eos=True))[0]
+    assert e.b.calls["commit_rest"] > 0 or force         # windows straddled boundaries
+    follow = prompt + out + [5, 6, 7]
+    before = e.metrics["prefix_cached_tokens"]
+    out2 = e.generate([follow], SamplingParams(max_tokens=20, ignore_eos=True))[0]
+    hit = e.metrics["prefix_cached_tokens"] - before
+    assert hit >= (len(prompt) + len(out) - 1) // 16 * 16 - 16 and hit > len(prompt)
+    if force:
+        assert out2[:1] == reference_greedy(follow, 1)   # forced acceptance emits drafts: only the first is target's
+    else:
+        assert out2 == reference_greedy(follow, 20)

@@ -52,3 +52,22 @@ def test_prefix_cache_hit_reproduces_output():
     b = llm2.engine.generate([base], SamplingParams(max_tokens=16, ignore_eos=True))[0]
     assert llm2.engine.metrics["prefix_cached_tokens"] >= 256
     assert a2 == b
+
+
+def test_decode_checkpoints_split_commits_stay_exact():
+    """With a state checkpoint every page, decode windows that straddle a page boundary commit in two parts (the
+    KDA recurrence replayed up to the boundary, the state saved, then the rest of the kept rows); greedy speculative
+    decoding must still emit exactly the tokens of plain greedy decoding, and a follow-up request that repeats the
+    prompt and answer resumes from a checkpoint inside the answer."""
+    from glm53.engine.llm import SamplingParams
+    prompt = _prompts(1, 100, seed=7)[0]
+    sp = SamplingParams(max_tokens=90, ignore_eos=True)
+    plain = _llm(speculative=False).engine.generate([prompt], sp)[0]
+    llm = _llm(speculative=True, checkpoints=8)
+    llm.engine.cfg.checkpoint_pages = 1
+    spec = llm.engine.generate([prompt], sp)[0]
+    assert spec == plain
+    follow = prompt + spec + [11, 12, 13]
+    before = llm.engine.metrics["prefix_cached_tokens"]
+    llm.engine.generate([follow], SamplingParams(max_tokens=4, ignore_eos=True))
+    assert llm.engine.metrics["prefix_cached_tokens"] - before > len(prompt)
