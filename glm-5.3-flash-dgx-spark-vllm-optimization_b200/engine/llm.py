@@ -55,6 +55,8 @@ class EngineConfig:
     checkpoints: int = 0                   # KDA state checkpoint slots (prefix cache for hybrid state)
     checkpoint_pages: int = 8              # checkpoint interval in pages
     prefill_first: bool = True             # a step with waiting prefill runs it before decode
+    mixed_prefill_chunk: int = 0           # > 0: prefill tokens per step while requests are decoding (bounds the
+                                           # decode stall a newcomer causes; 0 = the whole prefill_chunk budget)
     cuda_graphs: bool = True
     vtrim_tau: float = 0.0                 # > 0: verify only the drafts before the first one whose drafter
                                            # confidence (max softmax probability) is below tau
@@ -183,7 +185,10 @@ class LLMEngine:
         prefill = [r for r in self.running if r.state == State.PREFILL]
         decode = [r for r in self.running if r.state == State.RUNNING]
         if prefill and (self.cfg.prefill_first or not decode):
-            outs += self._prefill_step(prefill)
+            budget = self.cfg.prefill_chunk
+            if decode and self.cfg.mixed_prefill_chunk > 0:
+                budget = min(budget, self.cfg.mixed_prefill_chunk)
+            outs += self._prefill_step(prefill, budget)
         decode = [r for r in self.running if r.state == State.RUNNING]
         if decode:
             outs += self._decode_step(decode)
@@ -197,8 +202,8 @@ class LLMEngine:
         return SeqRows(tokens, positions, [self.kv.slot(r.cache, p) for p in positions], list(r.cache.pages),
                        r.slot, r.cur)
 
-    def _prefill_step(self, reqs: list[Request]) -> list[RequestOutput]:
-        budget = self.cfg.prefill_chunk
+    def _prefill_step(self, reqs: list[Request], budget: int | None = None) -> list[RequestOutput]:
+        budget = self.cfg.prefill_chunk if budget is None else budget
         batch, ends = [], []
         interval = self.cfg.checkpoint_pages * self.cfg.page_size if self.cfg.checkpoints else 0
         for r in reqs:

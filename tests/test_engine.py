@@ -192,3 +192,24 @@ def test_decode_checkpoints_serve_follow_up_turns(force):
         assert out2[:1] == reference_greedy(follow, 1)   # forced acceptance emits drafts: only the first is target's
     else:
         assert out2 == reference_greedy(follow, 20)
+
+
+def test_mixed_prefill_chunk_caps_prefill_beside_decodes():
+    """With mixed_prefill_chunk set, a newcomer's prompt is prefilled at most that many tokens per step while other
+    requests decode (their per-step stall stays bounded), and the whole budget is used when nothing decodes; the
+    outputs are unchanged."""
+    e = _engine(speculative=False, mixed_prefill_chunk=16, prefill_chunk=64)
+    a = e.add_request(list(range(20, 50)), SamplingParams(max_tokens=40))
+    e.step()                                       # a: the whole 30-token prompt (nothing decodes yet), then a decode
+    assert e.running[0].pos >= 30
+    b = e.add_request(list(range(100, 200)), SamplingParams(max_tokens=8))
+    positions = []
+    for _ in range(3):
+        e.step()
+        rb = next(r for r in e.running if r.rid == b)
+        positions.append(rb.pos)
+    assert positions == [16, 32, 48]
+    while e.has_work():
+        e.step()
+    assert e.done[a].output == reference_greedy(list(range(20, 50)), 40)
+    assert e.done[b].output == reference_greedy(list(range(100, 200)), 8)
