@@ -2,16 +2,18 @@
 //
 // Y[M, N] = X[M, K] @ (W8[N, K] * s[N])^T.  A decode projection reads every weight byte once, so its speed of light
 // is HBM bandwidth; what keeps a load-per-lane kernel below it is too few bytes in flight per SM.  Here one CTA per
-// SM is persistent over 16-row tiles: a producer warp streams each tile in stages of 16 rows x KC bytes into a ring
-// of shared-memory buffers with cp.async.bulk (one 1 KB row segment per lane, completion counted in bytes on the
-// stage's mbarrier, L2 evict-first: the weights are read once), so 11-12 stages x 17 KB per SM are always in flight,
-// independent of how long the math warps take.  Sixteen consumer warps split each stage's k range, load their
-// 16-byte weight segments from shared memory (rows padded by 64 bytes: the two rows a quarter-warp reads fall in
-// disjoint bank halves), convert e4m3 -> f16 exactly and run swap-AB mma.m16n8k16 (the weight tile is the 16-row
-// A operand, the at most 16 activation rows the B operand, with the same k permutation inside each 64-element chunk
-// as the load-per-lane kernel).  The per-warp partial tiles are summed in fixed warp order (deterministic) through
-// a double-buffered shared array, and the output modes are those of the load-per-lane kernel (bf16, fp32, fp32
-// accumulate, interleaved SwiGLU, fused push of the fp32 partial to every tensor-parallel peer).
+// SM is persistent over 16-row tiles: a producer warp streams each tile in stages of 16 rows x KC bytes (KC = 1, 2
+// or 4 KB) into a ring of shared-memory buffers with cp.async.bulk (one row segment per lane, completion counted in
+// bytes on the stage's mbarrier, L2 evict-first: the weights are read once), so about 200 KB per SM are in flight
+// independent of how long the math warps take.  The copy size matters: with 1 KB copies the stream stalled near
+// 2.5-3 TB/s whatever the ring depth, 4 KB copies reach 5.8 TB/s.  Sixteen consumer warps split each stage's k
+// range, load their 16-byte weight segments from shared memory (rows padded by 64 bytes: the two rows a
+// quarter-warp reads fall in disjoint bank halves), convert e4m3 -> f16 exactly and run swap-AB mma.m16n8k16 (the
+// weight tile is the 16-row A operand, the at most 16 activation rows the B operand, with the same k permutation
+// inside each 64-element chunk as the load-per-lane kernel); the activation fragments stay in registers for the
+// CTA's life when K is small enough.  The per-warp partial tiles are summed in fixed warp order (deterministic)
+// through a shared array, and the output modes are those of the load-per-lane kernel (bf16, fp32, fp32 accumulate,
+// interleaved SwiGLU, fused push of the fp32 partial to every tensor-parallel peer).
 //
 // The weight stream does not depend on the previous kernel, so the producer starts before griddepcontrol.wait
 // (programmatic dependent launch); the consumers wait before touching X or Y.  Every mbarrier wait is bounded: on a
