@@ -235,7 +235,8 @@ def main():
                                 f" EXL3 4bpw, vocab {cfg.vocab}" if args.model == "full" else "glm53-tiny",
                        "global_batch": 1, "seq_len": args.context, "parallelism": f"tp{world}", "K": K,
                        "tokens_per_step": rows, "acceptance": "forced (all K drafts accepted)",
-                       "drafter": "1-layer block drafter in every step", "cuda_graph": not args.no_graph,
+                       "drafter": "1-layer block drafter (grouped dynamic conv, CUDA graph) in every step",
+                       "cuda_graph": not args.no_graph,
                        "l2": "inputs larger than L2: every step streams ~35 GB of weights (no flush needed)"},
             "prefill": prefill,
             "e2e": {"value": emitted / wall, "unit": "tok/s", "h2d_bytes_per_step": h2d,
