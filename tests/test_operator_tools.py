@@ -150,3 +150,14 @@ def test_quality_compare_runs():
     assert r["decode_identical"] == 1 and r["first_divergence"] == [1]
     assert r["prefill"]["n"] == 2 and r["prefill"]["kl_max"] == pytest.approx(0.0, abs=1e-12)
     assert r["top1_agree"] == 1.0
+
+
+def test_llm_boot_checks_refuse_to_start_without_a_b200(monkeypatch):
+    """GLM53_BOOT_CHECKS=1: the engine runs the boot checks before touching a device and refuses to start when one
+    fails (here: no CUDA device)."""
+    if torch.cuda.is_available():
+        pytest.skip("CPU-only expectation")
+    from glm53.api.offline import LLM, LLMOptions
+    monkeypatch.setenv("GLM53_BOOT_CHECKS", "1")
+    with pytest.raises(RuntimeError, match="boot checks failed"):
+        LLM(LLMOptions(model="tiny"))
