@@ -147,6 +147,11 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
             "# TYPE glm53_spec_decode_num_drafts_total counter", f"glm53_spec_decode_num_drafts_total {m['spec_drafts']}",
             "# TYPE glm53_spec_decode_num_accepted_tokens_total counter",
             f"glm53_spec_decode_num_accepted_tokens_total {m['spec_accepted']}",
+            "# TYPE glm53_spec_decode_num_windows_total counter",
+            f"glm53_spec_decode_num_windows_total {m['spec_windows']}",
+            "# TYPE glm53_spec_decode_num_accepted_tokens_per_pos counter",
+            *[f'glm53_spec_decode_num_accepted_tokens_per_pos{{position="{i}"}} {c}'
+              for i, c in enumerate(m["spec_accepted_per_pos"]) if i < 8],
             "# TYPE glm53_prefix_cache_hits_total counter", f"glm53_prefix_cache_hits_total {pc['hits']}",
             "# TYPE glm53_prefix_cache_queries_total counter", f"glm53_prefix_cache_queries_total {pc['queries']}",
             "# TYPE glm53_prefix_cached_tokens_total counter",

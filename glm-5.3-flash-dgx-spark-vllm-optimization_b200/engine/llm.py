@@ -116,7 +116,8 @@ class LLMEngine:
         self.done: dict[str, Request] = {}
         self._ids = itertools.count()
         self.metrics = {"prompt_tokens": 0, "generation_tokens": 0, "steps": 0, "spec_drafts": 0,
-                        "spec_accepted": 0, "prefix_cached_tokens": 0, "requests_finished": 0, "vtrim_cut": 0}
+                        "spec_accepted": 0, "prefix_cached_tokens": 0, "requests_finished": 0, "vtrim_cut": 0,
+                        "spec_windows": 0, "spec_accepted_per_pos": [0] * 16}
         # verify-trim records (drafted K, verified after the trim), most recent last
         import collections
         self.vtrim_records = collections.deque(maxlen=4096)
@@ -312,6 +313,10 @@ class LLMEngine:
             if drafts:
                 self.metrics["spec_drafts"] += len(drafts)
                 self.metrics["spec_accepted"] += n_acc
+                self.metrics["spec_windows"] += 1
+                per_pos = self.metrics["spec_accepted_per_pos"]
+                for i in range(min(n_acc, len(per_pos))):
+                    per_pos[i] += 1
                 r.accepted.append(n_acc)
                 r.adaptive.update(n_acc)
         # a state checkpoint interval boundary strictly inside a sequence's kept rows splits its commit there, so
