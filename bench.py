@@ -29,12 +29,12 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-PUBLISHED_DECODE_TOK_S = 99.44        # 2x GB10, TP=2, structured workload (accept 7.0/step)
-PUBLISHED_PREFILL_TOK_S = 3046.0      # cold 32k prefill
+PUBLISHED_DECODE_TOK_S = 99.44        # the reference's published figure: 2x GB10, TP=2, structured workload (accept 7.0/step)
+PUBLISHED_PREFILL_TOK_S = 3046.0      # the reference's published figure: cold 32k prefill
 METRIC = "bs1 decode ms/step & tok/s (K=7); 32k cold-prefill tok/s; at 1/2/4/8 B200"
 
 REFERENCE_UNAVAILABLE = ("the reference is a vLLM plugin/overlay kit for an arm64 GB10 (sm_121a) image pulled from "
-                         "GHCR; /root/reference has no installable package at its root and its fork package builds "
+                         "GHCR; the reference repository has no installable package at its root and its fork package builds "
                          "only sm_121a extensions against an unpublished vLLM build, so it cannot run on B200 here")
 
 
