@@ -56,8 +56,14 @@ def test_completion_stream_and_chat(client):
 
 
 def test_metrics(client):
+    client.post("/v1/completions", json={"prompt": list(range(20, 60)), "max_tokens": 24})
     txt = client.get("/metrics").text
     assert "glm53_generation_tokens_total" in txt and "glm53_spec_decode_num_drafts_total" in txt
+    vals = {l.split(" ")[0]: float(l.split(" ")[1]) for l in txt.splitlines() if l and not l.startswith("#")}
+    windows = vals["glm53_spec_decode_num_windows_total"]
+    per_pos = [vals[f'glm53_spec_decode_num_accepted_tokens_per_pos{{position="{i}"}}'] for i in range(8)]
+    assert windows > 0 and per_pos[0] <= windows
+    assert all(a >= b for a, b in zip(per_pos, per_pos[1:]))     # position i is accepted only after 0 .. i-1
 
 
 def test_too_long_is_400(client):
