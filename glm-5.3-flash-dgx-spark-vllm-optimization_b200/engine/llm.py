@@ -24,7 +24,7 @@ from enum import Enum
 import torch
 
 from .kv_manager import KVManager, OutOfPages, SeqCache, StateSlots, page_hash
-from .spec import AdaptiveK, greedy_accept
+from .spec import AdaptiveK, greedy_accept, rejection_sample_host
 
 
 @dataclass
@@ -82,7 +82,7 @@ class Request:
     cur: int = 0
     pos: int = 0                            # tokens committed to the caches
     drafts: list[int] = field(default_factory=list)
-    draft_logits: torch.Tensor | None = None
+    draft_probs: torch.Tensor | None = None   # sampled requests: q_i of each draft row [k, V]
     hidden: torch.Tensor | None = None
     adaptive: AdaptiveK | None = None
     first_token_time: float | None = None
@@ -277,7 +277,17 @@ class LLMEngine:
             self.metrics["vtrim_cut"] += k - n
             self.vtrim_records.append((k, n))
         r.drafts = drafts[:n]
-        r.draft_logits = lg[:n].clone() if r.params.temperature > 0 else None
+        r.draft_probs = None
+        p = r.params
+        if p.temperature > 0 and n and not self.cfg.force_accept:
+            # probabilistic drafts: row i is drawn from q_i, the drafter's distribution after the request's
+            # temperature / top-k / top-p, and q_i is what the verifier divides by (rows of the block drafter do not
+            # depend on one another's tokens, so each q_i is a valid proposal on its own)
+            q = torch.softmax(apply_filters(self.b.full_logits(lg[:n]).float() / p.temperature, p), -1)
+            g = torch.Generator(device=q.device)
+            g.manual_seed(lane_key(seed_key(r, len(r.output)), 1))        # a lane apart from the target's keys
+            r.drafts = torch.multinomial(q, 1, generator=g).view(-1).tolist()
+            r.draft_probs = q
 
     def _decode_step(self, reqs: list[Request]) -> list[RequestOutput]:
         spec = self.cfg.speculative and self.b.drafter is not None
@@ -370,9 +380,15 @@ class LLMEngine:
         k = len(drafts)
         if k == 0:
             return 0, [sample_token(full[0], p, seed_key(r, len(r.output)))]
-        dl = self.b.full_logits(r.draft_logits).float()[:k]
-        dp = torch.softmax(apply_filters(dl / p.temperature, p), -1)
+        dp = r.draft_probs[:k]
         dev = tp.device
+        if not tp.is_cuda:
+            # host tensors (the CPU test backend): the same standard rule in PyTorch
+            if self.cfg.block_verify:
+                raise NotImplementedError("block verification runs in the CUDA kernel only")
+            g = torch.Generator()
+            g.manual_seed(lane_key(seed_key(r, len(r.output)), 2))
+            return rejection_sample_host(tp, dp, drafts, g)
         acc = torch.zeros(1, dtype=torch.int32, device=dev)
         nxt = torch.zeros(1, k + 1, dtype=torch.int32, device=dev)
         K.C().rejection_sample(tp.view(1, k + 1, -1).contiguous(), dp.view(1, k, -1).contiguous(),
@@ -430,6 +446,17 @@ class LLMEngine:
 def seed_key(r: Request, index: int) -> int:
     base = r.params.seed if r.params.seed is not None else (hash(r.rid) & 0xFFFFFFFF)
     return (base * 1000003 + index) & ((1 << 63) - 1)
+
+
+def lane_key(key: int, lane: int) -> int:
+    """The seed of one independent use (lane) of a sampling key: the SplitMix64 finaliser (Steele, Lea, Flood 2014)
+    of key + lane x the 64-bit golden-ratio increment. Every output bit depends on every input bit, so lanes differ in
+    the low 32 bits too (the CPU generator keeps only those of a seed)."""
+    m = (1 << 64) - 1
+    z = (key + lane * 0x9E3779B97F4A7C15) & m
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & m
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & m
+    return (z ^ (z >> 31)) & ((1 << 63) - 1)
 
 
 def apply_filters(logits: torch.Tensor, p: SamplingParams) -> torch.Tensor:
