@@ -51,3 +51,24 @@ def test_rejection_sampler_emits_target_distribution(block):
         # acceptance rate of the first draft = sum_x min(p0, q0)
         rate = (acc >= 1).double().mean().item()
         assert abs(rate - torch.minimum(p[0], q[0]).sum().item()) < 0.01
+
+
+@pytest.mark.parametrize("block", [False, True])
+def test_engine_sampled_speculative_decoding(block):
+    """Sampled requests through the engine with the tiny proxy: drafts drawn from the drafter's filtered distribution,
+    verified by the CUDA rejection kernel (standard or block). Every request reaches max_tokens, windows accept
+    drafts, and the same seeds reproduce the same tokens."""
+    from glm53.api.offline import LLM, LLMOptions
+    from glm53.engine.llm import SamplingParams
+    llm = LLM(LLMOptions(model="tiny", max_seqs=2, max_model_len=512, prefill_chunk=128, page_size=64,
+                         checkpoints=0, k_fixed=4))
+    llm.engine.cfg.block_verify = block
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(16, 4096, (96,), generator=g).tolist() for _ in range(2)]
+    sp = [SamplingParams(max_tokens=24, temperature=1.0, top_p=0.95, seed=7 + i, ignore_eos=True) for i in range(2)]
+    a = llm.engine.generate(prompts, sp)
+    b = llm.engine.generate(prompts, sp)
+    assert [len(o) for o in a] == [24, 24]
+    assert a == b
+    m = llm.engine.metrics
+    assert m["spec_windows"] > 0 and m["spec_drafts"] > 0
