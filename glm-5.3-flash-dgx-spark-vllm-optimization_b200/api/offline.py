@@ -37,6 +37,8 @@ class LLMOptions:
     overrides: dict | None = None       # checkpoint name -> tensor or file replacing it at load
     override_sha256: dict | None = None  # checkpoint name -> expected sha256 of the override file
     vtrim_tau: float = 0.0              # verify trimming by drafter confidence (0: off)
+    block_verify: bool = False          # sampled requests: block verification instead of standard
+    mixed_prefill_chunk: int = 0        # prefill tokens per step while requests decode (0: the whole chunk)
 
 
 class LLM:
@@ -77,7 +79,8 @@ class LLM:
                           max_model_len=opts.max_model_len, prefill_chunk=opts.prefill_chunk,
                           speculative=opts.speculative, k_set=opts.k_set, k_fixed=opts.k_fixed,
                           force_accept=opts.force_accept, checkpoints=opts.checkpoints,
-                          cuda_graphs=opts.cuda_graphs, vtrim_tau=opts.vtrim_tau)
+                          cuda_graphs=opts.cuda_graphs, vtrim_tau=opts.vtrim_tau,
+                          block_verify=opts.block_verify, mixed_prefill_chunk=opts.mixed_prefill_chunk)
         self.engine = LLMEngine(self.backend, ec, eos=tuple(cfg.eos))
         self.tokenizer = ByteTokenizer(cfg.vocab)
         from ..utils.trace import maybe_attach

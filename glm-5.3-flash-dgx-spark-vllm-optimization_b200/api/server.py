@@ -14,10 +14,18 @@
                                drafts / accepted tokens, prefix-cache hits / queries, finished requests
 
 One engine thread owns the GPU and steps the engine whenever requests are pending; HTTP handlers hand requests to
-it through a queue and receive tokens through per-request queues.  The reference serves the same API through vLLM
-(code/kit/launcher/start.sh:2666-2684; Responses-input robustness: code/vllm-patches/responses_utils.patch).
+it through a queue and receive tokens through per-request queues. A request whose answer hits a stop string, or
+whose client goes away, is aborted in the engine so its slot and pages are freed. The reference serves the same API
+through vLLM (code/kit/launcher/start.sh:2666-2684; Responses-input robustness: code/vllm-patches/responses_utils.patch).
+
+Tensor parallel (one process per GPU under torchrun): every rank loads its shard and runs the same engine; rank 0
+serves HTTP and, before each engine step, broadcasts that step's new requests and aborts over a CPU (gloo) group
+(``ControlPlane``); the other ranks apply them in the same order and step, so the schedulers stay in lockstep and
+every step's collectives line up (the reference's head serves and its workers run headless:
+code/kit/launcher/start.sh:2741, :2821).
 
   python -m glm53.api.server --model tiny --port 8000
+  torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m glm53.api.server --model full --port 8000
 """
 
 from __future__ import annotations
@@ -40,16 +48,77 @@ except ImportError:  # pragma: no cover
     FastAPI = None
 
 
-class EngineLoop:
-    """Runs ``engine.step()`` on its own thread; thread-safe submission and per-request token streams."""
+class ControlPlane:
+    """Keeps the engines of all tensor-parallel ranks in lockstep. Rank 0 calls ``lead`` once per loop turn with the
+    requests and aborts that arrived since the last one; a non-empty plan (or, while idle, an empty heartbeat every
+    ``heartbeat_s`` so the followers' waits stay inside the group's timeout) is broadcast over ``group`` and applied
+    on every rank in the same order. Ranks > 0 run ``follow`` until rank 0 sends stop. With no group (one rank)
+    nothing is sent."""
 
-    def __init__(self, llm):
+    def __init__(self, engine, group=None, heartbeat_s: float = 1.0):
+        self.engine = engine
+        self.group = group
+        self.heartbeat_s = heartbeat_s
+        if group is not None:
+            import torch.distributed as dist
+            self.world = dist.get_world_size(group)
+        else:
+            self.world = 1
+        self._last = time.monotonic()
+
+    def _bcast(self, plan):
+        if self.world == 1:
+            return plan
+        import torch.distributed as dist
+        box = [plan]
+        dist.broadcast_object_list(box, src=0, group=self.group)
+        return box[0]
+
+    def _apply(self, plan) -> list[tuple[str, str]]:
+        errors = []
+        for rid, ids, params in plan["add"]:
+            try:
+                self.engine.add_request(ids, params, rid=rid)
+            except ValueError as e:                  # raised alike on every rank
+                errors.append((rid, str(e)))
+        for rid in plan["abort"]:
+            self.engine.abort(rid)
+        return errors
+
+    def lead(self, adds=(), aborts=(), stop: bool = False) -> tuple[list[tuple[str, str]], bool]:
+        """Rank 0: publish and apply one plan. Returns (rejected requests with their errors, whether to step)."""
+        if not adds and not aborts and not stop and not self.engine.has_work():
+            if self.world == 1 or time.monotonic() - self._last < self.heartbeat_s:
+                return [], False
+        plan = self._bcast({"add": list(adds), "abort": list(aborts), "stop": stop})
+        self._last = time.monotonic()
+        errors = self._apply(plan)
+        return errors, (not stop and self.engine.has_work())
+
+    def follow(self) -> None:
+        """Ranks > 0: apply rank 0's plans and step whenever there is work, until rank 0 sends stop."""
+        while True:
+            plan = self._bcast(None)
+            if plan["stop"]:
+                return
+            self._apply(plan)
+            if self.engine.has_work():
+                self.engine.step()
+
+
+class EngineLoop:
+    """Runs ``engine.step()`` on its own thread; thread-safe submission, aborts and per-request token streams."""
+
+    def __init__(self, llm, group=None):
         self.llm = llm
         self.engine = llm.engine
+        self.plane = ControlPlane(self.engine, group)
         self.inbox: queue.Queue = queue.Queue()
+        self.aborts: queue.Queue = queue.Queue()
         self.streams: dict[str, tuple[asyncio.AbstractEventLoop, asyncio.Queue]] = {}
         self.alive = True
         self.error: str | None = None
+        self._stop = False
         self.thread = threading.Thread(target=self._run, daemon=True)
         self.thread.start()
 
@@ -59,29 +128,48 @@ class EngineLoop:
         self.inbox.put((rid, prompt_ids, params))
         return rid
 
+    def abort(self, rid: str) -> None:
+        self.streams.pop(rid, None)
+        self.aborts.put(rid)
+
+    def close(self) -> None:
+        """Stop the loop (and the follower ranks) after the current step."""
+        self._stop = True
+        self.thread.join(timeout=30)
+
+    def _drain(self, q: queue.Queue, block: bool) -> list:
+        items = []
+        try:
+            while True:
+                items.append(q.get(block=block and not items, timeout=0.05))
+        except queue.Empty:
+            pass
+        return items
+
     def _run(self):
-        while self.alive:
-            try:
-                while True:
-                    rid, ids, params = self.inbox.get(block=not self.engine.has_work(), timeout=0.05)
-                    try:
-                        self.engine.add_request(ids, params, rid=rid)
-                    except ValueError as e:
-                        self._push(rid, {"error": str(e), "finished": True})
-            except queue.Empty:
-                pass
-            if not self.engine.has_work():
-                continue
-            try:
+        try:
+            while self.alive and not self._stop:
+                adds = self._drain(self.inbox, block=not self.engine.has_work())
+                aborts = self._drain(self.aborts, block=False)
+                errors, step = self.plane.lead(adds, aborts)
+                for rid, msg in errors:
+                    self._push(rid, {"error": msg, "finished": True})
+                if not step:
+                    continue
                 outs = self.engine.step()
-            except Exception as e:  # pragma: no cover - surfaced to clients and /health
-                self.error = repr(e)
-                self.alive = False
-                for rid in list(self.streams):
-                    self._push(rid, {"error": self.error, "finished": True})
-                raise
-            for o in outs:
-                self._push(o.rid, {"tokens": o.new_tokens, "finished": o.finished, "reason": o.finish_reason})
+                for o in outs:
+                    self._push(o.rid, {"tokens": o.new_tokens, "finished": o.finished, "reason": o.finish_reason})
+        except Exception as e:  # pragma: no cover - surfaced to clients and /health
+            self.error = repr(e)
+            for rid in list(self.streams):
+                self._push(rid, {"error": self.error, "finished": True})
+            raise
+        finally:
+            self.alive = False
+            try:
+                self.plane.lead(stop=True)           # release the follower ranks
+            except Exception:  # pragma: no cover - the group itself failed; followers end on its timeout
+                pass
 
     def _push(self, rid, item):
         s = self.streams.get(rid)
@@ -108,9 +196,11 @@ def _stop_strings(body) -> list[str]:
     return [s] if isinstance(s, str) else list(s)
 
 
-def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None, reasoning: bool = True):
+def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None, reasoning: bool = True,
+              group=None):
     """``api_key``: when set, /v1 routes need ``Authorization: Bearer <api_key>``.  ``reasoning``: split
-    ``<think>`` reasoning from the answer and apply stop strings to the answer only."""
+    ``<think>`` reasoning from the answer and apply stop strings to the answer only. ``group``: the CPU process
+    group of the tensor-parallel ranks (rank 0 serves; the others run ``ControlPlane.follow``)."""
     if FastAPI is None:
         raise RuntimeError("fastapi is not installed")
 
@@ -119,7 +209,8 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
             raise HTTPException(status_code=401, detail="invalid API key")
 
     app = FastAPI(dependencies=[Depends(auth)] if api_key else [])
-    loop_holder = {"engine": EngineLoop(llm)}
+    loop_holder = {"engine": EngineLoop(llm, group)}
+    app.state.engine_loop = loop_holder["engine"]
     tok = llm.tokenizer
 
     @app.get("/health")
@@ -168,13 +259,25 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
         obj = "chat.completion" if chat else "text_completion"
 
         async def events():
+            engine_done = False
+            try:
+                async for ev in _events():
+                    engine_done = ev.pop("engine_done")
+                    yield ev
+            finally:
+                if not engine_done:
+                    # a stop string ended the answer or the client went away: free the request's slot and pages
+                    loop_holder["engine"].abort(rid)
+
+        async def _events():
             text_so_far = ""
             toks = []
             while True:
                 item = await q.get()
                 if "error" in item:
-                    yield {"error": item["error"]}
+                    yield {"error": item["error"], "engine_done": True}
                     return
+                engine_finished = bool(item["finished"])
                 toks += item["tokens"]
                 text = tok.decode(toks)
                 delta = text[len(text_so_far):]
@@ -187,7 +290,7 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
                     item["finished"] = True
                 text_so_far = text
                 yield {"delta": delta, "tokens": item["tokens"], "finished": item["finished"], "reason": reason,
-                       "all": toks, "text": text}
+                       "all": toks, "text": text, "engine_done": engine_finished}
                 if item["finished"]:
                     return
 
@@ -295,17 +398,48 @@ def serve(argv=None):
     ap.add_argument("--max-seqs", type=int, default=4)
     ap.add_argument("--max-model-len", type=int, default=8192)
     ap.add_argument("--prefill-chunk", type=int, default=2048)
+    ap.add_argument("--mixed-prefill-chunk", type=int, default=0,
+                    help="prefill tokens per step while requests decode (0: the whole prefill chunk)")
+    ap.add_argument("--page-size", type=int, default=64)
+    ap.add_argument("--checkpoints", type=int, default=4, help="KDA state checkpoint slots for prefix caching")
     ap.add_argument("--no-spec", action="store_true")
+    ap.add_argument("--num-speculative-tokens", type=int, default=None,
+                    help="fixed draft length (default: adaptive over --k-set)")
+    ap.add_argument("--k-set", default="4,5,7", help="draft lengths of the adaptive K")
+    ap.add_argument("--block-verify", action="store_true", help="block verification for sampled requests")
+    ap.add_argument("--vtrim-tau", type=float, default=0.0, help="verify trimming by drafter confidence (0: off)")
+    ap.add_argument("--no-cuda-graphs", action="store_true")
     ap.add_argument("--served-model-name", default="glm-5.3-flash")
     ap.add_argument("--api-key", default=None, help="require Authorization: Bearer <key> on /v1 routes")
     ap.add_argument("--no-reasoning-parser", action="store_true")
     args = ap.parse_args(argv)
-    import uvicorn
+    from ..parallel import dist as D
     from .offline import LLM, LLMOptions
+    rank, _, world = D.init()
+    comm, group = None, None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        comm = D.NcclComm()
+        group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=60))
     llm = LLM(LLMOptions(model=args.model, max_seqs=args.max_seqs, max_model_len=args.max_model_len,
-                         prefill_chunk=args.prefill_chunk, speculative=not args.no_spec))
-    uvicorn.run(build_app(llm, args.served_model_name, api_key=args.api_key, reasoning=not args.no_reasoning_parser),
-                host=args.host, port=args.port, log_level="info")
+                         prefill_chunk=args.prefill_chunk, mixed_prefill_chunk=args.mixed_prefill_chunk,
+                         page_size=args.page_size, checkpoints=args.checkpoints, speculative=not args.no_spec,
+                         k_set=tuple(int(k) for k in args.k_set.split(",")), k_fixed=args.num_speculative_tokens,
+                         block_verify=args.block_verify, vtrim_tau=args.vtrim_tau,
+                         cuda_graphs=not args.no_cuda_graphs),
+              comm=comm, rank=rank, world=world)
+    if rank != 0:
+        ControlPlane(llm.engine, group).follow()
+        return
+    import uvicorn
+    app = build_app(llm, args.served_model_name, api_key=args.api_key, reasoning=not args.no_reasoning_parser,
+                    group=group)
+    try:
+        uvicorn.run(app, host=args.host, port=args.port, log_level="info")
+    finally:
+        app.state.engine_loop.close()
 
 
 if __name__ == "__main__":

@@ -16,6 +16,7 @@ with adaptive K (README.md:40, REPRODUCE.md:333).
 
 from __future__ import annotations
 
+import hashlib
 import itertools
 import time
 from dataclasses import dataclass, field
@@ -393,7 +394,7 @@ class LLMEngine:
         nxt = torch.zeros(1, k + 1, dtype=torch.int32, device=dev)
         K.C().rejection_sample(tp.view(1, k + 1, -1).contiguous(), dp.view(1, k, -1).contiguous(),
                                torch.tensor([drafts], dtype=torch.int32, device=dev),
-                               int(p.seed if p.seed is not None else hash(r.rid)) & ((1 << 62) - 1),
+                               int(p.seed if p.seed is not None else rid_key(r.rid)) & ((1 << 62) - 1),
                                torch.tensor([r.pos], dtype=torch.int64, device=dev), self.cfg.block_verify, acc, nxt,
                                None)
         n = int(acc.item())
@@ -443,8 +444,14 @@ class LLMEngine:
         return [self.done[rid].output for rid in rids]
 
 
+def rid_key(rid: str) -> int:
+    """A key of a request id that is the same in every process (Python's str hash is salted per process, and the
+    tensor-parallel ranks must draw the same samples for an unseeded request)."""
+    return int.from_bytes(hashlib.blake2b(rid.encode(), digest_size=8).digest(), "little")
+
+
 def seed_key(r: Request, index: int) -> int:
-    base = r.params.seed if r.params.seed is not None else (hash(r.rid) & 0xFFFFFFFF)
+    base = r.params.seed if r.params.seed is not None else (rid_key(r.rid) & 0xFFFFFFFF)
     return (base * 1000003 + index) & ((1 << 63) - 1)
 
 

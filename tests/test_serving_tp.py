@@ -1,0 +1,83 @@
+"""Tensor-parallel serving control plane on CPU (gloo, world size 2): rank 0 publishes each step's new requests and
+aborts, the follower applies them in the same order and steps, and both ranks' engines emit the same tokens (greedy,
+seeded and unseeded sampled requests; an unseeded request's noise key is the same in both processes), reject the
+same over-long request, abort the same request, and stop together. The server aborts a request whose answer hit a
+stop string."""
+
+import time
+
+from test_dist_cpu import _run
+
+
+def _plane(rank, world):
+    import torch.distributed as dist
+    from glm53.api.server import ControlPlane
+    from glm53.engine.llm import EngineConfig, LLMEngine, SamplingParams
+    from glm53.parallel import dist as D
+    from tests.fake_backend import FakeBackend
+    D.init(backend="gloo", timeout_s=30)
+    group = dist.new_group(backend="gloo")
+    eng = LLMEngine(FakeBackend(max_seqs=4, checkpoints=0),
+                    EngineConfig(max_seqs=4, page_size=16, num_pages=128, max_model_len=256, prefill_chunk=32,
+                                 cuda_graphs=False))
+    plane = ControlPlane(eng, group, heartbeat_s=0.05)
+    errors = []
+    if rank == 0:
+        first = [("a", list(range(20, 60)), SamplingParams(max_tokens=30)),
+                 ("b", list(range(30, 50)), SamplingParams(max_tokens=40, temperature=3.0)),
+                 ("c", list(range(40, 90)), SamplingParams(max_tokens=25, temperature=1.0, seed=5))]
+        err, step = plane.lead(first)
+        errors += err
+        n = 0
+        while step:
+            eng.step()
+            n += 1
+            late = [("d", list(range(16, 36)), SamplingParams(max_tokens=12)),
+                    ("long", list(range(300)), SamplingParams(max_tokens=8))] if n == 3 else []
+            err, step = plane.lead(late, ["c"] if n == 5 else [])
+            errors += err
+        time.sleep(0.2)
+        plane.lead()                                   # idle heartbeat
+        plane.lead(stop=True)
+    else:
+        plane.follow()
+    out = {rid: (r.output, r.finish_reason) for rid, r in eng.done.items()}
+    hist = {s: list(h) for s, h in eng.b.hist.items()}
+    dist.destroy_process_group()
+    return out, hist, errors
+
+
+def test_control_plane_keeps_ranks_in_lockstep():
+    res = _run(_plane, 2)
+    (ok0, p0), (ok1, p1) = res[0], res[1]
+    assert ok0, p0
+    assert ok1, p1
+    out0, hist0, err0 = p0
+    out1, hist1, _ = p1
+    assert out0 == out1 and hist0 == hist1
+    assert set(out0) == {"a", "b", "c", "d"}
+    assert out0["c"][1] == "abort" and out0["a"][1] == "length" and len(out0["b"][0]) == 40
+    assert [rid for rid, _ in err0] == ["long"]
+
+
+def test_stop_string_aborts_the_engine_request():
+    from fastapi.testclient import TestClient
+    from glm53.api.server import build_app
+    from glm53.engine.tokenizer import ByteTokenizer
+    from tests.fake_backend import reference_greedy
+    from test_api import FakeLLM
+    llm = FakeLLM()
+    tok = ByteTokenizer(512)
+    prompt = list(range(20, 60))
+    text = tok.decode(reference_greedy(prompt, 200))
+    stop = next(text[i:i + 2] for i in range(4, len(text) - 2) if text[i:i + 2].strip() and text[i:i + 2] not in
+                text[:i + 1])
+    with TestClient(build_app(llm, "glm-test", reasoning=False)) as c:
+        body = c.post("/v1/completions", json={"prompt": prompt, "max_tokens": 200, "stop": [stop]}).json()
+        assert body["choices"][0]["finish_reason"] == "stop"
+        t0 = time.time()
+        while llm.engine.running and time.time() - t0 < 5:
+            time.sleep(0.02)
+        assert not llm.engine.running
+        done = list(llm.engine.done.values())
+        assert done and done[-1].finish_reason == "abort" and len(done[-1].output) < 200
