@@ -81,3 +81,54 @@ def test_stop_string_aborts_the_engine_request():
         assert not llm.engine.running
         done = list(llm.engine.done.values())
         assert done and done[-1].finish_reason == "abort" and len(done[-1].output) < 200
+
+
+def _lost_peer(rank, world, who_leaves):
+    import datetime
+
+    import torch.distributed as dist
+    from glm53.api.server import ControlPlane
+    from glm53.engine.llm import EngineConfig, LLMEngine, SamplingParams
+    from glm53.parallel import dist as D
+    from tests.fake_backend import FakeBackend
+    D.init(backend="gloo", timeout_s=30)
+    group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=3))
+    eng = LLMEngine(FakeBackend(max_seqs=2, checkpoints=0),
+                    EngineConfig(max_seqs=2, page_size=16, num_pages=32, max_model_len=128, prefill_chunk=32,
+                                 cuda_graphs=False))
+    plane = ControlPlane(eng, group, heartbeat_s=0.05)
+    if rank == 0:
+        plane.lead([("a", list(range(20, 40)), SamplingParams(max_tokens=4))])
+        if who_leaves == 0:
+            return "left"                              # the leader goes away between steps
+        t0 = time.time()
+        try:
+            for _ in range(100):
+                plane.lead()
+                time.sleep(0.05)
+        except Exception as e:
+            return ("error", type(e).__name__, time.time() - t0)
+        return ("no error", None, time.time() - t0)
+    plane._bcast(None)                                 # the first plan
+    if who_leaves == 1:
+        return "left"                                  # the follower goes away between steps
+    t0 = time.time()
+    try:
+        plane.follow()
+    except Exception as e:
+        return ("error", type(e).__name__, time.time() - t0)
+    return ("no error", None, time.time() - t0)
+
+
+def test_follower_ends_when_the_leader_is_gone():
+    res = _run(_lost_peer, 2, 0, timeout=60)
+    ok, payload = res[1]
+    assert ok, payload
+    assert payload[0] == "error" and payload[2] < 20, payload
+
+
+def test_leader_ends_when_a_follower_is_gone():
+    res = _run(_lost_peer, 2, 1, timeout=60)
+    ok, payload = res[0]
+    assert ok, payload
+    assert payload[0] == "error" and payload[2] < 20, payload
