@@ -26,6 +26,7 @@ class LLMOptions:
     max_model_len: int = 8192
     page_size: int = 64
     kv_pages: int | None = None         # default: enough for max_seqs * max_model_len
+    kv_cache_bytes: int | None = None   # KV budget in bytes per GPU (sets kv_pages; the reference's --kv-cache-memory)
     prefill_chunk: int = 2048
     speculative: bool = True
     k_set: tuple[int, ...] = (4, 5, 7)
@@ -65,6 +66,8 @@ class LLM:
         t0 = time.time()
         self.weights = W.prepare(src, cfg, rank=rank, world=world, device=dev)
         self.load_s = time.time() - t0
+        if opts.kv_cache_bytes and not opts.kv_pages:
+            opts.kv_pages = max(1, int(opts.kv_cache_bytes // (cfg.kv_bytes_per_token() * opts.page_size)))
         pages = opts.kv_pages or max(64, opts.max_seqs * ((opts.max_model_len + opts.page_size - 1)
                                                            // opts.page_size + 2))
         kmax = max(opts.k_set) if opts.k_fixed is None else opts.k_fixed

@@ -401,6 +401,8 @@ def serve(argv=None):
     ap.add_argument("--mixed-prefill-chunk", type=int, default=0,
                     help="prefill tokens per step while requests decode (0: the whole prefill chunk)")
     ap.add_argument("--page-size", type=int, default=64)
+    ap.add_argument("--kv-cache-bytes", type=int, default=None,
+                    help="KV cache budget per GPU in bytes (default: enough for max-seqs x max-model-len)")
     ap.add_argument("--checkpoints", type=int, default=4, help="KDA state checkpoint slots for prefix caching")
     ap.add_argument("--no-spec", action="store_true")
     ap.add_argument("--num-speculative-tokens", type=int, default=None,
@@ -425,7 +427,8 @@ def serve(argv=None):
         group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=60))
     llm = LLM(LLMOptions(model=args.model, max_seqs=args.max_seqs, max_model_len=args.max_model_len,
                          prefill_chunk=args.prefill_chunk, mixed_prefill_chunk=args.mixed_prefill_chunk,
-                         page_size=args.page_size, checkpoints=args.checkpoints, speculative=not args.no_spec,
+                         page_size=args.page_size, kv_cache_bytes=args.kv_cache_bytes, checkpoints=args.checkpoints,
+                         speculative=not args.no_spec,
                          k_set=tuple(int(k) for k in args.k_set.split(",")), k_fixed=args.num_speculative_tokens,
                          block_verify=args.block_verify, vtrim_tau=args.vtrim_tau,
                          cuda_graphs=not args.no_cuda_graphs),

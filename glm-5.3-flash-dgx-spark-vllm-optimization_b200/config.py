@@ -107,6 +107,13 @@ class ModelConfig:
     def moe_layers(self) -> list[int]:
         return [i for i, k in enumerate(self.mlp_kinds) if k == "moe"]
 
+    def kv_bytes_per_token(self) -> float:
+        """Device bytes per token slot of the paged caches, summed over the MLA/DSA layers: the fp8 latent and its
+        fp32 scale, the bf16 rope key, and the token's share of its pool's fp8 index key and fp32 scale. The same on
+        every tensor-parallel rank (the latent cache is not split by heads)."""
+        per_layer = self.kv_lora + 4 + 2 * max(self.qk_rope, 1) + (self.index_dim + 4) / self.kpool
+        return len(self.mla_layers()) * per_layer
+
     def validate(self, tp: int = 1) -> None:
         assert len(self.layer_kinds) == len(self.mlp_kinds)
         assert all(k in ("kda", "mla") for k in self.layer_kinds)

@@ -166,3 +166,12 @@ def test_host_codec_matches_format_oracle():
     assert torch.equal(C.exl3_codebook_cpu().view(torch.int16), exl3.codebook().view(torch.int16))
     tr, _, _ = exl3.random_linear(512, 256, generator=torch.Generator().manual_seed(3))
     assert torch.equal(C.exl3_decode_cpu(tr, 4).view(torch.int16), exl3.unpack(tr).view(torch.int16))
+
+
+def test_kv_bytes_per_token_of_the_full_model():
+    """fp8 latent 512 + fp32 scale 4 + the bf16 rope-key column 2 (the full model's MLA has no rope part; the cache
+    keeps one placeholder column) + pooled fp8 index key share (128 + 4) / 4, over 11 MLA layers: 6,061 bytes."""
+    from glm53.config import full_config
+    c = full_config()
+    assert len(c.mla_layers()) == 11
+    assert c.kv_bytes_per_token() == 11 * (c.kv_lora + 4 + 2 * max(c.qk_rope, 1) + (c.index_dim + 4) / c.kpool) == 6061

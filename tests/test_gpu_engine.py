@@ -71,3 +71,14 @@ def test_decode_checkpoints_split_commits_stay_exact():
     before = llm.engine.metrics["prefix_cached_tokens"]
     llm.engine.generate([follow], SamplingParams(max_tokens=4, ignore_eos=True))
     assert llm.engine.metrics["prefix_cached_tokens"] - before > len(prompt)
+
+
+def test_kv_budget_in_bytes_sizes_the_page_pool():
+    """kv_cache_bytes sets the page pool from the configuration's bytes per token, which equals what the runtime
+    allocates per token slot."""
+    from glm53.utils.longctx import kv_bytes_per_token
+    budget = 4 << 20
+    llm = _llm(kv_cache_bytes=budget)
+    bpt = llm.cfg.kv_bytes_per_token()
+    assert abs(kv_bytes_per_token(llm.backend.rt) - bpt) <= 1
+    assert llm.engine.cfg.num_pages == int(budget // (bpt * 64))
