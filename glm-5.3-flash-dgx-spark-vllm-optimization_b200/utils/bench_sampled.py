@@ -98,8 +98,8 @@ def main(argv=None):
     from ..api.offline import LLM, LLMOptions
     from ..engine.llm import SamplingParams
     llm = LLM(LLMOptions(model=args.model, max_seqs=1, max_model_len=args.prompt_len + args.max_tokens + 64,
-                         prefill_chunk=min(8192, args.prompt_len), speculative=True, checkpoints=0))
-    llm.engine.cfg.block_verify = args.block_verify
+                         prefill_chunk=min(8192, args.prompt_len), speculative=True, checkpoints=0,
+                         block_verify=args.block_verify))
     g = torch.Generator().manual_seed(args.seed_base)
     prompts = [torch.randint(16, llm.cfg.vocab, (args.prompt_len,), generator=g).tolist()
                for _ in range(args.seeds)]
