@@ -390,7 +390,7 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
     return app
 
 
-def serve(argv=None):
+def build_parser() -> argparse.ArgumentParser:
     ap = argparse.ArgumentParser(description="OpenAI-compatible GLM-5.3-Flash server on B200")
     ap.add_argument("--model", default="tiny")
     ap.add_argument("--host", default="127.0.0.1")
@@ -414,9 +414,24 @@ def serve(argv=None):
     ap.add_argument("--served-model-name", default="glm-5.3-flash")
     ap.add_argument("--api-key", default=None, help="require Authorization: Bearer <key> on /v1 routes")
     ap.add_argument("--no-reasoning-parser", action="store_true")
-    args = ap.parse_args(argv)
+    return ap
+
+
+def options_from_args(args):
+    """The engine options of a parsed command line."""
+    from .offline import LLMOptions
+    return LLMOptions(model=args.model, max_seqs=args.max_seqs, max_model_len=args.max_model_len,
+                      prefill_chunk=args.prefill_chunk, mixed_prefill_chunk=args.mixed_prefill_chunk,
+                      page_size=args.page_size, kv_cache_bytes=args.kv_cache_bytes, checkpoints=args.checkpoints,
+                      speculative=not args.no_spec, k_set=tuple(int(k) for k in args.k_set.split(",")),
+                      k_fixed=args.num_speculative_tokens, block_verify=args.block_verify,
+                      vtrim_tau=args.vtrim_tau, cuda_graphs=not args.no_cuda_graphs)
+
+
+def serve(argv=None):
+    args = build_parser().parse_args(argv)
     from ..parallel import dist as D
-    from .offline import LLM, LLMOptions
+    from .offline import LLM
     rank, _, world = D.init()
     comm, group = None, None
     if world > 1:
@@ -425,24 +440,25 @@ def serve(argv=None):
         import torch.distributed as dist
         comm = D.NcclComm()
         group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=60))
-    llm = LLM(LLMOptions(model=args.model, max_seqs=args.max_seqs, max_model_len=args.max_model_len,
-                         prefill_chunk=args.prefill_chunk, mixed_prefill_chunk=args.mixed_prefill_chunk,
-                         page_size=args.page_size, kv_cache_bytes=args.kv_cache_bytes, checkpoints=args.checkpoints,
-                         speculative=not args.no_spec,
-                         k_set=tuple(int(k) for k in args.k_set.split(",")), k_fixed=args.num_speculative_tokens,
-                         block_verify=args.block_verify, vtrim_tau=args.vtrim_tau,
-                         cuda_graphs=not args.no_cuda_graphs),
-              comm=comm, rank=rank, world=world)
-    if rank != 0:
-        ControlPlane(llm.engine, group).follow()
-        return
-    import uvicorn
-    app = build_app(llm, args.served_model_name, api_key=args.api_key, reasoning=not args.no_reasoning_parser,
-                    group=group)
+    llm = LLM(options_from_args(args), comm=comm, rank=rank, world=world)
     try:
-        uvicorn.run(app, host=args.host, port=args.port, log_level="info")
+        if rank != 0:
+            ControlPlane(llm.engine, group).follow()
+        else:
+            import uvicorn
+            app = build_app(llm, args.served_model_name, api_key=args.api_key,
+                            reasoning=not args.no_reasoning_parser, group=group)
+            try:
+                uvicorn.run(app, host=args.host, port=args.port, log_level="info")
+            finally:
+                app.state.engine_loop.close()
     finally:
-        app.state.engine_loop.close()
+        # graphs that hold collectives are released before the process group, or the exit waits on them
+        llm.backend._graphs.clear()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
 
 
 if __name__ == "__main__":

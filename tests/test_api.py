@@ -116,3 +116,16 @@ def test_api_key():
     with TestClient(app) as c:
         assert c.get("/v1/models").status_code == 401
         assert c.get("/v1/models", headers={"Authorization": "Bearer sekret"}).status_code == 200
+
+
+def test_server_flags_map_to_engine_options():
+    from glm53.api.server import build_parser, options_from_args
+    args = build_parser().parse_args(["--model", "full", "--num-speculative-tokens", "7", "--block-verify",
+                                      "--kv-cache-bytes", "16106127360", "--k-set", "3,5", "--checkpoints", "2",
+                                      "--mixed-prefill-chunk", "1024", "--no-cuda-graphs", "--vtrim-tau", "0.2"])
+    o = options_from_args(args)
+    assert (o.model, o.k_fixed, o.block_verify, o.kv_cache_bytes, o.k_set, o.checkpoints) == (
+        "full", 7, True, 16106127360, (3, 5), 2)
+    assert o.mixed_prefill_chunk == 1024 and not o.cuda_graphs and o.vtrim_tau == 0.2 and o.speculative
+    d = options_from_args(build_parser().parse_args([]))
+    assert d.k_fixed is None and d.k_set == (4, 5, 7) and not d.block_verify and d.cuda_graphs
