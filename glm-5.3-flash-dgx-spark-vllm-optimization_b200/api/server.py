@@ -51,28 +51,35 @@ except ImportError:  # pragma: no cover
 class ControlPlane:
     """Keeps the engines of all tensor-parallel ranks in lockstep. Rank 0 calls ``lead`` once per loop turn with the
     requests and aborts that arrived since the last one; a non-empty plan (or, while idle, an empty heartbeat every
-    ``heartbeat_s`` so the followers' waits stay inside the group's timeout) is broadcast over ``group`` and applied
-    on every rank in the same order. Ranks > 0 run ``follow`` until rank 0 sends stop. With no group (one rank)
-    nothing is sent."""
+    ``heartbeat_s`` so the followers' waits stay inside ``timeout_s``) goes to every rank (``parallel/control.py``:
+    shared memory on one node, or the CPU group) and is applied on every rank in the same order. Ranks > 0 run
+    ``follow`` until rank 0 sends stop. With no group (one rank) nothing is sent."""
 
-    def __init__(self, engine, group=None, heartbeat_s: float = 1.0):
+    def __init__(self, engine, group=None, heartbeat_s: float = 1.0, timeout_s: float = 60.0,
+                 transport: str = "shm"):
         self.engine = engine
-        self.group = group
         self.heartbeat_s = heartbeat_s
+        self.world, self.rank, self.chan = 1, 0, None
         if group is not None:
             import torch.distributed as dist
-            self.world = dist.get_world_size(group)
-        else:
-            self.world = 1
+            from ..parallel.control import GlooChannel, ShmChannel
+            self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+            if self.world > 1:
+                self.chan = ShmChannel(group, timeout_s) if transport == "shm" else GlooChannel(group)
         self._last = time.monotonic()
 
     def _bcast(self, plan):
-        if self.world == 1:
+        if self.chan is None:
             return plan
-        import torch.distributed as dist
-        box = [plan]
-        dist.broadcast_object_list(box, src=0, group=self.group)
-        return box[0]
+        if self.rank == 0:
+            self.chan.publish(plan)
+            return plan
+        return self.chan.receive()
+
+    def close(self) -> None:
+        if self.chan is not None:
+            self.chan.close()
+            self.chan = None
 
     def _apply(self, plan) -> list[tuple[str, str]]:
         errors = []
@@ -97,13 +104,16 @@ class ControlPlane:
 
     def follow(self) -> None:
         """Ranks > 0: apply rank 0's plans and step whenever there is work, until rank 0 sends stop."""
-        while True:
-            plan = self._bcast(None)
-            if plan["stop"]:
-                return
-            self._apply(plan)
-            if self.engine.has_work():
-                self.engine.step()
+        try:
+            while True:
+                plan = self._bcast(None)
+                if plan["stop"]:
+                    return
+                self._apply(plan)
+                if self.engine.has_work():
+                    self.engine.step()
+        finally:
+            self.close()
 
 
 class EngineLoop:
@@ -168,8 +178,9 @@ class EngineLoop:
             self.alive = False
             try:
                 self.plane.lead(stop=True)           # release the follower ranks
-            except Exception:  # pragma: no cover - the group itself failed; followers end on its timeout
+            except Exception:  # pragma: no cover - a follower is gone; the others end on their timeout
                 pass
+            self.plane.close()
 
     def _push(self, rid, item):
         s = self.streams.get(rid)

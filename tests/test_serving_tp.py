@@ -6,10 +6,12 @@ stop string."""
 
 import time
 
+import pytest
+
 from test_dist_cpu import _run
 
 
-def _plane(rank, world):
+def _plane(rank, world, transport):
     import torch.distributed as dist
     from glm53.api.server import ControlPlane
     from glm53.engine.llm import EngineConfig, LLMEngine, SamplingParams
@@ -20,7 +22,7 @@ def _plane(rank, world):
     eng = LLMEngine(FakeBackend(max_seqs=4, checkpoints=0),
                     EngineConfig(max_seqs=4, page_size=16, num_pages=128, max_model_len=256, prefill_chunk=32,
                                  cuda_graphs=False))
-    plane = ControlPlane(eng, group, heartbeat_s=0.05)
+    plane = ControlPlane(eng, group, heartbeat_s=0.05, transport=transport)
     errors = []
     if rank == 0:
         first = [("a", list(range(20, 60)), SamplingParams(max_tokens=30)),
@@ -41,14 +43,16 @@ def _plane(rank, world):
         plane.lead(stop=True)
     else:
         plane.follow()
+    plane.close()
     out = {rid: (r.output, r.finish_reason) for rid, r in eng.done.items()}
     hist = {s: list(h) for s, h in eng.b.hist.items()}
     dist.destroy_process_group()
     return out, hist, errors
 
 
-def test_control_plane_keeps_ranks_in_lockstep():
-    res = _run(_plane, 2)
+@pytest.mark.parametrize("transport", ["shm", "gloo"])
+def test_control_plane_keeps_ranks_in_lockstep(transport):
+    res = _run(_plane, 2, transport)
     (ok0, p0), (ok1, p1) = res[0], res[1]
     assert ok0, p0
     assert ok1, p1
@@ -96,7 +100,7 @@ def _lost_peer(rank, world, who_leaves):
     eng = LLMEngine(FakeBackend(max_seqs=2, checkpoints=0),
                     EngineConfig(max_seqs=2, page_size=16, num_pages=32, max_model_len=128, prefill_chunk=32,
                                  cuda_graphs=False))
-    plane = ControlPlane(eng, group, heartbeat_s=0.05)
+    plane = ControlPlane(eng, group, heartbeat_s=0.05, timeout_s=3)
     if rank == 0:
         plane.lead([("a", list(range(20, 40)), SamplingParams(max_tokens=4))])
         if who_leaves == 0:
@@ -132,3 +136,27 @@ def test_leader_ends_when_a_follower_is_gone():
     ok, payload = res[0]
     assert ok, payload
     assert payload[0] == "error" and payload[2] < 20, payload
+
+
+def _big_and_many(rank, world):
+    import torch.distributed as dist
+    from glm53.parallel import dist as D
+    from glm53.parallel.control import ShmChannel
+    D.init(backend="gloo", timeout_s=30)
+    group = dist.new_group(backend="gloo")
+    ch = ShmChannel(group, timeout_s=10, capacity=1 << 12)
+    msgs = [{"i": i, "blob": list(range(i * 300))} for i in range(40)]       # up to ~40 KB: many parts
+    got = []
+    for m in msgs:
+        if rank == 0:
+            ch.publish(m)
+        else:
+            got.append(ch.receive())
+    ch.close()
+    dist.destroy_process_group()
+    return got == msgs if rank else True
+
+
+def test_shm_channel_multi_part_messages_arrive_in_order():
+    res = _run(_big_and_many, 3)
+    assert all(ok and payload for ok, payload in res.values()), res
