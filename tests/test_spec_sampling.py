@@ -111,3 +111,16 @@ def test_greedy_draft_against_drafter_softmax_is_biased():
     exp = [float(v) * n for v in p[0]]
     assert scipy_stats.chisquare(drawn, exp).pvalue > 1e-4
     assert scipy_stats.chisquare(greedy, exp).pvalue < 1e-6
+
+
+def test_seed_lanes_differ_in_the_bits_the_cpu_generator_keeps():
+    """The CPU generator seeds from the low 32 bits only: the lanes of one key, and the keys of consecutive
+    positions, must differ there (a flip of a high bit would give the draft and residual draws one stream)."""
+    from glm53.engine.llm import lane_key, rid_key
+    keys = [k * 1000003 + i for k in (0, 7, 10_000) for i in range(64)]
+    low = {lane_key(k, lane) & 0xFFFFFFFF for k in keys for lane in (1, 2)}
+    assert len(low) == 2 * len(keys)
+    a = torch.Generator().manual_seed(lane_key(5, 1))
+    b = torch.Generator().manual_seed(lane_key(5, 2))
+    assert not torch.equal(torch.rand(8, generator=a), torch.rand(8, generator=b))
+    assert rid_key("cmpl-1") == rid_key("cmpl-1") != rid_key("cmpl-2")
