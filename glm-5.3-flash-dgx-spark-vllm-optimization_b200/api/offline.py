@@ -46,6 +46,8 @@ class LLM:
     def __init__(self, opts: LLMOptions | None = None, comm=None, rank: int = 0, world: int = 1, **kw):
         opts = opts or LLMOptions(**kw)
         self.opts = opts
+        from ..utils import switches
+        switches.enforce()                                        # malformed GLM53_* values stop the start
         if os.environ.get("GLM53_BOOT_CHECKS", "0") == "1":      # per-rank boot assertions (collective)
             from ..utils import boot_checks
             self.boot_report = boot_checks.run()

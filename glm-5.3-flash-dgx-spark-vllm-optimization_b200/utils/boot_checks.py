@@ -105,6 +105,8 @@ def run(group=None, selftest: bool = True) -> dict:
     group must call run() (it is the only collective step and comes first, so a rank whose device check fails
     still takes part in it)."""
     rep = {"env": check_env(group)}
+    from .switches import check as check_switches
+    rep["switches"] = check_switches()
     rep["device"] = check_device()
     if rep["device"]["ok"]:
         rep["extension"] = check_extension()
