@@ -160,3 +160,55 @@ def _big_and_many(rank, world):
 def test_shm_channel_multi_part_messages_arrive_in_order():
     res = _run(_big_and_many, 3)
     assert all(ok and payload for ok, payload in res.values()), res
+
+
+def _loop_and_follower(rank, world):
+    import asyncio
+
+    import torch.distributed as dist
+    from glm53.api.server import ControlPlane, EngineLoop
+    from glm53.engine.llm import EngineConfig, LLMEngine, SamplingParams
+    from glm53.parallel import dist as D
+    from tests.fake_backend import FakeBackend
+
+    class L:
+        engine = LLMEngine(FakeBackend(max_seqs=4, checkpoints=0),
+                           EngineConfig(max_seqs=4, page_size=16, num_pages=128, max_model_len=256,
+                                        prefill_chunk=32, cuda_graphs=False))
+    D.init(backend="gloo", timeout_s=30)
+    group = dist.new_group(backend="gloo")
+    if rank != 0:
+        ControlPlane(L.engine, group, timeout_s=20).follow()
+    else:
+        el = EngineLoop(L, group)
+
+        async def one(prompt, params):
+            q = asyncio.Queue()
+            rid = el.submit(prompt, params, asyncio.get_running_loop(), q)
+            toks = []
+            while True:
+                item = await q.get()
+                toks += item.get("tokens", [])
+                if item.get("finished"):
+                    return rid, toks
+
+        async def many():
+            return await asyncio.gather(
+                one(list(range(20, 60)), SamplingParams(max_tokens=20)),
+                one(list(range(25, 45)), SamplingParams(max_tokens=30, temperature=2.0)),
+                one(list(range(30, 90)), SamplingParams(max_tokens=15, temperature=2.0, seed=9)))
+        got = asyncio.run(many())
+        time.sleep(1.5)                                # idle: heartbeats keep the follower waiting
+        el.close()
+        assert [len(t) for _, t in got] == [20, 30, 15]
+    out = {rid: r.output for rid, r in L.engine.done.items()}
+    dist.destroy_process_group()
+    return out
+
+
+def test_engine_loop_drives_a_follower_rank():
+    res = _run(_loop_and_follower, 2, timeout=90)
+    (ok0, out0), (ok1, out1) = res[0], res[1]
+    assert ok0, out0
+    assert ok1, out1
+    assert out0 == out1 and len(out0) == 3
