@@ -168,7 +168,8 @@ class EngineLoop:
                     continue
                 outs = self.engine.step()
                 for o in outs:
-                    self._push(o.rid, {"tokens": o.new_tokens, "finished": o.finished, "reason": o.finish_reason})
+                    self._push(o.rid, {"tokens": o.new_tokens, "finished": o.finished, "reason": o.finish_reason,
+                                       "logprobs": o.new_logprobs})
         except Exception as e:  # pragma: no cover - surfaced to clients and /health
             self.error = repr(e)
             for rid in list(self.streams):
@@ -192,12 +193,18 @@ class EngineLoop:
             self.streams.pop(rid, None)
 
 
-def _params(body: dict, tok) -> SamplingParams:
+def _params(body: dict, tok, chat: bool = False) -> SamplingParams:
+    """Sampling fields of a request. Log-probabilities: completions take ``logprobs: n`` (top-n alternatives); chat
+    takes ``logprobs: true`` with ``top_logprobs: n``."""
     stop_ids = tuple(body.get("stop_token_ids") or ())
+    if chat:
+        lp = int(body.get("top_logprobs") or 0) if body.get("logprobs") else None
+    else:
+        lp = int(body["logprobs"]) if body.get("logprobs") is not None else None
     return SamplingParams(max_tokens=int(body.get("max_tokens") or 64), temperature=float(body.get("temperature", 0.0)),
                           top_p=float(body.get("top_p", 1.0)), top_k=int(body.get("top_k", 0) or 0),
                           seed=body.get("seed"), stop_token_ids=stop_ids,
-                          ignore_eos=bool(body.get("ignore_eos", False)))
+                          ignore_eos=bool(body.get("ignore_eos", False)), logprobs=lp)
 
 
 def _stop_strings(body) -> list[str]:
@@ -262,7 +269,7 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
         ]
         return PlainTextResponse("\n".join(lines) + "\n")
 
-    async def _run(prompt_ids, params, stops, chat: bool, stream: bool, body: dict):
+    async def _run(prompt_ids, params, stops, chat: bool, stream: bool, body: dict, raw: bool = False):
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
         rid = loop_holder["engine"].submit(prompt_ids, params, loop, q)
@@ -282,7 +289,7 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
 
         async def _events():
             text_so_far = ""
-            toks = []
+            toks, lps = [], []
             while True:
                 item = await q.get()
                 if "error" in item:
@@ -290,6 +297,7 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
                     return
                 engine_finished = bool(item["finished"])
                 toks += item["tokens"]
+                lps += item.get("logprobs") or []
                 text = tok.decode(toks)
                 delta = text[len(text_so_far):]
                 reason = item.get("reason")
@@ -301,11 +309,31 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
                     item["finished"] = True
                 text_so_far = text
                 yield {"delta": delta, "tokens": item["tokens"], "finished": item["finished"], "reason": reason,
-                       "all": toks, "text": text, "engine_done": engine_finished}
+                       "all": toks, "text": text, "engine_done": engine_finished,
+                       "new_lps": item.get("logprobs"), "lps": lps}
                 if item["finished"]:
                     return
 
-        def choice(delta=None, text=None, reason=None, toks=None):
+        def fmt_lps(toks, lps):
+            if params.logprobs is None or lps is None:
+                return None
+            if chat:
+                def entry(t, lp):
+                    s_ = tok.decode([t])
+                    return {"token": s_, "logprob": lp, "bytes": list(s_.encode())}
+                return {"content": [{**entry(t, lp), "top_logprobs": [entry(k, v) for k, v in top.items()]}
+                                    for t, (lp, top) in zip(toks, lps)]}
+            return {"tokens": [tok.decode([t]) for t in toks], "token_logprobs": [lp for lp, _ in lps],
+                    "top_logprobs": [{tok.decode([k]): v for k, v in top.items()} for _, top in lps]}
+
+        def choice(delta=None, text=None, reason=None, toks=None, lps=None):
+            out = _choice(delta, text, reason, toks)
+            lp = fmt_lps(toks or [], lps)
+            if lp is not None:
+                out["logprobs"] = lp
+            return out
+
+        def _choice(delta=None, text=None, reason=None, toks=None):
             if chat:
                 if delta is not None:
                     return {"index": 0, "delta": {"role": "assistant", "content": delta}, "finish_reason": reason}
@@ -334,7 +362,7 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
                     chunk = {"id": rid, "object": obj + (".chunk" if chat else ""), "created": created,
                              "model": model_name,
                              "choices": [choice(delta=ev["delta"], reason=ev["reason"] if ev["finished"] else None,
-                                                toks=ev["tokens"])]}
+                                                toks=ev["tokens"], lps=ev["new_lps"])]}
                     yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(sse(), media_type="text/event-stream")
@@ -345,10 +373,38 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
             last = ev
         usage = {"prompt_tokens": len(prompt_ids), "completion_tokens": len(last["all"]) if last else 0}
         usage["total_tokens"] = usage["prompt_tokens"] + usage["completion_tokens"]
-        return JSONResponse({"id": rid, "object": obj, "created": created, "model": model_name,
-                             "choices": [choice(text=last["text"] if last else "", reason=last["reason"] if last
-                                                else "stop", toks=last["all"] if last else [])],
-                             "usage": usage})
+        res = {"id": rid, "object": obj, "created": created, "model": model_name,
+               "choices": [choice(text=last["text"] if last else "", reason=last["reason"] if last else "stop",
+                                  toks=last["all"] if last else [], lps=last["lps"] if last else [])],
+               "usage": usage}
+        return res if raw else JSONResponse(res)
+
+    async def _run_n(prompt_ids, params, stops, chat: bool, body: dict, n: int):
+        """n completions of one prompt (non-streaming): request i samples with seed + i when a seed is given."""
+        from dataclasses import replace
+        outs = await asyncio.gather(*[
+            _run(prompt_ids, replace(params, seed=None if params.seed is None else params.seed + i), stops, chat,
+                 False, body, raw=True) for i in range(n)])
+        choices = []
+        for i, o in enumerate(outs):
+            c = o["choices"][0]
+            c["index"] = i
+            choices.append(c)
+        comp = sum(o["usage"]["completion_tokens"] for o in outs)
+        return JSONResponse({**outs[0], "choices": choices,
+                             "usage": {"prompt_tokens": len(prompt_ids), "completion_tokens": comp,
+                                       "total_tokens": len(prompt_ids) + comp}})
+
+    async def _dispatch(prompt_ids, params, stops, chat: bool, body: dict):
+        n = int(body.get("n") or 1)
+        stream = bool(body.get("stream"))
+        if n < 1:
+            raise HTTPException(status_code=400, detail="n must be >= 1")
+        if n > 1:
+            if stream:
+                raise HTTPException(status_code=400, detail="n > 1 is not supported with stream")
+            return await _run_n(prompt_ids, params, stops, chat, body, n)
+        return await _run(prompt_ids, params, stops, chat, stream, body)
 
     @app.post("/v1/completions")
     async def completions(req: Request):
@@ -360,7 +416,7 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
             ids = tok.encode("".join(str(p) for p in prompt))
         else:
             ids = tok.encode(str(prompt))
-        return await _run(ids, _params(body, tok), _stop_strings(body), False, bool(body.get("stream")), body)
+        return await _dispatch(ids, _params(body, tok), _stop_strings(body), False, body)
 
     @app.post("/v1/chat/completions")
     async def chat(req: Request):
@@ -368,7 +424,7 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
         msgs = [m for m in body.get("messages", []) if isinstance(m, dict)]     # skip unknown input items
         ids = tok.encode(tok.apply_chat_template(msgs, reasoning_effort=body.get("reasoning_effort"),
                                                  tools=body.get("tools")))
-        return await _run(ids, _params(body, tok), _stop_strings(body), True, bool(body.get("stream")), body)
+        return await _dispatch(ids, _params(body, tok, chat=True), _stop_strings(body), True, body)
 
     @app.post("/v1/responses")
     async def responses(req: Request):

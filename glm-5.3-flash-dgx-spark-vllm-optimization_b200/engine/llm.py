@@ -37,6 +37,8 @@ class SamplingParams:
     seed: int | None = None
     stop_token_ids: tuple[int, ...] = ()
     ignore_eos: bool = False
+    logprobs: int | None = None            # per emitted token: its log-probability and the top-n alternatives
+                                           # (raw model distribution, before temperature and filters)
 
 
 @dataclass
@@ -90,6 +92,8 @@ class Request:
     finish_reason: str | None = None
     cached_tokens: int = 0
     accepted: list = field(default_factory=list)
+    logprobs: list = field(default_factory=list)    # per output token: (logprob, {token: logprob} top-n)
+    _new_lp: list | None = None
 
     @property
     def tokens(self) -> list[int]:
@@ -103,6 +107,7 @@ class RequestOutput:
     finished: bool
     finish_reason: str | None
     output: list[int]
+    new_logprobs: list | None = None      # aligned with new_tokens when the request asked for logprobs
 
 
 class LLMEngine:
@@ -242,6 +247,11 @@ class LLMEngine:
             self._checkpoint(r)
         if finishing:
             toks = self._sample_rows(logits, [r for r, _ in finishing])
+            want = [i for i, (r, _) in enumerate(finishing) if r.params.logprobs is not None]
+            if want:
+                lps = self._logprobs(logits[want], [toks[i] for i in want], [finishing[i][0] for i in want])
+                for i, lp in zip(want, lps):
+                    finishing[i][0]._new_lp = [lp]
             for i, (r, row_idx) in enumerate(finishing):
                 r.state = State.RUNNING
                 r.first_token_time = time.time()
@@ -319,6 +329,8 @@ class LLMEngine:
                 n_acc, new = self._sampled_accept(r, logits[row:row + n_rows], drafts)
             keeps.append(n_acc + 1)
             r._new = new
+            if r.params.logprobs is not None:
+                r._new_lp = self._logprobs(logits[row:row + len(new)], new, [r] * len(new))
             r._last_row = row + n_acc
             row += n_rows
             if drafts:
@@ -372,6 +384,20 @@ class LLMEngine:
         if ck is not None:
             self.b.save_state(r.slot, r.cur, ck.slot)
 
+    def _logprobs(self, logits: torch.Tensor, tokens: list[int], reqs: list[Request]) -> list:
+        """(log-probability of each row's token, its top-n alternatives) from the rows' full logits."""
+        lp = torch.log_softmax(self.b.full_logits(logits).float(), -1)
+        n = max((r.params.logprobs or 0) for r in reqs)
+        chosen = lp.gather(1, torch.tensor(tokens, device=lp.device).view(-1, 1)).view(-1).tolist()
+        top = torch.topk(lp, n, -1) if n > 0 else None
+        tv = top.values.tolist() if top is not None else None
+        ti = top.indices.tolist() if top is not None else None
+        out = []
+        for i, r in enumerate(reqs):
+            k = r.params.logprobs or 0
+            out.append((chosen[i], {ti[i][j]: tv[i][j] for j in range(k)} if k else {}))
+        return out
+
     def _sampled_accept(self, r: Request, logits: torch.Tensor, drafts: list[int]):
         """Rejection sampling of one request's window (CUDA kernel; standard or block verification)."""
         from ..ops import kernels as K
@@ -404,9 +430,14 @@ class LLMEngine:
     # ------------------------------------------------------------------------------------------------ outputs
     def _emit(self, r: Request, new: list[int]) -> RequestOutput:
         emitted = []
-        for t in new:
+        lp, r._new_lp = r._new_lp, None
+        new_lp = [] if lp is not None else None
+        for i, t in enumerate(new):
             emitted.append(t)
             r.output.append(t)
+            if lp is not None:
+                r.logprobs.append(lp[i])
+                new_lp.append(lp[i])
             self.metrics["generation_tokens"] += 1
             if (t in self.eos and not r.params.ignore_eos) or t in r.params.stop_token_ids:
                 r.finish_reason = "stop"
@@ -416,7 +447,7 @@ class LLMEngine:
                 break
         if r.finish_reason is not None:
             self._finish(r)
-        return RequestOutput(r.rid, emitted, r.state == State.FINISHED, r.finish_reason, list(r.output))
+        return RequestOutput(r.rid, emitted, r.state == State.FINISHED, r.finish_reason, list(r.output), new_lp)
 
     def _finish(self, r: Request) -> None:
         if r in self.running:

@@ -129,3 +129,26 @@ def test_server_flags_map_to_engine_options():
     assert o.mixed_prefill_chunk == 1024 and not o.cuda_graphs and o.vtrim_tau == 0.2 and o.speculative
     d = options_from_args(build_parser().parse_args([]))
     assert d.k_fixed is None and d.k_set == (4, 5, 7) and not d.block_verify and d.cuda_graphs
+
+
+def test_logprobs_and_n(client):
+    """Completions: logprobs=n gives per-token log-probabilities and top-n alternatives; chat: logprobs with
+    top_logprobs; n > 1 returns n choices (seed + i each), refused with stream."""
+    prompt = list(range(20, 60))
+    body = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 6, "logprobs": 2}).json()
+    lp = body["choices"][0]["logprobs"]
+    assert len(lp["token_logprobs"]) == 6 and all(v <= 0 for v in lp["token_logprobs"])
+    assert all(len(t) <= 2 for t in lp["top_logprobs"]) and len(lp["tokens"]) == 6
+    body = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}],
+                                                     "max_tokens": 4, "logprobs": True, "top_logprobs": 3}).json()
+    content = body["choices"][0]["logprobs"]["content"]
+    assert len(content) == 4 and all(len(c["top_logprobs"]) == 3 for c in content)
+    assert "logprobs" not in client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 3}).json()[
+        "choices"][0]
+    body = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 5, "n": 3, "temperature": 1.0,
+                                                "seed": 4}).json()
+    assert [c["index"] for c in body["choices"]] == [0, 1, 2] and body["usage"]["completion_tokens"] == 15
+    greedy = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 5, "n": 2}).json()
+    assert greedy["choices"][0]["token_ids"] == greedy["choices"][1]["token_ids"] == reference_greedy(prompt, 5)
+    r = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 5, "n": 2, "stream": True})
+    assert r.status_code == 400

@@ -213,3 +213,28 @@ def test_mixed_prefill_chunk_caps_prefill_beside_decodes():
         e.step()
     assert e.done[a].output == reference_greedy(list(range(20, 50)), 40)
     assert e.done[b].output == reference_greedy(list(range(100, 200)), 8)
+
+
+@pytest.mark.parametrize("spec", [False, True])
+def test_logprobs_follow_each_emitted_token(spec):
+    """logprobs=n: every emitted token carries its log-probability under the model's raw distribution and the top-n
+    alternatives, with speculative windows (several tokens per step) and without."""
+    import math
+    from tests.fake_backend import next_tok, onehot
+    eng = _engine(speculative=spec)
+    prompt = list(range(20, 50))
+    rid = eng.add_request(prompt, SamplingParams(max_tokens=17, logprobs=2, ignore_eos=True))
+    while rid not in eng.done:
+        eng.step()
+    r = eng.done[rid]
+    assert len(r.logprobs) == len(r.output) == 17
+    hist = list(prompt)
+    for t, (lp, top) in zip(r.output, r.logprobs):
+        ref = torch.log_softmax(onehot(next_tok(hist)), -1)
+        assert math.isclose(lp, ref[t].item(), abs_tol=1e-5)
+        assert len(top) == 2 and max(top, key=top.get) == t == next_tok(hist)
+        hist.append(t)
+    rid = eng.add_request(prompt, SamplingParams(max_tokens=5))
+    while rid not in eng.done:
+        eng.step()
+    assert eng.done[rid].logprobs == []
