@@ -10,6 +10,7 @@
                                into message.tool_calls (api/parsers.py)
   POST /v1/responses           Responses API: input (string or items; unknown item types skipped), instructions,
                                max_output_tokens; output items reasoning / message / function_call
+  POST /tokenize, /detokenize  token ids of a prompt or of chat messages; text of token ids
   GET  /metrics                Prometheus text: requests running / waiting, prompt / generation tokens, speculative
                                drafts / accepted tokens, prefix-cache hits / queries, finished requests
 
@@ -417,6 +418,23 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
         else:
             ids = tok.encode(str(prompt))
         return await _dispatch(ids, _params(body, tok), _stop_strings(body), False, body)
+
+    @app.post("/tokenize")
+    async def tokenize(req: Request):
+        """Token ids of a prompt, or of chat messages after the chat template (``messages``)."""
+        body = await req.json()
+        if "messages" in body:
+            msgs = [m for m in body.get("messages") or [] if isinstance(m, dict)]
+            ids = tok.encode(tok.apply_chat_template(msgs, reasoning_effort=body.get("reasoning_effort"),
+                                                     tools=body.get("tools")))
+        else:
+            ids = tok.encode(str(body.get("prompt", "")))
+        return {"tokens": ids, "count": len(ids), "max_model_len": llm.engine.cfg.max_model_len}
+
+    @app.post("/detokenize")
+    async def detokenize(req: Request):
+        body = await req.json()
+        return {"prompt": tok.decode([int(t) for t in body.get("tokens") or []])}
 
     @app.post("/v1/chat/completions")
     async def chat(req: Request):

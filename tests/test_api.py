@@ -152,3 +152,11 @@ def test_logprobs_and_n(client):
     assert greedy["choices"][0]["token_ids"] == greedy["choices"][1]["token_ids"] == reference_greedy(prompt, 5)
     r = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 5, "n": 2, "stream": True})
     assert r.status_code == 400
+
+
+def test_tokenize_detokenize(client):
+    r = client.post("/tokenize", json={"prompt": "hello B200"}).json()
+    assert r["count"] == len(r["tokens"]) > 0 and r["max_model_len"] == 2048
+    assert client.post("/detokenize", json={"tokens": r["tokens"]}).json()["prompt"] == "hello B200"
+    chat = client.post("/tokenize", json={"messages": [{"role": "user", "content": "hi"}]}).json()
+    assert chat["count"] > 2
