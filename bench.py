@@ -224,6 +224,25 @@ def main():
     except Exception as e:  # pragma: no cover
         launches = {"error": str(e)[:200]}
 
+    # ---------------- correctness check (untimed): greedy tokens with real verification ----------------
+    # acceptance is no longer forced: every emitted token is the target's own greedy choice, so the tokens of
+    # this check should agree across GPU counts; the smallest top-1 / top-2 log-probability gap says how close a
+    # position was to a tie (a divergence between GPU counts at a near-tie is rounding, not a fault)
+    eng.abort(rid)
+    eng.cfg.force_accept = False
+    cprompt = torch.randint(0, cfg.vocab, (256,), generator=torch.Generator().manual_seed(99)).tolist()
+    cid = eng.add_request(cprompt, SamplingParams(max_tokens=16, ignore_eos=True, logprobs=2))
+    run_until(lambda: cid in eng.done)
+    creq = eng.done[cid]
+    ctoks = list(creq.output[:16])
+    gaps = []
+    for lp, top in creq.logprobs[:16]:
+        v = sorted(top.values(), reverse=True)
+        gaps.append(v[0] - v[1] if len(v) > 1 else float("inf"))
+    import hashlib
+    check = {"greedy_tokens": ctoks, "sha16": hashlib.sha256(json.dumps(ctoks).encode()).hexdigest()[:16],
+             "min_top2_gap": min(gaps) if gaps else None, "prompt": "256 uniform random ids (seed 99)"}
+
     if rank == 0:
         out = {
             "metric": METRIC, "value": tok_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -245,6 +264,7 @@ def main():
             "gpu_launches": (launches.get("per_step_ours", 0) * args.steps) if isinstance(launches, dict) else None,
             "launch_detail": launches,
             "clocks": ck,
+            "check": check,
             "load_s": t_load,
         }
         print(json.dumps(out))

@@ -194,18 +194,30 @@ class EngineLoop:
             self.streams.pop(rid, None)
 
 
-def _params(body: dict, tok, chat: bool = False) -> SamplingParams:
+def _params(body: dict, tok, chat: bool = False, engine=None) -> SamplingParams:
     """Sampling fields of a request. Log-probabilities: completions take ``logprobs: n`` (top-n alternatives); chat
-    takes ``logprobs: true`` with ``top_logprobs: n``."""
-    stop_ids = tuple(body.get("stop_token_ids") or ())
-    if chat:
-        lp = int(body.get("top_logprobs") or 0) if body.get("logprobs") else None
-    else:
-        lp = int(body["logprobs"]) if body.get("logprobs") is not None else None
-    return SamplingParams(max_tokens=int(body.get("max_tokens") or 64), temperature=float(body.get("temperature", 0.0)),
-                          top_p=float(body.get("top_p", 1.0)), top_k=int(body.get("top_k", 0) or 0),
-                          seed=body.get("seed"), stop_token_ids=stop_ids,
-                          ignore_eos=bool(body.get("ignore_eos", False)), logprobs=lp)
+    takes ``logprobs: true`` with ``top_logprobs: n``.  A field of the wrong type or out of range is a 400 here
+    (``engine.check_params``), so it never reaches the engine thread."""
+    try:
+        stop_ids = tuple(int(t) for t in (body.get("stop_token_ids") or ()))
+        if chat:
+            lp = int(body.get("top_logprobs") or 0) if body.get("logprobs") else None
+        else:
+            lp = int(body["logprobs"]) if body.get("logprobs") is not None else None
+        sp = SamplingParams(max_tokens=int(body.get("max_tokens") or 64),
+                            temperature=float(body.get("temperature", 0.0)), top_p=float(body.get("top_p", 1.0)),
+                            top_k=int(body.get("top_k", 0) or 0), seed=body.get("seed"), stop_token_ids=stop_ids,
+                            ignore_eos=bool(body.get("ignore_eos", False)), logprobs=lp)
+        if engine is not None:
+            engine.check_params(sp)
+    except (TypeError, ValueError) as e:
+        raise _bad_request(str(e)) from e
+    return sp
+
+
+def _bad_request(detail: str):
+    from fastapi import HTTPException
+    return HTTPException(status_code=400, detail=detail)
 
 
 def _stop_strings(body) -> list[str]:
@@ -216,10 +228,14 @@ def _stop_strings(body) -> list[str]:
 
 
 def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None, reasoning: bool = True,
-              group=None):
+              group=None, max_n: int | None = None):
     """``api_key``: when set, /v1 routes need ``Authorization: Bearer <api_key>``.  ``reasoning``: split
     ``<think>`` reasoning from the answer and apply stop strings to the answer only. ``group``: the CPU process
-    group of the tensor-parallel ranks (rank 0 serves; the others run ``ControlPlane.follow``)."""
+    group of the tensor-parallel ranks (rank 0 serves; the others run ``ControlPlane.follow``).  ``max_n``: most
+    choices one request may ask for (default: the engine's sequence slots), so one request cannot queue an
+    unbounded number of engine requests."""
+    if max_n is None:
+        max_n = max(1, llm.engine.cfg.max_seqs)
     if FastAPI is None:
         raise RuntimeError("fastapi is not installed")
 
@@ -399,8 +415,8 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
     async def _dispatch(prompt_ids, params, stops, chat: bool, body: dict):
         n = int(body.get("n") or 1)
         stream = bool(body.get("stream"))
-        if n < 1:
-            raise HTTPException(status_code=400, detail="n must be >= 1")
+        if not 1 <= n <= max_n:
+            raise HTTPException(status_code=400, detail=f"n must be in [1, {max_n}]")
         if n > 1:
             if stream:
                 raise HTTPException(status_code=400, detail="n > 1 is not supported with stream")
@@ -417,7 +433,7 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
             ids = tok.encode("".join(str(p) for p in prompt))
         else:
             ids = tok.encode(str(prompt))
-        return await _dispatch(ids, _params(body, tok), _stop_strings(body), False, body)
+        return await _dispatch(ids, _params(body, tok, engine=llm.engine), _stop_strings(body), False, body)
 
     @app.post("/tokenize")
     async def tokenize(req: Request):
@@ -442,7 +458,7 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
         msgs = [m for m in body.get("messages", []) if isinstance(m, dict)]     # skip unknown input items
         ids = tok.encode(tok.apply_chat_template(msgs, reasoning_effort=body.get("reasoning_effort"),
                                                  tools=body.get("tools")))
-        return await _dispatch(ids, _params(body, tok, chat=True), _stop_strings(body), True, body)
+        return await _dispatch(ids, _params(body, tok, chat=True, engine=llm.engine), _stop_strings(body), True, body)
 
     @app.post("/v1/responses")
     async def responses(req: Request):
@@ -451,7 +467,7 @@ def build_app(llm, model_name: str = "glm-5.3-flash", api_key: str | None = None
         ids = tok.encode(tok.apply_chat_template(msgs, reasoning_effort=(body.get("reasoning") or {}).get("effort"),
                                                  tools=body.get("tools")))
         cbody = dict(body, max_tokens=body.get("max_output_tokens") or body.get("max_tokens") or 64)
-        res = await _run(ids, _params(cbody, tok), _stop_strings(body), True, False, cbody)
+        res = await _run(ids, _params(cbody, tok, engine=llm.engine), _stop_strings(body), True, False, cbody)
         data = json.loads(res.body)
         msg = data["choices"][0]["message"]
         output = []

@@ -110,7 +110,7 @@ __global__ void __launch_bounds__(128) mla_decode_kernel(MlaAttnArgs a) {
   const int r = blockIdx.x, ht = blockIdx.y, sp = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
   const int h0 = ht * 16;
-  const int count = a.sel_count[r];
+  const int count = max(0, min(a.sel_count[r], a.max_sel));   // a row never reads past its max_sel selections
   const int chunk = (count + a.splits - 1) / a.splits;
   const int kbeg = sp * chunk, kend = min(count, kbeg + chunk);
 
@@ -372,21 +372,29 @@ std::mutex g_noalloc_mu;
 
 // Device address of the scratch array on the current device (looked up once per device).  A host-side use of the
 // symbol name itself would give a host stand-in address, not device memory, so the address is always taken from
-// cudaGetSymbolAddress with the device current.
-cudaError_t noalloc_scratch(float** out) {
+// cudaGetSymbolAddress with the device current.  Returns 0, the cudaError_t of a failed cudaGetDevice (or
+// cudaErrorInvalidDevice past the table), or G53_NOALLOC_ERR_SYMBOL when only the symbol lookup failed.
+int noalloc_scratch(float** out) {
   int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= kMaxDevices) return (int)cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
   if (g_noalloc_ptr[dev] == nullptr) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g53_mla_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) return e != cudaSuccess ? e : cudaErrorInvalidSymbol;
+    if (cudaGetSymbolAddress(&p, g53_mla_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();                       // the failed lookup's error is reported as ERR_SYMBOL, not left sticky
+      return G53_NOALLOC_ERR_SYMBOL;
+    }
     g_noalloc_ptr[dev] = static_cast<float*>(p);
   }
   *out = g_noalloc_ptr[dev];
-  return cudaSuccess;
+  return 0;
+}
+
+// the (L, rope) pairs the CUDA-core kernel is instantiated for
+bool noalloc_supported(int L, int rope) {
+  return (L == 512 && rope == 0) || (L == 128 && rope == 32) || (L == 128 && rope == 0);
 }
 }  // namespace
 
@@ -394,13 +402,16 @@ extern "C" int g53_mla_decode_noalloc(const void* q_lat, const void* q_pe, int64
                                       const void* kv_cache, const float* kv_scale, const void* kpe_cache,
                                       const int* sel, const int* sel_count, int max_sel, int R, int H, int L, int rope,
                                       float sm_scale, int splits, void* o_lat, void* stream) {
-  if (R < 1 || H < 1 || L < 1 || splits < 1) return (int)cudaErrorInvalidValue;
+  if (R < 1 || H < 1 || L < 1 || splits < 1 || splits > 16 || max_sel < 1) return (int)cudaErrorInvalidValue;
+  if (!noalloc_supported(L, rope)) return (int)cudaErrorInvalidValue;
+  if (!q_lat || !kv_cache || !kv_scale || !sel || !sel_count || !o_lat) return (int)cudaErrorInvalidValue;
+  if (rope > 0 && (!q_pe || !kpe_cache)) return (int)cudaErrorInvalidValue;   // the rope kernel reads both
   const int64_t partial = (int64_t)R * splits * H * L;
   const int64_t stats = (int64_t)R * splits * H * 2;
   if (partial > G53_MLA_NOALLOC_MAX_PARTIAL || stats > G53_MLA_NOALLOC_MAX_STATS) return G53_NOALLOC_ERR_TOO_LARGE;
   float* scratch = nullptr;
-  const cudaError_t e = noalloc_scratch(&scratch);
-  if (e != cudaSuccess) return G53_NOALLOC_ERR_SYMBOL;
+  const int se = noalloc_scratch(&scratch);
+  if (se != 0) return se;
   MlaAttnArgs a{};
   a.q_lat = static_cast<const __nv_bfloat16*>(q_lat);
   a.q_pe = static_cast<const __nv_bfloat16*>(q_pe);

@@ -12,6 +12,11 @@
 //     G53_MLA_NOALLOC_MAX_STATS floats of softmax statistics (R * splits * H * 2); larger problems are rejected
 //     with G53_NOALLOC_ERR_TOO_LARGE before anything is launched.  Every GPU that loads the library keeps this
 //     array (about 4.1 MB) for the life of the process.
+//   * arguments are checked on the host before any launch: null inputs or outputs, a rope kernel (rope > 0)
+//     without q_pe / kpe_cache, an (L, rope) pair other than (512, 0), (128, 0), (128, 32), splits outside
+//     [1, 16] or max_sel < 1 return cudaErrorInvalidValue.  A row's sel_count is clamped to max_sel on the device.
+//   * a failed device lookup returns its cudaError_t (for example cudaErrorInvalidDevice); only a failed symbol
+//     lookup returns G53_NOALLOC_ERR_SYMBOL.
 //   * nothing in the scratch has to start at zero: each call writes every partial it later reads.
 //   * all calls on a device share the one array, so calls that can overlap on the GPU (different streams, or
 //     different host threads, without ordering between them) race and corrupt each other's results; order them

@@ -28,6 +28,9 @@ from .kv_manager import KVManager, OutOfPages, SeqCache, StateSlots, page_hash
 from .spec import AdaptiveK, greedy_accept, rejection_sample_host
 
 
+MAX_LOGPROBS = 20      # most alternatives per token a request may ask for (the OpenAI API's top_logprobs limit)
+
+
 @dataclass
 class SamplingParams:
     max_tokens: int = 64
@@ -135,12 +138,33 @@ class LLMEngine:
             raise ValueError("empty prompt")
         if len(prompt) + params.max_tokens > self.cfg.max_model_len:
             raise ValueError(f"prompt + max_tokens exceeds max_model_len {self.cfg.max_model_len}")
+        self.check_params(params)
         rid = rid or f"req-{next(self._ids)}"
         r = Request(rid, list(prompt), params)
         r.adaptive = AdaptiveK(self.cfg.k_set, self.cfg.ema_alpha, self.cfg.k_margin, fixed=self.cfg.k_fixed)
         self.waiting.append(r)
         self.metrics["prompt_tokens"] += len(prompt)
         return rid
+
+    def check_params(self, params: SamplingParams) -> None:
+        """Reject sampling fields that a step could not serve, before the request is queued: a bad value raised
+        later inside ``step()`` (``topk`` over more alternatives than the vocabulary, say) would fail every request
+        in flight, not just this one."""
+        vocab = getattr(self.b, "vocab", None)
+        if params.max_tokens < 1:
+            raise ValueError("max_tokens must be >= 1")
+        if params.logprobs is not None:
+            cap = MAX_LOGPROBS if vocab is None else min(MAX_LOGPROBS, vocab)
+            if not 0 <= params.logprobs <= cap:
+                raise ValueError(f"logprobs must be in [0, {cap}]")
+        if params.temperature < 0:
+            raise ValueError("temperature must be >= 0")
+        if not 0.0 < params.top_p <= 1.0:
+            raise ValueError("top_p must be in (0, 1]")
+        if params.top_k < 0:
+            raise ValueError("top_k must be >= 0")
+        if vocab is not None and any(not 0 <= t < vocab for t in params.stop_token_ids):
+            raise ValueError("stop_token_ids must be token ids of the vocabulary")
 
     def abort(self, rid: str) -> None:
         for q in (self.waiting, self.running):

@@ -37,8 +37,9 @@ HBLOCK = 128
 
 @lru_cache(maxsize=1)
 def codebook() -> torch.Tensor:
-    """fp16 value of each of the 65536 states (computed once; the sum of two fp16 is exact in fp64, so rounding
-    the fp64 sum to fp16 is the single fp16 rounding the format specifies)."""
+    """The codebook as a table: the fp16 value of every 16-bit state, built once.  The two halves are added in
+    float64, which holds any sum of two fp16 numbers without loss, and the sum is then cast to fp16: one cast, as
+    the format prescribes."""
     s = torch.arange(65536, dtype=torch.int64)
     x = ((s * MCG_MUL) & 0xFFFFFFFF)
     x = (x & MCG_MASK) ^ MCG_XOR

@@ -44,15 +44,25 @@ def topk_logprobs(logits: torch.Tensor, k: int) -> list[dict]:
 
 
 def topk_kl(pa: dict, pb: dict) -> float:
-    """KL(A || B) over the union of the two top-k sets; a token missing from one set gets that set's smallest
-    log-probability minus one (the floor), then both are renormalised over the union."""
-    keys = set(pa) | set(pb)
-    floor = min(min(pa.values()), min(pb.values())) - 1.0
-    la = {x: pa.get(x, floor) for x in keys}
-    lb = {x: pb.get(x, floor) for x in keys}
-    za = math.log(sum(math.exp(v) for v in la.values()))
-    zb = math.log(sum(math.exp(v) for v in lb.values()))
-    return sum(math.exp(la[x] - za) * ((la[x] - za) - (lb[x] - zb)) for x in keys)
+    """Divergence of run B from run A at one position, from each run's saved top-k {token: log-probability}.
+
+    Definition: let U be the union of the two saved token sets and f one nat below the smallest saved
+    log-probability of either run.  Each run's distribution over U takes its saved value where it has one and f
+    elsewhere (a token outside a run's top-k is less likely than any it kept), renormalised over U; the statistic is
+    KL(A_U || B_U).  When both runs saved the whole vocabulary this is the exact KL.  The floor rule is the one the
+    reference's quality tooling uses, kept so that numbers from either side compare."""
+    toks = sorted(set(pa) | set(pb))
+    f = min(min(pa.values()), min(pb.values())) - 1.0
+    a = torch.tensor([pa.get(t, f) for t in toks], dtype=torch.float64)
+    b = torch.tensor([pb.get(t, f) for t in toks], dtype=torch.float64)
+    la, lb = a - torch.logsumexp(a, 0), b - torch.logsumexp(b, 0)
+    return float((la.exp() * (la - lb)).sum())
+
+
+def top1(p: dict) -> int:
+    """The most likely saved token (lowest id among ties)."""
+    best = max(p.values())
+    return min(t for t, v in p.items() if v == best)
 
 
 def first_divergence(a: list[int], b: list[int]) -> int | None:
@@ -84,7 +94,7 @@ def compare_runs(A: dict, B: dict, start: int = 0) -> dict:
             pa = {int(k): v for k, v in pa.items()}
             pb = {int(k): v for k, v in pb.items()}
             kls.append(topk_kl(pa, pb))
-            agree += max(pa, key=pa.get) == max(pb, key=pb.get)
+            agree += top1(pa) == top1(pb)
             n += 1
     out = {"decode_identical": same, "decode_streams": len(A["completions"]),
            "first_divergence": divs, "prefill": summarize(kls), "top1_agree": agree / n if n else None}

@@ -160,3 +160,35 @@ def test_tokenize_detokenize(client):
     assert client.post("/detokenize", json={"tokens": r["tokens"]}).json()["prompt"] == "hello B200"
     chat = client.post("/tokenize", json={"messages": [{"role": "user", "content": "hi"}]}).json()
     assert chat["count"] > 2
+
+
+def test_bad_sampling_fields_are_400_and_server_keeps_serving(client):
+    """A request whose sampling fields the engine could not serve (top_logprobs beyond the cap, a negative
+    temperature, n beyond the slot count, a non-numeric field) is refused with 400 before it reaches the engine
+    thread; requests after it are served normally."""
+    prompt = list(range(20, 60))
+    bad = [
+        ("/v1/chat/completions", {"messages": [{"role": "user", "content": "hi"}], "max_tokens": 2,
+                                  "logprobs": True, "top_logprobs": 10 ** 6}),
+        ("/v1/completions", {"prompt": prompt, "max_tokens": 2, "logprobs": 10 ** 6}),
+        ("/v1/completions", {"prompt": prompt, "max_tokens": 2, "logprobs": -1}),
+        ("/v1/completions", {"prompt": prompt, "max_tokens": 2, "temperature": -0.5}),
+        ("/v1/completions", {"prompt": prompt, "max_tokens": 2, "top_p": 0.0}),
+        ("/v1/completions", {"prompt": prompt, "max_tokens": 2, "top_k": "many"}),
+        ("/v1/completions", {"prompt": prompt, "max_tokens": 2, "n": 10 ** 6}),
+    ]
+    for route, body in bad:
+        r = client.post(route, json=body)
+        assert r.status_code == 400, (route, body, r.status_code)
+    assert client.get("/health").json()["status"] == "ok"
+    body = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 6}).json()
+    assert body["choices"][0]["token_ids"] == reference_greedy(prompt, 6)
+
+
+def test_engine_rejects_bad_sampling_fields_per_request():
+    """add_request raises ValueError (reported for that request alone) for logprobs beyond the cap."""
+    from glm53.engine.llm import MAX_LOGPROBS, SamplingParams
+    eng = FakeLLM().engine
+    with pytest.raises(ValueError):
+        eng.add_request([1, 2, 3], SamplingParams(max_tokens=2, logprobs=MAX_LOGPROBS + 1))
+    eng.add_request([1, 2, 3], SamplingParams(max_tokens=2, logprobs=MAX_LOGPROBS))

@@ -1,4 +1,4 @@
-"""Tensor parallelism on two GPUs (skipped with fewer): the fused reduction (partials pushed to the peers from the
+"""Tensor parallelism on 2, 4 and 8 GPUs (each world size skipped with fewer GPUs): the fused reduction (partials pushed to the peers from the
 projection's epilogue -- GEMV for decode windows, tcgen05 GEMM for prefill chunks -- and summed in rank order
 inside the next mHC kernel) gives the same logits as the NCCL all-reduce path, for a prefill chunk and for decode
 windows (GPU only)."""
@@ -45,14 +45,24 @@ def _worker(rank, world, port, result):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_fused_tp_matches_nccl_two_gpus():
+def _ngpu():
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_tp_matches_nccl(world):
+    if _ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     result = mp.Manager().dict()
-    mp.spawn(_worker, args=(2, 29541, result), nprocs=2, join=True)
-    assert len(result) == 2
-    # two ranks: a + b is the same fp32 sum in either order, so the paths agree bit for bit
-    assert max(result.values()) == 0.0, dict(result)
+    mp.spawn(_worker, args=(world, 29541 + world, result), nprocs=world, join=True)
+    assert len(result) == world
+    if world == 2:
+        # two ranks: a + b is the same fp32 sum in either order, so the paths agree bit for bit
+        assert max(result.values()) == 0.0, dict(result)
+    else:
+        # more ranks: the fused path sums in rank order, NCCL in its ring order -- fp32 rounding only
+        assert max(result.values()) < 5e-2, dict(result)
 
 
 def _push_worker(rank, world, port, result):
@@ -94,10 +104,12 @@ def _push_worker(rank, world, port, result):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_gemv_push_bulk_two_gpus():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_gemv_push_bulk(world):
+    if _ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     result = mp.Manager().dict()
-    mp.spawn(_push_worker, args=(2, 29547, result), nprocs=2, join=True)
-    assert len(result) == 2
+    mp.spawn(_push_worker, args=(world, 29557 + world, result), nprocs=world, join=True)
+    assert len(result) == world
     assert max(result.values()) == 0.0, dict(result)
