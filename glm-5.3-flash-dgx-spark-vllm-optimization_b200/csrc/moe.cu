@@ -174,52 +174,65 @@ __device__ __forceinline__ uint32_t dup_half(float v) {
   return b | (b << 16);
 }
 
-// the 8 masked products of lane's fragment.  The window extraction is spread over the ALU and FMA pipes (the
-// decode is bound by the ALU pipe): right shifts of whole words use the high half of an integer multiply, and the
-// lowest window uses s7 * C = cur * C - s3 * (C << 16) (mod 2^32) instead of masking cur.
-__device__ __forceinline__ void trellis_x8(uint32_t cur, uint32_t prev, uint32_t (&x)[8]) {
-  constexpr uint32_t C = 0xCBAC1FEDu, Cn = 0u - (C << 16);
-  const uint32_t v = __funnelshift_r(cur, prev, 20);     // bits [20, 52) of (prev:cur)
-  const uint32_t y = __umulhi(cur, 1u << 28);            // cur >> 4
-  const uint32_t s3 = __umulhi(cur, 1u << 16);           // cur >> 16
-  uint32_t s[7];
-  s[0] = __byte_perm(v, 0u, 0x4421);                     // bits [28, 44)
-  s[1] = __funnelshift_r(cur, prev, 24) & 0xffffu;       // bits [24, 40)
-  s[2] = v & 0xffffu;                                    // bits [20, 36)
-  s[3] = s3;
-  s[4] = __byte_perm(y, 0u, 0x4421);                     // bits [12, 28)
-  s[5] = __byte_perm(cur, 0u, 0x4421);                   // bits [8, 24)
-  s[6] = y & 0xffffu;                                    // bits [4, 20)
-#pragma unroll
-  for (int j = 0; j < 7; ++j) x[j] = ((s[j] * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;
-  x[7] = ((cur * C + s3 * Cn) & 0x8FFF8FFFu) ^ 0x3B603B60u;   // bits [0, 16)
+// ---------------------------------------------------------------------------------------------------------------
+// The 8 masked products of a lane's fragment, balanced over the two integer pipes.
+//
+// Measured on B200 (one warp instruction per SMSP per clock is issued): LOP3, PRMT, SHF and IMAD each retire 0.5
+// warp instructions per clock (LOP3 / PRMT / SHF on the ALU pipe, IMAD on the FMA-heavy pipe), IMAD.HI 0.25.  The
+// value of window b (stream bits [b, b + 16) counted from the LSB of the lane's word `cur`, with `prev` above it)
+// is x_b = (s_b * C & M) ^ X.  Any 32-bit t with s_b in its low half gives s_b * C = t * C - (t >> 16) * (C << 16)
+// (mod 2^32): the high half of t only adds (t >> 16) * C << 16 to the product.  And t >> 16 is itself the window
+// 16 bits further up, which the tile needs anyway, so a pair of windows (b, b + 16) costs one word t_b, one
+// extraction of s_{b+16} and three IMADs, instead of two extractions and two IMADs:
+//   pair (0, 16):  t = cur (free),                   s16 = prmt(cur)
+//   pair (8, 24):  t8 = prmt(cur, prev),              s24 = prmt(t8)
+//   pair (4, 20):  t4 = shf(prev:cur, 4),             s20 = prmt(t4)
+//   pair (12, 28): t12 = shf(prev:cur, 12),           s28 = prmt(t12)
+// Per word: 7 ALU extractions + 8 LOP3 on the ALU pipe, 12 IMADs on the FMA-heavy pipe (the previous all-ALU
+// extraction took 10 ALU operations plus two IMAD.HI).  Measured in isolation (decode + mma.sync, operands from
+// shared memory): 18.1 values per clock per SM against 12.8, bit-identical products.
+// Fragment order (value j = window b = 28 - 4j): a0 = {x0, x4, x1, x5}, a1 = {x2, x6, x3, x7}.
+// ---------------------------------------------------------------------------------------------------------------
+template <uint32_t SEL>
+__device__ __forceinline__ uint32_t prmt_(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "n"(SEL));
+  return r;
 }
 
-// one 16x16 trellis tile (two k16 steps) against 8 tokens' duplicated inputs b = {w0, w1, w2, w3}
-__device__ __forceinline__ void tile_mma(float (&c)[4], const uint32_t (&x)[8], const uint4& b) {
-  const uint32_t a0[4] = {x[0], x[4], x[1], x[5]};
-  const uint32_t a1[4] = {x[2], x[6], x[3], x[7]};
-  mma_f16_16816(c, a0, b.x, b.y);
-  mma_f16_16816(c, a1, b.z, b.w);
+template <uint32_t SH>
+__device__ __forceinline__ uint32_t shf_r_(uint32_t lo, uint32_t hi) {
+  uint32_t r;
+  asm("shf.r.wrap.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(lo), "r"(hi), "n"(SH));
+  return r;
 }
 
-// the same tile with the masked products written straight into the two A fragments in operand order
-// (a0 = {x0, x4, x1, x5}, a1 = {x2, x6, x3, x7}), so no value has to be moved into an operand register
+// (x & 0x8FFF8FFF) ^ 0x3B603B60 as one LOP3 (truth table 0x6a = (a & b) ^ c)
+__device__ __forceinline__ uint32_t mcg_mask_(uint32_t x) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, 0x8FFF8FFF, 0x3B603B60, 0x6a;" : "=r"(r) : "r"(x));
+  return r;
+}
+
 __device__ __forceinline__ void trellis_tile_mma(float (&c)[4], uint32_t cur, uint32_t prev, const uint4& b) {
   constexpr uint32_t C = 0xCBAC1FEDu, Cn = 0u - (C << 16);
-  const uint32_t v = __funnelshift_r(cur, prev, 20);
-  const uint32_t y = __umulhi(cur, 1u << 28);
-  const uint32_t s3 = __umulhi(cur, 1u << 16);
+  const uint32_t s16 = prmt_<0x4432>(cur, 0u);          // bits [16, 32)
+  const uint32_t t8 = prmt_<0x4321>(cur, prev);         // bits [8, 40)
+  const uint32_t s24 = prmt_<0x4432>(t8, 0u);           // bits [24, 40)
+  const uint32_t t4 = shf_r_<4>(cur, prev);             // bits [4, 36)
+  const uint32_t s20 = prmt_<0x4432>(t4, 0u);           // bits [20, 36)
+  const uint32_t t12 = shf_r_<12>(cur, prev);           // bits [12, 44)
+  const uint32_t s28 = prmt_<0x4432>(t12, 0u);          // bits [28, 44)
   uint32_t a0[4], a1[4];
-  a0[0] = ((__byte_perm(v, 0u, 0x4421) * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;                 // x0
-  a0[1] = ((__byte_perm(y, 0u, 0x4421) * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;                 // x4
-  a0[2] = (((__funnelshift_r(cur, prev, 24) & 0xffffu) * C) & 0x8FFF8FFFu) ^ 0x3B603B60u; // x1
-  a0[3] = ((__byte_perm(cur, 0u, 0x4421) * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;               // x5
+  a0[0] = mcg_mask_(s28 * C);                           // x0
+  a0[1] = mcg_mask_(t12 * C + s28 * Cn);                // x4
+  a0[2] = mcg_mask_(s24 * C);                           // x1
+  a0[3] = mcg_mask_(t8 * C + s24 * Cn);                 // x5
   mma_f16_16816(c, a0, b.x, b.y);
-  a1[0] = (((v & 0xffffu) * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;                              // x2
-  a1[1] = (((y & 0xffffu) * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;                              // x6
-  a1[2] = ((s3 * C) & 0x8FFF8FFFu) ^ 0x3B603B60u;                                          // x3
-  a1[3] = ((cur * C + s3 * Cn) & 0x8FFF8FFFu) ^ 0x3B603B60u;                               // x7
+  a1[0] = mcg_mask_(s20 * C);                           // x2
+  a1[1] = mcg_mask_(t4 * C + s20 * Cn);                 // x6
+  a1[2] = mcg_mask_(s16 * C);                           // x3
+  a1[3] = mcg_mask_(cur * C + s16 * Cn);                // x7
   mma_f16_16816(c, a1, b.z, b.w);
 }
 
