@@ -317,7 +317,10 @@ __device__ __forceinline__ void cluster_release() {
 // Up to 8 tokens of the group per pass (one n8 block; a decode window of R <= 8 rows never has more per expert);
 // larger groups decode the trellis again for every further 8 tokens.
 // ---------------------------------------------------------------------------------------------------------------
-template <int KSPL>
+// KS: the k-tile stride of the trellis in 32-bit words (N/16 tiles of 32 words), a compile-time constant for the
+// model's shapes (0: read from the arguments).  With it, the four words of a chunk are one pointer plus immediate
+// offsets and the walk over K is one pointer increment per chunk, instead of a 64-bit address product per load.
+template <int KSPL, int KS>
 __device__ __forceinline__ void gate_up_group(const Exl3Args& a, int u, float (*zg)[132], float (*zu)[132]) {
   const int e = a.group_expert[u];
   const int p0 = a.group_offset[u];
@@ -327,9 +330,11 @@ __device__ __forceinline__ void gate_up_group(const Exl3Args& a, int u, float (*
   const int nt = nb * 8 + warp;
   const int KT = a.K / 16, NT = a.N / 16;
   const int ks = KSPL > 1 ? (int)blockIdx.z : 0, cper = a.K / 64 / KSPL, c_lo = ks * cper, c_hi = c_lo + cper;
-  const uint32_t* wg = reinterpret_cast<const uint32_t*>(a.tr_g) + ((int64_t)e * KT * NT + nt) * 32 + lane;
-  const uint32_t* wu = reinterpret_cast<const uint32_t*>(a.tr_u) + ((int64_t)e * KT * NT + nt) * 32 + lane;
-  const int64_t kstride = (int64_t)NT * 32;
+  const int kstride = KS > 0 ? KS : NT * 32;
+  const uint32_t* wg = reinterpret_cast<const uint32_t*>(a.tr_g) + ((int64_t)e * KT * NT + nt) * 32 + lane +
+                       (int64_t)4 * c_lo * kstride;
+  const uint32_t* wu = reinterpret_cast<const uint32_t*>(a.tr_u) + ((int64_t)e * KT * NT + nt) * 32 + lane +
+                       (int64_t)4 * c_lo * kstride;
   const int src = (lane + 31) & 31;
   const uint64_t pol = l2_evict_first_policy();     // the codes are read once per step: replace them first in L2
 
@@ -339,27 +344,31 @@ __device__ __forceinline__ void gate_up_group(const Exl3Args& a, int u, float (*
     const int64_t r0 = (int64_t)(p0 + m0 + (g < nrows ? g : 0)) * 2 * a.K + q * 32;
     float cg[4] = {}, cu[4] = {};
     uint32_t pg[4], pu[4];
+    const uint32_t* pgp = wg;
+    const uint32_t* pup = wu;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      pg[i] = ldg_nc_u32_ef(wg + (4 * c_lo + i) * kstride, pol);
-      pu[i] = ldg_nc_u32_ef(wu + (4 * c_lo + i) * kstride, pol);
+      pg[i] = ldg_nc_u32_ef(pgp + i * kstride, pol);
+      pu[i] = ldg_nc_u32_ef(pup + i * kstride, pol);
     }
+    const uint4* bgp = reinterpret_cast<const uint4*>(a.xh_g + r0 + c_lo * 128);
+    const uint4* bup = reinterpret_cast<const uint4*>(a.xh_u + r0 + c_lo * 128);
     for (int c = c_lo; c < c_hi; ++c) {
       uint32_t ng[4], nu[4];
-      const int64_t noff = (c + 1 < c_hi ? 4 * c + 4 : 4 * c) * kstride;   // the last chunk reloads itself
+      if (c + 1 < c_hi) { pgp += 4 * kstride; pup += 4 * kstride; }    // the last chunk reloads itself
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        ng[i] = ldg_nc_u32_ef(wg + noff + i * kstride, pol);
-        nu[i] = ldg_nc_u32_ef(wu + noff + i * kstride, pol);
+        ng[i] = ldg_nc_u32_ef(pgp + i * kstride, pol);
+        nu[i] = ldg_nc_u32_ef(pup + i * kstride, pol);
       }
-      const uint4* bgp = reinterpret_cast<const uint4*>(a.xh_g + r0 + c * 128);
-      const uint4* bup = reinterpret_cast<const uint4*>(a.xh_u + r0 + c * 128);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint4 bg = bgp[i], bu = bup[i];
         trellis_tile_mma(cg, pg[i], __shfl_sync(0xffffffffu, pg[i], src), bg);
         trellis_tile_mma(cu, pu[i], __shfl_sync(0xffffffffu, pu[i], src), bu);
       }
+      bgp += 16;                                    // 128 halves = 16 uint4 per 64-wide chunk
+      bup += 16;
 #pragma unroll
       for (int i = 0; i < 4; ++i) { pg[i] = ng[i]; pu[i] = nu[i]; }
     }
@@ -413,7 +422,7 @@ __device__ __forceinline__ void l2_prefetch_share(const L2Ranges& r) {
 }
 
 // CTAs loop over the groups (grid.y may be smaller than the group table: a decode window routes to few experts)
-template <int KSPL>
+template <int KSPL, int KS>
 __global__ void __launch_bounds__(256, 4) exl3_gate_up_kernel(Exl3Args a) {
   __shared__ float zg[8][132];
   __shared__ float zu[8][132];
@@ -421,7 +430,7 @@ __global__ void __launch_bounds__(256, 4) exl3_gate_up_kernel(Exl3Args a) {
   pdl_wait();                          // rotated inputs and the group table from the previous kernels
   pdl_trigger();
   const int ng = min(a.group_count[0], a.max_groups);
-  for (int u = blockIdx.y; u < ng; u += gridDim.y) gate_up_group<KSPL>(a, u, zg, zu);
+  for (int u = blockIdx.y; u < ng; u += gridDim.y) gate_up_group<KSPL, KS>(a, u, zg, zu);
 }
 
 // expert parallelism: the last CTA of the down kernel (all pair rows stored into the sources' combine buffers and
@@ -443,7 +452,7 @@ __device__ __forceinline__ void ep_count_in(const Exl3Args& a) {
 // down: grid (Dout/128, max_groups, KSPL) with K split over a cluster as in gate_up; epilogue H128, * svh,
 // * routing weight -> yd[pair] fp32
 // ---------------------------------------------------------------------------------------------------------------
-template <int KSPL>
+template <int KSPL, int KS>
 __device__ __forceinline__ void down_group(const Exl3Args& a, int u, float (*zd)[132]) {   // KSPL in {1, 2}
   const int e = a.group_expert[u];
   const int p0 = a.group_offset[u];
@@ -453,8 +462,9 @@ __device__ __forceinline__ void down_group(const Exl3Args& a, int u, float (*zd)
   const int nt = nb * 8 + warp;
   const int KT = a.N / 16, NT = a.Dout / 16;
   const int ks = KSPL > 1 ? (int)blockIdx.z : 0, cper = a.N / 64 / KSPL, c_lo = ks * cper, c_hi = c_lo + cper;
-  const uint32_t* wd = reinterpret_cast<const uint32_t*>(a.tr_d) + ((int64_t)e * KT * NT + nt) * 32 + lane;
-  const int64_t kstride = (int64_t)NT * 32;
+  const int kstride = KS > 0 ? KS : NT * 32;
+  const uint32_t* wd = reinterpret_cast<const uint32_t*>(a.tr_d) + ((int64_t)e * KT * NT + nt) * 32 + lane +
+                       (int64_t)4 * c_lo * kstride;
   const int src = (lane + 31) & 31;
   const uint64_t pol = l2_evict_first_policy();     // the codes are read once per step: replace them first in L2
 
@@ -463,22 +473,62 @@ __device__ __forceinline__ void down_group(const Exl3Args& a, int u, float (*zd)
     // token columns past the group read the group's first row: their MMA columns are never stored
     const int64_t r0 = (int64_t)(p0 + m0 + (g < nrows ? g : 0)) * 2 * a.N + q * 32;
     float cd[4] = {};
-    uint32_t pd[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) pd[i] = ldg_nc_u32_ef(wd + (4 * c_lo + i) * kstride, pol);
-    for (int c = c_lo; c < c_hi; ++c) {
-      uint32_t nd[4];
-      const int64_t noff = (c + 1 < c_hi ? 4 * c + 4 : 4 * c) * kstride;   // the last chunk reloads itself
-#pragma unroll
-      for (int i = 0; i < 4; ++i) nd[i] = ldg_nc_u32_ef(wd + noff + i * kstride, pol);
-      const uint4* bp = reinterpret_cast<const uint4*>(a.xd + r0 + c * 128);
+    if ((c_hi - c_lo) % 2 == 0) {
+      // two independent k-streams per warp (the two halves of the warp's chunk range, one chunk of each in flight
+      // and one prefetched): twice the loads in flight of a single stream, which left the kernel waiting on memory
+      const int half = (c_hi - c_lo) / 2;
+      float ce[4] = {};
+      uint32_t pd[4], pe[4];
+      const uint32_t* pdp = wd;
+      const uint32_t* pep = wd + (int64_t)4 * half * kstride;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const uint4 b = bp[i];
-        trellis_tile_mma(cd, pd[i], __shfl_sync(0xffffffffu, pd[i], src), b);
+        pd[i] = ldg_nc_u32_ef(pdp + i * kstride, pol);
+        pe[i] = ldg_nc_u32_ef(pep + i * kstride, pol);
+      }
+      const uint4* bp = reinterpret_cast<const uint4*>(a.xd + r0 + c_lo * 128);
+      const uint4* bq = bp + 16 * half;
+      for (int c = 0; c < half; ++c) {
+        uint32_t nd[4], ne[4];
+        if (c + 1 < half) { pdp += 4 * kstride; pep += 4 * kstride; }    // the last chunk reloads itself
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          nd[i] = ldg_nc_u32_ef(pdp + i * kstride, pol);
+          ne[i] = ldg_nc_u32_ef(pep + i * kstride, pol);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 b = bp[i], b2 = bq[i];
+          trellis_tile_mma(cd, pd[i], __shfl_sync(0xffffffffu, pd[i], src), b);
+          trellis_tile_mma(ce, pe[i], __shfl_sync(0xffffffffu, pe[i], src), b2);
+        }
+        bp += 16;
+        bq += 16;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { pd[i] = nd[i]; pe[i] = ne[i]; }
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) pd[i] = nd[i];
+      for (int i = 0; i < 4; ++i) cd[i] += ce[i];
+    } else {
+      uint32_t pd[4];
+      const uint32_t* pdp = wd;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pd[i] = ldg_nc_u32_ef(pdp + i * kstride, pol);
+      const uint4* bp = reinterpret_cast<const uint4*>(a.xd + r0 + c_lo * 128);
+      for (int c = c_lo; c < c_hi; ++c) {
+        uint32_t nd[4];
+        if (c + 1 < c_hi) pdp += 4 * kstride;        // the last chunk reloads itself
+#pragma unroll
+        for (int i = 0; i < 4; ++i) nd[i] = ldg_nc_u32_ef(pdp + i * kstride, pol);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 b = bp[i];
+          trellis_tile_mma(cd, pd[i], __shfl_sync(0xffffffffu, pd[i], src), b);
+        }
+        bp += 16;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) pd[i] = nd[i];
+      }
     }
     acc_to_smem(cd, warp, zd);
     __syncthreads();
@@ -505,13 +555,13 @@ __device__ __forceinline__ void down_group(const Exl3Args& a, int u, float (*zd)
   }
 }
 
-template <int KSPL>
+template <int KSPL, int KS>
 __global__ void __launch_bounds__(256) exl3_down_kernel(Exl3Args a) {
   __shared__ float zd[8][132];
   pdl_wait();                          // the gate/up kernel's activations
   pdl_trigger();
   const int ng = min(a.group_count[0], a.max_groups);
-  for (int u = blockIdx.y; u < ng; u += gridDim.y) down_group<KSPL>(a, u, zd);
+  for (int u = blockIdx.y; u < ng; u += gridDim.y) down_group<KSPL, KS>(a, u, zd);
   if (a.out_ptrs) ep_count_in(a);                   // expert parallelism: every CTA counts towards the release
 }
 
@@ -578,26 +628,52 @@ static cudaError_t launch_split(void (*kern)(Exl3Args), dim3 grid, const Exl3Arg
   return g53_launch_pdl(kern, grid, dim3(256), 0, st, KSPL, a);
 }
 
-static int pick_split(int kc) { return kc % 4 == 0 ? 4 : kc % 2 == 0 ? 2 : 1; }
+// the trellis k-tile stride (words) as a template constant for the model's expert shapes (hidden 4096 with expert
+// width 2048 / TP for TP 1..8; the tiny proxy's 512 / 256), the generic kernel otherwise
+template <int KSPL>
+static cudaError_t gate_up_ks(const Exl3Args& a, dim3 grid, cudaStream_t st) {
+  switch (a.N / 16 * 32) {
+    case 4096: return launch_split<KSPL>(exl3_gate_up_kernel<KSPL, 4096>, grid, a, st);
+    case 2048: return launch_split<KSPL>(exl3_gate_up_kernel<KSPL, 2048>, grid, a, st);
+    case 1024: return launch_split<KSPL>(exl3_gate_up_kernel<KSPL, 1024>, grid, a, st);
+    case 512: return launch_split<KSPL>(exl3_gate_up_kernel<KSPL, 512>, grid, a, st);
+    default: return launch_split<KSPL>(exl3_gate_up_kernel<KSPL, 0>, grid, a, st);
+  }
+}
+
+template <int KSPL>
+static cudaError_t down_ks(const Exl3Args& a, dim3 grid, cudaStream_t st) {
+  switch (a.Dout / 16 * 32) {
+    case 8192: return launch_split<KSPL>(exl3_down_kernel<KSPL, 8192>, grid, a, st);
+    case 1024: return launch_split<KSPL>(exl3_down_kernel<KSPL, 1024>, grid, a, st);
+    default: return launch_split<KSPL>(exl3_down_kernel<KSPL, 0>, grid, a, st);
+  }
+}
 
 cudaError_t g53_exl3_gate_up(const Exl3Args& a, cudaStream_t st) {
   if (a.K % 128 || a.N % 128 || !a.decode_layout) return cudaErrorInvalidValue;
   const dim3 grid(a.N / 128, a.launch_groups > 0 ? std::min(a.launch_groups, a.max_groups) : a.max_groups);
-  switch (pick_split(a.K / 64)) {
-    case 4: return launch_split<4>(exl3_gate_up_kernel<4>, grid, a, st);
-    case 2: return launch_split<2>(exl3_gate_up_kernel<2>, grid, a, st);
-    default: return launch_split<1>(exl3_gate_up_kernel<1>, grid, a, st);
+  // K split by the expected grid: a window of 1-2 tokens touches few experts (4 CTAs per tile fill the SMs), 8 tokens
+  // about 57 of 288 (2 per tile: measured 0.342 vs 0.358 ms per layer with 4), larger windows need no split
+  const int groups = grid.y;
+  const int want = groups <= 16 ? 4 : groups <= 128 ? 2 : 1;
+  const int kc = a.K / 64;
+  const int split = (want == 4 && kc % 4 == 0) ? 4 : (want >= 2 && kc % 2 == 0) ? 2 : 1;
+  switch (split) {
+    case 4: return gate_up_ks<4>(a, grid, st);
+    case 2: return gate_up_ks<2>(a, grid, st);
+    default: return gate_up_ks<1>(a, grid, st);
   }
 }
 
 cudaError_t g53_exl3_down(const Exl3Args& a, cudaStream_t st) {
   if (a.Dout % 128 || a.N % 64 || !a.decode_layout) return cudaErrorInvalidValue;
   const dim3 grid(a.Dout / 128, a.launch_groups > 0 ? std::min(a.launch_groups, a.max_groups) : a.max_groups);
-  if (a.out_ptrs) return launch_split<1>(exl3_down_kernel<1>, grid, a, st);
+  if (a.out_ptrs) return down_ks<1>(a, grid, st);
   // the down grid is already twice the gate_up grid (Dout = 2 N at TP=1); split only short-K tensor shards
   const int kc = a.N / 64;
-  if (kc >= 16 || kc % 2) return launch_split<1>(exl3_down_kernel<1>, grid, a, st);
-  return launch_split<2>(exl3_down_kernel<2>, grid, a, st);
+  if (kc >= 16 || kc % 2) return down_ks<1>(a, grid, st);
+  return down_ks<2>(a, grid, st);
 }
 
 cudaError_t g53_moe_combine(const float* yd, const int* pair_of, int R, int top_k, int D, float* out,

@@ -1,6 +1,8 @@
 """Step-level profiles of the serving path on one GPU.
 
-  python -m glm53.utils.step_profile forward --rows 8        kernel breakdown of one decode window forward
+  python -m glm53.utils.step_profile forward --rows 8        kernel breakdown of one decode window forward (CUDA graph)
+  torchrun --nproc-per-node 4 --master-addr 127.0.0.1 -m glm53.utils.step_profile forward --rows 8
+                                                              the same per rank of a tensor-parallel group
   python -m glm53.utils.step_profile prefill --chunk 4096    kernel breakdown of one prefill chunk (context = chunk)
   torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m glm53.utils.step_profile prefill --chunk 8192
                                                               the same on rank 0 of a tensor-parallel group
@@ -22,7 +24,11 @@ import time
 import torch
 
 
-def _kernel_table(fn, reps: int = 1, top: int = 30):
+def _kernel_table(fn, reps: int = 1, top: int = 30, marginal: bool = False):
+    """Device time per kernel name over ``reps`` calls of ``fn``.  With ``marginal``, each kernel is charged the
+    time from the latest end of any earlier kernel to its own end (zero if it ended earlier): the critical-path
+    cost of the kernel, which excludes the time a programmatic-dependent kernel spends waiting for its
+    predecessor and includes the launch gap before it.  Marginal times add up to the span of the calls."""
     from torch.profiler import ProfilerActivity, profile
     torch.cuda.synchronize()
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
@@ -30,8 +36,18 @@ def _kernel_table(fn, reps: int = 1, top: int = 30):
             fn()
         torch.cuda.synchronize()
     agg = collections.defaultdict(lambda: [0, 0.0])
-    for e in prof.events():
-        if e.device_type.name == "CUDA":
+    evs = [e for e in prof.events() if e.device_type.name == "CUDA"]
+    if marginal:
+        evs.sort(key=lambda e: (e.time_range.end, e.time_range.start))
+        last = None
+        for e in evs:
+            a = agg[e.name[:100]]
+            a[0] += 1
+            t0 = e.time_range.start if last is None else max(last, e.time_range.start)
+            a[1] += max(0.0, e.time_range.end - t0)
+            last = e.time_range.end if last is None else max(last, e.time_range.end)
+    else:
+        for e in evs:
             a = agg[e.name[:100]]
             a[0] += 1
             a[1] += e.device_time_total
@@ -64,6 +80,10 @@ def _rank0() -> bool:
 
 
 def cmd_forward(a):
+    """One decode window of ``rows`` distinct random tokens (so the routed experts are those of real text, about 57
+    distinct of 288 for 8 rows) replayed as a CUDA graph: the window's time, and per kernel both the summed device
+    time and the marginal (critical-path) time.  Under torchrun every rank prints its table; compare rank 0 with
+    the slowest rank."""
     from .. import full_config
     from ..models.runtime import Graphed
     cfg = full_config()
@@ -71,18 +91,10 @@ def cmd_forward(a):
     g = torch.Generator().manual_seed(0)
     seq.prefill(torch.randint(0, cfg.vocab, (a.context,), generator=g).tolist(), chunk=a.chunk)
     R = a.rows
-
-    def step():
-        seq.stage([1] * R, list(range(R)))
-        seq._window = R
-        rt.forward(R, keep_window=True)
-        seq.commit(R)
-
-    for _ in range(3):
-        step()
-    total, rows = _kernel_table(step, reps=2)
+    toks = torch.randint(0, cfg.vocab, (R,), generator=g).tolist()
+    seq.stage(toks, list(range(R)))
+    seq._window = R
     graph = Graphed(lambda: rt.forward(R, keep_window=True))
-    seq.stage([1] * R, list(range(R)))
     for _ in range(3):
         graph()
     torch.cuda.synchronize()
@@ -92,10 +104,32 @@ def cmd_forward(a):
         graph()
     e1.record()
     torch.cuda.synchronize()
-    print(json.dumps({"mode": "forward", "rows": R, "context": a.context, "kernel_sum_us": total,
-                      "graph_replay_us": e0.elapsed_time(e1) * 100.0}))
+    window_us = e0.elapsed_time(e1) * 100.0
+    total, rows = _kernel_table(graph, reps=4, top=a.top)
+    mtotal, mrows = _kernel_table(graph, reps=4, top=a.top, marginal=True)
+    import torch.distributed as dist
+    tp = dist.get_world_size() if dist.is_initialized() else 1
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    spans = [window_us]
+    if tp > 1:
+        t = torch.tensor([window_us], device=rt.device)
+        out = [torch.zeros_like(t) for _ in range(tp)]
+        dist.all_gather(out, t)
+        spans = [float(x.item()) for x in out]
+    lines = [json.dumps({"mode": "forward", "tp": tp, "rank": rank, "rows": R, "context": a.context,
+                         "graph_window_us": window_us, "window_us_per_rank": spans,
+                         "kernel_sum_us": total, "marginal_sum_us": mtotal})]
+    mt = dict((n, t) for n, _, t in mrows)
+    lines.append(f"{'marginal':>10} {'device':>10} {'count':>6}  kernel")
     for n, c, t in rows:
-        print(f"{t:10.1f} us {c:6d}x  {n}")
+        lines.append(f"{mt.get(n, 0.0):8.1f}us {t:8.1f}us {c:6d}x  {n}")
+    for r in range(tp):
+        if r == rank:
+            print("\n".join(lines), flush=True)
+        if tp > 1:
+            dist.barrier()
+    if tp > 1:
+        dist.destroy_process_group()
 
 
 def cmd_prefill(a):
@@ -128,9 +162,13 @@ def cmd_prefill(a):
 def cmd_engine(a):
     from ..api.offline import LLM, LLMOptions
     from ..engine.llm import SamplingParams, State
+    from ..parallel import dist as D
     K = a.k
+    rank, _, world = D.init()
+    comm = D.NcclComm() if world > 1 else None
     llm = LLM(LLMOptions(model="full", max_seqs=1, max_model_len=a.context + (K + 1) * (2 * a.steps + 16) + 64,
-                         prefill_chunk=4096, speculative=True, k_fixed=K, force_accept=True, checkpoints=0))
+                         prefill_chunk=4096, speculative=True, k_fixed=K, force_accept=True, checkpoints=0),
+              comm=comm, rank=rank, world=world)
     eng = llm.engine
     g = torch.Generator().manual_seed(0)
     ctx = torch.randint(0, llm.cfg.vocab, (a.context,), generator=g).tolist()
@@ -172,12 +210,22 @@ def cmd_engine(a):
     torch.cuda.synchronize()
     inst = (time.perf_counter() - t0) * 1e3 / a.steps
     phases = {k: v * 1e3 / a.steps for k, v in sorted(acc.items(), key=lambda kv: -kv[1])}
-    total, rows = _kernel_table(lambda: [eng.step() for _ in range(2)], reps=1)
-    print(json.dumps({"mode": "engine", "k": K, "context": a.context, "plain_step_ms": plain,
-                      "instrumented_step_ms": inst, "phases_ms": phases,
-                      "unattributed_ms": inst - sum(phases.values()), "kernel_sum_us_per_step": total / 2}))
-    for n, c, t in rows:
-        print(f"{t / 2:10.1f} us {c // 2:6d}x  {n}")
+    total, rows = _kernel_table(lambda: [eng.step() for _ in range(2)], reps=1, top=a.top)
+    mtotal, mrows = _kernel_table(lambda: [eng.step() for _ in range(2)], reps=1, top=a.top, marginal=True)
+    mt = dict((n, t) for n, _, t in mrows)
+    if rank == 0:
+        print(json.dumps({"mode": "engine", "tp": world, "k": K, "context": a.context, "plain_step_ms": plain,
+                          "instrumented_step_ms": inst, "phases_ms": phases,
+                          "unattributed_ms": inst - sum(phases.values()), "kernel_sum_us_per_step": total / 2,
+                          "marginal_sum_us_per_step": mtotal / 2}))
+        print(f"{'marginal':>10} {'device':>10} {'count':>6}  kernel")
+        for n, c, t in rows:
+            print(f"{mt.get(n, 0.0) / 2:8.1f}us {t / 2:8.1f}us {c // 2:6d}x  {n}")
+    llm.backend._graphs.clear()
+    if comm:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():
@@ -188,6 +236,7 @@ def main():
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--k", type=int, default=7)
     ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--top", type=int, default=40)
     a = ap.parse_args()
     {"forward": cmd_forward, "prefill": cmd_prefill, "engine": cmd_engine}[a.mode](a)
 
