@@ -120,8 +120,10 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
   __syncthreads();
   // tile sums (fixed warp order) -> tot[t][row][tok]
   __shared__ float tot[NT][16][17];
+  // consecutive threads store consecutive output columns of one row (coalesced; for the tensor-parallel push these
+  // are peer stores over NVLink, where scattered 4-byte stores cost a transaction each)
   for (int e = threadIdx.x; e < NT * 16 * 16; e += blockDim.x) {
-    const int t = e / 256, r = (e / 16) % 16, tok = e % 16;
+    const int t = e / 256, r = e % 16, tok = (e / 16) % 16;
     float v = 0.f;
     if (tok < p.M) {
 #pragma unroll
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(256) gemv_kernel(GemvArgs p) {
   if (p.mode == GEMV_SWIGLU) {
     // rows 0..7 of every 16-row tile are gate rows j0..j0+7, rows 8..15 the matching up rows
     for (int e = threadIdx.x; e < NT * 8 * 16; e += blockDim.x) {
-      const int t = e / (8 * 16), r = (e / 16) % 8, tok = e % 16;
+      const int t = e / (8 * 16), r = e % 8, tok = (e / 8) % 16;     // consecutive threads: consecutive columns
       if (tok >= p.M) continue;
       const int nt0 = (blockIdx.x * NT + t) * 16;
       if (nt0 + r + 8 >= p.N) continue;

@@ -222,7 +222,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_bulk_kernel(GemvArgs p) {
     // epilogue element of this thread: (row r, token tok) of every tile (threads 0..255)
     const int e = threadIdx.x;
     const bool act = e < kRows * 16;
-    const int r = (e >> 4) & (kRows - 1), tok = e & 15;
+    // consecutive threads own consecutive output columns of one row: the final stores (and the tensor-parallel
+    // push into the peers' receive buffers over NVLink) are coalesced
+    const int r = e & (kRows - 1), tok = (e >> 4) & 15;
     const bool swiglu = p.mode == GEMV_SWIGLU;
     for (int t = blockIdx.x; t < T; t += gridDim.x) {
       float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};

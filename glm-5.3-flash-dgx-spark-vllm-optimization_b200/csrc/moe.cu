@@ -653,13 +653,15 @@ static cudaError_t down_ks(const Exl3Args& a, dim3 grid, cudaStream_t st) {
 cudaError_t g53_exl3_gate_up(const Exl3Args& a, cudaStream_t st) {
   if (a.K % 128 || a.N % 128 || !a.decode_layout) return cudaErrorInvalidValue;
   const dim3 grid(a.N / 128, a.launch_groups > 0 ? std::min(a.launch_groups, a.max_groups) : a.max_groups);
-  // K split by the expected grid: a window of 1-2 tokens touches few experts (4 CTAs per tile fill the SMs), 8 tokens
-  // about 57 of 288 (2 per tile: measured 0.342 vs 0.358 ms per layer with 4), larger windows need no split
-  const int groups = grid.y;
-  const int want = groups <= 16 ? 4 : groups <= 128 ? 2 : 1;
+  // K split over a cluster until the grid has about 2048 CTAs (3.5 waves of 4 per SM): measured at TP1 with 8 tokens
+  // (64 groups x 16 column blocks) a split of 2 beats 4 (0.342 vs 0.358 ms per layer) and 1 (0.352); the narrow
+  // expert shards of TP 4 / 8 (4 / 2 column blocks) need 8
   const int kc = a.K / 64;
-  const int split = (want == 4 && kc % 4 == 0) ? 4 : (want >= 2 && kc % 2 == 0) ? 2 : 1;
+  int split = 1;
+  while (split < 8 && (int64_t)grid.x * grid.y * split < 2048 && kc % (2 * split) == 0 && kc / (2 * split) >= 4)
+    split *= 2;
   switch (split) {
+    case 8: return gate_up_ks<8>(a, grid, st);
     case 4: return gate_up_ks<4>(a, grid, st);
     case 2: return gate_up_ks<2>(a, grid, st);
     default: return gate_up_ks<1>(a, grid, st);
@@ -669,11 +671,9 @@ cudaError_t g53_exl3_gate_up(const Exl3Args& a, cudaStream_t st) {
 cudaError_t g53_exl3_down(const Exl3Args& a, cudaStream_t st) {
   if (a.Dout % 128 || a.N % 64 || !a.decode_layout) return cudaErrorInvalidValue;
   const dim3 grid(a.Dout / 128, a.launch_groups > 0 ? std::min(a.launch_groups, a.max_groups) : a.max_groups);
-  if (a.out_ptrs) return down_ks<1>(a, grid, st);
-  // the down grid is already twice the gate_up grid (Dout = 2 N at TP=1); split only short-K tensor shards
-  const int kc = a.N / 64;
-  if (kc >= 16 || kc % 2) return down_ks<1>(a, grid, st);
-  return down_ks<2>(a, grid, st);
+  // the down grid is already Dout / 128 = 32 column blocks per group; its K (the local expert width) only shrinks
+  // with tensor parallelism, so it is never split (two k-streams per warp give each warp its loads in flight)
+  return down_ks<1>(a, grid, st);
 }
 
 cudaError_t g53_moe_combine(const float* yd, const int* pair_of, int R, int top_k, int D, float* out,

@@ -104,19 +104,47 @@ __device__ __forceinline__ void tma_2d(const CUtensorMap* m, uint64_t* bar, void
                ::"r"(su32(dst)), "l"(m), "r"(x), "r"(y), "r"(su32(bar)) : "memory");
 }
 
-// mcg trellis decode (same rules as moe.cu): 4 f16x2 fragment registers of lane l from words cur (l) / prev (l-1)
-__device__ __forceinline__ uint32_t mcg_x(uint32_t s) { return ((s * 0xCBAC1FEDu) & 0x8FFF8FFFu) ^ 0x3B603B60u; }
-__device__ __forceinline__ uint32_t mcg_pair(uint32_t s0, uint32_t s1) {
-  const uint32_t x0 = mcg_x(s0), x1 = mcg_x(s1);
-  const uint32_t lo = __byte_perm(x0, x1, 0x5410), hi = __byte_perm(x0, x1, 0x7632);
+// mcg trellis decode (same rules as moe.cu): 4 f16x2 fragment registers of lane l from words cur (l) / prev (l-1).
+// The window extraction pairs windows b and b + 16 as the decode kernels do (moe.cu, trellis_tile_mma): for any
+// 32-bit t holding window b in its low half, s_b * C = t * C - (t >> 16) * (C << 16) (mod 2^32), and t >> 16 is
+// window b + 16, so 7 ALU extractions and 12 IMADs give the 8 masked products (instead of 10 ALU extractions and
+// 8 IMADs); the two fp16 halves of each product are then added (one HADD2 per two values) as the format specifies.
+template <uint32_t SEL>
+__device__ __forceinline__ uint32_t prmt_(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "n"(SEL));
+  return r;
+}
+template <uint32_t SH>
+__device__ __forceinline__ uint32_t shf_r_(uint32_t lo, uint32_t hi) {
+  uint32_t r;
+  asm("shf.r.wrap.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(lo), "r"(hi), "n"(SH));
+  return r;
+}
+__device__ __forceinline__ uint32_t mcg_mask_(uint32_t x) {       // (x & 0x8FFF8FFF) ^ 0x3B603B60, one LOP3
+  uint32_t r;
+  asm("lop3.b32 %0, %1, 0x8FFF8FFF, 0x3B603B60, 0x6a;" : "=r"(r) : "r"(x));
+  return r;
+}
+// (fp16(lo0) + fp16(hi0), fp16(lo1) + fp16(hi1)) of two masked products
+__device__ __forceinline__ uint32_t mcg_sum2(uint32_t x0, uint32_t x1) {
+  const uint32_t lo = prmt_<0x5410>(x0, x1), hi = prmt_<0x7632>(x0, x1);
   __half2 r = __hadd2(*reinterpret_cast<const __half2*>(&lo), *reinterpret_cast<const __half2*>(&hi));
   return *reinterpret_cast<uint32_t*>(&r);
 }
 __device__ __forceinline__ void frags(uint32_t cur, uint32_t prev, uint32_t (&b)[4]) {
-  b[0] = mcg_pair(__funnelshift_r(cur, prev, 28) & 0xffffu, __funnelshift_r(cur, prev, 24) & 0xffffu);
-  b[1] = mcg_pair(__funnelshift_r(cur, prev, 20) & 0xffffu, cur >> 16);
-  b[2] = mcg_pair((cur >> 12) & 0xffffu, (cur >> 8) & 0xffffu);
-  b[3] = mcg_pair((cur >> 4) & 0xffffu, cur & 0xffffu);
+  constexpr uint32_t C = 0xCBAC1FEDu, Cn = 0u - (C << 16);
+  const uint32_t s16 = prmt_<0x4432>(cur, 0u);          // stream bits [16, 32) above cur's LSB
+  const uint32_t t8 = prmt_<0x4321>(cur, prev);         // [8, 40)
+  const uint32_t s24 = prmt_<0x4432>(t8, 0u);           // [24, 40)
+  const uint32_t t4 = shf_r_<4>(cur, prev);             // [4, 36)
+  const uint32_t s20 = prmt_<0x4432>(t4, 0u);           // [20, 36)
+  const uint32_t t12 = shf_r_<12>(cur, prev);           // [12, 44)
+  const uint32_t s28 = prmt_<0x4432>(t12, 0u);          // [28, 44)
+  b[0] = mcg_sum2(mcg_mask_(s28 * C), mcg_mask_(s24 * C));
+  b[1] = mcg_sum2(mcg_mask_(s20 * C), mcg_mask_(s16 * C));
+  b[2] = mcg_sum2(mcg_mask_(t12 * C + s28 * Cn), mcg_mask_(t8 * C + s24 * Cn));
+  b[3] = mcg_sum2(mcg_mask_(t4 * C + s20 * Cn), mcg_mask_(cur * C + s16 * Cn));
 }
 
 // byte offset of element (row, k) (k even) in a 128-row x 64-k f16 tile, K-major, 128-byte swizzle
