@@ -203,14 +203,33 @@ __global__ void __launch_bounds__(1024) dsa_select_kernel(DsaArgs a) {
       if ((u & mask) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1);
     }
     __syncthreads();
-    if (tid == 0) {
-      int acc = 0, b = 255;
-      for (; b > 0; --b) {
-        if (acc + hist[b] >= rem) break;
-        acc += hist[b];
+    if (tid < 32) {
+      // the highest bin b whose count from the top (bins 255..b) reaches rem (bin 0 when bins 255..1 do not):
+      // lane l holds bins 255 - 8l .. 248 - 8l, an exclusive prefix over the lanes gives each lane the count of
+      // the bins above its own, and the one lane whose range crosses rem (or lane 31) walks its 8 bins
+      const int lane = tid;
+      int cnt[8], sum = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { cnt[i] = hist[255 - 8 * lane - i]; sum += cnt[i]; }
+      int incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
       }
-      s_prefix = prefix | ((uint32_t)b << shift);
-      s_rem = rem - acc;
+      int acc = incl - sum;
+      if (acc < rem && (acc + sum >= rem || lane == 31)) {
+        int b = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int bin = 255 - 8 * lane - i;
+          if (bin == 0) break;                  // bin 0 is taken without a check
+          if (acc + cnt[i] >= rem) { b = bin; break; }
+          acc += cnt[i];
+        }
+        s_prefix = prefix | ((uint32_t)b << shift);
+        s_rem = rem - acc;
+      }
     }
     __syncthreads();
     prefix = s_prefix;

@@ -113,6 +113,13 @@ class Runtime:
         # all-reduce (32k prefill 10.1k vs 11.3k tok/s at TP2, 10.5k vs 15.3k at TP4) -- every rank stores its whole
         # partial into every peer, (W-1) x the ring's bytes per rank, from the GEMM epilogue's 4 warps
         self._fused_prefill = os.environ.get("GLM53_FUSED_TP_PREFILL", "0") == "1"
+        # sequence parallelism for prefill chunks (tensor parallel, at least GLM53_SP_MIN_ROWS rows, a multiple of the
+        # world size): rank j keeps the residual streams of rows [j R/W, (j+1) R/W) and runs mHC on them only; the
+        # normalised rows are all-gathered before each block and the block's fp32 partials reduce-scattered after
+        # it (the all-reduce's two halves, with the mHC work divided by W between them)
+        self.sp = dev.type == "cuda" and os.environ.get("GLM53_SP", "0") == "1"
+        self.sp_min_rows = int(os.environ.get("GLM53_SP_MIN_ROWS", "256"))
+        self._sp = None
         if comm is not None and self.tp > 1 and getattr(comm, "fused", False):
             from ..parallel.fused import PeerExchange
             rows = R if (self._fused_prefill and R >= K.GEMM_MIN_M) else min(R, rc.decode_rows, K.GEMV_MAX_M)
@@ -130,6 +137,8 @@ class Runtime:
         self.part = torch.zeros(R, D // 64, 32, dtype=f32, device=dev)
         self.branch = torch.zeros(R, D, dtype=f32, device=dev)
         self.hidden = torch.zeros(R, D, dtype=bf16, device=dev)
+        # reduce-scatter output of the sequence-parallel prefill (this rank's rows of the block sum)
+        self.rs = torch.zeros((R + self.tp - 1) // self.tp, D, dtype=f32, device=dev) if self.tp > 1 else None
         self.fnormed = torch.zeros(R, D, dtype=bf16, device=dev)
         self.lrows = torch.zeros(rc.logit_rows, D, dtype=bf16, device=dev)
         self.logits = torch.zeros(rc.logit_rows, w.head.n, dtype=f32, device=dev)
@@ -323,24 +332,32 @@ class Runtime:
         self._keep_window = keep_window
         Kc = K.C()
         X = self.X[:R]
-        Kc.embed(b.ids[:R], self.w.embed, X)
+        # sequence-parallel prefill: this rank's rows [r0, r1) of the residual streams (see __init__)
+        self._sp = None
+        if (getattr(self, "sp", False) and self.tp > 1 and self.comm is not None and not keep_window
+                and R >= self.sp_min_rows and R % self.tp == 0):
+            Rl = R // self.tp
+            self._sp = (self.w.rank * Rl, (self.w.rank + 1) * Rl)
+        rows = slice(*self._sp) if self._sp else slice(0, R)
+        Kc.embed(b.ids[rows], self.w.embed, X[rows])
         cur = 0
         first = True
         # tensor parallelism: block partials are pushed to the peers by the block's last projection (GEMV epilogue
         # for decode windows, tcgen05 GEMM epilogue for prefill chunks) and reduced inside the next mHC kernel
         # (parallel/fused.py); rows between the two kernels' ranges, or with the switch off, all-reduce by NCCL
-        self._fused = self.px is not None and R <= self.px.rows and (
+        self._fused = self._sp is None and self.px is not None and R <= self.px.rows and (
             R <= K.GEMV_MAX_M or (self._fused_prefill and R >= K.GEMM_MIN_M and K.GEMM_ENABLED))
         self._point = 0
         for lw in self.w.layers:
             # post of the previous FFN (none before layer 0) fused with this layer's attention pre
             nxt = 1 - cur
             if first:
-                Kc.hc_post_pre(X, None, None, None, lw.attn_hc.fn, lw.attn_hc.base, lw.attn_hc.scale, lw.in_norm,
-                               self.normed[:R], self.post[nxt][:R], self.comb[nxt][:R], self.part[:R], c.eps,
-                               c.hc_eps, c.hc_iters)
+                Kc.hc_post_pre(X[rows], None, None, None, lw.attn_hc.fn, lw.attn_hc.base, lw.attn_hc.scale,
+                               lw.in_norm, self.normed[rows], self.post[nxt][rows], self.comb[nxt][rows],
+                               self.part[:rows.stop - rows.start], c.eps, c.hc_eps, c.hc_iters)
             else:
                 self._post_pre(X, R, cur, nxt, lw.attn_hc, lw.in_norm)
+            self._sp_gather(self.normed, R)
             cur = nxt
             first = False
             if lw.kind == "kda":
@@ -349,13 +366,16 @@ class Runtime:
                 self._mla(lw, R)
             nxt = 1 - cur
             self._post_pre(X, R, cur, nxt, lw.ffn_hc, lw.post_norm)
+            self._sp_gather(self.normed, R)
             cur = nxt
             if lw.mlp is not None:
                 self._mlp(lw, R)
             else:
                 self._moe(lw, R)
         self._post_pre(X, R, cur, None, None, None)
-        Kc.stream_mean_norm(X, self.w.norm, c.eps, self.hidden[:R], self.fnormed[:R])
+        Kc.stream_mean_norm(X[rows], self.w.norm, c.eps, self.hidden[rows], self.fnormed[rows])
+        self._sp_gather(self.hidden, R)
+        self._sp_gather(self.fnormed, R)
         if not logits:
             return None
         n = b.n_logits
@@ -363,11 +383,29 @@ class Runtime:
         K.linear8(self.lrows[:n], self.w.head.w, self.w.head.s, self.logits[:n], K.GEMV_F32)
         return self.logits[:n]
 
+    def _sp_gather(self, buf, R):
+        """Sequence-parallel prefill: every rank's rows of ``buf`` to every rank (``buf[:R]`` in row order)."""
+        if self._sp is not None:
+            r0, r1 = self._sp
+            self.comm.all_gather(buf[:R].view(-1), buf[r0:r1].reshape(-1))
+
     def _post_pre(self, X, R, cur, nxt, hc, norm_w):
         """mHC post of the block just computed (reducing the tensor-parallel partials) fused with the next pre
         (hc None: post only)."""
         c = self.cfg
         Kc = K.C()
+        if self._sp is not None:
+            # this rank's rows: reduce-scatter of the block's partials, then post + pre on those rows only
+            r0, r1 = self._sp
+            n = r1 - r0
+            rs = self.rs[:n]
+            self.comm.reduce_scatter(rs, self.branch[:R])
+            pre = (hc.fn, hc.base, hc.scale, norm_w, self.normed[r0:r1], self.post[nxt][r0:r1],
+                   self.comb[nxt][r0:r1]) if hc is not None else (None,) * 7
+            Kc.hc_post_pre(X[r0:r1], rs, self.post[cur][r0:r1], self.comb[cur][r0:r1], *pre, self.part[:n], c.eps,
+                           c.hc_eps, c.hc_iters)
+            self._point += 1
+            return
         pre = (hc.fn, hc.base, hc.scale, norm_w, self.normed[:R], self.post[nxt][:R], self.comb[nxt][:R]) \
             if hc is not None else (None,) * 7
         if self._fused:

@@ -64,6 +64,15 @@ class NcclComm:
             out.copy_(t)
         return out
 
+    def reduce_scatter(self, out: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+        """out [n / world, ...] <- rank's block of the elementwise sum over ranks of t [n, ...] (rows in rank
+        order)."""
+        if self.world > 1:
+            dist.reduce_scatter_tensor(out, t, group=self.group)
+        else:
+            out.copy_(t)
+        return out
+
     def max_scalar(self, x: float) -> float:
         if self.world == 1:
             return x

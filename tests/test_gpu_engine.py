@@ -62,7 +62,11 @@ def test_decode_checkpoints_split_commits_stay_exact():
     from glm53.engine.llm import SamplingParams
     prompt = _prompts(1, 100, seed=7)[0]
     sp = SamplingParams(max_tokens=90, ignore_eos=True)
-    plain = _llm(speculative=False).engine.generate([prompt], sp)[0]
+    # the same checkpoint interval in both runs: prefill chunks end at checkpoint boundaries (64 + 36 rows here), and
+    # a different chunking would select different kernels (the 64-row chunk takes the decode-path MoE kernels)
+    plain_llm = _llm(speculative=False, checkpoints=8)
+    plain_llm.engine.cfg.checkpoint_pages = 1
+    plain = plain_llm.engine.generate([prompt], sp)[0]
     llm = _llm(speculative=True, checkpoints=8)
     llm.engine.cfg.checkpoint_pages = 1
     spec = llm.engine.generate([prompt], sp)[0]

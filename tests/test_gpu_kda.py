@@ -131,3 +131,29 @@ def test_kda_decode_fused_matches_five_kernels():
         cos = torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0).item()
         assert cos > 0.9999, cos
         assert (a - b).abs().max().item() < 5e-2 * max(1.0, a.abs().max().item())
+
+
+@pytest.mark.parametrize("Dh", [64, 128])
+def test_kda_recurrent_chaining_is_bit_exact(Dh):
+    """One launch over n rows leaves the same state and outputs, bit for bit, as n launches of one row each (plain
+    decoding steps one row at a time, speculative windows and commit replays run several rows per launch)."""
+    from glm53.ops import kernels as Kk
+    C = Kk.C()
+    H, T = 4, 8
+    proj, qkv, f, a_log, dt_bias, b_off = _inputs(T, H, Dh, 77)
+    S = torch.randn(3, H, Dh, Dh, device=DEV) * 0.1
+
+    def seq(r0, n, s_in, s_out):
+        return torch.tensor([[r0], [n], [s_in], [s_out], [0]], dtype=torch.int32, device=DEV)
+
+    o1 = torch.zeros(T, H * Dh, device=DEV)
+    C.kda_recurrent(proj, seq(0, T, 0, 1), f, qkv, a_log, dt_bias, S, o1, H, Dh, b_off, -5.0)
+    o2 = torch.zeros(T, H * Dh, device=DEV)
+    src = 0
+    for t in range(T):
+        dst = 2 if src == 0 else 0
+        C.kda_recurrent(proj, seq(t, 1, src, dst), f, qkv, a_log, dt_bias, S, o2, H, Dh, b_off, -5.0)
+        src = dst
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2), (o1 - o2).abs().max().item()
+    assert torch.equal(S[1], S[src]), (S[1] - S[src]).abs().max().item()

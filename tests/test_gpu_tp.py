@@ -113,3 +113,51 @@ def test_gemv_push_bulk(world):
     mp.spawn(_push_worker, args=(world, 29557 + world, result), nprocs=world, join=True)
     assert len(result) == world
     assert max(result.values()) == 0.0, dict(result)
+
+
+def _sp_worker(rank, world, port, result):
+    """Sequence-parallel prefill (mHC on each rank's rows, all-gather before and reduce-scatter after each block)
+    against the all-reduce path: logits of the prefill chunks and of a decode window after them."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0", GLM53_SP_MIN_ROWS="64")
+    import torch.distributed as dist
+    from glm53.config import tiny_config
+    from glm53.models import weights as W
+    from glm53.models.runtime import Runtime, RuntimeConfig
+    from glm53.models.session import Sequence
+    from glm53.parallel import dist as D
+    D.init(timeout_s=60)
+    try:
+        cfg = tiny_config()
+        dev = torch.device("cuda", rank)
+        w = W.prepare(W.RandomSource(cfg, seed=0, device=dev), cfg, rank=rank, world=world, device=dev)
+        rc = RuntimeConfig(max_rows=128, max_seqs=1, kv_slots=64 * 8, block_size=64, max_blocks=8)
+        g = torch.Generator().manual_seed(5)
+        prompt = torch.randint(16, cfg.vocab, (256,), generator=g).tolist()
+        outs = []
+        for sp in ("0", "1"):
+            os.environ["GLM53_SP"] = sp
+            rt = Runtime(w, rc, comm=D.NcclComm(fused=False))
+            seq = Sequence(rt)
+            lg = [seq.prefill(prompt, chunk=128).clone()]          # two 128-row chunks
+            lg.append(rt.hidden[:128].float().clone())
+            toks = [1, 2, 3, 4, 5, 6, 7, 8]
+            seq.stage(toks, list(range(8)))
+            lg.append(rt.forward(8, keep_window=True).clone())
+            outs.append(torch.cat([x.flatten() for x in lg]))
+        result[rank] = (outs[0] - outs[1]).abs().max().item()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sequence_parallel_prefill_matches_allreduce(world):
+    if _ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    result = mp.Manager().dict()
+    mp.spawn(_sp_worker, args=(world, 29571 + world, result), nprocs=world, join=True)
+    assert len(result) == world
+    # reduce-scatter + all-gather instead of the all-reduce: fp32 summation order only
+    assert max(result.values()) < 5e-2, dict(result)
