@@ -114,35 +114,27 @@ __global__ void kda_conv_commit_kernel(KdaArgs a) {
   for (int i = 0; i < T - 1; ++i) win[(int64_t)i * C + c] = f2bf(rows[i]);
 }
 
-// grid (H, Dh/32, sequences).  Rows are staged 8 at a time in shared memory (normalised q, k, the decay factor
-// exp(g), this CTA's 32 values of v, beta) by all 128 threads with coalesced loads, so the sequential recurrence
-// only reads shared memory; the state stays in registers.
+// grid (H, Dh/32, sequences).  Rows are staged 8 at a time in shared memory (normalised q, k, the decay g,
+// this CTA's 32 values of v, beta) by all 128 threads with coalesced loads, so the sequential recurrence only reads
+// shared memory; the state stays in registers.
 constexpr int kRecRows = 8;
 template <int DH>
 __global__ void __launch_bounds__(128) kda_recurrent_kernel(KdaArgs a) {
   pdl_trigger();                       // dependents (the next projection) may start prefetching
   constexpr int KP = DH / 4;
-  constexpr int SEG = KP + 4;          // padded segment: the 4 threads of a row read 4 distinct bank groups
-  __shared__ __align__(16) float sq[kRecRows][4 * SEG], sk[kRecRows][4 * SEG], sg[kRecRows][4 * SEG];
-  __shared__ float sv[kRecRows][32], sb[kRecRows];
+  __shared__ float sq[kRecRows][DH], sk[kRecRows][DH], sg[kRecRows][DH], sv[kRecRows][32], sb[kRecRows];
   const int h = blockIdx.x, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int vr = tid >> 2, kq = tid & 3;
   const int v0 = blockIdx.y * 32, v = v0 + vr;
-  // thread (vr, kq) owns the contiguous state channels [kq KP, (kq + 1) KP) of value row v: 16-byte state loads
-  // and stores, and 16-byte shared-memory reads of q, k and the decay (one per 4 channels); kda_decode.cu uses
-  // the same ownership and summation order, so a commit replay here reproduces its states bit for bit
+  // thread (vr, kq) owns state channels kq + 4 j (interleaved: the 4 threads of a row read 4 banks)
   const int HD = a.H * DH;
   const int base = a.row0[b], n = a.nrows[b];
   const int64_t sstride = (int64_t)a.H * DH * DH;
   float S[KP];
-  const float4* sin = reinterpret_cast<const float4*>(a.S_pool + a.s_in[b] * sstride + ((int64_t)h * DH + v) * DH +
-                                                      kq * KP);
+  const float* sin = a.S_pool + a.s_in[b] * sstride + ((int64_t)h * DH + v) * DH + kq;
 #pragma unroll
-  for (int i = 0; i < KP / 4; ++i) {
-    const float4 t = sin[i];
-    S[4 * i] = t.x; S[4 * i + 1] = t.y; S[4 * i + 2] = t.z; S[4 * i + 3] = t.w;
-  }
+  for (int j = 0; j < KP; ++j) S[j] = sin[4 * j];
   const float ea = __expf(a.a_log[h]);
   for (int r0 = 0; r0 < n; r0 += kRecRows) {
     const int nr = min(kRecRows, n - r0);
@@ -160,54 +152,43 @@ __global__ void __launch_bounds__(128) kda_recurrent_kernel(KdaArgs a) {
         k[i] = bf2f(row[HD + h * DH + c]);
         qq += q[i] * q[i];
         kk += k[i] * k[i];
-        sg[rr][(c / KP) * SEG + c % KP] =
-            __expf(a.lower * sigmoidf_(ea * (bf2f(a.f[(int64_t)t * HD + h * DH + c]) + a.dt_bias[h * DH + c])));
+        sg[rr][c] = a.lower * sigmoidf_(ea * (bf2f(a.f[(int64_t)t * HD + h * DH + c]) + a.dt_bias[h * DH + c]));
       }
       qq = warp_sum(qq);
       kk = warp_sum(kk);
       const float qn = rsqrtf(qq + 1e-6f) * rsqrtf((float)DH), kn = rsqrtf(kk + 1e-6f);
 #pragma unroll
       for (int i = 0; i < PL; ++i) {
-        const int c = lane + 32 * i, pc = (c / KP) * SEG + c % KP;
-        sq[rr][pc] = q[i] * qn;
-        sk[rr][pc] = k[i] * kn;
+        sq[rr][lane + 32 * i] = q[i] * qn;
+        sk[rr][lane + 32 * i] = k[i] * kn;
       }
       sv[rr][lane] = bf2f(row[2 * HD + h * DH + v0 + lane]);
       if (lane == 0) sb[rr] = sigmoidf_(bf2f(a.proj[(int64_t)t * a.ldp + a.b_off + h]));
     }
     __syncthreads();
     for (int rr = 0; rr < nr; ++rr) {
-      const float4* gp = reinterpret_cast<const float4*>(&sg[rr][kq * SEG]);
-      const float4* kp = reinterpret_cast<const float4*>(&sk[rr][kq * SEG]);
-      const float4* qp = reinterpret_cast<const float4*>(&sq[rr][kq * SEG]);
       float dot = 0.f;
 #pragma unroll
-      for (int i = 0; i < KP / 4; ++i) {
-        const float4 gv = gp[i], kv = kp[i];
-        S[4 * i] *= gv.x;     dot += S[4 * i] * kv.x;
-        S[4 * i + 1] *= gv.y; dot += S[4 * i + 1] * kv.y;
-        S[4 * i + 2] *= gv.z; dot += S[4 * i + 2] * kv.z;
-        S[4 * i + 3] *= gv.w; dot += S[4 * i + 3] * kv.w;
+      for (int j = 0; j < KP; ++j) {
+        S[j] *= __expf(sg[rr][kq + 4 * j]);
+        dot += S[j] * sk[rr][kq + 4 * j];
       }
       dot = group_sum<4>(dot);
       const float vn = sb[rr] * (sv[rr][vr] - dot);
       float o = 0.f;
 #pragma unroll
-      for (int i = 0; i < KP / 4; ++i) {
-        const float4 kv = kp[i], qv = qp[i];
-        S[4 * i] += vn * kv.x;     o += S[4 * i] * qv.x;
-        S[4 * i + 1] += vn * kv.y; o += S[4 * i + 1] * qv.y;
-        S[4 * i + 2] += vn * kv.z; o += S[4 * i + 2] * qv.z;
-        S[4 * i + 3] += vn * kv.w; o += S[4 * i + 3] * qv.w;
+      for (int j = 0; j < KP; ++j) {
+        S[j] += vn * sk[rr][kq + 4 * j];
+        o += S[j] * sq[rr][kq + 4 * j];
       }
       o = group_sum<4>(o);
       if (a.o_raw && kq == 0) a.o_raw[(int64_t)(base + r0 + rr) * HD + h * DH + v] = o;
     }
     __syncthreads();
   }
-  float4* sout = reinterpret_cast<float4*>(a.S_pool + a.s_out[b] * sstride + ((int64_t)h * DH + v) * DH + kq * KP);
+  float* sout = a.S_pool + a.s_out[b] * sstride + ((int64_t)h * DH + v) * DH + kq;
 #pragma unroll
-  for (int i = 0; i < KP / 4; ++i) sout[i] = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
+  for (int j = 0; j < KP; ++j) sout[4 * j] = S[j];
 }
 
 // one warp per (row, head)

@@ -11,9 +11,9 @@
 //      outputs rounded to bf16 and stored (the commit replay re-reads them);
 //   4. per row: l2-normalised q, k, the decay factor exp(g) (once per channel, not per state row) and beta
 //      (one warp per row);
-//   5. the delta-rule recurrence over the rows with thread (v, kq) holding the contiguous channels
-//      S[v][32 kq .. 32 kq + 31], exactly the arithmetic of kda_recurrent_kernel (kda.cu), so a commit that replays
-//      fewer rows from the stored conv outputs and decay logits reproduces the state;
+//   5. the delta-rule recurrence over the rows with thread (v, kq) holding S[v][kq + 4j], exactly the arithmetic
+//      of kda_recurrent_kernel (kda.cu), so a commit that replays fewer rows from the stored conv outputs and
+//      decay logits reproduces the state;
 //   6. the gated RMS norm of every row's head output (one warp per row), written as the o_proj input.
 // The recurrence reads S_in and writes S_out (double buffer), as the unfused path does.
 //
@@ -31,19 +31,16 @@ constexpr int DH = 128;
 constexpr int kThreads = 512;
 constexpr int kMaxRows = 16;
 constexpr int kWP = DH + 64;     // shared pitch of a weight row: the two rows a quarter-warp reads fall in disjoint banks
-constexpr int KP = DH / 4;       // state channels per thread of the recurrence
-constexpr int SEG = KP + 4;      // padded 32-channel segment of q / k / decay rows (4 threads of a row: 4 bank groups)
-__device__ __forceinline__ int pc(int c) { return (c / KP) * SEG + c % KP; }
 
 struct Smem {
   alignas(16) uint8_t wf[DH][kWP];
   alignas(16) uint8_t wg[DH][kWP];
   float f[kMaxRows][DH];          // decay logits (bf16 values)
   float gate[kMaxRows][DH];       // output-gate logits (bf16 values)
-  alignas(16) float q[kMaxRows][4 * SEG];   // conv outputs (bf16 values), then normalised (padded: pc())
-  alignas(16) float k[kMaxRows][4 * SEG];
+  float q[kMaxRows][DH];          // conv outputs (bf16 values), then normalised
+  float k[kMaxRows][DH];
   float v[kMaxRows][DH];
-  alignas(16) float g[kMaxRows][4 * SEG];   // decay factors exp(g), computed once per channel (padded)
+  float g[kMaxRows][DH];          // decay factors exp(g), computed once per channel
   float o[kMaxRows][DH];          // recurrence outputs
   float beta[kMaxRows];
 };
@@ -130,8 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_decode_kernel(KdaArgs a) {
     for (int i = 0; i < 3; ++i) xs[i] = bf2f(win[(int64_t)i * C3]);
 #pragma unroll
     for (int t = 0; t < kMaxRows; ++t) xs[3 + t] = t < n ? bf2f(a.proj[(int64_t)(base + t) * a.ldp + cch]) : 0.f;
-    float* dst = part == 0 ? &sm.q[0][0] : (part == 1 ? &sm.k[0][0] : &sm.v[0][0]);
-    const int pitch = part == 2 ? DH : 4 * SEG, col = part == 2 ? cc : pc(cc);
+    float (*dst)[DH] = part == 0 ? sm.q : (part == 1 ? sm.k : sm.v);
 #pragma unroll
     for (int t = 0; t < kMaxRows; ++t) {
       if (t >= n) break;
@@ -140,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1) kda_decode_kernel(KdaArgs a) {
       for (int i = 0; i < 4; ++i) s += w[i] * xs[t + i];
       const __nv_bfloat16 o = f2bf(siluf_(s));
       a.qkv[(int64_t)(base + t) * C3 + cch] = o;
-      dst[t * pitch + col] = __bfloat162float(o);
+      dst[t][cc] = __bfloat162float(o);
     }
   }
   __syncthreads();
@@ -154,67 +150,54 @@ __global__ void __launch_bounds__(kThreads, 1) kda_decode_kernel(KdaArgs a) {
 #pragma unroll
     for (int i = 0; i < PL; ++i) {
       const int c = lane + 32 * i;
-      qv[i] = sm.q[rr][pc(c)];
-      kv[i] = sm.k[rr][pc(c)];
+      qv[i] = sm.q[rr][c];
+      kv[i] = sm.k[rr][c];
       qq += qv[i] * qv[i];
       kk += kv[i] * kv[i];
-      sm.g[rr][pc(c)] = __expf(a.lower * sigmoidf_(ea * (sm.f[rr][c] + a.dt_bias[h * DH + c])));
+      sm.g[rr][c] = __expf(a.lower * sigmoidf_(ea * (sm.f[rr][c] + a.dt_bias[h * DH + c])));
     }
     qq = warp_sum(qq);
     kk = warp_sum(kk);
     const float qn = rsqrtf(qq + 1e-6f) * rsqrtf((float)DH), kn = rsqrtf(kk + 1e-6f);
 #pragma unroll
     for (int i = 0; i < PL; ++i) {
-      sm.q[rr][pc(lane + 32 * i)] = qv[i] * qn;
-      sm.k[rr][pc(lane + 32 * i)] = kv[i] * kn;
+      sm.q[rr][lane + 32 * i] = qv[i] * qn;
+      sm.k[rr][lane + 32 * i] = kv[i] * kn;
     }
     if (lane == 0) sm.beta[rr] = sigmoidf_(bf2f(a.proj[(int64_t)(base + rr) * a.ldp + a.b_off + h]));
   }
   __syncthreads();
 
-  // 5. recurrence: thread (vr, kq) owns S[vr][kq KP + j], j < KP (the ownership and summation order of
-  //    kda_recurrent_kernel in kda.cu); q / k / decay read as 16-byte vectors from the padded rows
+  // 5. recurrence: thread (vr, kq) owns S[vr][kq + 4j]
   {
+    constexpr int KP = DH / 4;
     const int vr = tid >> 2, kq = tid & 3;
     const int64_t sstride = (int64_t)a.H * DH * DH;
     float S[KP];
-    const float4* sin =
-        reinterpret_cast<const float4*>(a.S_pool + a.s_in[b] * sstride + ((int64_t)h * DH + vr) * DH + kq * KP);
+    const float* sin = a.S_pool + a.s_in[b] * sstride + ((int64_t)h * DH + vr) * DH + kq;
 #pragma unroll
-    for (int i = 0; i < KP / 4; ++i) {
-      const float4 t = sin[i];
-      S[4 * i] = t.x; S[4 * i + 1] = t.y; S[4 * i + 2] = t.z; S[4 * i + 3] = t.w;
-    }
+    for (int j = 0; j < KP; ++j) S[j] = sin[4 * j];
     for (int rr = 0; rr < n; ++rr) {
-      const float4* gp = reinterpret_cast<const float4*>(&sm.g[rr][kq * SEG]);
-      const float4* kp = reinterpret_cast<const float4*>(&sm.k[rr][kq * SEG]);
-      const float4* qp = reinterpret_cast<const float4*>(&sm.q[rr][kq * SEG]);
       float dot = 0.f;
 #pragma unroll
-      for (int i = 0; i < KP / 4; ++i) {
-        const float4 gv = gp[i], kv = kp[i];
-        S[4 * i] *= gv.x;     dot += S[4 * i] * kv.x;
-        S[4 * i + 1] *= gv.y; dot += S[4 * i + 1] * kv.y;
-        S[4 * i + 2] *= gv.z; dot += S[4 * i + 2] * kv.z;
-        S[4 * i + 3] *= gv.w; dot += S[4 * i + 3] * kv.w;
+      for (int j = 0; j < KP; ++j) {
+        S[j] *= sm.g[rr][kq + 4 * j];
+        dot += S[j] * sm.k[rr][kq + 4 * j];
       }
       dot = group_sum<4>(dot);
       const float vn = sm.beta[rr] * (sm.v[rr][vr] - dot);
       float o = 0.f;
 #pragma unroll
-      for (int i = 0; i < KP / 4; ++i) {
-        const float4 kv = kp[i], qv = qp[i];
-        S[4 * i] += vn * kv.x;     o += S[4 * i] * qv.x;
-        S[4 * i + 1] += vn * kv.y; o += S[4 * i + 1] * qv.y;
-        S[4 * i + 2] += vn * kv.z; o += S[4 * i + 2] * qv.z;
-        S[4 * i + 3] += vn * kv.w; o += S[4 * i + 3] * qv.w;
+      for (int j = 0; j < KP; ++j) {
+        S[j] += vn * sm.k[rr][kq + 4 * j];
+        o += S[j] * sm.q[rr][kq + 4 * j];
       }
       o = group_sum<4>(o);
       if (kq == 0) sm.o[rr][vr] = o;
     }
-    float4* sout = reinterpret_cast<float4*>(a.S_pool + a.s_out[b] * sstride + ((int64_t)h * DH + vr) * DH + kq * KP);
+    float* sout = a.S_pool + a.s_out[b] * sstride + ((int64_t)h * DH + vr) * DH + kq;
 #pragma unroll
-    for (int i = 0; i < KP / 4; ++i) sout[i] = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
+    for (int j = 0; j < KP; ++j) sout[4 * j] = S[j];
   }
   __syncthreads();
 
