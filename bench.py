@@ -116,6 +116,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=45)
     ap.add_argument("--model", default="full", choices=["full", "tiny"])
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--ep", action="store_true", help="routed experts expert-parallel over the GPUs (TP elsewhere)")
     return ap.parse_args()
 
 
@@ -141,8 +142,8 @@ def main():
     t0 = time.time()
     llm = LLM(LLMOptions(model=args.model, layers=args.layers if args.layers != 45 else None, max_seqs=1,
                          max_model_len=max_len, prefill_chunk=chunk, speculative=True, k_fixed=K,
-                         force_accept=True, checkpoints=0, cuda_graphs=not args.no_graph), comm=comm, rank=rank,
-              world=world)
+                         force_accept=True, checkpoints=0, cuda_graphs=not args.no_graph, ep=args.ep), comm=comm,
+              rank=rank, world=world)
     torch.cuda.synchronize()
     t_load = time.time() - t0
     eng = llm.engine
@@ -252,7 +253,8 @@ def main():
             "data": "synthetic: random-init weights (seed 0), uniform random token ids",
             "config": {"model": f"glm-5.3-flash {cfg.layers} layers (34 KDA + 11 MLA/DSA), 288 experts top-8 + shared,"
                                 f" EXL3 4bpw, vocab {cfg.vocab}" if args.model == "full" else "glm53-tiny",
-                       "global_batch": 1, "seq_len": args.context, "parallelism": f"tp{world}", "K": K,
+                       "global_batch": 1, "seq_len": args.context,
+                       "parallelism": f"tp{world}" + (f"+ep{world}" if args.ep and world > 1 else ""), "K": K,
                        "tokens_per_step": rows, "acceptance": "forced (all K drafts accepted)",
                        "drafter": "1-layer block drafter (grouped dynamic conv, CUDA graph) in every step",
                        "cuda_graph": not args.no_graph,

@@ -40,6 +40,7 @@ class LLMOptions:
     vtrim_tau: float = 0.0              # verify trimming by drafter confidence (0: off)
     block_verify: bool = False          # sampled requests: block verification instead of standard
     mixed_prefill_chunk: int = 0        # prefill tokens per step while requests decode (0: the whole chunk)
+    ep: bool = False                    # routed experts expert-parallel over the ranks (parallel/ep.py)
 
 
 class LLM:
@@ -66,7 +67,7 @@ class LLM:
             src = W.OverrideSource(src, opts.overrides, opts.override_sha256)
         self.cfg: ModelConfig = cfg
         t0 = time.time()
-        self.weights = W.prepare(src, cfg, rank=rank, world=world, device=dev)
+        self.weights = W.prepare(src, cfg, rank=rank, world=world, device=dev, ep=opts.ep)
         self.load_s = time.time() - t0
         if opts.kv_cache_bytes and not opts.kv_pages:
             opts.kv_pages = max(1, int(opts.kv_cache_bytes // (cfg.kv_bytes_per_token() * opts.page_size)))

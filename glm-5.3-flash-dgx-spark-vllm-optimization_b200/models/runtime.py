@@ -251,7 +251,18 @@ class Runtime:
             self.p_counts = torch.zeros(c.experts, dtype=i32, device=dev)
             self.p_fill = torch.zeros(c.experts, dtype=i32, device=dev)
             P = max(P, PP)
-        if moe0 is not None:
+        # expert parallelism (weights prepared with ep=True): each rank routes its own share of the rows, dispatches
+        # them to the ranks owning their experts and receives their outputs (parallel/ep.py, one exchange and one
+        # scratch for all MoE layers); the shared expert and everything else stay tensor-parallel
+        self.ep = None
+        if moe0 is not None and w.meta.get("ep") and self.tp > 1 and comm is not None:
+            from ..parallel.ep import EPBuffers, EPMoE
+            self.ep_bufs = EPBuffers(c, moe0.gate.n, (R + self.tp - 1) // self.tp, w.rank, w.world, device=dev)
+            self.ep = {lw.index: EPMoE(c, lw.moe.router, lw.moe.bias, lw.moe.gate, lw.moe.up, lw.moe.down, 0,
+                                       w.rank, w.world, bufs=self.ep_bufs)
+                       for lw in w.layers if lw.moe is not None}
+            self.prefill_moe = False
+        if moe0 is not None and self.ep is None:
             # the decode path stores its rotated inputs as duplicated f16 pairs (2 halves per element)
             PX = max(P, 2 * MR * tk)
             self.xh_g = torch.zeros(PX, D, dtype=torch.float16, device=dev)
@@ -567,9 +578,22 @@ class Runtime:
                            self.p_group_expert, self.p_group_offset, self.xd[:P], None, self.yd[:P], c.limit, False)
             Kc.moe_combine(self.yd, self.p_pair_of[:P], c.top_k, self.branch[r0:r1], 0)
 
+    def _moe_ep(self, lw, R):
+        """Expert-parallel routed experts: rank j owns rows [j R / W, (j+1) R / W) of the layer input; its routed
+        outputs land in those rows of the branch (zero elsewhere), so the tensor-parallel reduction of the branch
+        (shared expert partials added) assembles every row."""
+        W, j = self.tp, self.w.rank
+        r0, r1 = R * j // W, R * (j + 1) // W
+        self.branch[:R].zero_()
+        self.ep[lw.index].forward(self.normed[r0:r1], out=self.branch[r0:r1])
+        self._shared_expert(lw, R)
+
     def _moe(self, lw, R):
         c, m = self.cfg, lw.moe
         Kc = K.C()
+        if self.ep is not None:
+            self._moe_ep(lw, R)
+            return
         if self.prefill_moe and R > MOE_PREFILL_MIN_ROWS:
             self._moe_prefill(lw, R)
             self._shared_expert(lw, R)

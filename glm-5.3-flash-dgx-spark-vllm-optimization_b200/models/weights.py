@@ -517,8 +517,12 @@ def _rows(x: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
 
 def prepare(src: TensorSource, cfg: ModelConfig, *, rank: int = 0, world: int = 1,
             device: str | torch.device = "cpu", layers: list[int] | None = None,
-            progress: Callable[[str], None] | None = None) -> Weights:
-    """Quantise and shard a checkpoint into runtime weights for rank ``rank`` of ``world``."""
+            progress: Callable[[str], None] | None = None, ep: bool = False) -> Weights:
+    """Quantise and shard a checkpoint into runtime weights for rank ``rank`` of ``world``.  ``ep``: the routed
+    experts are sharded by expert (rank j holds experts [j E/W, (j+1) E/W) at full width, for the expert-parallel
+    MoE of parallel/ep.py) instead of by width; everything else stays tensor-parallel."""
+    if ep and world > 1 and cfg.experts % world:
+        raise ValueError(f"{cfg.experts} experts do not split over {world} ranks")
     c = cfg
     c.validate(world)
     dev = torch.device(device)
@@ -589,7 +593,10 @@ def prepare(src: TensorSource, cfg: ModelConfig, *, rank: int = 0, world: int = 
     def experts(i, proj):
         st = src.experts(i, proj, c.experts)
         tr, su, sv = st.trellis, st.suh, st.svh
-        if world > 1:
+        if world > 1 and ep:             # expert-parallel: this rank's experts at full width
+            el = c.experts // world
+            tr, su, sv = tr[rank * el:(rank + 1) * el], su[rank * el:(rank + 1) * el], sv[rank * el:(rank + 1) * el]
+        elif world > 1:
             if proj == "down_proj":      # row-parallel: split k tiles and suh
                 tr, su = _rows(tr, rank, world, 1), _rows(su, rank, world, 1)
             else:                        # column-parallel: split n tiles and svh
@@ -620,4 +627,5 @@ def prepare(src: TensorSource, cfg: ModelConfig, *, rank: int = 0, world: int = 
             lw.moe = moe(i)
         out_layers.append(lw)
     head = lin(_rows(g("lm_head.weight"), rank, world))
-    return Weights(c, bf(g(P + "embed_tokens.weight")), out_layers, bf(g(P + "norm.weight")), head, rank, world)
+    return Weights(c, bf(g(P + "embed_tokens.weight")), out_layers, bf(g(P + "norm.weight")), head, rank, world,
+                   meta={"ep": bool(ep and world > 1)})

@@ -99,25 +99,21 @@ class EPExchange:
                                f"52/53: a receive buffer overflowed)")
 
 
-class EPMoE:
-    """One routed-MoE layer, experts sharded over the process group; forward(x [T, K] bf16) -> [T, K] fp32."""
+class EPBuffers:
+    """The exchange and the scratch of the expert-parallel MoE, shared by every MoE layer of a model (the layers run
+    one after another, each step alternating the exchange's parity)."""
 
-    def __init__(self, cfg, router: torch.Tensor, bias: torch.Tensor, gate: Exl3Stack, up: Exl3Stack,
-                 down: Exl3Stack, max_tokens: int, rank: int = 0, world: int = 1, group=None, device="cuda"):
-        self.cfg, self.rank, self.world = cfg, rank, world
+    def __init__(self, cfg, N: int, max_tokens: int, rank: int = 0, world: int = 1, group=None, device="cuda"):
         dev = torch.device(device)
         E, tk = cfg.experts, cfg.top_k
         self.El = E // world
-        self.gate, self.up, self.down = gate, up, down           # local experts (El)
-        self.router, self.bias = router, bias
         Kd = cfg.hidden
-        N = gate.n
         self.max_tokens = max_tokens
-        self.cap = max_tokens * tk
+        self.cap = max(1, max_tokens) * tk
         self.recv_cap = world * self.cap
         self.x_ex = EPExchange(world, rank, self.El, self.cap, Kd, dev, group)
         i32, f32 = torch.int32, torch.float32
-        T, P = max_tokens, self.cap
+        T, P = max(1, max_tokens), self.cap
         self.logits = torch.zeros(T, E, dtype=f32, device=dev)
         self.topk_ids = torch.zeros(T, tk, dtype=i32, device=dev)
         self.topk_w = torch.zeros(T, tk, dtype=f32, device=dev)
@@ -143,6 +139,38 @@ class EPMoE:
         self.out = torch.zeros(T, Kd, dtype=f32, device=dev)
         self.step = 0
 
+
+class EPMoE:
+    """One routed-MoE layer, experts sharded over the process group; forward(x [T, K] bf16) -> [T, K] fp32.  The
+    exchange and scratch come from ``bufs`` (shared by the layers of a model) or are allocated for this layer."""
+
+    def __init__(self, cfg, router: torch.Tensor, bias: torch.Tensor, gate: Exl3Stack, up: Exl3Stack,
+                 down: Exl3Stack, max_tokens: int, rank: int = 0, world: int = 1, group=None, device="cuda",
+                 bufs: EPBuffers | None = None):
+        self.cfg, self.rank, self.world = cfg, rank, world
+        self.gate, self.up, self.down = gate, up, down           # local experts (El)
+        self.router, self.bias = router, bias
+        self.b = bufs or EPBuffers(cfg, gate.n, max_tokens, rank, world, group, device)
+        self.El = self.b.El
+        self.max_tokens = self.b.max_tokens
+        self.cap, self.recv_cap = self.b.cap, self.b.recv_cap
+        self.x_ex = self.b.x_ex
+
+    def __getattr__(self, name):
+        # scratch tensors live in the shared buffers
+        b = self.__dict__.get("b")
+        if b is not None and hasattr(b, name):
+            return getattr(b, name)
+        raise AttributeError(name)
+
+    @property
+    def step(self) -> int:
+        return self.b.step
+
+    @step.setter
+    def step(self, v: int) -> None:
+        self.b.step = v
+
     def tensor_core_experts(self, T: int) -> bool:
         """tcgen05 grouped GEMMs (trellis decoded into shared memory) once the rows per local expert reach 16;
         the register-decode (mma.sync) kernels below that.  Each rank decides for the rows it receives (about
@@ -150,10 +178,12 @@ class EPMoE:
         return T * self.cfg.top_k >= 16 * self.El and self.gate.n % 128 == 0
 
     @torch.no_grad()
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """x [T, K] bf16 -> [T, K] fp32 (into ``out`` when given: a contiguous fp32 [T, K] view)."""
         c = self.cfg
         Kc = K.C()
         T = x.shape[0]
+        dst = self.out[:T] if out is None else out
         if T > self.max_tokens:
             raise ValueError("more tokens than the exchange buffers hold")
         tk = c.top_k
@@ -176,11 +206,11 @@ class EPMoE:
         ex = self.x_ex
         st = ex.state[p]
         st[3].fill_(P)
-        Kc.ep_moe_step(x, self.out[:T], self.pair_token[:P], self.pair_expert[:P], self.pair_w[:P],
+        Kc.ep_moe_step(x, dst, self.pair_token[:P], self.pair_expert[:P], self.pair_w[:P],
                        self.pair_of[:P], self.gate.trellis, self.gate.suh, self.gate.svh, self.up.trellis,
                        self.up.suh, self.up.svh, self.down.trellis, self.down.suh, self.down.svh, ex.peer[p],
                        ex.local[p], st, self.seg, self.groups, self.rp_i, self.rp_w, self.rp_out, self.xh_g,
                        self.xh_u, self.xd, self.El, self.rank, self.world, self.cap, self.recv_cap, tk, c.limit,
                        self.tensor_core_experts(T))
         self.step += 1
-        return self.out[:T]
+        return dst

@@ -161,3 +161,59 @@ def test_sequence_parallel_prefill_matches_allreduce(world):
     assert len(result) == world
     # reduce-scatter + all-gather instead of the all-reduce: fp32 summation order only
     assert max(result.values()) < 5e-2, dict(result)
+
+
+def _ep_worker(rank, world, port, result):
+    """The model with its routed experts expert-parallel (weights sharded by expert, rows of each layer split over
+    the ranks, dispatch and combine through the peers' buffers) against the tensor-parallel model: logits of a
+    prefill chunk and of two decode windows (one captured as a CUDA graph and replayed)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from glm53.config import tiny_config
+    from glm53.models import weights as W
+    from glm53.models.runtime import Graphed, Runtime, RuntimeConfig
+    from glm53.models.session import Sequence
+    from glm53.parallel import dist as D
+    D.init(timeout_s=60)
+    try:
+        cfg = tiny_config()
+        dev = torch.device("cuda", rank)
+        rc = RuntimeConfig(max_rows=128, max_seqs=1, kv_slots=64 * 8, block_size=64, max_blocks=8)
+        g = torch.Generator().manual_seed(9)
+        prompt = torch.randint(16, cfg.vocab, (160,), generator=g).tolist()
+        outs = []
+        for ep in (False, True):
+            w = W.prepare(W.RandomSource(cfg, seed=0, device=dev), cfg, rank=rank, world=world, device=dev, ep=ep)
+            rt = Runtime(w, rc, comm=D.NcclComm())
+            assert (rt.ep is not None) == ep
+            seq = Sequence(rt)
+            lg = [seq.prefill(prompt, chunk=128).clone()]
+            toks = [3, 1, 4, 1, 5, 9, 2, 6]
+            seq.stage(toks, list(range(8)))
+            lg.append(rt.forward(8, keep_window=True).clone())
+            graph = Graphed(lambda: rt.forward(8, keep_window=True))
+            graph()
+            lg.append(graph().clone())
+            if rt.px is not None:
+                rt.px.check()
+            if rt.ep is not None:
+                rt.ep_bufs.x_ex.check()
+            outs.append(torch.cat([x.flatten() for x in lg]))
+            del rt, w
+        result[rank] = (outs[0] - outs[1]).abs().max().item()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_expert_parallel_model_matches_tensor_parallel(world):
+    if _ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    result = mp.Manager().dict()
+    mp.spawn(_ep_worker, args=(world, 29591 + world, result), nprocs=world, join=True)
+    assert len(result) == world
+    # full-width experts on the owner vs width-sharded experts summed over ranks: fp32 summation order only
+    assert max(result.values()) < 5e-2, dict(result)
