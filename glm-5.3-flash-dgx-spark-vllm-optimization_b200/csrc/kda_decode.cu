@@ -67,6 +67,13 @@ __global__ void __launch_bounds__(kThreads, 1) kda_decode_kernel(KdaArgs a) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) w[i] = a.conv_w[(int64_t)cch * 4 + i];
   }
+  // the head's input state (64 KB, contiguous) was written by an earlier step, not by the kernel this one waits
+  // for: pull it towards L2 now, so the recurrence's state loads (issued after three dependent phases) hit L2
+  if (tid < 16) {
+    const float* sblk = a.S_pool + a.s_in[blockIdx.y] * ((int64_t)a.H * DH * DH) + (int64_t)h * DH * DH;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(sblk + tid * (DH * DH / 16)),
+                 "r"((uint32_t)(DH * DH / 16 * 4)) : "memory");
+  }
   pdl_wait();                                                 // the input projection and the states are ready
   const int base = a.row0[b], n = min(a.nrows[b], kMaxRows);
   __syncthreads();

@@ -35,8 +35,8 @@ class GPUBackend:
         self.world = weights.world
         dev = weights.device
         self.sampler = GreedySampler(rc.logit_rows, self.world, weights.rank * weights.head.n, comm, dev)
-        self.drafter = BlockDrafter(self.cfg, weights, device=dev) if drafter else None
-        self.draft_sampler = GreedySampler(8, self.world, weights.rank * weights.head.n, comm, dev)
+        self.drafter = BlockDrafter(self.cfg, weights, device=dev, max_batch=rc.max_seqs) if drafter else None
+        self.draft_sampler = GreedySampler(8 * rc.max_seqs, self.world, weights.rank * weights.head.n, comm, dev)
         self.cuda_graphs = cuda_graphs
         self._graphs: dict = {}
         self.vocab = self.cfg.vocab
@@ -137,6 +137,23 @@ class GPUBackend:
                 self._graphs[("draft", k)] = g
             lg = g()
         return self.draft_sampler(lg).tolist(), lg
+
+    @torch.no_grad()
+    def draft_batch(self, last_tokens: list[int], hiddens: list[torch.Tensor], k: int):
+        """K draft tokens (greedy) of several requests in one drafter pass (one CUDA graph per (k, batch)): per
+        request its drafts, and the logits [B k, V_local] (request b's rows at [b k, (b+1) k))."""
+        B = len(last_tokens)
+        self.drafter.stage_batch(last_tokens, hiddens, k)
+        if not self.cuda_graphs:
+            lg = self.drafter.run_batch(B, k)
+        else:
+            g = self._graphs.get(("draft", k, B))
+            if g is None:
+                g = Graphed(lambda: self.drafter.run_batch(B, k))
+                self._graphs[("draft", k, B)] = g
+            lg = g()
+        toks = self.draft_sampler(lg).tolist()
+        return [toks[b * k:(b + 1) * k] for b in range(B)], lg
 
     @torch.no_grad()
     def draft_confidence(self, logits: torch.Tensor) -> list[float]:

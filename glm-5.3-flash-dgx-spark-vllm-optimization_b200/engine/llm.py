@@ -276,13 +276,15 @@ class LLMEngine:
                 lps = self._logprobs(logits[want], [toks[i] for i in want], [finishing[i][0] for i in want])
                 for i, lp in zip(want, lps):
                     finishing[i][0]._new_lp = [lp]
+            to_draft = []
             for i, (r, row_idx) in enumerate(finishing):
                 r.state = State.RUNNING
                 r.first_token_time = time.time()
                 r.hidden = self.b.hidden(row_idx).clone()
                 outs.append(self._emit(r, [toks[i]]))
                 if r.state == State.RUNNING and self.cfg.speculative and self.b.drafter is not None:
-                    self._draft(r)
+                    to_draft.append(r)
+            self._draft_many(to_draft)
         return outs
 
     def _sample_rows(self, logits: torch.Tensor, reqs: list[Request]) -> list[int]:
@@ -300,9 +302,27 @@ class LLMEngine:
             out.append(sample_token(full[i], p, seed_key(r, len(r.output))))
         return out
 
-    def _draft(self, r: Request) -> None:
+    def _draft_many(self, reqs: list[Request]) -> None:
+        """Drafts of several requests: those with the same draft length share one drafter pass (one graph per
+        (k, batch) in the backend) instead of one pass per request."""
+        if len(reqs) <= 1 or not hasattr(self.b, "draft_batch"):
+            for r in reqs:
+                self._draft(r)
+            return
+        groups: dict[int, list[Request]] = {}
+        for r in reqs:
+            groups.setdefault(r.adaptive.current(), []).append(r)
+        for k, rs in groups.items():
+            if len(rs) == 1:
+                self._draft(rs[0])
+                continue
+            drafts, lg = self.b.draft_batch([r.output[-1] for r in rs], [r.hidden for r in rs], k)
+            for b, r in enumerate(rs):
+                self._draft(r, (drafts[b], lg[b * k:(b + 1) * k]))
+
+    def _draft(self, r: Request, drafted=None) -> None:
         k = r.adaptive.current()
-        drafts, lg = self.b.draft(r.output[-1], r.hidden, k)
+        drafts, lg = drafted if drafted is not None else self.b.draft(r.output[-1], r.hidden, k)
         n = k
         if self.cfg.vtrim_tau > 0 and not self.cfg.force_accept:
             # verify trimming (the reference's n* rule, code/fork/glm53_spec_vtrim.py:11-23): rows past the first
@@ -391,11 +411,13 @@ class LLMEngine:
                 r.cur = 1 - r.cur
                 self.kv.commit_tokens(r.cache, r.tokens + r._new[:keeps[i] - 1], r.pos)
                 self._checkpoint(r)
+        to_draft = []
         for (r, rows), keep in zip(batch, keeps):
             r.hidden = self.b.hidden(r._last_row).clone()
             outs.append(self._emit(r, r._new))
             if r.state == State.RUNNING and spec:
-                self._draft(r)
+                to_draft.append(r)
+        self._draft_many(to_draft)
         return outs
 
     def _checkpoint(self, r: Request) -> None:

@@ -48,7 +48,7 @@ class DrafterConfig:
 
 class BlockDrafter:
     def __init__(self, cfg: ModelConfig, target_w, dc: DrafterConfig | None = None, seed: int = 1,
-                 device="cuda"):
+                 device="cuda", max_batch: int = 1):
         self.cfg, self.tw = cfg, target_w
         dc = dc or DrafterConfig(heads=max(1, cfg.hidden // 128), head_dim=min(128, cfg.hidden),
                                  mlp_width=2 * cfg.hidden)
@@ -83,12 +83,14 @@ class BlockDrafter:
             return b.to(torch.bfloat16)
         self.conv_a = (lin("drafter.conv_attn.delta", taps * G, D), conv_base("drafter.conv_attn.base"))
         self.conv_m = (lin("drafter.conv_mlp.delta", taps * G, D), conv_base("drafter.conv_mlp.base"))
-        self.delta = torch.zeros(dc.block, taps * G, dtype=torch.bfloat16, device=dev)
-        self.xc = torch.zeros(dc.block, D, dtype=torch.bfloat16, device=dev)
+        # several requests draft in one pass (max_batch blocks of rows, request b's rows at [b k, (b+1) k))
+        self.max_batch = max(1, max_batch)
+        R = dc.block * self.max_batch
+        self.delta = torch.zeros(R, taps * G, dtype=torch.bfloat16, device=dev)
+        self.xc = torch.zeros(R, D, dtype=torch.bfloat16, device=dev)
         g = torch.Generator(device=dev)
         g.manual_seed(_seed_of(seed, "drafter.slot"))
         self.slot_emb = (torch.randn(dc.block, D, generator=g, device=dev) * 0.1).float()
-        R = dc.block
         bf = torch.bfloat16
         self.inp = torch.zeros(R, 2 * D, dtype=bf, device=dev)
         self.emb = torch.zeros(R, 1, D, dtype=bf, device=dev)
@@ -99,13 +101,15 @@ class BlockDrafter:
         self.act = torch.zeros(R, dc.mlp_width, dtype=bf, device=dev)
         self.logits = torch.zeros(R, target_w.head.n, dtype=torch.float32, device=dev)
         self.ids = torch.full((R,), MASK_TOKEN, dtype=torch.int32, device=dev)
-        self.hid = torch.zeros(D, dtype=bf, device=dev)
+        self.hid = torch.zeros(self.max_batch, D, dtype=bf, device=dev)
+        self._k = 1
 
-    def _dconv(self, conv, R: int) -> None:
-        """xc[:R] = grouped dynamic conv of xn[:R] (the kernel deltas projected from xn itself)."""
+    def _dconv(self, conv, R: int, k: int) -> None:
+        """xc[:R] = grouped dynamic conv of xn[:R] within each request's block of k rows (the kernel deltas projected
+        from xn itself)."""
         proj, base = conv
         K.linear8(self.xn[:R], proj.w, proj.s, self.delta[:R])
-        K.C().dconv(self.xn[:R], self.delta[:R], base, self.xc[:R], self.dc.conv_group, self.dc.block)
+        K.C().dconv(self.xn[:R], self.delta[:R], base, self.xc[:R], self.dc.conv_group, k)
 
     @torch.no_grad()
     def forward(self, last_token: torch.Tensor, hidden: torch.Tensor, k: int) -> torch.Tensor:
@@ -121,27 +125,49 @@ class BlockDrafter:
             self.ids[:1].fill_(last_token)
         else:
             self.ids[:1].copy_(last_token)
-        self.hid.copy_(hidden.view(-1))
+        self.hid[0].copy_(hidden.view(-1))
+
+    def stage_batch(self, last_tokens: list[int], hiddens: list[torch.Tensor], k: int) -> None:
+        """Inputs of one draft pass for several requests (outside any CUDA graph): request b's last token goes to
+        row b k of its block (the other rows of the block are MASK) and its target hidden state to hid[b]."""
+        B = len(last_tokens)
+        if B > self.max_batch or k > self.dc.block:
+            raise ValueError("draft batch exceeds the drafter's buffers")
+        ids = torch.full((B, k), MASK_TOKEN, dtype=torch.int32)
+        ids[:, 0] = torch.tensor(last_tokens, dtype=torch.int32)
+        self.ids[:B * k].copy_(ids.view(-1), non_blocking=True)
+        for b, h in enumerate(hiddens):
+            self.hid[b].copy_(h.view(-1))
 
     @torch.no_grad()
     def run(self, k: int) -> torch.Tensor:
-        """The draft block from the staged inputs (static buffers only: capturable as a CUDA graph per k)."""
+        """The draft block of one request from the staged inputs (static buffers only: capturable as a CUDA graph
+        per k)."""
+        return self.run_batch(1, k)
+
+    @torch.no_grad()
+    def run_batch(self, B: int, k: int) -> torch.Tensor:
+        """Draft blocks of B requests in one pass (rows [b k, (b+1) k) of request b; the block attention and the
+        dynamic convolutions stay inside each request's block, the projections read their weights once for all
+        rows).  Returns logits [B k, V_local]; capturable as a CUDA graph per (B, k).  With B = 1 this is the
+        single-request draft, bit for bit."""
         Kc = K.C()
         D = self.cfg.hidden
-        R = max(k, 1)
+        k = max(k, 1)
+        R = B * k
         # [h ; emb(t_i)]
         Kc.embed(self.ids[:R], self.tw.embed, self.emb[:R])
         self.inp[:R, D:].copy_(self.emb[:R, 0])
-        self.inp[:R, :D].copy_(self.hid.view(1, D).expand(R, D))
-        self.x[:R].copy_(self.slot_emb[:R])
+        self.inp[:R, :D].view(B, k, D).copy_(self.hid[:B].view(B, 1, D).expand(B, k, D))
+        self.x[:R].view(B, k, D).copy_(self.slot_emb[:k].view(1, k, D).expand(B, k, D))
         K.linear8(self.inp[:R], self.fc.w, self.fc.s, self.x[:R], K.GEMV_F32_ACC)
         Kc.rmsnorm_f32(self.x[:R], self.n1, self.cfg.eps, self.xn[:R])
-        self._dconv(self.conv_a, R)
+        self._dconv(self.conv_a, R, k)
         K.linear8(self.xc[:R], self.qkv.w, self.qkv.s, self.qkv_buf[:R])
-        Kc.block_attn(self.qkv_buf[:R], self.dc.heads, self.dc.head_dim, R, self.dc.head_dim ** -0.5, self.att[:R])
+        Kc.block_attn(self.qkv_buf[:R], self.dc.heads, self.dc.head_dim, k, self.dc.head_dim ** -0.5, self.att[:R])
         K.linear8(self.att[:R], self.o.w, self.o.s, self.x[:R], K.GEMV_F32_ACC)
         Kc.rmsnorm_f32(self.x[:R], self.n2, self.cfg.eps, self.xn[:R])
-        self._dconv(self.conv_m, R)
+        self._dconv(self.conv_m, R, k)
         K.linear8(self.xc[:R], self.gu.w, self.gu.s, self.act[:R], K.GEMV_SWIGLU, self.cfg.limit)
         K.linear8(self.act[:R], self.down.w, self.down.s, self.x[:R], K.GEMV_F32_ACC)
         Kc.rmsnorm_f32(self.x[:R], self.nf, self.cfg.eps, self.xn[:R])

@@ -591,7 +591,7 @@ class Runtime:
     def _moe(self, lw, R):
         c, m = self.cfg, lw.moe
         Kc = K.C()
-        if self.ep is not None:
+        if getattr(self, "ep", None) is not None:
             self._moe_ep(lw, R)
             return
         if self.prefill_moe and R > MOE_PREFILL_MIN_ROWS:

@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import sys
 import time
 
 import torch
@@ -78,8 +79,13 @@ def main(argv=None):
             rids = [eng.add_request(torch.randint(0, cfg.vocab, (ctx,), generator=gen).tolist(),
                                     SamplingParams(max_tokens=max_len - ctx - 8, ignore_eos=True))
                     for _ in range(conc)]
+            nsteps = 0
             while not (len(eng.running) == conc and all(r.state == State.RUNNING for r in eng.running)):
                 eng.step()
+                nsteps += 1
+                if rank == 0 and nsteps % 16 == 0:
+                    print(f"# prefill: {nsteps} steps, {time.perf_counter() - t0:.1f} s, running "
+                          f"{len(eng.running)}, waiting {len(eng.waiting)}", file=sys.stderr, flush=True)
             sync()
             prefill_s = time.perf_counter() - t0
             for _ in range(args.warmup):

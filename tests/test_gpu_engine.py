@@ -86,3 +86,24 @@ def test_kv_budget_in_bytes_sizes_the_page_pool():
     bpt = llm.cfg.kv_bytes_per_token()
     assert abs(kv_bytes_per_token(llm.backend.rt) - bpt) <= 1
     assert llm.engine.cfg.num_pages == int(budget // (bpt * 64))
+
+
+def test_batched_drafter_equals_single_drafts():
+    """Several requests drafted in one pass (rows of request b at [b k, (b+1) k), attention and dynamic convolutions
+    inside each block) give each request's logits bit for bit as its own single-request pass."""
+    from glm53.config import tiny_config
+    from glm53.models import weights as W
+    from glm53.models.drafter import BlockDrafter
+    cfg = tiny_config()
+    w = W.prepare(W.RandomSource(cfg, seed=0, device="cuda"), cfg, device="cuda")
+    d = BlockDrafter(cfg, w, device="cuda", max_batch=4)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    hid = [(torch.randn(cfg.hidden, device="cuda", generator=g)).to(torch.bfloat16) for _ in range(3)]
+    last = [17, 401, 3999]
+    for k in (4, 7):
+        d.stage_batch(last, hid, k)
+        batched = d.run_batch(3, k).clone()
+        for b in range(3):
+            d.stage(last[b], hid[b])
+            single = d.run(k).clone()
+            assert torch.equal(batched[b * k:(b + 1) * k], single), (k, b)
