@@ -41,6 +41,7 @@ class LLMOptions:
     block_verify: bool = False          # sampled requests: block verification instead of standard
     mixed_prefill_chunk: int = 0        # prefill tokens per step while requests decode (0: the whole chunk)
     ep: bool = False                    # routed experts expert-parallel over the ranks (parallel/ep.py)
+    sp_mla: bool = os.environ.get("GLM53_SP_MLA", "0") == "1"   # row-parallel MLA in sequence-parallel prefill
 
 
 class LLM:
@@ -67,7 +68,7 @@ class LLM:
             src = W.OverrideSource(src, opts.overrides, opts.override_sha256)
         self.cfg: ModelConfig = cfg
         t0 = time.time()
-        self.weights = W.prepare(src, cfg, rank=rank, world=world, device=dev, ep=opts.ep)
+        self.weights = W.prepare(src, cfg, rank=rank, world=world, device=dev, ep=opts.ep, sp_mla=opts.sp_mla)
         self.load_s = time.time() - t0
         if opts.kv_cache_bytes and not opts.kv_pages:
             opts.kv_pages = max(1, int(opts.kv_cache_bytes // (cfg.kv_bytes_per_token() * opts.page_size)))

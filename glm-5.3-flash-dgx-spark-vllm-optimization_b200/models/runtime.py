@@ -410,8 +410,12 @@ class Runtime:
             # this rank's rows: reduce-scatter of the block's partials, then post + pre on those rows only
             r0, r1 = self._sp
             n = r1 - r0
-            rs = self.rs[:n]
-            self.comm.reduce_scatter(rs, self.branch[:R])
+            if getattr(self, "_branch_local", False):     # the block computed this rank's rows completely
+                rs = self.branch[r0:r1]
+                self._branch_local = False
+            else:
+                rs = self.rs[:n]
+                self.comm.reduce_scatter(rs, self.branch[:R])
             pre = (hc.fn, hc.base, hc.scale, norm_w, self.normed[r0:r1], self.post[nxt][r0:r1],
                    self.comb[nxt][r0:r1]) if hc is not None else (None,) * 7
             Kc.hc_post_pre(X[r0:r1], rs, self.post[cur][r0:r1], self.comb[cur][r0:r1], *pre, self.part[:n], c.eps,
@@ -508,9 +512,61 @@ class Runtime:
         Kc.kda_gated_norm(self.ko[:R], self.kg[:R], k.o_norm, self.kout[:R], H, Dh, c.eps)
         self._final_linear(self.kout[:R], k.o_proj, R)
 
+    def _mla_rows(self, lw, R):
+        """Row-parallel MLA for a sequence-parallel prefill chunk: the latent / index caches and the indexer keys
+        for every row (each rank's rows attend to all earlier tokens), then the query, DSA selection, sparse
+        attention and output projection of this rank's rows over all heads, with the full-head projections
+        (``MLAW.full``).  The rows come out complete, so the block needs no reduce-scatter; the per-row key gathers
+        of the attention are divided by the world size."""
+        c, a, b = self.cfg, lw.mla, self.batch
+        f = a.full
+        Kc = K.C()
+        li = self.mla_index[lw.index]
+        H, L, rope, nope, qd = c.heads, c.kv_lora, c.qk_rope, c.qk_nope, c.qk_dim
+        r0, r1 = self._sp
+        n = r1 - r0
+        K.linear8(self.normed[:R], a.qkv_a.w, a.qkv_a.s, self.qkv_a[:R])
+        Kc.mla_prep(self.qkv_a[:R], a.q_norm, a.kv_norm, self.qr[:R], self.kv[li], self.kv_scale[li],
+                    self.kpe[li] if rope else None, b.slots[:R], b.positions[:R], c.q_lora, L, rope, c.eps,
+                    c.rope_theta)
+        K.linear_bf16(self.normed[:R], a.index.proj, self.iproj[:R])
+        Kc.dsa_update(self.iproj[:R], a.index.ln_w, a.index.ln_b, a.index.ape, self.ik_rows, self.ig_rows,
+                      self.ik_ring[li], self.ig_ring[li], self.pool[li], self.pool_scale[li], b.slots[:R],
+                      b.positions[:R], b.block_table, b.row_seq[:R], b.kda_seq[:, :b.B], self.rc.block_size,
+                      c.index_heads, c.kpool, c.eps)
+        # this rank's rows x all heads fit the per-rank buffers (R x H/W elements per row = n x H)
+        q = self.q.view(-1)[:n * H * qd].view(n, H, qd)
+        q_lat = self.q_lat.view(-1)[:n * H * L].view(n, H, L)
+        o_lat = self.o_lat.view(-1)[:n * H * L].view(n, H, L)
+        ob = self.obuf.view(-1)[:n * H * c.v_dim].view(n, H, c.v_dim)
+        K.linear8(self.qr[r0:r1], f.q_b.w, f.q_b.s, q.view(n, H * qd))
+        if rope:
+            Kc.rope_q(q, b.positions[r0:r1], nope, rope, c.rope_theta)
+        K.linear8(q[:, :, :nope].transpose(0, 1), f.w_uk_t.w, f.w_uk_t.s, q_lat.transpose(0, 1))
+        K.linear8(self.qr[r0:r1], a.index.wq_b.w, a.index.wq_b.s, self.qi[r0:r1])
+        AR = self.sel.shape[0]
+        sm_scale = qd ** -0.5
+        for s0 in range(0, n, AR):
+            s1 = min(n, s0 + AR)
+            m = s1 - s0
+            g0, g1 = r0 + s0, r0 + s1
+            Kc.dsa_select(self.iproj[g0:g1], self.qi[g0:g1], a.index.ln_w, self.pool[li], self.pool_scale[li],
+                          b.positions[g0:g1], b.block_table, b.row_seq[g0:g1], self.rc.block_size, c.index_heads,
+                          c.kpool, c.pools_selected, self.dsa_logits[:m], self.sel[:m], self.sel_count[:m])
+            qpe = q[s0:s1, :, nope:] if rope else None
+            Kc.mla_decode(q_lat[s0:s1], qpe, H * qd, qd, self.kv[li], self.kv_scale[li],
+                          self.kpe[li] if rope else None, self.sel[:m], self.sel_count[:m], rope, sm_scale, 1,
+                          self.part_o, self.part_ml, o_lat[s0:s1])
+        K.linear8(o_lat.transpose(0, 1), f.w_uv.w, f.w_uv.s, ob.transpose(0, 1))
+        K.linear8(ob.view(n, H * c.v_dim), f.o_proj.w, f.o_proj.s, self.branch[r0:r1], proj="mla_o_proj")
+        self._branch_local = True
+
     def _mla(self, lw, R):
         c, a, b = self.cfg, lw.mla, self.batch
         Kc = K.C()
+        if self._sp is not None and a.full is not None:
+            self._mla_rows(lw, R)
+            return
         li = self.mla_index[lw.index]
         H, L, rope, nope = self.mH, c.kv_lora, c.qk_rope, c.qk_nope
         K.linear8(self.normed[:R], a.qkv_a.w, a.qkv_a.s, self.qkv_a[:R])

@@ -122,6 +122,18 @@ class MLAW:
     o_proj: Linear8           # [D, Hl*v]
     index: IndexW
     heads: int
+    full: "MLAFull | None" = None   # all heads' query / output projections (row-parallel prefill), when kept
+
+
+@dataclass
+class MLAFull:
+    """The head-dependent MLA projections of every head (the same fp8 bits as the tensor-parallel shards): with
+    sequence-parallel prefill a rank runs the attention of its own rows over all heads, so the block needs no
+    cross-rank reduction and the per-row key gathers are divided by the world size."""
+    q_b: Linear8              # [H*qk, q_lora]
+    w_uk_t: Linear8           # [H, kv_lora, nope]
+    w_uv: Linear8             # [H, v, kv_lora]
+    o_proj: Linear8           # [D, H*v]
 
 
 @dataclass
@@ -517,10 +529,11 @@ def _rows(x: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
 
 def prepare(src: TensorSource, cfg: ModelConfig, *, rank: int = 0, world: int = 1,
             device: str | torch.device = "cpu", layers: list[int] | None = None,
-            progress: Callable[[str], None] | None = None, ep: bool = False) -> Weights:
+            progress: Callable[[str], None] | None = None, ep: bool = False, sp_mla: bool = False) -> Weights:
     """Quantise and shard a checkpoint into runtime weights for rank ``rank`` of ``world``.  ``ep``: the routed
     experts are sharded by expert (rank j holds experts [j E/W, (j+1) E/W) at full width, for the expert-parallel
-    MoE of parallel/ep.py) instead of by width; everything else stays tensor-parallel."""
+    MoE of parallel/ep.py) instead of by width; everything else stays tensor-parallel.  ``sp_mla``: the MLA
+    layers also keep every head's query / output projections (``MLAW.full``) for row-parallel prefill."""
     if ep and world > 1 and cfg.experts % world:
         raise ValueError(f"{cfg.experts} experts do not split over {world} ranks")
     c = cfg
@@ -581,9 +594,15 @@ def prepare(src: TensorSource, cfg: ModelConfig, *, rank: int = 0, world: int = 
                            g(ix + "index_kpool_compress_gate").to(dev)], 0)
         index = IndexW(bf(iproj), lin(g(ix + "wq_b.weight")), f32(g(ix + "k_norm.weight")),
                        f32(g(ix + "k_norm.bias")), f32(g(ix + "index_kpool_compress_ape")))
+        full = None
+        if sp_mla and world > 1:
+            kvf = g(a + "kv_b_proj.weight").float().to(dev).view(c.heads, c.qk_nope + c.v_dim, c.kv_lora)
+            full = MLAFull(lin(g(a + "q_b_proj.weight")),
+                           quantize_fp8_rows(kvf[:, :c.qk_nope, :].transpose(1, 2).contiguous()),
+                           quantize_fp8_rows(kvf[:, c.qk_nope:, :].contiguous()), lin(g(a + "o_proj.weight")))
         return MLAW(qkv_a, bf(g(a + "q_a_layernorm.weight")), bf(g(a + "kv_a_layernorm.weight")),
                     lin(_rows(g(a + "q_b_proj.weight"), rank, world)), w_uk_t, w_uv,
-                    lin_rowpar(g(a + "o_proj.weight")), index, Hl)
+                    lin_rowpar(g(a + "o_proj.weight")), index, Hl, full)
 
     def mlp(prefix, width):
         gate = _rows(g(prefix + "gate_proj.weight"), rank, world).to(dev)

@@ -116,8 +116,9 @@ def test_gemv_push_bulk(world):
 
 
 def _sp_worker(rank, world, port, result):
-    """Sequence-parallel prefill (mHC on each rank's rows, all-gather before and reduce-scatter after each block)
-    against the all-reduce path: logits of the prefill chunks and of a decode window after them."""
+    """Sequence-parallel prefill (mHC on each rank's rows, all-gather before and reduce-scatter after each block),
+    also with the MLA blocks row-parallel over all heads, against the all-reduce path: logits of the prefill chunks
+    and of a decode window after them."""
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0", GLM53_SP_MIN_ROWS="64")
     import torch.distributed as dist
@@ -131,13 +132,16 @@ def _sp_worker(rank, world, port, result):
         cfg = tiny_config()
         dev = torch.device("cuda", rank)
         w = W.prepare(W.RandomSource(cfg, seed=0, device=dev), cfg, rank=rank, world=world, device=dev)
+        w_rows = W.prepare(W.RandomSource(cfg, seed=0, device=dev), cfg, rank=rank, world=world, device=dev,
+                           sp_mla=True)
         rc = RuntimeConfig(max_rows=128, max_seqs=1, kv_slots=64 * 8, block_size=64, max_blocks=8)
         g = torch.Generator().manual_seed(5)
         prompt = torch.randint(16, cfg.vocab, (256,), generator=g).tolist()
         outs = []
-        for sp in ("0", "1"):
+        # all-reduce path; sequence parallel; sequence parallel with the row-parallel (all-head) MLA blocks
+        for sp, wts in (("0", w), ("1", w), ("1", w_rows)):
             os.environ["GLM53_SP"] = sp
-            rt = Runtime(w, rc, comm=D.NcclComm(fused=False))
+            rt = Runtime(wts, rc, comm=D.NcclComm(fused=False))
             seq = Sequence(rt)
             lg = [seq.prefill(prompt, chunk=128).clone()]          # two 128-row chunks
             lg.append(rt.hidden[:128].float().clone())
@@ -145,7 +149,7 @@ def _sp_worker(rank, world, port, result):
             seq.stage(toks, list(range(8)))
             lg.append(rt.forward(8, keep_window=True).clone())
             outs.append(torch.cat([x.flatten() for x in lg]))
-        result[rank] = (outs[0] - outs[1]).abs().max().item()
+        result[rank] = max((outs[0] - outs[1]).abs().max().item(), (outs[0] - outs[2]).abs().max().item())
         dist.barrier()
     finally:
         dist.destroy_process_group()
