@@ -41,7 +41,7 @@ class LLMOptions:
     block_verify: bool = False          # sampled requests: block verification instead of standard
     mixed_prefill_chunk: int = 0        # prefill tokens per step while requests decode (0: the whole chunk)
     ep: bool = False                    # routed experts expert-parallel over the ranks (parallel/ep.py)
-    sp_mla: bool = os.environ.get("GLM53_SP_MLA", "0") == "1"   # row-parallel MLA in sequence-parallel prefill
+    sp_mla: bool = os.environ.get("GLM53_SP_MLA", "1") == "1"   # row-parallel MLA in sequence-parallel prefill
 
 
 class LLM:

@@ -40,7 +40,7 @@ SWITCHES: dict[str, Switch] = {
     "GLM53_FUSED_TP_PREFILL": Switch("bool", "0", "prefill chunks push partials from the GEMM epilogue"),
     "GLM53_SP": Switch("bool", "1", "sequence-parallel prefill: mHC on each rank's rows, all-gather / reduce-scatter"),
     "GLM53_SP_MIN_ROWS": Switch("int", "256", "rows of a prefill chunk from which sequence parallelism is used"),
-    "GLM53_SP_MLA": Switch("bool", "0", "sequence-parallel prefill runs the MLA attention of each rank's rows over "
+    "GLM53_SP_MLA": Switch("bool", "1", "sequence-parallel prefill runs the MLA attention of each rank's rows over "
                                         "all heads (keeps the full-head MLA projections on every rank)"),
     "GLM53_L2_PREFETCH": Switch("bool", "0", "routed-expert CTAs prefetch the next layer's weights into L2"),
     "GLM53_L2_PREFETCH_MB": Switch("float", "32", "L2 prefetch budget in MiB"),
