@@ -6,6 +6,27 @@
 
 #include "launchers.h"
 
+#include <mutex>
+#include <vector>
+
+// Bounds-checked debug build: every CUDA source registers its device error record here at load time (see
+// common.cuh); bounds_status() reads them, bounds_reset() clears them.  The regular build registers none.
+struct G53BoundsRecHost {
+  int count;
+  int code;
+  long long index;
+  long long limit;
+};
+static std::vector<const void*>& g53_bounds_symbols() {
+  static std::vector<const void*> v;
+  return v;
+}
+static std::mutex g53_bounds_mu;
+void g53_bounds_register(const void* symbol) {
+  std::lock_guard<std::mutex> lock(g53_bounds_mu);
+  g53_bounds_symbols().push_back(symbol);
+}
+
 namespace {
 
 using at::Tensor;
@@ -346,6 +367,8 @@ Exl3Args exl3_args(const Tensor& x, const Tensor& tr_g, const Tensor& suh_g, con
   a.limit = (float)limit;
   a.xh_g = P<__half>(xh_g); a.xh_u = P<__half>(xh_u); a.xd = P<__half>(xd); a.yd = P<float>(yd);
   a.decode_layout = 1;
+  a.n_rows = x.size(0);
+  a.n_experts = tr_g.size(0);
   TORCH_CHECK(tr_g.scalar_type() == at::kShort && tr_d.scalar_type() == at::kShort, "trellis must be int16");
   // decode layout: rotated inputs are duplicated f16 pairs, 2K (2N) halves per pair
   TORCH_CHECK(xh_g.numel() >= (int64_t)a.pairs * 2 * a.K && xh_u.numel() >= (int64_t)a.pairs * 2 * a.K &&
@@ -420,6 +443,7 @@ void ep_moe_step(const Tensor& x, const Tensor& out, const Tensor& pair_token, c
   a.tr_u = P<const int16_t>(tr_u); a.suh_u = P<const __half>(suh_u); a.svh_u = P<const __half>(svh_u);
   a.tr_d = P<const int16_t>(tr_d); a.suh_d = P<const __half>(suh_d); a.svh_d = P<const __half>(svh_d);
   a.K = K; a.N = (int)svh_g.size(-1); a.Dout = (int)svh_d.size(-1);
+  a.n_experts = tr_g.size(0);
   a.group_count = e.group_count; a.group_expert = e.group_expert; a.group_offset = e.group_offset;
   a.pair_token = e.rp_token; a.pair_expert = e.rp_expert; a.pair_w = e.rp_w;
   a.max_groups = (int)El; a.pairs = (int)recv_cap; a.limit = (float)limit;
@@ -472,6 +496,8 @@ void exl3_rot_in(const Tensor& x, const Tensor& suh_g, const Tensor& suh_u, cons
   a.pairs = (int)pair_token.size(0);
   a.xh_g = P<__half>(xh_g);
   a.xh_u = P<__half>(xh_u);
+  a.n_rows = x.size(0);
+  a.n_experts = suh_g.size(0);
   TORCH_CHECK(xh_g.size(0) >= a.pairs && xh_u.size(0) >= a.pairs);
   check(g53_exl3_rot_in(a, stream()), "exl3_rot_in");
 }
@@ -516,6 +542,7 @@ void moe_prefill(const Tensor& tr0, const OptT& tr1, const Tensor& svh0, const O
   p.group_count = P<const int>(group_count);
   p.group_expert = P<const int>(group_expert);
   p.group_offset = P<const int>(group_offset);
+  p.n_experts = tr0.size(0);
   p.x0 = P<const __half>(x0);
   p.x1 = P<const __half>(x1);
   p.rows = x0.size(0);
@@ -586,8 +613,8 @@ void hc_post_pre(const Tensor& X, const OptT& branch, const OptT& post, const Op
 }
 
 void embed(const Tensor& ids, const Tensor& table, const Tensor& X) {
-  check(g53_embed(P<const int>(ids), P<const __nv_bfloat16>(table), (int)X.size(0), (int)X.size(2), (int)X.size(1),
-                  P<__nv_bfloat16>(X), stream()),
+  check(g53_embed(P<const int>(ids), P<const __nv_bfloat16>(table), (int)table.size(0), (int)X.size(0),
+                  (int)X.size(2), (int)X.size(1), P<__nv_bfloat16>(X), stream()),
         "embed");
 }
 
@@ -678,6 +705,7 @@ void kda_conv(const Tensor& proj, const Tensor& seq, int64_t max_rows, const Ten
   KdaArgs a = kda_args(proj, seq, max_rows, H, Dh, conv_w.size(1));
   a.conv_w = P<const float>(conv_w);
   a.conv_pool = P<__nv_bfloat16>(conv_pool);
+  a.n_conv = conv_pool.size(0);
   a.qkv = P<__nv_bfloat16>(qkv);
   check(g53_kda_conv(a, stream()), "kda_conv");
 }
@@ -686,6 +714,7 @@ void kda_conv_commit(const Tensor& proj, const Tensor& seq, const Tensor& conv_p
                      int64_t taps) {
   KdaArgs a = kda_args(proj, seq, 0, H, Dh, taps);
   a.conv_pool = P<__nv_bfloat16>(conv_pool);
+  a.n_conv = conv_pool.size(0);
   check(g53_kda_conv_commit(a, stream()), "kda_conv_commit");
 }
 
@@ -698,6 +727,7 @@ void kda_recurrent(const Tensor& proj, const Tensor& seq, const Tensor& f, const
   a.a_log = P<const float>(a_log);
   a.dt_bias = P<const float>(dt_bias);
   a.S_pool = P<float>(S_pool);
+  a.n_states = S_pool.size(0);
   a.o_raw = P<float>(o_raw);
   a.b_off = (int)b_off;
   a.lower = (float)lower;
@@ -720,12 +750,14 @@ void kda_decode(const Tensor& proj, const Tensor& seq, int64_t max_rows, const T
   a.gb_w = P<const uint8_t>(gb_w); a.gb_s = P<const float>(gb_s);
   a.conv_w = P<const float>(conv_w);
   a.conv_pool = P<__nv_bfloat16>(conv_pool);
+  a.n_conv = conv_pool.size(0);
   a.qkv = P<__nv_bfloat16>(qkv);
   a.f_store = P<__nv_bfloat16>(f_store);
   a.a_log = P<const float>(a_log);
   a.dt_bias = P<const float>(dt_bias);
   a.o_norm = P<const __nv_bfloat16>(o_norm);
   a.S_pool = P<float>(S_pool);
+  a.n_states = S_pool.size(0);
   a.out = P<__nv_bfloat16>(out);
   a.fa_off = (int)fa_off;
   a.b_off = (int)b_off;
@@ -748,6 +780,7 @@ void kda_chunk(const Tensor& proj, const Tensor& seq, const Tensor& f, const Ten
   a.a_log = P<const float>(a_log);
   a.dt_bias = P<const float>(dt_bias);
   a.S_pool = P<float>(S_pool);
+  a.n_states = S_pool.size(0);
   a.o_raw = P<float>(o_raw);
   a.b_off = (int)b_off;
   a.lower = (float)lower;
@@ -784,6 +817,7 @@ void mla_prep(const Tensor& qkv_a, const Tensor& q_norm, const Tensor& kv_norm, 
   a.R = (int)qkv_a.size(0);
   a.q_lora = (int)q_lora; a.kv_lora = (int)kv_lora; a.rope = (int)rope;
   a.eps = (float)eps; a.theta = (float)theta;
+  a.n_slots = kv_cache.size(0);
   check(g53_mla_prep(a, stream()), "mla_prep");
 }
 
@@ -818,6 +852,7 @@ void mla_decode(const Tensor& q_lat, const OptT& q_pe, int64_t q_pe_ld, int64_t 
   a.kv_cache = P<const uint8_t>(kv_cache);
   a.kv_scale = P<const float>(kv_scale);
   a.kpe_cache = P<const __nv_bfloat16>(kpe_cache);
+  a.n_slots = kv_cache.size(0);
   a.sel = P<const int>(sel);
   a.sel_count = P<const int>(sel_count);
   a.max_sel = (int)sel.size(1);
@@ -857,6 +892,7 @@ DsaArgs dsa_args(const Tensor& iproj, const Tensor& ln_w, const Tensor& ln_b, co
   a.ig_cache = P<float>(ig_cache);
   a.pool_cache = P<uint8_t>(pool_cache);
   a.pool_scale = P<float>(pool_scale);
+  a.n_pools = pool_scale.size(0);
   a.slots = P<const int>(slots);
   a.positions = P<const int>(positions);
   a.block_table = P<const int>(block_table);
@@ -891,6 +927,7 @@ void dsa_update(const Tensor& iproj, const Tensor& ln_w, const Tensor& ln_b, con
   TORCH_CHECK(seq_desc.dim() == 2 && seq_desc.size(0) == 5 && seq_desc.scalar_type() == at::kInt, "seq_desc");
   a.ik_ring = P<__nv_bfloat16>(ik_ring);
   a.ig_ring = P<float>(ig_ring);
+  a.n_owners = ik_ring.size(0) / kDsaRing;
   a.seq_desc = P<const int>(seq_desc);
   a.seq_ld = (int)seq_desc.stride(0);
   check(g53_dsa_update(a, stream()), "dsa_update");
@@ -981,6 +1018,30 @@ void rejection_sample(const Tensor& target_probs, const Tensor& draft_probs, con
 
 void register_exl3_codec(pybind11::module& m);   // exl3_codec.cpp (host codec)
 
+namespace {
+// (enabled, [(code, index, limit, count), ...]) of the bounds-checked build's records that saw an error
+py::tuple bounds_status() {
+  py::list out;
+  std::lock_guard<std::mutex> lock(g53_bounds_mu);
+  for (const void* sym : g53_bounds_symbols()) {
+    G53BoundsRecHost r{};
+    const cudaError_t e = cudaMemcpyFromSymbol(&r, sym, sizeof(r));
+    TORCH_CHECK(e == cudaSuccess, "bounds_status: ", cudaGetErrorString(e));
+    if (r.count) out.append(py::make_tuple(r.code, r.index, r.limit, r.count));
+  }
+  return py::make_tuple(!g53_bounds_symbols().empty(), out);
+}
+
+void bounds_reset() {
+  std::lock_guard<std::mutex> lock(g53_bounds_mu);
+  const G53BoundsRecHost z{};
+  for (const void* sym : g53_bounds_symbols()) {
+    const cudaError_t e = cudaMemcpyToSymbol(sym, &z, sizeof(z));
+    TORCH_CHECK(e == cudaSuccess, "bounds_reset: ", cudaGetErrorString(e));
+  }
+}
+}  // namespace
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_exl3_codec(m);
   m.doc() = "glm53 sm_100a kernels";
@@ -1005,6 +1066,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_prefill", &moe_prefill);
   m.def("exl3_rot_in", &exl3_rot_in);
   m.def("ep_moe_step", &ep_moe_step);
+  m.def("bounds_status", &bounds_status);
+  m.def("bounds_reset", &bounds_reset);
   m.def("exl3_unpack", &exl3_unpack);
   m.def("hc_post_pre", &hc_post_pre, py::arg("X"), py::arg("branch"), py::arg("post"), py::arg("comb"), py::arg("fn"),
         py::arg("base"), py::arg("hscale"), py::arg("norm_w"), py::arg("normed"), py::arg("post_out"),

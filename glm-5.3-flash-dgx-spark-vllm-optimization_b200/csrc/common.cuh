@@ -10,6 +10,60 @@
 
 #define G53_CHECK_LAUNCH() do { cudaError_t e_ = cudaGetLastError(); if (e_ != cudaSuccess) return e_; } while (0)
 
+// ---------------------------------------------------------------------------------------------------------------
+// Bounds-checked debug build (GLM53_BOUNDS=1 compiles every source with -DG53_BOUNDS=1 into a second library).
+// Indices that come from device data (token ids, cache slots from page tables and selections, state-pool slots,
+// expert ids and row ids of the routing tables) are checked against the size of what they index.  An index out of
+// range records (code, index, limit) in this source file's error record and the access is skipped (the kernel
+// returns, skips the item, or reads a substitute in-range element); no assert and no trap, so the context stays
+// usable.  The host reads and clears the records of every source file (bounds_status / bounds_reset).  In the
+// regular build the checks compile to nothing.  A limit of 0 means "unknown" (not checked).
+// Codes: 1 embedding row, 2 MLA cache slot written, 3 MLA cache slot read, 4 DSA cache slot / pool, 5 KDA state or
+// conv slot, 6 MoE expert id, 7 MoE token row, 8 DSA tail-ring owner.
+// ---------------------------------------------------------------------------------------------------------------
+#ifndef G53_BOUNDS
+#define G53_BOUNDS 0
+#endif
+struct G53BoundsRec {
+  int count;
+  int code;
+  long long index;
+  long long limit;
+};
+#ifdef __CUDACC__
+#if G53_BOUNDS
+static __device__ G53BoundsRec g53_bounds_rec;
+#endif
+__device__ __forceinline__ bool g53_in_bounds(long long i, long long n, int code) {
+#if G53_BOUNDS
+  if (n <= 0 || (i >= 0 && i < n)) return true;
+  if (atomicAdd(&g53_bounds_rec.count, 1) == 0) {
+    g53_bounds_rec.code = code;
+    g53_bounds_rec.index = i;
+    g53_bounds_rec.limit = n;
+  }
+  return false;
+#else
+  (void)i; (void)n; (void)code;
+  return true;
+#endif
+}
+// an index from device data, or `sub` (an in-range substitute, or -1 = masked) when it is out of range
+__device__ __forceinline__ int g53_checked(int i, long long n, int code, int sub) {
+  return g53_in_bounds(i, n, code) ? i : sub;
+}
+#if G53_BOUNDS && !defined(__CUDA_ARCH__)
+// host pass: register this source file's record (its host-side symbol, for cudaMemcpyFromSymbol) at load time
+void g53_bounds_register(const void* symbol);
+namespace {
+struct G53BoundsRegistrar {
+  G53BoundsRegistrar() { g53_bounds_register(&g53_bounds_rec); }
+};
+G53BoundsRegistrar g53_bounds_registrar;
+}  // namespace
+#endif
+#endif
+
 // Programmatic dependent launch.  A kernel launched with the programmatic-stream-serialization attribute may start
 // while the previous kernel of the stream still runs: it must call pdl_wait() before it reads anything that kernel
 // writes (pdl_wait returns at once when the launch has no programmatic dependency).  pdl_trigger() lets the

@@ -46,7 +46,7 @@ __device__ __forceinline__ int64_t dsa_src_row(const DsaArgs& a, int r, int pos,
     return rr;
   }
   ring = true;
-  const int owner = a.seq_desc[4 * a.seq_ld + a.row_seq[r]];
+  const int owner = g53_checked(a.seq_desc[4 * a.seq_ld + a.row_seq[r]], a.n_owners, 8, 0);
   return (int64_t)owner * kDsaRing + (p % kDsaRing);
 }
 
@@ -57,6 +57,7 @@ __global__ void __launch_bounds__(128) dsa_ring_kernel(DsaArgs a) {
   const int last = a.seq_desc[b] + a.seq_desc[a.seq_ld + b] - 1;
   if (r <= last - kDsaRing) return;
   const int owner = a.seq_desc[4 * a.seq_ld + b];
+  if (!g53_in_bounds(owner, a.n_owners, 8)) return;    // uniform per CTA (one row)
   const int64_t dst = ((int64_t)owner * kDsaRing + a.positions[r] % kDsaRing) * a.ID;
   const int c = threadIdx.x;
   a.ik_ring[dst + c] = a.ik_cache[(int64_t)r * a.ID + c];
@@ -109,6 +110,7 @@ __global__ void dsa_pool_kernel(DsaArgs a) {
   amax = fmaxf(warp_max(amax), 1e-4f);
   const float scale = exp2f(ceilf(log2f(amax / 448.f)));
   const int pslot = slot_of(bt, a.block_size, p0) / kp;
+  if (!g53_in_bounds(pslot, a.n_pools, 4)) return;       // warp-uniform; nothing follows
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const __nv_fp8_e4m3 q8(v[i] / scale);
@@ -140,7 +142,7 @@ __global__ void __launch_bounds__(256) dsa_logits_kernel(DsaArgs a) {
   __syncthreads();
   if (j >= c) return;
   const int* bt = a.block_table + (int64_t)a.row_seq[r] * a.bt_ld;
-  const int pslot = slot_of(bt, a.block_size, j * a.kpool) / a.kpool;
+  const int pslot = g53_checked(slot_of(bt, a.block_size, j * a.kpool) / a.kpool, a.n_pools, 4, 0);
   const uint8_t* pk = a.pool_cache + (int64_t)pslot * 128;
   float kv[128];
 #pragma unroll

@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1) dsa_logits_tc_kernel(DsaArgs a)
         const int j = t * kTP + p;
         uint4 kw[8];
         if (j < jhi) {
-          const int pslot = slot_of_tc(bt, a.block_size, j * a.kpool) / a.kpool;
+          const int pslot = g53_checked(slot_of_tc(bt, a.block_size, j * a.kpool) / a.kpool, a.n_pools, 4, 0);
           const uint4* src = reinterpret_cast<const uint4*>(a.pool_cache + (int64_t)pslot * 128);
 #pragma unroll
           for (int c = 0; c < 8; ++c) kw[c] = src[c];
@@ -206,7 +206,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1) dsa_logits_tc_kernel(DsaArgs a)
         tc::fence_after();
         const int j = t * kTP + p;
         const bool jv = j < g_jhi[gi];
-        const float s = jv ? a.pool_scale[slot_of_tc(bt, a.block_size, j * a.kpool) / a.kpool] : 0.f;
+        const float s =
+            jv ? a.pool_scale[g53_checked(slot_of_tc(bt, a.block_size, j * a.kpool) / a.kpool, a.n_pools, 4, 0)] : 0.f;
         for (int c0 = 0; c0 < kTN; c0 += 32) {
           float v[32];
           tc::tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * kTN + c0), v);

@@ -23,7 +23,7 @@ __global__ void kda_conv_kernel(KdaArgs a) {
   const int C = 3 * a.H * a.Dh;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int b = blockIdx.z;
-  if (c >= C) return;
+  if (c >= C || !g53_in_bounds(a.conv_slot[b], a.n_conv, 5)) return;
   const int base = a.row0[b], n = a.nrows[b];
   const int t0 = blockIdx.y * kConvRB;
   if (t0 >= n) return;
@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(256) kda_conv_vec_kernel(KdaArgs a) {
   const int C = 3 * a.H * a.Dh;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   const int b = blockIdx.z;
-  if (c >= C) return;
+  if (c >= C || !g53_in_bounds(a.conv_slot[b], a.n_conv, 5)) return;
   const int base = a.row0[b], n = a.nrows[b];
   const int t0 = blockIdx.y * kConvRB;
   if (t0 >= n) return;
@@ -102,7 +102,7 @@ __global__ void kda_conv_commit_kernel(KdaArgs a) {
   const int C = 3 * a.H * a.Dh;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int b = blockIdx.y;
-  if (c >= C) return;
+  if (c >= C || !g53_in_bounds(a.conv_slot[b], a.n_conv, 5)) return;
   const int T = a.taps;
   const int base = a.row0[b], keep = a.nrows[b];
   __nv_bfloat16* win = a.conv_pool + (int64_t)a.conv_slot[b] * (T - 1) * C;
@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(128) kda_recurrent_kernel(KdaArgs a) {
   constexpr int KP = DH / 4;
   __shared__ float sq[kRecRows][DH], sk[kRecRows][DH], sg[kRecRows][DH], sv[kRecRows][32], sb[kRecRows];
   const int h = blockIdx.x, b = blockIdx.z;
+  if (!g53_in_bounds(a.s_in[b], a.n_states, 5) || !g53_in_bounds(a.s_out[b], a.n_states, 5)) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int vr = tid >> 2, kq = tid & 3;
   const int v0 = blockIdx.y * 32, v = v0 + vr;

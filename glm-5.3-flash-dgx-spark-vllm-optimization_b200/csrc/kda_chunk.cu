@@ -351,6 +351,7 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
   float* sV = sZ + kC * LV;        // [kC][LV]  v'
 
   const int h = blockIdx.x, b = blockIdx.z;
+  if (!g53_in_bounds(a.s_in[b], a.n_states, 5) || !g53_in_bounds(a.s_out[b], a.n_states, 5)) return;
   const int v0 = blockIdx.y * 32;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
   const int HD = a.H * DH;

@@ -50,6 +50,9 @@ __global__ void __launch_bounds__(kThreads, 1) kda_decode_kernel(KdaArgs a) {
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   pdl_trigger();
   const int h = blockIdx.x, b = blockIdx.y;
+  if (!g53_in_bounds(a.s_in[b], a.n_states, 5) || !g53_in_bounds(a.s_out[b], a.n_states, 5) ||
+      !g53_in_bounds(a.conv_slot[b], a.n_conv, 5))
+    return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int HD = a.H * DH, C3 = 3 * HD;
 

@@ -137,6 +137,7 @@ struct Exl3Args {
   // decode: weight ranges the gate/up CTAs prefetch into L2 (64 KB bulk prefetches spread over the grid) while the
   // ALU-bound trellis decode leaves HBM idle; count 0 = none
   L2Ranges pf;
+  int64_t n_rows, n_experts;    // bounds-checked build: rows of x, experts of the stacked tensors (0: unknown)
 };
 cudaError_t g53_exl3_rot_in(const Exl3Args& a, cudaStream_t st);
 // ---------------------------------------------------------------- expert parallelism (ep_moe.cu)
@@ -188,6 +189,7 @@ struct MoePrefillArgs {
   int* err;
   // expert parallelism (down): per-row output addresses (peer memory) and the flags released by the last CTA
   const int64_t* out_ptrs; unsigned* done; const int64_t* push_flags; int push_world;
+  int64_t n_experts;                              // bounds-checked build: experts of the trellis tensors (0: unknown)
 };
 cudaError_t g53_moe_prefill(const MoePrefillArgs& p, bool gate_up, cudaStream_t st);
 // scalable routing for prefill: per-row top-k, expert histogram, scan, scatter (positions within an expert in
@@ -228,7 +230,7 @@ bool g53_hc_decode_ok(const HcArgs& a);
 cudaError_t g53_hc_decode(const HcArgs& a, cudaStream_t st);
 // tensor-core partial pass only (post + mixing dots + sums of squares into part [R, D / 512, 32])
 cudaError_t g53_hc_partial_tc(const HcArgs& a, cudaStream_t st);
-cudaError_t g53_embed(const int* ids, const __nv_bfloat16* table, int R, int D, int S, __nv_bfloat16* X,
+cudaError_t g53_embed(const int* ids, const __nv_bfloat16* table, int V, int R, int D, int S, __nv_bfloat16* X,
                       cudaStream_t st);
 cudaError_t g53_stream_mean_norm(const __nv_bfloat16* X, int R, int S, int D, const __nv_bfloat16* w, float eps,
                                  __nv_bfloat16* hidden, __nv_bfloat16* normed, cudaStream_t st);
@@ -266,6 +268,7 @@ struct KdaArgs {
   const uint8_t* gb_w; const float* gb_s;
   int fa_off;                                // column of f_a in proj (g_a follows at fa_off + Dh)
   __nv_bfloat16* f_store;                    // [R, H*Dh] decay logits kept for the commit replay
+  int64_t n_states, n_conv;                  // bounds-checked build: state-pool and conv-pool slots (0: unknown)
 };
 cudaError_t g53_kda_conv(const KdaArgs& a, cudaStream_t st);          // qkv = silu(conv(window ++ proj rows))
 cudaError_t g53_kda_recurrent(const KdaArgs& a, cudaStream_t st);     // per sequence: S_in -> S_out, o_raw
@@ -289,6 +292,7 @@ struct MlaPrepArgs {
   const int* positions;                       // [R] absolute positions (rope)
   int R, q_lora, kv_lora, rope;
   float eps, theta;
+  int64_t n_slots;                            // bounds-checked build: cache slots (0: unknown)
 };
 cudaError_t g53_mla_prep(const MlaPrepArgs& a, cudaStream_t st);
 cudaError_t g53_rope_q(__nv_bfloat16* q, int R, int H, int qk, int nope, int rope, const int* positions, float theta,
@@ -310,6 +314,7 @@ struct MlaAttnArgs {
   __nv_bfloat16* o_lat;         // [R, H, L] out (bf16)
   int use_tc;                   // 1: tensor-core kernel (L = 512, no rope, H <= 64); 0: CUDA-core kernel
   int* err;                     // error word of the bounded waits (tensor-core kernel)
+  int64_t n_slots;              // bounds-checked build: cache slots (0: unknown)
 };
 cudaError_t g53_mla_decode(const MlaAttnArgs& a, cudaStream_t st);
 // tensor-core attention only (no merge); splits > 1 leaves partials in part_o / part_ml
@@ -340,6 +345,8 @@ struct DsaArgs {
   int max_pools;
   int* sel; int* sel_count; int max_sel;   // out: selected token slots per row
   int* err;                      // device error word (bounded waits of the tensor-core logits kernel)
+  int64_t n_pools;               // bounds-checked build: pool slots of the index cache (0: unknown)
+  int64_t n_owners;              // bounds-checked build: ring owners (state slots) of the tail rings (0: unknown)
 };
 cudaError_t g53_dsa_update(const DsaArgs& a, cudaStream_t st);   // index keys, gate scores, completed pools
 cudaError_t g53_dsa_logits(const DsaArgs& a, cudaStream_t st);  // pool logits of every row (CUDA cores)

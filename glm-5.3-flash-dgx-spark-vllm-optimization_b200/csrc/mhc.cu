@@ -224,11 +224,13 @@ __global__ void __launch_bounds__(512) hc_finish_kernel(HcArgs a) {
   }
 }
 
-__global__ void embed_kernel(const int* ids, const __nv_bfloat16* table, int D, int S, __nv_bfloat16* X) {
+__global__ void embed_kernel(const int* ids, const __nv_bfloat16* table, int V, int D, int S, __nv_bfloat16* X) {
   const int r = blockIdx.y;
   const int d = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (d >= D) return;
-  const uint4 v = *reinterpret_cast<const uint4*>(table + (int64_t)ids[r] * D + d);
+  const int id = ids[r];
+  if (!g53_in_bounds(id, V, 1)) return;
+  const uint4 v = *reinterpret_cast<const uint4*>(table + (int64_t)id * D + d);
   for (int s = 0; s < S; ++s) *reinterpret_cast<uint4*>(X + ((int64_t)r * S + s) * D + d) = v;
 }
 
@@ -315,11 +317,11 @@ cudaError_t g53_hc_post_pre(const HcArgs& args, cudaStream_t st) {
   return cudaSuccess;
 }
 
-cudaError_t g53_embed(const int* ids, const __nv_bfloat16* table, int R, int D, int S, __nv_bfloat16* X,
+cudaError_t g53_embed(const int* ids, const __nv_bfloat16* table, int V, int R, int D, int S, __nv_bfloat16* X,
                       cudaStream_t st) {
   if (D % 8) return cudaErrorInvalidValue;
   dim3 grid((D / 8 + 127) / 128, R);
-  embed_kernel<<<grid, 128, 0, st>>>(ids, table, D, S, X);
+  embed_kernel<<<grid, 128, 0, st>>>(ids, table, V, D, S, X);
   G53_CHECK_LAUNCH();
   return cudaSuccess;
 }

@@ -56,6 +56,7 @@ __global__ void __launch_bounds__(256) mla_prep_kernel(MlaPrepArgs a) {
   for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
   const float scale = fmaxf(m, 1e-8f) / 448.f;
   const int slot = a.slots[r];
+  if (!g53_in_bounds(slot, a.n_slots, 2)) return;        // uniform per CTA (one row)
   for (int i = threadIdx.x; i < a.kv_lora; i += blockDim.x) {
     const __nv_fp8_e4m3 q8(vals[i] / scale);
     a.kv_cache[(int64_t)slot * a.kv_lora + i] = q8.__x;
@@ -138,14 +139,17 @@ __global__ void __launch_bounds__(128) mla_decode_kernel(MlaAttnArgs a) {
     for (int i = tid; i < KT * (L / 16); i += 128) {
       const int key = i / (L / 16), c = i % (L / 16);
       uint4 v = make_uint4(0, 0, 0, 0);
-      if (key < nk) v = *reinterpret_cast<const uint4*>(a.kv_cache + (int64_t)sel[kb + key] * L + c * 16);
+      if (key < nk)
+        v = *reinterpret_cast<const uint4*>(a.kv_cache + (int64_t)g53_checked(sel[kb + key], a.n_slots, 3, 0) * L +
+                                            c * 16);
       *reinterpret_cast<uint4*>(&kt[key][c * 16]) = v;
     }
-    if (tid < KT) ksc[tid] = tid < nk ? a.kv_scale[sel[kb + tid]] : 0.f;
+    if (tid < KT) ksc[tid] = tid < nk ? a.kv_scale[g53_checked(sel[kb + tid], a.n_slots, 3, 0)] : 0.f;
     if (ROPE > 0) {
       for (int i = tid; i < KT * ROPE; i += 128) {
         const int key = i / ROPE, l = i % ROPE;
-        const float v = key < nk ? bf2f(a.kpe_cache[(int64_t)sel[kb + key] * ROPE + l]) : 0.f;
+        const float v =
+            key < nk ? bf2f(a.kpe_cache[(int64_t)g53_checked(sel[kb + key], a.n_slots, 3, 0) * ROPE + l]) : 0.f;
         kpe[key][l] = __float2half_rn(v);
       }
     }

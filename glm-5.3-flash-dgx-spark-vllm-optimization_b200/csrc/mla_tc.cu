@@ -336,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(MlaAttnArgs a) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int k = k0 + i * kProd + tid;
-          sl[i] = k < w.kend ? sel[k] : -1;
+          sl[i] = k < w.kend ? g53_checked(sel[k], a.n_slots, 3, -1) : -1;
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) km = fmaxf(km, sl[i] >= 0 ? a.kv_scale[sl[i]] : 0.f);
@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(MlaAttnArgs a) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int k = w.kbeg + tid + e * kProd;
-        slot[e] = k < w.kend ? sel[k] : -1;
+        slot[e] = k < w.kend ? g53_checked(sel[k], a.n_slots, 3, -1) : -1;
       }
       for (int j = 0; j < w.nt; ++j) {
         const int gg = g + j, s = gg % kStages;
@@ -399,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(MlaAttnArgs a) {
         for (int e = 0; e < 2; ++e) {
           scl[e] = slot[e] >= 0 ? a.kv_scale[slot[e]] : 0.f;
           const int k = w.kbeg + (j + 1) * kKeys + tid + e * kProd;
-          if (j + 1 < w.nt && k < w.kend) nxt[e] = sel[k];
+          if (j + 1 < w.nt && k < w.kend) nxt[e] = g53_checked(sel[k], a.n_slots, 3, -1);
         }
         if (gg >= kStages && !tc::warp_wait(&k_empty[s], ((gg / kStages) & 1) ^ 1, &fail, a.err, 63)) {
           ok = false;

@@ -248,6 +248,7 @@ __global__ void __launch_bounds__(128) exl3_rot_in_kernel(Exl3Args a) {
   const int np = a.pair_count ? min(*a.pair_count, a.pairs) : a.pairs;
   for (int p = blockIdx.x; p < np; p += gridDim.x) {   // pairs on grid.x (prefill chunks exceed 65535 pairs)
     const int r = a.pair_token[p], e = a.pair_expert[p];
+    if (!g53_in_bounds(r, a.n_rows, 7) || !g53_in_bounds(e, a.n_experts, 6)) continue;   // warp-uniform
     const int c0 = blk * 128 + lane * 4;
     const __nv_bfloat16* xr = a.x + (int64_t)r * a.ldx + c0;
     float xv[4];
@@ -323,6 +324,7 @@ __device__ __forceinline__ void cluster_release() {
 template <int KSPL, int KS>
 __device__ __forceinline__ void gate_up_group(const Exl3Args& a, int u, float (*zg)[132], float (*zu)[132]) {
   const int e = a.group_expert[u];
+  if (!g53_in_bounds(e, a.n_experts, 6)) return;       // uniform over the cluster (same group)
   const int p0 = a.group_offset[u];
   const int np = a.group_offset[u + 1] - p0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
@@ -455,6 +457,7 @@ __device__ __forceinline__ void ep_count_in(const Exl3Args& a) {
 template <int KSPL, int KS>
 __device__ __forceinline__ void down_group(const Exl3Args& a, int u, float (*zd)[132]) {   // KSPL in {1, 2}
   const int e = a.group_expert[u];
+  if (!g53_in_bounds(e, a.n_experts, 6)) return;       // uniform over the cluster (same group)
   const int p0 = a.group_offset[u];
   const int np = a.group_offset[u + 1] - p0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;

@@ -189,6 +189,10 @@ __global__ void __launch_bounds__(Cfg<GU>::kThreads, Cfg<GU>::kMinBlocks) moe_pr
     return;
   }
   const int e = p.group_expert[u];
+  if (!g53_in_bounds(e, p.n_experts, 6)) {
+    if (!GU && p.out_ptrs) ep_count_in(p);
+    return;
+  }
   const int p0 = p.group_offset[u];
   const int np = p.group_offset[u + 1] - p0;
   const int nb = blockIdx.x;                            // 128-channel output block

@@ -26,6 +26,7 @@ import torch
 
 from ..config import ModelConfig
 from ..ops import kernels as K
+from ..utils.canary import Scratch
 from .weights import Linear8, Weights
 
 bf16, f32, i32 = torch.bfloat16, torch.float32, torch.int32
@@ -130,19 +131,23 @@ class Runtime:
         for lw in w.layers:
             m = lw.mlp if lw.mlp is not None else lw.moe.shared
             self.gu_il[lw.index] = interleave_gate_up(m.gu)
+        # scratch: guard bands around every buffer in the bounds-checked build (utils/canary.py)
+        self.scratch = Scratch(dev)
+        self.scratch.attach(self)
+        z = self.scratch.zeros
         # --- activations ---
-        self.X = torch.zeros(R, S, D, dtype=bf16, device=dev)
-        self.normed = torch.zeros(R, D, dtype=bf16, device=dev)
-        self.post = [torch.zeros(R, S, dtype=f32, device=dev) for _ in range(2)]
-        self.comb = [torch.zeros(R, S, S, dtype=f32, device=dev) for _ in range(2)]
-        self.part = torch.zeros(R, D // 64, 32, dtype=f32, device=dev)
-        self.branch = torch.zeros(R, D, dtype=f32, device=dev)
-        self.hidden = torch.zeros(R, D, dtype=bf16, device=dev)
+        self.X = z(R, S, D, dtype=bf16, device=dev)
+        self.normed = z(R, D, dtype=bf16, device=dev)
+        self.post = [z(R, S, dtype=f32, device=dev) for _ in range(2)]
+        self.comb = [z(R, S, S, dtype=f32, device=dev) for _ in range(2)]
+        self.part = z(R, D // 64, 32, dtype=f32, device=dev)
+        self.branch = z(R, D, dtype=f32, device=dev)
+        self.hidden = z(R, D, dtype=bf16, device=dev)
         # reduce-scatter output of the sequence-parallel prefill (this rank's rows of the block sum)
-        self.rs = torch.zeros((R + self.tp - 1) // self.tp, D, dtype=f32, device=dev) if self.tp > 1 else None
-        self.fnormed = torch.zeros(R, D, dtype=bf16, device=dev)
-        self.lrows = torch.zeros(rc.logit_rows, D, dtype=bf16, device=dev)
-        self.logits = torch.zeros(rc.logit_rows, w.head.n, dtype=f32, device=dev)
+        self.rs = z((R + self.tp - 1) // self.tp, D, dtype=f32, device=dev) if self.tp > 1 else None
+        self.fnormed = z(R, D, dtype=bf16, device=dev)
+        self.lrows = z(rc.logit_rows, D, dtype=bf16, device=dev)
+        self.logits = z(rc.logit_rows, w.head.n, dtype=f32, device=dev)
         # --- KDA ---
         kda = [lw for lw in w.layers if lw.kind == "kda"]
         self.kda_index = {lw.index: i for i, lw in enumerate(kda)}
@@ -154,24 +159,24 @@ class Runtime:
             self.kda_width = width
             width = (width + 63) // 64 * 64          # padded row stride: 16-byte aligned rows for vector loads
             C3 = 3 * H * Dh
-            self.S_pool = [torch.zeros(2 * rc.max_seqs, H, Dh, Dh, dtype=f32, device=dev) for _ in kda]
-            self.conv_pool = [torch.zeros(rc.max_seqs, c.conv - 1, C3, dtype=bf16, device=dev) for _ in kda]
+            self.S_pool = [z(2 * rc.max_seqs, H, Dh, Dh, dtype=f32, device=dev) for _ in kda]
+            self.conv_pool = [z(rc.max_seqs, c.conv - 1, C3, dtype=bf16, device=dev) for _ in kda]
             dr = min(rc.decode_rows, R)
-            self.kproj_l = [torch.zeros(dr, width, dtype=bf16, device=dev) for _ in kda]
-            self.kf_l = [torch.zeros(dr, H * Dh, dtype=bf16, device=dev) for _ in kda]
-            self.kqkv_l = [torch.zeros(dr, C3, dtype=bf16, device=dev) for _ in kda]
-            self.kproj = torch.zeros(R, width, dtype=bf16, device=dev)
-            self.kf = torch.zeros(R, H * Dh, dtype=bf16, device=dev)
-            self.kqkv = torch.zeros(R, C3, dtype=bf16, device=dev)
-            self.kg = torch.zeros(R, H * Dh, dtype=bf16, device=dev)
+            self.kproj_l = [z(dr, width, dtype=bf16, device=dev) for _ in kda]
+            self.kf_l = [z(dr, H * Dh, dtype=bf16, device=dev) for _ in kda]
+            self.kqkv_l = [z(dr, C3, dtype=bf16, device=dev) for _ in kda]
+            self.kproj = z(R, width, dtype=bf16, device=dev)
+            self.kf = z(R, H * Dh, dtype=bf16, device=dev)
+            self.kqkv = z(R, C3, dtype=bf16, device=dev)
+            self.kg = z(R, H * Dh, dtype=bf16, device=dev)
             # chunked prefill records per (64-row chunk slot, head): Q~, K~, K^ [64, Dh] (fp16), T, P [64, 64],
             # e^{G_C} [Dh] (slots = chunks of the longest launch + sequences + 1; layout in csrc/kda_chunk.cu)
             self.kda_scr = None
             if R > KDA_CHUNK_MIN_ROWS:
                 n = K.C().kda_chunk_scratch_floats(R, rc.max_seqs, H, Dh)
-                self.kda_scr = torch.empty(n, dtype=f32, device=dev)
-            self.ko = torch.zeros(R, H * Dh, dtype=f32, device=dev)
-            self.kout = torch.zeros(R, H * Dh, dtype=bf16, device=dev)
+                self.kda_scr = z(n, dtype=f32, device=dev)
+            self.ko = z(R, H * Dh, dtype=f32, device=dev)
+            self.kout = z(R, H * Dh, dtype=bf16, device=dev)
         # --- MLA / DSA ---
         mla = [lw for lw in w.layers if lw.kind == "mla"]
         self.mla_index = {lw.index: i for i, lw in enumerate(mla)}
@@ -181,56 +186,56 @@ class Runtime:
             L, rope = c.kv_lora, c.qk_rope
             ns = rc.kv_slots
             assert ns % rc.block_size == 0 and rc.block_size % c.kpool == 0
-            self.kv = [torch.zeros(ns, L, dtype=torch.uint8, device=dev) for _ in mla]
-            self.kv_scale = [torch.zeros(ns, dtype=f32, device=dev) for _ in mla]
-            self.kpe = [torch.zeros(ns, max(rope, 1), dtype=bf16, device=dev) for _ in mla]
+            self.kv = [z(ns, L, dtype=torch.uint8, device=dev) for _ in mla]
+            self.kv_scale = [z(ns, dtype=f32, device=dev) for _ in mla]
+            self.kpe = [z(ns, max(rope, 1), dtype=bf16, device=dev) for _ in mla]
             # raw index keys / pool gate scores live only until their pool of kpool tokens is complete: this
             # forward's rows in shared row buffers, earlier tokens of open pools in a per-sequence tail ring per layer
             # (indexed by the sequence's state slot); the paged cache holds pooled keys only
             ring = K.DSA_RING
-            self.ik_rows = torch.zeros(R, c.index_dim, dtype=bf16, device=dev)
-            self.ig_rows = torch.zeros(R, c.index_dim, dtype=f32, device=dev)
-            self.ik_ring = [torch.zeros(rc.max_seqs * ring, c.index_dim, dtype=bf16, device=dev) for _ in mla]
-            self.ig_ring = [torch.zeros(rc.max_seqs * ring, c.index_dim, dtype=f32, device=dev) for _ in mla]
-            self.pool = [torch.zeros(ns // c.kpool, c.index_dim, dtype=torch.uint8, device=dev) for _ in mla]
-            self.pool_scale = [torch.zeros(ns // c.kpool, dtype=f32, device=dev) for _ in mla]
+            self.ik_rows = z(R, c.index_dim, dtype=bf16, device=dev)
+            self.ig_rows = z(R, c.index_dim, dtype=f32, device=dev)
+            self.ik_ring = [z(rc.max_seqs * ring, c.index_dim, dtype=bf16, device=dev) for _ in mla]
+            self.ig_ring = [z(rc.max_seqs * ring, c.index_dim, dtype=f32, device=dev) for _ in mla]
+            self.pool = [z(ns // c.kpool, c.index_dim, dtype=torch.uint8, device=dev) for _ in mla]
+            self.pool_scale = [z(ns // c.kpool, dtype=f32, device=dev) for _ in mla]
             AR = min(R, rc.attn_chunk)
-            self.qkv_a = torch.zeros(R, a0.qkv_a.n, dtype=bf16, device=dev)
-            self.qr = torch.zeros(R, c.q_lora, dtype=bf16, device=dev)
-            self.q = torch.zeros(R, H, c.qk_dim, dtype=bf16, device=dev)
-            self.q_lat = torch.zeros(R, H, L, dtype=bf16, device=dev)
-            self.o_lat = torch.zeros(R, H, L, dtype=bf16, device=dev)
-            self.obuf = torch.zeros(R, H * c.v_dim, dtype=bf16, device=dev)
-            self.iproj = torch.zeros(R, 2 * c.index_dim + c.index_heads, dtype=f32, device=dev)
-            self.qi = torch.zeros(R, c.index_heads * c.index_dim, dtype=bf16, device=dev)
+            self.qkv_a = z(R, a0.qkv_a.n, dtype=bf16, device=dev)
+            self.qr = z(R, c.q_lora, dtype=bf16, device=dev)
+            self.q = z(R, H, c.qk_dim, dtype=bf16, device=dev)
+            self.q_lat = z(R, H, L, dtype=bf16, device=dev)
+            self.o_lat = z(R, H, L, dtype=bf16, device=dev)
+            self.obuf = z(R, H * c.v_dim, dtype=bf16, device=dev)
+            self.iproj = z(R, 2 * c.index_dim + c.index_heads, dtype=f32, device=dev)
+            self.qi = z(R, c.index_heads * c.index_dim, dtype=bf16, device=dev)
             self.max_pools = rc.max_blocks * rc.block_size // c.kpool
-            self.dsa_logits = torch.zeros(AR, self.max_pools, dtype=f32, device=dev)
+            self.dsa_logits = z(AR, self.max_pools, dtype=f32, device=dev)
             self.max_sel = max(c.index_topk, 1)
-            self.sel = torch.zeros(AR, max(self.max_sel, c.index_topk), dtype=i32, device=dev)
-            self.sel_count = torch.zeros(AR, dtype=i32, device=dev)
+            self.sel = z(AR, max(self.max_sel, c.index_topk), dtype=i32, device=dev)
+            self.sel_count = z(AR, dtype=i32, device=dev)
             self.splits = rc.mla_splits
             self.sms = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
             # partials: decode-sized forwards split the keys; the CUDA-core kernel also stages unsplit rows here
             PR = max(min(AR, rc.decode_rows) * rc.mla_splits, AR)
-            self.part_o = torch.zeros(PR * H * L, dtype=f32, device=dev)
-            self.part_ml = torch.zeros(PR * H * 2, dtype=f32, device=dev)
+            self.part_o = z(PR * H * L, dtype=f32, device=dev)
+            self.part_ml = z(PR * H * 2, dtype=f32, device=dev)
         # --- MLP / MoE ---
         MR = min(R, rc.moe_chunk)
         tk = c.top_k
         P = MR * tk
         widths = [self.gu_il[i].w.shape[0] // 2 for i in self.gu_il]
-        self.act = torch.zeros(R, max(widths), dtype=bf16, device=dev)
-        self.rlogits = torch.zeros(MR, c.experts, dtype=f32, device=dev)
-        self.topk_ids = torch.zeros(MR, tk, dtype=i32, device=dev)
-        self.topk_w = torch.zeros(MR, tk, dtype=f32, device=dev)
+        self.act = z(R, max(widths), dtype=bf16, device=dev)
+        self.rlogits = z(MR, c.experts, dtype=f32, device=dev)
+        self.topk_ids = z(MR, tk, dtype=i32, device=dev)
+        self.topk_w = z(MR, tk, dtype=f32, device=dev)
         self.max_groups = min(P, c.experts)
-        self.group_count = torch.zeros(1, dtype=i32, device=dev)
-        self.group_expert = torch.zeros(self.max_groups, dtype=i32, device=dev)
-        self.group_offset = torch.zeros(self.max_groups + 1, dtype=i32, device=dev)
-        self.pair_token = torch.zeros(P, dtype=i32, device=dev)
-        self.pair_expert = torch.zeros(P, dtype=i32, device=dev)
-        self.pair_w = torch.zeros(P, dtype=f32, device=dev)
-        self.pair_of = torch.zeros(P, dtype=i32, device=dev)
+        self.group_count = z(1, dtype=i32, device=dev)
+        self.group_expert = z(self.max_groups, dtype=i32, device=dev)
+        self.group_offset = z(self.max_groups + 1, dtype=i32, device=dev)
+        self.pair_token = z(P, dtype=i32, device=dev)
+        self.pair_expert = z(P, dtype=i32, device=dev)
+        self.pair_w = z(P, dtype=f32, device=dev)
+        self.pair_of = z(P, dtype=i32, device=dev)
         moe0 = next((lw.moe for lw in w.layers if lw.moe is not None), None)
         self.prefill_moe = R > MOE_PREFILL_MIN_ROWS and moe0 is not None
         if self.prefill_moe:
@@ -238,18 +243,18 @@ class Runtime:
             PR = min(R, rc.moe_prefill_rows)
             self.p_rows = PR
             PP = PR * tk
-            self.p_logits = torch.zeros(PR, c.experts, dtype=f32, device=dev)
-            self.p_topk_ids = torch.zeros(PR, tk, dtype=i32, device=dev)
-            self.p_topk_w = torch.zeros(PR, tk, dtype=f32, device=dev)
+            self.p_logits = z(PR, c.experts, dtype=f32, device=dev)
+            self.p_topk_ids = z(PR, tk, dtype=i32, device=dev)
+            self.p_topk_w = z(PR, tk, dtype=f32, device=dev)
             self.p_groups = c.experts
-            self.p_group_expert = torch.zeros(c.experts, dtype=i32, device=dev)
-            self.p_group_offset = torch.zeros(c.experts + 1, dtype=i32, device=dev)
-            self.p_pair_token = torch.zeros(PP, dtype=i32, device=dev)
-            self.p_pair_expert = torch.zeros(PP, dtype=i32, device=dev)
-            self.p_pair_w = torch.zeros(PP, dtype=f32, device=dev)
-            self.p_pair_of = torch.zeros(PP, dtype=i32, device=dev)
-            self.p_counts = torch.zeros(c.experts, dtype=i32, device=dev)
-            self.p_fill = torch.zeros(c.experts, dtype=i32, device=dev)
+            self.p_group_expert = z(c.experts, dtype=i32, device=dev)
+            self.p_group_offset = z(c.experts + 1, dtype=i32, device=dev)
+            self.p_pair_token = z(PP, dtype=i32, device=dev)
+            self.p_pair_expert = z(PP, dtype=i32, device=dev)
+            self.p_pair_w = z(PP, dtype=f32, device=dev)
+            self.p_pair_of = z(PP, dtype=i32, device=dev)
+            self.p_counts = z(c.experts, dtype=i32, device=dev)
+            self.p_fill = z(c.experts, dtype=i32, device=dev)
             P = max(P, PP)
         # expert parallelism (weights prepared with ep=True): each rank routes its own share of the rows, dispatches
         # them to the ranks owning their experts and receives their outputs (parallel/ep.py, one exchange and one
@@ -265,10 +270,10 @@ class Runtime:
         if moe0 is not None and self.ep is None:
             # the decode path stores its rotated inputs as duplicated f16 pairs (2 halves per element)
             PX = max(P, 2 * MR * tk)
-            self.xh_g = torch.zeros(PX, D, dtype=torch.float16, device=dev)
-            self.xh_u = torch.zeros(PX, D, dtype=torch.float16, device=dev)
-            self.xd = torch.zeros(PX, moe0.gate.n, dtype=torch.float16, device=dev)
-            self.yd = torch.zeros(P, D, dtype=f32, device=dev)
+            self.xh_g = z(PX, D, dtype=torch.float16, device=dev)
+            self.xh_u = z(PX, D, dtype=torch.float16, device=dev)
+            self.xd = z(PX, moe0.gate.n, dtype=torch.float16, device=dev)
+            self.yd = z(P, D, dtype=f32, device=dev)
 
     # ------------------------------------------------------------------------------------------------------------
     # host-side batch staging (pinned buffer -> one H2D copy per array)

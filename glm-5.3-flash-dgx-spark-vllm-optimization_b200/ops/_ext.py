@@ -5,6 +5,12 @@ into ``<package>/_build/``, next to the sources, so the built ``.so`` travels wi
 imports a built library directly (no rebuild check) and builds it when it is missing; ``build()`` always runs the
 (incremental, ninja) build.  On a machine with a CUDA device the extension is mandatory: ``require()`` raises if it
 cannot be loaded, so no op silently falls back to PyTorch.
+
+``GLM53_BOUNDS=1`` selects the bounds-checked debug build instead: the same sources compiled with
+``-DG53_BOUNDS=1`` into ``glm53_C_bounds`` under ``<package>/_build_bounds/``.  Its kernels check every index
+they read from device data (token ids, cache slots, state slots, expert ids, token rows of the MoE pairs) against
+the tensor it indexes, skip the access when it is out of range and record the first failure per compilation unit;
+``bounds_status()`` / ``bounds_reset()`` of the module read and clear the records.
 """
 
 from __future__ import annotations
@@ -17,10 +23,12 @@ import threading
 
 _PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 CSRC = os.path.join(_PKG, "csrc")
-BUILD_DIR = os.path.join(_PKG, "_build")
-NAME = "glm53_C"
+BOUNDS = os.environ.get("GLM53_BOUNDS", "0") == "1"
+BUILD_DIR = os.path.join(_PKG, "_build_bounds" if BOUNDS else "_build")
+NAME = "glm53_C_bounds" if BOUNDS else "glm53_C"
 ARCH_FLAGS = ["-gencode=arch=compute_100a,code=sm_100a"]
-NVCC_FLAGS = ARCH_FLAGS + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xptxas=-v"]
+_DEFS = ["-DG53_BOUNDS=1"] if BOUNDS else []
+NVCC_FLAGS = ARCH_FLAGS + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xptxas=-v"] + _DEFS
 
 _lock = threading.Lock()
 _mod = None
@@ -54,7 +62,7 @@ def build(verbose: bool = False):
     os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
     with _lock:
         _mod = ce.load(name=NAME, sources=sources(), extra_cuda_cflags=NVCC_FLAGS,
-                       extra_cflags=["-O3", "-std=c++17"], build_directory=BUILD_DIR, verbose=verbose,
+                       extra_cflags=["-O3", "-std=c++17"] + _DEFS, build_directory=BUILD_DIR, verbose=verbose,
                        with_cuda=True)
     return _mod
 

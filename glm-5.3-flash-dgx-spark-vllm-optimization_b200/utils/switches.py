@@ -42,6 +42,8 @@ SWITCHES: dict[str, Switch] = {
     "GLM53_SP_MIN_ROWS": Switch("int", "256", "rows of a prefill chunk from which sequence parallelism is used"),
     "GLM53_SP_MLA": Switch("bool", "1", "sequence-parallel prefill runs the MLA attention of each rank's rows over "
                                         "all heads (keeps the full-head MLA projections on every rank)"),
+    "GLM53_BOUNDS": Switch("bool", "0", "load the bounds-checked debug build (glm53_C_bounds): device indices "
+                                        "checked against their tensors, guard bands around runtime scratch"),
     "GLM53_L2_PREFETCH": Switch("bool", "0", "routed-expert CTAs prefetch the next layer's weights into L2"),
     "GLM53_L2_PREFETCH_MB": Switch("float", "32", "L2 prefetch budget in MiB"),
     "GLM53_PREFILL_W8A8": Switch("projections", ",".join(W8A8_PROJECTIONS),

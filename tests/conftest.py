@@ -30,6 +30,29 @@ def _exact_prefill_projections(request, monkeypatch):
     yield
 
 
+@pytest.fixture(autouse=True)
+def _bounds_and_guards(request):
+    """Under the bounds-checked build (GLM53_BOUNDS=1) every GPU test ends with no out-of-range index recorded by
+    a kernel and every guard band around the runtimes' scratch buffers intact."""
+    if os.environ.get("GLM53_BOUNDS", "0") != "1" or not request.node.get_closest_marker("gpu"):
+        yield
+        return
+    import torch
+    from glm53.ops import _ext
+    from glm53.utils import canary
+    mod = _ext.require()
+    torch.cuda.synchronize()
+    mod.bounds_reset()
+    yield
+    torch.cuda.synchronize()
+    enabled, fails = mod.bounds_status()
+    bad = canary.check_all()
+    mod.bounds_reset()
+    assert enabled, "GLM53_BOUNDS=1 but the loaded extension was built without bounds checks"
+    assert not fails, f"out-of-range device indices (code, index, limit, count): {fails}"
+    assert not bad, f"guard bands overwritten: {bad}"
+
+
 @pytest.fixture(scope="session")
 def tiny_cfg():
     import glm53
