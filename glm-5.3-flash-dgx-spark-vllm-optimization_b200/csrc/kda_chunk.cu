@@ -6,10 +6,11 @@
 //   o    = Q~ S0^T + P v',    P_ts = sum_c q_t k_s e^{G_t - G_s} (s <= t)
 //   S_C  = S0 diag(e^{G_C}) + v'^T K^ ,   K~_t = k_t e^{G_t},  Q~_t = q_t e^{G_t},  K^_s = k_s e^{G_C - G_s}
 //
-// kda_prep_kernel   one CTA per (chunk, head, sequence), all chunks in parallel: normalised rows, cumulative
-//                   decay, M and P (fp32, with 16-row sub-chunk reference points so every exponential factor stays
-//                   bounded), the unit lower-triangular inverse by forward substitution, T, and the scaled rows
-//                   Q~, K~, K^ and e^{G_C}; written to a per-(chunk, head) scratch.
+// kda_prep_kernel   one CTA per (chunk, head, sequence), two per SM, all chunks in parallel, over 64-channel
+//                   blocks: normalised rows, cumulative decay, M and P (3xTF32 tensor-core products with fp32
+//                   accumulation, 16-row sub-chunk reference points so every exponential factor stays bounded),
+//                   the unit lower-triangular inverse by forward substitution, T, and the scaled rows Q~, K~, K^
+//                   and e^{G_C}; written to a per-(chunk, head) scratch.
 // kda_scan_kernel   one CTA per (head, 32 value rows, sequence), sequential over the chunks: the four chunk
 //                   products (K~ S0^T, T Z, Q~ S0^T + P v', v'^T K^) on the tensor cores (mma.sync m16n8k8 tf32,
 //                   fp32 accumulate) with the state S kept in fp32 in shared memory.
@@ -31,242 +32,7 @@ __host__ __device__ constexpr int64_t kda_scr_per_head(int dh) { return 3LL * kC
 __device__ __forceinline__ int chunk_slot(int row0, int b, int c) { return row0 / kC + b + c; }
 
 // ---------------------------------------------------------------------------------------------------------------
-// prep: grid (max chunks, H, B), 256 threads
-// ---------------------------------------------------------------------------------------------------------------
-template <int DH>
-__global__ void __launch_bounds__(256, 1) kda_prep_kernel(KdaArgs a) {
-  constexpr int P1 = DH + 1;
-  extern __shared__ float sm[];
-  float* sK = sm;                       // [kC][P1] normalised k
-  float* sQ = sK + kC * P1;             // [kC][P1] normalised, scaled q
-  float* sG = sQ + kC * P1;             // [kC][P1] raw g, then cumulative G
-  float* sX = sG + kC * P1;             // [kC][P1] scratch: k_s e^{G_r - G_s}, then K^
-  float* sA = sX + kC * P1;             // [kSubR][P1] k_t e^{G_t - G_r}
-  float* sQt = sA + kSubR * P1;         // [kSubR][P1] q_t e^{G_t - G_r}
-  float* sM = sQt + kSubR * P1;         // [kC][kC+1]
-  float* sP = sM + kC * (kC + 1);       // [kC][kC+1]
-  float* sI = sP + kC * (kC + 1);       // [kC][kC+1] (I + diag(beta) M)^{-1}
-  float* sB = sI + kC * (kC + 1);       // [kC] beta
-
-  const int ci = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int base = a.row0[b], n_all = a.nrows[b];
-  const int c0 = ci * kC;
-  if (c0 >= n_all) return;
-  const int n = min(kC, n_all - c0);
-  const int slot = chunk_slot(base, b, ci);
-  if (slot >= a.scr_slots) return;                 // the launcher sizes the scratch; never reached
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int HD = a.H * DH;
-  const float ea = __expf(a.a_log[h]);
-
-  // 1. rows: normalised q, k; raw g; beta.  A warp owns rows warp, warp + 8, ...; the loads of 4 rows are issued
-  //    together (raw bf16 in registers) before any of them is reduced, so the global latency is paid twice, not 8x
-  constexpr int PL = DH / 32;
-  for (int t0 = warp; t0 < kC; t0 += 32) {
-    __nv_bfloat16 rq[4][PL], rk[4][PL], rf[4][PL], rb[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int t = t0 + 8 * u, row = base + c0 + t;
-      const bool on = t < n;
-      const __nv_bfloat16* rp = a.qkv + (int64_t)(on ? row : base) * 3 * HD;
-      const __nv_bfloat16* fp = a.f + (int64_t)(on ? row : base) * HD + h * DH;
-#pragma unroll
-      for (int i = 0; i < PL; ++i) {
-        const int c = lane + 32 * i;
-        rq[u][i] = rp[h * DH + c];
-        rk[u][i] = rp[HD + h * DH + c];
-        rf[u][i] = fp[c];
-      }
-      rb[u] = a.proj[(int64_t)(on ? row : base) * a.ldp + a.b_off + h];
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int t = t0 + 8 * u;
-      const bool on = t < n;
-      float q[PL], k[PL], g[PL];
-      float sq = 0.f, sk = 0.f;
-#pragma unroll
-      for (int i = 0; i < PL; ++i) {
-        const int c = lane + 32 * i;
-        q[i] = on ? bf2f(rq[u][i]) : 0.f;
-        k[i] = on ? bf2f(rk[u][i]) : 0.f;
-        g[i] = on ? a.lower * sigmoidf_(ea * (bf2f(rf[u][i]) + a.dt_bias[h * DH + c])) : 0.f;
-        sq += q[i] * q[i];
-        sk += k[i] * k[i];
-      }
-      sq = warp_sum(sq);
-      sk = warp_sum(sk);
-      const float qn = rsqrtf(sq + 1e-6f) * rsqrtf((float)DH), kn = rsqrtf(sk + 1e-6f);
-#pragma unroll
-      for (int i = 0; i < PL; ++i) {
-        const int c = lane + 32 * i;
-        sQ[t * P1 + c] = q[i] * qn;
-        sK[t * P1 + c] = k[i] * kn;
-        sG[t * P1 + c] = g[i];
-      }
-      if (lane == 0) sB[t] = on ? sigmoidf_(bf2f(rb[u])) : 0.f;
-    }
-  }
-  __syncthreads();
-  // 2. cumulative log-decay per channel (rows past n add 0 and keep the last value): 4 segments of 16 rows per
-  //    channel summed in parallel (two per thread), then each segment adds the totals of the segments before it
-  {
-    constexpr int TPC = 256 / DH;                    // threads per channel (2 or 4)
-    constexpr int SPT = 4 / TPC;                     // segments per thread
-    const int c = tid % DH, sb = tid / DH;           // this thread's segments: sb, sb + TPC, ...
-    float acc[SPT];
-#pragma unroll
-    for (int i = 0; i < SPT; ++i) acc[i] = 0.f;
-#pragma unroll 4
-    for (int t = 0; t < 16; ++t) {
-#pragma unroll
-      for (int i = 0; i < SPT; ++i) {
-        const int r = (sb + TPC * i) * 16 + t;
-        acc[i] += sG[r * P1 + c];
-        sG[r * P1 + c] = acc[i];
-      }
-    }
-    __syncthreads();
-    const float tot0 = sG[15 * P1 + c], tot1 = sG[31 * P1 + c], tot2 = sG[47 * P1 + c];
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < SPT; ++i) {
-      const int sg = sb + TPC * i;
-      if (sg == 0) continue;
-      const float add = sg == 1 ? tot0 : (sg == 2 ? tot0 + tot1 : (tot0 + tot1) + tot2);
-#pragma unroll 4
-      for (int t = 0; t < 16; ++t) sG[(sg * 16 + t) * P1 + c] += add;
-    }
-  }
-  __syncthreads();
-  // 3. M (strictly lower) and P (lower incl. diagonal), one 16-row sub-chunk of t at a time; reference row r
-  for (int j = 0; j < kC / kSubR; ++j) {
-    const int r = j * kSubR;
-    const int ns = r + kSubR;                      // s ranges over [0, ns)
-    for (int e = tid; e < kSubR * DH; e += blockDim.x) {
-      const int t = e / DH, c = e % DH;
-      const float f = __expf(sG[(r + t) * P1 + c] - sG[r * P1 + c]);
-      sA[t * P1 + c] = sK[(r + t) * P1 + c] * f;
-      sQt[t * P1 + c] = sQ[(r + t) * P1 + c] * f;
-    }
-    for (int e = tid; e < ns * DH; e += blockDim.x) {
-      const int s = e / DH, c = e % DH;
-      sX[s * P1 + c] = sK[s * P1 + c] * __expf(sG[r * P1 + c] - sG[s * P1 + c]);
-    }
-    __syncthreads();
-    const int strips = ns / 4;
-    for (int e = tid; e < kSubR * strips; e += blockDim.x) {
-      const int t = e / strips, s0 = (e % strips) * 4;
-      const int tt = r + t;
-      float m[4] = {0.f, 0.f, 0.f, 0.f}, pp[4] = {0.f, 0.f, 0.f, 0.f};
-      if (s0 <= tt) {
-#pragma unroll 4
-        for (int c = 0; c < DH; ++c) {
-          const float av = sA[t * P1 + c], qv = sQt[t * P1 + c];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float bs = sX[(s0 + i) * P1 + c];
-            m[i] += av * bs;
-            pp[i] += qv * bs;
-          }
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int s = s0 + i;
-        sM[tt * (kC + 1) + s] = s < tt ? m[i] : 0.f;
-        sP[tt * (kC + 1) + s] = s <= tt ? pp[i] : 0.f;
-      }
-    }
-    __syncthreads();
-  }
-  // zero the upper parts of M and P (columns >= ns of each sub-chunk were not written)
-  for (int e = tid; e < kC * kC; e += blockDim.x) {
-    const int t = e / kC, s = e % kC;
-    if (s >= (t / kSubR + 1) * kSubR) { sM[t * (kC + 1) + s] = 0.f; sP[t * (kC + 1) + s] = 0.f; }
-  }
-  __syncthreads();
-  // 4. X = (I + diag(beta) M)^{-1} (unit lower triangular) in 16 x 16 blocks: the four diagonal blocks by forward
-  //    substitution, one warp each with a column per lane held in registers (no block-wide barriers), then the
-  //    blocks below the diagonal by distance d = i - j: X_ij = -X_ii sum_{k=j}^{i-1} (diag(beta) M)_ik X_kj
-  {
-    for (int e = tid; e < kC * kC; e += blockDim.x) sI[(e / kC) * (kC + 1) + e % kC] = 0.f;
-    __syncthreads();
-    if (warp < 4 && lane < kSubR) {
-      const int o = warp * kSubR, j = lane;
-      float x[kSubR];
-#pragma unroll
-      for (int t = 0; t < kSubR; ++t) x[t] = t == j ? 1.f : 0.f;
-#pragma unroll
-      for (int t = 1; t < kSubR; ++t) {
-        float acc = 0.f;
-#pragma unroll
-        for (int s2 = 0; s2 < t; ++s2) acc += sM[(o + t) * (kC + 1) + o + s2] * x[s2];
-        if (t > j) x[t] = -sB[o + t] * acc;
-      }
-#pragma unroll
-      for (int t = 0; t < kSubR; ++t) sI[(o + t) * (kC + 1) + o + j] = x[t];
-    }
-    __syncthreads();
-    float* sW = sX;                                   // free until step 5: W blocks of one distance
-    for (int d = 1; d < kC / kSubR; ++d) {
-      const int nblk = kC / kSubR - d;
-      for (int e = tid; e < nblk * kSubR * kSubR; e += blockDim.x) {
-        const int j = e / (kSubR * kSubR), r = (e / kSubR) % kSubR, col = e % kSubR, i = j + d;
-        float w = 0.f;
-        for (int kb = j; kb < i; ++kb)
-#pragma unroll 4
-          for (int m = 0; m < kSubR; ++m)
-            w += sM[(kSubR * i + r) * (kC + 1) + kSubR * kb + m] * sI[(kSubR * kb + m) * (kC + 1) + kSubR * j + col];
-        sW[e] = w * sB[kSubR * i + r];
-      }
-      __syncthreads();
-      for (int e = tid; e < nblk * kSubR * kSubR; e += blockDim.x) {
-        const int j = e / (kSubR * kSubR), r = (e / kSubR) % kSubR, col = e % kSubR, i = j + d;
-        float x = 0.f;
-#pragma unroll 4
-        for (int m = 0; m < kSubR; ++m)
-          x += sI[(kSubR * i + r) * (kC + 1) + kSubR * i + m] * sW[j * kSubR * kSubR + m * kSubR + col];
-        sI[(kSubR * i + r) * (kC + 1) + kSubR * j + col] = -x;
-      }
-      __syncthreads();
-    }
-  }
-  // 5. scaled rows: Q~ = q e^{G}, K~ = k e^{G} (in place), K^ = k e^{G_C - G} (rows past n: 0)
-  const int last = n - 1;
-  for (int e = tid; e < kC * DH; e += blockDim.x) {
-    const int t = e / DH, c = e % DH;
-    const float G = sG[t * P1 + c];
-    sX[t * P1 + c] = t < n ? sK[t * P1 + c] * __expf(sG[last * P1 + c] - G) : 0.f;
-    const float d = __expf(G);
-    sK[t * P1 + c] *= d;
-    sQ[t * P1 + c] *= d;
-  }
-  __syncthreads();
-  // 6. write the chunk record: Q~, K~, K^ [kC][DH], T = X diag(beta) [kC][kC], P [kC][kC], e^{G_C} [DH]
-  float* out = a.scr + ((int64_t)slot * a.H + h) * kda_scr_per_head(DH);
-  __half* oQ = reinterpret_cast<__half*>(out);
-  __half* oK = oQ + kC * DH;
-  __half* oKb = oK + kC * DH;
-  float* oT = out + 3 * kC * DH / 2;
-  float* oP = oT + kC * kC;
-  float* oE = oP + kC * kC;
-  for (int e = tid; e < kC * DH / 2; e += blockDim.x) {
-    const int t = (2 * e) / DH, c = (2 * e) % DH;
-    reinterpret_cast<__half2*>(oQ)[e] = __floats2half2_rn(sQ[t * P1 + c], sQ[t * P1 + c + 1]);
-    reinterpret_cast<__half2*>(oK)[e] = __floats2half2_rn(sK[t * P1 + c], sK[t * P1 + c + 1]);
-    reinterpret_cast<__half2*>(oKb)[e] = __floats2half2_rn(sX[t * P1 + c], sX[t * P1 + c + 1]);
-  }
-  for (int e = tid; e < kC * kC; e += blockDim.x) {
-    const int t = e / kC, s = e % kC;
-    oT[e] = sI[t * (kC + 1) + s] * sB[s];
-    oP[e] = sP[t * (kC + 1) + s];
-  }
-  for (int c = tid; c < DH; c += blockDim.x) oE[c] = __expf(sG[last * P1 + c]);
-}
-
-// ---------------------------------------------------------------------------------------------------------------
-// scan: grid (H, DH/32, B), 256 threads (8 warps)
+// tf32 tensor-core helpers (both kernels)
 // ---------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t to_tf32(float x) {
   uint32_t r;
@@ -280,6 +46,261 @@ __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// x = hi + lo with hi and lo both tf32 (3xTF32: hi*hi + hi*lo + lo*hi keeps about fp32 accuracy)
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = to_tf32(x);
+  lo = to_tf32(x - __uint_as_float(hi));
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// prep: grid (max chunks, H, B), 256 threads, two CTAs per SM.
+// The channels are taken in blocks of kCB = 64 (DH / 64 blocks): a block's rows, cumulative decay and scaled rows
+// need only its own channels, and M / P are sums over channels, so each block adds its part to M and P and writes
+// its columns of Q~, K~, K^ and e^{G_C} to the record; the unit lower-triangular inverse runs once at the end.
+// The M / P products (16 rows of t x up to 64 keys s x 64 channels per sub-chunk) run on the tensor cores as
+// 3xTF32 m16n8k8 products.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kCB = 64;                 // channels per block
+constexpr int kPH = kCB + 4;            // row pitch of the block tiles: the mma fragment loads hit 32 banks
+constexpr int kPM = kC + 1;             // row pitch of the 64 x 64 chunk matrices
+
+__host__ __device__ constexpr int prep_smem_floats() { return 4 * kC * kPH + 2 * kSubR * kPH + 2 * kC * kPM + kC; }
+
+template <int DH>
+__global__ void __launch_bounds__(256, 2) kda_prep_kernel(KdaArgs a) {
+  constexpr int NB = DH / kCB;          // channel blocks
+  constexpr int PL = DH / 32;           // channels per lane of a full row
+  extern __shared__ float sm[];
+  float* sK = sm;                       // [kC][kPH] normalised k of the block's channels
+  float* sQ = sK + kC * kPH;            // [kC][kPH] normalised, scaled q
+  float* sG = sQ + kC * kPH;            // [kC][kPH] raw g, then cumulative G
+  float* sX = sG + kC * kPH;            // [kC][kPH] k_s e^{G_r - G_s}
+  float* sA = sX + kC * kPH;            // [kSubR][kPH] k_t e^{G_t - G_r}
+  float* sQt = sA + kSubR * kPH;        // [kSubR][kPH] q_t e^{G_t - G_r}
+  float* sM = sQt + kSubR * kPH;        // [kC][kPM] M (summed over the channel blocks)
+  float* sP = sM + kC * kPM;            // [kC][kPM] P
+  float* sB = sP + kC * kPM;            // [kC] beta
+  float* sI = sm;                       // [kC][kPM] (I + diag(beta) M)^{-1}: after the blocks, over sK / sQ
+  float* sW = sm + kC * kPM;            // W blocks of one distance (step 4)
+
+  const int ci = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int base = a.row0[b], n_all = a.nrows[b];
+  const int c0 = ci * kC;
+  if (c0 >= n_all) return;
+  const int n = min(kC, n_all - c0);
+  const int slot = chunk_slot(base, b, ci);
+  if (slot >= a.scr_slots) return;                 // the launcher sizes the scratch; never reached
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g8 = lane >> 2, q4 = lane & 3;
+  const int HD = a.H * DH;
+  const float ea = __expf(a.a_log[h]);
+  const int last = n - 1;
+
+  float* out = a.scr + ((int64_t)slot * a.H + h) * kda_scr_per_head(DH);
+  __half* oQ = reinterpret_cast<__half*>(out);
+  __half* oK = oQ + kC * DH;
+  __half* oKb = oK + kC * DH;
+  float* oT = out + 3 * kC * DH / 2;
+  float* oP = oT + kC * kC;
+  float* oE = oP + kC * kC;
+
+  for (int e = tid; e < 2 * kC * kPM; e += blockDim.x) sM[e] = 0.f;     // sM and sP are adjacent
+
+  for (int hb = 0; hb < NB; ++hb) {
+    const int cb = hb * kCB;
+    if (hb > 0) __syncthreads();                  // the previous block's tiles are consumed
+    // 1. rows: normalised q, k (norms over all DH channels), this block's raw g, beta.  A warp owns rows warp,
+    //    warp + 8, ...; the loads of 4 rows are issued together before any of them is reduced
+    for (int t0 = warp; t0 < kC; t0 += 32) {
+      __nv_bfloat16 rq[4][PL], rk[4][PL], rf[4][2], rb[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = t0 + 8 * u, row = base + c0 + t;
+        const bool on = t < n;
+        const __nv_bfloat16* rp = a.qkv + (int64_t)(on ? row : base) * 3 * HD;
+        const __nv_bfloat16* fp = a.f + (int64_t)(on ? row : base) * HD + h * DH + cb;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) {
+          const int c = lane + 32 * i;
+          rq[u][i] = rp[h * DH + c];
+          rk[u][i] = rp[HD + h * DH + c];
+        }
+#pragma unroll
+        for (int i = 0; i < 2; ++i) rf[u][i] = fp[lane + 32 * i];
+        rb[u] = a.proj[(int64_t)(on ? row : base) * a.ldp + a.b_off + h];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int t = t0 + 8 * u;
+        const bool on = t < n;
+        float q[PL], k[PL];
+        float sq = 0.f, sk = 0.f;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) {
+          q[i] = on ? bf2f(rq[u][i]) : 0.f;
+          k[i] = on ? bf2f(rk[u][i]) : 0.f;
+          sq += q[i] * q[i];
+          sk += k[i] * k[i];
+        }
+        sq = warp_sum(sq);
+        sk = warp_sum(sk);
+        const float qn = rsqrtf(sq + 1e-6f) * rsqrtf((float)DH), kn = rsqrtf(sk + 1e-6f);
+#pragma unroll
+        for (int i = 0; i < PL; ++i) {               // the lane's channels of this block: i / 2 == hb
+          if ((i >> 1) != hb) continue;
+          const int cl = lane + 32 * (i & 1), c = cb + cl;
+          sQ[t * kPH + cl] = q[i] * qn;
+          sK[t * kPH + cl] = k[i] * kn;
+          sG[t * kPH + cl] = on ? a.lower * sigmoidf_(ea * (bf2f(rf[u][i & 1]) + a.dt_bias[h * DH + c])) : 0.f;
+        }
+        if (hb == 0 && lane == 0) sB[t] = on ? sigmoidf_(bf2f(rb[u])) : 0.f;
+      }
+    }
+    __syncthreads();
+    // 2. cumulative log-decay per channel (rows past n add 0 and keep the last value): four 16-row segments per
+    //    channel summed in parallel, one per thread, then each segment adds the totals of the segments before it
+    {
+      const int c = tid % kCB, sb = tid / kCB;
+      float acc = 0.f;
+#pragma unroll 4
+      for (int t = 0; t < 16; ++t) {
+        const int r = sb * 16 + t;
+        acc += sG[r * kPH + c];
+        sG[r * kPH + c] = acc;
+      }
+      __syncthreads();
+      const float tot0 = sG[15 * kPH + c], tot1 = sG[31 * kPH + c], tot2 = sG[47 * kPH + c];
+      __syncthreads();
+      if (sb > 0) {
+        const float add = sb == 1 ? tot0 : (sb == 2 ? tot0 + tot1 : (tot0 + tot1) + tot2);
+#pragma unroll 4
+        for (int t = 0; t < 16; ++t) sG[(sb * 16 + t) * kPH + c] += add;
+      }
+    }
+    __syncthreads();
+    // 3. this block's part of M (strictly lower) and P (lower incl. diagonal), one 16-row sub-chunk of t at a time
+    //    with reference row r (every exponential factor stays bounded); warp jobs = (matrix, 8-key tile)
+    for (int j = 0; j < kC / kSubR; ++j) {
+      const int r = j * kSubR;
+      const int ns = r + kSubR;                    // s ranges over [0, ns)
+      for (int e = tid; e < kSubR * kCB; e += blockDim.x) {
+        const int t = e / kCB, c = e % kCB;
+        const float f = __expf(sG[(r + t) * kPH + c] - sG[r * kPH + c]);
+        sA[t * kPH + c] = sK[(r + t) * kPH + c] * f;
+        sQt[t * kPH + c] = sQ[(r + t) * kPH + c] * f;
+      }
+      for (int e = tid; e < ns * kCB; e += blockDim.x) {
+        const int s = e / kCB, c = e % kCB;
+        sX[s * kPH + c] = sK[s * kPH + c] * __expf(sG[r * kPH + c] - sG[s * kPH + c]);
+      }
+      __syncthreads();
+      const int jobs = 2 * (ns / 8);
+      for (int jb = warp; jb < jobs; jb += 8) {
+        const int mm = jb & 1, nt = jb >> 1;
+        const float* As = mm ? sQt : sA;
+        const float* Bs = sX + (nt * 8 + g8) * kPH;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+        for (int k0 = 0; k0 < kCB; k0 += 8) {
+          uint32_t ah[4], al[4], bh[2], bl[2];
+          split_tf32(As[g8 * kPH + k0 + q4], ah[0], al[0]);
+          split_tf32(As[(g8 + 8) * kPH + k0 + q4], ah[1], al[1]);
+          split_tf32(As[g8 * kPH + k0 + q4 + 4], ah[2], al[2]);
+          split_tf32(As[(g8 + 8) * kPH + k0 + q4 + 4], ah[3], al[3]);
+          split_tf32(Bs[k0 + q4], bh[0], bl[0]);
+          split_tf32(Bs[k0 + q4 + 4], bh[1], bl[1]);
+          mma_tf32(acc, al, bh[0], bh[1]);
+          mma_tf32(acc, ah, bl[0], bl[1]);
+          mma_tf32(acc, ah, bh[0], bh[1]);
+        }
+        // accumulator (t = r + g8 (+8), s = nt*8 + 2 q4 (+1)); each element has one owner: plain adds
+        float* dst = mm ? sP : sM;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int tt = r + g8 + (i >> 1) * 8, s = nt * 8 + 2 * q4 + (i & 1);
+          const bool keep = mm ? s <= tt : s < tt;
+          if (keep) dst[tt * kPM + s] += acc[i];
+        }
+      }
+      __syncthreads();
+    }
+    // 5. this block's scaled rows into the record: Q~ = q e^{G}, K~ = k e^{G}, K^ = k e^{G_C - G} (rows past n: 0),
+    //    and e^{G_C}
+    for (int e = tid; e < kC * kCB / 2; e += blockDim.x) {
+      const int t = (2 * e) / kCB, c = (2 * e) % kCB;
+      float vq[2], vk[2], vb[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const float G = sG[t * kPH + c + i];
+        const float d = __expf(G);
+        vq[i] = sQ[t * kPH + c + i] * d;
+        vk[i] = sK[t * kPH + c + i] * d;
+        vb[i] = t < n ? sK[t * kPH + c + i] * __expf(sG[last * kPH + c + i] - G) : 0.f;
+      }
+      const int64_t o = (int64_t)t * DH + cb + c;
+      *reinterpret_cast<__half2*>(oQ + o) = __floats2half2_rn(vq[0], vq[1]);
+      *reinterpret_cast<__half2*>(oK + o) = __floats2half2_rn(vk[0], vk[1]);
+      *reinterpret_cast<__half2*>(oKb + o) = __floats2half2_rn(vb[0], vb[1]);
+    }
+    for (int c = tid; c < kCB; c += blockDim.x) oE[cb + c] = __expf(sG[last * kPH + c]);
+  }
+  __syncthreads();
+  // 4. X = (I + diag(beta) M)^{-1} (unit lower triangular) in 16 x 16 blocks: the four diagonal blocks by forward
+  //    substitution, one warp each with a column per lane held in registers (no block-wide barriers), then the
+  //    blocks below the diagonal by distance d = i - j: X_ij = -X_ii sum_{k=j}^{i-1} (diag(beta) M)_ik X_kj
+  {
+    for (int e = tid; e < kC * kC; e += blockDim.x) sI[(e / kC) * kPM + e % kC] = 0.f;
+    __syncthreads();
+    if (warp < 4 && lane < kSubR) {
+      const int o = warp * kSubR, jc = lane;
+      float x[kSubR];
+#pragma unroll
+      for (int t = 0; t < kSubR; ++t) x[t] = t == jc ? 1.f : 0.f;
+#pragma unroll
+      for (int t = 1; t < kSubR; ++t) {
+        float acc = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < t; ++s2) acc += sM[(o + t) * kPM + o + s2] * x[s2];
+        if (t > jc) x[t] = -sB[o + t] * acc;
+      }
+#pragma unroll
+      for (int t = 0; t < kSubR; ++t) sI[(o + t) * kPM + o + jc] = x[t];
+    }
+    __syncthreads();
+    for (int d = 1; d < kC / kSubR; ++d) {
+      const int nblk = kC / kSubR - d;
+      for (int e = tid; e < nblk * kSubR * kSubR; e += blockDim.x) {
+        const int jb = e / (kSubR * kSubR), rr = (e / kSubR) % kSubR, col = e % kSubR, ib = jb + d;
+        float w = 0.f;
+        for (int kb = jb; kb < ib; ++kb)
+#pragma unroll 4
+          for (int m = 0; m < kSubR; ++m)
+            w += sM[(kSubR * ib + rr) * kPM + kSubR * kb + m] * sI[(kSubR * kb + m) * kPM + kSubR * jb + col];
+        sW[e] = w * sB[kSubR * ib + rr];
+      }
+      __syncthreads();
+      for (int e = tid; e < nblk * kSubR * kSubR; e += blockDim.x) {
+        const int jb = e / (kSubR * kSubR), rr = (e / kSubR) % kSubR, col = e % kSubR, ib = jb + d;
+        float x = 0.f;
+#pragma unroll 4
+        for (int m = 0; m < kSubR; ++m)
+          x += sI[(kSubR * ib + rr) * kPM + kSubR * ib + m] * sW[jb * kSubR * kSubR + m * kSubR + col];
+        sI[(kSubR * ib + rr) * kPM + kSubR * jb + col] = -x;
+      }
+      __syncthreads();
+    }
+  }
+  // 6. T = X diag(beta) and P into the record
+  for (int e = tid; e < kC * kC; e += blockDim.x) {
+    const int t = e / kC, s = e % kC;
+    oT[e] = sI[t * kPM + s] * sB[s];
+    oP[e] = sP[t * kPM + s];
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// scan: grid (H, DH/32, B), 256 threads (8 warps)
+// ---------------------------------------------------------------------------------------------------------------
 // A fragment (16 x 8) of a row-major matrix: element (m, k) at p[m * ld + k]
 __device__ __forceinline__ void frag_a_row(const float* p, int ld, uint32_t (&f)[4]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
@@ -544,9 +565,7 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
 
 template <int DH>
 cudaError_t launch_chunk(const KdaArgs& a, cudaStream_t st) {
-  constexpr int P1 = DH + 1;
-  const size_t smem_prep =
-      sizeof(float) * ((size_t)4 * kC * P1 + 2 * kSubR * P1 + 3 * kC * (kC + 1) + kC);
+  const size_t smem_prep = sizeof(float) * (size_t)prep_smem_floats();
   const size_t smem_scan = sizeof(float) * ((size_t)2 * ScanBuf<DH>::FLOATS + 32 * (DH + 4) + 2 * kC * 36);
   cudaError_t e = cudaFuncSetAttribute(kda_prep_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem_prep);

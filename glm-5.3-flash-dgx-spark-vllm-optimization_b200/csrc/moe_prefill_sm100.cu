@@ -147,6 +147,10 @@ __device__ __forceinline__ void frags(uint32_t cur, uint32_t prev, uint32_t (&b)
   b[3] = mcg_sum2(mcg_mask_(t4 * C + s20 * Cn), mcg_mask_(cur * C + s16 * Cn));
 }
 
+__device__ __forceinline__ void sts_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
 // byte offset of element (row, k) (k even) in a 128-row x 64-k f16 tile, K-major, 128-byte swizzle
 __device__ __forceinline__ uint32_t sw_off(int row, int k) {
   return (uint32_t)(row * 128 + ((((k * 2) >> 4) ^ (row & 7)) << 4) + ((k * 2) & 15));
@@ -224,50 +228,67 @@ __global__ void __launch_bounds__(Cfg<GU>::kThreads, Cfg<GU>::kMinBlocks) moe_pr
 
   if (warp < kDecWarps) {
     // ------------------------------------------------------------------ decoders, then epilogue
-    const uint32_t* trw[2] = {reinterpret_cast<const uint32_t*>(p.tr0), reinterpret_cast<const uint32_t*>(p.tr1)};
     constexpr int TILES = NM * 4 * 8;                   // (matrix, k-tile, n-tile) of one stage
     constexpr int PER = TILES / kDecWarps;
     const int src = (lane + 31) & 31;
     const int g = lane >> 2, q = lane & 3;
+    // The warp's PER tiles of a stage, tile i = (matrix idx / 32, k-tile (idx / 8) % 4, n-tile idx % 8) with
+    // idx = warp + i * kDecWarps, are the same in every stage: their trellis word addresses advance by one stage
+    // of k-tiles (4 * NT tiles of 32 words) and their shared-memory offsets repeat.  Both are formed once here, so
+    // the decode loop is the trellis arithmetic, one load and four stores per tile.
+    // the expert's words of both matrices; tile i's word within them (u32: an expert holds KT * NT * 32 words)
+    const uint32_t* wb0 = reinterpret_cast<const uint32_t*>(p.tr0) + (int64_t)e * KT * NT * 32;
+    const uint32_t* wb1 = reinterpret_cast<const uint32_t*>(p.tr1) + (int64_t)e * KT * NT * 32;
+    uint32_t wo[PER];                                   // word offset of tile i in stage 0
+    uint32_t so[PER];                                   // byte offset of (row n0, k0) of tile i in a stage
+    const uint32_t kstep = 4u * NT * 32u;               // words per stage of k-tiles
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int idx = warp + i * kDecWarps;
+      const int m = idx / 32, kt = (idx / 8) & 3, nt = idx & 7;
+      wo[i] = (uint32_t)((kt * NT + nb * 8 + nt) * 32 + lane);
+      so[i] = (uint32_t)(m * A_BYTES) + sw_off(nt * 16 + g, kt * 16 + 2 * q);
+    }
+    const uint32_t sbase = su32(sm);
     int it = 0;                                         // global stage counter (continues across passes)
     for (int pass = 0; pass < passes; ++pass) {
       const int rows = min(kNmax, np - pass * kNmax);
-      uint32_t wcur[PER];
-      auto load = [&](int kb, uint32_t (&w)[PER]) {
+      uint32_t koff = 0;                                // every pass decodes the same K range from stage 0
+      auto load = [&](uint32_t (&w)[PER]) {            // the stage at koff, then advance koff one stage
 #pragma unroll
         for (int i = 0; i < PER; ++i) {
-          const int idx = warp + i * kDecWarps;
-          const int m = idx / 32, kt = (idx / 8) & 3, nt = idx & 7;
-          const int64_t tile = ((int64_t)e * KT + kb * 4 + kt) * NT + nb * 8 + nt;
-          w[i] = ldg_nc_u32(trw[m] + tile * 32 + lane);
+          // matrix of tile i: (warp + i * kDecWarps) / 32 = i * kDecWarps / 32, a constant (warp < kDecWarps <= 16)
+          constexpr int kDW = kDecWarps;
+          const bool m1 = NM > 1 && (i * kDW) / 32 > 0;
+          w[i] = ldg_nc_u32((m1 ? wb1 : wb0) + (wo[i] + koff));
         }
+        koff += kstep;
       };
-      uint32_t wnext[PER];                              // trellis words two stages ahead of the decode
-      load(0, wcur);
-      if (nkb > 1) load(1, wnext);
+      uint32_t wcur[PER], wnext[PER];                   // trellis words of this stage and the next
+      load(wcur);
+      if (nkb > 1) load(wnext);
       for (int kb = 0; kb < nkb; ++kb, ++it) {
         const int s = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        uint32_t wnext2[PER];
-        if (kb + 2 < nkb) load(kb + 2, wnext2);
+        uint32_t wnext2[PER];                           // two stages ahead of the decode
+        if (kb + 2 < nkb) load(wnext2);
         if (it >= STAGES) {
           int okw = 0;
           if (lane == 0) okw = bar_wait(&empty[s], ph ^ 1, &fail, p.err, 11) ? 1 : 0;
           if (!__shfl_sync(0xffffffffu, okw, 0)) break;
         }
-        uint8_t* abase = sm + s * STAGE;
+        const uint32_t ab = sbase + (uint32_t)(s * STAGE);
 #pragma unroll
         for (int i = 0; i < PER; ++i) {
-          const int idx = warp + i * kDecWarps;
-          const int m = idx / 32, kt = (idx / 8) & 3, nt = idx & 7;
           uint32_t b[4];
           frags(wcur[i], __shfl_sync(0xffffffffu, wcur[i], src), b);
-          uint8_t* at = abase + m * A_BYTES;
-          const int n0 = nt * 16 + g, k0 = kt * 16 + 2 * q;
-          *reinterpret_cast<uint32_t*>(at + sw_off(n0, k0)) = b[0];
-          *reinterpret_cast<uint32_t*>(at + sw_off(n0, k0 + 8)) = b[1];
-          *reinterpret_cast<uint32_t*>(at + sw_off(n0 + 8, k0)) = b[2];
-          *reinterpret_cast<uint32_t*>(at + sw_off(n0 + 8, k0 + 8)) = b[3];
+          // (n0, k0), (n0, k0 + 8), (n0 + 8, k0), (n0 + 8, k0 + 8): k0 + 8 flips the 16-byte chunk's low bit
+          // (the chunk index 2 * kt is even before the swizzle), row n0 + 8 is 1024 bytes further
+          const uint32_t a0 = ab + so[i], a1 = ab + (so[i] ^ 16u);
+          sts_u32(a0, b[0]);
+          sts_u32(a1, b[1]);
+          sts_u32(a0 + 1024u, b[2]);
+          sts_u32(a1 + 1024u, b[3]);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
