@@ -260,6 +260,30 @@ __device__ __forceinline__ void fwht128_warp(float (&v)[4]) {
   for (int i = 0; i < 4; ++i) v[i] *= s;
 }
 
+// The same transform with each cross-lane butterfly as one FFMA (bit-identical results, fewer instructions, one
+// more live register per stage): for kernels with registers to spare (the prefill MoE epilogue); the decode
+// kernels, capped at 64 registers, keep the predicated form above.
+__device__ __forceinline__ void fwht128_warp_fma(float (&v)[4]) {
+  const int lane = threadIdx.x & 31;
+  // in-lane stages (h = 1, 2)
+  float a0 = v[0] + v[1], a1 = v[0] - v[1], a2 = v[2] + v[3], a3 = v[2] - v[3];
+  v[0] = a0 + a2; v[2] = a0 - a2; v[1] = a1 + a3; v[3] = a1 - a3;
+  // cross-lane stages (h = 4 .. 64 -> lane bit 1 .. 16)
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    // lower lane: v + p, upper lane: p - v, as one FFMA p + (+-1) v (the product is exact: same single rounding)
+    const float sg = (lane & m) ? -1.f : 1.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float p = __shfl_xor_sync(0xffffffffu, v[i], m);
+      v[i] = fmaf(sg, v[i], p);
+    }
+  }
+  const float s = 0.08838834764831845f;   // 1/sqrt(128)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] *= s;
+}
+
 // exclusive scan of an int over the block (blockDim multiple of 32, <= 1024); returns (prefix, total)
 __device__ __forceinline__ int2 block_scan(int v, int* wsum) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;

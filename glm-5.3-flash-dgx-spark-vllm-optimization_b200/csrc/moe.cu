@@ -278,6 +278,75 @@ __global__ void __launch_bounds__(128) exl3_rot_in_kernel(Exl3Args a) {
   }
 }
 
+// Prefill layout (plain f16 rows), 16-byte accesses: a half-warp owns one 128-column block, a lane 8 consecutive
+// columns; grid (pairs, K / 2048), 256 threads.  The butterflies are those of fwht128_warp in the same stage order
+// (h = 1, 2, 4 inside the lane, then lane bits 0..3 for h = 8 .. 64), each stage's (a + b, a - b) computed with the
+// same single roundings, so the output is bit-identical to exl3_rot_in_kernel's.
+__device__ __forceinline__ void fwht128_half(float (&v)[8]) {
+#pragma unroll
+  for (int h = 1; h < 8; h <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (i & h) continue;
+      const float x0 = v[i], x1 = v[i + h];
+      v[i] = x0 + x1;
+      v[i + h] = x0 - x1;
+    }
+  }
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int m = 1; m < 16; m <<= 1) {
+    const float sg = (lane & m) ? -1.f : 1.f;         // lower lane: v + p, upper lane: p - v
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float pv = __shfl_xor_sync(0xffffffffu, v[i], m);
+      v[i] = fmaf(sg, v[i], pv);
+    }
+  }
+  const float s = 0.08838834764831845f;   // 1/sqrt(128)
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] *= s;
+}
+
+__global__ void __launch_bounds__(256) exl3_rot_in_wide_kernel(Exl3Args a) {
+  pdl_wait();                          // pairs from the routing kernel
+  pdl_trigger();
+  const int blk = blockIdx.y * 16 + (threadIdx.x >> 4);
+  if (blk * 128 >= a.K) return;        // whole warps: K is a multiple of 256
+  const int c0 = blk * 128 + (threadIdx.x & 15) * 8;
+  const int np = a.pair_count ? min(*a.pair_count, a.pairs) : a.pairs;
+  for (int p = blockIdx.x; p < np; p += gridDim.x) {
+    const int r = a.pair_token[p], e = a.pair_expert[p];
+    if (!g53_in_bounds(r, a.n_rows, 7) || !g53_in_bounds(e, a.n_experts, 6)) continue;   // CTA-uniform
+    const uint4 xw = *reinterpret_cast<const uint4*>(a.x + (int64_t)r * a.ldx + c0);
+    const uint4 gw = *reinterpret_cast<const uint4*>(a.suh_g + (int64_t)e * a.K + c0);
+    const uint4 uw = *reinterpret_cast<const uint4*>(a.suh_u + (int64_t)e * a.K + c0);
+    const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xw);
+    const __half2* g2 = reinterpret_cast<const __half2*>(&gw);
+    const __half2* u2 = reinterpret_cast<const __half2*>(&uw);
+    float g[8], u[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 xf = __bfloat1622float2(x2[i]);
+      const float2 gf = __half22float2(g2[i]), uf = __half22float2(u2[i]);
+      g[2 * i] = xf.x * gf.x; g[2 * i + 1] = xf.y * gf.y;
+      u[2 * i] = xf.x * uf.x; u[2 * i + 1] = xf.y * uf.y;
+    }
+    fwht128_half(g);
+    fwht128_half(u);
+    uint4 og, ou;
+    __half2* og2 = reinterpret_cast<__half2*>(&og);
+    __half2* ou2 = reinterpret_cast<__half2*>(&ou);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      og2[i] = __floats2half2_rn(g[2 * i], g[2 * i + 1]);
+      ou2[i] = __floats2half2_rn(u[2 * i], u[2 * i + 1]);
+    }
+    *reinterpret_cast<uint4*>(a.xh_g + (int64_t)p * a.K + c0) = og;
+    *reinterpret_cast<uint4*>(a.xh_u + (int64_t)p * a.K + c0) = ou;
+  }
+}
+
 // accumulator (16 features x 8 tokens) of one warp's n-tile -> z[token][feature]
 __device__ __forceinline__ void acc_to_smem(const float (&c)[4], int warp, float (*z)[132]) {
   const int lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
@@ -620,8 +689,13 @@ cudaError_t g53_moe_route(const RouteArgs& a, cudaStream_t st) {
 
 cudaError_t g53_exl3_rot_in(const Exl3Args& a, cudaStream_t st) {
   // device-side pair count (expert parallelism): a bounded grid strides over the rows that arrived
-  dim3 grid(a.pair_count ? std::min(a.pairs, 1184) : a.pairs, (a.K / 128 + 3) / 4);
-  return g53_launch_pdl(exl3_rot_in_kernel, grid, dim3(128), 0, st, 1, a);
+  const int gx = a.pair_count ? std::min(a.pairs, 1184) : a.pairs;
+  const bool wide = !a.decode_layout && a.K % 256 == 0 && a.ldx % 8 == 0 &&
+                    ((reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.suh_g) |
+                      reinterpret_cast<uintptr_t>(a.suh_u) | reinterpret_cast<uintptr_t>(a.xh_g) |
+                      reinterpret_cast<uintptr_t>(a.xh_u)) & 15) == 0;
+  if (wide) return g53_launch_pdl(exl3_rot_in_wide_kernel, dim3(gx, (a.K + 2047) / 2048), dim3(256), 0, st, 1, a);
+  return g53_launch_pdl(exl3_rot_in_kernel, dim3(gx, (a.K / 128 + 3) / 4), dim3(128), 0, st, 1, a);
 }
 
 // K split over a cluster of KSPL CTAs (more, smaller CTAs: the grid of a decode window is a couple of waves)

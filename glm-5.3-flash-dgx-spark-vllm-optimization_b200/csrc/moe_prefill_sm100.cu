@@ -331,8 +331,8 @@ __global__ void __launch_bounds__(Cfg<GU>::kThreads, Cfg<GU>::kMinBlocks) moe_pr
             const float4 u4 = *reinterpret_cast<const float4*>(&zb[(32 + j) * ZS + lane * 4]);
             vg[0] = g4.x; vg[1] = g4.y; vg[2] = g4.z; vg[3] = g4.w;
             vu[0] = u4.x; vu[1] = u4.y; vu[2] = u4.z; vu[3] = u4.w;
-            fwht128_warp(vg);
-            fwht128_warp(vu);
+            fwht128_warp_fma(vg);
+            fwht128_warp_fma(vu);
             float act[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(Cfg<GU>::kThreads, Cfg<GU>::kMinBlocks) moe_pr
               uv = fminf(fmaxf(uv, -p.limit), p.limit);
               act[i] = siluf_(gv) * uv * __half2float(p.suh_next[(int64_t)e * p.N + col + i]);
             }
-            fwht128_warp(act);
+            fwht128_warp_fma(act);
             __half2* o = reinterpret_cast<__half2*>(reinterpret_cast<__half*>(p.out) + (int64_t)pr * p.N + col);
             o[0] = __floats2half2_rn(act[0], act[1]);
             o[1] = __floats2half2_rn(act[2], act[3]);
@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(Cfg<GU>::kThreads, Cfg<GU>::kMinBlocks) moe_pr
             float v[4];
             const float4 v4 = *reinterpret_cast<const float4*>(&zb[j * ZS + lane * 4]);
             v[0] = v4.x; v[1] = v4.y; v[2] = v4.z; v[3] = v4.w;
-            fwht128_warp(v);
+            fwht128_warp_fma(v);
             const float w = p.pair_w[pr];
             float4 o;
             o.x = v[0] * __half2float(p.svh0[(int64_t)e * p.N + col + 0]) * w;

@@ -482,3 +482,35 @@ def test_dconv_matches_eager_chain(C, T, blk):
         p = p * (pos >= k)[:, None].to(torch.bfloat16)
         ref = ref + p
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("K", [256, 4096])
+def test_rot_in_wide_matches_narrow_bitexact(C, K):
+    """The 16-byte rotated-input kernel of the prefill layout (a half-warp per 128-column block) against the
+    warp-per-block kernel (taken for an x whose row stride is not a multiple of 8): bit-identical f16 outputs,
+    including pairs that repeat a token and experts out of order."""
+    g = torch.Generator(device=DEV).manual_seed(7)
+    T, E, P = 37, 5, 150
+    x_wide = torch.randn(T, K + 4, device=DEV, generator=g).to(torch.bfloat16)
+    x_narrow = x_wide[:, :K]                      # row stride K + 4: the narrow kernel
+    x_dense = x_narrow.contiguous()               # row stride K: the wide kernel
+    suh_g = (torch.randn(E, K, device=DEV, generator=g) * 0.5).to(torch.float16)
+    suh_u = (torch.randn(E, K, device=DEV, generator=g) * 0.5).to(torch.float16)
+    pt = torch.randint(0, T, (P,), device=DEV, generator=g).to(torch.int32)
+    pe = torch.randint(0, E, (P,), device=DEV, generator=g).to(torch.int32)
+    outs = []
+    for x in (x_narrow, x_dense):
+        xg = torch.full((P, K), float("nan"), device=DEV, dtype=torch.float16)
+        xu = torch.full((P, K), float("nan"), device=DEV, dtype=torch.float16)
+        C.exl3_rot_in(x, suh_g, suh_u, pt, pe, xg, xu)
+        outs.append((xg, xu))
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0][0].view(torch.int16), outs[1][0].view(torch.int16))
+    assert torch.equal(outs[0][1].view(torch.int16), outs[1][1].view(torch.int16))
+    # and the rotation itself: H128 (x * suh) per 128-column block, fp32 reference
+    i = torch.arange(128)
+    parity = torch.tensor([bin(v).count("1") & 1 for v in (i[:, None] & i[None, :]).flatten().tolist()])
+    H = (1 - 2 * parity.view(128, 128)).float().to(DEV) / 128 ** 0.5    # Sylvester order: H[i, j] = (-1)^|i & j|
+    xs = (x_dense.float()[pt.long()] * suh_g.float()[pe.long()]).view(P, K // 128, 128)
+    ref = (xs @ H.T).view(P, K)
+    torch.testing.assert_close(outs[1][0].float(), ref, rtol=2e-3, atol=2e-3)
