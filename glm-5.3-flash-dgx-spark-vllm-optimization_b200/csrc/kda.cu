@@ -78,22 +78,39 @@ __global__ void __launch_bounds__(256) kda_conv_vec_kernel(KdaArgs a) {
     const int t = t0 - (T - 1) + i;
     load8(t < 0 ? win + (int64_t)(T - 1 + t) * C + c : a.proj + (int64_t)(base + t) * a.ldp + c, hist[i]);
   }
-  for (int t = t0; t < t1; ++t) {
-    load8(a.proj + (int64_t)(base + t) * a.ldp + c, hist[T - 1]);
-    uint32_t o[4];
+  // rows in groups of kGrp: the group's loads are issued together (read-only path) before any of its rows is
+  // convolved, so a thread keeps kGrp 16-byte loads in flight instead of one
+  constexpr int kGrp = 4;
+  for (int tg = t0; tg < t1; tg += kGrp) {
+    uint4 raw[kGrp];
 #pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      float s0 = 0.f, s1 = 0.f;
+    for (int j = 0; j < kGrp; ++j)
+      raw[j] = tg + j < t1 ? ldg_nc_v4(a.proj + (int64_t)(base + tg + j) * a.ldp + c) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-      for (int i = 0; i < T; ++i) { s0 += w[i][e] * hist[i][e]; s1 += w[i][e + 1] * hist[i][e + 1]; }
-      __nv_bfloat162 p2 = __floats2bfloat162_rn(siluf_(s0), siluf_(s1));
-      o[e >> 1] = *reinterpret_cast<uint32_t*>(&p2);
+    for (int j = 0; j < kGrp; ++j) {
+      const int t = tg + j;
+      if (t >= t1) break;
+      const uint32_t ws[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        hist[T - 1][2 * e] = __uint_as_float(ws[e] << 16);
+        hist[T - 1][2 * e + 1] = __uint_as_float(ws[e] & 0xffff0000u);
+      }
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < T; ++i) { s0 += w[i][e] * hist[i][e]; s1 += w[i][e + 1] * hist[i][e + 1]; }
+        __nv_bfloat162 p2 = __floats2bfloat162_rn(siluf_(s0), siluf_(s1));
+        o[e >> 1] = *reinterpret_cast<uint32_t*>(&p2);
+      }
+      *reinterpret_cast<uint4*>(a.qkv + (int64_t)(base + t) * C + c) = make_uint4(o[0], o[1], o[2], o[3]);
+#pragma unroll
+      for (int i = 0; i < T - 1; ++i)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) hist[i][e] = hist[i + 1][e];
     }
-    *reinterpret_cast<uint4*>(a.qkv + (int64_t)(base + t) * C + c) = make_uint4(o[0], o[1], o[2], o[3]);
-#pragma unroll
-    for (int i = 0; i < T - 1; ++i)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) hist[i][e] = hist[i + 1][e];
   }
 }
 
