@@ -965,9 +965,19 @@ void dsa_select(const Tensor& iproj, const Tensor& qi, const Tensor& ln_w, const
   a.ik_cache = nullptr;
   a.ig_cache = nullptr;
   a.err = P<int>(err_word(logits));
-  // tcgen05 logits for prefill-sized launches where the head count fits the kernel (IH | 32, ID = 128); decode
-  // windows (a few rows: one query tile, pools split over CTAs) are faster on the CUDA-core kernel
-  if (tc_dsa_enabled() && a.R >= 64 && g53_dsa_logits_tc(a, stream()) == cudaSuccess) {
+  // tcgen05 logits for prefill-sized launches where the head count fits the kernel (IH | 32, ID = 128).  Decode
+  // windows (a few rows: one query tile, pools split over CTAs) launch both kernels: the CUDA-core kernel is
+  // faster up to kDsaTcMinPools complete pools (measured at 8 rows: 37 vs 47 us at 8192 pools), the tcgen05 kernel
+  // above (76 vs 108 us at 32768 pools, 94 vs 403 us at 131072); the device picks from the rows' positions
+  constexpr int kDsaTcMinPools = 16384;
+  const bool tc_ok = tc_dsa_enabled() && a.ID == 128 && (a.IH == 4 || a.IH == 8 || a.IH == 16 || a.IH == 32);
+  if (tc_ok && a.R >= 64) {
+    check(g53_dsa_logits_tc(a, stream()), "dsa_logits_tc");
+  } else if (tc_ok && a.max_pools > kDsaTcMinPools) {
+    a.tc_min_pools = kDsaTcMinPools;
+    check(g53_dsa_logits(a, stream()), "dsa_logits");
+    check(g53_dsa_logits_tc(a, stream()), "dsa_logits_tc");
+    a.tc_min_pools = 0;
   } else {
     check(g53_dsa_logits(a, stream()), "dsa_logits");
   }

@@ -122,6 +122,7 @@ __global__ void dsa_pool_kernel(DsaArgs a) {
 constexpr int kMaxIH = 64;
 
 __global__ void __launch_bounds__(256) dsa_logits_kernel(DsaArgs a) {
+  if (a.tc_min_pools > 0 && dsa_long_rows(a)) return;     // the tcgen05 kernel of this launch pair takes it
   const int r = blockIdx.x;
   const int pos = a.positions[r];
   const int c = pos / a.kpool;
@@ -175,14 +176,140 @@ __device__ __forceinline__ uint32_t order_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Rows with more than kSelSplit complete pools are selected by a cluster of kSelNC CTAs (one pool slice each: the
+// radix histograms are summed over the cluster through distributed shared memory, the slices' counts give each
+// CTA its output offset); shorter rows by rank 0 alone.  Both paths select the same pools in the same order.
+constexpr int kSelNC = 8;
+constexpr int kSelSplit = 16384;         // measured crossover (8 rows: single CTA 24 us vs cluster 32 us at 8192 pools)
+
+__device__ __forceinline__ void cl_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ const int* cl_map(const int* p, int rank) {
+  uint64_t r;
+  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(p), "r"(rank));
+  return reinterpret_cast<const int*>(r);
+}
+
+// the bin decision of one radix pass from the (summed) 256-bin histogram: lane l holds bins 255 - 8l .. 248 - 8l,
+// an exclusive prefix over the lanes gives each lane the count of the bins above its own, and the one lane whose
+// range crosses rem (or lane 31) walks its 8 bins; writes the new prefix and remainder
+__device__ __forceinline__ void sel_decide(const int (&cnt)[8], uint32_t prefix, int shift, int rem,
+                                           uint32_t* s_prefix, int* s_rem) {
+  const int lane = threadIdx.x & 31;
+  int sum = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sum += cnt[i];
+  int incl = sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  int acc = incl - sum;
+  if (acc < rem && (acc + sum >= rem || lane == 31)) {
+    int b = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int bin = 255 - 8 * lane - i;
+      if (bin == 0) break;                  // bin 0 is taken without a check
+      if (acc + cnt[i] >= rem) { b = bin; break; }
+      acc += cnt[i];
+    }
+    *s_prefix = prefix | ((uint32_t)b << shift);
+    *s_rem = rem - acc;
+  }
+}
+
 __global__ void __launch_bounds__(1024) dsa_select_kernel(DsaArgs a) {
-  const int r = blockIdx.x;
+  pdl_wait();                               // the logits of the previous kernel
+  const int r = blockIdx.x, rank = blockIdx.z, nc = gridDim.z;
   const int tid = threadIdx.x, bd = blockDim.x;
   const int pos = a.positions[r];
   const int kp = a.kpool, P = a.topk_pools;
   const int c = pos / kp;
   const int* bt = a.block_table + (int64_t)a.row_seq[r] * a.bt_ld;
   int* out = a.sel + (int64_t)r * a.max_sel;
+  if (nc > 1 && c > kSelSplit && c > P - 1) {
+    // ---- cluster path: rank k owns pools [j0, j1)
+    __shared__ int hist2[2][256];
+    __shared__ uint32_t c_prefix;
+    __shared__ int c_rem, c_cnt[2], c_wsum[32];
+    const int j0 = (int)((int64_t)c * rank / nc), j1 = (int)((int64_t)c * (rank + 1) / nc);
+    const float* lg = a.logits + (int64_t)r * a.max_pools;
+    const int K = P - 1;
+    uint32_t prefix = 0u, mask = 0u;
+    int rem = K;
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      int* h = hist2[pass & 1];
+      for (int i = tid; i < 256; i += bd) h[i] = 0;
+      __syncthreads();
+      for (int j = j0 + tid; j < j1; j += bd) {
+        const uint32_t u = order_key(lg[j]);
+        if ((u & mask) == prefix) atomicAdd(&h[(u >> shift) & 255u], 1);
+      }
+      cl_sync();                            // every slice's histogram of this pass is complete
+      if (tid < 32) {
+        int cnt[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) cnt[i] = 0;
+        for (int k = 0; k < nc; ++k) {      // fixed rank order: every CTA forms the same sums
+          const int* hk = cl_map(h, k);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) cnt[i] += hk[255 - 8 * tid - i];
+        }
+        sel_decide(cnt, prefix, shift, rem, &c_prefix, &c_rem);
+      }
+      __syncthreads();
+      prefix = c_prefix;
+      rem = c_rem;
+      mask |= 255u << shift;
+    }
+    // counts of this slice: keys above the threshold and keys equal to it
+    if (tid < 2) c_cnt[tid] = 0;
+    __syncthreads();
+    int gt_l = 0, eq_l = 0;
+    for (int j = j0 + tid; j < j1; j += bd) {
+      const uint32_t u = order_key(lg[j]);
+      gt_l += u > prefix;
+      eq_l += u == prefix;
+    }
+    gt_l = warp_sum_int(gt_l);
+    eq_l = warp_sum_int(eq_l);
+    if ((tid & 31) == 0) { atomicAdd(&c_cnt[0], gt_l); atomicAdd(&c_cnt[1], eq_l); }
+    cl_sync();
+    // output offset of this slice: the pools selected by the lower ranks (ties in index order, first rem taken)
+    int base_sel = 0, base_eq = 0;
+    for (int k = 0; k < rank; ++k) {
+      const int* ck = cl_map(c_cnt, k);
+      const int gk = ck[0], ek = ck[1];
+      base_sel += gk + max(0, min(ek, rem - base_eq));
+      base_eq += ek;
+    }
+    cl_sync();                              // no CTA leaves while another reads its counts
+    for (int jb = j0; jb < j1; jb += bd) {
+      const int j = jb + tid;
+      const uint32_t u = j < j1 ? order_key(lg[j]) : 0u;
+      const int eq = (j < j1) && (u == prefix);
+      const int gt = (j < j1) && (u > prefix);
+      const int2 se = block_scan(eq, c_wsum);
+      const int selected = gt || (eq && (base_eq + se.x) < rem);
+      const int2 ss = block_scan(selected, c_wsum);
+      if (selected) {
+        const int o = (base_sel + ss.x) * kp;
+        for (int i = 0; i < kp; ++i) out[o + i] = slot_of(bt, a.block_size, j * kp + i);
+      }
+      base_eq += se.y;
+      base_sel += ss.y;
+    }
+    if (rank == 0) {
+      for (int p = c * kp + tid; p <= pos; p += bd) out[K * kp + (p - c * kp)] = slot_of(bt, a.block_size, p);
+      if (tid == 0) a.sel_count[r] = K * kp + (pos - c * kp + 1);
+    }
+    return;
+  }
+  if (rank != 0) return;                    // short rows: rank 0 alone
   if (c <= P - 1) {
     for (int p = tid; p <= pos; p += bd) out[p] = slot_of(bt, a.block_size, p);
     if (tid == 0) a.sel_count[r] = pos + 1;
@@ -206,32 +333,11 @@ __global__ void __launch_bounds__(1024) dsa_select_kernel(DsaArgs a) {
     }
     __syncthreads();
     if (tid < 32) {
-      // the highest bin b whose count from the top (bins 255..b) reaches rem (bin 0 when bins 255..1 do not):
-      // lane l holds bins 255 - 8l .. 248 - 8l, an exclusive prefix over the lanes gives each lane the count of
-      // the bins above its own, and the one lane whose range crosses rem (or lane 31) walks its 8 bins
-      const int lane = tid;
-      int cnt[8], sum = 0;
+      // the highest bin b whose count from the top (bins 255..b) reaches rem (bin 0 when bins 255..1 do not)
+      int cnt[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) { cnt[i] = hist[255 - 8 * lane - i]; sum += cnt[i]; }
-      int incl = sum;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      int acc = incl - sum;
-      if (acc < rem && (acc + sum >= rem || lane == 31)) {
-        int b = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int bin = 255 - 8 * lane - i;
-          if (bin == 0) break;                  // bin 0 is taken without a check
-          if (acc + cnt[i] >= rem) { b = bin; break; }
-          acc += cnt[i];
-        }
-        s_prefix = prefix | ((uint32_t)b << shift);
-        s_rem = rem - acc;
-      }
+      for (int i = 0; i < 8; ++i) cnt[i] = hist[255 - 8 * tid - i];
+      sel_decide(cnt, prefix, shift, rem, &s_prefix, &s_rem);
     }
     __syncthreads();
     prefix = s_prefix;
@@ -282,7 +388,7 @@ cudaError_t g53_dsa_logits(const DsaArgs& a, cudaStream_t st) {
 }
 
 cudaError_t g53_dsa_select(const DsaArgs& a, cudaStream_t st) {
-  dsa_select_kernel<<<a.R, 1024, 0, st>>>(a);
-  G53_CHECK_LAUNCH();
-  return cudaSuccess;
+  // clusters of kSelNC CTAs when the logits buffer can hold rows long enough for the split path
+  const int nc = a.max_pools > kSelSplit ? kSelNC : 1;
+  return g53_launch_pdl(dsa_select_kernel, dim3(a.R, 1, nc), dim3(1024), 0, st, nc, a);
 }

@@ -51,6 +51,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1) dsa_logits_tc_kernel(DsaArgs a)
   __shared__ float r_w[kTN];                         // head weights, column order (row, head)
 
   constexpr int QR = kTN / IH;
+  if (a.tc_min_pools > 0 && !dsa_long_rows(a)) return;    // short rows: the CUDA-core kernel of this pair runs
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int r0 = blockIdx.x * QR;
   const int split = blockIdx.y, nsplit = gridDim.y;

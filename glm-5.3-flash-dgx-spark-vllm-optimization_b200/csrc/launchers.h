@@ -347,7 +347,21 @@ struct DsaArgs {
   int* err;                      // device error word (bounded waits of the tensor-core logits kernel)
   int64_t n_pools;               // bounds-checked build: pool slots of the index cache (0: unknown)
   int64_t n_owners;              // bounds-checked build: ring owners (state slots) of the tail rings (0: unknown)
+  // decode windows launch both logits kernels; each runs only on its side of this pool count (the longest row of
+  // the launch decides): CUDA cores up to it, tcgen05 above it.  0: the kernel runs unconditionally.
+  int tc_min_pools;
 };
+#ifdef __CUDACC__
+// true when the longest row of the launch has more complete pools than a.tc_min_pools (every warp forms the same
+// answer from the same positions)
+__device__ __forceinline__ bool dsa_long_rows(const DsaArgs& a) {
+  int mx = 0;
+  for (int r = threadIdx.x & 31; r < a.R; r += 32) mx = max(mx, a.positions[r] / a.kpool);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  return mx > a.tc_min_pools;
+}
+#endif
 cudaError_t g53_dsa_update(const DsaArgs& a, cudaStream_t st);   // index keys, gate scores, completed pools
 cudaError_t g53_dsa_logits(const DsaArgs& a, cudaStream_t st);  // pool logits of every row (CUDA cores)
 cudaError_t g53_dsa_logits_tc(const DsaArgs& a, cudaStream_t st);   // same on tcgen05 (dsa_tc.cu)

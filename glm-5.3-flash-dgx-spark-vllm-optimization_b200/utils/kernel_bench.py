@@ -437,13 +437,52 @@ def bench_hc(args, T: Timer):
                   "GBps": (R * S * D * 2 * 2 + R * D * 4 + NM * S * D * 2 + R * D * 2 * 2) / ms / 1e6})
 
 
+def bench_dsa(args, T: Timer):
+    """DSA indexer at decode: pool logits (CUDA-core kernel, the decode path) and the radix top-k selection for R
+    query rows at the end of a `--context`-token sequence (full config: 32 index heads x 128, pools of 4 tokens,
+    top 512 pools); the e4m3 pool cache is random, one page table of 64-token pages."""
+    from glm53.ops import kernels as K
+    C = K.C()
+    dev = "cuda"
+    IH, ID, kpool, bs, topk_pools = 32, 128, 4, 64, 2048 // 4
+    g = torch.Generator(device=dev).manual_seed(0)
+    for ctx in args.context:
+        for R in args.rows:
+            pages = (ctx + bs - 1) // bs
+            npools = pages * bs // kpool
+            raw = torch.randint(0, 256, (npools, ID), generator=g, device=dev, dtype=torch.int32)
+            raw[(raw == 0x7F) | (raw == 0xFF)] = 0
+            pool_cache = raw.to(torch.uint8)
+            pool_scale = torch.ones(npools, device=dev)
+            bt = torch.randperm(pages, device=dev, generator=g).to(torch.int32).view(1, pages)
+            iproj = torch.randn(R, ID + IH + ID, device=dev, generator=g)
+            qi = torch.randn(R, IH * ID, device=dev, generator=g).to(torch.bfloat16)
+            positions = torch.arange(ctx - R, ctx, device=dev, dtype=torch.int32)
+            row_seq = torch.zeros(R, device=dev, dtype=torch.int32)
+            ln_w = torch.ones(ID, device=dev)
+            logits = torch.empty(R, npools, device=dev)
+            sel = torch.empty(R, topk_pools * kpool, device=dev, dtype=torch.int32)
+            cnt = torch.empty(R, device=dev, dtype=torch.int32)
+            ms_l = T(lambda: C.dsa_logits(iproj, qi, ln_w, pool_cache, pool_scale, positions, bt, row_seq, bs, IH,
+                                          kpool, logits, False))
+            ms_t = T(lambda: C.dsa_logits(iproj, qi, ln_w, pool_cache, pool_scale, positions, bt, row_seq, bs, IH,
+                                          kpool, logits, True))
+            ms_s = T(lambda: C.dsa_select(iproj, qi, ln_w, pool_cache, pool_scale, positions, bt, row_seq, bs, IH,
+                                          kpool, topk_pools, logits, sel, cnt))
+            emit({"case": "dsa_decode", "context": ctx, "rows": R, "pools": npools, "ms_logits_cuda_cores": ms_l,
+                  "ms_logits_tcgen05": ms_t, "ms_select_default_path": ms_s,
+                  "pool_cache_GBps_cuda_cores": npools * ID / ms_l / 1e6})
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["moe", "gemv", "gemm", "kda", "mla", "ep", "hc", "ag", "all"])
+    ap.add_argument("case", choices=["moe", "gemv", "gemm", "kda", "mla", "ep", "hc", "ag", "dsa", "all"])
     ap.add_argument("--tokens", type=int, nargs="+", default=[1, 8, 64, 512, 8192])
     ap.add_argument("--rows", type=int, nargs="+", default=[8])
     ap.add_argument("--kda-rows", type=int, nargs="+", default=[8, 8192])
     ap.add_argument("--mla-rows", type=int, nargs="+", default=[8, 1024])
+    ap.add_argument("--context", type=int, nargs="+", default=[4096, 131072, 524288],
+                    help="dsa: context lengths (tokens)")
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)

@@ -129,3 +129,66 @@ def test_dsa_pools_tail_ring_any_launch_split():
             npools = N // 4
             assert torch.equal(got[base:base + npools], ref[base:base + npools]), (s, final)
             assert torch.equal(got_s[base:base + npools], ref_s[base:base + npools])
+
+
+def _ref_selection(lg_row, c, pos, P, kp, bt_row, bs):
+    """Top P - 1 complete pools by logit (ties: lower index first), listed in index order and expanded to token
+    slots through the page table, then the row's own partial pool."""
+    order = sorted(range(c), key=lambda j: (-lg_row[j], j))[:P - 1]
+    slots = []
+    for j in sorted(order):
+        for i in range(kp):
+            p = j * kp + i
+            slots.append(bt_row[p // bs] * bs + p % bs)
+    for p in range(c * kp, pos + 1):
+        slots.append(bt_row[p // bs] * bs + p % bs)
+    return slots
+
+
+def test_dsa_select_long_rows_cluster_path():
+    """Rows longer than the split threshold are selected by a cluster of CTAs (histograms summed through DSMEM,
+    per-slice output offsets); a short row in the same launch by one CTA.  The logits of a decode-sized launch come
+    from the tcgen05 kernel when the longest row is long.  Both must give exactly the reference selection, with
+    exact ties (repeated pool keys) broken by index."""
+    from glm53.ops import kernels as Kk
+    C = Kk.C()
+    g = torch.Generator(device=DEV).manual_seed(11)
+    ID, IH, kp, bs, P = 128, 4, 4, 64, 512
+    rows = [(0, 80003), (1, 36001), (2, 12002)]           # (sequence, position): 20000, 9000 and 3000 pools
+    pages_per_seq = 1300
+    n_pages = pages_per_seq * len(rows)
+    bt = torch.randperm(n_pages, generator=torch.Generator().manual_seed(3)).to(torch.int32).view(len(rows), -1)
+    bt = bt.contiguous().to(DEV)
+    raw = torch.randint(0, 256, (n_pages * bs // kp, ID), generator=g, device=DEV, dtype=torch.int32)
+    raw[(raw == 0x7F) | (raw == 0xFF)] = 0
+    pool_cache = raw.to(torch.uint8)
+    # exact ties: a few pools of each sequence share one key
+    for s in range(len(rows)):
+        for j in (5, 77, 1234, 2999):
+            p = j * kp
+            slot = int(bt[s, p // bs]) * bs + p % bs
+            pool_cache[slot // kp] = pool_cache[int(bt[s, 0]) * bs // kp]
+    pool_scale = torch.ones(n_pages * bs // kp, device=DEV)
+    R = len(rows)
+    iproj = torch.randn(R, ID + IH + ID, generator=g, device=DEV)
+    qi = torch.randn(R, IH * ID, generator=g, device=DEV).to(torch.bfloat16)
+    positions = torch.tensor([p for _, p in rows], dtype=torch.int32, device=DEV)
+    row_seq = torch.tensor([s for s, _ in rows], dtype=torch.int32, device=DEV)
+    ln_w = torch.ones(ID, device=DEV)
+    max_pools = 32768
+    lg_tc = torch.zeros(R, max_pools, device=DEV)
+    C.dsa_logits(iproj, qi, ln_w, pool_cache, pool_scale, positions, bt, row_seq, bs, IH, kp, lg_tc, True)
+    lg = torch.zeros(R, max_pools, device=DEV)
+    sel = torch.zeros(R, P * kp, dtype=torch.int32, device=DEV)
+    cnt = torch.zeros(R, dtype=torch.int32, device=DEV)
+    C.dsa_select(iproj, qi, ln_w, pool_cache, pool_scale, positions, bt, row_seq, bs, IH, kp, P, lg, sel, cnt)
+    torch.cuda.synchronize()
+    assert C.gemm_error(lg) == 0 and C.gemm_error(lg_tc) == 0
+    bt_h = bt.cpu().tolist()
+    for r, (s, pos) in enumerate(rows):
+        c = pos // kp
+        assert torch.equal(lg[r, :c], lg_tc[r, :c])          # the tcgen05 kernel of the pair wrote the logits
+        exp = _ref_selection(lg[r, :c].cpu().tolist(), c, pos, P, kp, bt_h[s], bs)
+        n = int(cnt[r])
+        assert n == len(exp)
+        assert sel[r, :n].cpu().tolist() == exp, r
