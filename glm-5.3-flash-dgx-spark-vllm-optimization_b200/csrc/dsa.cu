@@ -388,7 +388,8 @@ cudaError_t g53_dsa_logits(const DsaArgs& a, cudaStream_t st) {
 }
 
 cudaError_t g53_dsa_select(const DsaArgs& a, cudaStream_t st) {
-  // clusters of kSelNC CTAs when the logits buffer can hold rows long enough for the split path
-  const int nc = a.max_pools > kSelSplit ? kSelNC : 1;
+  // clusters of kSelNC CTAs for decode-sized launches (fewer than 64 rows: one CTA per row would leave most SMs
+  // idle) whose logits buffer can hold rows long enough for the split path; prefill chunks keep one CTA per row
+  const int nc = (a.R < 64 && a.max_pools > kSelSplit) ? kSelNC : 1;
   return g53_launch_pdl(dsa_select_kernel, dim3(a.R, 1, nc), dim3(1024), 0, st, nc, a);
 }
