@@ -16,6 +16,7 @@
 //            chosen by a 4-pass 8-bit radix select on the logits (ties: lower pool index), expanded to token
 //            slots in ascending position order; while the row has at most topk_pools - 1 complete pools it sees
 //            every earlier key (dense).
+#include <algorithm>
 #include "common.cuh"
 #include "launchers.h"
 
@@ -381,7 +382,9 @@ cudaError_t g53_dsa_update(const DsaArgs& a, cudaStream_t st) {
 
 cudaError_t g53_dsa_logits(const DsaArgs& a, cudaStream_t st) {
   if (a.ID != 128 || a.IH > kMaxIH) return cudaErrorInvalidValue;
-  dim3 grid(a.R, (a.max_pools + 255) / 256);
+  // paired with the tcgen05 kernel, this kernel only serves launches whose rows have at most tc_min_pools pools
+  const int pools = a.tc_min_pools > 0 ? std::min(a.max_pools, a.tc_min_pools) : a.max_pools;
+  dim3 grid(a.R, (pools + 255) / 256);
   dsa_logits_kernel<<<grid, 256, 0, st>>>(a);
   G53_CHECK_LAUNCH();
   return cudaSuccess;

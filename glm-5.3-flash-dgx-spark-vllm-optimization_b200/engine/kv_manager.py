@@ -209,8 +209,9 @@ class KVManager:
         sc.hashes = list(hashes)
         sc.num_tokens = len(pids) * self.page_size
 
-    def commit_tokens(self, sc: SeqCache, tokens: list[int], upto: int) -> None:
-        """Positions [0, upto) are committed; publish newly full pages in the prefix cache."""
+    def commit_tokens(self, sc: SeqCache, tokens, upto: int) -> None:
+        """Positions [0, upto) are committed; publish newly full pages in the prefix cache.  `tokens` is a list or
+        any object whose contiguous slices give the sequence's tokens (engine.llm.TokenView)."""
         ps = self.page_size
         sc.num_tokens = upto
         while len(sc.hashes) < upto // ps:

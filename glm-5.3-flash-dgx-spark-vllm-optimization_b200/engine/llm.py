@@ -102,6 +102,35 @@ class Request:
     def tokens(self) -> list[int]:
         return self.prompt + self.output
 
+    def token_view(self, extra: list[int] = ()) -> "TokenView":
+        """prompt + output + extra without building the list (long contexts: the engine hashes only new pages)."""
+        return TokenView((self.prompt, self.output, list(extra)))
+
+
+class TokenView:
+    """Read-only concatenation of token lists, sliced on demand.  The prefix cache hashes only the pages completed
+    by a step, so a decode step at a 512k context copies a few pages instead of the whole prompt."""
+
+    def __init__(self, parts):
+        self.parts = parts
+
+    def __len__(self) -> int:
+        return sum(len(p) for p in self.parts)
+
+    def __getitem__(self, sl: slice) -> list[int]:
+        start, stop, step = sl.indices(len(self))
+        assert step == 1, "contiguous slices only"
+        out, base = [], 0
+        for p in self.parts:
+            n = len(p)
+            lo, hi = max(start - base, 0), min(stop - base, n)
+            if lo < hi:
+                out.extend(p[lo:hi])
+            base += n
+            if base >= stop:
+                break
+        return out
+
 
 @dataclass
 class RequestOutput:
@@ -267,7 +296,7 @@ class LLMEngine:
         for r, rows in batch:
             r.pos += len(rows.tokens)
             r.cur = 1 - r.cur
-            self.kv.commit_tokens(r.cache, r.tokens, r.pos)
+            self.kv.commit_tokens(r.cache, r.token_view(), r.pos)
             self._checkpoint(r)
         if finishing:
             toks = self._sample_rows(logits, [r for r, _ in finishing])
@@ -401,7 +430,7 @@ class LLMEngine:
             r.pos += k1
             r.cur = 1 - r.cur
             # the accepted drafts are not in r.output yet: hash the committed positions' own tokens
-            self.kv.commit_tokens(r.cache, r.tokens + r._new[:keep - 1], r.pos)
+            self.kv.commit_tokens(r.cache, r.token_view(r._new[:keep - 1]), r.pos)
             self._checkpoint(r)
         if rest:
             self.b.commit_rest(rest)
@@ -409,7 +438,7 @@ class LLMEngine:
                 r = batch[i][0]
                 r.pos += n
                 r.cur = 1 - r.cur
-                self.kv.commit_tokens(r.cache, r.tokens + r._new[:keeps[i] - 1], r.pos)
+                self.kv.commit_tokens(r.cache, r.token_view(r._new[:keeps[i] - 1]), r.pos)
                 self._checkpoint(r)
         to_draft = []
         for (r, rows), keep in zip(batch, keeps):

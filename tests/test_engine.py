@@ -238,3 +238,27 @@ def test_logprobs_follow_each_emitted_token(spec):
     while rid not in eng.done:
         eng.step()
     assert eng.done[rid].logprobs == []
+
+
+def test_token_view_slices_match_the_concatenated_list():
+    """The prefix cache hashes pages from a lazy view of prompt + output + accepted drafts: every contiguous slice
+    equals the same slice of the materialised list, and committing through the view publishes the same hashes."""
+    import random
+    from glm53.engine.llm import TokenView
+    from glm53.engine.kv_manager import page_hash
+    rng = random.Random(0)
+    parts = ([rng.randrange(1000) for _ in range(130)], [rng.randrange(1000) for _ in range(7)], [1, 2, 3])
+    full = parts[0] + parts[1] + parts[2]
+    v = TokenView(parts)
+    assert len(v) == len(full)
+    for _ in range(200):
+        a = rng.randrange(0, len(full) + 5)
+        b = rng.randrange(a, len(full) + 10)
+        assert v[a:b] == full[a:b]
+    ps, h_list, h_view, prev_l, prev_v = 16, [], [], None, None
+    for i in range(len(full) // ps):
+        prev_l = page_hash(prev_l, full[i * ps:(i + 1) * ps])
+        prev_v = page_hash(prev_v, v[i * ps:(i + 1) * ps])
+        h_list.append(prev_l)
+        h_view.append(prev_v)
+    assert h_list == h_view
