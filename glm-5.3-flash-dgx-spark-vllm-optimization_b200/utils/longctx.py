@@ -80,7 +80,13 @@ def main(argv=None):
                                     SamplingParams(max_tokens=max_len - ctx - 8, ignore_eos=True))
                     for _ in range(conc)]
             nsteps = 0
+            stalled = False
             while not (len(eng.running) == conc and all(r.state == State.RUNNING for r in eng.running)):
+                if not eng.running and not eng.waiting:
+                    # every request ended before decoding (the KV pool or a request limit cut it short): nothing
+                    # left to time; every rank sees the same engine state, so all leave together
+                    stalled = True
+                    break
                 eng.step()
                 nsteps += 1
                 if rank == 0 and nsteps % 16 == 0:
@@ -88,6 +94,15 @@ def main(argv=None):
                           f"{len(eng.running)}, waiting {len(eng.waiting)}", file=sys.stderr, flush=True)
             sync()
             prefill_s = time.perf_counter() - t0
+            if stalled:
+                if rank == 0:
+                    print(json.dumps({"context": ctx, "concurrency": conc, "tp": world,
+                                      "error": "requests finished during prefill (KV pool or request limits)",
+                                      "requests_finished": eng.metrics["requests_finished"]}), flush=True)
+                llm.backend._graphs.clear()
+                del llm, eng
+                torch.cuda.empty_cache()
+                continue
             for _ in range(args.warmup):
                 eng.step()
             sync()
