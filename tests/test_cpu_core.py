@@ -175,3 +175,32 @@ def test_kv_bytes_per_token_of_the_full_model():
     c = full_config()
     assert len(c.mla_layers()) == 11
     assert c.kv_bytes_per_token() == 11 * (c.kv_lora + 4 + 2 * max(c.qk_rope, 1) + (c.index_dim + 4) / c.kpool) == 6061
+
+
+def test_scratch_guard_bands_detect_overruns():
+    """Guard bands of the bounds-checked build's scratch allocator: intact after in-range writes, named after the
+    owner's attribute when a write runs past either end of a buffer, and absent (plain zeros) when disabled."""
+    from glm53.utils.canary import GUARD, Scratch
+
+    class Owner:
+        pass
+
+    own = Owner()
+    sc = Scratch("cpu", enabled=True)
+    sc.attach(own)
+    own.a = sc.zeros(5, 7, dtype=torch.float32)
+    own.b = [sc.zeros(3, dtype=torch.int32), sc.zeros(2, 4, dtype=torch.bfloat16)]
+    assert own.a.shape == (5, 7) and own.a.dtype == torch.float32 and not own.a.any()
+    assert own.a.data_ptr() % 256 == sc._bands[0][0].data_ptr() % 256     # the band keeps 256-byte alignment
+    own.a.fill_(3.0)
+    own.b[0].fill_(-1)
+    assert sc.check() == [] and len(sc) == 3
+    # one element past the end of b[1] and one before the start of a
+    raw_b1 = sc._bands[2][0]
+    raw_b1[GUARD + own.b[1].numel() * 2] = 0
+    raw_a = sc._bands[0][0]
+    raw_a[GUARD - 1] = 0
+    assert sorted(sc.check()) == ["a", "b[1]"]
+    plain = Scratch("cpu", enabled=False)
+    t = plain.zeros(4, dtype=torch.float32)
+    assert t.shape == (4,) and len(plain) == 0 and plain.check() == []
