@@ -153,6 +153,27 @@ void gemm_w8(const Tensor& x, const Tensor& w, const Tensor& scale, const Tensor
   gemm_common(q, true, qs, w, scale, y, mode, limit);
 }
 
+// per-row e4m3 quantisation of bf16 rows (the W8A8 activation format: q [M, K] uint8, qs [M] fp32).  A row's
+// codes depend on that row only, so rows quantised on their own rank and all-gathered equal rows gathered first
+void quant_rows(const Tensor& x, const Tensor& q, const Tensor& qs) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1);
+  TORCH_CHECK(q.scalar_type() == at::kByte && q.is_contiguous() && q.size(0) == x.size(0) && q.size(1) == x.size(1),
+              "q must be uint8 [M, K], contiguous");
+  TORCH_CHECK(qs.scalar_type() == at::kFloat && qs.numel() >= x.size(0), "qs must be fp32 [M]");
+  check(g53_quant_rows_e4m3(P<const __nv_bfloat16>(x), x.stride(0), (int)x.size(0), (int)x.size(1), P<uint8_t>(q),
+                            P<float>(qs), stream()),
+        "quant_rows_e4m3");
+}
+
+// W8A8 GEMM of rows already in the e4m3 row format (quant_rows): the sequence-parallel prefill all-gathers the
+// quantised rows of the KDA input projection instead of bf16 rows
+void gemm_w8q(const Tensor& q, const Tensor& qs, const Tensor& w, const Tensor& scale, const Tensor& y, int64_t mode,
+              double limit) {
+  TORCH_CHECK(q.scalar_type() == at::kByte && q.dim() == 2 && q.stride(1) == 1);
+  TORCH_CHECK(qs.scalar_type() == at::kFloat && qs.numel() >= q.size(0));
+  gemm_common(q, true, qs, w, scale, y, mode, limit);
+}
+
 // W8A16: the fp8 weight widened exactly to bf16 in a scratch, then the bf16 tcgen05 GEMM with the per-row
 // weight scales applied in the epilogue (same numerics as the small-M kernel: bf16 activations, exact weights)
 void gemm_w8a16(const Tensor& x, const Tensor& w, const Tensor& scale, const Tensor& y, int64_t mode, double limit,
@@ -1058,6 +1079,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemv", &gemv, py::arg("x"), py::arg("w"), py::arg("scale"), py::arg("y"), py::arg("mode"), py::arg("limit"),
         py::arg("ks") = 0, py::arg("cl") = 0);
   m.def("gemm_w8", &gemm_w8);
+  m.def("quant_rows", &quant_rows);
+  m.def("gemm_w8q", &gemm_w8q);
   m.def("gemm_bf16", &gemm_bf16);
   m.def("gemm_w8a16", &gemm_w8a16);
   m.def("gemm_error", &gemm_error);

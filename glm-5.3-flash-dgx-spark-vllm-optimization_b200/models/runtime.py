@@ -121,6 +121,10 @@ class Runtime:
         # chunk at TP2: 451 ms against 475 ms with the all-reduce
         self.sp = dev.type == "cuda" and os.environ.get("GLM53_SP", "1") == "1"
         self.sp_min_rows = int(os.environ.get("GLM53_SP_MIN_ROWS", "256"))
+        # with W8A8 on the KDA input projection, sequence-parallel chunks all-gather its e4m3 rows (and row scales)
+        # instead of bf16 rows: half the bytes, the same codes (per-row quantisation is row-local)
+        self.sp_fp8ag = os.environ.get("GLM53_SP_FP8AG", "1") == "1"
+        self._qin = None
         self._sp = None
         if comm is not None and self.tp > 1 and getattr(comm, "fused", False):
             from ..parallel.fused import PeerExchange
@@ -145,6 +149,9 @@ class Runtime:
         self.hidden = z(R, D, dtype=bf16, device=dev)
         # reduce-scatter output of the sequence-parallel prefill (this rank's rows of the block sum)
         self.rs = z((R + self.tp - 1) // self.tp, D, dtype=f32, device=dev) if self.tp > 1 else None
+        sp_q = self.tp > 1 and self.sp and self.sp_fp8ag and R >= K.GEMM_MIN_M
+        self.q_rows = z(R, D, dtype=torch.uint8, device=dev) if sp_q else None
+        self.q_scale = z(R, dtype=f32, device=dev) if sp_q else None
         self.fnormed = z(R, D, dtype=bf16, device=dev)
         self.lrows = z(rc.logit_rows, D, dtype=bf16, device=dev)
         self.logits = z(rc.logit_rows, w.head.n, dtype=f32, device=dev)
@@ -374,7 +381,10 @@ class Runtime:
                                self.part[:rows.stop - rows.start], c.eps, c.hc_eps, c.hc_iters)
             else:
                 self._post_pre(X, R, cur, nxt, lw.attn_hc, lw.in_norm)
-            self._sp_gather(self.normed, R)
+            if lw.kind == "kda" and self._sp_fp8(R):
+                self._sp_gather_q(R)
+            else:
+                self._sp_gather(self.normed, R)
             cur = nxt
             first = False
             if lw.kind == "kda":
@@ -399,6 +409,20 @@ class Runtime:
         torch.index_select(self.fnormed[:R], 0, b.logit_rows[:n], out=self.lrows[:n])
         K.linear8(self.lrows[:n], self.w.head.w, self.w.head.s, self.logits[:n], K.GEMV_F32)
         return self.logits[:n]
+
+    def _sp_fp8(self, R) -> bool:
+        """Whether this sequence-parallel chunk all-gathers the KDA input rows in e4m3 (see __init__)."""
+        return (self._sp is not None and self.q_rows is not None and R <= self.q_rows.shape[0]
+                and R >= K.GEMM_MIN_M and K.w8a8_large_m("kda_in_proj"))
+
+    def _sp_gather_q(self, R):
+        """This rank's normalised rows quantised to the W8A8 row format, then every rank's codes and scales to every
+        rank; the KDA input projection consumes them (self._qin) instead of bf16 rows."""
+        r0, r1 = self._sp
+        K.C().quant_rows(self.normed[r0:r1], self.q_rows[r0:r1], self.q_scale[r0:r1])
+        self.comm.all_gather(self.q_rows[:R].view(-1), self.q_rows[r0:r1].reshape(-1))
+        self.comm.all_gather(self.q_scale[:R], self.q_scale[r0:r1])
+        self._qin = (self.q_rows[:R], self.q_scale[:R])
 
     def _sp_gather(self, buf, R):
         """Sequence-parallel prefill: every rank's rows of ``buf`` to every rank (``buf[:R]`` in row order)."""
@@ -483,7 +507,12 @@ class Runtime:
         else:
             proj, fb, qkv = self.kproj[:R], self.kf[:R], self.kqkv[:R]
         C3 = 3 * H * Dh
-        K.linear8(self.normed[:R], k.in_proj.w, k.in_proj.s, proj, proj="kda_in_proj")
+        if self._qin is not None:         # sequence-parallel chunk: rows arrived as e4m3 codes and row scales
+            q, qs = self._qin
+            self._qin = None
+            Kc.gemm_w8q(q, qs, k.in_proj.w, k.in_proj.s, proj, K.GEMV_BF16, 0.0)
+        else:
+            K.linear8(self.normed[:R], k.in_proj.w, k.in_proj.s, proj, proj="kda_in_proj")
         if self._keep_window and self.kda_fused and Dh == 128 and c.conv == 4 and 1 <= b.max_rows_per_seq <= 16:
             # decode window: f_b, g_b, conv, recurrence and gated norm in one kernel (conv outputs and decay
             # logits stored for the commit replay)

@@ -67,6 +67,11 @@ def linear8(x: torch.Tensor, w: torch.Tensor, s: torch.Tensor, y: torch.Tensor, 
     return y
 
 
+def w8a8_large_m(proj: str) -> bool:
+    """True when a large-M call of projection `proj` runs W8A8 (activations quantised per row to e4m3)."""
+    return GEMM_ENABLED and (PREFILL_W8A8 or proj in W8A8_PROJ)
+
+
 def linear_bf16(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
     """y fp32 [M, N] = x bf16 [M, K] @ w bf16 [N, K]^T."""
     M = x.shape[0]

@@ -40,6 +40,8 @@ SWITCHES: dict[str, Switch] = {
     "GLM53_FUSED_TP_PREFILL": Switch("bool", "0", "prefill chunks push partials from the GEMM epilogue"),
     "GLM53_SP": Switch("bool", "1", "sequence-parallel prefill: mHC on each rank's rows, all-gather / reduce-scatter"),
     "GLM53_SP_MIN_ROWS": Switch("int", "256", "rows of a prefill chunk from which sequence parallelism is used"),
+    "GLM53_SP_FP8AG": Switch("bool", "1", "sequence-parallel prefill all-gathers the KDA input rows as e4m3 codes "
+                                          "when that projection runs W8A8"),
     "GLM53_SP_MLA": Switch("bool", "1", "sequence-parallel prefill runs the MLA attention of each rank's rows over "
                                         "all heads (keeps the full-head MLA projections on every rank)"),
     "GLM53_BOUNDS": Switch("bool", "0", "load the bounds-checked debug build (glm53_C_bounds): device indices "

@@ -170,6 +170,54 @@ def test_sequence_parallel_prefill_matches_allreduce(world):
     assert max(v[1] for v in result.values()) < 5e-2, ("row-parallel MLA", dict(result))
 
 
+def _sp_fp8_worker(rank, world, port, result):
+    """Sequence-parallel prefill with W8A8 on the KDA input projection: all-gathering the rows as e4m3 codes and
+    row scales against all-gathering bf16 rows and quantising after the gather.  Per-row quantisation is row-local,
+    so the two must agree bit for bit (and the all-reduce path is the W8A8 reference)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0", GLM53_SP_MIN_ROWS="64",
+                      GLM53_PREFILL_W8A8="kda_in_proj")
+    import torch.distributed as dist
+    from glm53.config import tiny_config
+    from glm53.models import weights as W
+    from glm53.models.runtime import Runtime, RuntimeConfig
+    from glm53.models.session import Sequence
+    from glm53.parallel import dist as D
+    D.init(timeout_s=60)
+    try:
+        cfg = tiny_config()
+        dev = torch.device("cuda", rank)
+        w = W.prepare(W.RandomSource(cfg, seed=0, device=dev), cfg, rank=rank, world=world, device=dev)
+        rc = RuntimeConfig(max_rows=128, max_seqs=1, kv_slots=64 * 8, block_size=64, max_blocks=8)
+        g = torch.Generator().manual_seed(6)
+        prompt = torch.randint(16, cfg.vocab, (256,), generator=g).tolist()
+        outs, used = [], []
+        for fp8ag in ("0", "1"):
+            os.environ["GLM53_SP"] = "1"
+            os.environ["GLM53_SP_FP8AG"] = fp8ag
+            rt = Runtime(w, rc, comm=D.NcclComm(fused=False))
+            seq = Sequence(rt)
+            lg = [seq.prefill(prompt, chunk=128).clone(), rt.hidden[:128].float().clone()]
+            used.append(rt._sp is not None and rt._sp_fp8(128))     # the last chunk ran sequence parallel
+            outs.append(torch.cat([x.flatten() for x in lg]))
+        result[rank] = ((outs[0] - outs[1]).abs().max().item(), used[1], rt.q_rows is not None)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sequence_parallel_fp8_allgather_bit_exact(world):
+    if _ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    result = mp.Manager().dict()
+    mp.spawn(_sp_fp8_worker, args=(world, 29591 + world, result), nprocs=world, join=True)
+    assert len(result) == world
+    assert all(v[1] and v[2] for v in result.values()), ("the e4m3 all-gather path was not taken", dict(result))
+    assert max(v[0] for v in result.values()) == 0.0, dict(result)
+
+
 def _ep_worker(rank, world, port, result):
     """The model with its routed experts expert-parallel (weights sharded by expert, rows of each layer split over
     the ranks, dispatch and combine through the peers' buffers) against the tensor-parallel model: logits of a
