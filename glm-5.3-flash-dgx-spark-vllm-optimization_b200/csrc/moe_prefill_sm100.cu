@@ -147,8 +147,10 @@ __device__ __forceinline__ void frags(uint32_t cur, uint32_t prev, uint32_t (&b)
   b[3] = mcg_sum2(mcg_mask_(t4 * C + s20 * Cn), mcg_mask_(cur * C + s16 * Cn));
 }
 
-__device__ __forceinline__ void sts_u32(uint32_t addr, uint32_t v) {
-  asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+__device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3])
+               : "memory");
 }
 
 // byte offset of element (row, k) (k even) in a 128-row x 64-k f16 tile, K-major, 128-byte swizzle
@@ -231,7 +233,6 @@ __global__ void __launch_bounds__(Cfg<GU>::kThreads, Cfg<GU>::kMinBlocks) moe_pr
     constexpr int TILES = NM * 4 * 8;                   // (matrix, k-tile, n-tile) of one stage
     constexpr int PER = TILES / kDecWarps;
     const int src = (lane + 31) & 31;
-    const int g = lane >> 2, q = lane & 3;
     // The warp's PER tiles of a stage, tile i = (matrix idx / 32, k-tile (idx / 8) % 4, n-tile idx % 8) with
     // idx = warp + i * kDecWarps, are the same in every stage: their trellis word addresses advance by one stage
     // of k-tiles (4 * NT tiles of 32 words) and their shared-memory offsets repeat.  Both are formed once here, so
@@ -240,14 +241,17 @@ __global__ void __launch_bounds__(Cfg<GU>::kThreads, Cfg<GU>::kMinBlocks) moe_pr
     const uint32_t* wb0 = reinterpret_cast<const uint32_t*>(p.tr0) + (int64_t)e * KT * NT * 32;
     const uint32_t* wb1 = reinterpret_cast<const uint32_t*>(p.tr1) + (int64_t)e * KT * NT * 32;
     uint32_t wo[PER];                                   // word offset of tile i in stage 0
-    uint32_t so[PER];                                   // byte offset of (row n0, k0) of tile i in a stage
+    uint32_t so[PER];                                   // byte offset of this lane's stmatrix row of tile i
     const uint32_t kstep = 4u * NT * 32u;               // words per stage of k-tiles
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       const int idx = warp + i * kDecWarps;
       const int m = idx / 32, kt = (idx / 8) & 3, nt = idx & 7;
       wo[i] = (uint32_t)((kt * NT + nb * 8 + nt) * 32 + lane);
-      so[i] = (uint32_t)(m * A_BYTES) + sw_off(nt * 16 + g, kt * 16 + 2 * q);
+      // stmatrix x4: lane l addresses row l % 8 of 8 x 8 block l / 8; blocks 0..3 = (rows 0-7 | 8-15) x
+      // (k 0-7 | 8-15) of the 16 x 16 tile, in the order of the fragment registers b[0..3]
+      const int mrow = nt * 16 + (lane & 7) + ((lane >> 4) & 1) * 8, mk = kt * 16 + ((lane >> 3) & 1) * 8;
+      so[i] = (uint32_t)(m * A_BYTES) + sw_off(mrow, mk);
     }
     const uint32_t sbase = su32(sm);
     int it = 0;                                         // global stage counter (continues across passes)
@@ -282,13 +286,9 @@ __global__ void __launch_bounds__(Cfg<GU>::kThreads, Cfg<GU>::kMinBlocks) moe_pr
         for (int i = 0; i < PER; ++i) {
           uint32_t b[4];
           frags(wcur[i], __shfl_sync(0xffffffffu, wcur[i], src), b);
-          // (n0, k0), (n0, k0 + 8), (n0 + 8, k0), (n0 + 8, k0 + 8): k0 + 8 flips the 16-byte chunk's low bit
-          // (the chunk index 2 * kt is even before the swizzle), row n0 + 8 is 1024 bytes further
-          const uint32_t a0 = ab + so[i], a1 = ab + (so[i] ^ 16u);
-          sts_u32(a0, b[0]);
-          sts_u32(a1, b[1]);
-          sts_u32(a0 + 1024u, b[2]);
-          sts_u32(a1 + 1024u, b[3]);
+          // b[0..3] hold (row g, k 2q..2q+1) of the blocks (n0, k0), (n0, k0 + 8), (n0 + 8, k0), (n0 + 8, k0 + 8):
+          // the mma fragment layout that stmatrix stores, each block row a 16-byte chunk of the swizzled tile
+          stsm_x4(ab + so[i], b);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
