@@ -14,6 +14,7 @@
 // :529/:582 (route_prep / route_ids).
 #include <algorithm>
 #include <cooperative_groups.h>
+#include <cstdlib>
 #include "common.cuh"
 #include "launchers.h"
 
@@ -730,13 +731,21 @@ static cudaError_t down_ks(const Exl3Args& a, dim3 grid, cudaStream_t st) {
 cudaError_t g53_exl3_gate_up(const Exl3Args& a, cudaStream_t st) {
   if (a.K % 128 || a.N % 128 || !a.decode_layout) return cudaErrorInvalidValue;
   const dim3 grid(a.N / 128, a.launch_groups > 0 ? std::min(a.launch_groups, a.max_groups) : a.max_groups);
-  // K split over a cluster until the grid has about 2048 CTAs (3.5 waves of 4 per SM): measured at TP1 with 8 tokens
-  // (64 groups x 16 column blocks) a split of 2 beats 4 (0.342 vs 0.358 ms per layer) and 1 (0.352); the narrow
-  // expert shards of TP 4 / 8 (4 / 2 column blocks) need 8
+  // K split over a cluster: at least 2, then doubled up to 4 while the grid has fewer than 1024 CTAs.  Measured
+  // per MoE layer at 8 tokens (kernel_bench moe --tp N, splits 1 / 2 / 4 / 8, us): TP1 349 / 341 / 356 / 395,
+  // TP2 214 / 191 / 203 / 218, TP4 194 / 138 / 136 / 145, TP8 186 / 129 / 100 / 103
   const int kc = a.K / 64;
   int split = 1;
-  while (split < 8 && (int64_t)grid.x * grid.y * split < 2048 && kc % (2 * split) == 0 && kc / (2 * split) >= 4)
+  while ((split < 2 || (split < 4 && (int64_t)grid.x * grid.y * split < 1024)) && kc % (2 * split) == 0 &&
+         kc / (2 * split) >= 4)
     split *= 2;
+  // GLM53_MOE_DECODE_SPLIT (1, 2, 4 or 8) overrides the choice, for tuning; the K range must divide
+  static const int forced = [] {
+    const char* e = std::getenv("GLM53_MOE_DECODE_SPLIT");
+    return e ? std::atoi(e) : 0;
+  }();
+  if ((forced == 1 || forced == 2 || forced == 4 || forced == 8) && kc % forced == 0 && kc / forced >= 2)
+    split = forced;
   switch (split) {
     case 8: return gate_up_ks<8>(a, grid, st);
     case 4: return gate_up_ks<4>(a, grid, st);

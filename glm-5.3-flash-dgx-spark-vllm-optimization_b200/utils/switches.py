@@ -40,6 +40,8 @@ SWITCHES: dict[str, Switch] = {
     "GLM53_FUSED_TP_PREFILL": Switch("bool", "0", "prefill chunks push partials from the GEMM epilogue"),
     "GLM53_SP": Switch("bool", "1", "sequence-parallel prefill: mHC on each rank's rows, all-gather / reduce-scatter"),
     "GLM53_SP_MIN_ROWS": Switch("int", "256", "rows of a prefill chunk from which sequence parallelism is used"),
+    "GLM53_MOE_DECODE_SPLIT": Switch("int", "0", "decode MoE gate/up: K split over a cluster (1, 2, 4, 8; 0 = "
+                                                "chosen from the grid size), for tuning"),
     "GLM53_SP_FP8AG": Switch("bool", "1", "sequence-parallel prefill all-gathers the KDA input rows as e4m3 codes "
                                           "when that projection runs W8A8"),
     "GLM53_SP_MLA": Switch("bool", "1", "sequence-parallel prefill runs the MLA attention of each rank's rows over "
