@@ -232,7 +232,7 @@ def main():
     eng.abort(rid)
     eng.cfg.force_accept = False
     cprompt = torch.randint(0, cfg.vocab, (256,), generator=torch.Generator().manual_seed(99)).tolist()
-    cid = eng.add_request(cprompt, SamplingParams(max_tokens=16, ignore_eos=True, logprobs=2))
+    cid = eng.add_request(cprompt, SamplingParams(max_tokens=16, ignore_eos=True, logprobs=5))
     run_until(lambda: cid in eng.done)
     creq = eng.done[cid]
     ctoks = list(creq.output[:16])
@@ -241,8 +241,14 @@ def main():
         v = sorted(top.values(), reverse=True)
         gaps.append(v[0] - v[1] if len(v) > 1 else float("inf"))
     import hashlib
+    first = sorted(creq.logprobs[0][1].items(), key=lambda kv: -kv[1]) if creq.logprobs else []
     check = {"greedy_tokens": ctoks, "sha16": hashlib.sha256(json.dumps(ctoks).encode()).hexdigest()[:16],
-             "min_top2_gap": min(gaps) if gaps else None, "prompt": "256 uniform random ids (seed 99)"}
+             "min_top2_gap": min(gaps) if gaps else None, "top2_gaps": [round(x, 4) for x in gaps],
+             "first_top5": [[int(t), round(float(v), 4)] for t, v in first[:5]],
+             "prompt": "256 uniform random ids (seed 99)",
+             "note": "random-init weights make the greedy sequence sensitive to rounding: at 1 GPU, exact W8A16 "
+                     "instead of W8A8 on two prefill projections (GLM53_PREFILL_W8A8=none) already changes the "
+                     "first token; across GPU counts compare first_top5 (ids and log-probabilities)"}
 
     if rank == 0:
         out = {
