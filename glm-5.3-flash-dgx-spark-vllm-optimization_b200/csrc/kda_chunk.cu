@@ -26,8 +26,11 @@ constexpr int kC = 64;       // chunk rows
 constexpr int kSubR = 16;    // sub-chunk rows (reference points)
 
 // record per (chunk slot, head), in floats: Q~, K~, K^ as fp16 [kC][dh] each (exact for the tf32 products; every
-// value is a unit-normalised row times a decay factor <= 1), T and P fp32 [kC][kC], e^{G_C} fp32 [dh]
-__host__ __device__ constexpr int64_t kda_scr_per_head(int dh) { return 3LL * kC * dh / 2 + 2LL * kC * kC + dh; }
+// value is a unit-normalised row times a decay factor <= 1), T and P as fp16 [kC][kC] (the scan feeds them to tf32
+// products: fp16 keeps the same 10 explicit significand bits; T's columns are those of a product of delta-rule
+// contractions and P's entries are decayed dot products of normalised rows, far inside the fp16 range), e^{G_C}
+// fp32 [dh]
+__host__ __device__ constexpr int64_t kda_scr_per_head(int dh) { return 3LL * kC * dh / 2 + 1LL * kC * kC + dh; }
 
 __device__ __forceinline__ int chunk_slot(int row0, int b, int c) { return row0 / kC + b + c; }
 
@@ -100,9 +103,9 @@ __global__ void __launch_bounds__(256, 2) kda_prep_kernel(KdaArgs a) {
   __half* oQ = reinterpret_cast<__half*>(out);
   __half* oK = oQ + kC * DH;
   __half* oKb = oK + kC * DH;
-  float* oT = out + 3 * kC * DH / 2;
-  float* oP = oT + kC * kC;
-  float* oE = oP + kC * kC;
+  __half* oT = reinterpret_cast<__half*>(out + 3 * kC * DH / 2);
+  __half* oP = oT + kC * kC;
+  float* oE = out + 3 * kC * DH / 2 + kC * kC;
 
   for (int e = tid; e < 2 * kC * kPM; e += blockDim.x) sM[e] = 0.f;     // sM and sP are adjacent
 
@@ -293,8 +296,8 @@ __global__ void __launch_bounds__(256, 2) kda_prep_kernel(KdaArgs a) {
   // 6. T = X diag(beta) and P into the record
   for (int e = tid; e < kC * kC; e += blockDim.x) {
     const int t = e / kC, s = e % kC;
-    oT[e] = sI[t * kPM + s] * sB[s];
-    oP[e] = sP[t * kPM + s];
+    oT[e] = __float2half_rn(sI[t * kPM + s] * sB[s]);
+    oP[e] = __float2half_rn(sP[t * kPM + s]);
   }
 }
 
@@ -353,21 +356,24 @@ __device__ __forceinline__ void cp16(void* dst, const void* src, uint32_t bytes)
 template <int DH>
 struct ScanBuf {
   static constexpr int LH = DH + 8;                        // row pitch (halves) of the fp16 tiles
-  static constexpr int LT = kC + 4;                        // row pitch of T and P
+  static constexpr int LT = kC + 8;                        // row pitch (halves) of T and P
   static constexpr int H3 = 3 * kC * LH / 2;               // floats of the three fp16 tiles
-  static constexpr int T_OFF = H3, P_OFF = H3 + kC * LT, E_OFF = H3 + 2 * kC * LT, V_OFF = E_OFF + DH;
+  static constexpr int T_OFF = H3, P_OFF = H3 + kC * LT / 2, E_OFF = H3 + kC * LT, V_OFF = E_OFF + DH;
   static constexpr int FLOATS = V_OFF + kC * 32 / 2;        // + [kC][32] bf16 value slice
 };
 
-template <int DH>
-__global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
+// DB: two record buffers, one CTA per SM (the next chunk's record loads during this chunk); otherwise one
+// buffer and two CTAs per SM (used when the grid has more CTAs than SMs: all of them run in one round, each
+// CTA's record load overlapping the other CTA's products)
+template <int DH, bool DB>
+__global__ void __launch_bounds__(256, DB ? 1 : 2) kda_scan_kernel(KdaArgs a) {
   using B = ScanBuf<DH>;
   constexpr int LH = B::LH, LT = B::LT;
   constexpr int LD = DH + 4;       // row pitch of the fp32 state tile
   constexpr int LV = 36;           // row pitch of the [kC][32] value tiles
   extern __shared__ float sm[];
-  float* buf0 = sm;                // 2 record buffers (chunk ci uses buffer ci % 2; ci + 1 loads meanwhile)
-  float* sS = sm + 2 * B::FLOATS;  // [32][LD]  state rows v0..v0+31 (v-major), fp32
+  float* buf0 = sm;                // record buffers (DB: chunk ci uses buffer ci % 2; ci + 1 loads meanwhile)
+  float* sS = sm + (DB ? 2 : 1) * B::FLOATS;   // [32][LD]  state rows v0..v0+31 (v-major), fp32
   float* sZ = sS + 32 * LD;        // [kC][LV]  V, then V - K~ S0^T
   float* sV = sZ + kC * LV;        // [kC][LV]  v'
 
@@ -392,12 +398,14 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
       const int m = e / (kC * (DH / 8)), t = (e / (DH / 8)) % kC, c = e % (DH / 8);
       cp16(hq + m * kC * LH + t * LH + c * 8, rh + (int64_t)m * kC * DH + t * DH + c * 8, 16u);
     }
-    const float* rt = rec + 3 * kC * DH / 2;
-    for (int e = tid; e < 2 * kC * (kC / 4); e += blockDim.x) {       // T then P
-      const int m = e / (kC * (kC / 4)), t = (e / (kC / 4)) % kC, c = e % (kC / 4);
-      cp16(bf + B::T_OFF + m * kC * LT + t * LT + c * 4, rt + m * kC * kC + t * kC + c * 4, 16u);
+    const __half* rt = reinterpret_cast<const __half*>(rec + 3 * kC * DH / 2);
+    __half* ht = reinterpret_cast<__half*>(bf + B::T_OFF);
+    for (int e = tid; e < 2 * kC * (kC / 8); e += blockDim.x) {       // T then P, fp16
+      const int m = e / (kC * (kC / 8)), t = (e / (kC / 8)) % kC, c = e % (kC / 8);
+      cp16(ht + m * kC * LT + t * LT + c * 8, rt + m * kC * kC + t * kC + c * 8, 16u);
     }
-    for (int e = tid; e < DH / 4; e += blockDim.x) cp16(bf + B::E_OFF + e * 4, rt + 2 * kC * kC + e * 4, 16u);
+    const float* re = rec + 3 * kC * DH / 2 + kC * kC;
+    for (int e = tid; e < DH / 4; e += blockDim.x) cp16(bf + B::E_OFF + e * 4, re + e * 4, 16u);
     const int c0 = ci * kC, n = min(kC, n_all - c0);
     __nv_bfloat16* vr = reinterpret_cast<__nv_bfloat16*>(bf + B::V_OFF);
     for (int e = tid; e < kC * 4; e += blockDim.x) {                  // 4 x 16 bytes per value row
@@ -422,15 +430,19 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
     const int c0 = ci * kC;
     const int n = min(kC, n_all - c0);
     if (chunk_slot(base, b, ci) >= a.scr_slots) break;
+    if (!DB && ci > 0) {
+      __syncthreads();                       // every thread is done with chunk ci - 1's record: reuse the buffer
+      issue(ci, 0);
+    }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();                         // chunk ci landed for every thread; buffer (ci + 1) % 2 is free
-    if (ci + 1 < nchunks) issue(ci + 1, (ci + 1) & 1);
-    const float* bf = buf0 + (ci & 1) * B::FLOATS;
+    __syncthreads();                         // chunk ci landed for every thread; DB: buffer (ci + 1) % 2 is free
+    if (DB && ci + 1 < nchunks) issue(ci + 1, (ci + 1) & 1);
+    const float* bf = buf0 + (DB ? (ci & 1) : 0) * B::FLOATS;
     const __half* sQ = reinterpret_cast<const __half*>(bf);
     const __half* sKt = sQ + kC * LH;
     const __half* sKb = sKt + kC * LH;
-    const float* sT = bf + B::T_OFF;
-    const float* sP = bf + B::P_OFF;
+    const __half* sT = reinterpret_cast<const __half*>(bf + B::T_OFF);
+    const __half* sP = reinterpret_cast<const __half*>(bf + B::P_OFF);
     const float* sE = bf + B::E_OFF;
     const __nv_bfloat16* vr = reinterpret_cast<const __nv_bfloat16*>(bf + B::V_OFF);
     for (int e = tid; e < kC * 32; e += blockDim.x) {
@@ -466,7 +478,7 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
       float acc[2][4] = {};
       for (int k0 = 0; k0 < (mt + 1) * 16; k0 += 8) {
         uint32_t fa[4];
-        frag_a_row(sT + mt * 16 * LT + k0, LT, fa);
+        frag_a_row_h(sT + mt * 16 * LT + k0, LT, fa);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           uint32_t b0, b1;
@@ -499,7 +511,7 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
       }
       for (int k0 = 0; k0 < (mt + 1) * 16; k0 += 8) {
         uint32_t fa[4];
-        frag_a_row(sP + mt * 16 * LT + k0, LT, fa);
+        frag_a_row_h(sP + mt * 16 * LT + k0, LT, fa);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           uint32_t b0, b1;
@@ -563,22 +575,38 @@ __global__ void __launch_bounds__(256, 1) kda_scan_kernel(KdaArgs a) {
   }
 }
 
+template <int DH, bool DB>
+cudaError_t launch_scan(const KdaArgs& a, cudaStream_t st) {
+  const size_t smem = sizeof(float) * ((size_t)(DB ? 2 : 1) * ScanBuf<DH>::FLOATS + 32 * (DH + 4) + 2 * kC * 36);
+  cudaError_t e = cudaFuncSetAttribute(kda_scan_kernel<DH, DB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  kda_scan_kernel<DH, DB><<<dim3(a.H, DH / 32, a.B), 256, smem, st>>>(a);
+  return cudaGetLastError();
+}
+
+static int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      n = 148;
+  }
+  return n;
+}
+
 template <int DH>
 cudaError_t launch_chunk(const KdaArgs& a, cudaStream_t st) {
   const size_t smem_prep = sizeof(float) * (size_t)prep_smem_floats();
-  const size_t smem_scan = sizeof(float) * ((size_t)2 * ScanBuf<DH>::FLOATS + 32 * (DH + 4) + 2 * kC * 36);
   cudaError_t e = cudaFuncSetAttribute(kda_prep_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)smem_prep);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(kda_scan_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_scan);
   if (e != cudaSuccess) return e;
   const dim3 gp((a.R + kC - 1) / kC, a.H, a.B);     // chunks past a sequence's rows exit at once
   kda_prep_kernel<DH><<<gp, 256, smem_prep, st>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const dim3 gs(a.H, DH / 32, a.B);
-  kda_scan_kernel<DH><<<gs, 256, smem_scan, st>>>(a);
-  return cudaGetLastError();
+  // scan CTAs: (head, 32 value rows, sequence); more of them than SMs -> the single-buffer, two-per-SM form
+  if ((int64_t)a.H * (DH / 32) * a.B > sm_count()) return launch_scan<DH, false>(a, st);
+  return launch_scan<DH, true>(a, st);
 }
 
 }  // namespace g53

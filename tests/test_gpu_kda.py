@@ -49,6 +49,27 @@ def test_kda_chunk_matches_recurrent(Dh, T):
     _close(S[3], S[1])
 
 
+def test_kda_chunk_many_heads_single_buffer_scan():
+    """48 heads x 4 value blocks = 192 scan CTAs, more than the SMs: the scan runs its single-buffer, two-CTAs-per-SM
+    form; it must match the recurrent form like the double-buffer one does."""
+    from glm53.ops import kernels as Kk
+    C = Kk.C()
+    H, Dh, T = 48, 128, 200
+    proj, qkv, f, a_log, dt_bias, b_off = _inputs(T, H, Dh, 77)
+    S = torch.randn(4, H, Dh, Dh, device=DEV) * 0.1
+    S[1].zero_()
+    S[3].zero_()
+    o1 = torch.zeros(T, H * Dh, device=DEV)
+    C.kda_recurrent(proj, torch.tensor([[0], [T], [0], [1], [0]], dtype=torch.int32, device=DEV), f, qkv, a_log,
+                    dt_bias, S, o1, H, Dh, b_off, -5.0)
+    o2 = torch.zeros(T, H * Dh, device=DEV)
+    scr = torch.empty(C.kda_chunk_scratch_floats(T, 1, H, Dh), device=DEV)
+    C.kda_chunk(proj, torch.tensor([[0], [T], [0], [3], [0]], dtype=torch.int32, device=DEV), f, qkv, a_log, dt_bias,
+                S, o2, H, Dh, b_off, -5.0, scr)
+    _close(o2, o1)
+    _close(S[3], S[1])
+
+
 def test_kda_chunk_two_sequences_unaligned():
     """Two sequences in one chunked launch, the second starting at a row that is not a multiple of 64."""
     from glm53.ops import kernels as Kk
