@@ -204,3 +204,65 @@ def test_scratch_guard_bands_detect_overruns():
     plain = Scratch("cpu", enabled=False)
     t = plain.zeros(4, dtype=torch.float32)
     assert t.shape == (4,) and len(plain) == 0 and plain.check() == []
+
+
+def _order_key(f):
+    import struct
+    u = struct.unpack("<I", struct.pack("<f", f))[0]
+    return (~u & 0xFFFFFFFF) if (u & 0x80000000) else (u | 0x80000000)
+
+
+def _sliced_radix_select(vals, K, nc):
+    """Python model of the DSA select's cluster path: slices of the logits, 256-bin radix histograms summed over
+    the slices for each of four 8-bit passes, then per-slice counts of keys above / equal to the threshold key give
+    each slice its output offset; ties are taken in index order up to the remainder."""
+    c = len(vals)
+    keys = [_order_key(v) for v in vals]
+    bounds = [(c * k // nc, c * (k + 1) // nc) for k in range(nc)]
+    prefix, mask, rem = 0, 0, K
+    for p in range(4):
+        shift = 24 - 8 * p
+        hist = [0] * 256
+        for j0, j1 in bounds:                       # per-slice histograms, summed in rank order
+            for j in range(j0, j1):
+                if keys[j] & mask == prefix:
+                    hist[(keys[j] >> shift) & 255] += 1
+        acc, b = 0, 0
+        for bin_ in range(255, 0, -1):              # highest bin whose count from the top reaches rem
+            if acc + hist[bin_] >= rem:
+                b = bin_
+                break
+            acc += hist[bin_]
+        prefix |= b << shift
+        rem -= acc
+        mask |= 255 << shift
+    counts = [(sum(keys[j] > prefix for j in range(j0, j1)), sum(keys[j] == prefix for j in range(j0, j1)))
+              for j0, j1 in bounds]
+    out = [None] * K
+    for k, (j0, j1) in enumerate(bounds):
+        base_sel = base_eq = 0
+        for gk, ek in counts[:k]:
+            base_sel += gk + max(0, min(ek, rem - base_eq))
+            base_eq += ek
+        for j in range(j0, j1):
+            if keys[j] > prefix or (keys[j] == prefix and base_eq < rem):
+                out[base_sel] = j
+                base_sel += 1
+            base_eq += keys[j] == prefix
+    return out
+
+
+@pytest.mark.parametrize("nc", [1, 3, 8])
+def test_sliced_radix_select_matches_sorted_selection(nc):
+    """The cluster select's offset rule (counts of lower slices, ties in index order) gives exactly the top-K
+    indices of a stable descending sort, listed in index order, for any number of slices."""
+    import random
+    rng = random.Random(nc)
+    for trial in range(20):
+        c = rng.randrange(40, 400)
+        vals = [round(rng.gauss(0, 1), 1) for _ in range(c)]          # one decimal: many exact ties
+        if trial % 4 == 0:
+            vals = [0.0] * c                                          # all tied
+        K = rng.randrange(1, c)
+        ref = sorted(sorted(range(c), key=lambda j: (-vals[j], j))[:K])
+        assert _sliced_radix_select(vals, K, nc) == ref
