@@ -19,6 +19,7 @@ code/fork/overlay/patch_mamba_align_seed.py).
 from __future__ import annotations
 
 import hashlib
+from array import array
 from collections import OrderedDict
 from dataclasses import dataclass, field
 
@@ -157,8 +158,9 @@ class StateSlots:
 
 @dataclass
 class SeqCache:
-    """Cache state of one request: its page table and prefix hashes."""
-    pages: list[int] = field(default_factory=list)
+    """Cache state of one request: its page table and prefix hashes.  The page table is a compact int32 array, so
+    staging it for a step is one buffer copy (16,384 pages at a 1M context) instead of a per-element conversion."""
+    pages: array = field(default_factory=lambda: array("i"))
     hashes: list[bytes] = field(default_factory=list)   # hash of each full page, in order
     num_tokens: int = 0                                   # tokens with cache entries written (committed)
 
@@ -205,7 +207,7 @@ class KVManager:
     def adopt_prefix(self, sc: SeqCache, pids: list[int], hashes: list[bytes]) -> None:
         for pid in pids:
             self.alloc.retain(pid)
-        sc.pages = list(pids)
+        sc.pages = array("i", pids)
         sc.hashes = list(hashes)
         sc.num_tokens = len(pids) * self.page_size
 
@@ -223,4 +225,4 @@ class KVManager:
     def free(self, sc: SeqCache) -> None:
         for pid in sc.pages:
             self.alloc.release(pid)
-        sc.pages = []
+        sc.pages = array("i")

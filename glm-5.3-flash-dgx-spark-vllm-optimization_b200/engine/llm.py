@@ -19,6 +19,7 @@ from __future__ import annotations
 import hashlib
 import itertools
 import time
+from array import array
 from dataclasses import dataclass, field
 from enum import Enum
 
@@ -259,7 +260,7 @@ class LLMEngine:
         n = len(tokens)
         self.kv.grow(r.cache, pos0 + n)
         positions = list(range(pos0, pos0 + n))
-        return SeqRows(tokens, positions, [self.kv.slot(r.cache, p) for p in positions], list(r.cache.pages),
+        return SeqRows(tokens, positions, [self.kv.slot(r.cache, p) for p in positions], array("i", r.cache.pages),
                        r.slot, r.cur)
 
     def _prefill_step(self, reqs: list[Request], budget: int | None = None) -> list[RequestOutput]:

@@ -17,11 +17,12 @@ keep < rows, from the layer's saved window inputs) and shifts the conv windows.
 
 from __future__ import annotations
 
-import os
-
 import math
+import os
+from array import array
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from ..config import ModelConfig
@@ -316,7 +317,8 @@ class Runtime:
         sq_off = o - 5 * B
         bt_off = o
         for t in block_tables:
-            h[o:o + len(t)] = t
+            # int32 arrays (the engine's page tables) copy as one buffer; lists convert element by element
+            h[o:o + len(t)] = np.frombuffer(t, dtype=np.int32) if isinstance(t, array) and t.itemsize == 4 else t
             o += nbt
         o += o & 1                                        # 8-byte alignment of the int64 logit-row indices
         lr = h[o:o + 2 * len(logit_rows)].view("int64")
