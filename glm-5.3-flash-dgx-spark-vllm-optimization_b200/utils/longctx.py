@@ -61,7 +61,10 @@ def main(argv=None):
     results = []
     for conc in args.concurrency:
         for ctx in args.contexts:
-            max_len = ctx + rows * (args.steps + args.warmup + 8) + 64
+            # requests that finish their prefill first decode (K + 1 tokens per engine step) while the others are
+            # still prefilling: budget those steps too, or the early ones reach max_tokens before the timed steps
+            prefill_steps = -(-conc * ctx // args.prefill_chunk) + conc
+            max_len = ctx + rows * (args.steps + args.warmup + 8 + prefill_steps) + 64
             llm = LLM(LLMOptions(model=args.model, max_seqs=conc, max_model_len=max_len,
                                  prefill_chunk=args.prefill_chunk, speculative=True, k_fixed=K, force_accept=True,
                                  checkpoints=0, cuda_graphs=True), comm=comm, rank=rank, world=world)
