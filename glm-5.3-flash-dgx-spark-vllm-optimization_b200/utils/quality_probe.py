@@ -6,9 +6,9 @@ They run in-process on the engine and runtime of this package instead of through
   run      fixed prompts: greedy completions through the engine (speculative decode on) and teacher-forced top-k
            log-probabilities of every prompt position through the prefill kernels; saved as JSON.  Run once per
            configuration (e.g. per arm of an environment A/B)
-  compare  two saved runs: identical completions and the first divergent token; per-position KL over the union of
-           both top-k sets (mass outside a set floored one nat below its smallest entry), mean / p95 / max, top-1
-           agreement
+  compare  two saved runs: identical completions and the first divergent token; per-position KL over a partition
+           of the vocabulary (one cell per token either run saved, one cell for the rest; each run's unsaved mass
+           shared evenly over its unsaved tokens), mean / p95 / max, top-1 agreement
   dvp      decode vs prefill on the same sequences: every position's logits from decode windows (GEMV, per-row
            attention, recurrent KDA: the decode kernels) against prefill chunks (tcgen05 GEMM, chunked KDA, tensor-core
            attention); KL and top-1 per position bucket
@@ -43,20 +43,32 @@ def topk_logprobs(logits: torch.Tensor, k: int) -> list[dict]:
     return [{int(a): float(b) for a, b in zip(ii.tolist(), vv.tolist())} for ii, vv in zip(i, v)]
 
 
-def topk_kl(pa: dict, pb: dict) -> float:
-    """Divergence of run B from run A at one position, from each run's saved top-k {token: log-probability}.
+def topk_kl(pa: dict, pb: dict, vocab: int) -> float:
+    """KL(A || B) at one position, estimated from each run's saved top-k {token: log-probability} over a vocabulary
+    of `vocab` tokens.
 
-    Definition: let U be the union of the two saved token sets and f one nat below the smallest saved
-    log-probability of either run.  Each run's distribution over U takes its saved value where it has one and f
-    elsewhere (a token outside a run's top-k is less likely than any it kept), renormalised over U; the statistic is
-    KL(A_U || B_U).  When both runs saved the whole vocabulary this is the exact KL.  The floor rule is the one the
-    reference's quality tooling uses, kept so that numbers from either side compare."""
-    toks = sorted(set(pa) | set(pb))
-    f = min(min(pa.values()), min(pb.values())) - 1.0
-    a = torch.tensor([pa.get(t, f) for t in toks], dtype=torch.float64)
-    b = torch.tensor([pb.get(t, f) for t in toks], dtype=torch.float64)
-    la, lb = a - torch.logsumexp(a, 0), b - torch.logsumexp(b, 0)
-    return float((la.exp() * (la - lb)).sum())
+    The vocabulary is partitioned into one cell per token saved by either run, plus one cell for every other token.
+    A run's probability of a cell:
+    - a token it saved: the exponential of the saved log-probability;
+    - any other token: an equal share of the mass it did not save, 1 - sum(exp(saved)), spread over its unsaved
+      tokens (a token that only the other run kept thus gets this run's tail share);
+    - the remaining cell: that share times the number of tokens in it.
+    The statistic is the KL divergence of A's cell distribution from B's. It is non-negative. It is the exact KL
+    when both runs saved the whole vocabulary, and it shrinks towards 0 as the runs agree on their top tokens."""
+    union = sorted(set(pa) | set(pb))
+
+    def cells(p: dict) -> torch.Tensor:
+        lp = torch.tensor([p[t] for t in p], dtype=torch.float64)
+        tail = max(0.0, 1.0 - float(lp.exp().sum()))
+        share = tail / (vocab - len(p)) if vocab > len(p) else 0.0
+        v = [math.exp(p[t]) if t in p else share for t in union]
+        v.append(share * (vocab - len(union)))
+        return torch.tensor(v, dtype=torch.float64)
+
+    a, b = cells(pa), cells(pb)
+    a, b = a / a.sum(), b / b.sum()                     # saved values may carry rounding: renormalise
+    m = a > 0
+    return float((a[m] * (a[m].log() - b[m].clamp_min(1e-300).log())).sum())
 
 
 def top1(p: dict) -> int:
@@ -82,6 +94,9 @@ def summarize(kls: list[float]) -> dict:
 
 def compare_runs(A: dict, B: dict, start: int = 0) -> dict:
     """Statistics of two saved runs (same prompts)."""
+    vocab = A.get("vocab") or B.get("vocab")
+    if not vocab:
+        raise ValueError("saved runs carry no vocabulary size (re-run `quality_probe run`)")
     same, divs = 0, []
     for ca, cb in zip(A["completions"], B["completions"]):
         d = first_divergence(ca, cb)
@@ -93,7 +108,7 @@ def compare_runs(A: dict, B: dict, start: int = 0) -> dict:
         for pa, pb in list(zip(ta, tb))[start:]:
             pa = {int(k): v for k, v in pa.items()}
             pb = {int(k): v for k, v in pb.items()}
-            kls.append(topk_kl(pa, pb))
+            kls.append(topk_kl(pa, pb, vocab))
             agree += top1(pa) == top1(pb)
             n += 1
     out = {"decode_identical": same, "decode_streams": len(A["completions"]),
@@ -128,6 +143,7 @@ def cmd_run(args) -> dict:
     run = runtime_provider(w, window=args.chunk, max_len=args.len + 64)
     lps = [topk_logprobs(run(p)[:-1], args.topk) for p in ps]
     res = {"model": args.model, "seed": args.seed, "len": args.len, "gen": args.gen, "topk": args.topk,
+           "vocab": int(w.cfg.vocab),
            "completions": comps, "prompt_logprobs": [[{str(k): v for k, v in d.items()} for d in t] for t in lps]}
     if args.out:
         with open(args.out, "w") as f:

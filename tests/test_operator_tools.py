@@ -131,11 +131,14 @@ def test_quality_topk_kl():
     pa, pb = topk_logprobs(a, 32), topk_logprobs(b, 32)
     exact = kl_rows(a, b)
     for i in range(3):
-        assert math.isclose(topk_kl(pa[i], pb[i]), exact[i].item(), rel_tol=1e-9, abs_tol=1e-12)
-        assert topk_kl(pa[i], pa[i]) == pytest.approx(0.0, abs=1e-12)
-    # partial sets: the floor keeps the statistic finite and non-negative
+        assert math.isclose(topk_kl(pa[i], pb[i], 32), exact[i].item(), rel_tol=1e-9, abs_tol=1e-12)
+        assert topk_kl(pa[i], pa[i], 32) == pytest.approx(0.0, abs=1e-12)
+    # partial sets: finite, non-negative, zero for identical runs, and closer runs score lower
     qa, qb = topk_logprobs(a, 4), topk_logprobs(b, 4)
-    assert all(topk_kl(x, y) >= -1e-12 for x, y in zip(qa, qb))
+    assert all(0.0 <= topk_kl(x, y, 32) < math.inf for x, y in zip(qa, qb))
+    assert all(topk_kl(x, x, 32) == pytest.approx(0.0, abs=1e-12) for x in qa)
+    near = topk_logprobs(a + 0.01 * b, 4)
+    assert all(topk_kl(x, y, 32) <= topk_kl(x, z, 32) + 1e-12 for x, y, z in zip(qa, near, qb))
 
 
 def test_quality_compare_runs():
@@ -144,8 +147,8 @@ def test_quality_compare_runs():
     assert first_divergence([1, 2, 3], [1, 5, 3]) == 1
     assert first_divergence([1, 2], [1, 2, 3]) == 2
     lp = [[{"5": -0.1, "6": -2.5}, {"7": -0.3, "8": -1.5}]]
-    A = {"completions": [[1, 2, 3], [4, 5]], "prompt_logprobs": lp}
-    B = {"completions": [[1, 2, 3], [4, 9]], "prompt_logprobs": lp}
+    A = {"completions": [[1, 2, 3], [4, 5]], "prompt_logprobs": lp, "vocab": 16}
+    B = {"completions": [[1, 2, 3], [4, 9]], "prompt_logprobs": lp, "vocab": 16}
     r = compare_runs(A, B)
     assert r["decode_identical"] == 1 and r["first_divergence"] == [1]
     assert r["prefill"]["n"] == 2 and r["prefill"]["kl_max"] == pytest.approx(0.0, abs=1e-12)
