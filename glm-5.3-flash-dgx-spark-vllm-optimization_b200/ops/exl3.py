@@ -9,9 +9,9 @@ code/fork/kernels/exl3_format_ref.py:1-31).  A linear with K inputs and N output
     svh      fp16  [N]                     output sign/scale vector
     mcg      int32 [1]                     marker of the mcg codebook
 
-Value p (0..255) of a tile is the 16-bit state ending at stream bit (p+1)*bits, mapped through
-``x = (s * 0xCBAC1FED mod 2^32 & 0x8FFF8FFF) ^ 0x3B603B60``, value = fp16(low half) + fp16(high half) rounded once
-to fp16.  It lands at tile (row, col) = (2*(l%4) + (j&1) + 8*((j>>1)&1), l//4 + 8*(j>>2)) with l = p//8, j = p%8
+Value p (0..255) of a tile is read from the 16-bit state that ends at stream bit (p+1)*bits.  The state s is
+multiplied by 0xCBAC1FED (mod 2^32), masked with 0x8FFF8FFF and xor-ed with 0x3B603B60; the two 16-bit halves of
+that word, read as fp16 numbers, add up to the weight (the sum is rounded to fp16 a single time).  It lands at tile (row, col) = (2*(l%4) + (j&1) + 8*((j>>1)&1), l//4 + 8*(j>>2)) with l = p//8, j = p%8
 (the tensor-core B-fragment order of m16n8k16: lane l holds values j = 0..7).  With H the 128-point orthonormal
 Sylvester Hadamard transform applied per 128-block,
 
@@ -37,9 +37,9 @@ HBLOCK = 128
 
 @lru_cache(maxsize=1)
 def codebook() -> torch.Tensor:
-    """The codebook as a table: the fp16 value of every 16-bit state, built once.  The two halves are added in
-    float64, which holds any sum of two fp16 numbers without loss, and the sum is then cast to fp16: one cast, as
-    the format prescribes."""
+    """Lookup table of all 65,536 states -> fp16 weight value (computed on first use).  Both halves of the masked
+    product are widened to float64 before they are added; a double has room for the exact result of adding two
+    half-precision numbers, so the only rounding is the final conversion back to fp16."""
     s = torch.arange(65536, dtype=torch.int64)
     x = ((s * MCG_MUL) & 0xFFFFFFFF)
     x = (x & MCG_MASK) ^ MCG_XOR
