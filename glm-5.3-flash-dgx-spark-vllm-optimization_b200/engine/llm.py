@@ -25,7 +25,7 @@ from enum import Enum
 
 import torch
 
-from .kv_manager import KVManager, OutOfPages, SeqCache, StateSlots, page_hash
+from .kv_manager import KVManager, OutOfPages, SeqCache, StateSlots
 from .spec import AdaptiveK, greedy_accept, rejection_sample_host
 
 

@@ -31,7 +31,7 @@ import torch
 from ..config import ModelConfig
 from ..ops import kernels as K
 from .runtime import interleave_gate_up
-from .weights import Linear8, quantize_fp8_rows, _seed_of
+from .weights import quantize_fp8_rows, _seed_of
 
 MASK_TOKEN = 0
 

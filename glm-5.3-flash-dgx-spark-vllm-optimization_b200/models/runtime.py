@@ -17,7 +17,6 @@ keep < rows, from the layer's saved window inputs) and shifts the conv windows.
 
 from __future__ import annotations
 
-import math
 import os
 from array import array
 from dataclasses import dataclass
@@ -25,7 +24,6 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from ..config import ModelConfig
 from ..ops import kernels as K
 from ..utils.canary import Scratch
 from .weights import Linear8, Weights

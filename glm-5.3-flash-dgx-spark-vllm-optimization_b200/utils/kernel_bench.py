@@ -61,7 +61,7 @@ def bench_moe(args, T: Timer):
     """One MoE layer: routing + routed EXL3 experts (+ combine), hidden 4096, 288 experts of width 2048/tp."""
     import glm53
     from glm53.models.runtime import Runtime, RuntimeConfig
-    from glm53.models.weights import MoEW, MLPW, LayerW, HCW, Weights, quantize_fp8_rows
+    from glm53.models.weights import MoEW, MLPW, LayerW, Weights, quantize_fp8_rows
     from glm53.ops import exl3
     cfg = glm53.full_config(4)
     dev = torch.device("cuda")
@@ -97,7 +97,6 @@ def bench_moe(args, T: Timer):
 
 def _moe_only_runtime(rt, w, rc, dev):
     """A Runtime holding only the MoE scratch (no attention / KDA caches)."""
-    import types
     from glm53.models import runtime as RT
     c = w.cfg
     rt.w, rt.rc, rt.comm, rt.cfg, rt.device, rt.tp = w, rc, None, c, dev, 1

@@ -114,7 +114,6 @@ def test_tensor_parallel_partials_sum_to_full():
 
 
 def _failing_peer(rank, world):
-    import datetime
     import torch.distributed as dist
     from glm53.parallel import dist as D
     D.init(backend="gloo", timeout_s=5)
